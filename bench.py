@@ -1,0 +1,326 @@
+"""Benchmark of the B200 quantized-GEMM engine on BASELINE's headline workload.
+
+Workload: one decode MoE layer of 16 tokens, hidden 4096, 128 routed IQ2_XXS experts, top-6
+(softmax, renormalised) plus one shared expert, expert FFN 2048 with ReLU^2.  A step is one pass of the layer
+(router -> up -> down -> combine) over one batch of 16 tokens.  Metric: IQ2_XXS MoE decode GB/s = the algorithmic
+bytes of the step (every touched expert's up and down weights read once, plus x, the logits and the output) / the
+step time.  L2 is defeated by rotating 4 layer copies (2.2 GB of experts) and 8 token batches.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the reference's arithmetic on the host cores: the CPU oracle (a scalar C restatement of
+libbolt's kernels; libbolt has no CPU implementation of this path) with every host thread, on a bounded sample.
+Under torchrun each rank runs its own replica of the layer on its own tokens (weak scaling); rank 0 prints one line.
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "nemotron-3.5-bolt-tensorfold-dgx-spark_b200")
+sys.path[:0] = [PKG]
+
+METRIC = "IQ2_XXS MoE decode GB/s"
+T, H, F, E, TOPK = 16, 4096, 2048, 128, 6
+LAYERS, BATCHES = 4, 8
+EXPERT_BYTES = 2 * (F * (H // 256) * 66)      # up [F][H] + down [H][F]: 4,325,376 B
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            m = json.load(f)
+        return float(m["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms in the background during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"b200q_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.remove(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_layers(b200q, device):
+    """4 layer copies of 128 experts (packed rt32) + a shared expert each, generated on the device."""
+    up_b, down_b = b200q.iq2_bytes(F, H), b200q.iq2_bytes(H, F)
+    layers = []
+    for L in range(LAYERS):
+        up = torch.empty(E * up_b, dtype=torch.uint8, device=device)
+        down = torch.empty(E * down_b, dtype=torch.uint8, device=device)
+        raw = b200q.synth_iq2(1000 + 10 * L, E * F * (H // 256), device)
+        b200q.repack_iq2(raw, E * F, H, out=up)
+        raw = b200q.synth_iq2(1001 + 10 * L, E * H * (F // 256), device)
+        b200q.repack_iq2(raw, E * H, F, out=down)
+        del raw
+        su = b200q.repack_iq2(b200q.synth_iq2(1002 + 10 * L, F * (H // 256), device), F, H)
+        sd = b200q.repack_iq2(b200q.synth_iq2(1003 + 10 * L, H * (F // 256), device), H, F)
+        layers.append(b200q.MoeDecodeLayer(up, down, su, sd, H, F, E, TOPK, route=b200q.ROUTE_SOFTMAX, max_tokens=T))
+    torch.cuda.synchronize()
+    return layers
+
+
+def make_batches(rank, device):
+    g = torch.Generator().manual_seed(77 + rank)
+    xs = [torch.randn(T, H, generator=g).to(torch.bfloat16) for _ in range(BATCHES)]
+    ls = [torch.randn(T, E, generator=g).to(torch.bfloat16) for _ in range(BATCHES)]
+    return xs, ls
+
+
+def step_bytes(ridx_np):
+    """algorithmic bytes of one step: distinct routed experts + the shared one, read once; x, logits, output."""
+    distinct = len(np.unique(ridx_np))
+    return (distinct + 1) * EXPERT_BYTES + T * H * 2 + T * E * 2 + T * H * 4, distinct
+
+
+def run_ours(args, rank, world, local_rank):
+    import b200q
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    dist = world > 1
+    if dist:
+        import torch.distributed as td
+        import datetime
+        td.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    layers = make_layers(b200q, device)
+    xs_h, ls_h = make_batches(rank, device)
+    xs = [x.to(device) for x in xs_h]
+    ls = [l.to(device) for l in ls_h]
+    out = torch.empty(T, H, dtype=torch.float32, device=device)
+    ridx = [torch.empty(T, TOPK, dtype=torch.int32, device=device) for _ in range(BATCHES)]
+    rw = torch.empty(T, TOPK, dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream()
+
+    def step(i, **kw):
+        layers[i % LAYERS](xs[i % BATCHES], ls[i % BATCHES], out=out, ridx=ridx[i % BATCHES], rw=rw, **kw)
+
+    def barrier():
+        if dist:
+            torch.distributed.barrier()
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    byts = [step_bytes(r.cpu().numpy()) for r in ridx]
+
+    # ---- the timed region: K steps, device-timed with events, barrier + synchronize on both sides
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with Clocks(local_rank) as clk:
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    total_bytes = sum(byts[(args.warmup + i) % BATCHES][0] for i in range(args.steps))
+    gbs_rank = total_bytes / (ms * 1e-3) / 1e9
+    value = gbs_rank * world      # every rank does the same amount of work; the time is the max over ranks
+
+    # ---- per-kernel durations (a second pass with events between the four launches)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    stage_ms = np.zeros(4)
+    nprof = max(args.steps, 4)
+    for i in range(nprof):
+        step(args.warmup + i, stage_events=evs)
+        torch.cuda.synchronize()
+        stage_ms += [evs[j].elapsed_time(evs[j + 1]) for j in range(4)]
+    stage_ms /= nprof
+    names = ["prep (router+group+quant)", "up GEMV (relu^2 + int8)", "down GEMV", "combine"]
+    dom = int(np.argmax(stage_ms))
+    mean_distinct = np.mean([byts[(args.warmup + i) % BATCHES][1] for i in range(nprof)])
+    half = (mean_distinct + 1) * EXPERT_BYTES / 2
+    dom_bytes = {1: half + T * H + (T * TOPK + T) * F * 1.125, 2: half + (T * TOPK + T) * (F * 1.125 + H * 4)}.get(dom, 0)
+    peak, peak_kind = peaks()
+    achieved = dom_bytes / (stage_ms[dom] * 1e-3) / 1e9 if dom_bytes else None
+
+    # ---- e2e: the public API with host buffers (pinned), H2D of x and logits, D2H of the output, every step
+    xh = [x.pin_memory() for x in xs_h]
+    lh = [l.pin_memory() for l in ls_h]
+    oh = torch.empty(T, H, dtype=torch.float32).pin_memory()
+    xd = torch.empty(T, H, dtype=torch.bfloat16, device=device)
+    ld = torch.empty(T, E, dtype=torch.bfloat16, device=device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(args.steps):
+        j = args.warmup + i
+        xd.copy_(xh[j % BATCHES], non_blocking=True)
+        ld.copy_(lh[j % BATCHES], non_blocking=True)
+        layers[j % LAYERS](xd, ld, out=out)
+        oh.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([e2e_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_gbs = total_bytes / (e2e_ms * 1e-3) / 1e9 * world
+
+    line = None
+    if rank == 0:
+        cpu = cpu_baseline(threads=os.cpu_count() or 1, sample_tokens=2)
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "BASELINE config 2: decode MoE layer, 16 tokens, hidden 4096, 128 IQ2_XXS experts "
+                                   "top-6 (softmax, renormalised) + 1 shared, FFN 2048, ReLU^2",
+                       "tokens": T, "hidden": H, "experts": E, "topk": TOPK, "ffn": F, "shared_experts": 1,
+                       "mean_distinct_experts": round(float(mean_distinct), 2),
+                       "l2": f"{LAYERS} rotating layer copies ({LAYERS * (E + 1) * EXPERT_BYTES / 1e9:.2f} GB) and "
+                             f"{BATCHES} token batches, larger than the 126 MB L2",
+                       "parallelism": f"replicas{world}" if world > 1 else "single"},
+            "hbm_fraction": round(value / world / peak, 4),
+            "roofline": {"bound": "hbm", "kernel": names[dom], "achieved": round(achieved, 1) if achieved else None,
+                         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None,
+                         "traffic": None, "peak_kind": peak_kind,
+                         "stage_ms": {n: round(float(v), 5) for n, v in zip(names, stage_ms)}},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": T * H * 2 + T * E * 2,
+                    "d2h_bytes_per_step": T * H * 4},
+            "gpu_launches": 4 * args.steps,
+            "clocks": clk.summary(),
+        }
+    if dist:
+        torch.distributed.destroy_process_group()
+    return line
+
+
+def cpu_baseline(threads, sample_tokens):
+    """The CPU oracle (int8-per-32 arithmetic, all host threads) on a bounded sample: the first `sample_tokens`
+    tokens of one batch of the same layer shapes; GB/s over the sample's touched experts."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle as O
+    import b200q
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(sample_tokens, H, generator=g).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    lg = torch.randn(sample_tokens, E, generator=g).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    lgf = (lg.astype(np.uint32) << 16).view(np.float32)
+    ridx, _ = O.route_softmax(lgf, TOPK)
+    used = sorted(set(ridx.reshape(-1).tolist()))
+    # only the touched experts are generated (the oracle indexes the slab by expert id)
+    up = np.zeros((E, F * (H // 256) * 66), np.uint8)
+    down = np.zeros((E, H * (F // 256) * 66), np.uint8)
+    for e in used:
+        up[e] = b200q.synth_iq2_host(50 + e, F * (H // 256))
+        down[e] = b200q.synth_iq2_host(500 + e, H * (F // 256))
+    su = b200q.synth_iq2_host(7, F * (H // 256))
+    sd = b200q.synth_iq2_host(8, H * (F // 256))
+    t0 = time.perf_counter()
+    O.moe_layer(x, lg, up, down, su, sd, sample_tokens, H, F, E, TOPK, mode=0)
+    dt = time.perf_counter() - t0
+    nbytes = (len(used) + 1) * EXPERT_BYTES
+    return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{sample_tokens} tokens of the config-2 layer ({len(used)} routed experts + shared), "
+                      f"{dt:.2f} s, OpenMP over rows"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    vals = []
+    for _ in range(args.warmup):
+        cpu_baseline(threads, 1)
+    for _ in range(args.steps):
+        vals.append(cpu_baseline(threads, 1))
+    v = float(np.median([c["value"] for c in vals]))
+    c = dict(vals[-1])
+    c["value"] = round(v, 3)
+    return {"metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": "BASELINE config 2 decode MoE layer (one token a step: a bounded CPU sample)",
+                       "tokens": 1, "hidden": H, "experts": E, "topk": TOPK, "ffn": F, "shared_experts": 1},
+            "cpu_baseline": c,
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+    else:
+        line = run_ours(args, rank, world, local_rank)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

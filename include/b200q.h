@@ -1,0 +1,161 @@
+/*
+ * b200q.h -- the C ABI of libb200q, a B200 (sm_100a) engine for the weight-bound quantized GEMMs of
+ * Nemotron-3.5-Bolt: the IQ2_XXS routed-expert MoE, the NVFP4 Mamba-2 projections and the Q8_0 projections.
+ *
+ * It replaces the operator launchers of the reference engine libbolt (engine/bolt_common.h:77-157), which are
+ * C++ functions returning void.  Here every entry point is extern "C", takes plain device pointers, sizes and
+ * a stream (a cudaStream_t passed as void*), and returns a status:
+ *     B200Q_OK (0)  enqueued;   B200Q_EINVAL (-1)  bad pointer or shape (libbolt's -1);
+ *     B200Q_ECUDA (-3)  a CUDA launch error (libbolt's -3, run_blocks, bolt_host.cu:865-869);
+ *     B200Q_ENOSPACE (-2)  a workspace or fixed capacity too small.
+ * Every operator is asynchronous on its stream, allocates nothing, never synchronises and never reads device
+ * data on the host, so a sequence of them can be captured in a CUDA graph (the reference captures
+ * enqueue_block, bolt_host.cu:839-857).  The caller owns every buffer, scratch included; the *_workspace_bytes
+ * queries give the scratch sizes.  Kernels use programmatic dependent launch like libbolt's (bolt_common.h:84-110);
+ * B200Q_PDL=0 in the environment turns it off.
+ *
+ * Weight layouts.  The packers take the checkpoint's raw bytes (already on the device) and write this library's
+ * layouts (same byte counts):
+ *     IQ2_XXS  ggml blocks [rows][k/256][66]       -> b200q_iq2_pack      (n % 32 == 0, k % 256 == 0)
+ *     Q8_0     ggml blocks [rows][k/32][34]        -> b200q_q8_pack       (n % 32 == 0, k % 256 == 0)
+ *     NVFP4    q [rows][k/2], sc [rows][k/16] e4m3 -> b200q_nv4_pack      (n % 32 == 0, k % 256 == 0)
+ * A slab of experts is packed as one matrix of experts*rows rows (every expert's rows are a multiple of 32), so
+ * expert e starts at e * b200q_iq2_bytes(rows, k).
+ */
+#ifndef B200Q_H
+#define B200Q_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200Q_ABI 1
+
+#define B200Q_OK 0
+#define B200Q_EINVAL (-1)
+#define B200Q_ENOSPACE (-2)
+#define B200Q_ECUDA (-3)
+
+/* activation element types */
+#define B200Q_F32 0
+#define B200Q_BF16 1
+
+/* router forms */
+#define B200Q_ROUTE_SOFTMAX 0   /* softmax over the logits, top-k, renormalised to sum 1 */
+#define B200Q_ROUTE_SIGMOID 1   /* sigmoid + bias, top-k, sigmoids normalised and scaled (route_k)           */
+
+/* ABI version; libbolt's is bolt_abi() (bolt_host.cu:1139), checked by bolt_native.zig:516. */
+int b200q_abi(void);
+/* The CUDA error behind the last B200Q_ECUDA of this thread (cudaError_t as int), 0 if none. */
+int b200q_last_cuda_error(void);
+const char* b200q_strerror(int status);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Load-time packers (raw checkpoint bytes on the device -> this library's layouts).
+ * --------------------------------------------------------------------------------------------------------- */
+
+/* Bytes of an IQ2_XXS matrix of n rows: n*k/256*66 (the checkpoint tensor [n][k/256][66], bolt_host.cu:269). */
+size_t b200q_iq2_bytes(int64_t n, int k);
+/* Replaces repack_iq2 (bolt_kernels.cu:1054-1068, via load_slab bolt_host.cu:306-328) and tile_iq2
+ * (bolt_mma.cu:1336-1361): ggml blocks [n][k/256][66] -> the rt32 layout.  raw and packed must not overlap. */
+int b200q_iq2_pack(const void* raw, void* packed, int64_t n, int k, void* stream);
+
+size_t b200q_q8_bytes(int64_t n, int k);
+/* Replaces tile_q8 (bolt_mma.cu:1270-1311, via load_q8 bolt_host.cu:198-217). */
+int b200q_q8_pack(const void* raw, void* packed, int64_t n, int k, void* stream);
+
+size_t b200q_nv4_bytes(int64_t n, int k);
+/* Replaces tile_nv4 / tile_nv4w (bolt_mma.cu:1231-1268, 892-923, via load_nv4 bolt_host.cu:219-264). */
+int b200q_nv4_pack(const void* q, const void* sc, void* packed, int64_t n, int k, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Router, grouping, activation quantisation, combine.
+ * --------------------------------------------------------------------------------------------------------- */
+
+/* Replaces k_quant_rows (bolt_kernels.cu:347-363): int8 per 32, s = amax/127, q = rn(x*127/amax).
+ * x [rows][ldx] (B200Q_F32 or B200Q_BF16) -> q [rows][ldq] int8, s [rows][lds] fp32.  k % 32 == 0. */
+int b200q_quant_rows(const void* x, int x_dtype, int ldx, int8_t* q, int ldq, float* s, int lds, int rows, int k,
+                     void* stream);
+
+/* Replaces k_route (bolt_kernels.cu:1655-1712).  logits [T][ldl] (fp32 or bf16) -> ridx [T][topk] int,
+ * rw [T][topk] fp32.  mode B200Q_ROUTE_SOFTMAX: softmax, top-k, renormalised (bias and scale unused);
+ * B200Q_ROUTE_SIGMOID: route_k's form, bias [E] may be NULL.  Ties go to the lower expert.  E <= 512, topk <= 16. */
+int b200q_route(const void* logits, int l_dtype, int ldl, const float* bias, int T, int E, int topk, int mode,
+                float scale, int* ridx, float* rw, void* stream);
+
+/* Replaces k_moe_group (bolt_kernels.cu:275-325): counting sort of the pairs by expert.
+ * counts [E], offsets [E+1] (exclusive prefix), order [pairs]: the pairs of each expert in increasing order
+ * (libbolt fills an expert's run with atomics; this order is deterministic).  pairs <= 4096, E <= 512. */
+int b200q_moe_group(const int* ridx, int pairs, int E, int* counts, int* offsets, int* order, void* stream);
+
+/* Replaces k_combine (bolt_kernels.cu:1714-1727), generalised from TOPN=9 and width 1024:
+ * out[t][h] = sum_k rw[t][k] * mo[t*topk+k][h]  (+ shared[t][h] when shared is not NULL).
+ * mo [T*topk][H] fp32, out [T][H] fp32 or bf16 (out_dtype).  H % 4 == 0. */
+int b200q_combine(const float* mo, const float* rw, const float* shared, int T, int topk, int H, void* out,
+                  int out_dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * IQ2_XXS GEMVs on int8 activation rows (the routed-expert arithmetic of moe_mma_k / moe_coop_k,
+ * bolt_kernels.cu:373-519, 542-667): per 32-weight chunk an exact int32 dot of the signed grid integers and the
+ * int8 row, then acc += (d*(0.5+s4)*0.25 * s_row) * dot.
+ * --------------------------------------------------------------------------------------------------------- */
+
+/* Dense: y[t][n] = W[n] . x[t] for T rows.  Replaces mma_iq2 (bolt_mma.cu:1196-1203) and moe_coop_dense
+ * (bolt_kernels.cu:881-887).  w packed rt32 [n][k]; xq [T][k] int8, xs [T][k/32]; y [T][ldy] fp32.
+ * epi 0: store; epi 1: store relu(v)^2.  n % 32 == 0, k % 256 == 0, k <= 8192. */
+int b200q_iq2_gemv(const void* w, int n, int k, const int8_t* xq, const float* xs, int T, float* y, int ldy,
+                   int epi, void* stream);
+
+/* Test hook for the bit-exactness contract: the int32 dot of every (row, 32-chunk, token), computed by the same
+ * device code as the GEMVs.  dots [T][n][k/32] int32. */
+int b200q_iq2_chunk_dots(const void* w, int n, int k, const int8_t* xq, int T, int32_t* dots, void* stream);
+
+/* Routed experts, one launch over every (token, expert) pair.  Replace moe_up / moe_down
+ * (bolt_kernels.cu:682-695), generalised from k=1024, n=1024 and TOPN=9.
+ * slab: E experts, packed rt32, expert e at e*b200q_iq2_bytes(n, k).  counts/offsets/order from b200q_moe_group.
+ * up:   act row of pair p is xq[p / topk]; out row p.  down: act row p; out row p.
+ * y: epi 0 fp32 [pairs][ldy]; epi 1 relu^2 fp32.
+ * b200q_moe_up_q8 writes relu(up)^2 quantised to int8 per 32 (aq [pairs][n], as [pairs][n/32]), the fused form of
+ * moe_up + k_quant_rows (bolt_host.cu:709-712). */
+int b200q_moe_up(const void* slab, int E, int n, int k, const int* counts, const int* offsets, const int* order,
+                 int topk, const int8_t* xq, const float* xs, float* y, int ldy, int epi, void* stream);
+int b200q_moe_up_q8(const void* slab, int E, int n, int k, const int* counts, const int* offsets, const int* order,
+                    int topk, const int8_t* xq, const float* xs, int8_t* aq, float* as, void* stream);
+int b200q_moe_down(const void* slab, int E, int n, int k, const int* counts, const int* offsets, const int* order,
+                   const int8_t* aq, const float* as, float* y, int ldy, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * One decode MoE layer, the sequence enqueue_block runs for a MoE block
+ * (bolt_host.cu:665-720) fused into four launches: router + grouping + int8 rows of x; up with relu^2 and the
+ * int8 rows of the result; down; weighted combine plus the shared expert.
+ *   x [T][H] bf16, logits [T][E] bf16 (the gate GEMM's output), up slab [E] x [F][H], down slab [E] x [H][F]
+ *   (packed rt32), shared_up [F][H] / shared_down [H][F] (NULL: none), out [T][H] fp32 or bf16.
+ *   route: B200Q_ROUTE_SOFTMAX or B200Q_ROUTE_SIGMOID (bias, scale as b200q_route).
+ *   T <= 64, E <= 512, topk <= 16, H and F multiples of 256, H, F <= 8192.
+ * workspace: workspace_bytes >= b200q_moe_decode_workspace_bytes(T, H, F, E, topk), 256-byte aligned.
+ * ridx_out / rw_out: optional copies of the routing ([T][topk]).
+ * stage_events: NULL, or 5 cudaEvent_t recorded on the stream before the prologue and after each of the four
+ * launches (router/grouping/quantisation, up, down, combine), for per-kernel timing; the events' record calls sit
+ * between the launches, so leave it NULL outside of profiling. */
+size_t b200q_moe_decode_workspace_bytes(int T, int H, int F, int E, int topk);
+int b200q_moe_decode(const void* x, const void* logits, const void* up, const void* down, const void* shared_up,
+                     const void* shared_down, int T, int H, int F, int E, int topk, int route, const float* bias,
+                     float scale, void* out, int out_dtype, void* workspace, size_t workspace_bytes, int* ridx_out,
+                     float* rw_out, void* const* stage_events, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Synthetic inputs (BASELINE's generators), host and device producing the same bytes.
+ * --------------------------------------------------------------------------------------------------------- */
+
+/* IQ2_XXS ggml blocks [nblocks][66]: d fp16 ~ U[1e-3, 1e-2], grid indices U{0..255}, sign indices U{0..127},
+ * sub-scales U{0..15}; block i depends on (seed, i) only. */
+void b200q_synth_iq2_host(uint64_t seed, int64_t nblocks, void* out);
+int b200q_synth_iq2(uint64_t seed, int64_t nblocks, void* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,249 @@
+"""Host-side mirror of libbolt's operator interface over libb200q's C ABI (include/b200q.h).
+
+The reference engine's operators are C++ launchers (engine/bolt_common.h:77-157): k_route, k_moe_group,
+k_quant_rows, moe_up, moe_down, k_combine, mma_iq2, mma_nv4, mma_q8, quant_nv4_rows, repack_iq2, tile_*.  This module
+gives the same operators by the same names, taking torch tensors for device memory and the current torch stream,
+and calling the sm_100a kernels through ctypes.  Errors raise B200QError with libb200q's status (the reference
+returns void and logs; its C ABI returns -1/-3).  There is no CPU fallback: without libb200q.so, or without a GPU,
+every operator raises.
+"""
+import ctypes
+import os
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libb200q.so")
+
+OK, EINVAL, ENOSPACE, ECUDA = 0, -1, -2, -3
+F32, BF16 = 0, 1
+ROUTE_SOFTMAX, ROUTE_SIGMOID = 0, 1
+
+_LIB = None
+
+
+class B200QError(RuntimeError):
+    def __init__(self, status, what):
+        self.status = status
+        msg = lib().b200q_strerror(status).decode()
+        if status == ECUDA:
+            msg += f" (cudaError {lib().b200q_last_cuda_error()})"
+        super().__init__(f"{what}: {msg}")
+
+
+def lib():
+    """The loaded libb200q.so (built in place by build.py; a missing library is an error, never a fallback)."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"libb200q.so is missing at {LIB_PATH}: run build.py (nvcc, sm_100a)")
+        L = ctypes.CDLL(LIB_PATH)
+        vp, i32, i64, f32, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
+        sig = {
+            "b200q_abi": (i32, []), "b200q_last_cuda_error": (i32, []), "b200q_strerror": (ctypes.c_char_p, [i32]),
+            "b200q_iq2_bytes": (sz, [i64, i32]), "b200q_iq2_pack": (i32, [vp, vp, i64, i32, vp]),
+            "b200q_quant_rows": (i32, [vp, i32, i32, vp, i32, vp, i32, i32, i32, vp]),
+            "b200q_route": (i32, [vp, i32, i32, vp, i32, i32, i32, i32, f32, vp, vp, vp]),
+            "b200q_moe_group": (i32, [vp, i32, i32, vp, vp, vp, vp]),
+            "b200q_combine": (i32, [vp, vp, vp, i32, i32, i32, vp, i32, vp]),
+            "b200q_iq2_gemv": (i32, [vp, i32, i32, vp, vp, i32, vp, i32, i32, vp]),
+            "b200q_iq2_chunk_dots": (i32, [vp, i32, i32, vp, i32, vp, vp]),
+            "b200q_moe_up": (i32, [vp, i32, i32, i32, vp, vp, vp, i32, vp, vp, vp, i32, i32, vp]),
+            "b200q_moe_up_q8": (i32, [vp, i32, i32, i32, vp, vp, vp, i32, vp, vp, vp, vp, vp]),
+            "b200q_moe_down": (i32, [vp, i32, i32, i32, vp, vp, vp, vp, vp, vp, i32, vp]),
+            "b200q_moe_decode_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
+            "b200q_moe_decode": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, f32, vp, i32, vp, sz,
+                                       vp, vp, vp, vp]),
+            "b200q_synth_iq2_host": (None, [ctypes.c_uint64, i64, vp]),
+            "b200q_synth_iq2": (i32, [ctypes.c_uint64, i64, vp, vp]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype, fn.argtypes = res, args
+        _LIB = L
+    return _LIB
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _s(stream=None):
+    return ctypes.c_void_p((stream or torch.cuda.current_stream()).cuda_stream)
+
+
+def _check(status, what):
+    if status != OK:
+        raise B200QError(status, what)
+
+
+def _dev(t, name):
+    if not (isinstance(t, torch.Tensor) and t.is_cuda):
+        raise B200QError(EINVAL, f"{name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise B200QError(EINVAL, f"{name} must be contiguous")
+    return t
+
+
+def _dtype_code(t):
+    if t.dtype == torch.float32:
+        return F32
+    if t.dtype == torch.bfloat16:
+        return BF16
+    raise B200QError(EINVAL, f"unsupported activation dtype {t.dtype}")
+
+
+# -------------------------------------------------------------------------------------------------------------
+# load-time packing (repack_iq2 / load_slab, bolt_kernels.cu:1054-1068, bolt_host.cu:306-328)
+# -------------------------------------------------------------------------------------------------------------
+def iq2_bytes(n, k):
+    return lib().b200q_iq2_bytes(n, k)
+
+
+def repack_iq2(raw, n, k, out=None):
+    """ggml IQ2_XXS blocks (uint8 CUDA tensor, [n][k/256][66] bytes) -> the rt32 device layout (same byte count)."""
+    _dev(raw, "raw")
+    if out is None:
+        out = torch.empty(iq2_bytes(n, k), dtype=torch.uint8, device=raw.device)
+    _check(lib().b200q_iq2_pack(_p(raw), _p(out), n, k, _s()), "repack_iq2")
+    return out
+
+
+def synth_iq2(seed, nblocks, device="cuda"):
+    """BASELINE's synthetic IQ2_XXS blocks, generated on the device (the same bytes as synth_iq2_host)."""
+    out = torch.empty(nblocks * 66, dtype=torch.uint8, device=device)
+    _check(lib().b200q_synth_iq2(seed, nblocks, _p(out), _s()), "synth_iq2")
+    return out
+
+
+def synth_iq2_host(seed, nblocks):
+    import numpy as np
+    out = np.zeros(nblocks * 66, np.uint8)
+    lib().b200q_synth_iq2_host(seed, nblocks, out.ctypes.data_as(ctypes.c_void_p))
+    return out
+
+
+# -------------------------------------------------------------------------------------------------------------
+# router, grouping, activation quantisation, combine
+# -------------------------------------------------------------------------------------------------------------
+def k_quant_rows(x, q=None, s=None):
+    """int8 per 32 (quant_rows_k): x [rows][k] fp32/bf16 -> q [rows][k] int8, s [rows][k/32] fp32."""
+    _dev(x, "x")
+    rows, k = x.shape
+    q = torch.empty(rows, k, dtype=torch.int8, device=x.device) if q is None else q
+    s = torch.empty(rows, k // 32, dtype=torch.float32, device=x.device) if s is None else s
+    _check(lib().b200q_quant_rows(_p(x), _dtype_code(x), k, _p(q), k, _p(s), k // 32, rows, k, _s()), "k_quant_rows")
+    return q, s
+
+
+def k_route(logits, topk, mode=ROUTE_SOFTMAX, bias=None, scale=1.0):
+    """Router (route_k): logits [T][E] -> ridx [T][topk] int32, rw [T][topk] fp32."""
+    _dev(logits, "logits")
+    T, E = logits.shape
+    ridx = torch.empty(T, topk, dtype=torch.int32, device=logits.device)
+    rw = torch.empty(T, topk, dtype=torch.float32, device=logits.device)
+    _check(lib().b200q_route(_p(logits), _dtype_code(logits), E, _p(bias), T, E, topk, mode, float(scale), _p(ridx),
+                             _p(rw), _s()), "k_route")
+    return ridx, rw
+
+
+def k_moe_group(ridx, E):
+    """Counting sort of the pairs by expert (moe_group_k): counts [E], offsets [E+1], order [pairs]."""
+    _dev(ridx, "ridx")
+    pairs = ridx.numel()
+    counts = torch.empty(E, dtype=torch.int32, device=ridx.device)
+    offsets = torch.empty(E + 1, dtype=torch.int32, device=ridx.device)
+    order = torch.empty(max(pairs, 1), dtype=torch.int32, device=ridx.device)
+    _check(lib().b200q_moe_group(_p(ridx), pairs, E, _p(counts), _p(offsets), _p(order), _s()), "k_moe_group")
+    return counts, offsets, order[:pairs]
+
+
+def k_combine(mo, rw, topk, shared=None, out_dtype=torch.float32):
+    """out[t] = sum_k rw[t][k] mo[t*topk+k] (+ shared[t]) (combine_k)."""
+    _dev(mo, "mo")
+    T = rw.numel() // topk
+    H = mo.shape[-1]
+    out = torch.empty(T, H, dtype=out_dtype, device=mo.device)
+    _check(lib().b200q_combine(_p(mo), _p(rw), _p(shared), T, topk, H, _p(out), _dtype_code(out), _s()), "k_combine")
+    return out
+
+
+# -------------------------------------------------------------------------------------------------------------
+# IQ2_XXS GEMVs over int8 rows
+# -------------------------------------------------------------------------------------------------------------
+def mma_iq2(w, n, k, xq, xs, epi=0):
+    """Dense IQ2_XXS GEMV (mma_iq2 / moe_coop_dense): y [T][n] fp32 = W . x for the int8 rows xq/xs."""
+    T = xq.shape[0]
+    y = torch.empty(T, n, dtype=torch.float32, device=xq.device)
+    _check(lib().b200q_iq2_gemv(_p(w), n, k, _p(_dev(xq, "xq")), _p(_dev(xs, "xs")), T, _p(y), n, epi, _s()), "mma_iq2")
+    return y
+
+
+def iq2_chunk_dots(w, n, k, xq):
+    T = xq.shape[0]
+    d = torch.empty(T, n, k // 32, dtype=torch.int32, device=xq.device)
+    _check(lib().b200q_iq2_chunk_dots(_p(w), n, k, _p(_dev(xq, "xq")), T, _p(d), _s()), "iq2_chunk_dots")
+    return d
+
+
+def moe_up(slab, E, n, k, counts, offsets, order, topk, xq, xs, epi=1):
+    pairs = order.numel()
+    y = torch.empty(max(pairs, 1), n, dtype=torch.float32, device=xq.device)
+    _check(lib().b200q_moe_up(_p(slab), E, n, k, _p(counts), _p(offsets), _p(order), topk, _p(xq), _p(xs), _p(y), n, epi,
+                              _s()), "moe_up")
+    return y[:pairs]
+
+
+def moe_up_q8(slab, E, n, k, counts, offsets, order, topk, xq, xs):
+    pairs = order.numel()
+    aq = torch.empty(max(pairs, 1), n, dtype=torch.int8, device=xq.device)
+    as_ = torch.empty(max(pairs, 1), n // 32, dtype=torch.float32, device=xq.device)
+    _check(lib().b200q_moe_up_q8(_p(slab), E, n, k, _p(counts), _p(offsets), _p(order), topk, _p(xq), _p(xs), _p(aq),
+                                 _p(as_), _s()), "moe_up_q8")
+    return aq[:pairs], as_[:pairs]
+
+
+def moe_down(slab, E, n, k, counts, offsets, order, aq, as_):
+    pairs = order.numel()
+    y = torch.empty(max(pairs, 1), n, dtype=torch.float32, device=aq.device)
+    _check(lib().b200q_moe_down(_p(slab), E, n, k, _p(counts), _p(offsets), _p(order), _p(aq), _p(as_), _p(y), n, _s()),
+           "moe_down")
+    return y[:pairs]
+
+
+# -------------------------------------------------------------------------------------------------------------
+# the decode MoE layer
+# -------------------------------------------------------------------------------------------------------------
+class MoeDecodeLayer:
+    """One decode MoE layer (router, up with relu^2, down, combine, shared expert) over packed IQ2_XXS slabs.
+
+    up: packed [E] x [F][H], down: packed [E] x [H][F] (CUDA uint8 tensors in the rt32 layout); shared_up/down
+    optional.  The workspace is allocated once here, for up to max_tokens tokens; __call__ only launches kernels.
+    """
+
+    def __init__(self, up, down, shared_up, shared_down, H, F, E, topk, route=ROUTE_SOFTMAX, bias=None, scale=1.0,
+                 max_tokens=16):
+        self.up, self.down, self.shared_up, self.shared_down = up, down, shared_up, shared_down
+        self.H, self.F, self.E, self.topk, self.route, self.bias, self.scale = H, F, E, topk, route, bias, scale
+        self.max_tokens = max_tokens
+        nbytes = lib().b200q_moe_decode_workspace_bytes(max_tokens, H, F, E, topk)
+        self.workspace = torch.empty(nbytes + 256, dtype=torch.uint8, device=up.device)
+        off = (-self.workspace.data_ptr()) % 256
+        self._ws_ptr = self.workspace.data_ptr() + off
+        self._ws_bytes = nbytes
+
+    def __call__(self, x, logits, out=None, ridx=None, rw=None, stream=None, stage_events=None):
+        """x [T][H] bf16, logits [T][E] bf16 (CUDA) -> out [T][H]; stage_events: 5 torch.cuda.Event for profiling."""
+        T = x.shape[0]
+        if T > self.max_tokens:
+            raise B200QError(EINVAL, f"{T} tokens > max_tokens {self.max_tokens}")
+        out = torch.empty(T, self.H, dtype=torch.float32, device=x.device) if out is None else out
+        need = lib().b200q_moe_decode_workspace_bytes(T, self.H, self.F, self.E, self.topk)
+        ev = None
+        if stage_events is not None:
+            ev = (ctypes.c_void_p * 5)(*[e.cuda_event for e in stage_events])
+        _check(lib().b200q_moe_decode(_p(x), _p(logits), _p(self.up), _p(self.down), _p(self.shared_up),
+                                      _p(self.shared_down), T, self.H, self.F, self.E, self.topk, self.route, _p(self.bias),
+                                      float(self.scale), _p(out), _dtype_code(out), ctypes.c_void_p(self._ws_ptr), need,
+                                      _p(ridx), _p(rw), ev, _s(stream)), "moe_decode")
+        return out

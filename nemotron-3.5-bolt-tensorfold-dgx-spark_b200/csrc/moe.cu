@@ -1,0 +1,379 @@
+// The MoE layer around the expert GEMVs: int8 rows of the activations, the router, the expert-sorted grouping,
+// the weighted combine, and the decode layer that chains them.
+#include "iq2.cuh"
+
+#include <cstdlib>
+
+namespace b200q {
+
+
+
+// ---------------------------------------------------------------------------------------------------------
+// status plumbing
+// ---------------------------------------------------------------------------------------------------------
+static thread_local int g_last_cuda = 0;
+int status_from(cudaError_t e) {
+    if (e == cudaSuccess) return B200Q_OK;
+    g_last_cuda = (int)e;
+    return B200Q_ECUDA;
+}
+bool pdl_enabled() {
+    static const bool on = [] { const char* e = getenv("B200Q_PDL"); return !(e && atoi(e) == 0); }();
+    return on;
+}
+
+__device__ __forceinline__ float load_act(const void* p, int dtype, size_t i) {
+    return dtype == B200Q_BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]) : reinterpret_cast<const float*>(p)[i];
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// quant_rows_k's arithmetic (bolt_kernels.cu:347-360), a warp per 32-group: s = amax/127, q = rn(x * 127/amax)
+// ---------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void quant_group(float v, int lane, int8_t* q, float* s) {
+    float am = fabsf(v);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    const float inv = am > 0.f ? 127.f / am : 0.f;
+    q[lane] = (int8_t)__float2int_rn(v * inv);
+    if (lane == 0) *s = am / 127.f;
+}
+
+__global__ void quant_rows_k(const void* __restrict__ x, int dtype, int ldx, int8_t* __restrict__ q, int ldq,
+                             float* __restrict__ s, int lds, int rows, int k) {
+    pdl_wait();
+    const int groups = k >> 5;
+    const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (gw < (int64_t)rows * groups) {
+        const int r = (int)(gw / groups), g = (int)(gw - (int64_t)r * groups);
+        const float v = load_act(x, dtype, (size_t)r * ldx + g * 32 + lane);
+        quant_group(v, lane, q + (size_t)r * ldq + g * 32, s + (size_t)r * lds + g);
+    }
+    pdl_trigger();
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// router: a warp per token (route_k's shape, bolt_kernels.cu:1655-1712), E <= 512 so a lane holds 16 logits.
+// Top-k by repeated warp argmax, ties to the lower index.
+//   softmax: w_i = exp(z_i - max) / sum over the picked of exp(z_j - max)   (softmax, top-k, renormalised)
+//   sigmoid: route_k's form: pick by sigmoid(z) + bias, w = sigmoid / (1e-20 + sum of picked) * scale
+// ---------------------------------------------------------------------------------------------------------
+__device__ void route_token(const void* logits, int dtype, int ldl, const float* bias, int E, int topk, int mode,
+                           float scale, int t, int lane, int* ridx, float* rw) {
+    float val[16], key[16];
+    float mx = -3.0e38f;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        const int i = lane + 32 * j;
+        if (i < E) {
+            const float z = load_act(logits, dtype, (size_t)t * ldl + i);
+            if (mode == B200Q_ROUTE_SOFTMAX) {
+                val[j] = z;
+                key[j] = z;
+            } else {
+                val[j] = 1.f / (1.f + expf(-z));
+                key[j] = val[j] + (bias ? bias[i] : 0.f);
+            }
+            mx = fmaxf(mx, z);
+        } else {
+            val[j] = 0.f;
+            key[j] = -3.0e38f;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float picked = 0.f, sum = mode == B200Q_ROUTE_SOFTMAX ? 0.f : 1e-20f;
+    int pick_i = 0;
+    for (int kk = 0; kk < topk; kk++) {
+        float bv = -3.4e38f;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            const int i = lane + 32 * j;
+            if (i < E && key[j] > bv) { bv = key[j]; bi = i; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        float pv = 0.f;
+#pragma unroll
+        for (int j = 0; j < 16; j++)
+            if (lane + 32 * j == bi) { pv = val[j]; key[j] = -3.4e38f; }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) pv += __shfl_xor_sync(0xffffffffu, pv, o);   // only one lane is non-zero
+        if (mode == B200Q_ROUTE_SOFTMAX) pv = expf(pv - mx);
+        sum += pv;
+        if (lane == kk) { picked = pv; pick_i = bi; }
+    }
+    if (lane < topk) {
+        ridx[t * topk + lane] = pick_i;
+        rw[t * topk + lane] = mode == B200Q_ROUTE_SOFTMAX ? picked / sum : picked / sum * scale;
+    }
+}
+
+__global__ void route_k(const void* __restrict__ logits, int dtype, int ldl, const float* __restrict__ bias, int T, int E,
+                        int topk, int mode, float scale, int* __restrict__ ridx, float* __restrict__ rw) {
+    pdl_wait();
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t < T) route_token(logits, dtype, ldl, bias, E, topk, mode, scale, t, threadIdx.x & 31, ridx, rw);
+    pdl_trigger();
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// grouping (moe_group_k's counting sort, bolt_kernels.cu:275-325), deterministic: thread e collects the pairs of
+// expert e in increasing pair order.  One CTA of 512 threads, E <= 512, pairs <= 4096.  extra > 0 appends a slot
+// E with ids pairs .. pairs + extra - 1 (the shared expert over every token).
+// ---------------------------------------------------------------------------------------------------------
+__device__ void group_pairs(const int* ridx_s, int pairs, int E, int extra, int* counts, int* offsets, int* order,
+                            int* scan_s) {
+    const int tid = threadIdx.x;
+    int c = 0;
+    if (tid < E)
+        for (int p = 0; p < pairs; p++) c += ridx_s[p] == tid;
+    scan_s[tid] = tid < E ? c : 0;
+    __syncthreads();
+    for (int off = 1; off < 512; off <<= 1) {
+        const int v = tid >= off ? scan_s[tid - off] : 0;
+        __syncthreads();
+        scan_s[tid] += v;
+        __syncthreads();
+    }
+    const int start = scan_s[tid] - (tid < E ? c : 0);
+    if (tid < E) {
+        counts[tid] = c;
+        offsets[tid] = start;
+        int w = start;
+        for (int p = 0; p < pairs; p++)
+            if (ridx_s[p] == tid) order[w++] = p;
+    }
+    if (tid == 0) {
+        offsets[E] = pairs;
+        if (extra > 0) { counts[E] = extra; offsets[E + 1] = pairs + extra; }
+    }
+    for (int i = tid; i < extra; i += blockDim.x) order[pairs + i] = pairs + i;
+}
+
+__global__ void __launch_bounds__(512) group_k(const int* __restrict__ ridx, int pairs, int E, int* __restrict__ counts,
+                                               int* __restrict__ offsets, int* __restrict__ order) {
+    pdl_wait();
+    __shared__ int ridx_s[4096];
+    __shared__ int scan_s[512];
+    for (int i = threadIdx.x; i < pairs; i += blockDim.x) ridx_s[i] = ridx[i];
+    __syncthreads();
+    group_pairs(ridx_s, pairs, E, 0, counts, offsets, order, scan_s);
+    pdl_trigger();
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// decode prologue, one launch: block 0 routes every token (a warp per token) and groups the pairs; the other
+// blocks write the int8 rows of x (a warp per 32-group).
+// ---------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(512) moe_prep_k(const void* __restrict__ x, const void* __restrict__ logits, int T, int H,
+                                                  int E, int topk, int route, const float* __restrict__ bias, float scale,
+                                                  int extra, int* __restrict__ ridx, float* __restrict__ rw,
+                                                  int* __restrict__ counts, int* __restrict__ offsets, int* __restrict__ order,
+                                                  int8_t* __restrict__ xq, float* __restrict__ xs) {
+    pdl_wait();
+    __shared__ int ridx_s[4096];
+    __shared__ int scan_s[512];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (blockIdx.x == 0) {
+        for (int t = warp; t < T; t += 16) route_token(logits, B200Q_BF16, E, bias, E, topk, route, scale, t, lane, ridx, rw);
+        __syncthreads();
+        __threadfence_block();
+        for (int i = threadIdx.x; i < T * topk; i += blockDim.x) ridx_s[i] = ridx[i];
+        __syncthreads();
+        group_pairs(ridx_s, T * topk, E, extra, counts, offsets, order, scan_s);
+    } else {
+        const int groups = H >> 5;
+        const int gw = (blockIdx.x - 1) * 16 + warp;
+        if (gw < T * groups) {
+            const int r = gw / groups, g = gw - r * groups;
+            const float v = load_act(x, B200Q_BF16, (size_t)r * H + g * 32 + lane);
+            quant_group(v, lane, xq + (size_t)r * H + g * 32, xs + (size_t)r * (H >> 5) + g);
+        }
+    }
+    pdl_trigger();
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// combine (combine_k, bolt_kernels.cu:1714-1727): out[t][h] = sum_k rw[t][k] mo[t*topk+k][h] (+ shared[t][h])
+// ---------------------------------------------------------------------------------------------------------
+__global__ void combine_k(const float* __restrict__ mo, const float* __restrict__ rw, const float* __restrict__ shared, int T,
+                          int topk, int H, void* __restrict__ out, int out_dtype) {
+    pdl_wait();
+    const int t = blockIdx.y;
+    const int h4 = blockIdx.x * blockDim.x + threadIdx.x;
+    if (h4 * 4 < H) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int kk = 0; kk < topk; kk++) {
+            const float wk = rw[t * topk + kk];
+            const float4 v = reinterpret_cast<const float4*>(mo + ((size_t)t * topk + kk) * H)[h4];
+            acc.x = fmaf(wk, v.x, acc.x); acc.y = fmaf(wk, v.y, acc.y);
+            acc.z = fmaf(wk, v.z, acc.z); acc.w = fmaf(wk, v.w, acc.w);
+        }
+        if (shared) {
+            const float4 sv = reinterpret_cast<const float4*>(shared + (size_t)t * H)[h4];
+            acc.x += sv.x; acc.y += sv.y; acc.z += sv.z; acc.w += sv.w;
+        }
+        if (out_dtype == B200Q_BF16) {
+            __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(out) + (size_t)t * H) + 2 * h4;
+            o[0] = __floats2bfloat162_rn(acc.x, acc.y);
+            o[1] = __floats2bfloat162_rn(acc.z, acc.w);
+        } else {
+            reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)t * H)[h4] = acc;
+        }
+    }
+    pdl_trigger();
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// workspace of the decode layer (256-byte aligned pieces)
+// ---------------------------------------------------------------------------------------------------------
+struct DecodeWs {
+    int* ridx; float* rw; int* counts; int* offsets; int* order;
+    int8_t* xq; float* xs; int8_t* aq; float* as; float* mo;
+    size_t bytes;
+};
+static size_t al(size_t v) { return (v + 255) & ~(size_t)255; }
+static DecodeWs decode_ws(char* base, int T, int H, int F, int E, int topk) {
+    const size_t pairs = (size_t)T * topk, ids = pairs + T;
+    DecodeWs w;
+    size_t o = 0;
+    w.ridx = (int*)(base + o); o += al(pairs * 4);
+    w.rw = (float*)(base + o); o += al(pairs * 4);
+    w.counts = (int*)(base + o); o += al((size_t)(E + 1) * 4);
+    w.offsets = (int*)(base + o); o += al((size_t)(E + 2) * 4);
+    w.order = (int*)(base + o); o += al(ids * 4);
+    w.xq = (int8_t*)(base + o); o += al((size_t)T * H);
+    w.xs = (float*)(base + o); o += al((size_t)T * (H / 32) * 4);
+    w.aq = (int8_t*)(base + o); o += al(ids * F);
+    w.as = (float*)(base + o); o += al(ids * (F / 32) * 4);
+    w.mo = (float*)(base + o); o += al(ids * H * 4);
+    w.bytes = o;
+    return w;
+}
+
+}  // namespace b200q
+
+using namespace b200q;
+
+extern "C" {
+
+int b200q_abi(void) { return B200Q_ABI; }
+int b200q_last_cuda_error(void) { return g_last_cuda; }
+const char* b200q_strerror(int status) {
+    switch (status) {
+        case B200Q_OK: return "ok";
+        case B200Q_EINVAL: return "invalid argument (null pointer, shape or alignment)";
+        case B200Q_ENOSPACE: return "workspace or capacity too small";
+        case B200Q_ECUDA: return "CUDA launch error (see b200q_last_cuda_error)";
+        default: return "unknown status";
+    }
+}
+
+int b200q_quant_rows(const void* x, int x_dtype, int ldx, int8_t* q, int ldq, float* s, int lds, int rows, int k,
+                     void* stream) {
+    if (!x || !q || !s || rows < 0 || k <= 0 || k % 32 || ldx < k || ldq < k || lds < k / 32 ||
+        (x_dtype != B200Q_F32 && x_dtype != B200Q_BF16))
+        return B200Q_EINVAL;
+    if (rows == 0) return B200Q_OK;
+    const int64_t warps = (int64_t)rows * (k / 32);
+    launch(quant_rows_k, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, (cudaStream_t)stream, x, x_dtype, ldx, q, ldq, s,
+           lds, rows, k);
+    return launched();
+}
+
+int b200q_route(const void* logits, int l_dtype, int ldl, const float* bias, int T, int E, int topk, int mode,
+                float scale, int* ridx, float* rw, void* stream) {
+    if (!logits || !ridx || !rw || T < 0 || E <= 0 || E > 512 || topk <= 0 || topk > 16 || topk > E || ldl < E ||
+        (mode != B200Q_ROUTE_SOFTMAX && mode != B200Q_ROUTE_SIGMOID) || (l_dtype != B200Q_F32 && l_dtype != B200Q_BF16))
+        return B200Q_EINVAL;
+    if (T == 0) return B200Q_OK;
+    launch(route_k, dim3((T + 7) / 8), dim3(256), 0, (cudaStream_t)stream, logits, l_dtype, ldl, bias, T, E, topk, mode,
+           scale, ridx, rw);
+    return launched();
+}
+
+int b200q_moe_group(const int* ridx, int pairs, int E, int* counts, int* offsets, int* order, void* stream) {
+    if (!ridx || !counts || !offsets || !order || pairs < 0 || pairs > 4096 || E <= 0 || E > 512) return B200Q_EINVAL;
+    launch(group_k, dim3(1), dim3(512), 0, (cudaStream_t)stream, ridx, pairs, E, counts, offsets, order);
+    return launched();
+}
+
+int b200q_combine(const float* mo, const float* rw, const float* shared, int T, int topk, int H, void* out, int out_dtype,
+                  void* stream) {
+    if (!mo || !rw || !out || T < 0 || topk <= 0 || H <= 0 || H % 4 || (out_dtype != B200Q_F32 && out_dtype != B200Q_BF16))
+        return B200Q_EINVAL;
+    if (T == 0) return B200Q_OK;
+    launch(combine_k, dim3((H / 4 + 255) / 256, T), dim3(256), 0, (cudaStream_t)stream, mo, rw, shared, T, topk, H, out,
+           out_dtype);
+    return launched();
+}
+
+size_t b200q_moe_decode_workspace_bytes(int T, int H, int F, int E, int topk) {
+    if (T <= 0 || H <= 0 || F <= 0 || E <= 0 || topk <= 0) return 0;
+    return decode_ws(nullptr, T, H, F, E, topk).bytes;
+}
+
+int b200q_moe_decode(const void* x, const void* logits, const void* up, const void* down, const void* shared_up,
+                     const void* shared_down, int T, int H, int F, int E, int topk, int route, const float* bias,
+                     float scale, void* out, int out_dtype, void* workspace, size_t workspace_bytes, int* ridx_out,
+                     float* rw_out, void* const* stage_events, void* stream) {
+    if (!x || !logits || !up || !down || !out || !workspace || T <= 0 || T > 64 || E <= 0 || E > 512 || topk <= 0 ||
+        topk > 16 || topk > E || !iq2_shape_ok(F, H) || !iq2_shape_ok(H, F) || ((shared_up == nullptr) != (shared_down == nullptr)) ||
+        (route != B200Q_ROUTE_SOFTMAX && route != B200Q_ROUTE_SIGMOID) || (out_dtype != B200Q_F32 && out_dtype != B200Q_BF16) ||
+        ((uintptr_t)workspace & 255))
+        return B200Q_EINVAL;
+    DecodeWs w = decode_ws((char*)workspace, T, H, F, E, topk);
+    if (workspace_bytes < w.bytes) return B200Q_ENOSPACE;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int pairs = T * topk;
+    const int extra = shared_up ? T : 0;
+    const int nslots = E + (extra ? 1 : 0);
+    const int maxcnt = T;
+    int st;
+    auto mark = [&](int i) { if (stage_events) cudaEventRecord((cudaEvent_t)stage_events[i], s); };
+
+    mark(0);
+    // 1. router + grouping (block 0) and the int8 rows of x (the rest)
+    const int qwarps = T * (H / 32);
+    launch(moe_prep_k, dim3(1 + (qwarps + 15) / 16), dim3(512), 0, s, x, logits, T, H, E, topk, route, bias, scale, extra,
+           w.ridx, w.rw, w.counts, w.offsets, w.order, w.xq, w.xs);
+    if ((st = launched()) != B200Q_OK) return st;
+    mark(1);
+
+    // 2. up, relu^2, int8 rows of the result: ids < pairs read token id / topk, the shared ids pairs + t read token t
+    GemvArgs a = {};
+    a.slab = (const uint8_t*)up; a.expert_bytes = iq2_bytes(F, H); a.extra_w = (const uint8_t*)shared_up;
+    a.nslot_routed = E; a.n = F; a.k = H; a.counts = w.counts; a.offsets = w.offsets; a.order = w.order;
+    a.act_div = topk; a.act_split = pairs; a.act_base = 0; a.xq = w.xq; a.xs = w.xs; a.aq = w.aq; a.as = w.as;
+    if ((st = status_from(launch_iq2_gemv(a, nslots, maxcnt, 2, s))) != B200Q_OK) return st;
+    mark(2);
+
+    // 3. down over the int8 rows of every id
+    GemvArgs b = {};
+    b.slab = (const uint8_t*)down; b.expert_bytes = iq2_bytes(H, F); b.extra_w = (const uint8_t*)shared_down;
+    b.nslot_routed = E; b.n = H; b.k = F; b.counts = w.counts; b.offsets = w.offsets; b.order = w.order;
+    b.act_div = 1; b.act_split = 1 << 30; b.xq = w.aq; b.xs = w.as; b.y = w.mo; b.ldy = H;
+    if ((st = status_from(launch_iq2_gemv(b, nslots, maxcnt, 0, s))) != B200Q_OK) return st;
+    mark(3);
+
+    // 4. combine + the shared expert's rows
+    launch(combine_k, dim3((H / 4 + 255) / 256, T), dim3(256), 0, s, (const float*)w.mo, (const float*)w.rw,
+           extra ? (const float*)(w.mo + (size_t)pairs * H) : (const float*)nullptr, T, topk, H, out, out_dtype);
+    if ((st = launched()) != B200Q_OK) return st;
+    mark(4);
+    if (ridx_out) {
+        if (cudaMemcpyAsync(ridx_out, w.ridx, sizeof(int) * pairs, cudaMemcpyDeviceToDevice, s) != cudaSuccess) return status_from(cudaGetLastError());
+    }
+    if (rw_out) {
+        if (cudaMemcpyAsync(rw_out, w.rw, sizeof(float) * pairs, cudaMemcpyDeviceToDevice, s) != cudaSuccess) return status_from(cudaGetLastError());
+    }
+    return B200Q_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,68 @@
+"""CPU tests of the C ABI: the library loads, exports every entry point include/b200q.h declares, validates its
+arguments before touching the GPU, and its host-side generator is deterministic."""
+import ctypes
+import os
+import re
+
+import numpy as np
+
+import b200q
+from conftest import ROOT
+
+
+def declared_symbols():
+    text = open(os.path.join(ROOT, "include", "b200q.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(b200q_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    L = ctypes.CDLL(b200q.LIB_PATH)
+    names = declared_symbols()
+    assert len(names) >= 20
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+
+
+def test_abi_and_strerror():
+    L = b200q.lib()
+    assert L.b200q_abi() == 1
+    assert L.b200q_strerror(b200q.EINVAL).startswith(b"invalid")
+
+
+def test_bad_arguments_fail_before_any_launch():
+    L = b200q.lib()
+    null = None
+    assert L.b200q_iq2_pack(null, null, 32, 256, null) == b200q.EINVAL
+    buf = ctypes.create_string_buffer(64)
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    assert L.b200q_iq2_pack(p, p, 31, 256, null) == b200q.EINVAL       # rows not a multiple of 32
+    assert L.b200q_iq2_pack(p, p, 32, 300, null) == b200q.EINVAL       # k not a multiple of 256
+    assert L.b200q_route(p, 1, 128, null, 4, 600, 6, 0, 1.0, p, p, null) == b200q.EINVAL   # E > 512
+    assert L.b200q_route(p, 1, 128, null, 4, 128, 20, 0, 1.0, p, p, null) == b200q.EINVAL  # topk > 16
+    assert L.b200q_moe_group(p, 5000, 128, p, p, p, null) == b200q.EINVAL
+    assert L.b200q_quant_rows(p, 0, 64, p, 64, p, 2, 4, 48, null) == b200q.EINVAL         # k % 32
+    # workspace too small / misaligned
+    ws = L.b200q_moe_decode_workspace_bytes(16, 4096, 2048, 128, 6)
+    assert ws > 16 * 6 * 4096 * 4
+    assert L.b200q_moe_decode(p, p, p, p, null, null, 16, 4096, 2048, 128, 6, 0, null, 1.0, p, 0,
+                              ctypes.c_void_p(256), ws - 1, null, null, null, null) == b200q.ENOSPACE
+    assert L.b200q_moe_decode(p, p, p, p, null, null, 16, 4096, 2048, 128, 6, 0, null, 1.0, p, 0,
+                              ctypes.c_void_p(257), ws, null, null, null, null) == b200q.EINVAL
+    assert L.b200q_moe_decode(p, p, p, p, p, null, 16, 4096, 2048, 128, 6, 0, null, 1.0, p, 0,
+                              ctypes.c_void_p(256), ws, null, null, null, null) == b200q.EINVAL   # half a shared expert
+
+
+def test_host_generator_is_deterministic_and_in_range():
+    a = b200q.synth_iq2_host(7, 100)
+    b = b200q.synth_iq2_host(7, 100)
+    c = b200q.synth_iq2_host(8, 100)
+    assert np.array_equal(a, b) and not np.array_equal(a, c)
+    blocks = a.reshape(100, 66)
+    d = blocks[:, :2].copy().view(np.float16).astype(np.float32)[:, 0]
+    assert (d >= 9.99e-4).all() and (d <= 1.001e-2).all()
+    qy = np.stack([blocks[:, 6 + 8 * c:10 + 8 * c].copy().view(np.uint32)[:, 0] for c in range(8)], 1)
+    s4 = qy >> 28
+    assert s4.min() == 0 and s4.max() == 15
+    # block i depends only on (seed, i)
+    assert np.array_equal(b200q.synth_iq2_host(7, 10), a[:660])
