@@ -180,6 +180,8 @@ def run_ours(args, rank, world, local_rank):
 
     # ---- per-kernel durations (a second pass with events between the four launches)
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    for e in evs:
+        e.record(stream)      # torch creates the CUDA event on its first record
     stage_ms = np.zeros(4)
     nprof = max(args.steps, 4)
     for i in range(nprof):

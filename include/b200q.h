@@ -17,8 +17,8 @@
  * Weight layouts.  The packers take the checkpoint's raw bytes (already on the device) and write this library's
  * layouts (same byte counts):
  *     IQ2_XXS  ggml blocks [rows][k/256][66]       -> b200q_iq2_pack      (n % 32 == 0, k % 256 == 0)
- *     Q8_0     ggml blocks [rows][k/32][34]        -> b200q_q8_pack       (n % 32 == 0, k % 256 == 0)
- *     NVFP4    q [rows][k/2], sc [rows][k/16] e4m3 -> b200q_nv4_pack      (n % 32 == 0, k % 256 == 0)
+ *     Q8_0     ggml blocks [rows][k/32][34]        -> b200q_q8_pack       (n % 16 == 0, k % 256 == 0)
+ *     NVFP4    q [rows][k/2], sc [rows][k/16] e4m3 -> b200q_nv4_pack      (n % 16 == 0, k % 256 == 0)
  * A slab of experts is packed as one matrix of experts*rows rows (every expert's rows are a multiple of 32), so
  * expert e starts at e * b200q_iq2_bytes(rows, k).
  */
@@ -63,13 +63,30 @@ size_t b200q_iq2_bytes(int64_t n, int k);
  * (bolt_mma.cu:1336-1361): ggml blocks [n][k/256][66] -> the rt32 layout.  raw and packed must not overlap. */
 int b200q_iq2_pack(const void* raw, void* packed, int64_t n, int k, void* stream);
 
+/* Bytes of a Q8_0 matrix: n*k/32*34.  Replaces tile_q8 (bolt_mma.cu:1270-1311, via load_q8 bolt_host.cu:198-217):
+ * ggml blocks [n][k/32][34] -> the t16 layout. */
 size_t b200q_q8_bytes(int64_t n, int k);
-/* Replaces tile_q8 (bolt_mma.cu:1270-1311, via load_q8 bolt_host.cu:198-217). */
 int b200q_q8_pack(const void* raw, void* packed, int64_t n, int k, void* stream);
 
+/* Bytes of an NVFP4 matrix: n*k/2 + n*k/16.  Replaces tile_nv4 / tile_nv4w (bolt_mma.cu:1231-1268, 892-923, via
+ * load_nv4 bolt_host.cu:219-264): q [n][k/2] (low nibble first) and sc [n][k/16] e4m3 -> the t16 layout. */
 size_t b200q_nv4_bytes(int64_t n, int k);
-/* Replaces tile_nv4 / tile_nv4w (bolt_mma.cu:1231-1268, 892-923, via load_nv4 bolt_host.cu:219-264). */
 int b200q_nv4_pack(const void* q, const void* sc, void* packed, int64_t n, int k, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * NVFP4 and Q8_0 decode GEMVs: y[t][n] = W[n] . x[t] for T <= 16 rows, x fp32 or bf16 [T][ldx], y fp32 [T][ldy].
+ * NVFP4: y = s2 * sum e2m1 * e4m3 * x (exact products, fp32 sums), replacing mma_nv4 (bolt_mma.cu:1190) at decode
+ * and verify row counts.  Q8_0: y = sum (q * d) * x, replacing mma_q8 (bolt_mma.cu:1194) and gemv_q8
+ * (bolt_kernels.cu:228-231).  K is split across CTAs; the fp32 partials go to `workspace`
+ * (>= b200q_*_gemv_workspace_bytes, 0 when no split is needed) and are summed in a fixed order.  A NULL or small
+ * workspace runs without the split (slower, same result order).
+ * --------------------------------------------------------------------------------------------------------- */
+size_t b200q_nv4_gemv_workspace_bytes(int n, int k, int T);
+int b200q_nv4_gemv(const void* w, float s2, int n, int k, const void* x, int x_dtype, int ldx, int T, float* y, int ldy,
+                   void* workspace, size_t workspace_bytes, void* stream);
+size_t b200q_q8_gemv_workspace_bytes(int n, int k, int T);
+int b200q_q8_gemv(const void* w, int n, int k, const void* x, int x_dtype, int ldx, int T, float* y, int ldy,
+                  void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------
  * Router, grouping, activation quantisation, combine.

@@ -56,6 +56,12 @@ def lib():
                                        vp, vp, vp, vp]),
             "b200q_synth_iq2_host": (None, [ctypes.c_uint64, i64, vp]),
             "b200q_synth_iq2": (i32, [ctypes.c_uint64, i64, vp, vp]),
+            "b200q_nv4_bytes": (sz, [i64, i32]), "b200q_nv4_pack": (i32, [vp, vp, vp, i64, i32, vp]),
+            "b200q_q8_bytes": (sz, [i64, i32]), "b200q_q8_pack": (i32, [vp, vp, i64, i32, vp]),
+            "b200q_nv4_gemv_workspace_bytes": (sz, [i32, i32, i32]),
+            "b200q_nv4_gemv": (i32, [vp, f32, i32, i32, vp, i32, i32, i32, vp, i32, vp, sz, vp]),
+            "b200q_q8_gemv_workspace_bytes": (sz, [i32, i32, i32]),
+            "b200q_q8_gemv": (i32, [vp, i32, i32, vp, i32, i32, i32, vp, i32, vp, sz, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -209,6 +215,60 @@ def moe_down(slab, E, n, k, counts, offsets, order, aq, as_):
     _check(lib().b200q_moe_down(_p(slab), E, n, k, _p(counts), _p(offsets), _p(order), _p(aq), _p(as_), _p(y), n, _s()),
            "moe_down")
     return y[:pairs]
+
+
+# -------------------------------------------------------------------------------------------------------------
+# NVFP4 and Q8_0 (tile_nv4 / tile_q8 packing; mma_nv4 / mma_q8 at decode row counts)
+# -------------------------------------------------------------------------------------------------------------
+def tile_nv4(q, sc, n, k):
+    """NVFP4 q [n][k/2] and e4m3 sc [n][k/16] (uint8 CUDA tensors) -> the t16 layout."""
+    out = torch.empty(lib().b200q_nv4_bytes(n, k), dtype=torch.uint8, device=q.device)
+    _check(lib().b200q_nv4_pack(_p(_dev(q, "q")), _p(_dev(sc, "sc")), _p(out), n, k, _s()), "tile_nv4")
+    return out
+
+
+def tile_q8(raw, n, k):
+    """Q8_0 ggml blocks [n][k/32][34] (uint8 CUDA tensor) -> the t16 layout."""
+    out = torch.empty(lib().b200q_q8_bytes(n, k), dtype=torch.uint8, device=raw.device)
+    _check(lib().b200q_q8_pack(_p(_dev(raw, "raw")), _p(out), n, k, _s()), "tile_q8")
+    return out
+
+
+class _Workspace:
+    def __init__(self):
+        self.buf = None
+
+    def get(self, nbytes, device):
+        if nbytes == 0:
+            return None, 0
+        if self.buf is None or self.buf.numel() < nbytes or self.buf.device != device:
+            self.buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        return ctypes.c_void_p(self.buf.data_ptr()), self.buf.numel()
+
+
+_WS = _Workspace()
+
+
+def mma_nv4(w, s2, n, k, x, y=None):
+    """y [T][n] fp32 = s2 * W . x for T <= 16 rows of x (fp32 or bf16)."""
+    _dev(x, "x")
+    T = x.shape[0]
+    y = torch.empty(T, n, dtype=torch.float32, device=x.device) if y is None else y
+    ws, wb = _WS.get(lib().b200q_nv4_gemv_workspace_bytes(n, k, T), x.device)
+    _check(lib().b200q_nv4_gemv(_p(w), float(s2), n, k, _p(x), _dtype_code(x), x.stride(0), T, _p(y), y.stride(0), ws, wb,
+                                _s()), "mma_nv4")
+    return y
+
+
+def mma_q8(w, n, k, x, y=None):
+    """y [T][n] fp32 = W . x for T <= 16 rows of x (fp32 or bf16)."""
+    _dev(x, "x")
+    T = x.shape[0]
+    y = torch.empty(T, n, dtype=torch.float32, device=x.device) if y is None else y
+    ws, wb = _WS.get(lib().b200q_q8_gemv_workspace_bytes(n, k, T), x.device)
+    _check(lib().b200q_q8_gemv(_p(w), n, k, _p(x), _dtype_code(x), x.stride(0), T, _p(y), y.stride(0), ws, wb, _s()),
+           "mma_q8")
+    return y
 
 
 # -------------------------------------------------------------------------------------------------------------

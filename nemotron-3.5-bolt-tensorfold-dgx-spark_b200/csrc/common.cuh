@@ -50,31 +50,22 @@ int status_from(cudaError_t e);
 inline int launched() { return status_from(cudaGetLastError()); }
 
 // ---------------------------------------------------------------------------------------------------------
-// IQ2_XXS device layout ("rt32"): rows in tiles of 32, so that lane l of a warp owns row 32*t + l and one
-// 16-byte load of every lane fetches two consecutive 32-weight chunks of each of the warp's 32 rows (512
-// contiguous bytes a warp).
-//   qs  [n/32][k/64][32][16 B]   lane l's 16 bytes: chunks 2j, 2j+1 of its row; each chunk is ggml's 8 bytes
-//                                (4 grid-index bytes, then a u32 of four 7-bit sign indices + the 4-bit sub-scale)
-//   d   [n/32][k/256][32] fp16   the super-block scale of each row
-// The two planes share one buffer: qs first (n*k/4 bytes), then d (n*k/128 bytes); n*k/256*66 bytes in all, the
-// same bytes as ggml's blocks.  A slab of E experts is E such buffers back to back.
+// IQ2_XXS device layout ("rt32"): rows in tiles of 32, so that lane l of a warp owns row 32*t + l.  Every
+// (row tile t, super-block b of 256 k) is one contiguous unit of 2112 bytes:
+//   [4 chunk pairs j][32 lanes][16 B]   lane l's 16 bytes: chunks 2j, 2j+1 of its row in the super-block; each
+//                                       chunk is ggml's 8 bytes (4 grid-index bytes, then a u32 of four 7-bit sign
+//                                       indices + the 4-bit sub-scale in bits 28-31)
+//   [32 lanes] fp16                     the super-block scale d of each row
+// Units are ordered t-major: unit (t, b) at (t * k/256 + b) * 2112.  A warp's step over one super-block reads 2112
+// contiguous bytes; n*k/256*66 bytes in all, ggml's byte count.  A row tile is self-contained, so a slab of E
+// experts of n rows (n % 32 == 0) packed as one matrix of E*n rows has expert e at e * iq2_bytes(n, k).
 // ---------------------------------------------------------------------------------------------------------
 constexpr int kIq2Tile = 32;
-__host__ __device__ inline size_t iq2_qs_bytes(int64_t n, int k) { return (size_t)n * (size_t)(k / 4); }
+constexpr int kIq2Unit = 2112;   // bytes of a (32-row tile, 256-k super-block) unit
 __host__ __device__ inline size_t iq2_bytes(int64_t n, int k) { return (size_t)n * (size_t)(k / 256) * 66; }
 
-// Q8_0 device layout ("rt32"): rows in tiles of 32; lane l owns row 32*t + l.
-//   q  [n/32][k/32][32][32 B]  the row's 32 int8 of block b
-//   d  [n/32][k/32][32] fp16
-// n*k/32*34 bytes in all.
-__host__ __device__ inline size_t q8_q_bytes(int64_t n, int k) { return (size_t)n * (size_t)k; }
+// Q8_0 and NVFP4 device layouts ("t16", tiles of 16 rows in the tensor cores' A-fragment order): gemv_tc.cu.
 __host__ __device__ inline size_t q8_bytes(int64_t n, int k) { return (size_t)n * (size_t)(k / 32) * 34; }
-
-// NVFP4 device layout ("rt32"): rows in tiles of 32; lane l owns row 32*t + l.
-//   q   [n/32][k/32][32][16 B]  32 e2m1 nibbles of the row (element 2j low nibble of byte j)
-//   sc  [n/32][k/32][32][2 B]   the two e4m3 scales of those 32 elements
-// n*k*9/16 bytes in all; the fp32 tensor scale is an argument.
-__host__ __device__ inline size_t nv4_q_bytes(int64_t n, int k) { return (size_t)n * (size_t)(k / 2); }
 __host__ __device__ inline size_t nv4_bytes(int64_t n, int k) { return (size_t)n * (size_t)(k / 2) + (size_t)n * (size_t)(k / 16); }
 
 }  // namespace b200q

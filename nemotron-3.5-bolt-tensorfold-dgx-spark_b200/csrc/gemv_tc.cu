@@ -1,0 +1,423 @@
+// NVFP4 and Q8_0 decode GEMVs (T <= 16 activation rows): HBM-streaming, the dequantised weights fed to the tensor
+// cores as the A operand of mma.m16n8k16 (fp16 in, fp32 accumulate), the activation rows as B.
+//
+// Numerics (exact operands, fp32 sums):
+//   NVFP4  a = e2m1 * e4m3 scale, exact in fp16 (2 + 4 significant bits, the scale range 2^-9..448), the tensor
+//          scale s2 applied to the fp32 result: the arithmetic of libbolt's PNV4 policy (bolt_mma.cu:98-175).
+//   Q8_0   a = the int8 itself (exact in fp16); the per-32 scale d multiplies the fp32 partial of each 32-block,
+//          FmtQ8's w = q * d (bolt_kernels.cu:41-52) with no rounding of the product (libbolt's PQ8 rounds
+//          q * d to fp16, bolt_mma.cu:234-254).
+//   The activations are converted to fp16 once (exact for bf16 inputs in fp16's normal range).
+// Mapping: a warp owns one 16-row tile over one K slice; the eight warps of a CTA own eight consecutive tiles and
+// share the slice's activations in shared memory.  grid.y splits K so that about four CTAs run per SM; the slices'
+// fp32 partials are summed in slice order by a second kernel, so results do not depend on timing.
+#include "common.cuh"
+
+namespace b200q {
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(s));
+    return d;
+}
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+// two e4m3 bytes (low byte -> low half) to f16x2, exact
+__device__ __forceinline__ uint32_t e4m3x2_f16x2(uint32_t v) {
+    uint32_t d;
+    asm("{ .reg .b16 t; cvt.u16.u32 t, %1; cvt.rn.f16x2.e4m3x2 %0, t; }" : "=r"(d) : "r"(v));
+    return d;
+}
+__device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint2 ldg_stream2(const void* p) {
+    uint2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t ldg_stream1(const void* p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// layouts ("t16"): rows in tiles of 16; lane (g, t) = (lane / 4, lane % 4) holds the m16n8k16 A fragment
+//   a0 = (row g, k 2t..2t+1)  a1 = (row g+8, k 2t..)  a2 = (row g, k 2t+8..)  a3 = (row g+8, k 2t+8..)
+// NVFP4: unit (tile, 64-k step s) = 576 B: [32 lanes][4 words] then [8 g][8 B].  Word j of a lane covers k16
+//   step j: nibble i (i < 4) is the low element of a_i and nibble i+4 its high element.  The 8 bytes of group g
+//   are the e4m3 scales of row g for the step's four 16-blocks, then those of row g+8.
+// Q8_0: unit (tile, 32-k block b) = 544 B: [32 lanes][16 B] then [8 g][2 x fp16].  Bytes 8u..8u+7 of a lane are
+//   a0, a1, a2, a3 (two int8 each, low k first) of k16 step u; group g's word holds d of row g, then of row g+8.
+// ---------------------------------------------------------------------------------------------------------
+constexpr int kNv4Unit = 576, kQ8Unit = 544;
+
+__global__ void nv4_pack_k(const uint8_t* __restrict__ q, const uint8_t* __restrict__ sc, uint8_t* __restrict__ out, int n, int k) {
+    pdl_wait();
+    const int steps = k / 64;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < (int64_t)(n / 16) * steps * 32) {
+        const int lane = (int)(i & 31);
+        const int64_t unit = i >> 5;
+        const int tile = (int)(unit / steps), s = (int)(unit % steps);
+        const int g = lane >> 2, t = lane & 3;
+        auto nib = [&](int row, int kk) { return (uint32_t)(q[(size_t)row * (k / 2) + kk / 2] >> (4 * (kk & 1))) & 15u; };
+        uint32_t w[4];
+        for (int j = 0; j < 4; j++) {
+            const int k0 = 64 * s + 16 * j + 2 * t;
+            const int rr[4] = {16 * tile + g, 16 * tile + g + 8, 16 * tile + g, 16 * tile + g + 8};
+            const int kk[4] = {k0, k0, k0 + 8, k0 + 8};
+            uint32_t v = 0;
+            for (int r = 0; r < 4; r++) v |= nib(rr[r], kk[r]) << (4 * r) | nib(rr[r], kk[r] + 1) << (4 * (r + 4));
+            w[j] = v;
+        }
+        uint8_t* u = out + (size_t)unit * kNv4Unit;
+        reinterpret_cast<uint4*>(u)[lane] = make_uint4(w[0], w[1], w[2], w[3]);
+        if (t == 0) {
+            for (int h = 0; h < 2; h++)
+                for (int j = 0; j < 4; j++) u[512 + 8 * g + 4 * h + j] = sc[(size_t)(16 * tile + g + 8 * h) * (k / 16) + 4 * s + j];
+        }
+    }
+    pdl_trigger();
+}
+
+__global__ void q8_pack_k(const uint8_t* __restrict__ raw, uint8_t* __restrict__ out, int n, int k) {
+    pdl_wait();
+    const int nb = k / 32;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < (int64_t)(n / 16) * nb * 32) {
+        const int lane = (int)(i & 31);
+        const int64_t unit = i >> 5;
+        const int tile = (int)(unit / nb), b = (int)(unit % nb);
+        const int g = lane >> 2, t = lane & 3;
+        auto val = [&](int row, int kk) { return raw[((size_t)row * nb + b) * 34 + 2 + kk]; };
+        uint8_t* u = out + (size_t)unit * kQ8Unit;
+        for (int uu = 0; uu < 2; uu++) {
+            const int k0 = 16 * uu + 2 * t;
+            const int rr[4] = {16 * tile + g, 16 * tile + g + 8, 16 * tile + g, 16 * tile + g + 8};
+            const int kk[4] = {k0, k0, k0 + 8, k0 + 8};
+            for (int r = 0; r < 4; r++) {
+                u[16 * lane + 8 * uu + 2 * r] = val(rr[r], kk[r]);
+                u[16 * lane + 8 * uu + 2 * r + 1] = val(rr[r], kk[r] + 1);
+            }
+        }
+        if (t == 0) {
+            for (int h = 0; h < 2; h++) {
+                const uint8_t* blk = raw + ((size_t)(16 * tile + g + 8 * h) * nb + b) * 34;
+                u[512 + 4 * g + 2 * h] = blk[0];
+                u[512 + 4 * g + 2 * h + 1] = blk[1];
+            }
+        }
+    }
+    pdl_trigger();
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// the GEMV
+// ---------------------------------------------------------------------------------------------------------
+struct TcArgs {
+    const uint8_t* w;
+    int n, k;
+    const void* x;
+    int x_dtype, ldx, T;
+    int L;          // K slice of a CTA (multiple of 256)
+    float s2;       // NVFP4 tensor scale (1 for Q8_0)
+    float* out;     // KS == 1: y [T][ldy]; else partials [KS][T][n]
+    int ldo;
+};
+
+constexpr int kTcWarps = 8;
+enum { kFmtNv4 = 0, kFmtQ8 = 1 };
+
+// the four A fragments of one NVFP4 k16 step from word `w`, scaled by (sg, sg8) = the step's scales of rows g, g+8
+__device__ __forceinline__ void nv4_frag(uint32_t w, uint32_t hg, uint32_t hg8, uint32_t (&a)[4]) {
+    // fp16 high bytes of the magnitudes 0, .5, 1, 1.5, 2, 3, 4, 6 (low bytes are zero)
+    const uint32_t ml = prmt(0x3E3C3800u, 0x46444240u, w & 0x7777u);
+    const uint32_t mh = prmt(0x3E3C3800u, 0x46444240u, (w >> 16) & 0x7777u);
+    // a_i = half2(nibble i, nibble i + 4): bytes [0, ml.i, 0, mh.i]; the zero bytes come from prmt's sign-replicate
+    // mode on a byte whose top bit is clear; the signs (bit 3 of the nibbles) move to bits 15 and 31
+    a[0] = prmt(ml, mh, 0x4808u) | ((w << 12) & 0x80008000u);
+    a[1] = prmt(ml, mh, 0x5919u) | ((w << 8) & 0x80008000u);
+    a[2] = prmt(ml, mh, 0x6A2Au) | ((w << 4) & 0x80008000u);
+    a[3] = prmt(ml, mh, 0x7B3Bu) | (w & 0x80008000u);
+    a[0] = hmul2(a[0], hg); a[2] = hmul2(a[2], hg);
+    a[1] = hmul2(a[1], hg8); a[3] = hmul2(a[3], hg8);
+}
+
+// int8 pairs -> f16x2 exactly: 1152 + b as fp16 (0x64 high byte, b ^ 0x80 low byte), minus 1152
+__device__ __forceinline__ void q8_frag(uint32_t w0, uint32_t w1, uint32_t (&a)[4]) {
+    const uint32_t x0 = w0 ^ 0x80808080u, x1 = w1 ^ 0x80808080u;
+    const uint32_t bias = 0x64806480u;   // 1152, 1152
+    a[0] = hsub2(prmt(x0, 0x64646464u, 0x5140u), bias);
+    a[1] = hsub2(prmt(x0, 0x64646464u, 0x7362u), bias);
+    a[2] = hsub2(prmt(x1, 0x64646464u, 0x5140u), bias);
+    a[3] = hsub2(prmt(x1, 0x64646464u, 0x7362u), bias);
+}
+
+template <int FMT, int NT>
+__global__ void __launch_bounds__(kTcWarps * 32) tc_gemv_k(TcArgs a) {
+    pdl_wait();
+    extern __shared__ __align__(16) unsigned char dyn[];
+    const int L = a.L, stride = L + 8;   // halves a staged row (the padding spreads the B loads over the banks)
+    __half* xs = reinterpret_cast<__half*>(dyn);
+    const int ks = blockIdx.y, k0 = ks * L, len = min(L, a.k - k0);
+    for (int i = threadIdx.x; i < NT * 8 * (len / 2); i += blockDim.x) {
+        const int r = i / (len / 2), c = 2 * (i - r * (len / 2));
+        float v0 = 0.f, v1 = 0.f;
+        if (r < a.T) {
+            const size_t off = (size_t)r * a.ldx + k0 + c;
+            if (a.x_dtype == B200Q_BF16) {
+                const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(reinterpret_cast<const __nv_bfloat16*>(a.x) + off);
+                v0 = __low2float(b); v1 = __high2float(b);
+            } else {
+                const float2 f = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(a.x) + off);
+                v0 = f.x; v1 = f.y;
+            }
+        }
+        *reinterpret_cast<__half2*>(xs + (size_t)r * stride + c) = __floats2half2_rn(v0, v1);
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int tile = blockIdx.x * kTcWarps + warp;
+    if (tile * 16 < a.n) {
+        float acc[NT][4];
+#pragma unroll
+        for (int i = 0; i < NT; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+        const __half* xb = xs + (size_t)g * stride + 2 * t;
+        auto bfrag = [&](int nt, int kk, uint32_t& b0, uint32_t& b1) {
+            const __half* p = xb + (size_t)nt * 8 * stride + kk;
+            b0 = *reinterpret_cast<const uint32_t*>(p);
+            b1 = *reinterpret_cast<const uint32_t*>(p + 8);
+        };
+        if constexpr (FMT == kFmtNv4) {
+            const int steps = a.k / 64, s0 = k0 / 64, ns = len / 64;
+            const uint8_t* base = a.w + ((size_t)tile * steps + s0) * kNv4Unit;
+            constexpr int PF = 4;
+            uint4 qb[PF];
+            uint2 sb[PF];
+#pragma unroll
+            for (int i = 0; i < PF; i++) {
+                if (i < ns) {
+                    qb[i] = ldg_stream(base + (size_t)i * kNv4Unit + 16 * lane);
+                    sb[i] = ldg_stream2(base + (size_t)i * kNv4Unit + 512 + 8 * g);
+                }
+            }
+            for (int s = 0; s < ns; s += PF) {
+#pragma unroll
+                for (int i = 0; i < PF; i++) {
+                    if (s + i < ns) {
+                        const uint4 q = qb[i];
+                        const uint2 sc = sb[i];
+                        if (s + i + PF < ns) {
+                            qb[i] = ldg_stream(base + (size_t)(s + i + PF) * kNv4Unit + 16 * lane);
+                            sb[i] = ldg_stream2(base + (size_t)(s + i + PF) * kNv4Unit + 512 + 8 * g);
+                        }
+                        // the step's scales: half2 (row g, row g + 8) for blocks 0,1 and 2,3, duplicated per row
+                        const uint32_t h01 = e4m3x2_f16x2(prmt(sc.x, sc.y, 0x5140u));   // bytes g.0, g8.0 | g.1, g8.1
+                        const uint32_t h23 = e4m3x2_f16x2(prmt(sc.x, sc.y, 0x7362u));
+                        const uint32_t h01b = e4m3x2_f16x2(prmt(sc.x, sc.y, 0x5140u) >> 16);
+                        const uint32_t h23b = e4m3x2_f16x2(prmt(sc.x, sc.y, 0x7362u) >> 16);
+                        const uint32_t hs[4] = {h01, h01b, h23, h23b};   // block j: (row g, row g + 8)
+                        const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const uint32_t hg = prmt(hs[j], 0, 0x1010u), hg8 = prmt(hs[j], 0, 0x3232u);
+                            uint32_t af[4];
+                            nv4_frag(words[j], hg, hg8, af);
+                            const int kk = (s + i) * 64 + 16 * j;
+#pragma unroll
+                            for (int nt = 0; nt < NT; nt++) {
+                                uint32_t b0, b1;
+                                bfrag(nt, kk, b0, b1);
+                                mma16816(acc[nt], af[0], af[1], af[2], af[3], b0, b1);
+                            }
+                        }
+                    }
+                }
+            }
+        } else {
+            const int nbk = a.k / 32, b0i = k0 / 32, nblk = len / 32;
+            const uint8_t* base = a.w + ((size_t)tile * nbk + b0i) * kQ8Unit;
+            constexpr int PF = 4;
+            uint4 qb[PF];
+            uint32_t db[PF];
+#pragma unroll
+            for (int i = 0; i < PF; i++) {
+                if (i < nblk) {
+                    qb[i] = ldg_stream(base + (size_t)i * kQ8Unit + 16 * lane);
+                    db[i] = ldg_stream1(base + (size_t)i * kQ8Unit + 512 + 4 * g);
+                }
+            }
+            for (int b = 0; b < nblk; b += PF) {
+#pragma unroll
+                for (int i = 0; i < PF; i++) {
+                    if (b + i < nblk) {
+                        const uint4 q = qb[i];
+                        const uint32_t dd = db[i];
+                        if (b + i + PF < nblk) {
+                            qb[i] = ldg_stream(base + (size_t)(b + i + PF) * kQ8Unit + 16 * lane);
+                            db[i] = ldg_stream1(base + (size_t)(b + i + PF) * kQ8Unit + 512 + 4 * g);
+                        }
+                        const float dg = __half2float(__ushort_as_half((unsigned short)(dd & 0xffff)));
+                        const float dg8 = __half2float(__ushort_as_half((unsigned short)(dd >> 16)));
+                        float part[NT][4];
+#pragma unroll
+                        for (int nt = 0; nt < NT; nt++) part[nt][0] = part[nt][1] = part[nt][2] = part[nt][3] = 0.f;
+#pragma unroll
+                        for (int u = 0; u < 2; u++) {
+                            uint32_t af[4];
+                            q8_frag(u ? q.z : q.x, u ? q.w : q.y, af);
+                            const int kk = (b + i) * 32 + 16 * u;
+#pragma unroll
+                            for (int nt = 0; nt < NT; nt++) {
+                                uint32_t b0, b1;
+                                bfrag(nt, kk, b0, b1);
+                                mma16816(part[nt], af[0], af[1], af[2], af[3], b0, b1);
+                            }
+                        }
+#pragma unroll
+                        for (int nt = 0; nt < NT; nt++) {
+                            acc[nt][0] = fmaf(dg, part[nt][0], acc[nt][0]);
+                            acc[nt][1] = fmaf(dg, part[nt][1], acc[nt][1]);
+                            acc[nt][2] = fmaf(dg8, part[nt][2], acc[nt][2]);
+                            acc[nt][3] = fmaf(dg8, part[nt][3], acc[nt][3]);
+                        }
+                    }
+                }
+            }
+        }
+        // outputs: acc[nt][0..3] = (row g, tok 2t), (row g, tok 2t+1), (row g+8, tok 2t), (row g+8, tok 2t+1)
+        const bool partial = gridDim.y > 1;
+        const float sc = partial ? 1.f : a.s2;
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int tok = nt * 8 + 2 * t + (j & 1);
+                const int row = tile * 16 + g + ((j >> 1) ? 8 : 0);
+                if (tok < a.T && row < a.n) {
+                    float* o = partial ? a.out + ((size_t)ks * a.T + tok) * a.n + row : a.out + (size_t)tok * a.ldo + row;
+                    *o = acc[nt][j] * sc;
+                }
+            }
+    }
+    pdl_trigger();
+}
+
+__global__ void splitk_sum_k(const float* __restrict__ part, int KS, int T, int n, float s2, float* __restrict__ y, int ldy) {
+    pdl_wait();
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < (int64_t)T * n) {
+        const int tok = (int)(i / n), row = (int)(i - (int64_t)tok * n);
+        float s = 0.f;
+        for (int ks = 0; ks < KS; ks++) s += part[((size_t)ks * T + tok) * n + row];
+        y[(size_t)tok * ldy + row] = s * s2;
+    }
+    pdl_trigger();
+}
+
+// K slice: about four CTAs an SM over the row tiles, slices a multiple of 256
+static int slice_len(int n, int k) {
+    const int ctas_x = (n / 16 + kTcWarps - 1) / kTcWarps;
+    const int want = (4 * 148 + ctas_x - 1) / ctas_x;
+    int L = (k + want - 1) / want;
+    L = ((L + 255) / 256) * 256;
+    return L > k ? k : L;
+}
+
+static size_t splitk_ws(int n, int k, int T) {
+    const int L = slice_len(n, k), KS = (k + L - 1) / L;
+    return KS > 1 ? (size_t)KS * T * n * sizeof(float) : 0;
+}
+
+template <int FMT>
+static int run_tc(const uint8_t* w, float s2, int n, int k, const void* x, int x_dtype, int ldx, int T, float* y, int ldy,
+                  void* ws, size_t ws_bytes, cudaStream_t s) {
+    int L = slice_len(n, k);
+    int KS = (k + L - 1) / L;
+    if (KS > 1 && (!ws || ws_bytes < (size_t)KS * T * n * sizeof(float))) { L = k; KS = 1; }   // no workspace: one slice
+    TcArgs a{w, n, k, x, x_dtype, ldx, T, L, s2, KS > 1 ? (float*)ws : y, ldy};
+    const size_t smem = (size_t)(T > 8 ? 16 : 8) * (L + 8) * 2;
+    const dim3 grid((n / 16 + kTcWarps - 1) / kTcWarps, KS);
+    cudaError_t e;
+    if (T > 8) {
+        static size_t opted = 0;
+        if (smem > 48 * 1024 && smem > opted) { cudaFuncSetAttribute(tc_gemv_k<FMT, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); opted = smem; }
+        e = launch(tc_gemv_k<FMT, 2>, grid, dim3(kTcWarps * 32), smem, s, a);
+    } else {
+        static size_t opted = 0;
+        if (smem > 48 * 1024 && smem > opted) { cudaFuncSetAttribute(tc_gemv_k<FMT, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); opted = smem; }
+        e = launch(tc_gemv_k<FMT, 1>, grid, dim3(kTcWarps * 32), smem, s, a);
+    }
+    if (e != cudaSuccess) return status_from(e);
+    if (KS > 1) {
+        const int64_t tot = (int64_t)T * n;
+        e = launch(splitk_sum_k, dim3((unsigned)((tot + 255) / 256)), dim3(256), 0, s, (const float*)ws, KS, T, n, s2, y, ldy);
+        if (e != cudaSuccess) return status_from(e);
+    }
+    return B200Q_OK;
+}
+
+static bool tc_shape_ok(int64_t n, int k) { return n > 0 && n % 16 == 0 && k > 0 && k % 256 == 0; }
+
+}  // namespace b200q
+
+using namespace b200q;
+
+extern "C" {
+
+size_t b200q_nv4_bytes(int64_t n, int k) { return nv4_bytes(n, k); }
+size_t b200q_q8_bytes(int64_t n, int k) { return q8_bytes(n, k); }
+
+int b200q_nv4_pack(const void* q, const void* sc, void* packed, int64_t n, int k, void* stream) {
+    if (!q || !sc || !packed || !tc_shape_ok(n, k) || n > (1 << 30)) return B200Q_EINVAL;
+    const int64_t th = (n / 16) * (k / 64) * 32;
+    launch(nv4_pack_k, dim3((unsigned)((th + 255) / 256)), dim3(256), 0, (cudaStream_t)stream, (const uint8_t*)q,
+           (const uint8_t*)sc, (uint8_t*)packed, (int)n, k);
+    return launched();
+}
+
+int b200q_q8_pack(const void* raw, void* packed, int64_t n, int k, void* stream) {
+    if (!raw || !packed || !tc_shape_ok(n, k) || n > (1 << 30)) return B200Q_EINVAL;
+    const int64_t th = (n / 16) * (k / 32) * 32;
+    launch(q8_pack_k, dim3((unsigned)((th + 255) / 256)), dim3(256), 0, (cudaStream_t)stream, (const uint8_t*)raw,
+           (uint8_t*)packed, (int)n, k);
+    return launched();
+}
+
+size_t b200q_nv4_gemv_workspace_bytes(int n, int k, int T) { return tc_shape_ok(n, k) && T > 0 ? splitk_ws(n, k, T) : 0; }
+size_t b200q_q8_gemv_workspace_bytes(int n, int k, int T) { return tc_shape_ok(n, k) && T > 0 ? splitk_ws(n, k, T) : 0; }
+
+int b200q_nv4_gemv(const void* w, float s2, int n, int k, const void* x, int x_dtype, int ldx, int T, float* y, int ldy,
+                   void* workspace, size_t workspace_bytes, void* stream) {
+    if (!w || !x || !y || !tc_shape_ok(n, k) || T <= 0 || T > 16 || ldx < k || ldy < n ||
+        (x_dtype != B200Q_F32 && x_dtype != B200Q_BF16))
+        return B200Q_EINVAL;
+    return run_tc<kFmtNv4>((const uint8_t*)w, s2, n, k, x, x_dtype, ldx, T, y, ldy, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int b200q_q8_gemv(const void* w, int n, int k, const void* x, int x_dtype, int ldx, int T, float* y, int ldy,
+                  void* workspace, size_t workspace_bytes, void* stream) {
+    if (!w || !x || !y || !tc_shape_ok(n, k) || T <= 0 || T > 16 || ldx < k || ldy < n ||
+        (x_dtype != B200Q_F32 && x_dtype != B200Q_BF16))
+        return B200Q_EINVAL;
+    return run_tc<kFmtQ8>((const uint8_t*)w, 1.f, n, k, x, x_dtype, ldx, T, y, ldy, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+}  // extern "C"

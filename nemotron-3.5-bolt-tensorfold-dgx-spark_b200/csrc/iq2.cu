@@ -78,8 +78,7 @@ __global__ void synth_iq2_k(uint64_t seed, int64_t nblocks, uint8_t* __restrict_
 }
 
 // ---------------------------------------------------------------------------------------------------------
-// packer: ggml blocks [n][k/256][66] -> rt32 (qs [n/32][k/64][32][16 B], then d [n/32][k/256][32] fp16)
-// one thread per (row, chunk pair)
+// packer: ggml blocks [n][k/256][66] -> rt32 units (see common.cuh), one thread per (row, chunk pair)
 // ---------------------------------------------------------------------------------------------------------
 __global__ void iq2_pack_k(const uint8_t* __restrict__ raw, uint8_t* __restrict__ out, int64_t n, int k) {
     pdl_wait();
@@ -96,11 +95,9 @@ __global__ void iq2_pack_k(const uint8_t* __restrict__ raw, uint8_t* __restrict_
             w[q] = (uint32_t)src[4 * q] | (uint32_t)src[4 * q + 1] << 8 | (uint32_t)src[4 * q + 2] << 16 | (uint32_t)src[4 * q + 3] << 24;
         const int64_t rt = row / kIq2Tile;
         const int lane = (int)(row % kIq2Tile);
-        reinterpret_cast<uint4*>(out)[((size_t)rt * npair + j) * kIq2Tile + lane] = make_uint4(w[0], w[1], w[2], w[3]);
-        if ((j & 3) == 0) {
-            uint16_t* dpl = reinterpret_cast<uint16_t*>(out + iq2_qs_bytes(n, k));
-            dpl[((size_t)rt * nb + j / 4) * kIq2Tile + lane] = (uint16_t)(blk[0] | blk[1] << 8);
-        }
+        uint8_t* unit = out + ((size_t)rt * nb + j / 4) * kIq2Unit;
+        reinterpret_cast<uint4*>(unit)[(j & 3) * kIq2Tile + lane] = make_uint4(w[0], w[1], w[2], w[3]);
+        if ((j & 3) == 0) reinterpret_cast<uint16_t*>(unit + 2048)[lane] = (uint16_t)(blk[0] | blk[1] << 8);
     }
     pdl_trigger();
 }
@@ -175,8 +172,10 @@ __global__ void __launch_bounds__(kWarps * 32) iq2_gemv_k(GemvArgs a) {
     const int rt = blockIdx.x * kWarps + warp;     // this warp's row tile
     const bool active = rt * kIq2Tile < n;
     const int row = rt * kIq2Tile + lane;
-    const uint4* qp = reinterpret_cast<const uint4*>(W) + (size_t)rt * npair * kIq2Tile + lane;
-    const uint16_t* dp = reinterpret_cast<const uint16_t*>(W + iq2_qs_bytes(n, k)) + (size_t)rt * (k >> 8) * kIq2Tile + lane;
+    // super-block b of this tile: 4 x 512 bytes of chunk pairs, then 32 fp16 scales
+    const uint8_t* tile = W + (size_t)rt * (k >> 8) * kIq2Unit;
+    auto qptr = [&](int j) { return reinterpret_cast<const uint4*>(tile + (size_t)(j >> 2) * kIq2Unit) + (j & 3) * kIq2Tile + lane; };
+    auto dptr = [&](int b) { return reinterpret_cast<const uint16_t*>(tile + (size_t)b * kIq2Unit + 2048) + lane; };
 
     for (int b0 = 0; b0 < cnt; b0 += MAXT) {
         const int nt = min(MAXT, cnt - b0);
@@ -206,9 +205,9 @@ __global__ void __launch_bounds__(kWarps * 32) iq2_gemv_k(GemvArgs a) {
         for (int m = 0; m < MAXT; m++) acc[m] = 0.f;
 
         uint4 buf[kPF];
-        uint16_t dnext = ld_stream_u16(dp);
+        uint16_t dnext = ld_stream_u16(dptr(0));
 #pragma unroll
-        for (int i = 0; i < kPF; i++) buf[i] = ld_stream(qp + (size_t)i * kIq2Tile);
+        for (int i = 0; i < kPF; i++) buf[i] = ld_stream(qptr(i));
 
         for (int j0 = 0; j0 < npair; j0 += kPF) {
             uint4 cur[kPF];
@@ -217,8 +216,8 @@ __global__ void __launch_bounds__(kWarps * 32) iq2_gemv_k(GemvArgs a) {
             const float dh = __half2float(__ushort_as_half(dnext));
             if (j0 + kPF < npair) {
 #pragma unroll
-                for (int i = 0; i < kPF; i++) buf[i] = ld_stream(qp + (size_t)(j0 + kPF + i) * kIq2Tile);
-                dnext = ld_stream_u16(dp + (size_t)((j0 + kPF) >> 2) * kIq2Tile);
+                for (int i = 0; i < kPF; i++) buf[i] = ld_stream(qptr(j0 + kPF + i));
+                dnext = ld_stream_u16(dptr((j0 + kPF) >> 2));
             }
 #pragma unroll
             for (int i = 0; i < 2 * kPF; i++) {

@@ -299,7 +299,8 @@ int b200q_route(const void* logits, int l_dtype, int ldl, const float* bias, int
 }
 
 int b200q_moe_group(const int* ridx, int pairs, int E, int* counts, int* offsets, int* order, void* stream) {
-    if (!ridx || !counts || !offsets || !order || pairs < 0 || pairs > 4096 || E <= 0 || E > 512) return B200Q_EINVAL;
+    if ((!ridx && pairs > 0) || !counts || !offsets || !order || pairs < 0 || pairs > 4096 || E <= 0 || E > 512)
+        return B200Q_EINVAL;
     launch(group_k, dim3(1), dim3(512), 0, (cudaStream_t)stream, ridx, pairs, E, counts, offsets, order);
     return launched();
 }
@@ -336,15 +337,17 @@ int b200q_moe_decode(const void* x, const void* logits, const void* up, const vo
     const int nslots = E + (extra ? 1 : 0);
     const int maxcnt = T;
     int st;
-    auto mark = [&](int i) { if (stage_events) cudaEventRecord((cudaEvent_t)stage_events[i], s); };
+    auto mark = [&](int i) {
+        return stage_events ? status_from(cudaEventRecord((cudaEvent_t)stage_events[i], s)) : B200Q_OK;
+    };
 
-    mark(0);
+    if ((st = mark(0)) != B200Q_OK) return st;
     // 1. router + grouping (block 0) and the int8 rows of x (the rest)
     const int qwarps = T * (H / 32);
     launch(moe_prep_k, dim3(1 + (qwarps + 15) / 16), dim3(512), 0, s, x, logits, T, H, E, topk, route, bias, scale, extra,
            w.ridx, w.rw, w.counts, w.offsets, w.order, w.xq, w.xs);
     if ((st = launched()) != B200Q_OK) return st;
-    mark(1);
+    if ((st = mark(1)) != B200Q_OK) return st;
 
     // 2. up, relu^2, int8 rows of the result: ids < pairs read token id / topk, the shared ids pairs + t read token t
     GemvArgs a = {};
@@ -352,7 +355,7 @@ int b200q_moe_decode(const void* x, const void* logits, const void* up, const vo
     a.nslot_routed = E; a.n = F; a.k = H; a.counts = w.counts; a.offsets = w.offsets; a.order = w.order;
     a.act_div = topk; a.act_split = pairs; a.act_base = 0; a.xq = w.xq; a.xs = w.xs; a.aq = w.aq; a.as = w.as;
     if ((st = status_from(launch_iq2_gemv(a, nslots, maxcnt, 2, s))) != B200Q_OK) return st;
-    mark(2);
+    if ((st = mark(2)) != B200Q_OK) return st;
 
     // 3. down over the int8 rows of every id
     GemvArgs b = {};
@@ -360,13 +363,13 @@ int b200q_moe_decode(const void* x, const void* logits, const void* up, const vo
     b.nslot_routed = E; b.n = H; b.k = F; b.counts = w.counts; b.offsets = w.offsets; b.order = w.order;
     b.act_div = 1; b.act_split = 1 << 30; b.xq = w.aq; b.xs = w.as; b.y = w.mo; b.ldy = H;
     if ((st = status_from(launch_iq2_gemv(b, nslots, maxcnt, 0, s))) != B200Q_OK) return st;
-    mark(3);
+    if ((st = mark(3)) != B200Q_OK) return st;
 
     // 4. combine + the shared expert's rows
     launch(combine_k, dim3((H / 4 + 255) / 256, T), dim3(256), 0, s, (const float*)w.mo, (const float*)w.rw,
            extra ? (const float*)(w.mo + (size_t)pairs * H) : (const float*)nullptr, T, topk, H, out, out_dtype);
     if ((st = launched()) != B200Q_OK) return st;
-    mark(4);
+    if ((st = mark(4)) != B200Q_OK) return st;
     if (ridx_out) {
         if (cudaMemcpyAsync(ridx_out, w.ridx, sizeof(int) * pairs, cudaMemcpyDeviceToDevice, s) != cudaSuccess) return status_from(cudaGetLastError());
     }

@@ -25,10 +25,13 @@ import refbind as R  # noqa: E402
 from helpers import iq2_blocks, normal_bf16  # noqa: E402
 
 DEV = "cuda"
+_KEEP = []   # device copies stay alive until the next case: a pointer taken from a temporary would be recycled
 
 
 def _d(a):
-    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+    t = torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+    _KEEP.append(t)
+    return t
 
 
 def _p(t):
@@ -168,6 +171,7 @@ def main(out_dir):
     os.makedirs(out_dir, exist_ok=True)
     for name, fn in CASES.items():
         inputs, outputs = fn()
+        _KEEP.clear()
         np.savez_compressed(os.path.join(out_dir, f"ref_{name}.npz"),
                             **{f"in_{k}": v for k, v in inputs.items()}, **{f"out_{k}": v for k, v in outputs.items()})
         print("wrote", name)

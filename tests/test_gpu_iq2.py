@@ -25,12 +25,13 @@ def packed(blocks, n, k):
 
 
 def np_pack_rt32(blocks, n, k):
-    """numpy statement of the rt32 layout (qs [n/32][k/64][32][16 B] then d [n/32][k/256][32] fp16)."""
-    b = blocks.reshape(n, k // 256, 66)
-    qs = b[:, :, 2:].reshape(n, k // 64, 16)
-    qs = qs.reshape(n // 32, 32, k // 64, 16).transpose(0, 2, 1, 3).reshape(-1)
-    d = b[:, :, :2].reshape(n // 32, 32, k // 256, 2).transpose(0, 2, 1, 3).reshape(-1)
-    return np.concatenate([qs, d])
+    """numpy statement of the rt32 layout: per (32-row tile, 256-k super-block) unit, [4 chunk pairs][32 rows][16 B]
+    of the rows' ggml chunk bytes, then the 32 rows' fp16 d."""
+    nb = k // 256
+    b = blocks.reshape(n, nb, 66)
+    qs = b[:, :, 2:].reshape(n // 32, 32, nb, 4, 16).transpose(0, 2, 3, 1, 4).reshape(n // 32, nb, 2048)
+    d = b[:, :, :2].reshape(n // 32, 32, nb, 2).transpose(0, 2, 1, 3).reshape(n // 32, nb, 64)
+    return np.concatenate([qs, d], axis=2).reshape(-1)
 
 
 @pytest.mark.parametrize("n,k", [(32, 256), (64, 1024), (2048, 4096)])
