@@ -137,8 +137,99 @@ __device__ __forceinline__ void iq2_chunk_weights(uint32_t qx, uint32_t qy, cons
     }
 }
 
+// what a warp's walk over its 32 rows needs
+struct RowCtx {
+    const GemvArgs& a;
+    const uint8_t* tile;     // the warp's row tile
+    const int8_t* xsm;       // staged int8 rows [nt][k]
+    const float* ssm;        // their scales [nt][k/32]
+    const uint2* grid;
+    const uint2* sgn;
+    const int* ids;
+    int k, n, nc, npair, lane, row, rt, nt;
+};
+
+// One warp, 32 rows (a lane each), K in chunk order, NT token rows (nt <= NT of them real; for NT in {1, 2} nt == NT).
+template <int NT, int EPI>
+__device__ __forceinline__ void iq2_rows(const RowCtx& c) {
+    const int lane = c.lane;
+    auto qptr = [&](int j) { return reinterpret_cast<const uint4*>(c.tile + (size_t)(j >> 2) * kIq2Unit) + (j & 3) * kIq2Tile + lane; };
+    auto dptr = [&](int b) { return reinterpret_cast<const uint16_t*>(c.tile + (size_t)b * kIq2Unit + 2048) + lane; };
+    float acc[NT];
+#pragma unroll
+    for (int m = 0; m < NT; m++) acc[m] = 0.f;
+
+    uint4 buf[kPF];
+    uint16_t dnext = ld_stream_u16(dptr(0));
+#pragma unroll
+    for (int i = 0; i < kPF; i++) buf[i] = ld_stream(qptr(i));
+
+    for (int j0 = 0; j0 < c.npair; j0 += kPF) {
+        uint4 cur[kPF];
+#pragma unroll
+        for (int i = 0; i < kPF; i++) cur[i] = buf[i];
+        const float dh = __half2float(__ushort_as_half(dnext));
+        if (j0 + kPF < c.npair) {
+#pragma unroll
+            for (int i = 0; i < kPF; i++) buf[i] = ld_stream(qptr(j0 + kPF + i));
+            dnext = ld_stream_u16(dptr((j0 + kPF) >> 2));
+        }
+#pragma unroll
+        for (int i = 0; i < 2 * kPF; i++) {
+            const int ch = 2 * j0 + i;
+            const uint32_t qx = (i & 1) ? cur[i >> 1].z : cur[i >> 1].x;
+            const uint32_t qy = (i & 1) ? cur[i >> 1].w : cur[i >> 1].y;
+            uint32_t w[8];
+            iq2_chunk_weights(qx, qy, c.grid, c.sgn, w);
+            const float dA = dh * (0.5f + (float)(qy >> 28)) * 0.25f;
+#pragma unroll
+            for (int m = 0; m < NT; m++) {
+                if (NT <= 2 || m < c.nt) {
+                    const int4* xa = reinterpret_cast<const int4*>(c.xsm + (size_t)m * c.k + ch * 32);
+                    const int4 x0 = xa[0], x1 = xa[1];
+                    int dot = __dp4a((int)w[0], x0.x, 0);
+                    dot = __dp4a((int)w[1], x0.y, dot);
+                    dot = __dp4a((int)w[2], x0.z, dot);
+                    dot = __dp4a((int)w[3], x0.w, dot);
+                    dot = __dp4a((int)w[4], x1.x, dot);
+                    dot = __dp4a((int)w[5], x1.y, dot);
+                    dot = __dp4a((int)w[6], x1.z, dot);
+                    dot = __dp4a((int)w[7], x1.w, dot);
+                    if constexpr (EPI == kDots) {
+                        c.a.dots[((size_t)c.ids[m] * c.n + c.row) * c.nc + ch] = dot;
+                    } else {
+                        acc[m] = fmaf(dA * c.ssm[m * c.nc + ch], (float)dot, acc[m]);
+                    }
+                }
+            }
+        }
+    }
+
+    if constexpr (EPI != kDots) {
+#pragma unroll
+        for (int m = 0; m < NT; m++) {
+            if (NT <= 2 || m < c.nt) {
+                float v = acc[m];
+                if constexpr (EPI != kStore) v = v > 0.f ? v * v : 0.f;
+                const int id = c.ids[m];
+                if constexpr (EPI == kRelu2Q8) {
+                    // quant_rows_k over this warp's 32 consecutive outputs (one 32-group of the row)
+                    float am = v;   // v >= 0 after relu^2
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+                    const float inv = am > 0.f ? 127.f / am : 0.f;
+                    c.a.aq[(size_t)id * c.n + c.row] = (int8_t)__float2int_rn(v * inv);
+                    if (lane == 0) c.a.as[(size_t)id * (c.n >> 5) + c.rt] = am / 127.f;
+                } else {
+                    c.a.y[(size_t)id * c.a.ldy + c.row] = v;
+                }
+            }
+        }
+    }
+}
+
 template <int MAXT, int EPI>
-__global__ void __launch_bounds__(kWarps * 32) iq2_gemv_k(GemvArgs a) {
+__global__ void __launch_bounds__(kWarps * 32, 2) iq2_gemv_k(GemvArgs a) {
     pdl_wait();
     __shared__ uint2 grid_s[256];
     __shared__ uint2 sgn_s[128];
@@ -174,8 +265,6 @@ __global__ void __launch_bounds__(kWarps * 32) iq2_gemv_k(GemvArgs a) {
     const int row = rt * kIq2Tile + lane;
     // super-block b of this tile: 4 x 512 bytes of chunk pairs, then 32 fp16 scales
     const uint8_t* tile = W + (size_t)rt * (k >> 8) * kIq2Unit;
-    auto qptr = [&](int j) { return reinterpret_cast<const uint4*>(tile + (size_t)(j >> 2) * kIq2Unit) + (j & 3) * kIq2Tile + lane; };
-    auto dptr = [&](int b) { return reinterpret_cast<const uint16_t*>(tile + (size_t)b * kIq2Unit + 2048) + lane; };
 
     for (int b0 = 0; b0 < cnt; b0 += MAXT) {
         const int nt = min(MAXT, cnt - b0);
@@ -199,78 +288,13 @@ __global__ void __launch_bounds__(kWarps * 32) iq2_gemv_k(GemvArgs a) {
         }
         __syncthreads();
         if (!active) continue;
-
-        float acc[MAXT];
-#pragma unroll
-        for (int m = 0; m < MAXT; m++) acc[m] = 0.f;
-
-        uint4 buf[kPF];
-        uint16_t dnext = ld_stream_u16(dptr(0));
-#pragma unroll
-        for (int i = 0; i < kPF; i++) buf[i] = ld_stream(qptr(i));
-
-        for (int j0 = 0; j0 < npair; j0 += kPF) {
-            uint4 cur[kPF];
-#pragma unroll
-            for (int i = 0; i < kPF; i++) cur[i] = buf[i];
-            const float dh = __half2float(__ushort_as_half(dnext));
-            if (j0 + kPF < npair) {
-#pragma unroll
-                for (int i = 0; i < kPF; i++) buf[i] = ld_stream(qptr(j0 + kPF + i));
-                dnext = ld_stream_u16(dptr((j0 + kPF) >> 2));
-            }
-#pragma unroll
-            for (int i = 0; i < 2 * kPF; i++) {
-                const int c = 2 * j0 + i;
-                const uint32_t qx = (i & 1) ? cur[i >> 1].z : cur[i >> 1].x;
-                const uint32_t qy = (i & 1) ? cur[i >> 1].w : cur[i >> 1].y;
-                uint32_t w[8];
-                iq2_chunk_weights(qx, qy, grid_s, sgn_s, w);
-                const float dA = dh * (0.5f + (float)(qy >> 28)) * 0.25f;
-#pragma unroll
-                for (int m = 0; m < MAXT; m++) {
-                    if (m < nt) {
-                        const int4* xa = reinterpret_cast<const int4*>(xsm + (size_t)m * k + c * 32);
-                        const int4 x0 = xa[0], x1 = xa[1];
-                        int dot = __dp4a((int)w[0], x0.x, 0);
-                        dot = __dp4a((int)w[1], x0.y, dot);
-                        dot = __dp4a((int)w[2], x0.z, dot);
-                        dot = __dp4a((int)w[3], x0.w, dot);
-                        dot = __dp4a((int)w[4], x1.x, dot);
-                        dot = __dp4a((int)w[5], x1.y, dot);
-                        dot = __dp4a((int)w[6], x1.z, dot);
-                        dot = __dp4a((int)w[7], x1.w, dot);
-                        if constexpr (EPI == kDots) {
-                            a.dots[((size_t)ids_s[m] * n + row) * nc + c] = dot;
-                        } else {
-                            acc[m] = fmaf(dA * ssm[m * nc + c], (float)dot, acc[m]);
-                        }
-                    }
-                }
-            }
-        }
-
-        if constexpr (EPI != kDots) {
-#pragma unroll
-            for (int m = 0; m < MAXT; m++) {
-                if (m < nt) {
-                    float v = acc[m];
-                    if constexpr (EPI != kStore) v = v > 0.f ? v * v : 0.f;
-                    const int id = ids_s[m];
-                    if constexpr (EPI == kRelu2Q8) {
-                        // quant_rows_k over this warp's 32 consecutive outputs (one 32-group of the row)
-                        float am = v;   // v >= 0 after relu^2
-#pragma unroll
-                        for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-                        const float inv = am > 0.f ? 127.f / am : 0.f;
-                        a.aq[(size_t)id * n + row] = (int8_t)__float2int_rn(v * inv);
-                        if (lane == 0) a.as[(size_t)id * (n >> 5) + rt] = am / 127.f;
-                    } else {
-                        a.y[(size_t)id * a.ldy + row] = v;
-                    }
-                }
-            }
-        }
+        RowCtx c{a, tile, xsm, ssm, grid_s, sgn_s, ids_s, k, n, nc, npair, lane, row, rt, nt};
+        // the token count picks the code: a slot of one token runs the one-token loop, and so on
+        if (nt == 1) iq2_rows<1, EPI>(c);
+        else if (nt == 2) iq2_rows<2, EPI>(c);
+        else if (MAXT >= 4 && nt <= 4) iq2_rows<(MAXT >= 4 ? 4 : 1), EPI>(c);
+        else if (MAXT >= 8 && nt <= 8) iq2_rows<(MAXT >= 8 ? 8 : 1), EPI>(c);
+        else if (MAXT >= 16) iq2_rows<(MAXT >= 16 ? 16 : 1), EPI>(c);
     }
     pdl_trigger();
 }

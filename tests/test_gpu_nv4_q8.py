@@ -109,4 +109,4 @@ def test_gemv_without_workspace_matches_split():
     st = L.b200q_nv4_gemv(ctypes.c_void_p(w.data_ptr()), 1.0, n, k, ctypes.c_void_p(x.data_ptr()), 1, k, T,
                           ctypes.c_void_p(y2.data_ptr()), n, None, 0, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert st == 0
-    assert rel_l2(y2.cpu().numpy(), y1.cpu().numpy()) < 1e-6
+    assert rel_l2(y2.cpu().numpy(), y1.cpu().numpy()) < 1e-5   # the same products, summed in another order
