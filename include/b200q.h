@@ -163,6 +163,19 @@ int b200q_moe_decode(const void* x, const void* logits, const void* up, const vo
                      float scale, void* out, int out_dtype, void* workspace, size_t workspace_bytes, int* ridx_out,
                      float* rw_out, void* const* stage_events, void* stream);
 
+/* The decode MoE layer without a caller-provided workspace, for callers that cannot allocate device memory (a host
+ * whose allocator owns the GPU's memory, a plugin that receives only tensors, a loop that must not take cudaMalloc's
+ * implicit synchronisation).  No counterpart in the reference: libbolt allocates its own scratch at bolt_open.
+ * Arguments and results are those of b200q_moe_decode.  Scratch is a library-resident device array of
+ * b200q_moe_decode_noalloc_max_bytes() bytes (3 MiB: enough for T <= 16, H <= 4096, F <= 2048, E <= 128,
+ * topk <= 8), held by every GPU that loads the library until exit; larger shapes return B200Q_ENOSPACE.  The first
+ * call on a device looks up the array's device address, so make it before any stream capture.  All calls share the
+ * array: calls that overlap on the GPU race.  It allocates nothing. */
+size_t b200q_moe_decode_noalloc_max_bytes(void);
+int b200q_moe_decode_noalloc(const void* x, const void* logits, const void* up, const void* down, const void* shared_up,
+                             const void* shared_down, int T, int H, int F, int E, int topk, int route, const float* bias,
+                             float scale, void* out, int out_dtype, int* ridx_out, float* rw_out, void* stream);
+
 /* ---------------------------------------------------------------------------------------------------------
  * Synthetic inputs (BASELINE's generators), host and device producing the same bytes.
  * --------------------------------------------------------------------------------------------------------- */

@@ -380,3 +380,59 @@ int b200q_moe_decode(const void* x, const void* logits, const void* up, const vo
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------------------
+// The decode MoE layer for callers that cannot allocate device memory.
+//
+// Some hosts of this library cannot call cudaMalloc: a framework whose caching allocator owns the GPU's memory and
+// fixes its budget at start-up, a plugin boundary that hands the operator nothing but tensors, or a decode loop that
+// must never take cudaMalloc's implicit device synchronisation.  They cannot provide b200q_moe_decode's workspace, so
+// this entry point runs the same four launches on a scratch array that lives in the library itself: a file-scope
+// __device__ array of kNoAllocScratchBytes, which every GPU that loads the library holds until the process exits.
+// Host code cannot use the array's name as a device address (it is a host-side stand-in), so the first call on each
+// device, with that device current, asks the runtime for the address (cudaGetSymbolAddress) and keeps it; that first
+// call should therefore come before any stream capture.  Every call shares the one array: the layer writes every
+// byte of scratch it reads before reading it, so nothing has to start at zero, but calls that overlap on the GPU
+// (two streams, two threads) race on it.  Shapes whose scratch would exceed the array are refused with
+// B200Q_ENOSPACE.
+// ---------------------------------------------------------------------------------------------------------
+#include <mutex>
+
+namespace b200q {
+constexpr size_t kNoAllocScratchBytes = (size_t)3 << 20;   // covers T <= 16, H <= 4096, F <= 2048, E <= 128, topk <= 8
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[256];   // the array's device address, by device ordinal
+
+static int noalloc_scratch(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return status_from(e);
+    if (dev < 0 || dev >= 256) return B200Q_EINVAL;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return status_from(e);
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return B200Q_OK;
+}
+}  // namespace b200q
+
+extern "C" size_t b200q_moe_decode_noalloc_max_bytes(void) { return b200q::kNoAllocScratchBytes; }
+
+extern "C" int b200q_moe_decode_noalloc(const void* x, const void* logits, const void* up, const void* down,
+                                        const void* shared_up, const void* shared_down, int T, int H, int F, int E, int topk,
+                                        int route, const float* bias, float scale, void* out, int out_dtype, int* ridx_out,
+                                        float* rw_out, void* stream) {
+    const size_t need = b200q_moe_decode_workspace_bytes(T, H, F, E, topk);
+    if (need == 0) return B200Q_EINVAL;
+    if (need > b200q::kNoAllocScratchBytes) return B200Q_ENOSPACE;
+    void* scratch = nullptr;
+    const int st = b200q::noalloc_scratch(&scratch);
+    if (st != B200Q_OK) return st;
+    return b200q_moe_decode(x, logits, up, down, shared_up, shared_down, T, H, F, E, topk, route, bias, scale, out,
+                            out_dtype, scratch, b200q::kNoAllocScratchBytes, ridx_out, rw_out, nullptr, stream);
+}
