@@ -52,6 +52,10 @@ int b200q_abi(void);
 /* The CUDA error behind the last B200Q_ECUDA of this thread (cudaError_t as int), 0 if none. */
 int b200q_last_cuda_error(void);
 const char* b200q_strerror(int status);
+/* Errors the kernels recorded on the current device (a bitmask, 0 if none; bit 0: a streaming GEMV's bounded wait for
+ * its copies ran out, so its outputs are incomplete); synchronous.  clear != 0 resets it.  No counterpart in libbolt,
+ * whose kernels do not wait on barriers. */
+int b200q_device_error(int clear);
 
 /* ---------------------------------------------------------------------------------------------------------
  * Load-time packers (raw checkpoint bytes on the device -> this library's layouts).

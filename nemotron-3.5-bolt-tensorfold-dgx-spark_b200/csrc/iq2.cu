@@ -2,16 +2,34 @@
 // activation rows (dense, and grouped by expert for the routed MoE).
 //
 // Arithmetic (the routed-expert kernels moe_mma_k / moe_coop_k of the reference, bolt_kernels.cu:445-483 and
-// 599-652): a row's 32-weight chunk c holds four grid-index bytes and a word of four 7-bit sign indices plus a 4-bit
-// sub-scale.  Its weights are the signed grid integers (iq2xxs_grid bytes, negated where ksigns64 says); the chunk's
-// exact int32 dot with the int8 activation row is scaled by dA * s, dA = d * (0.5 + s4) * 0.25 and s the row's
-// activation scale of that chunk, and accumulated in chunk order:  acc = fma(dA * s, (float)dot, acc).
+// 599-652): a row's 32-weight chunk holds four grid-index bytes, four 7-bit sign indices and a 4-bit sub-scale s4.
+// Its weights are the signed grid integers (iq2xxs_grid bytes, negated where ksigns_iq2xs says); the chunk's exact
+// int32 dot with the int8 activation row is scaled by dA * s, dA = d * (0.5 + s4) * 0.25 = (d / 8) * (2 s4 + 1)
+// (both forms are exact in fp32) and s the row's activation scale of that chunk, and accumulated in chunk order:
+// acc = fma(dA * s, (float)dot, acc).
 //
-// Mapping: a warp owns 32 weight rows (lane l = row 32t + l) and walks K in order, so every lane's accumulation is
-// the reference's own order and the result is reproducible bit for bit by a scalar loop.  A CTA of 8 warps covers
-// 256 rows of one expert ("slot"); the slot's tokens (at most kMaxTok at a time) sit in shared memory as int8 rows
-// and every lane reads the same activation word (a broadcast).  The weights stream once per slot: each lane
-// keeps four 16-byte loads (64 weights each) in flight ahead of the math.
+// Mapping: a lane owns one weight row and walks K in order, so every output is the reference's own chunk-ordered
+// sum, reproducible bit for bit by a scalar loop.  A warp owns 32 rows of one expert ("slot") and up to 4 of the
+// slot's tokens: a work unit.  CTAs are persistent (one of 12 warps per SM); every warp takes a contiguous range of
+// units weighted by their cost (weights streamed + tokens dotted), and neighbouring ranges go to different SMs, so a
+// slot with many tokens (the shared expert) is spread out instead of holding up the tail.
+//
+// Streaming: the (32-row tile, 256-k super-block) pieces of the layout are contiguous 2112-byte units, so each warp
+// runs its own ring of kStages shared-memory stages filled by TMA bulk copies (cp.async.bulk, completion on an
+// mbarrier): a stage holds one super-block of the warp's 32 rows plus the matching 256 bytes of int8 activations and
+// 32 bytes of scales of each of the unit's tokens.  Lane 0 keeps kStages - 1 stages in flight across unit boundaries;
+// every lane reads its row's 16-byte chunk pairs from the stage and every token's activation words as shared-memory
+// broadcasts.  Waits are bounded (%globaltimer): on a timeout the kernel sets an error flag, lets its own copies
+// land and returns.
+//
+// Dequantisation without bank conflicts: a 64 KB table in shared memory gives, per lane, its own copy of two 32-bit
+// words for every grid index r: codes(r), the eight magnitude codes of grid entry r as nibbles (8 -> 0, 25 -> 1,
+// 43 -> 2), and signs(r & 127), three times the eight sign bits of ksigns_iq2xs as nibbles.  The word of row r, lane
+// l sits at r * 256 + l * 4 (+ 128 for signs): every lane reads its own bank, and one prmt turns a grid-index byte
+// (or a sign-index byte) and the lane offset into the address.  codes + signs is a prmt selector into the six signed
+// magnitudes {8, 25, 43, -8, -25, -43}: two prmt give eight int8 weights.  For the sign index to be a byte the packer
+// re-encodes ggml's sign word (four 7-bit fields, s4 in bits 28-31) as four bytes, byte g = field g | bit g of s4 << 7;
+// the spare top bit selects the table's second, identical half of sign words.
 #include "iq2.cuh"
 
 #include <cstring>
@@ -39,7 +57,7 @@ __host__ __device__ inline uint16_t f2h_bits_pos(float f) {
     const int e = (int)((u >> 23) & 255) - 127;   // f = 1.m * 2^e
     uint32_t mant = (u & 0x7fffffu) | 0x800000u;  // 24 bits
     if (e < -14) {                                // half subnormal: multiples of 2^-24
-        const int sh = -e - 14 + 13;              // keep 24 - 13 - (-e - 14) bits
+        const int sh = -e - 14 + 13;
         const uint32_t q = mant >> sh, rem = mant & ((1u << sh) - 1), half = 1u << (sh - 1);
         return (uint16_t)(q + ((rem > half || (rem == half && (q & 1))) ? 1 : 0));
     }
@@ -77,8 +95,16 @@ __global__ void synth_iq2_k(uint64_t seed, int64_t nblocks, uint8_t* __restrict_
     if (i < nblocks) synth_iq2_block(seed, (uint64_t)i, out + i * 66);
 }
 
+// ggml's sign word (four 7-bit sign indices, s4 in bits 28-31) -> four bytes: field g | (bit g of s4) << 7
+__host__ __device__ inline uint32_t iq2_sign_bytes(uint32_t qy) {
+    uint32_t r = 0;
+    for (int g = 0; g < 4; g++) r |= ((((qy >> (7 * g)) & 127u) | (((qy >> (28 + g)) & 1u) << 7)) << (8 * g));
+    return r;
+}
+
 // ---------------------------------------------------------------------------------------------------------
-// packer: ggml blocks [n][k/256][66] -> rt32 units (see common.cuh), one thread per (row, chunk pair)
+// packer: ggml blocks [n][k/256][66] -> rt32 units (see common.cuh), one thread per (row, chunk pair); the sign
+// word of every chunk is re-encoded by iq2_sign_bytes
 // ---------------------------------------------------------------------------------------------------------
 __global__ void iq2_pack_k(const uint8_t* __restrict__ raw, uint8_t* __restrict__ out, int64_t n, int k) {
     pdl_wait();
@@ -93,6 +119,8 @@ __global__ void iq2_pack_k(const uint8_t* __restrict__ raw, uint8_t* __restrict_
 #pragma unroll
         for (int q = 0; q < 4; q++)
             w[q] = (uint32_t)src[4 * q] | (uint32_t)src[4 * q + 1] << 8 | (uint32_t)src[4 * q + 2] << 16 | (uint32_t)src[4 * q + 3] << 24;
+        w[1] = iq2_sign_bytes(w[1]);
+        w[3] = iq2_sign_bytes(w[3]);
         const int64_t rt = row / kIq2Tile;
         const int lane = (int)(row % kIq2Tile);
         uint8_t* unit = out + ((size_t)rt * nb + j / 4) * kIq2Unit;
@@ -105,234 +133,382 @@ __global__ void iq2_pack_k(const uint8_t* __restrict__ raw, uint8_t* __restrict_
 // ---------------------------------------------------------------------------------------------------------
 // the GEMV
 // ---------------------------------------------------------------------------------------------------------
-constexpr int kWarps = 8;                   // warps a CTA: 256 weight rows
-constexpr int kPF = 4;                      // chunk pairs (16-byte loads) a lane keeps in flight: one super-block
+constexpr int kGemvWarps = 12;              // one persistent CTA of 12 warps an SM
+constexpr int kStages = 4;                  // ring stages a warp (kStages - 1 super-blocks in flight)
+constexpr int kUnitTok = 4;                 // most tokens a work unit dots
+constexpr int kTableBytes = 65536;
+constexpr int kStageAct = kIq2Unit;                       // 2112: tokens' int8 rows (kUnitTok x 256 B)
+constexpr int kStageScl = kStageAct + kUnitTok * 256;     // 3136: their scales (kUnitTok x 32 B)
+constexpr int kStageBytes = kStageScl + kUnitTok * 32;    // 3264
+constexpr size_t kGemvSmem = (size_t)kTableBytes + (size_t)kGemvWarps * kStages * kStageBytes + kGemvWarps * kStages * 8;
+constexpr int kMaxSlots = 520;
+constexpr int kCostRows = 3;                // a unit costs kCostRows (its weights) + its token count
+constexpr unsigned long long kWaitNs = 2000000000ull;   // a ring stage not filled within 2 s: give up
 
 enum Epi { kStore = 0, kRelu2 = 1, kRelu2Q8 = 2, kDots = 3 };
 
+__device__ int g_iq2_error;   // bit 0: a ring wait timed out
 
-
-__device__ __forceinline__ uint4 ld_stream(const uint4* p) {
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(s));
+    return d;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
     uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
     return v;
 }
-__device__ __forceinline__ uint16_t ld_stream_u16(const uint16_t* p) {
+__device__ __forceinline__ uint16_t lds16(uint32_t addr) {
     uint16_t v;
-    asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
     return v;
+}
+__device__ __forceinline__ unsigned long long globaltimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+// bounded wait for a stage: false when it has not completed within `ns`
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned long long ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity))
+        if (globaltimer() - t0 > ns) return false;
+    return true;
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
 }
 
-// the 32 signed grid integers of a chunk as 8 words of int8: (grid ^ mask) + (mask & 1s) negates a byte where the
-// mask is 0xFF (grid bytes are at most 43, so no byte carries into the next)
-__device__ __forceinline__ void iq2_chunk_weights(uint32_t qx, uint32_t qy, const uint2* __restrict__ grid,
-                                                  const uint2* __restrict__ sgn, uint32_t (&w)[8]) {
+// the 64 KB table: row r (256 B) = [codes(r) x 32 lanes][signs(r & 127) x 32 lanes]
+__device__ void build_table(uint32_t* tbl) {
+    for (int i = threadIdx.x; i < 512; i += blockDim.x) {
+        const int r = i & 255;
+        uint32_t word = 0;
+        if (i < 256) {
+            const unsigned long long g = iq2xxs_grid[r];
 #pragma unroll
-    for (int g = 0; g < 4; g++) {
-        const uint2 G = grid[(qx >> (8 * g)) & 255];
-        const uint2 S = sgn[(qy >> (7 * g)) & 127];
-        w[2 * g] = (G.x ^ S.x) + (S.x & 0x01010101u);
-        w[2 * g + 1] = (G.y ^ S.y) + (S.y & 0x01010101u);
+            for (int j = 0; j < 8; j++) {
+                const uint32_t mag = (uint32_t)(g >> (8 * j)) & 255u;
+                word |= (mag == 8 ? 0u : mag == 25 ? 1u : 2u) << (4 * j);
+            }
+        } else {
+            const uint32_t sg = ksigns_iq2xs[r & 127];
+#pragma unroll
+            for (int j = 0; j < 8; j++) word |= (((sg >> j) & 1u) * 3u) << (4 * j);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(tbl + r * 64 + (i < 256 ? 0 : 32));
+        const uint4 v = make_uint4(word, word, word, word);
+#pragma unroll
+        for (int q = 0; q < 8; q++) dst[q] = v;
     }
 }
 
-// what a warp's walk over its 32 rows needs
-struct RowCtx {
-    const GemvArgs& a;
-    const uint8_t* tile;     // the warp's row tile
-    const int8_t* xsm;       // staged int8 rows [nt][k]
-    const float* ssm;        // their scales [nt][k/32]
-    const uint2* grid;
-    const uint2* sgn;
-    const int* ids;
-    int k, n, nc, npair, lane, row, rt, nt;
+// the eight int8 weights of group g of a chunk (grid bytes qx, sign bytes qyp) as two words
+__device__ __forceinline__ void group_weights(uint32_t tb, uint32_t lane4, uint32_t qx, uint32_t qyp, int g, uint32_t& lo,
+                                              uint32_t& hi) {
+    // address = tb + (index byte << 8) + lane * 4 (+ 128 for the sign half)
+    const uint32_t sel_b = 0x7604u | ((uint32_t)g << 4);
+    const uint32_t ac = prmt(qx, lane4, sel_b);
+    const uint32_t as = prmt(qyp, lane4 | 128u, sel_b);
+    const uint32_t sel = lds32(tb + ac) + lds32(tb + as);      // nibble j: code_j + 3 * sign_j, in 0..5
+    lo = prmt(0xF82B1908u, 0x0000D5E7u, sel);                  // bytes 8, 25, 43, -8 | -25, -43
+    hi = prmt(0xF82B1908u, 0x0000D5E7u, sel >> 16);
+}
+
+// The walk over a warp's units: slot-major (slots with tokens only), then token batch b0 (kUnitTok tokens), then
+// 32-row group g; unit (s, b0, g) starts at cost start(s, b0) + g * (kCostRows + nt) and belongs to the warp whose
+// cost range [lo, hi) holds that start.
+struct Walk {
+    const int* cnt;
+    const int* pre;
+    int nslots, G;
+    long long lo, hi;
+    int s, b0, g, g1;
+    long long start;
+    bool ok;
+
+    __device__ void begin() {
+        s = 0;
+        while (s < nslots && pre[s + 1] <= lo) s++;
+        b0 = 0;
+        start = s < nslots ? pre[s] : 0;
+        enter();
+    }
+    __device__ void enter() {
+        for (;;) {
+            if (s >= nslots || pre[s] >= hi) { ok = false; return; }
+            const int c = cnt[s];
+            if (b0 >= c) { s++; b0 = 0; if (s < nslots) start = pre[s]; continue; }
+            const int cost = kCostRows + min(kUnitTok, c - b0);
+            long long g0 = lo > start ? (lo - start + cost - 1) / cost : 0;
+            long long e = hi > start ? (hi - start + cost - 1) / cost : 0;
+            if (e > G) e = G;
+            if (g0 < e) { g = (int)g0; g1 = (int)e; ok = true; return; }
+            start += (long long)G * cost;
+            b0 += kUnitTok;
+        }
+    }
+    __device__ void next() {
+        if (++g < g1) return;
+        start += (long long)G * (kCostRows + min(kUnitTok, cnt[s] - b0));
+        b0 += kUnitTok;
+        enter();
+    }
+    __device__ int nt() const { return min(kUnitTok, cnt[s] - b0); }
 };
 
-// One warp, 32 rows (a lane each), K in chunk order, NT token rows (nt <= NT of them real; for NT in {1, 2} nt == NT).
+struct Ring {
+    uint32_t stage0, bar0;   // this warp's stages and barriers
+    int issued, consumed;    // super-blocks issued into / consumed from the ring
+    __device__ uint32_t stage(int i) const { return stage0 + (uint32_t)((i % kStages) * kStageBytes); }
+    __device__ uint32_t bar(int i) const { return bar0 + (uint32_t)((i % kStages) * 8); }
+};
+
+// a unit's token ids and activation rows
+struct Toks {
+    int id[kUnitTok];
+    int arow[kUnitTok];
+};
+
+__device__ __forceinline__ void unit_tokens(const GemvArgs& a, const Walk& w, int nt, Toks& t) {
+    const int base = a.counts ? a.offsets[w.s] : 0;
+#pragma unroll
+    for (int m = 0; m < kUnitTok; m++) {
+        const int mm = m < nt ? m : 0;
+        const int id = a.counts ? a.order[base + w.b0 + mm] : w.b0 + mm;
+        t.id[m] = id;
+        t.arow[m] = id < a.act_split ? id / a.act_div : id - a.act_split + a.act_base;
+    }
+}
+
+__device__ __forceinline__ const uint8_t* slot_weights(const GemvArgs& a, int s) {
+    return (a.counts == nullptr || s < a.nslot_routed) ? a.slab + (size_t)s * a.expert_bytes : a.extra_w;
+}
+
+// Lane 0: fill the next ring stage with the producer walk's next super-block (weights, tokens' rows and scales).
+__device__ void issue_next(const GemvArgs& a, Walk& pw, int& psb, Toks& pt, Ring& r, int nsb) {
+    if (!pw.ok) return;
+    const int nt = pw.nt();
+    if (psb == 0) unit_tokens(a, pw, nt, pt);
+    const uint8_t* src = slot_weights(a, pw.s) + ((size_t)pw.g * nsb + psb) * kIq2Unit;
+    const uint32_t st = r.stage(r.issued), bar = r.bar(r.issued);
+    const bool scales = a.xs != nullptr;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the warp's reads of the stage come first
+    mbar_expect_tx(bar, (uint32_t)(kIq2Unit + nt * 256 + (scales ? nt * 32 : 0)));
+    bulk_g2s(st, src, kIq2Unit, bar);
+    for (int m = 0; m < nt; m++) {
+        bulk_g2s(st + kStageAct + m * 256, a.xq + (size_t)pt.arow[m] * a.k + psb * 256, 256, bar);
+        if (scales) bulk_g2s(st + kStageScl + m * 32, a.xs + (size_t)pt.arow[m] * (a.k >> 5) + psb * 8, 32, bar);
+    }
+    r.issued++;
+    if (++psb == nsb) { psb = 0; pw.next(); }
+}
+
+// One unit: its 32 rows (a lane each) over K in chunk order, NT token rows (nt <= NT real; nt == NT for NT <= 2).
+// Returns false when a ring wait timed out.
 template <int NT, int EPI>
-__device__ __forceinline__ void iq2_rows(const RowCtx& c) {
-    const int lane = c.lane;
-    auto qptr = [&](int j) { return reinterpret_cast<const uint4*>(c.tile + (size_t)(j >> 2) * kIq2Unit) + (j & 3) * kIq2Tile + lane; };
-    auto dptr = [&](int b) { return reinterpret_cast<const uint16_t*>(c.tile + (size_t)b * kIq2Unit + 2048) + lane; };
+__device__ bool unit_rows(const GemvArgs& a, const Walk& w, const Toks& t, int nt, uint32_t tb, int lane, Ring& r,
+                          Walk& pw, int& psb, Toks& pt, int nsb) {
+    const uint32_t lane4 = (uint32_t)lane * 4u;
+    const int row = w.g * kIq2Tile + lane, nc = a.k >> 5;
     float acc[NT];
 #pragma unroll
     for (int m = 0; m < NT; m++) acc[m] = 0.f;
-
-    uint4 buf[kPF];
-    uint16_t dnext = ld_stream_u16(dptr(0));
+    for (int sb = 0; sb < nsb; sb++) {
+        const uint32_t st = r.stage(r.consumed);
+        const bool ok = mbar_wait(r.bar(r.consumed), (uint32_t)((r.consumed / kStages) & 1), kWaitNs);
+        if (__any_sync(0xffffffffu, !ok)) return false;
+        const float dh8 = __half2float(__ushort_as_half(lds16(st + 2048 + lane * 2))) * 0.125f;
+#pragma unroll 1
+        for (int j = 0; j < 4; j++) {
+            const uint4 q = lds128(st + j * 512 + lane * 16);
 #pragma unroll
-    for (int i = 0; i < kPF; i++) buf[i] = ld_stream(qptr(i));
-
-    for (int j0 = 0; j0 < c.npair; j0 += kPF) {
-        uint4 cur[kPF];
+            for (int h = 0; h < 2; h++) {
+                const int c8 = 2 * j + h;
+                const uint32_t qx = h ? q.z : q.x, qy = h ? q.w : q.y;
+                // s4 from the four spare bits (bits 7, 15, 23, 31 -> 28..31), then dA = (d/8) * (2 s4 + 1)
+                const uint32_t s4x2p1 = ((((qy & 0x80808080u) * 0x00204081u) >> 27) & 0x1eu) | 1u;
+                const float dA = dh8 * (float)s4x2p1;
+                uint32_t wq[8];
 #pragma unroll
-        for (int i = 0; i < kPF; i++) cur[i] = buf[i];
-        const float dh = __half2float(__ushort_as_half(dnext));
-        if (j0 + kPF < c.npair) {
+                for (int g = 0; g < 4; g++) group_weights(tb, lane4, qx, qy, g, wq[2 * g], wq[2 * g + 1]);
 #pragma unroll
-            for (int i = 0; i < kPF; i++) buf[i] = ld_stream(qptr(j0 + kPF + i));
-            dnext = ld_stream_u16(dptr((j0 + kPF) >> 2));
-        }
-#pragma unroll
-        for (int i = 0; i < 2 * kPF; i++) {
-            const int ch = 2 * j0 + i;
-            const uint32_t qx = (i & 1) ? cur[i >> 1].z : cur[i >> 1].x;
-            const uint32_t qy = (i & 1) ? cur[i >> 1].w : cur[i >> 1].y;
-            uint32_t w[8];
-            iq2_chunk_weights(qx, qy, c.grid, c.sgn, w);
-            const float dA = dh * (0.5f + (float)(qy >> 28)) * 0.25f;
-#pragma unroll
-            for (int m = 0; m < NT; m++) {
-                if (NT <= 2 || m < c.nt) {
-                    const int4* xa = reinterpret_cast<const int4*>(c.xsm + (size_t)m * c.k + ch * 32);
-                    const int4 x0 = xa[0], x1 = xa[1];
-                    int dot = __dp4a((int)w[0], x0.x, 0);
-                    dot = __dp4a((int)w[1], x0.y, dot);
-                    dot = __dp4a((int)w[2], x0.z, dot);
-                    dot = __dp4a((int)w[3], x0.w, dot);
-                    dot = __dp4a((int)w[4], x1.x, dot);
-                    dot = __dp4a((int)w[5], x1.y, dot);
-                    dot = __dp4a((int)w[6], x1.z, dot);
-                    dot = __dp4a((int)w[7], x1.w, dot);
-                    if constexpr (EPI == kDots) {
-                        c.a.dots[((size_t)c.ids[m] * c.n + c.row) * c.nc + ch] = dot;
-                    } else {
-                        acc[m] = fmaf(dA * c.ssm[m * c.nc + ch], (float)dot, acc[m]);
+                for (int m = 0; m < NT; m++) {
+                    if (NT <= 2 || m < nt) {
+                        const uint32_t xa = st + kStageAct + m * 256 + c8 * 32;
+                        const uint4 x0 = lds128(xa), x1 = lds128(xa + 16);
+                        int dot = __dp4a((int)wq[0], (int)x0.x, 0);
+                        dot = __dp4a((int)wq[1], (int)x0.y, dot);
+                        dot = __dp4a((int)wq[2], (int)x0.z, dot);
+                        dot = __dp4a((int)wq[3], (int)x0.w, dot);
+                        dot = __dp4a((int)wq[4], (int)x1.x, dot);
+                        dot = __dp4a((int)wq[5], (int)x1.y, dot);
+                        dot = __dp4a((int)wq[6], (int)x1.z, dot);
+                        dot = __dp4a((int)wq[7], (int)x1.w, dot);
+                        if constexpr (EPI == kDots) {
+                            a.dots[((size_t)t.id[m] * a.n + row) * nc + sb * 8 + c8] = dot;
+                        } else {
+                            const float s = __uint_as_float(lds32(st + kStageScl + m * 32 + c8 * 4));
+                            acc[m] = fmaf(dA * s, (float)dot, acc[m]);
+                        }
                     }
                 }
             }
         }
+        __syncwarp();   // every lane is done with the stage: lane 0 refills it
+        r.consumed++;
+        if (lane == 0) issue_next(a, pw, psb, pt, r, nsb);
+        __syncwarp();
     }
-
     if constexpr (EPI != kDots) {
 #pragma unroll
         for (int m = 0; m < NT; m++) {
-            if (NT <= 2 || m < c.nt) {
+            if (NT <= 2 || m < nt) {
                 float v = acc[m];
                 if constexpr (EPI != kStore) v = v > 0.f ? v * v : 0.f;
-                const int id = c.ids[m];
+                const int id = t.id[m];
                 if constexpr (EPI == kRelu2Q8) {
-                    // quant_rows_k over this warp's 32 consecutive outputs (one 32-group of the row)
+                    // quant_rows_k over this warp's 32 consecutive outputs (one 32-group of the output row)
                     float am = v;   // v >= 0 after relu^2
 #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
                     const float inv = am > 0.f ? 127.f / am : 0.f;
-                    c.a.aq[(size_t)id * c.n + c.row] = (int8_t)__float2int_rn(v * inv);
-                    if (lane == 0) c.a.as[(size_t)id * (c.n >> 5) + c.rt] = am / 127.f;
+                    a.aq[(size_t)id * a.n + row] = (int8_t)__float2int_rn(v * inv);
+                    if (lane == 0) a.as[(size_t)id * (a.n >> 5) + w.g] = am / 127.f;
                 } else {
-                    c.a.y[(size_t)id * c.a.ldy + c.row] = v;
+                    a.y[(size_t)id * a.ldy + row] = v;
                 }
             }
         }
     }
+    return true;
 }
 
-template <int MAXT, int EPI>
-__global__ void __launch_bounds__(kWarps * 32, 2) iq2_gemv_k(GemvArgs a) {
-    pdl_wait();
-    __shared__ uint2 grid_s[256];
-    __shared__ uint2 sgn_s[128];
-    __shared__ int ids_s[MAXT];
-    extern __shared__ __align__(16) unsigned char dyn[];
-    const int k = a.k, n = a.n, nc = k >> 5, npair = k >> 6;
-    int8_t* xsm = reinterpret_cast<int8_t*>(dyn);                                   // [MAXT][k]
-    float* ssm = reinterpret_cast<float*>(dyn + (size_t)MAXT * k);                  // [MAXT][k/32]
-
-    const int slot = blockIdx.y;
-    int cnt, base;
-    const uint8_t* W;
-    if (a.counts == nullptr) { cnt = a.dense_rows; base = 0; W = a.slab; }
-    else {
-        cnt = a.counts[slot];
-        base = a.offsets[slot];
-        W = slot < a.nslot_routed ? a.slab + (size_t)slot * a.expert_bytes : a.extra_w;
-    }
-    if (cnt == 0 || W == nullptr) { pdl_trigger(); return; }
-
+template <int EPI>
+__global__ void __launch_bounds__(kGemvWarps * 32, 1) iq2_gemv_k(GemvArgs a, int nslots) {
+    extern __shared__ __align__(128) unsigned char dyn[];
+    __shared__ int s_cnt[kMaxSlots], s_pre[kMaxSlots + 1];
+    uint32_t* tbl = reinterpret_cast<uint32_t*>(dyn);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    for (int i = tid; i < 256; i += blockDim.x) {
-        const unsigned long long g = iq2xxs_grid[i];
-        grid_s[i] = make_uint2((uint32_t)g, (uint32_t)(g >> 32));
+    const uint32_t tb = (uint32_t)__cvta_generic_to_shared(tbl);
+    Ring r;
+    r.stage0 = tb + kTableBytes + (uint32_t)(warp * kStages * kStageBytes);
+    r.bar0 = tb + kTableBytes + (uint32_t)(kGemvWarps * kStages * kStageBytes) + (uint32_t)(warp * kStages * 8);
+    r.issued = r.consumed = 0;
+    if (lane == 0) {
+        for (int i = 0; i < kStages; i++) mbar_init(r.bar0 + 8 * i, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    for (int i = tid; i < 128; i += blockDim.x) {
-        const unsigned long long m = ksigns64[i];
-        sgn_s[i] = make_uint2((uint32_t)m, (uint32_t)(m >> 32));
+    build_table(tbl);
+    pdl_wait();
+    const int G = a.n / kIq2Tile, nsb = a.k >> 8;
+    for (int s = tid; s < nslots; s += blockDim.x) {
+        int cnt = a.counts ? a.counts[s] : a.dense_rows;
+        if (slot_weights(a, s) == nullptr) cnt = 0;
+        s_cnt[s] = cnt;
     }
-
-    const int rt = blockIdx.x * kWarps + warp;     // this warp's row tile
-    const bool active = rt * kIq2Tile < n;
-    const int row = rt * kIq2Tile + lane;
-    // super-block b of this tile: 4 x 512 bytes of chunk pairs, then 32 fp16 scales
-    const uint8_t* tile = W + (size_t)rt * (k >> 8) * kIq2Unit;
-
-    for (int b0 = 0; b0 < cnt; b0 += MAXT) {
-        const int nt = min(MAXT, cnt - b0);
-        __syncthreads();   // the previous batch is done with the staged rows
-        if (tid < MAXT) ids_s[tid] = tid < nt ? (a.counts ? a.order[base + b0 + tid] : b0 + tid) : 0;
-        __syncthreads();
-        {   // stage the batch's int8 rows and their scales
-            const int per = k >> 4;
-            for (int idx = tid; idx < nt * per; idx += blockDim.x) {
-                const int r = idx / per, i = idx - r * per;
-                const int id = ids_s[r];
-                const int arow = id < a.act_split ? id / a.act_div : id - a.act_split + a.act_base;
-                reinterpret_cast<uint4*>(xsm + (size_t)r * k)[i] = __ldg(reinterpret_cast<const uint4*>(a.xq + (size_t)arow * k) + i);
-            }
-            for (int idx = tid; EPI != kDots && idx < nt * nc; idx += blockDim.x) {
-                const int r = idx / nc, i = idx - r * nc;
-                const int id = ids_s[r];
-                const int arow = id < a.act_split ? id / a.act_div : id - a.act_split + a.act_base;
-                ssm[r * nc + i] = __ldg(a.xs + (size_t)arow * nc + i);
-            }
+    __syncthreads();
+    if (tid == 0) {   // exclusive prefix of slot costs (nslots <= 520: a serial loop is cheap)
+        long long acc = 0;
+        for (int s = 0; s < nslots; s++) {
+            s_pre[s] = (int)acc;
+            const int cnt = s_cnt[s];
+            const int nb = (cnt + kUnitTok - 1) / kUnitTok;
+            acc += (long long)G * (nb * kCostRows + cnt);
         }
-        __syncthreads();
-        if (!active) continue;
-        RowCtx c{a, tile, xsm, ssm, grid_s, sgn_s, ids_s, k, n, nc, npair, lane, row, rt, nt};
-        // the token count picks the code: a slot of one token runs the one-token loop, and so on
-        if (nt == 1) iq2_rows<1, EPI>(c);
-        else if (nt == 2) iq2_rows<2, EPI>(c);
-        else if (MAXT >= 4 && nt <= 4) iq2_rows<(MAXT >= 4 ? 4 : 1), EPI>(c);
-        else if (MAXT >= 8 && nt <= 8) iq2_rows<(MAXT >= 8 ? 8 : 1), EPI>(c);
-        else if (MAXT >= 16) iq2_rows<(MAXT >= 16 ? 16 : 1), EPI>(c);
+        s_pre[nslots] = (int)acc;
+    }
+    __syncthreads();
+    const long long total = s_pre[nslots];
+    const int nwarps = gridDim.x * kGemvWarps;
+    const int gw = warp * gridDim.x + blockIdx.x;   // neighbouring cost ranges go to different SMs
+    Walk w{s_cnt, s_pre, nslots, G, total * gw / nwarps, total * (gw + 1) / nwarps, 0, 0, 0, 0, 0, false};
+    w.begin();
+    Walk pw = w;       // lane 0's producer walk: the ring is refilled as soon as a stage is consumed
+    int psb = 0;
+    Toks pt{};
+    if (lane == 0)
+        for (int i = 0; i < kStages; i++) issue_next(a, pw, psb, pt, r, nsb);
+    __syncwarp();
+    bool healthy = true;
+    while (w.ok && healthy) {
+        const int nt = w.nt();
+        Toks t;
+        unit_tokens(a, w, nt, t);
+        if (nt == 1) healthy = unit_rows<1, EPI>(a, w, t, nt, tb, lane, r, pw, psb, pt, nsb);
+        else if (nt == 2) healthy = unit_rows<2, EPI>(a, w, t, nt, tb, lane, r, pw, psb, pt, nsb);
+        else healthy = unit_rows<4, EPI>(a, w, t, nt, tb, lane, r, pw, psb, pt, nsb);
+        w.next();
+    }
+    if (!healthy) {
+        // a stage never filled: flag it, and let this warp's copies in flight land before the CTA's memory goes away
+        if (lane == 0) {
+            atomicOr(&g_iq2_error, 1);
+            for (int i = r.consumed; i < r.issued; i++) mbar_wait(r.bar(i), (uint32_t)((i / kStages) & 1), kWaitNs);
+        }
+        __syncwarp();
     }
     pdl_trigger();
 }
 
-static size_t gemv_smem(int maxt, int k) { return (size_t)maxt * k + (size_t)maxt * (k / 32) * 4; }
-
-template <int MAXT, int EPI>
-static cudaError_t launch_gemv_t(const GemvArgs& a, int nslots, cudaStream_t s) {
-    const size_t sm = gemv_smem(MAXT, a.k);
-    static size_t opted = 0;
-    if (sm > 48 * 1024 && sm > opted) {
-        cudaError_t e = cudaFuncSetAttribute(iq2_gemv_k<MAXT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-        if (e != cudaSuccess) return e;
-        opted = sm;
+static int num_sms() {
+    static int sms[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!sms[dev]) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        sms[dev] = v > 0 ? v : 148;
     }
-    const dim3 grid((a.n / kIq2Tile + kWarps - 1) / kWarps, nslots);
-    return launch(iq2_gemv_k<MAXT, EPI>, grid, dim3(kWarps * 32), sm, s, a);
+    return sms[dev];
 }
 
 template <int EPI>
-static cudaError_t launch_gemv_e(const GemvArgs& a, int nslots, int maxcnt, cudaStream_t s) {
-    if (maxcnt <= 1) return launch_gemv_t<1, EPI>(a, nslots, s);
-    if (maxcnt <= 2) return launch_gemv_t<2, EPI>(a, nslots, s);
-    if (maxcnt <= 4) return launch_gemv_t<4, EPI>(a, nslots, s);
-    if (maxcnt <= 8) return launch_gemv_t<8, EPI>(a, nslots, s);
-    return launch_gemv_t<16, EPI>(a, nslots, s);
+static cudaError_t launch_gemv_e(const GemvArgs& a, int nslots, cudaStream_t s) {
+    static bool opted = false;
+    if (!opted) {
+        cudaError_t e = cudaFuncSetAttribute(iq2_gemv_k<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvSmem);
+        if (e != cudaSuccess) return e;
+        opted = true;
+    }
+    return launch(iq2_gemv_k<EPI>, dim3(num_sms()), dim3(kGemvWarps * 32), kGemvSmem, s, a, nslots);
 }
 
-cudaError_t launch_iq2_gemv(const GemvArgs& a, int nslots, int maxcnt, int epi, cudaStream_t s) {
+cudaError_t launch_iq2_gemv(const GemvArgs& a, int nslots, int /*maxcnt*/, int epi, cudaStream_t s) {
+    if (nslots <= 0 || nslots > kMaxSlots) return cudaErrorInvalidValue;
     switch (epi) {
-        case kStore: return launch_gemv_e<kStore>(a, nslots, maxcnt, s);
-        case kRelu2: return launch_gemv_e<kRelu2>(a, nslots, maxcnt, s);
-        case kRelu2Q8: return launch_gemv_e<kRelu2Q8>(a, nslots, maxcnt, s);
-        default: return launch_gemv_e<kDots>(a, nslots, maxcnt, s);
+        case kStore: return launch_gemv_e<kStore>(a, nslots, s);
+        case kRelu2: return launch_gemv_e<kRelu2>(a, nslots, s);
+        case kRelu2Q8: return launch_gemv_e<kRelu2Q8>(a, nslots, s);
+        default: return launch_gemv_e<kDots>(a, nslots, s);
     }
 }
 
-bool iq2_shape_ok(int64_t n, int k) { return n > 0 && n % kIq2Tile == 0 && k > 0 && k % 256 == 0 && k <= 8192; }
+bool iq2_shape_ok(int64_t n, int k) { return n > 0 && n % kIq2Tile == 0 && n <= (1 << 24) && k > 0 && k % 256 == 0 && k <= 8192; }
+
+// the GEMVs stream weights, int8 rows and scales with bulk copies, which need 16-byte aligned addresses
+static bool a16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
 }  // namespace b200q
 
@@ -362,9 +538,21 @@ int b200q_synth_iq2(uint64_t seed, int64_t nblocks, void* out, void* stream) {
     return launched();
 }
 
+int b200q_device_error(int clear) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_iq2_error, sizeof(int)) != cudaSuccess) return -1;
+    if (clear) {
+        const int z = 0;
+        cudaMemcpyToSymbol(g_iq2_error, &z, sizeof(int));
+    }
+    return v;
+}
+
 int b200q_iq2_gemv(const void* w, int n, int k, const int8_t* xq, const float* xs, int T, float* y, int ldy, int epi,
                    void* stream) {
-    if (!w || !xq || !xs || !y || !iq2_shape_ok(n, k) || T <= 0 || ldy < n || (epi != 0 && epi != 1)) return B200Q_EINVAL;
+    if (!w || !xq || !xs || !y || !iq2_shape_ok(n, k) || T <= 0 || ldy < n || (epi != 0 && epi != 1) || !a16(w) ||
+        !a16(xq) || !a16(xs))
+        return B200Q_EINVAL;
     GemvArgs a = {};
     a.slab = (const uint8_t*)w; a.n = n; a.k = k; a.dense_rows = T;
     a.act_div = 1; a.act_split = 1 << 30; a.xq = xq; a.xs = xs; a.y = y; a.ldy = ldy;
@@ -372,7 +560,7 @@ int b200q_iq2_gemv(const void* w, int n, int k, const int8_t* xq, const float* x
 }
 
 int b200q_iq2_chunk_dots(const void* w, int n, int k, const int8_t* xq, int T, int32_t* dots, void* stream) {
-    if (!w || !xq || !dots || !iq2_shape_ok(n, k) || T <= 0) return B200Q_EINVAL;
+    if (!w || !xq || !dots || !iq2_shape_ok(n, k) || T <= 0 || !a16(w) || !a16(xq)) return B200Q_EINVAL;
     GemvArgs a = {};
     a.slab = (const uint8_t*)w; a.n = n; a.k = k; a.dense_rows = T;
     a.act_div = 1; a.act_split = 1 << 30; a.xq = xq; a.dots = dots;
@@ -382,7 +570,7 @@ int b200q_iq2_chunk_dots(const void* w, int n, int k, const int8_t* xq, int T, i
 int b200q_moe_up(const void* slab, int E, int n, int k, const int* counts, const int* offsets, const int* order,
                  int topk, const int8_t* xq, const float* xs, float* y, int ldy, int epi, void* stream) {
     if (!slab || !counts || !offsets || !order || !xq || !xs || !y || E <= 0 || E > 512 || topk <= 0 ||
-        !iq2_shape_ok(n, k) || ldy < n || (epi != 0 && epi != 1))
+        !iq2_shape_ok(n, k) || ldy < n || (epi != 0 && epi != 1) || !a16(slab) || !a16(xq) || !a16(xs))
         return B200Q_EINVAL;
     GemvArgs a = {};
     a.slab = (const uint8_t*)slab; a.expert_bytes = iq2_bytes(n, k); a.nslot_routed = E; a.n = n; a.k = k;
@@ -394,7 +582,7 @@ int b200q_moe_up(const void* slab, int E, int n, int k, const int* counts, const
 int b200q_moe_up_q8(const void* slab, int E, int n, int k, const int* counts, const int* offsets, const int* order,
                     int topk, const int8_t* xq, const float* xs, int8_t* aq, float* as, void* stream) {
     if (!slab || !counts || !offsets || !order || !xq || !xs || !aq || !as || E <= 0 || E > 512 || topk <= 0 ||
-        !iq2_shape_ok(n, k))
+        !iq2_shape_ok(n, k) || !a16(slab) || !a16(xq) || !a16(xs))
         return B200Q_EINVAL;
     GemvArgs a = {};
     a.slab = (const uint8_t*)slab; a.expert_bytes = iq2_bytes(n, k); a.nslot_routed = E; a.n = n; a.k = k;
@@ -405,7 +593,8 @@ int b200q_moe_up_q8(const void* slab, int E, int n, int k, const int* counts, co
 
 int b200q_moe_down(const void* slab, int E, int n, int k, const int* counts, const int* offsets, const int* order,
                    const int8_t* aq, const float* as, float* y, int ldy, void* stream) {
-    if (!slab || !counts || !offsets || !order || !aq || !as || !y || E <= 0 || E > 512 || !iq2_shape_ok(n, k) || ldy < n)
+    if (!slab || !counts || !offsets || !order || !aq || !as || !y || E <= 0 || E > 512 || !iq2_shape_ok(n, k) || ldy < n ||
+        !a16(slab) || !a16(aq) || !a16(as))
         return B200Q_EINVAL;
     GemvArgs a = {};
     a.slab = (const uint8_t*)slab; a.expert_bytes = iq2_bytes(n, k); a.nslot_routed = E; a.n = n; a.k = k;

@@ -327,7 +327,8 @@ int b200q_moe_decode(const void* x, const void* logits, const void* up, const vo
     if (!x || !logits || !up || !down || !out || !workspace || T <= 0 || T > 64 || E <= 0 || E > 512 || topk <= 0 ||
         topk > 16 || topk > E || !iq2_shape_ok(F, H) || !iq2_shape_ok(H, F) || ((shared_up == nullptr) != (shared_down == nullptr)) ||
         (route != B200Q_ROUTE_SOFTMAX && route != B200Q_ROUTE_SIGMOID) || (out_dtype != B200Q_F32 && out_dtype != B200Q_BF16) ||
-        ((uintptr_t)workspace & 255))
+        ((uintptr_t)workspace & 255) || ((uintptr_t)up & 15) || ((uintptr_t)down & 15) || ((uintptr_t)shared_up & 15) ||
+        ((uintptr_t)shared_down & 15))
         return B200Q_EINVAL;
     DecodeWs w = decode_ws((char*)workspace, T, H, F, E, topk);
     if (workspace_bytes < w.bytes) return B200Q_ENOSPACE;

@@ -28,7 +28,15 @@ def np_pack_rt32(blocks, n, k):
     """numpy statement of the rt32 layout: per (32-row tile, 256-k super-block) unit, [4 chunk pairs][32 rows][16 B]
     of the rows' ggml chunk bytes, then the 32 rows' fp16 d."""
     nb = k // 256
-    b = blocks.reshape(n, nb, 66)
+    b = blocks.reshape(n, nb, 66).copy()
+    # each chunk's sign word -> four bytes: 7-bit sign index g | bit g of the sub-scale << 7
+    qy = b[:, :, 2:].reshape(n, nb, 8, 8)[..., 4:8].copy().view(np.uint32)[..., 0]
+    enc = np.zeros_like(qy)
+    for g in range(4):
+        enc |= (((qy >> (7 * g)) & 127) | (((qy >> (28 + g)) & 1) << 7)) << (8 * g)
+    chunks = b[:, :, 2:].reshape(n, nb, 8, 8)
+    chunks[..., 4:8] = enc[..., None].view(np.uint8).reshape(n, nb, 8, 4)
+    b[:, :, 2:] = chunks.reshape(n, nb, 64)
     qs = b[:, :, 2:].reshape(n // 32, 32, nb, 4, 16).transpose(0, 2, 3, 1, 4).reshape(n // 32, nb, 2048)
     d = b[:, :, :2].reshape(n // 32, 32, nb, 2).transpose(0, 2, 1, 3).reshape(n // 32, nb, 64)
     return np.concatenate([qs, d], axis=2).reshape(-1)
