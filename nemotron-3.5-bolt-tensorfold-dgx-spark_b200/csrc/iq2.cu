@@ -133,21 +133,28 @@ __global__ void iq2_pack_k(const uint8_t* __restrict__ raw, uint8_t* __restrict_
 // ---------------------------------------------------------------------------------------------------------
 // the GEMV
 // ---------------------------------------------------------------------------------------------------------
-constexpr int kGemvWarps = 12;              // one persistent CTA of 12 warps an SM
-constexpr int kStages = 4;                  // ring stages a warp (kStages - 1 super-blocks in flight)
+constexpr int kGemvWarps = 16;              // one persistent CTA of 16 warps an SM
+constexpr int kStages = 3;                  // ring stages a warp (kStages - 1 super-blocks in flight)
 constexpr int kUnitTok = 4;                 // most tokens a work unit dots
-constexpr int kTableBytes = 65536;
 constexpr int kStageAct = kIq2Unit;                       // 2112: tokens' int8 rows (kUnitTok x 256 B)
 constexpr int kStageScl = kStageAct + kUnitTok * 256;     // 3136: their scales (kUnitTok x 32 B)
 constexpr int kStageBytes = kStageScl + kUnitTok * 32;    // 3264
-constexpr size_t kGemvSmem = (size_t)kTableBytes + (size_t)kGemvWarps * kStages * kStageBytes + kGemvWarps * kStages * 8;
 constexpr int kMaxSlots = 520;
+// Shared memory: the 64 KB table sits at the fixed shared address kTblAddr, so one prmt builds a lookup address
+// (table base, index byte, lane offset) with no add.  Below it: the ring barriers, the slot counts and prefix, and
+// the first stages; above it, the remaining stages.  The layout holds for a dynamic-memory base below 1 KB.
+constexpr uint32_t kTblAddr = 0x10000;
+constexpr uint32_t kHdrBytes = kGemvWarps * kStages * 8 + (2 * kMaxSlots + 1) * 4 + 12;   // barriers, counts, prefix
+constexpr int kNumStages = kGemvWarps * kStages;
+constexpr uint32_t kMaxDynBase = 1024;
+constexpr int kStagesBelowMin = (int)((kTblAddr - kMaxDynBase - kHdrBytes - 16) / kStageBytes);
+constexpr size_t kGemvSmem = (size_t)kTblAddr * 2 + (size_t)(kNumStages - kStagesBelowMin) * kStageBytes;
 constexpr int kCostRows = 3;                // a unit costs kCostRows (its weights) + its token count
 constexpr unsigned long long kWaitNs = 2000000000ull;   // a ring stage not filled within 2 s: give up
 
 enum Epi { kStore = 0, kRelu2 = 1, kRelu2Q8 = 2, kDots = 3 };
 
-__device__ int g_iq2_error;   // bit 0: a ring wait timed out
+__device__ int g_iq2_error;   // bit 0: a ring wait timed out; bit 1: the shared-memory layout did not fit
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
     uint32_t d;
@@ -223,14 +230,15 @@ __device__ void build_table(uint32_t* tbl) {
     }
 }
 
-// the eight int8 weights of group g of a chunk (grid bytes qx, sign bytes qyp) as two words
-__device__ __forceinline__ void group_weights(uint32_t tb, uint32_t lane4, uint32_t qx, uint32_t qyp, int g, uint32_t& lo,
-                                              uint32_t& hi) {
-    // address = tb + (index byte << 8) + lane * 4 (+ 128 for the sign half)
+// the eight int8 weights of group g of a chunk (grid bytes qx, sign bytes qyp) as two words; lane_c = kTblAddr | lane*4,
+// lane_s = lane_c | 128
+__device__ __forceinline__ void group_weights(uint32_t lane_c, uint32_t lane_s, uint32_t qx, uint32_t qyp, int g,
+                                              uint32_t& lo, uint32_t& hi) {
+    // address = kTblAddr | (index byte << 8) | lane * 4 (| 128 for the sign half): bytes 0, 2, 3 from the lane word
     const uint32_t sel_b = 0x7604u | ((uint32_t)g << 4);
-    const uint32_t ac = prmt(qx, lane4, sel_b);
-    const uint32_t as = prmt(qyp, lane4 | 128u, sel_b);
-    const uint32_t sel = lds32(tb + ac) + lds32(tb + as);      // nibble j: code_j + 3 * sign_j, in 0..5
+    const uint32_t ac = prmt(qx, lane_c, sel_b);
+    const uint32_t as = prmt(qyp, lane_s, sel_b);
+    const uint32_t sel = lds32(ac) + lds32(as);                // nibble j: code_j + 3 * sign_j, in 0..5
     lo = prmt(0xF82B1908u, 0x0000D5E7u, sel);                  // bytes 8, 25, 43, -8 | -25, -43
     hi = prmt(0xF82B1908u, 0x0000D5E7u, sel >> 16);
 }
@@ -278,10 +286,14 @@ struct Walk {
 };
 
 struct Ring {
-    uint32_t stage0, bar0;   // this warp's stages and barriers
+    uint32_t bar0, a0;       // the CTA's barriers; its first stage below the table
+    int q0, nA;              // this warp's first stage index; stages below the table
     int issued, consumed;    // super-blocks issued into / consumed from the ring
-    __device__ uint32_t stage(int i) const { return stage0 + (uint32_t)((i % kStages) * kStageBytes); }
-    __device__ uint32_t bar(int i) const { return bar0 + (uint32_t)((i % kStages) * 8); }
+    __device__ uint32_t stage(int i) const {
+        const int q = q0 + (i % kStages);
+        return q < nA ? a0 + (uint32_t)(q * kStageBytes) : 2u * kTblAddr + (uint32_t)((q - nA) * kStageBytes);
+    }
+    __device__ uint32_t bar(int i) const { return bar0 + (uint32_t)((q0 + (i % kStages)) * 8); }
 };
 
 // a unit's token ids and activation rows
@@ -327,10 +339,14 @@ __device__ void issue_next(const GemvArgs& a, Walk& pw, int& psb, Toks& pt, Ring
 // One unit: its 32 rows (a lane each) over K in chunk order, NT token rows (nt <= NT real; nt == NT for NT <= 2).
 // Returns false when a ring wait timed out.
 template <int NT, int EPI>
-__device__ bool unit_rows(const GemvArgs& a, const Walk& w, const Toks& t, int nt, uint32_t tb, int lane, Ring& r,
-                          Walk& pw, int& psb, Toks& pt, int nsb) {
-    const uint32_t lane4 = (uint32_t)lane * 4u;
+__device__ bool unit_rows(const GemvArgs& a, const Walk& w, const Toks& t, int nt, int lane, Ring& r, Walk& pw, int& psb,
+                          Toks& pt, int nsb) {
+    const uint32_t lane_c = kTblAddr | ((uint32_t)lane * 4u), lane_s = lane_c | 128u;
     const int row = w.g * kIq2Tile + lane, nc = a.k >> 5;
+    // exact int -> float without a conversion instruction: an integer i with |i| < 2^22 added to the bits of 1.5 * 2^23
+    // gives the float 1.5 * 2^23 + i (the dot's bound is 32 * 43 * 127 = 174752); likewise 2 s4 + 1 in 2^23's mantissa
+    constexpr int kBias = 0x4B400000;
+    constexpr float kBiasF = 12582912.f;
     float acc[NT];
 #pragma unroll
     for (int m = 0; m < NT; m++) acc[m] = 0.f;
@@ -339,6 +355,7 @@ __device__ bool unit_rows(const GemvArgs& a, const Walk& w, const Toks& t, int n
         const bool ok = mbar_wait(r.bar(r.consumed), (uint32_t)((r.consumed / kStages) & 1), kWaitNs);
         if (__any_sync(0xffffffffu, !ok)) return false;
         const float dh8 = __half2float(__ushort_as_half(lds16(st + 2048 + lane * 2))) * 0.125f;
+        const float dh8m = -8388608.f * dh8;   // exact: a power-of-two scaling
 #pragma unroll 1
         for (int j = 0; j < 4; j++) {
             const uint4 q = lds128(st + j * 512 + lane * 16);
@@ -346,30 +363,33 @@ __device__ bool unit_rows(const GemvArgs& a, const Walk& w, const Toks& t, int n
             for (int h = 0; h < 2; h++) {
                 const int c8 = 2 * j + h;
                 const uint32_t qx = h ? q.z : q.x, qy = h ? q.w : q.y;
-                // s4 from the four spare bits (bits 7, 15, 23, 31 -> 28..31), then dA = (d/8) * (2 s4 + 1)
-                const uint32_t s4x2p1 = ((((qy & 0x80808080u) * 0x00204081u) >> 27) & 0x1eu) | 1u;
-                const float dA = dh8 * (float)s4x2p1;
+                // s4 from the four spare bits (bits 7, 15, 23, 31 -> 28..31); dA = (d/8) * (2 s4 + 1), one exact fma:
+                // (2^23 + 2 s4 + 1) * d/8 - 2^23 * d/8
+                const uint32_t s4f = ((((qy & 0x80808080u) * 0x00204081u) >> 27) & 0x1eu) | 0x4B000001u;
+                const float dA = fmaf(__uint_as_float(s4f), dh8, dh8m);
                 uint32_t wq[8];
 #pragma unroll
-                for (int g = 0; g < 4; g++) group_weights(tb, lane4, qx, qy, g, wq[2 * g], wq[2 * g + 1]);
+                for (int g = 0; g < 4; g++) group_weights(lane_c, lane_s, qx, qy, g, wq[2 * g], wq[2 * g + 1]);
 #pragma unroll
                 for (int m = 0; m < NT; m++) {
                     if (NT <= 2 || m < nt) {
                         const uint32_t xa = st + kStageAct + m * 256 + c8 * 32;
                         const uint4 x0 = lds128(xa), x1 = lds128(xa + 16);
-                        int dot = __dp4a((int)wq[0], (int)x0.x, 0);
-                        dot = __dp4a((int)wq[1], (int)x0.y, dot);
-                        dot = __dp4a((int)wq[2], (int)x0.z, dot);
-                        dot = __dp4a((int)wq[3], (int)x0.w, dot);
-                        dot = __dp4a((int)wq[4], (int)x1.x, dot);
-                        dot = __dp4a((int)wq[5], (int)x1.y, dot);
-                        dot = __dp4a((int)wq[6], (int)x1.z, dot);
-                        dot = __dp4a((int)wq[7], (int)x1.w, dot);
+                        // two independent chains of four (half the dependent latency), joined by one add
+                        int da = __dp4a((int)wq[0], (int)x0.x, kBias);
+                        int db = __dp4a((int)wq[4], (int)x1.x, 0);
+                        da = __dp4a((int)wq[1], (int)x0.y, da);
+                        db = __dp4a((int)wq[5], (int)x1.y, db);
+                        da = __dp4a((int)wq[2], (int)x0.z, da);
+                        db = __dp4a((int)wq[6], (int)x1.z, db);
+                        da = __dp4a((int)wq[3], (int)x0.w, da);
+                        db = __dp4a((int)wq[7], (int)x1.w, db);
+                        const int dot = da + db;
                         if constexpr (EPI == kDots) {
-                            a.dots[((size_t)t.id[m] * a.n + row) * nc + sb * 8 + c8] = dot;
+                            a.dots[((size_t)t.id[m] * a.n + row) * nc + sb * 8 + c8] = dot - kBias;
                         } else {
                             const float s = __uint_as_float(lds32(st + kStageScl + m * 32 + c8 * 4));
-                            acc[m] = fmaf(dA * s, (float)dot, acc[m]);
+                            acc[m] = fmaf(dA * s, __int_as_float(dot) - kBiasF, acc[m]);
                         }
                     }
                 }
@@ -407,19 +427,28 @@ __device__ bool unit_rows(const GemvArgs& a, const Walk& w, const Toks& t, int n
 template <int EPI>
 __global__ void __launch_bounds__(kGemvWarps * 32, 1) iq2_gemv_k(GemvArgs a, int nslots) {
     extern __shared__ __align__(128) unsigned char dyn[];
-    __shared__ int s_cnt[kMaxSlots], s_pre[kMaxSlots + 1];
-    uint32_t* tbl = reinterpret_cast<uint32_t*>(dyn);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t tb = (uint32_t)__cvta_generic_to_shared(tbl);
+    // the layout around the table at kTblAddr (see kTblAddr): barriers, counts, prefix, stages below; stages above
+    const uint32_t base = (uint32_t)__cvta_generic_to_shared(dyn);
+    int* s_cnt = reinterpret_cast<int*>(dyn + kNumStages * 8);
+    int* s_pre = s_cnt + kMaxSlots;
     Ring r;
-    r.stage0 = tb + kTableBytes + (uint32_t)(warp * kStages * kStageBytes);
-    r.bar0 = tb + kTableBytes + (uint32_t)(kGemvWarps * kStages * kStageBytes) + (uint32_t)(warp * kStages * 8);
+    r.bar0 = base;
+    r.a0 = (base + kHdrBytes + 15u) & ~15u;
+    r.nA = r.a0 <= kTblAddr ? (int)((kTblAddr - r.a0) / kStageBytes) : 0;
+    if (r.nA > kNumStages) r.nA = kNumStages;
+    r.q0 = warp * kStages;
     r.issued = r.consumed = 0;
+    const uint32_t end = 2u * kTblAddr + (uint32_t)((kNumStages - r.nA) * kStageBytes);
+    if (base + kHdrBytes > kTblAddr || (size_t)end > (size_t)base + kGemvSmem) {
+        if (tid == 0) atomicOr(&g_iq2_error, 2);   // the dynamic shared memory does not start low enough
+        return;
+    }
     if (lane == 0) {
-        for (int i = 0; i < kStages; i++) mbar_init(r.bar0 + 8 * i, 1);
+        for (int i = 0; i < kStages; i++) mbar_init(r.bar0 + 8u * (uint32_t)(r.q0 + i), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    build_table(tbl);
+    build_table(reinterpret_cast<uint32_t*>(dyn + (kTblAddr - base)));
     pdl_wait();
     const int G = a.n / kIq2Tile, nsb = a.k >> 8;
     for (int s = tid; s < nslots; s += blockDim.x) {
@@ -455,9 +484,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) iq2_gemv_k(GemvArgs a, int
         const int nt = w.nt();
         Toks t;
         unit_tokens(a, w, nt, t);
-        if (nt == 1) healthy = unit_rows<1, EPI>(a, w, t, nt, tb, lane, r, pw, psb, pt, nsb);
-        else if (nt == 2) healthy = unit_rows<2, EPI>(a, w, t, nt, tb, lane, r, pw, psb, pt, nsb);
-        else healthy = unit_rows<4, EPI>(a, w, t, nt, tb, lane, r, pw, psb, pt, nsb);
+        if (nt == 1) healthy = unit_rows<1, EPI>(a, w, t, nt, lane, r, pw, psb, pt, nsb);
+        else if (nt == 2) healthy = unit_rows<2, EPI>(a, w, t, nt, lane, r, pw, psb, pt, nsb);
+        else healthy = unit_rows<4, EPI>(a, w, t, nt, lane, r, pw, psb, pt, nsb);
         w.next();
     }
     if (!healthy) {
