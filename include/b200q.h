@@ -149,6 +149,35 @@ int b200q_moe_down(const void* slab, int E, int n, int k, const int* counts, con
                    const int8_t* aq, const float* as, float* y, int ldy, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------
+ * Prompt-length GEMMs on the tcgen05 tensor cores (kind::f16: fp16 operands, fp32 accumulation in TMEM).
+ * --------------------------------------------------------------------------------------------------------- */
+
+/* Grouping for prompt chunks, any number of pairs (moe_group_k's job at prompt sizes, bolt_kernels.cu:275-325, which
+ * libbolt does in one CTA): counts [E], offsets [E+1], order [pairs] (an expert's pairs in arrival order),
+ * fill_scratch [E] ints.  E <= 512. */
+int b200q_moe_group_large(const int* ridx, int pairs, int E, int* counts, int* offsets, int* order, int* fill_scratch,
+                          void* stream);
+
+/* The prompt path of the routed experts (replaces moe_up_tile / moe_down_tile, moe_tile_k bolt_kernels.cu:697-862):
+ * one launch per projection over the expert-sorted pairs, 128 pairs x 256 weight rows a CTA.  Weights fp16 with the
+ * chunk scale folded in (PIQ2's arithmetic, bolt_mma.cu:380-397, in fp16), activations fp16.
+ *   up:   act_f16[p][0..n) = relu(W_up[e] . x[p / topk])^2 as fp16;   x [T][k] bf16 or fp32
+ *   down: y[p][0..n) = W_down[e] . act_f16[p] (fp32)
+ * slab: E experts packed rt32 (b200q_iq2_pack).  max_tiles >= sum over experts of ceil(count / 128), for example
+ * pairs / 128 + E.  n % 32 == 0, k % 256 == 0; pointers 16-byte aligned. */
+int b200q_moe_up_tc(const void* slab, int E, int n, int k, const int* counts, const int* offsets, const int* order, int topk,
+                    const void* x, int x_dtype, void* act_f16, int max_tiles, void* stream);
+int b200q_moe_down_tc(const void* slab, int E, int n, int k, const int* counts, const int* offsets, const int* order,
+                      const void* act_f16, float* y, int max_tiles, void* stream);
+
+/* Q8_0 prompt GEMM (replaces mma_q8 / mma_q8_multi at prompt row counts, mma_big_k bolt_mma.cu:611-696):
+ * y[t][n] = sum_k fp16(q * d) x[t][k] for any T.  The weights use the "rows" layout (b200q_q8_rows_pack: q [n][k] then
+ * d [n][k/32] fp16, n*k*17/16 bytes); fused q/k/v projections are one matrix of their stacked rows.  k % 64 == 0. */
+size_t b200q_q8_rows_bytes(int64_t n, int k);
+int b200q_q8_rows_pack(const void* raw, void* packed, int64_t n, int k, void* stream);
+int b200q_q8_gemm(const void* w, int n, int k, const void* x, int x_dtype, int ldx, int T, float* y, int ldy, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------
  * One decode MoE layer, the sequence enqueue_block runs for a MoE block
  * (bolt_host.cu:665-720) fused into four launches: router + grouping + int8 rows of x; up with relu^2 and the
  * int8 rows of the result; down; weighted combine plus the shared expert.

@@ -62,6 +62,13 @@ def lib():
             "b200q_nv4_gemv": (i32, [vp, f32, i32, i32, vp, i32, i32, i32, vp, i32, vp, sz, vp]),
             "b200q_q8_gemv_workspace_bytes": (sz, [i32, i32, i32]),
             "b200q_q8_gemv": (i32, [vp, i32, i32, vp, i32, i32, i32, vp, i32, vp, sz, vp]),
+            "b200q_moe_group_large": (i32, [vp, i32, i32, vp, vp, vp, vp, vp]),
+            "b200q_moe_up_tc": (i32, [vp, i32, i32, i32, vp, vp, vp, i32, vp, i32, vp, i32, vp]),
+            "b200q_moe_down_tc": (i32, [vp, i32, i32, i32, vp, vp, vp, vp, vp, i32, vp]),
+            "b200q_q8_rows_bytes": (sz, [i64, i32]),
+            "b200q_q8_rows_pack": (i32, [vp, vp, i64, i32, vp]),
+            "b200q_q8_gemm": (i32, [vp, i32, i32, vp, i32, i32, i32, vp, i32, vp]),
+            "b200q_device_error": (i32, [i32]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -269,6 +276,64 @@ def mma_q8(w, n, k, x, y=None):
     _check(lib().b200q_q8_gemv(_p(w), n, k, _p(x), _dtype_code(x), x.stride(0), T, _p(y), y.stride(0), ws, wb, _s()),
            "mma_q8")
     return y
+
+
+# -------------------------------------------------------------------------------------------------------------
+# prompt-length GEMMs (tcgen05)
+# -------------------------------------------------------------------------------------------------------------
+def device_error(clear=True):
+    """Errors the kernels recorded on this device (0: none), see b200q_device_error."""
+    return lib().b200q_device_error(1 if clear else 0)
+
+
+def tile_q8_rows(raw, n, k):
+    """Q8_0 ggml blocks [n][k/32][34] -> the prompt GEMM's rows layout (q [n][k], then d [n][k/32] fp16)."""
+    out = torch.empty(lib().b200q_q8_rows_bytes(n, k), dtype=torch.uint8, device=raw.device)
+    _check(lib().b200q_q8_rows_pack(_p(_dev(raw, "raw")), _p(out), n, k, _s()), "tile_q8_rows")
+    return out
+
+
+def mma_q8_prompt(w_rows, n, k, x, y=None):
+    """y [T][n] fp32 = fp16(q d) . fp16(x) for any T (the tcgen05 prompt GEMM)."""
+    _dev(x, "x")
+    T = x.shape[0]
+    y = torch.empty(T, n, dtype=torch.float32, device=x.device) if y is None else y
+    _check(lib().b200q_q8_gemm(_p(w_rows), n, k, _p(x), _dtype_code(x), x.stride(0), T, _p(y), y.stride(0), _s()),
+           "mma_q8_prompt")
+    return y
+
+
+def k_moe_group_large(ridx, E):
+    """Grouping for any number of pairs: counts [E], offsets [E+1], order [pairs]."""
+    _dev(ridx, "ridx")
+    pairs = ridx.numel()
+    counts = torch.empty(E, dtype=torch.int32, device=ridx.device)
+    offsets = torch.empty(E + 1, dtype=torch.int32, device=ridx.device)
+    order = torch.empty(max(pairs, 1), dtype=torch.int32, device=ridx.device)
+    fill = torch.empty(E, dtype=torch.int32, device=ridx.device)
+    _check(lib().b200q_moe_group_large(_p(ridx), pairs, E, _p(counts), _p(offsets), _p(order), _p(fill), _s()),
+           "k_moe_group_large")
+    return counts, offsets, order[:pairs]
+
+
+def moe_up_tile(slab, E, n, k, counts, offsets, order, topk, x, act=None):
+    """Prompt path of the routed up projection: act [pairs][n] fp16 = relu(W_up[e] . x[p / topk])^2."""
+    pairs = order.numel()
+    act = torch.empty(max(pairs, 1), n, dtype=torch.float16, device=x.device) if act is None else act
+    tiles = pairs // 128 + E
+    _check(lib().b200q_moe_up_tc(_p(slab), E, n, k, _p(counts), _p(offsets), _p(order), topk, _p(_dev(x, "x")),
+                                 _dtype_code(x), _p(act), tiles, _s()), "moe_up_tile")
+    return act[:pairs]
+
+
+def moe_down_tile(slab, E, n, k, counts, offsets, order, act, y=None):
+    """Prompt path of the routed down projection: y [pairs][n] fp32 = W_down[e] . act[p]."""
+    pairs = order.numel()
+    y = torch.empty(max(pairs, 1), n, dtype=torch.float32, device=act.device) if y is None else y
+    tiles = pairs // 128 + E
+    _check(lib().b200q_moe_down_tc(_p(slab), E, n, k, _p(counts), _p(offsets), _p(order), _p(act), _p(y), tiles, _s()),
+           "moe_down_tile")
+    return y[:pairs]
 
 
 # -------------------------------------------------------------------------------------------------------------

@@ -539,6 +539,8 @@ bool iq2_shape_ok(int64_t n, int k) { return n > 0 && n % kIq2Tile == 0 && n <= 
 // the GEMVs stream weights, int8 rows and scales with bulk copies, which need 16-byte aligned addresses
 static bool a16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
+int tc_error_read(int clear);   // tc_gemm.cu
+
 }  // namespace b200q
 
 using namespace b200q;
@@ -574,7 +576,9 @@ int b200q_device_error(int clear) {
         const int z = 0;
         cudaMemcpyToSymbol(g_iq2_error, &z, sizeof(int));
     }
-    return v;
+    const int t = b200q::tc_error_read(clear);
+    if (t < 0) return -1;
+    return v | (t << 4);
 }
 
 int b200q_iq2_gemv(const void* w, int n, int k, const int8_t* xq, const float* xs, int T, float* y, int ldy, int epi,

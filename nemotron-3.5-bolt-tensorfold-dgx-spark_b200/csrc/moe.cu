@@ -168,6 +168,46 @@ __global__ void __launch_bounds__(512) group_k(const int* __restrict__ ridx, int
 }
 
 // ---------------------------------------------------------------------------------------------------------
+// grouping for prompt chunks (any number of pairs): histogram, scan, scatter.  Inside an expert's run the pairs are in
+// arrival order; the prompt GEMMs compute every row on its own, so their results do not depend on that order.
+// ---------------------------------------------------------------------------------------------------------
+__global__ void group_zero_k(int* __restrict__ counts, int* __restrict__ fill, int E) {
+    pdl_wait();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < E; i += gridDim.x * blockDim.x) { counts[i] = 0; fill[i] = 0; }
+    pdl_trigger();
+}
+__global__ void group_hist_k(const int* __restrict__ ridx, int pairs, int* __restrict__ counts) {
+    pdl_wait();
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < pairs; p += gridDim.x * blockDim.x) atomicAdd(&counts[ridx[p]], 1);
+    pdl_trigger();
+}
+__global__ void __launch_bounds__(512) group_scan_k(const int* __restrict__ counts, int E, int* __restrict__ offsets) {
+    pdl_wait();
+    __shared__ int s[512];
+    const int tid = threadIdx.x;
+    s[tid] = tid < E ? counts[tid] : 0;
+    __syncthreads();
+    for (int off = 1; off < 512; off <<= 1) {
+        const int v = tid >= off ? s[tid - off] : 0;
+        __syncthreads();
+        s[tid] += v;
+        __syncthreads();
+    }
+    if (tid < E) offsets[tid] = s[tid] - counts[tid];
+    if (tid == 0) offsets[E] = s[511];
+    pdl_trigger();
+}
+__global__ void group_scatter_k(const int* __restrict__ ridx, int pairs, const int* __restrict__ offsets, int* __restrict__ fill,
+                                int* __restrict__ order) {
+    pdl_wait();
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < pairs; p += gridDim.x * blockDim.x) {
+        const int e = ridx[p];
+        order[offsets[e] + atomicAdd(&fill[e], 1)] = p;
+    }
+    pdl_trigger();
+}
+
+// ---------------------------------------------------------------------------------------------------------
 // decode prologue, one launch: block 0 routes every token (a warp per token) and groups the pairs; the other
 // blocks write the int8 rows of x (a warp per 32-group).
 // ---------------------------------------------------------------------------------------------------------
@@ -302,6 +342,23 @@ int b200q_moe_group(const int* ridx, int pairs, int E, int* counts, int* offsets
     if ((!ridx && pairs > 0) || !counts || !offsets || !order || pairs < 0 || pairs > 4096 || E <= 0 || E > 512)
         return B200Q_EINVAL;
     launch(group_k, dim3(1), dim3(512), 0, (cudaStream_t)stream, ridx, pairs, E, counts, offsets, order);
+    return launched();
+}
+
+int b200q_moe_group_large(const int* ridx, int pairs, int E, int* counts, int* offsets, int* order, int* fill_scratch,
+                          void* stream) {
+    if ((!ridx && pairs > 0) || !counts || !offsets || !order || !fill_scratch || pairs < 0 || E <= 0 || E > 512)
+        return B200Q_EINVAL;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int blocks = pairs > 0 ? (pairs + 255) / 256 < 1024 ? (pairs + 255) / 256 : 1024 : 1;
+    int st;
+    launch(group_zero_k, dim3(1), dim3(512), 0, s, counts, fill_scratch, E);
+    if ((st = launched()) != B200Q_OK) return st;
+    launch(group_hist_k, dim3(blocks), dim3(256), 0, s, ridx, pairs, counts);
+    if ((st = launched()) != B200Q_OK) return st;
+    launch(group_scan_k, dim3(1), dim3(512), 0, s, (const int*)counts, E, offsets);
+    if ((st = launched()) != B200Q_OK) return st;
+    launch(group_scatter_k, dim3(blocks), dim3(256), 0, s, ridx, pairs, (const int*)offsets, fill_scratch, order);
     return launched();
 }
 
