@@ -115,6 +115,75 @@ def make_layers(b200q, device):
     return layers
 
 
+def zipf_routing(seed, tokens, topk, s=1.1):
+    """BASELINE config 4's routing: Zipf(s) over the experts through a seeded rank -> expert permutation, top-k
+    distinct experts a token."""
+    rng = np.random.default_rng(seed)
+    perm = rng.permutation(E)
+    p = 1.0 / np.arange(1, E + 1) ** s
+    p /= p.sum()
+    ridx = np.empty((tokens, topk), np.int32)
+    for t in range(tokens):
+        ridx[t] = perm[rng.choice(E, size=topk, replace=False, p=p)]
+    return ridx
+
+
+def prefill_bench(b200q, layer, device, iters=5):
+    """BASELINE config 4 on the tcgen05 prompt GEMMs: the routed experts' grouped up (ReLU^2) and down GEMMs over
+    8192 tokens x top-6 (Zipf 1.1), and the Q8_0 GQA projections (q/k/v fused, then o) on the same 8192 tokens."""
+    Tp = 8192
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(Tp, H, generator=g).to(torch.bfloat16).to(device)
+    ridx = torch.from_numpy(zipf_routing(12, Tp, TOPK).reshape(-1)).to(device)
+    pairs = Tp * TOPK
+    counts, offsets, order = b200q.k_moe_group_large(ridx, E)
+    act = torch.empty(pairs, F, dtype=torch.float16, device=device)
+    y = torch.empty(pairs, H, dtype=torch.float32, device=device)
+    # Q8_0 GQA weights (32 q heads / 8 kv heads x 128): int8 U{-127..127}, fp16 d per 32
+    def q8(seed, n, k):
+        r = np.random.default_rng(seed)
+        qv = r.integers(-127, 128, (n, k // 32, 32), dtype=np.int8)
+        d = r.uniform(1e-3, 1e-2, (n, k // 32)).astype(np.float16)
+        raw = np.concatenate([d.view(np.uint8).reshape(n, k // 32, 2), qv.view(np.uint8)], -1).reshape(-1)
+        return b200q.tile_q8_rows(torch.from_numpy(raw).to(device), n, k)
+    wqkv, wo = q8(21, 6144, H), q8(22, H, H)
+    qkv = torch.empty(Tp, 6144, dtype=torch.float32, device=device)
+    attn = torch.randn(Tp, H, generator=g).to(torch.bfloat16).to(device)
+    o = torch.empty(Tp, H, dtype=torch.float32, device=device)
+
+    def moe():
+        b200q.moe_up_tile(layer.up, E, F, H, counts, offsets, order, TOPK, x, act=act)
+        b200q.moe_down_tile(layer.down, E, H, F, counts, offsets, order, act, y=y)
+
+    def gqa():
+        b200q.mma_q8_prompt(wqkv, 6144, H, x, y=qkv)
+        b200q.mma_q8_prompt(wo, H, H, attn, y=o)
+
+    res = {}
+    s = torch.cuda.current_stream()
+    for name, fn, flops in (("moe", moe, 2.0 * pairs * H * F * 2), ("gqa", gqa, 2.0 * Tp * H * (6144 + H))):
+        for _ in range(2):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(s)
+        for _ in range(iters):
+            fn()
+        e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        res[name] = (ms, flops / (ms * 1e-3) / 1e12)
+    err = b200q.device_error()
+    cnt = counts.cpu().numpy()
+    return {"workload": "BASELINE config 4: 8192 tokens x top-6 = 49152 rows over 128 IQ2_XXS experts (Zipf 1.1, "
+                        "seeded permutation), 4096 -> 2048 -> 4096 ReLU^2; Q8_0 GQA q/k/v (fused 6144) + o on the "
+                        "same 8192 tokens",
+            "arithmetic": "fp16 operands (scales folded, rounded once), fp32 accumulation: tcgen05.mma kind::f16",
+            "moe_ms": round(res["moe"][0], 4), "moe_tflops": round(res["moe"][1], 1),
+            "gqa_ms": round(res["gqa"][0], 4), "gqa_tflops": round(res["gqa"][1], 1),
+            "hottest_expert_rows": int(cnt.max()), "device_error": err}
+
+
 def make_batches(rank, device):
     g = torch.Generator().manual_seed(77 + rank)
     xs = [torch.randn(T, H, generator=g).to(torch.bfloat16) for _ in range(BATCHES)]
@@ -225,6 +294,17 @@ def run_ours(args, rank, world, local_rank):
 
     line = None
     if rank == 0:
+        pre = prefill_bench(b200q, layers[0], device) if args.prefill else None
+        if pre:
+            bf16_peak = 1590.0
+            pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+            if os.path.exists(pk):
+                with open(pk) as f:
+                    bf16_peak = float(json.load(f).get("bf16_tflops", bf16_peak))
+            pre["peak_tflops"] = bf16_peak
+            pre["peak_kind"] = "measured cuBLAS bf16 burst (fp16 runs at the same dense rate)"
+            pre["moe_frac"] = round(pre["moe_tflops"] / bf16_peak, 4)
+            pre["gqa_frac"] = round(pre["gqa_tflops"] / bf16_peak, 4)
         cpu = cpu_baseline(threads=os.cpu_count() or 1, min_seconds=args.cpu_seconds)
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -248,6 +328,8 @@ def run_ours(args, rank, world, local_rank):
             "gpu_launches": 4 * args.steps,
             "clocks": clk.summary(),
         }
+        if pre:
+            line["prefill"] = pre
     if dist:
         torch.distributed.destroy_process_group()
     return line
@@ -317,6 +399,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=4, help="layer copies rotated to defeat L2 (1 for small profiles)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="length of the CPU-baseline sample")
+    ap.add_argument("--no-prefill", dest="prefill", action="store_false", help="skip the config-4 prefill GEMMs")
     args = ap.parse_args()
     global LAYERS
     LAYERS = max(1, args.layers)
