@@ -53,7 +53,8 @@ int b200q_abi(void);
 int b200q_last_cuda_error(void);
 const char* b200q_strerror(int status);
 /* Errors the kernels recorded on the current device (a bitmask, 0 if none; bit 0: a streaming GEMV's bounded wait for
- * its copies ran out, so its outputs are incomplete); synchronous.  clear != 0 resets it.  No counterpart in libbolt,
+ * its copies ran out, so its outputs are incomplete; bit 4: the same in an fp16 tensor-core GEMM; bit 8: in the NVFP4
+ * tensor-core GEMM); synchronous.  clear != 0 resets it.  No counterpart in libbolt,
  * whose kernels do not wait on barriers. */
 int b200q_device_error(int clear);
 
@@ -176,6 +177,20 @@ int b200q_moe_down_tc(const void* slab, int E, int n, int k, const int* counts, 
 size_t b200q_q8_rows_bytes(int64_t n, int k);
 int b200q_q8_rows_pack(const void* raw, void* packed, int64_t n, int k, void* stream);
 int b200q_q8_gemm(const void* w, int n, int k, const void* x, int x_dtype, int ldx, int T, float* y, int ldy, void* stream);
+
+/* NVFP4 prompt GEMM on the block-scaled fp4 tensor cores (replaces quant_nv4_rows + mma_nv4_fp4, bolt_mma.cu:925-1059,
+ * dispatched for T >= 256 at bolt_host.cu:634,644):
+ *   y[t][n] = s2 * sum_k e2m1(x4[t][k]) e4m3(sx[t][k/16]) e2m1(q[n][k]) e4m3(sc[n][k/16])      (fp32, [T][ldy])
+ * Weights: b200q_nv4_tc_pack turns the checkpoint's q [n][k/2] (low nibble first) and sc [n][k/16] e4m3 into the
+ * tensor cores' tile image (tile_nv4w_k, bolt_mma.cu:892-923): b200q_nv4_tc_bytes(n, k) bytes, n rounded up to 256.
+ * Rows: b200q_quant_nv4_rows quantises x [T][ldx] (fp32 or bf16) to NVFP4 exactly as quant_nv4_rows_k does (scale
+ * e4m3_enc(amax / 6) per 16, values e2m1_enc(v / scale)) into b200q_nv4_rows_bytes(T, k) bytes (T rounded up to
+ * 128).  k % 256 == 0; pointers 16-byte aligned. */
+size_t b200q_nv4_tc_bytes(int64_t n, int k);
+int b200q_nv4_tc_pack(const void* q, const void* sc, void* packed, int64_t n, int k, void* stream);
+size_t b200q_nv4_rows_bytes(int T, int k);
+int b200q_quant_nv4_rows(const void* x, int x_dtype, int ldx, int T, int k, void* rows, void* stream);
+int b200q_nv4_gemm(const void* w, int n, int k, float s2, const void* rows, int T, float* y, int ldy, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------
  * One decode MoE layer, the sequence enqueue_block runs for a MoE block

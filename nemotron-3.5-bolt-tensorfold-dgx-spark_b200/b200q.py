@@ -69,6 +69,11 @@ def lib():
             "b200q_q8_rows_pack": (i32, [vp, vp, i64, i32, vp]),
             "b200q_q8_gemm": (i32, [vp, i32, i32, vp, i32, i32, i32, vp, i32, vp]),
             "b200q_device_error": (i32, [i32]),
+            "b200q_nv4_tc_bytes": (sz, [i64, i32]),
+            "b200q_nv4_tc_pack": (i32, [vp, vp, vp, i64, i32, vp]),
+            "b200q_nv4_rows_bytes": (sz, [i32, i32]),
+            "b200q_quant_nv4_rows": (i32, [vp, i32, i32, i32, i32, vp, vp]),
+            "b200q_nv4_gemm": (i32, [vp, i32, i32, f32, vp, i32, vp, i32, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -300,6 +305,30 @@ def mma_q8_prompt(w_rows, n, k, x, y=None):
     y = torch.empty(T, n, dtype=torch.float32, device=x.device) if y is None else y
     _check(lib().b200q_q8_gemm(_p(w_rows), n, k, _p(x), _dtype_code(x), x.stride(0), T, _p(y), y.stride(0), _s()),
            "mma_q8_prompt")
+    return y
+
+
+def tile_nv4w(q, sc, n, k):
+    """NVFP4 q [n][k/2] + sc [n][k/16] e4m3 -> the block-scaled fp4 prompt GEMM's tile image (tile_nv4w)."""
+    out = torch.empty(lib().b200q_nv4_tc_bytes(n, k), dtype=torch.uint8, device=q.device)
+    _check(lib().b200q_nv4_tc_pack(_p(_dev(q, "q")), _p(_dev(sc, "sc")), _p(out), n, k, _s()), "tile_nv4w")
+    return out
+
+
+def quant_nv4_rows(x, k=None, out=None):
+    """Rows x [T][k] (fp32 or bf16) -> NVFP4 rows tile image (quant_nv4_rows: e4m3 scale amax/6 per 16, e2m1 values)."""
+    _dev(x, "x")
+    T, k = x.shape[0], x.shape[1] if k is None else k
+    nb = lib().b200q_nv4_rows_bytes(T, k)
+    out = torch.empty(nb, dtype=torch.uint8, device=x.device) if out is None else out
+    _check(lib().b200q_quant_nv4_rows(_p(x), _dtype_code(x), x.stride(0), T, k, _p(out), _s()), "quant_nv4_rows")
+    return out
+
+
+def mma_nv4_fp4(w_tc, s2, n, k, rows, T, y=None):
+    """y [T][n] fp32 = s2 * (NVFP4 rows) . (NVFP4 weights) on the block-scaled fp4 tensor cores (mma_nv4_fp4)."""
+    y = torch.empty(T, n, dtype=torch.float32, device=rows.device) if y is None else y
+    _check(lib().b200q_nv4_gemm(_p(w_tc), n, k, float(s2), _p(rows), T, _p(y), y.stride(0), _s()), "mma_nv4_fp4")
     return y
 
 

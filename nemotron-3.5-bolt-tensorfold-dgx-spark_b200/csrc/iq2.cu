@@ -540,6 +540,7 @@ bool iq2_shape_ok(int64_t n, int k) { return n > 0 && n % kIq2Tile == 0 && n <= 
 static bool a16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
 int tc_error_read(int clear);   // tc_gemm.cu
+int nv4_error_read(int clear);  // nv4_gemm.cu
 
 }  // namespace b200q
 
@@ -576,9 +577,9 @@ int b200q_device_error(int clear) {
         const int z = 0;
         cudaMemcpyToSymbol(g_iq2_error, &z, sizeof(int));
     }
-    const int t = b200q::tc_error_read(clear);
-    if (t < 0) return -1;
-    return v | (t << 4);
+    const int t = b200q::tc_error_read(clear), f = b200q::nv4_error_read(clear);
+    if (t < 0 || f < 0) return -1;
+    return v | (t << 4) | (f << 8);
 }
 
 int b200q_iq2_gemv(const void* w, int n, int k, const int8_t* xq, const float* xs, int T, float* y, int ldy, int epi,

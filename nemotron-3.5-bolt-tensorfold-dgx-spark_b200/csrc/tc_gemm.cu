@@ -16,7 +16,7 @@
 //   A      activations rounded to fp16 once (exact for bf16 inputs in fp16's normal range).
 // Every barrier wait is bounded (%globaltimer); on a timeout the kernel records an error (b200q_device_error), frees
 // its TMEM and returns.
-#include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace b200q {
 
@@ -28,7 +28,6 @@ constexpr int kStage = kATile + kBTile;         // 48 KB
 constexpr int kProdWarps = 8, kEpiWarps = 4;
 constexpr int kTcThreads = (kEpiWarps + 1 + kProdWarps) * 32;   // epilogue warps, the MMA warp, producer warps
 constexpr size_t kTcSmem = (size_t)kTcStages * kStage + 1024 /*align*/ + 256 /*barriers*/;
-constexpr unsigned long long kTcWaitNs = 2000000000ull;
 
 __device__ int g_tc_error;   // bit 0: a barrier wait timed out (reported by b200q_device_error)
 
@@ -42,48 +41,6 @@ int tc_error_read(int clear) {
     return v;
 }
 
-// ---------------------------------------------------------------------------------------------------------
-// PTX helpers
-// ---------------------------------------------------------------------------------------------------------
-__device__ __forceinline__ unsigned long long tc_now() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ __forceinline__ void tc_mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void tc_mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ bool tc_mbar_try(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ bool tc_mbar_wait(uint32_t bar, uint32_t parity) {
-    if (tc_mbar_try(bar, parity)) return true;
-    const unsigned long long t0 = tc_now();
-    while (!tc_mbar_try(bar, parity))
-        if (tc_now() - t0 > kTcWaitNs) return false;
-    return true;
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-// UMMA shared-memory descriptor, K-major, 128-byte swizzle: start >> 4, leading offset 1 (unused for swizzled
-// K-major), stride offset 1024 B (8-row atoms), version 1, layout type 2 (SWIZZLE_128B)
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-    d |= (uint64_t)1 << 16;
-    d |= (uint64_t)(1024 >> 4) << 32;
-    d |= (uint64_t)1 << 46;
-    d |= (uint64_t)2 << 61;
-    return d;
-}
 // instruction descriptor, kind::f16: fp32 accumulator, fp16 A and B, both K-major, N = 256, M = 128
 constexpr uint32_t kIdescF16 = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(kTN >> 3) << 17) | ((uint32_t)(kTM >> 4) << 24);
 
@@ -92,26 +49,6 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b
         "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p; }"
         ::"r"(tmem_d), "l"(a), "l"(b), "r"(kIdescF16), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
-}
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// the 16-byte chunk c of row r of a swizzled K-major tile
-__device__ __forceinline__ uint32_t sw128(uint32_t tile, int r, int c) { return tile + (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
-__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
-    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
 }
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
