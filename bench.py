@@ -137,7 +137,6 @@ def prefill_bench(b200q, layer, device, iters=5):
     ridx = torch.from_numpy(zipf_routing(12, Tp, TOPK).reshape(-1)).to(device)
     pairs = Tp * TOPK
     counts, offsets, order = b200q.k_moe_group_large(ridx, E)
-    act = torch.empty(pairs, F, dtype=torch.float16, device=device)
     y = torch.empty(pairs, H, dtype=torch.float32, device=device)
     # Q8_0 GQA weights (32 q heads / 8 kv heads x 128): int8 U{-127..127}, fp16 d per 32
     def q8(seed, n, k):
@@ -145,15 +144,14 @@ def prefill_bench(b200q, layer, device, iters=5):
         qv = r.integers(-127, 128, (n, k // 32, 32), dtype=np.int8)
         d = r.uniform(1e-3, 1e-2, (n, k // 32)).astype(np.float16)
         raw = np.concatenate([d.view(np.uint8).reshape(n, k // 32, 2), qv.view(np.uint8)], -1).reshape(-1)
-        return b200q.tile_q8_rows(torch.from_numpy(raw).to(device), n, k)
+        return b200q.tile_q8_tc(torch.from_numpy(raw).to(device), n, k)
     wqkv, wo = q8(21, 6144, H), q8(22, H, H)
     qkv = torch.empty(Tp, 6144, dtype=torch.float32, device=device)
     attn = torch.randn(Tp, H, generator=g).to(torch.bfloat16).to(device)
     o = torch.empty(Tp, H, dtype=torch.float32, device=device)
 
     def moe():
-        b200q.moe_up_tile(layer.up, E, F, H, counts, offsets, order, TOPK, x, act=act)
-        b200q.moe_down_tile(layer.down, E, H, F, counts, offsets, order, act, y=y)
+        b200q.moe_prompt(layer.up, layer.down, E, H, F, counts, offsets, order, TOPK, x, mo=y)
 
     def gqa():
         b200q.mma_q8_prompt(wqkv, 6144, H, x, y=qkv)
@@ -222,6 +220,8 @@ def run_ours(args, rank, world, local_rank):
         if dist:
             torch.distributed.barrier()
 
+    for i in range(BATCHES):      # one untimed pass over every batch records its routing for the byte count
+        step(i)
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()

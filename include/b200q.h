@@ -159,24 +159,35 @@ int b200q_moe_down(const void* slab, int E, int n, int k, const int* counts, con
 int b200q_moe_group_large(const int* ridx, int pairs, int E, int* counts, int* offsets, int* order, int* fill_scratch,
                           void* stream);
 
-/* The prompt path of the routed experts (replaces moe_up_tile / moe_down_tile, moe_tile_k bolt_kernels.cu:697-862):
- * one launch per projection over the expert-sorted pairs, 128 pairs x 256 weight rows a CTA.  Weights fp16 with the
- * chunk scale folded in (PIQ2's arithmetic, bolt_mma.cu:380-397, in fp16), activations fp16.
- *   up:   act_f16[p][0..n) = relu(W_up[e] . x[p / topk])^2 as fp16;   x [T][k] bf16 or fp32
- *   down: y[p][0..n) = W_down[e] . act_f16[p] (fp32)
- * slab: E experts packed rt32 (b200q_iq2_pack).  max_tiles >= sum over experts of ceil(count / 128), for example
- * pairs / 128 + E.  n % 32 == 0, k % 256 == 0; pointers 16-byte aligned. */
-int b200q_moe_up_tc(const void* slab, int E, int n, int k, const int* counts, const int* offsets, const int* order, int topk,
-                    const void* x, int x_dtype, void* act_f16, int max_tiles, void* stream);
-int b200q_moe_down_tc(const void* slab, int E, int n, int k, const int* counts, const int* offsets, const int* order,
-                      const void* act_f16, float* y, int max_tiles, void* stream);
+/* ---------------------------------------------------------------------------------------------------------
+ * Prompt-length GEMMs on the tcgen05 tensor cores (kind::f16, fp32 accumulation): the weights are dequantised
+ * inside the kernel to fp16 with their scale folded in and rounded once (libbolt's PQ8 / PIQ2 arithmetic,
+ * bolt_mma.cu:234-254, 380-397, in fp16), the activations rounded to fp16 once.  A CTA computes 256 rows x 256
+ * weight rows; the activations are first converted into an fp16 "rows image" in the workspace.
+ * --------------------------------------------------------------------------------------------------------- */
+
+/* One prompt MoE projection pair over the expert-sorted pairs (replaces moe_up_tile / moe_down_tile, moe_tile_k
+ * bolt_kernels.cu:697-862, and the shared expert's moe_tile_dense, :881-893):
+ *   act[p] = fp16(relu(W_up[e] . x[p / topk])^2),   mo[p][0..H) = W_down[e] . act[p]   (fp32, pair-indexed)
+ * for every pair p of expert e, given b200q_moe_group_large's counts / offsets / order of the pairs' experts.
+ * up: slab of E experts [F][H], down: slab of E experts [H][F] (packed rt32); x [T][H] fp32 or bf16 (ldx = H).
+ * act_rows: NULL, or [pairs][F] fp16 receiving act (inspection only; it costs one extra pass).
+ * workspace >= b200q_moe_prompt_workspace_bytes(pairs, E, H, F) (about (pairs + 128 E) (H + F) 2 bytes), 256-byte
+ * aligned.  H % 256 == 0, F % 256 == 0, E <= 512. */
+size_t b200q_moe_prompt_workspace_bytes(int pairs, int E, int H, int F);
+int b200q_moe_prompt(const void* up, const void* down, int E, int H, int F, const int* counts, const int* offsets,
+                     const int* order, int topk, int pairs, const void* x, int x_dtype, float* mo, void* act_rows,
+                     void* workspace, size_t workspace_bytes, void* stream);
 
 /* Q8_0 prompt GEMM (replaces mma_q8 / mma_q8_multi at prompt row counts, mma_big_k bolt_mma.cu:611-696):
- * y[t][n] = sum_k fp16(q * d) x[t][k] for any T.  The weights use the "rows" layout (b200q_q8_rows_pack: q [n][k] then
- * d [n][k/32] fp16, n*k*17/16 bytes); fused q/k/v projections are one matrix of their stacked rows.  k % 64 == 0. */
-size_t b200q_q8_rows_bytes(int64_t n, int k);
-int b200q_q8_rows_pack(const void* raw, void* packed, int64_t n, int k, void* stream);
-int b200q_q8_gemm(const void* w, int n, int k, const void* x, int x_dtype, int ldx, int T, float* y, int ldy, void* stream);
+ * y[t][n] = sum_k fp16(q * d) x[t][k] for any T.  Weights in the "q8 tc" layout (b200q_q8_tc_pack: units of 32 rows x
+ * 32 k, [32][32] int8 then [32] fp16 d, the checkpoint's byte count); fused q/k/v projections are one matrix of
+ * their stacked rows.  workspace >= b200q_q8_gemm_workspace_bytes(T, k).  n % 32 == 0, k % 256 == 0. */
+size_t b200q_q8_tc_bytes(int64_t n, int k);
+int b200q_q8_tc_pack(const void* raw, void* packed, int64_t n, int k, void* stream);
+size_t b200q_q8_gemm_workspace_bytes(int T, int k);
+int b200q_q8_gemm(const void* w, int n, int k, const void* x, int x_dtype, int ldx, int T, float* y, int ldy,
+                  void* workspace, size_t workspace_bytes, void* stream);
 
 /* NVFP4 prompt GEMM on the block-scaled fp4 tensor cores (replaces quant_nv4_rows + mma_nv4_fp4, bolt_mma.cu:925-1059,
  * dispatched for T >= 256 at bolt_host.cu:634,644):

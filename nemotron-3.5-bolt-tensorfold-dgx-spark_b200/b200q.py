@@ -63,11 +63,12 @@ def lib():
             "b200q_q8_gemv_workspace_bytes": (sz, [i32, i32, i32]),
             "b200q_q8_gemv": (i32, [vp, i32, i32, vp, i32, i32, i32, vp, i32, vp, sz, vp]),
             "b200q_moe_group_large": (i32, [vp, i32, i32, vp, vp, vp, vp, vp]),
-            "b200q_moe_up_tc": (i32, [vp, i32, i32, i32, vp, vp, vp, i32, vp, i32, vp, i32, vp]),
-            "b200q_moe_down_tc": (i32, [vp, i32, i32, i32, vp, vp, vp, vp, vp, i32, vp]),
-            "b200q_q8_rows_bytes": (sz, [i64, i32]),
-            "b200q_q8_rows_pack": (i32, [vp, vp, i64, i32, vp]),
-            "b200q_q8_gemm": (i32, [vp, i32, i32, vp, i32, i32, i32, vp, i32, vp]),
+            "b200q_moe_prompt_workspace_bytes": (sz, [i32, i32, i32, i32]),
+            "b200q_moe_prompt": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, i32, i32, vp, i32, vp, vp, vp, sz, vp]),
+            "b200q_q8_tc_bytes": (sz, [i64, i32]),
+            "b200q_q8_tc_pack": (i32, [vp, vp, i64, i32, vp]),
+            "b200q_q8_gemm_workspace_bytes": (sz, [i32, i32]),
+            "b200q_q8_gemm": (i32, [vp, i32, i32, vp, i32, i32, i32, vp, i32, vp, sz, vp]),
             "b200q_device_error": (i32, [i32]),
             "b200q_nv4_tc_bytes": (sz, [i64, i32]),
             "b200q_nv4_tc_pack": (i32, [vp, vp, vp, i64, i32, vp]),
@@ -291,20 +292,21 @@ def device_error(clear=True):
     return lib().b200q_device_error(1 if clear else 0)
 
 
-def tile_q8_rows(raw, n, k):
-    """Q8_0 ggml blocks [n][k/32][34] -> the prompt GEMM's rows layout (q [n][k], then d [n][k/32] fp16)."""
-    out = torch.empty(lib().b200q_q8_rows_bytes(n, k), dtype=torch.uint8, device=raw.device)
-    _check(lib().b200q_q8_rows_pack(_p(_dev(raw, "raw")), _p(out), n, k, _s()), "tile_q8_rows")
+def tile_q8_tc(raw, n, k):
+    """Q8_0 ggml blocks [n][k/32][34] -> the prompt GEMM's q8 tc layout (units of 32 rows x 32 k)."""
+    out = torch.empty(lib().b200q_q8_tc_bytes(n, k), dtype=torch.uint8, device=raw.device)
+    _check(lib().b200q_q8_tc_pack(_p(_dev(raw, "raw")), _p(out), n, k, _s()), "tile_q8_tc")
     return out
 
 
-def mma_q8_prompt(w_rows, n, k, x, y=None):
-    """y [T][n] fp32 = fp16(q d) . fp16(x) for any T (the tcgen05 prompt GEMM)."""
+def mma_q8_prompt(w_tc, n, k, x, y=None):
+    """y [T][n] fp32 = fp16(q d) . fp16(x) for any T (the tcgen05 prompt GEMM; its rows image in a cached workspace)."""
     _dev(x, "x")
     T = x.shape[0]
     y = torch.empty(T, n, dtype=torch.float32, device=x.device) if y is None else y
-    _check(lib().b200q_q8_gemm(_p(w_rows), n, k, _p(x), _dtype_code(x), x.stride(0), T, _p(y), y.stride(0), _s()),
-           "mma_q8_prompt")
+    ws, wb = _WS.get(lib().b200q_q8_gemm_workspace_bytes(T, k), x.device)
+    _check(lib().b200q_q8_gemm(_p(w_tc), n, k, _p(x), _dtype_code(x), x.stride(0), T, _p(y), y.stride(0), ws, wb,
+                               _s()), "mma_q8_prompt")
     return y
 
 
@@ -345,24 +347,21 @@ def k_moe_group_large(ridx, E):
     return counts, offsets, order[:pairs]
 
 
-def moe_up_tile(slab, E, n, k, counts, offsets, order, topk, x, act=None):
-    """Prompt path of the routed up projection: act [pairs][n] fp16 = relu(W_up[e] . x[p / topk])^2."""
+def moe_prompt(up, down, E, H, F, counts, offsets, order, topk, x, mo=None, act=None, workspace=None):
+    """Prompt path of the routed experts (moe_up_tile + moe_down_tile): mo [pairs][H] fp32 = W_down[e] . act[p],
+    act[p] = fp16(relu(W_up[e] . x[p / topk])^2); act (optional, [pairs][F] fp16) receives the intermediate."""
+    _dev(x, "x")
     pairs = order.numel()
-    act = torch.empty(max(pairs, 1), n, dtype=torch.float16, device=x.device) if act is None else act
-    tiles = pairs // 128 + E
-    _check(lib().b200q_moe_up_tc(_p(slab), E, n, k, _p(counts), _p(offsets), _p(order), topk, _p(_dev(x, "x")),
-                                 _dtype_code(x), _p(act), tiles, _s()), "moe_up_tile")
-    return act[:pairs]
-
-
-def moe_down_tile(slab, E, n, k, counts, offsets, order, act, y=None):
-    """Prompt path of the routed down projection: y [pairs][n] fp32 = W_down[e] . act[p]."""
-    pairs = order.numel()
-    y = torch.empty(max(pairs, 1), n, dtype=torch.float32, device=act.device) if y is None else y
-    tiles = pairs // 128 + E
-    _check(lib().b200q_moe_down_tc(_p(slab), E, n, k, _p(counts), _p(offsets), _p(order), _p(act), _p(y), tiles, _s()),
-           "moe_down_tile")
-    return y[:pairs]
+    mo = torch.empty(pairs, H, dtype=torch.float32, device=x.device) if mo is None else mo
+    nb = lib().b200q_moe_prompt_workspace_bytes(pairs, E, H, F)
+    if workspace is None:
+        ws, wb = _WS.get(nb, x.device)
+    else:
+        ws, wb = _p(workspace), workspace.numel()
+    _check(lib().b200q_moe_prompt(_p(up), _p(down), E, H, F, _p(counts), _p(offsets), _p(order), topk, pairs, _p(x),
+                                  _dtype_code(x), _p(mo), _p(act) if act is not None else None, ws, wb, _s()),
+           "moe_prompt")
+    return mo
 
 
 # -------------------------------------------------------------------------------------------------------------

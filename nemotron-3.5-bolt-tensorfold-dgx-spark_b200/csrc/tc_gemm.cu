@@ -1,33 +1,50 @@
-// Prompt-length GEMMs on the sm_100a tensor cores: tcgen05.mma (kind::f16, fp32 accumulation in TMEM).
+// Prompt-length GEMMs of the IQ2_XXS experts and the Q8_0 projections on the sm_100a tensor cores: tcgen05.mma
+// kind::f16 (fp16 operands, fp32 accumulation in TMEM), the weights dequantised inside the kernel.
 //
-// C[m][n] = sum_k A[m][k] * B[n][k]: A the activation rows (tokens), B the weight rows, both K-major.  A CTA owns one
-// 128 x 256 output tile (tokens x weight rows); its accumulator is 256 TMEM columns.  Eight producer warps fill a
-// ring of kStages shared-memory stages: the 128 x 64 fp16 A tile (activation rows converted from bf16 or fp32, or
-// gathered for the grouped MoE) and the 256 x 64 fp16 B tile (weights dequantised from their packed format), both in
-// the 128-byte-swizzled K-major layout the UMMA descriptors name (8-row atoms of 1024 B, row r's 16-byte chunk c at
-// position c ^ (r & 7)).  One thread issues the four m128n256k16 MMAs of a stage and commits them to the stage's
-// "empty" barrier; after the last stage a commit to the "done" barrier releases four epilogue warps, which read the
-// accumulator with tcgen05.ld (warp w: TMEM lanes 32w..32w+31 = tile rows) and write the outputs.
+// C[m][n] = sum_k A[m][k] B[n][k]: A the activation rows (tokens, or the expert-sorted pairs of the MoE), B the weight
+// rows.  A CTA computes a 256 x 256 tile as two 128-row halves that share one B tile (two accumulators of 256 TMEM
+// columns), so every dequantised weight feeds 256 rows.  Per 32-k stage of a 5-stage shared-memory ring:
+//   A        the two 128-row halves (8 KB each), bulk-copied (cp.async.bulk, no tensor map) from an fp16 rows image
+//            by one lane of warp 0;
+//   B        256 weight rows x 32 k in fp16, written by 8 dequantising warps (warp w: rows 32w..32w+31, lane = row)
+//            from the packed weights, which each lane prefetches into registers ahead of use.  IQ2_XXS: a prmt picks
+//            every fp16 value out of its chunk's three scaled magnitudes and a xor sets its sign, with the selectors and
+//            sign masks read from lane-replicated shared-memory tables (conflict-free).  Q8_0: a magic-number prmt
+//            makes the int8 exact in fp16 and one hmul2 applies the scale;
+//   MMA      one lane of warp 1 issues the m128n256k16 MMAs of both halves and commits them to the stage's barrier;
+//   epilogue 8 warps drain the accumulators (tcgen05.ld), hand them back to the MMA warp, and write the outputs.
+// Tiles (up to 256 rows of one group x 256 weight rows) are handed out persistently, one CTA per SM.
 //
-// Numerics: fp16 operands, fp32 accumulation.
-//   Q8_0   B = fp16(q * d): the scale folded and rounded once (2^-11), libbolt's PQ8 (bolt_mma.cu:234-254).
-//   IQ2    B = fp16(d (0.5 + s4) 0.25 * signed grid): the chunk scale folded and rounded once, libbolt's PIQ2
-//          (bolt_mma.cu:380-397) in fp16 instead of bf16.  (FP8 cannot hold the grid magnitudes 25 and 43.)
-//   A      activations rounded to fp16 once (exact for bf16 inputs in fp16's normal range).
-// Every barrier wait is bounded (%globaltimer); on a timeout the kernel records an error (b200q_device_error), frees
-// its TMEM and returns.
+// Shared-memory tiles are K-major with the 64-byte swizzle of the UMMA descriptors: rows of 64 B (32 fp16), 8-row
+// atoms of 512 B, the 16-byte chunk c of row r at position c ^ ((r >> 1) & 3).
+//
+// Rows image: the activations of a launch in fp16, in slots of 128 rows; record (slot, 32-k block kk), 8 KB, is the
+// shared-memory tile above, at (slot * K/32 + kk) * 8192.  For the MoE the slots of expert e hold its pairs in
+// expert-sorted order, 128 a slot; the up projection's epilogue writes fp16(relu(v)^2) straight into the down
+// projection's rows image.
+//
+// Numerics (libbolt's prompt fold, PQ8 bolt_mma.cu:234-254 and PIQ2 bolt_mma.cu:380-397, in fp16):
+//   Q8_0   B = fp16(q * d), the scale folded and rounded once.
+//   IQ2    B = fp16(d (0.5 + s4) / 4 * signed grid), rounded once.  (FP8 cannot hold the grid magnitudes 25 and 43.)
+//   A      activations rounded to fp16 once; the MoE's intermediate act = fp16(relu(v)^2).
+// Every barrier wait is bounded (%globaltimer); on a timeout the kernel records an error (b200q_device_error bit 4),
+// waits for its own copies and MMAs, frees its TMEM and returns.
 #include "tcgen05.cuh"
 
 namespace b200q {
 
-constexpr int kTM = 128, kTN = 256, kTK = 64;
-constexpr int kTcStages = 4;
-constexpr int kATile = kTM * kTK * 2;           // 16 KB
-constexpr int kBTile = kTN * kTK * 2;           // 32 KB
-constexpr int kStage = kATile + kBTile;         // 48 KB
-constexpr int kProdWarps = 8, kEpiWarps = 4;
-constexpr int kTcThreads = (kEpiWarps + 1 + kProdWarps) * 32;   // epilogue warps, the MMA warp, producer warps
-constexpr size_t kTcSmem = (size_t)kTcStages * kStage + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int kXM = 128;                        // rows of a slot and of an MMA half
+constexpr int kXN = 256;                        // weight rows of a tile
+constexpr int kXRec = kXM * 64;                 // 8 KB: a rows-image record (128 rows x 32 fp16)
+constexpr int kXB = kXN * 64;                   // 16 KB: the B tile of a stage
+constexpr int kXStage = 2 * kXRec + kXB;        // 32 KB
+constexpr int kXStages = 5;
+constexpr int kDeqWarps = 8, kXEpiWarps = 8;
+constexpr int kXThreads = (2 + kDeqWarps + kXEpiWarps) * 32;   // 576
+constexpr int kGridTbl = 256 * 16 * 8;          // 32 KB: grid-entry prmt selectors, 16 copies
+constexpr int kSignTbl = 128 * 32 * 4;          // 16 KB: sign masks, 32 copies
+constexpr size_t kXSmem = (size_t)kXStages * kXStage + kGridTbl + kSignTbl + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint32_t kXTmemCols = 512;            // two 256-column accumulators
 
 __device__ int g_tc_error;   // bit 0: a barrier wait timed out (reported by b200q_device_error)
 
@@ -42,7 +59,7 @@ int tc_error_read(int clear) {
 }
 
 // instruction descriptor, kind::f16: fp32 accumulator, fp16 A and B, both K-major, N = 256, M = 128
-constexpr uint32_t kIdescF16 = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(kTN >> 3) << 17) | ((uint32_t)(kTM >> 4) << 24);
+constexpr uint32_t kIdescF16 = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(kXN >> 3) << 17) | ((uint32_t)(kXM >> 4) << 24);
 
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
     asm volatile(
@@ -51,302 +68,575 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b
         ::"r"(tmem_d), "l"(a), "l"(b), "r"(kIdescF16), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-
-// ---------------------------------------------------------------------------------------------------------
-// operands
-// ---------------------------------------------------------------------------------------------------------
-struct TcA {                 // activation rows: row m of the tile is source row rows[m] (or m0 + m), K-major
-    const void* x;           // [rows][ldx], bf16 (dtype 1), fp32 (0) or fp16 (2)
-    int dtype, ldx;
-    const int* gather;       // nullptr: row = m0 + m; else row = gather[m0 + m]
-    int gather_div;          // row = gather[..] / gather_div (pairs -> tokens)
-};
-
-// B producers: fill 8 chunks (64 k) of one weight row into the swizzled tile
-struct ProdQ8 {              // Q8_0 "rows" layout: q [n][k] int8 then d [n][k/32] fp16
-    const int8_t* q;
-    const __half* d;
-    int n, k;
-    __device__ void row(uint32_t tile, int r, int nrow, int ks) const {
-        if (nrow >= n) {
-            for (int c = 0; c < 8; c++) sts128(sw128(tile, r, c), make_uint4(0, 0, 0, 0));
-            return;
-        }
-        const uint4* src = reinterpret_cast<const uint4*>(q + (size_t)nrow * k + ks * kTK);
-        const __half2 d0 = __half2half2(d[(size_t)nrow * (k >> 5) + ks * 2]);
-        const __half2 d1 = __half2half2(d[(size_t)nrow * (k >> 5) + ks * 2 + 1]);
-#pragma unroll
-        for (int h = 0; h < 4; h++) {
-            const uint4 v = __ldg(src + h);   // 16 int8 = two chunks
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-            const __half2 ds = h < 2 ? d0 : d1;
-            uint32_t o[8];
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int8_t b0 = (int8_t)(w[j] & 255), b1 = (int8_t)((w[j] >> 8) & 255), b2 = (int8_t)((w[j] >> 16) & 255),
-                             b3 = (int8_t)(w[j] >> 24);
-                o[2 * j] = h2u(__hmul2(__halves2half2(__short2half_rn(b0), __short2half_rn(b1)), ds));
-                o[2 * j + 1] = h2u(__hmul2(__halves2half2(__short2half_rn(b2), __short2half_rn(b3)), ds));
-            }
-            sts128(sw128(tile, r, 2 * h), make_uint4(o[0], o[1], o[2], o[3]));
-            sts128(sw128(tile, r, 2 * h + 1), make_uint4(o[4], o[5], o[6], o[7]));
-        }
-    }
-};
-
-struct ProdIQ2 {             // IQ2_XXS rt32 layout (see common.cuh); sign words re-encoded by the packer
-    const uint8_t* w;        // the matrix (an expert) [n][k]
-    int n, k;
-    __device__ void row(uint32_t tile, int r, int nrow, int ks) const {
-        if (nrow >= n) {
-            for (int c = 0; c < 8; c++) sts128(sw128(tile, r, c), make_uint4(0, 0, 0, 0));
-            return;
-        }
-        const int nb = k >> 8, rt = nrow >> 5, lane = nrow & 31, sb = ks >> 2, j = ks & 3;
-        const uint8_t* unit = w + ((size_t)rt * nb + sb) * kIq2Unit;
-        const uint4 qv = __ldg(reinterpret_cast<const uint4*>(unit + j * 512 + lane * 16));
-        const float d = __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short*>(unit + 2048) + lane)));
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const uint32_t qx = h ? qv.z : qv.x, qy = h ? qv.w : qv.y;
-            const uint32_t s4 = ((qy >> 7) & 1u) | ((qy >> 14) & 2u) | ((qy >> 21) & 4u) | ((qy >> 28) & 8u);
-            const float db = d * (0.5f + (float)s4) * 0.25f;
-#pragma unroll
-            for (int g = 0; g < 4; g++) {
-                const unsigned long long gr = iq2xxs_grid[(qx >> (8 * g)) & 255];
-                const uint32_t sg = ksigns_iq2xs[(qy >> (8 * g)) & 127];
-                float v[8];
-#pragma unroll
-                for (int e = 0; e < 8; e++) {
-                    const float mag = (float)((gr >> (8 * e)) & 255);
-                    v[e] = ((sg >> e) & 1) ? -mag * db : mag * db;
-                }
-                sts128(sw128(tile, r, 4 * h + g),
-                       make_uint4(h2u(__floats2half2_rn(v[0], v[1])), h2u(__floats2half2_rn(v[2], v[3])),
-                                  h2u(__floats2half2_rn(v[4], v[5])), h2u(__floats2half2_rn(v[6], v[7]))));
-            }
-        }
-    }
-};
-
-// epilogues: out[row][col] for the tile's real rows / cols
-struct EpiStore {            // fp32 [rows][ldo] (rows scattered by `scatter` when given)
-    float* out;
-    int ldo;
-    const int* scatter;
-    float scale;
-    __device__ void put(int grow, int col, const float* v, int nv) const {
-        const int orow = scatter ? scatter[grow] : grow;
-        float* o = out + (size_t)orow * ldo + col;
-        for (int i = 0; i < nv; i++) o[i] = v[i] * scale;
-    }
-};
-struct EpiRelu2H {           // relu(v)^2 as fp16 [rows][ldo] (the next GEMM's A)
-    __half* out;
-    int ldo;
-    const int* scatter;
-    float scale;
-    __device__ void put(int grow, int col, const float* v, int nv) const {
-        const int orow = scatter ? scatter[grow] : grow;
-        __half* o = out + (size_t)orow * ldo + col;
-        for (int i = 0; i < nv; i++) { const float t = v[i] > 0.f ? v[i] * v[i] : 0.f; o[i] = __float2half_rn(t); }
-    }
-};
-
-// The work of one launch: a list of (group, m-tile) tiles times n-tiles.  Group g has rows [row0[g], row0[g] + cnt[g])
-// of the A source list and weight matrix wbase + g * wstride; with groups == nullptr there is one group of M rows.
-struct TcGroups {
-    const int* counts;       // per group rows (nullptr: one group)
-    const int* offsets;      // per group first row
-    int ngroups;
-    int M;                   // rows of the single group
-};
-
-template <class Prod, class Epi>
-struct TcArgsT {
-    TcA a;
-    Prod b;                  // b.w / b.q advanced by g * wstride per group
-    size_t wstride;          // bytes (IQ2) between groups' weight matrices
-    Epi epi;
-    TcGroups grp;
-    int N, K;
-};
-
-template <class Prod>
-__device__ __forceinline__ Prod prod_for_group(const Prod& p, size_t wstride, int g);
-template <>
-__device__ __forceinline__ ProdQ8 prod_for_group<ProdQ8>(const ProdQ8& p, size_t, int) { return p; }
-template <>
-__device__ __forceinline__ ProdIQ2 prod_for_group<ProdIQ2>(const ProdIQ2& p, size_t wstride, int g) {
-    ProdIQ2 q = p;
-    q.w = p.w + (size_t)g * wstride;
-    return q;
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(s));
+    return d;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint4 ldg_nc(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t ldg_u16(const void* p) {
+    unsigned short v;
+    asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
 }
 
-template <class Prod, class Epi>
-__global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_k(TcArgsT<Prod, Epi> a) {
-    extern __shared__ __align__(1024) unsigned char tc_dyn[];
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t raw = (uint32_t)__cvta_generic_to_shared(tc_dyn);
-    const uint32_t sbase = (raw + 1023u) & ~1023u;                   // stages, 1024-byte aligned
-    const uint32_t bars = sbase + kTcStages * kStage;                // full[s], empty[s], done, tmem slot
-    auto full = [&](int s) { return bars + 8u * s; };
-    auto empty = [&](int s) { return bars + 8u * (kTcStages + s); };
-    const uint32_t done = bars + 8u * (2 * kTcStages);
-    const uint32_t tmem_slot = done + 8u;
-    unsigned char* tmem_slot_ptr = tc_dyn + (tmem_slot - raw);
+// ---------------------------------------------------------------------------------------------------------
+// launch description
+// ---------------------------------------------------------------------------------------------------------
+struct XArgs {
+    const uint8_t* w;        // packed weights of group 0
+    size_t wstride;          // bytes between the groups' weight matrices
+    const uint8_t* a;        // rows image
+    int N, K;
+    const int4* tiles;       // grouped: {group, first slot, first row in the group, rows}; nullptr: dense
+    const int* ntiles;       // grouped: number of tiles (device)
+    int max_mtiles;          // grouped: capacity of `tiles`; dense: ceil(T / 256)
+    int T;                   // dense: rows
+};
 
-    // which tile: blockIdx.x = n-tile, blockIdx.y = tile index over the groups' m-tiles
-    const int ntn = (a.N + kTN - 1) / kTN;
-    int g = 0, m0 = 0, rows = a.grp.M;
-    if (a.grp.counts) {
-        pdl_wait();
-        int t = blockIdx.y;
-        rows = 0;
-        for (g = 0; g < a.grp.ngroups; g++) {
-            const int c = a.grp.counts[g];
-            const int mt = (c + kTM - 1) / kTM;
-            if (t < mt) { m0 = t * kTM; rows = c - m0; break; }
-            t -= mt;
+__device__ __forceinline__ int4 x_tile(const XArgs& a, int mt) {
+    if (a.tiles) return a.tiles[mt];
+    const int m0 = mt * 2 * kXM;
+    return make_int4(0, 2 * mt, m0, min(2 * kXM, a.T - m0));
+}
+
+// epilogues: v = 32 accumulator columns [col, col + 32) of row r (0..127) of half h of tile t
+struct EpiRows {             // fp32 y[orow][col]; orow = rowmap[row0[g] + m0 + 128 h + r] (or the dense row)
+    float* y;
+    int ldy;
+    const int* row0;         // per-group first row in the row list (offsets), nullptr: 0
+    const int* rowmap;       // nullptr: identity
+    __device__ void put(int4 t, int h, int r, int col, int N, const uint32_t (&v)[32]) const {
+        const int grow = (row0 ? row0[t.x] : 0) + t.z + h * kXM + r;
+        const int orow = rowmap ? rowmap[grow] : grow;
+        float* o = y + (size_t)orow * ldy + col;
+        if (col + 32 <= N && ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0)) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+                *reinterpret_cast<float4*>(o + i) =
+                    make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]), __uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; i++)
+                if (col + i < N) o[i] = __uint_as_float(v[i]);
         }
-        if (g >= a.grp.ngroups) { pdl_trigger(); return; }   // past the last tile
-    } else {
-        m0 = blockIdx.y * kTM;
-        rows = a.grp.M - m0;
-        if (rows <= 0) return;
     }
-    if (rows > kTM) rows = kTM;
-    const int row_base = a.grp.counts ? a.grp.offsets[g] + m0 : m0;   // index into the A row list
-    const int n0 = (blockIdx.x % ntn) * kTN;
-    const Prod prod = prod_for_group(a.b, a.wstride, g);
-    const int nk = a.K / kTK;
+};
+struct EpiImg {              // fp16(relu(v)^2) into the next GEMM's rows image (its K = this GEMM's N)
+    uint8_t* img;
+    __device__ void put(int4 t, int h, int r, int col, int N, const uint32_t (&v)[32]) const {
+        uint8_t* rec = img + ((size_t)(t.y + h) * (N / 32) + col / 32) * kXRec;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const float a0 = __uint_as_float(v[8 * c + 2 * j]), a1 = __uint_as_float(v[8 * c + 2 * j + 1]);
+                o[j] = h2u(__floats2half2_rn(a0 > 0.f ? a0 * a0 : 0.f, a1 > 0.f ? a1 * a1 : 0.f));
+            }
+            *reinterpret_cast<uint4*>(rec + sw64_off(r, c)) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    }
+};
 
+// ---------------------------------------------------------------------------------------------------------
+// B dequantisers.  run() produces every stage of one tile for the calling warp's 32 rows (lane = row): for each 32-k
+// block it waits for the stage to be free, writes the row's 64 B, and arrives on the stage's "full" barrier.
+// ---------------------------------------------------------------------------------------------------------
+struct XRing {               // stage bookkeeping shared by the warps of one CTA
+    uint32_t sbase, bars;
+    __device__ uint32_t full(int s) const { return bars + 8u * s; }
+    __device__ uint32_t empty(int s) const { return bars + 8u * (kXStages + s); }
+    __device__ uint32_t stage(int s) const { return sbase + (uint32_t)(s * kXStage); }
+};
+
+// waits (lane 0) for the stage of iteration `it` to be free; false on a timeout (warp-uniform)
+__device__ __forceinline__ bool x_wait_free(const XRing& R, int it, int lane) {
+    const int s = it % kXStages, use = it / kXStages;
+    int ok = 1;
+    if (use > 0 && lane == 0) ok = tc_mbar_wait(R.empty(s), (uint32_t)((use - 1) & 1)) ? 1 : 0;
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+__device__ __forceinline__ void x_stage_done(const XRing& R, int it, int lane) {
+    tc_fence_proxy_async();   // the generic-proxy writes are visible to the tensor core
+    __syncwarp();
+    if (lane == 0) tc_mbar_arrive(R.full(it % kXStages));
+}
+
+struct DeqIQ2 {              // IQ2_XXS rt32 layout (common.cuh); sign words re-encoded by the packer
+    static constexpr bool kTables = true;
+    uint32_t gtbl, stbl;     // shared-memory tables (set in the kernel)
+    // 8 fp16 of one 8-element group: magnitudes by prmt from {h8, h25, h43}, then the signs
+    __device__ __forceinline__ uint4 group(uint32_t P0, uint32_t P1, uint32_t gi, uint32_t si, int lane) const {
+        const uint2 sel = lds64(gtbl + ((gi * 16u + (uint32_t)(lane & 15)) << 3));
+        const uint32_t sp = lds32(stbl + ((si * 32u + (uint32_t)lane) << 2));
+        uint4 o;
+        o.x = prmt(P0, P1, sel.x) ^ ((sp << 15) & 0x80008000u);
+        o.y = prmt(P0, P1, sel.x >> 16) ^ ((sp << 14) & 0x80008000u);
+        o.z = prmt(P0, P1, sel.y) ^ ((sp << 13) & 0x80008000u);
+        o.w = prmt(P0, P1, sel.y >> 16) ^ ((sp << 12) & 0x80008000u);
+        return o;
+    }
+    __device__ __forceinline__ void chunk(uint32_t qx, uint32_t qy, float d, uint32_t row_addr, int lane) const {
+        const uint32_t s4 = ((qy >> 7) & 1u) | ((qy >> 14) & 2u) | ((qy >> 21) & 4u) | ((qy >> 28) & 8u);
+        const float db = d * (0.5f + (float)s4) * 0.25f;
+        const uint32_t P0 = h2u(__floats2half2_rn(8.f * db, 25.f * db));
+        const uint32_t P1 = (uint32_t)__half_as_ushort(__float2half_rn(43.f * db));
+        const int sw = (lane >> 1) & 3;
+#pragma unroll
+        for (int g = 0; g < 4; g++)
+            sts128(row_addr + (uint32_t)((g ^ sw) << 4), group(P0, P1, (qx >> (8 * g)) & 255u, (qy >> (8 * g)) & 127u, lane));
+    }
+    // rows of row tile rt of the group's matrix wm (n x K); valid: rt's rows exist
+    __device__ bool run(const XRing& R, int& it, const uint8_t* wm, int K, int rt, bool valid, int wd, int lane) const {
+        const int nb = K >> 8;
+        const uint8_t* base = wm + (size_t)rt * nb * kIq2Unit;
+        uint4 c[4], n[4];
+        uint32_t dc = 0, dn = 0;
+        if (valid) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) c[j] = ldg_nc(base + j * 512 + lane * 16);
+            dc = ldg_u16(base + 2048 + lane * 2);
+        }
+        for (int sb = 0; sb < nb; sb++) {
+            if (valid && sb + 1 < nb) {
+                const uint8_t* u = base + (size_t)(sb + 1) * kIq2Unit;
+#pragma unroll
+                for (int j = 0; j < 4; j++) n[j] = ldg_nc(u + j * 512 + lane * 16);
+                dn = ldg_u16(u + 2048 + lane * 2);
+            }
+            const float d = __half2float(__ushort_as_half((unsigned short)dc));
+#pragma unroll
+            for (int ch = 0; ch < 8; ch++, it++) {
+                if (!x_wait_free(R, it, lane)) return false;
+                const uint32_t row_addr = R.stage(it % kXStages) + 2 * kXRec + (uint32_t)((wd * 32 + lane) * 64);
+                if (valid) {
+                    const uint4 u = c[ch >> 1];
+                    chunk((ch & 1) ? u.z : u.x, (ch & 1) ? u.w : u.y, d, row_addr, lane);
+                } else {
+#pragma unroll
+                    for (int g = 0; g < 4; g++) sts128(row_addr + g * 16, make_uint4(0, 0, 0, 0));
+                }
+                x_stage_done(R, it, lane);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; j++) c[j] = n[j];
+            dc = dn;
+        }
+        return true;
+    }
+};
+
+// Q8_0 prompt layout ("q8 tc"): units (32-row tile t, 32-k block kb) of 1088 B, [32 lanes][32 int8] then [32] fp16 d,
+// at (t * K/32 + kb) * 1088 -- a warp's step over one 32-k block reads 1088 contiguous bytes.
+constexpr int kQ8Unit = 1088;
+struct DeqQ8 {
+    static constexpr bool kTables = false;
+    uint32_t gtbl, stbl;
+    // 0x64XX as fp16 is 1024 + XX exactly; with the int8's sign bit flipped XX = q + 128, so minus 1152 gives q exactly,
+    // and one fp16 multiply by d rounds q * d once
+    __device__ __forceinline__ static uint32_t pair(uint32_t x, uint32_t sel, __half2 d2) {
+        const __half2 mg = __half2half2(__ushort_as_half((unsigned short)0x6480));   // 1152
+        const uint32_t b = prmt(x, 0x64646464u, sel);
+        const __half2 q = __hsub2(*reinterpret_cast<const __half2*>(&b), mg);
+        return h2u(__hmul2(q, d2));
+    }
+    __device__ __forceinline__ static uint4 quad(uint32_t w0, uint32_t w1, __half2 d2) {
+        const uint32_t x0 = w0 ^ 0x80808080u, x1 = w1 ^ 0x80808080u;
+        return make_uint4(pair(x0, 0x4140u, d2), pair(x0, 0x4342u, d2), pair(x1, 0x4140u, d2), pair(x1, 0x4342u, d2));
+    }
+    __device__ bool run(const XRing& R, int& it, const uint8_t* wm, int K, int rt, bool valid, int wd, int lane) const {
+        const int nk = K >> 5;   // a multiple of 8
+        const uint8_t* base = wm + (size_t)rt * nk * kQ8Unit;
+        uint4 qa[4], qb[4];
+        uint32_t dd[4];
+        if (valid) {
+#pragma unroll
+            for (int u = 0; u < 3; u++) {
+                const uint8_t* p = base + (size_t)u * kQ8Unit;
+                qa[u] = ldg_nc(p + lane * 32);
+                qb[u] = ldg_nc(p + lane * 32 + 16);
+                dd[u] = ldg_u16(p + 1024 + lane * 2);
+            }
+        }
+        for (int k0 = 0; k0 < nk; k0 += 4) {
+#pragma unroll
+            for (int u = 0; u < 4; u++, it++) {
+                const int kb = k0 + u, nx = kb + 3;
+                if (valid && nx < nk) {   // prefetch three blocks ahead into the ring slot of block kb + 3
+                    const uint8_t* p = base + (size_t)nx * kQ8Unit;
+                    qa[(u + 3) & 3] = ldg_nc(p + lane * 32);
+                    qb[(u + 3) & 3] = ldg_nc(p + lane * 32 + 16);
+                    dd[(u + 3) & 3] = ldg_u16(p + 1024 + lane * 2);
+                }
+                if (!x_wait_free(R, it, lane)) return false;
+                const uint32_t row_addr = R.stage(it % kXStages) + 2 * kXRec + (uint32_t)((wd * 32 + lane) * 64);
+                const int sw = (lane >> 1) & 3;
+                if (valid) {
+                    const __half2 d2 = __half2half2(__ushort_as_half((unsigned short)dd[u]));
+                    sts128(row_addr + (uint32_t)((0 ^ sw) << 4), quad(qa[u].x, qa[u].y, d2));
+                    sts128(row_addr + (uint32_t)((1 ^ sw) << 4), quad(qa[u].z, qa[u].w, d2));
+                    sts128(row_addr + (uint32_t)((2 ^ sw) << 4), quad(qb[u].x, qb[u].y, d2));
+                    sts128(row_addr + (uint32_t)((3 ^ sw) << 4), quad(qb[u].z, qb[u].w, d2));
+                } else {
+#pragma unroll
+                    for (int g = 0; g < 4; g++) sts128(row_addr + g * 16, make_uint4(0, 0, 0, 0));
+                }
+                x_stage_done(R, it, lane);
+            }
+        }
+        return true;
+    }
+};
+
+// ---------------------------------------------------------------------------------------------------------
+// the GEMM
+// ---------------------------------------------------------------------------------------------------------
+template <class Deq, class Epi>
+__global__ void __launch_bounds__(kXThreads, 1) tcx_gemm_k(XArgs a, Epi epi) {
+    extern __shared__ __align__(1024) unsigned char x_dyn[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t raw = (uint32_t)__cvta_generic_to_shared(x_dyn);
+    XRing R;
+    R.sbase = (raw + 1023u) & ~1023u;
+    const uint32_t gtbl = R.sbase + kXStages * kXStage, stbl = gtbl + kGridTbl;
+    R.bars = stbl + kSignTbl;
+    const uint32_t acc_full = R.bars + 8u * (2 * kXStages), acc_empty = acc_full + 8u, drain = acc_full + 16u;
+    const uint32_t tmem_slot = acc_full + 24u;
+    unsigned char* tmem_slot_ptr = x_dyn + (tmem_slot - raw);
+
+    if (Deq::kTables) {
+        // grid selectors: entry g, copy c (lanes c and c + 16): two words of four prmt selectors over {h8, h25, h43}
+        for (int i = tid; i < 256 * 16; i += kXThreads) {
+            const unsigned long long gr = iq2xxs_grid[i >> 4];
+            uint32_t w[2] = {0u, 0u};
+#pragma unroll
+            for (int p = 0; p < 4; p++) {
+                const uint32_t m0 = (uint32_t)((gr >> (16 * p)) & 255), m1 = (uint32_t)((gr >> (16 * p + 8)) & 255);
+                const uint32_t a0 = m0 == 8 ? 0u : m0 == 25 ? 2u : 4u, a1 = m1 == 8 ? 0u : m1 == 25 ? 2u : 4u;
+                const uint32_t sel = a0 | (a0 + 1) << 4 | a1 << 8 | (a1 + 1) << 12;
+                w[p >> 1] |= sel << (16 * (p & 1));
+            }
+            asm volatile("st.shared.v2.u32 [%0], {%1,%2};" ::"r"(gtbl + (uint32_t)i * 8u), "r"(w[0]), "r"(w[1]) : "memory");
+        }
+        // sign masks: sign index i, copy l: the 8 sign bits with element 2p at bit p and 2p + 1 at bit 16 + p
+        for (int i = tid; i < 128 * 32; i += kXThreads) {
+            const uint32_t s = ksigns_iq2xs[i >> 5];
+            uint32_t sp = 0;
+#pragma unroll
+            for (int p = 0; p < 4; p++) sp |= ((s >> (2 * p)) & 1u) << p | ((s >> (2 * p + 1)) & 1u) << (16 + p);
+            asm volatile("st.shared.u32 [%0], %1;" ::"r"(stbl + (uint32_t)i * 4u), "r"(sp) : "memory");
+        }
+    }
     if (tid == 0) {
-        for (int s = 0; s < kTcStages; s++) { tc_mbar_init(full(s), kProdWarps * 32); tc_mbar_init(empty(s), 1); }
-        tc_mbar_init(done, 1);
+        for (int s = 0; s < kXStages; s++) { tc_mbar_init(R.full(s), 1 + kDeqWarps); tc_mbar_init(R.empty(s), 1); }
+        tc_mbar_init(acc_full, 1);
+        tc_mbar_init(acc_empty, kXEpiWarps);
+        tc_mbar_init(drain, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 0) {   // the whole warp allocates the accumulator's 256 TMEM columns
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot), "r"(kTN));
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot), "r"(kXTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot_ptr);
-    if (!a.grp.counts) pdl_wait();
-    bool healthy = true;
+    pdl_wait();
 
-    if (warp >= kEpiWarps + 1) {
-        // producers: 256 threads; A: 128 rows x 8 chunks (4 a thread), B: 256 rows (one a thread)
-        const int p = tid - (kEpiWarps + 1) * 32;
-        for (int i = 0; i < nk && healthy; i++) {
-            const int s = i % kTcStages, use = i / kTcStages;
-            if (use > 0 && !tc_mbar_wait(empty(s), (uint32_t)((use - 1) & 1))) { healthy = false; break; }
-            const uint32_t at = sbase + (uint32_t)(s * kStage), bt = at + kATile;
-            for (int q = p; q < kTM * 8; q += kProdWarps * 32) {
-                const int r = q >> 3, c = q & 7;
-                uint4 v = make_uint4(0, 0, 0, 0);
-                if (r < rows) {
-                    int src = row_base + r;
-                    if (a.a.gather) src = a.a.gather[src] / a.a.gather_div;
-                    const size_t off = (size_t)src * a.a.ldx + (size_t)i * kTK + c * 8;
-                    if (a.a.dtype == 2) {
-                        v = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(a.a.x) + off));
-                    } else if (a.a.dtype == B200Q_BF16) {
-                        const uint4 u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.a.x) + off));
-                        const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
-                        uint32_t o[4];
-#pragma unroll
-                        for (int j = 0; j < 4; j++)
-                            o[j] = h2u(__floats2half2_rn(__uint_as_float(uw[j] << 16), __uint_as_float(uw[j] & 0xffff0000u)));
-                        v = make_uint4(o[0], o[1], o[2], o[3]);
-                    } else {
-                        const float4* f = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.a.x) + off);
-                        const float4 f0 = __ldg(f), f1 = __ldg(f + 1);
-                        v = make_uint4(h2u(__floats2half2_rn(f0.x, f0.y)), h2u(__floats2half2_rn(f0.z, f0.w)),
-                                       h2u(__floats2half2_rn(f1.x, f1.y)), h2u(__floats2half2_rn(f1.z, f1.w)));
-                    }
-                }
-                sts128(sw128(at, r, c), v);
-            }
-            prod.row(bt, p, n0 + p, i);
-            tc_fence_proxy_async();   // the generic-proxy writes are visible to the tensor core's reads
-            tc_mbar_arrive(full(s));
-        }
-        if (!healthy) atomicOr(&g_tc_error, 1);
-    } else if (warp == kEpiWarps) {
-        // the MMA issuer
+    const int NT = (a.N + kXN - 1) / kXN, KK = a.K / 32;
+    const int mtiles = a.tiles ? min(*a.ntiles, a.max_mtiles) : a.max_mtiles;
+    const int total = mtiles * NT;
+
+    if (warp == 0) {
+        // rows producer: one lane bulk-copies each stage's A records
         if (lane == 0) {
-            for (int i = 0; i < nk; i++) {
-                const int s = i % kTcStages;
-                if (!tc_mbar_wait(full(s), (uint32_t)((i / kTcStages) & 1))) { healthy = false; break; }
-                tc_fence_after();
-                const uint32_t at = sbase + (uint32_t)(s * kStage), bt = at + kATile;
-#pragma unroll
-                for (int kk = 0; kk < kTK / 16; kk++)
-                    umma_f16(tmem, umma_desc_sw128(at + kk * 32), umma_desc_sw128(bt + kk * 32), (i | kk) ? 1u : 0u);
-                umma_commit(empty(s));   // the stage is free once these MMAs have read it
+            bool healthy = true;
+            int it = 0;
+            for (int L = blockIdx.x; L < total && healthy; L += gridDim.x) {
+                const int4 t = x_tile(a, L / NT);
+                const int halves = t.w > kXM ? 2 : 1;
+                const uint8_t* a0 = a.a + (size_t)t.y * KK * kXRec;
+                for (int kk = 0; kk < KK; kk++, it++) {
+                    const int s = it % kXStages, use = it / kXStages;
+                    if (use > 0 && !tc_mbar_wait(R.empty(s), (uint32_t)((use - 1) & 1))) { healthy = false; break; }
+                    const uint32_t st = R.stage(s);
+                    tc_mbar_arrive_tx(R.full(s), (uint32_t)(halves * kXRec));
+                    tc_bulk_g2s(st, a0 + (size_t)kk * kXRec, (uint32_t)kXRec, R.full(s));
+                    if (halves == 2) tc_bulk_g2s(st + kXRec, a0 + ((size_t)KK + kk) * kXRec, (uint32_t)kXRec, R.full(s));
+                }
             }
-            umma_commit(done);           // all MMAs issued so far: the accumulator is final when this arrives
+            // the copies of the last uses of every stage have landed before the CTA may exit
+            for (int i = it - kXStages > 0 ? it - kXStages : 0; i < it; i++)
+                if (!tc_mbar_wait(R.full(i % kXStages), (uint32_t)((i / kXStages) & 1))) healthy = false;
             if (!healthy) atomicOr(&g_tc_error, 1);
         }
         __syncwarp();
-    } else {
-        // epilogue: warp w reads TMEM lanes 32w.. (tile rows), 32 columns at a time
-        if (tc_mbar_wait(done, 0)) {
-            tc_fence_after();
-            const int r = warp * 32 + lane;
-            for (int cb = 0; cb < kTN; cb += 32) {
-                uint32_t v[32];
-                tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)cb, v);
-                tmem_ld_wait();
-                const int col = n0 + cb;
-                if (r < rows && col < a.N) {
-                    float f[32];
+    } else if (warp == 1) {
+        // MMA issuer
+        if (lane == 0) {
+            bool healthy = true;
+            int it = 0, tl = 0;
+            for (int L = blockIdx.x; L < total && healthy; L += gridDim.x, tl++) {
+                const int4 t = x_tile(a, L / NT);
+                const bool two = t.w > kXM;
+                if (tl > 0 && !tc_mbar_wait(acc_empty, (uint32_t)((tl - 1) & 1))) { healthy = false; break; }
+                tc_fence_after();
+                for (int kk = 0; kk < KK; kk++, it++) {
+                    const int s = it % kXStages;
+                    if (!tc_mbar_wait(R.full(s), (uint32_t)((it / kXStages) & 1))) { healthy = false; break; }
+                    tc_fence_after();
+                    const uint32_t st = R.stage(s), bt = st + 2 * kXRec;
 #pragma unroll
-                    for (int i = 0; i < 32; i++) f[i] = __uint_as_float(v[i]);
-                    a.epi.put(row_base + r, col, f, min(32, a.N - col));
+                    for (int ki = 0; ki < 2; ki++)
+                        umma_f16(tmem, umma_desc_sw64(st + ki * 32), umma_desc_sw64(bt + ki * 32), (kk | ki) ? 1u : 0u);
+                    if (two) {
+#pragma unroll
+                        for (int ki = 0; ki < 2; ki++)
+                            umma_f16(tmem + 256u, umma_desc_sw64(st + kXRec + ki * 32), umma_desc_sw64(bt + ki * 32), (kk | ki) ? 1u : 0u);
+                    }
+                    umma_commit(R.empty(s));
                 }
+                if (healthy) umma_commit(acc_full);
             }
-        } else {
-            if (lane == 0) atomicOr(&g_tc_error, 1);
+            // every MMA this thread issued has completed before the TMEM is freed
+            umma_commit(drain);
+            if (!tc_mbar_wait(drain, 0)) healthy = false;
+            if (!healthy) atomicOr(&g_tc_error, 1);
+        }
+        __syncwarp();
+    } else if (warp < 2 + kDeqWarps) {
+        // dequantisers: warp wd owns weight rows 32 wd .. 32 wd + 31 of every tile
+        const int wd = warp - 2;
+        Deq dq;
+        dq.gtbl = gtbl;
+        dq.stbl = stbl;
+        int it = 0;
+        for (int L = blockIdx.x; L < total; L += gridDim.x) {
+            const int4 t = x_tile(a, L / NT);
+            const int n0 = (L % NT) * kXN + wd * 32;
+            const uint8_t* wm = a.w + (size_t)t.x * a.wstride;
+            if (!dq.run(R, it, wm, a.K, n0 >> 5, n0 < a.N, wd, lane)) {
+                if (lane == 0) atomicOr(&g_tc_error, 1);
+                break;
+            }
+        }
+    } else {
+        // epilogue: warp w reads TMEM lanes 32 (w % 4).. of accumulator h = (w - 10) / 4
+        const int q = warp & 3, h = (warp - 2 - kDeqWarps) >> 2;
+        const int r = q * 32 + lane;
+        int tl = 0;
+        for (int L = blockIdx.x; L < total; L += gridDim.x, tl++) {
+            const int4 t = x_tile(a, L / NT);
+            const int n0 = (L % NT) * kXN;
+            if (!tc_mbar_wait(acc_full, (uint32_t)(tl & 1))) {
+                if (lane == 0) atomicOr(&g_tc_error, 1);
+                break;
+            }
+            tc_fence_after();
+            if (h == 0 || t.w > kXM) {
+                const bool row_ok = h * kXM + r < t.w;
+#pragma unroll 1
+                for (int cb = 0; cb < kXN / 32; cb++) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 256 + cb * 32), v);
+                    tmem_ld_wait();
+                    if (cb == kXN / 32 - 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) tc_mbar_arrive(acc_empty);   // the accumulators may be overwritten now
+                    }
+                    const int col = n0 + cb * 32;
+                    if (row_ok && col < a.N) epi.put(t, h, r, col, a.N, v);
+                }
+            } else {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc_mbar_arrive(acc_empty);
+            }
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTN));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kXTmemCols));
     }
     pdl_trigger();
 }
 
-template <class Prod, class Epi>
-static cudaError_t launch_tc(const TcArgsT<Prod, Epi>& a, int m_tiles, cudaStream_t s) {
+static int x_num_sms() {
+    static int sms[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!sms[dev]) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        sms[dev] = v > 0 ? v : 148;
+    }
+    return sms[dev];
+}
+
+template <class Deq, class Epi>
+static cudaError_t launch_x(const XArgs& a, const Epi& epi, cudaStream_t s) {
     static bool opted = false;
     if (!opted) {
-        cudaError_t e = cudaFuncSetAttribute(tc_gemm_k<Prod, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+        const cudaError_t e = cudaFuncSetAttribute(tcx_gemm_k<Deq, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kXSmem);
         if (e != cudaSuccess) return e;
         opted = true;
     }
-    const int ntn = (a.N + kTN - 1) / kTN;
-    return launch(tc_gemm_k<Prod, Epi>, dim3(ntn, m_tiles), dim3(kTcThreads), kTcSmem, s, a);
+    const long long work = (long long)a.max_mtiles * ((a.N + kXN - 1) / kXN);
+    const int grid = (int)(work < x_num_sms() ? work : x_num_sms());
+    if (grid <= 0) return cudaSuccess;
+    return launch(tcx_gemm_k<Deq, Epi>, dim3(grid), dim3(kXThreads), kXSmem, s, a, epi);
 }
 
 // ---------------------------------------------------------------------------------------------------------
-// Q8_0 "rows" packing for the prompt GEMM: q [n][k] int8, then d [n][k/32] fp16
+// rows images, tile tables, packing
 // ---------------------------------------------------------------------------------------------------------
-__global__ void q8_rows_pack_k(const uint8_t* __restrict__ raw, int8_t* __restrict__ q, __half* __restrict__ d, int64_t n, int k) {
+// rows image from activation rows.  Grouped (slots != nullptr): slot s = {expert e, local slot j}, row r is pair
+// offsets[e] + 128 j + r of the expert-sorted list (if it exists), source row order[pair] / div.  Dense: slot s row r
+// is source row 128 s + r (if < T).  Missing rows are zeros.  A thread converts 8 k.
+__global__ void rows_image_k(const void* __restrict__ x, int dtype, int ldx, int K, int T, const int2* __restrict__ slots,
+                             const int* __restrict__ nslots, int max_slots, const int* __restrict__ counts,
+                             const int* __restrict__ offsets, const int* __restrict__ order, int div,
+                             uint8_t* __restrict__ img) {
     pdl_wait();
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // one block of 32
-    const int nb = k / 32;
-    if (i < n * nb) {
-        const uint8_t* blk = raw + (size_t)i * 34;
-        d[i] = __ushort_as_half((unsigned short)(blk[0] | blk[1] << 8));
-        for (int j = 0; j < 32; j++) q[(size_t)i * 32 + j] = (int8_t)blk[2 + j];
+    const int per = K >> 3;
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int limit = slots ? min(*nslots, max_slots) : max_slots;
+    if (i < (size_t)limit * kXM * per) {
+        const int c8 = (int)(i % per);
+        const int r = (int)((i / per) % kXM);
+        const int s = (int)(i / ((size_t)per * kXM));
+        int src = -1;
+        if (slots) {
+            const int2 sl = slots[s];
+            const int local = sl.y * kXM + r;
+            if (local < counts[sl.x]) src = order[offsets[sl.x] + local] / div;
+        } else {
+            const int row = s * kXM + r;
+            if (row < T) src = row;
+        }
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (src >= 0) {
+            if (dtype == B200Q_BF16) {
+                const uint4 u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(x) + (size_t)src * ldx + c8 * 8));
+                const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+                uint32_t o[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++) o[j] = h2u(__floats2half2_rn(__uint_as_float(uw[j] << 16), __uint_as_float(uw[j] & 0xffff0000u)));
+                v = make_uint4(o[0], o[1], o[2], o[3]);
+            } else {
+                const float4* f = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + (size_t)src * ldx + c8 * 8);
+                const float4 f0 = __ldg(f), f1 = __ldg(f + 1);
+                v = make_uint4(h2u(__floats2half2_rn(f0.x, f0.y)), h2u(__floats2half2_rn(f0.z, f0.w)),
+                               h2u(__floats2half2_rn(f1.x, f1.y)), h2u(__floats2half2_rn(f1.z, f1.w)));
+            }
+        }
+        *reinterpret_cast<uint4*>(img + ((size_t)s * (K / 32) + c8 / 4) * kXRec + sw64_off(r, c8 & 3)) = v;
     }
     pdl_trigger();
+}
+
+// tiles and slots of the grouped launch from the per-expert counts (one block): tiles[] = {e, first slot, first row,
+// rows} in expert order, slots[] = {e, j}; meta = {tiles, slots}
+__global__ void moe_tiles_k(const int* __restrict__ counts, int E, int4* __restrict__ tiles, int2* __restrict__ slots,
+                            int* __restrict__ meta) {
+    pdl_wait();
+    __shared__ int s_t[512], s_s[512];
+    const int e = threadIdx.x;
+    const int c = e < E ? counts[e] : 0;
+    const int nt = (c + 2 * kXM - 1) / (2 * kXM), ns = (c + kXM - 1) / kXM;
+    s_t[e] = nt;
+    s_s[e] = ns;
+    __syncthreads();
+    for (int off = 1; off < 512; off <<= 1) {   // inclusive scans
+        const int a = e >= off ? s_t[e - off] : 0, b = e >= off ? s_s[e - off] : 0;
+        __syncthreads();
+        s_t[e] += a;
+        s_s[e] += b;
+        __syncthreads();
+    }
+    const int tb = s_t[e] - nt, sb = s_s[e] - ns;
+    for (int i = 0; i < nt; i++) tiles[tb + i] = make_int4(e, sb + 2 * i, 2 * kXM * i, min(2 * kXM, c - 2 * kXM * i));
+    for (int j = 0; j < ns; j++) slots[sb + j] = make_int2(e, j);
+    if (e == 511) { meta[0] = s_t[511]; meta[1] = s_s[511]; }
+    pdl_trigger();
+}
+
+// act image -> pair-indexed rows act[pair][F] fp16 (for inspection)
+__global__ void act_rows_k(const uint8_t* __restrict__ img, int F, const int2* __restrict__ slots, const int* __restrict__ nslots,
+                           int max_slots, const int* __restrict__ counts, const int* __restrict__ offsets,
+                           const int* __restrict__ order, __half* __restrict__ act) {
+    pdl_wait();
+    const int per = F >> 3;
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < (size_t)min(*nslots, max_slots) * kXM * per) {
+        const int c8 = (int)(i % per), r = (int)((i / per) % kXM), s = (int)(i / ((size_t)per * kXM));
+        const int2 sl = slots[s];
+        const int local = sl.y * kXM + r;
+        if (local < counts[sl.x]) {
+            const int pair = order[offsets[sl.x] + local];
+            *reinterpret_cast<uint4*>(act + (size_t)pair * F + c8 * 8) =
+                *reinterpret_cast<const uint4*>(img + ((size_t)s * (F / 32) + c8 / 4) * kXRec + sw64_off(r, c8 & 3));
+        }
+    }
+    pdl_trigger();
+}
+
+// Q8_0 ggml blocks [n][k/32][34] -> the q8 tc layout; a thread moves one block
+__global__ void q8_tc_pack_k(const uint8_t* __restrict__ raw, uint8_t* __restrict__ out, int64_t n, int k) {
+    pdl_wait();
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int nb = k / 32;
+    if (i < n * nb) {
+        const int64_t row = i / nb;
+        const int kb = (int)(i % nb);
+        const uint8_t* blk = raw + (size_t)i * 34;
+        uint8_t* u = out + ((size_t)(row >> 5) * nb + kb) * kQ8Unit;
+        const int l = (int)(row & 31);
+        u[1024 + 2 * l] = blk[0];
+        u[1024 + 2 * l + 1] = blk[1];
+        for (int j = 0; j < 32; j++) u[l * 32 + j] = blk[2 + j];
+    }
+    pdl_trigger();
+}
+
+static inline bool x16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+static inline size_t x_align(size_t v) { return (v + 255) & ~(size_t)255; }
+
+struct MoeWs {               // workspace of b200q_moe_prompt
+    size_t tiles, slots, meta, aimg, actimg, total;
+    int max_tiles, max_slots;
+};
+static MoeWs moe_ws(int pairs, int E, int H, int F) {
+    MoeWs w{};
+    w.max_tiles = pairs / (2 * kXM) + E;
+    w.max_slots = pairs / kXM + E;
+    w.tiles = 0;
+    w.slots = x_align(w.tiles + (size_t)w.max_tiles * sizeof(int4));
+    w.meta = x_align(w.slots + (size_t)w.max_slots * sizeof(int2));
+    w.aimg = x_align(w.meta + 16);
+    w.actimg = x_align(w.aimg + (size_t)w.max_slots * (H / 32) * kXRec);
+    w.total = x_align(w.actimg + (size_t)w.max_slots * (F / 32) * kXRec);
+    return w;
 }
 
 }  // namespace b200q
@@ -355,65 +645,98 @@ using namespace b200q;
 
 extern "C" {
 
-size_t b200q_q8_rows_bytes(int64_t n, int k) { return (size_t)n * k + (size_t)n * (k / 32) * 2; }
+size_t b200q_q8_tc_bytes(int64_t n, int k) {
+    if (n <= 0 || n % 32 || k <= 0 || k % 256) return 0;
+    return (size_t)n * (k / 32) * 34;
+}
 
-int b200q_q8_rows_pack(const void* raw, void* packed, int64_t n, int k, void* stream) {
-    if (!raw || !packed || n <= 0 || k <= 0 || k % 64 || ((uintptr_t)packed & 15)) return B200Q_EINVAL;
-    int8_t* q = (int8_t*)packed;
-    __half* d = (__half*)((char*)packed + (size_t)n * k);
+int b200q_q8_tc_pack(const void* raw, void* packed, int64_t n, int k, void* stream) {
+    if (!raw || !packed || n <= 0 || n % 32 || k <= 0 || k % 256 || !x16(packed)) return B200Q_EINVAL;
     const int64_t th = n * (k / 32);
-    launch(q8_rows_pack_k, dim3((unsigned)((th + 255) / 256)), dim3(256), 0, (cudaStream_t)stream, (const uint8_t*)raw, q,
-           d, n, k);
-    return launched();
+    return status_from(launch(q8_tc_pack_k, dim3((unsigned)((th + 255) / 256)), dim3(256), 0, (cudaStream_t)stream,
+                              (const uint8_t*)raw, (uint8_t*)packed, n, k));
 }
 
-int b200q_q8_gemm(const void* w, int n, int k, const void* x, int x_dtype, int ldx, int T, float* y, int ldy, void* stream) {
-    if (!w || !x || !y || n <= 0 || k <= 0 || k % 64 || T <= 0 || ldx < k || ldy < n ||
-        (x_dtype != B200Q_F32 && x_dtype != B200Q_BF16) || ((uintptr_t)w & 15) || ((uintptr_t)x & 15) || (ldx % 8))
-        return B200Q_EINVAL;
-    TcArgsT<ProdQ8, EpiStore> a{};
-    a.a = TcA{x, x_dtype, ldx, nullptr, 1};
-    a.b = ProdQ8{(const int8_t*)w, (const __half*)((const char*)w + (size_t)n * k), n, k};
-    a.epi = EpiStore{y, ldy, nullptr, 1.f};
-    a.grp = TcGroups{nullptr, nullptr, 1, T};
-    a.N = n;
-    a.K = k;
-    return status_from(launch_tc(a, (T + kTM - 1) / kTM, (cudaStream_t)stream));
+size_t b200q_q8_gemm_workspace_bytes(int T, int k) {
+    if (T <= 0 || k <= 0 || k % 256) return 0;
+    return (size_t)((T + 2 * kXM - 1) / (2 * kXM)) * 2 * (k / 32) * kXRec;
 }
 
-// Grouped IQ2_XXS prompt GEMMs over expert-sorted rows (order from b200q_moe_group_large):
-//  up:   act[p][0..n) = relu(W_up[e] . x[p / topk])^2 as fp16, for the pairs p of each expert e
-//  down: y[p][0..n) = W_down[e] . act[p] (fp32)
-int b200q_moe_up_tc(const void* slab, int E, int n, int k, const int* counts, const int* offsets, const int* order, int topk,
-                    const void* x, int x_dtype, void* act_f16, int max_tiles, void* stream) {
-    if (!slab || !counts || !offsets || !order || !x || !act_f16 || E <= 0 || E > 512 || topk <= 0 || n % 32 || k % 256 ||
-        (x_dtype != B200Q_F32 && x_dtype != B200Q_BF16) || ((uintptr_t)slab & 15) || ((uintptr_t)x & 15) || max_tiles <= 0)
+int b200q_q8_gemm(const void* w, int n, int k, const void* x, int x_dtype, int ldx, int T, float* y, int ldy, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+    if (!w || !x || !y || n <= 0 || n % 32 || k <= 0 || k % 256 || T <= 0 || ldx < k || ldy < n ||
+        (x_dtype != B200Q_F32 && x_dtype != B200Q_BF16) || !x16(w) || !x16(x) || (ldx % 8) || !workspace || !x16(workspace))
         return B200Q_EINVAL;
-    TcArgsT<ProdIQ2, EpiRelu2H> a{};
-    a.a = TcA{x, x_dtype, k, order, topk};
-    a.b = ProdIQ2{(const uint8_t*)slab, n, k};
-    a.wstride = iq2_bytes(n, k);
-    a.epi = EpiRelu2H{(__half*)act_f16, n, order, 1.f};
-    a.grp = TcGroups{counts, offsets, E, 0};
+    if (workspace_bytes < b200q_q8_gemm_workspace_bytes(T, k)) return B200Q_ENOSPACE;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int mt = (T + 2 * kXM - 1) / (2 * kXM);
+    const size_t th = (size_t)mt * 2 * kXM * (k / 8);
+    cudaError_t e = launch(rows_image_k, dim3((unsigned)((th + 255) / 256)), dim3(256), 0, s, x, x_dtype, ldx, k, T,
+                           (const int2*)nullptr, (const int*)nullptr, 2 * mt, (const int*)nullptr, (const int*)nullptr,
+                           (const int*)nullptr, 1, (uint8_t*)workspace);
+    if (e != cudaSuccess) return status_from(e);
+    XArgs a{};
+    a.w = (const uint8_t*)w;
+    a.a = (const uint8_t*)workspace;
     a.N = n;
     a.K = k;
-    return status_from(launch_tc(a, max_tiles, (cudaStream_t)stream));
+    a.max_mtiles = mt;
+    a.T = T;
+    return status_from(launch_x<DeqQ8>(a, EpiRows{y, ldy, nullptr, nullptr}, s));
 }
 
-int b200q_moe_down_tc(const void* slab, int E, int n, int k, const int* counts, const int* offsets, const int* order,
-                      const void* act_f16, float* y, int max_tiles, void* stream) {
-    if (!slab || !counts || !offsets || !order || !act_f16 || !y || E <= 0 || E > 512 || n % 32 || k % 256 ||
-        ((uintptr_t)slab & 15) || ((uintptr_t)act_f16 & 15) || max_tiles <= 0)
+size_t b200q_moe_prompt_workspace_bytes(int pairs, int E, int H, int F) {
+    if (pairs <= 0 || E <= 0 || H <= 0 || F <= 0 || H % 256 || F % 256) return 0;
+    return moe_ws(pairs, E, H, F).total;
+}
+
+int b200q_moe_prompt(const void* up, const void* down, int E, int H, int F, const int* counts, const int* offsets,
+                     const int* order, int topk, int pairs, const void* x, int x_dtype, float* mo, void* act_rows,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+    if (!up || !down || !counts || !offsets || !order || !x || !mo || !workspace || E <= 0 || E > 512 || topk <= 0 ||
+        pairs <= 0 || H % 256 || F % 256 || H <= 0 || F <= 0 || (x_dtype != B200Q_F32 && x_dtype != B200Q_BF16) ||
+        !x16(up) || !x16(down) || !x16(x) || !x16(workspace) || (act_rows && !x16(act_rows)))
         return B200Q_EINVAL;
-    TcArgsT<ProdIQ2, EpiStore> a{};
-    a.a = TcA{act_f16, 2, k, order, 1};
-    a.b = ProdIQ2{(const uint8_t*)slab, n, k};
-    a.wstride = iq2_bytes(n, k);
-    a.epi = EpiStore{y, n, order, 1.f};
-    a.grp = TcGroups{counts, offsets, E, 0};
-    a.N = n;
-    a.K = k;
-    return status_from(launch_tc(a, max_tiles, (cudaStream_t)stream));
+    const MoeWs L = moe_ws(pairs, E, H, F);
+    if (workspace_bytes < L.total) return B200Q_ENOSPACE;
+    cudaStream_t s = (cudaStream_t)stream;
+    uint8_t* ws = (uint8_t*)workspace;
+    int4* tiles = (int4*)(ws + L.tiles);
+    int2* slots = (int2*)(ws + L.slots);
+    int* meta = (int*)(ws + L.meta);
+    uint8_t* aimg = ws + L.aimg;
+    uint8_t* actimg = ws + L.actimg;
+
+    cudaError_t e = launch(moe_tiles_k, dim3(1), dim3(512), 0, s, counts, E, tiles, slots, meta);
+    if (e != cudaSuccess) return status_from(e);
+    size_t th = (size_t)L.max_slots * kXM * (H / 8);
+    e = launch(rows_image_k, dim3((unsigned)((th + 255) / 256)), dim3(256), 0, s, x, x_dtype, H, H, 0, (const int2*)slots,
+               (const int*)(meta + 1), L.max_slots, counts, offsets, order, topk, aimg);
+    if (e != cudaSuccess) return status_from(e);
+
+    XArgs a{};
+    a.w = (const uint8_t*)up;
+    a.wstride = iq2_bytes(F, H);
+    a.a = aimg;
+    a.N = F;
+    a.K = H;
+    a.tiles = tiles;
+    a.ntiles = meta;
+    a.max_mtiles = L.max_tiles;
+    e = launch_x<DeqIQ2>(a, EpiImg{actimg}, s);
+    if (e != cudaSuccess) return status_from(e);
+    if (act_rows) {
+        th = (size_t)L.max_slots * kXM * (F / 8);
+        e = launch(act_rows_k, dim3((unsigned)((th + 255) / 256)), dim3(256), 0, s, (const uint8_t*)actimg, F,
+                   (const int2*)slots, (const int*)(meta + 1), L.max_slots, counts, offsets, order, (__half*)act_rows);
+        if (e != cudaSuccess) return status_from(e);
+    }
+    a.w = (const uint8_t*)down;
+    a.wstride = iq2_bytes(H, F);
+    a.a = actimg;
+    a.N = H;
+    a.K = F;
+    return status_from(launch_x<DeqIQ2>(a, EpiRows{mo, H, offsets, order}, s));
 }
 
 }  // extern "C"

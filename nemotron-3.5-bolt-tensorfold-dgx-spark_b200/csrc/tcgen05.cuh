@@ -57,6 +57,20 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
     d |= (uint64_t)2 << 61;
     return d;
 }
+// UMMA shared-memory descriptor, K-major, 64-byte swizzle: rows of 64 B, 8-row atoms of 512 B (stride offset 512 B),
+// version 1, layout type 4 (SWIZZLE_64B)
+__device__ __forceinline__ uint64_t umma_desc_sw64(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)(512 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)4 << 61;
+    return d;
+}
+// the 16-byte chunk c (0..3) of row r of a 64-byte-swizzled K-major tile
+__host__ __device__ __forceinline__ uint32_t sw64_off(int r, int c) { return (uint32_t)(r * 64 + ((c ^ ((r >> 1) & 3)) << 4)); }
+
 // descriptor of an unswizzled K-major matrix of 16-byte rows (8-row core matrices of 128 B, stride 128 B): the source
 // of tcgen05.cp 32x128b
 __device__ __forceinline__ uint64_t umma_desc_rows16(uint32_t saddr) {

@@ -26,12 +26,29 @@ def q8_blocks(seed, n, k):
     return np.concatenate([d.view(np.uint8).reshape(n, k // 32, 2), qv.view(np.uint8)], -1).reshape(n, -1)
 
 
-@pytest.mark.parametrize("n,k,T", [(256, 64, 1), (256, 512, 5), (512, 1024, 300), (6144, 4096, 256)])
-def test_q8_prompt_gemm(n, k, T):
+def np_q8_tc(blocks, n, k):
+    """numpy statement of the q8 tc layout: units (32-row tile, 32-k block) of [32][32] int8 then [32] fp16 d"""
+    b = blocks.reshape(n // 32, 32, k // 32, 34).transpose(0, 2, 1, 3)   # [t][kb][lane][34]
+    q = b[..., 2:].reshape(n // 32, k // 32, 1024)
+    d = b[..., :2].reshape(n // 32, k // 32, 64)
+    return np.concatenate([q, d], -1).reshape(-1)
+
+
+def test_q8_tc_pack_layout():
+    n, k = 64, 512
+    blocks = q8_blocks(3, n, k)
+    got = b200q.tile_q8_tc(dev(blocks), n, k).cpu().numpy()
+    assert np.array_equal(got, np_q8_tc(blocks, n, k))
+
+
+@pytest.mark.parametrize("n,k,T,dt", [(256, 256, 1, "bf16"), (288, 512, 5, "f32"), (512, 1024, 300, "bf16"),
+                                      (6144, 4096, 256, "bf16"), (1024, 512, 515, "f32")])
+def test_q8_prompt_gemm(n, k, T, dt):
     blocks = q8_blocks(n + T, n, k)
     xb, x = normal_bf16(n * 3 + T, (T, k))
-    w = b200q.tile_q8_rows(dev(blocks), n, k)
-    y = b200q.mma_q8_prompt(w, n, k, dev(xb).view(torch.bfloat16)).cpu().numpy()
+    xt = dev(xb).view(torch.bfloat16) if dt == "bf16" else dev(x)
+    w = b200q.tile_q8_tc(dev(blocks), n, k)
+    y = b200q.mma_q8_prompt(w, n, k, xt).cpu().numpy()
     assert b200q.device_error() == 0
     assert rel_l2(y, O.q8_gemm_f16fold(blocks, n, k, x)) < 1e-4
     assert_tolerance(y, O.q8_gemm_exact(blocks, n, k, x))
@@ -51,8 +68,8 @@ def test_group_large():
         assert np.array_equal(np.sort(got[oo[e]:oo[e + 1]]), oord[oo[e]:oo[e + 1]])
 
 
-@pytest.mark.parametrize("T,H,F,E,topk", [(40, 512, 256, 8, 3), (300, 1024, 512, 16, 6)])
-def test_moe_prompt_up_down(T, H, F, E, topk):
+@pytest.mark.parametrize("T,H,F,E,topk", [(40, 512, 256, 8, 3), (300, 1024, 512, 16, 6), (700, 512, 768, 4, 2)])
+def test_moe_prompt(T, H, F, E, topk):
     up = iq2_blocks(7 + T, E * F, H)
     down = iq2_blocks(8 + T, E * H, F)
     xb, x = normal_bf16(9 + T, (T, H))
@@ -61,15 +78,17 @@ def test_moe_prompt_up_down(T, H, F, E, topk):
     counts, offsets, order = b200q.k_moe_group_large(dev(ridx.reshape(-1)), E)
     pu = b200q.repack_iq2(dev(up.reshape(-1)), E * F, H)
     pd = b200q.repack_iq2(dev(down.reshape(-1)), E * H, F)
-    act = b200q.moe_up_tile(pu, E, F, H, counts, offsets, order, topk, dev(xb).view(torch.bfloat16))
+    pairs = T * topk
+    act = torch.full((pairs, F), float("nan"), dtype=torch.float16, device=DEV)
+    y = b200q.moe_prompt(pu, pd, E, H, F, counts, offsets, order, topk, dev(xb).view(torch.bfloat16), act=act)
+    y = y.cpu().numpy()
     act_np = act.float().cpu().numpy()
-    y = b200q.moe_down_tile(pd, E, H, F, counts, offsets, order, act).cpu().numpy()
     assert b200q.device_error() == 0
     ub, db = up.reshape(E, -1), down.reshape(E, -1)
     r = ridx.reshape(-1)
-    ref_act = np.stack([O.iq2_gemm_f16fold(ub[r[p]], F, H, x[p // topk], 1)[0] for p in range(T * topk)])
+    ref_act = np.stack([O.iq2_gemm_f16fold(ub[r[p]], F, H, x[p // topk], 1)[0] for p in range(pairs)])
     assert rel_l2(act_np, ref_act.astype(np.float16).astype(np.float32)) < 2e-3   # act is rounded to fp16
-    ref_y = np.stack([O.iq2_gemm_f16fold(db[r[p]], H, F, act_np[p], 0)[0] for p in range(T * topk)])
+    ref_y = np.stack([O.iq2_gemm_f16fold(db[r[p]], H, F, act_np[p], 0)[0] for p in range(pairs)])
     assert rel_l2(y, ref_y) < 1e-4
-    ex_act = np.stack([O.iq2_gemm_exact(ub[r[p]], F, H, x[p // topk], 1)[0] for p in range(T * topk)])
+    ex_act = np.stack([O.iq2_gemm_exact(ub[r[p]], F, H, x[p // topk], 1)[0] for p in range(pairs)])
     assert_tolerance(act_np, ex_act)
