@@ -10,7 +10,10 @@ step time.  L2 is defeated by rotating 4 layer copies (2.2 GB of experts) and 8 
 
 --impl reference times the reference's arithmetic on the host cores: the CPU oracle (a scalar C restatement of
 libbolt's kernels; libbolt has no CPU implementation of this path) with every host thread, on a bounded sample.
-Under torchrun each rank runs its own replica of the layer on its own tokens (weak scaling); rank 0 prints one line.
+Under torchrun (N > 1) the layer runs expert-parallel: 128/N experts a rank, 16 tokens a rank,
+NCCL all-to-all dispatch and combine; the line's value is the decode GB/s over all ranks (weak scaling), its
+"prefill" the prompt layer at 8192 tokens a rank.  At N = 1 the "ep" object reports the same expert-parallel code on
+one rank, the basis of the scaling.
 """
 import argparse
 import ctypes
@@ -115,11 +118,11 @@ def make_layers(b200q, device):
     return layers
 
 
-def zipf_routing(seed, tokens, topk, s=1.1):
-    """BASELINE config 4's routing: Zipf(s) over the experts through a seeded rank -> expert permutation, top-k
-    distinct experts a token."""
+def zipf_routing(seed, tokens, topk, s=1.1, perm_seed=None):
+    """BASELINE config 4's routing: Zipf(s) over the experts through a seeded rank -> expert permutation (from
+    perm_seed when given, so that several draws share the experts' popularity), top-k distinct experts a token."""
     rng = np.random.default_rng(seed)
-    perm = rng.permutation(E)
+    perm = np.random.default_rng(perm_seed).permutation(E) if perm_seed is not None else rng.permutation(E)
     p = 1.0 / np.arange(1, E + 1) ** s
     p /= p.sum()
     ridx = np.empty((tokens, topk), np.int32)
@@ -182,6 +185,177 @@ def prefill_bench(b200q, layer, device, iters=5):
             "hottest_expert_rows": int(cnt.max()), "device_error": err}
 
 
+def full_layer(b200q, device, L):
+    """layer copy L of make_layers: the packed up / down slabs of all experts and the shared expert (same seeds)"""
+    up = b200q.repack_iq2(b200q.synth_iq2(1000 + 10 * L, E * F * (H // 256), device), E * F, H)
+    down = b200q.repack_iq2(b200q.synth_iq2(1001 + 10 * L, E * H * (F // 256), device), E * H, F)
+    su = b200q.repack_iq2(b200q.synth_iq2(1002 + 10 * L, F * (H // 256), device), F, H)
+    sd = b200q.repack_iq2(b200q.synth_iq2(1003 + 10 * L, H * (F // 256), device), H, F)
+    return up, down, su, sd
+
+
+def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
+    """the MoE layer expert-parallel over the ranks (128 / N experts a rank), each rank with its
+    own tokens.  decode: 16 tokens a rank, uniform placement, fixed-capacity exchange, shared expert on every rank;
+    GB/s = the touched experts' bytes over all ranks (+ activations) / the slowest rank's step time.  prefill: 8192
+    tokens a rank, Zipf(1.1) routing, LPT placement with the hottest experts split; TFLOPS over all ranks."""
+    from ep import ExpertParallelMoE, LocalExperts, Placement, SharedExpert, slice_slab
+    dist = world > 1
+    up_b, down_b = b200q.iq2_bytes(F, H), b200q.iq2_bytes(H, F)
+
+    def barrier():
+        if dist:
+            torch.distributed.barrier()
+
+    def max_ms(ms):
+        if dist:
+            t = torch.tensor([ms], device=device)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    res = {}
+    # ---- decode ----------------------------------------------------------------------------------------------
+    pl = Placement(E, world, seed=7)
+    loc = pl.local[rank]
+    layers, ex_ms = [], []
+    for L in range(LAYERS):
+        up, down, su, sd = full_layer(b200q, device, L)
+        ex = LocalExperts(slice_slab(up, loc, up_b), slice_slab(down, loc, down_b), len(loc), H, F)
+        del up, down
+        moe = ExpertParallelMoE(pl, rank, world, H, TOPK, ex.decode, shared_fn=SharedExpert(su, sd, H, F, T, device),
+                                layout="capacity", device=device)
+        moe.ex = ex
+        layers.append(moe)
+    torch.cuda.synchronize()
+    xs_h, ls_h = make_batches(rank, device)
+    xs = [x.to(device) for x in xs_h]
+    ls = [l.to(device) for l in ls_h]
+
+    def step(i):
+        ridx, rw = b200q.k_route(ls[i % BATCHES], TOPK)
+        return layers[i % LAYERS](xs[i % BATCHES], ridx, rw)
+
+    # bytes of a step of batch b over all ranks: every rank's touched local experts + its shared expert + activations
+    step_bytes_b, rank_hits = [], []
+    for b in range(BATCHES):
+        ridx, _ = b200q.k_route(ls[b], TOPK)
+        if dist:
+            allr = [torch.empty_like(ridx) for _ in range(world)]
+            torch.distributed.all_gather(allr, ridx)
+        else:
+            allr = [ridx]
+        hit = np.unique(torch.cat(allr).cpu().numpy())
+        n_hit = sum(len(pl.owners[e]) for e in hit)
+        step_bytes_b.append((n_hit + world) * EXPERT_BYTES + world * (T * H * 2 + T * E * 2 + T * H * 4))
+        rank_hits.append(sum(1 for e in hit if rank in pl.owners[e]))
+    for i in range(warmup):
+        step(i)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    if clk:
+        clk.__enter__()
+    ev0.record()
+    for i in range(steps):
+        step(warmup + i)
+    ev1.record()
+    torch.cuda.synchronize()
+    if clk:
+        clk.__exit__()
+    barrier()
+    ms = max_ms(ev0.elapsed_time(ev1))
+    nbytes = sum(step_bytes_b[(warmup + i) % BATCHES] for i in range(steps))
+    # a second pass with events around the exchanges and the local expert GEMVs
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    for e in evs:
+        e.record()
+    acc = np.zeros(3)
+    nprof = min(steps, 50)
+    for i in range(nprof):
+        moe = layers[(warmup + i) % LAYERS]
+        moe.timing = evs[:4]
+        inner = moe.expert_fn
+
+        def timed(rows, lidx, n, inner=inner):
+            evs[4].record()
+            y = inner(rows, lidx, n)
+            evs[5].record()
+            return y
+        moe.expert_fn = timed
+        step(warmup + i)
+        moe.expert_fn, moe.timing = inner, None
+        torch.cuda.synchronize()
+        acc += [evs[0].elapsed_time(evs[1]), evs[2].elapsed_time(evs[3]), evs[4].elapsed_time(evs[5])]
+    acc /= nprof
+    # end to end: every step copies its tokens and logits from pinned host memory and reads the output back
+    xh = [x.pin_memory() for x in xs_h]
+    lh = [l.pin_memory() for l in ls_h]
+    oh = torch.empty(T, H, dtype=torch.float32).pin_memory()
+    xd = torch.empty(T, H, dtype=torch.bfloat16, device=device)
+    ld = torch.empty(T, E, dtype=torch.bfloat16, device=device)
+    barrier()
+    torch.cuda.synchronize()
+    ev0.record()
+    for i in range(steps):
+        b = (warmup + i) % BATCHES
+        xd.copy_(xh[b], non_blocking=True)
+        ld.copy_(lh[b], non_blocking=True)
+        ridx, rw = b200q.k_route(ld, TOPK)
+        oh.copy_(layers[(warmup + i) % LAYERS](xd, ridx, rw), non_blocking=True)
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_ms(ev0.elapsed_time(ev1))
+    res["decode"] = {"gbs": round(nbytes / (ms * 1e-3) / 1e9, 2), "ms_per_step": round(ms / steps, 5),
+                     "steps": steps, "experts_per_rank": len(loc), "layout": "capacity",
+                     "dispatch_plus_shared_ms": round(float(acc[0]), 5), "return_ms": round(float(acc[1]), 5),
+                     "local_experts_ms": round(float(acc[2]), 5), "step_bytes_mean": float(np.mean(step_bytes_b)),
+                     "rank_local_expert_bytes": float(np.mean(rank_hits)) * EXPERT_BYTES,
+                     "e2e_gbs": round(nbytes / (e2e_ms * 1e-3) / 1e9, 2),
+                     "h2d_bytes_per_step": T * H * 2 + T * E * 2, "d2h_bytes_per_step": T * H * 4}
+    del layers
+    torch.cuda.empty_cache()
+
+    # ---- prefill -------------------------------------------------------------------------------------------
+    if prefill:
+        Tp = 8192
+        calib = zipf_routing(999, 2048, TOPK, perm_seed=12)
+        loads = np.bincount(calib.reshape(-1), minlength=E).astype(np.float64)
+        plp = Placement(E, world, loads=loads, replicate=8 if world > 1 else 0)
+        locp = plp.local[rank]
+        up, down, _, _ = full_layer(b200q, device, 0)
+        ex = LocalExperts(slice_slab(up, locp, up_b), slice_slab(down, locp, down_b), len(locp), H, F)
+        del up, down
+        moe = ExpertParallelMoE(plp, rank, world, H, TOPK, ex.prompt, layout="exact", device=device)
+        g = torch.Generator().manual_seed(300 + rank)
+        x = torch.randn(Tp, H, generator=g).to(torch.bfloat16).to(device)
+        ridx = torch.from_numpy(zipf_routing(12 + 1000 * rank, Tp, TOPK, perm_seed=12)).to(device)
+        rw = torch.full((Tp, TOPK), 1.0 / TOPK, device=device)
+        for _ in range(2):
+            moe(x, ridx, rw)
+        iters = 5
+        barrier()
+        torch.cuda.synchronize()
+        ev0.record()
+        for _ in range(iters):
+            moe(x, ridx, rw)
+        ev1.record()
+        torch.cuda.synchronize()
+        barrier()
+        pms = max_ms(ev0.elapsed_time(ev1)) / iters
+        flops = world * 2.0 * Tp * TOPK * H * F * 2
+        res["prefill"] = {"tflops": round(flops / (pms * 1e-3) / 1e12, 1), "ms": round(pms, 4),
+                          "tokens_per_rank": Tp, "experts_per_rank": len(locp),
+                          "expected_rank_imbalance": round(plp.imbalance(), 4),
+                          "copies": int(sum(len(o) for o in plp.owners)), "layout": "exact",
+                          "step": "dispatch + group + tcgen05 up/down + return + combine"}
+        del moe, ex
+        torch.cuda.empty_cache()
+    res["device_error"] = b200q.device_error()
+    return res
+
+
 def make_batches(rank, device):
     g = torch.Generator().manual_seed(77 + rank)
     xs = [torch.randn(T, H, generator=g).to(torch.bfloat16) for _ in range(BATCHES)]
@@ -195,8 +369,52 @@ def step_bytes(ridx_np):
     return (distinct + 1) * EXPERT_BYTES + T * H * 2 + T * E * 2 + T * H * 4, distinct
 
 
+def run_ep(args, rank, world, local_rank):
+    """N > 1: BASELINE config 5, the MoE layer expert-parallel over the ranks (see ep_bench); rank 0 prints."""
+    import b200q
+    import datetime
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    clk = Clocks(local_rank)
+    r = ep_bench(b200q, rank, world, device, args.steps, args.warmup, prefill=args.prefill, clk=clk)
+    line = None
+    if rank == 0:
+        d = r["decode"]
+        peak, peak_kind = peaks()
+        ach = d["rank_local_expert_bytes"] / (d["local_experts_ms"] * 1e-3) / 1e9 if d["local_experts_ms"] else None
+        line = {
+            "metric": METRIC, "value": d["gbs"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": d["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "BASELINE config 5 (decode): the config-2 MoE layer expert-parallel over N GPUs, "
+                                   "128/N experts a GPU, 16 tokens a GPU, NCCL all-to-all dispatch and combine (bf16)",
+                       "tokens_per_gpu": T, "hidden": H, "experts": E, "topk": TOPK, "ffn": F, "shared_experts": 1,
+                       "l2": f"{LAYERS} rotating layer copies and {BATCHES} token batches",
+                       "parallelism": f"ep{world}"},
+            "hbm_fraction": round(d["gbs"] / world / peak, 4),
+            "roofline": {"bound": "hbm", "kernel": "local expert GEMVs (int8 up + down) on rank 0",
+                         "achieved": round(ach, 1) if ach else None, "peak": peak, "unit": "GB/s",
+                         "frac": round(ach / peak, 4) if ach else None, "traffic": None, "peak_kind": peak_kind},
+            "cpu_baseline": None,
+            "cpu_baseline_note": "the CPU oracle is timed at N=1 only",
+            "e2e": {"value": d["e2e_gbs"], "unit": "GB/s", "h2d_bytes_per_step": d["h2d_bytes_per_step"],
+                    "d2h_bytes_per_step": d["d2h_bytes_per_step"]},
+            "gpu_launches": 9 * args.steps,
+            "clocks": clk.summary(),
+            "ep": r,
+        }
+        if "prefill" in r:
+            line["prefill"] = r["prefill"]
+    torch.distributed.barrier()
+    torch.distributed.destroy_process_group()
+    return line
+
+
 def run_ours(args, rank, world, local_rank):
     import b200q
+    if world > 1:
+        return run_ep(args, rank, world, local_rank)
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     dist = world > 1
@@ -330,6 +548,7 @@ def run_ours(args, rank, world, local_rank):
         }
         if pre:
             line["prefill"] = pre
+        line["ep"] = ep_bench(b200q, 0, 1, device, min(args.steps, 500), args.warmup, prefill=args.prefill)
     if dist:
         torch.distributed.destroy_process_group()
     return line

@@ -1,0 +1,259 @@
+"""Expert-parallel MoE across the GPUs of one box: the routed experts are sharded over the ranks, the tokens move by
+all-to-all (NCCL over NVLink/NVSwitch on B200; the exchange itself runs on any torch.distributed backend).
+
+libbolt runs every expert of a layer on its one GB10 (the MoE block of enqueue_block, bolt_host.cu:665-720: route,
+group, up, down, combine).  Across ranks the same layer becomes, per step:
+
+  1. route locally (b200q_route over this rank's tokens);
+  2. give every (token, expert) pair a destination: the rank holding the expert (a replicated expert's pairs are
+     split between its copies by token index);
+  3. dispatch the pairs' token rows (bf16, hidden 8 KB) with all_to_all_single, and with them the expert's local
+     index on the destination;
+  4. run the grouped expert GEMMs on the received rows (decode: the int8 IQ2 GEMVs; prompt: the tcgen05 GEMMs);
+  5. return the pair outputs (bf16 by default) with the reverse all_to_all_single;
+  6. combine them with the router weights at the source (b200q_combine), adding the shared expert, which every
+     rank runs for its own tokens while the dispatch is in flight.
+
+Two exchange layouts:
+  * "capacity" (decode): every rank sends a fixed `cap` rows to every peer (cap = the most pairs a rank can route,
+    T * topk, so nothing is ever dropped); rows past a peer's real count carry the discard index and are never
+    computed.  No device-to-host read, so a decode step can be captured in a CUDA graph.
+  * "exact" (prompt): the per-peer counts are exchanged first and read on the host to size the transfers.
+
+Placement: with uniform loads, a round-robin over a seeded permutation of the experts.  With expected loads, the
+`replicate` hottest experts are cut into copies of at most half a rank's mean load, and the pieces are placed by LPT
+(largest first, each to the least-loaded rank that does not hold that expert yet).
+"""
+import numpy as np
+import torch
+import torch.distributed as dist
+
+
+class Placement:
+    """Where the experts live.  owners[e]: the ranks holding expert e (pair with token t -> owners[e][t % n]);
+    local[r]: the experts of rank r in local order; lidx[(e, r)]: e's index on rank r."""
+
+    def __init__(self, E, world, loads=None, replicate=0, seed=0):
+        self.E, self.world = E, world
+        if loads is None:
+            rng = np.random.default_rng(seed)
+            perm = rng.permutation(E)
+            owners = [[] for _ in range(E)]
+            for i, e in enumerate(perm):
+                owners[e].append(i % world)
+            rank_load = np.zeros(world)
+        else:
+            # the `replicate` hottest experts are cut into copies of at most half a rank's mean load each; then LPT
+            # over the pieces, largest first, each to the least-loaded rank that does not hold that expert yet
+            loads = np.asarray(loads, np.float64)
+            hot = set(np.argsort(-loads, kind="stable")[:replicate].tolist()) if world > 1 else set()
+            piece_cap = loads.sum() / world / 2
+            pieces = []
+            for e in range(E):
+                n = min(world, max(1, int(np.ceil(loads[e] / piece_cap)))) if e in hot and piece_cap > 0 else 1
+                pieces += [(loads[e] / n, e)] * n
+            owners = [[] for _ in range(E)]
+            rank_load = np.zeros(world)
+            for share, e in sorted(pieces, key=lambda t: (-t[0], t[1])):
+                r = min((r for r in range(world) if r not in owners[e]), key=lambda r: (rank_load[r], r))
+                owners[e].append(r)
+                rank_load[r] += share
+        self.owners = owners
+        self.rank_load = rank_load
+        self.local = [[] for _ in range(world)]
+        self.lidx = {}
+        for e in range(E):
+            for r in owners[e]:
+                self.lidx[(e, r)] = len(self.local[r])
+                self.local[r].append(e)
+        self.max_rep = max(len(o) for o in owners)
+
+    def tables(self, device):
+        """dest [E][max_rep], lidx [E][max_rep] (int64), nrep [E] as tensors for the device-side lookup."""
+        dest = torch.zeros(self.E, self.max_rep, dtype=torch.int64)
+        lid = torch.zeros(self.E, self.max_rep, dtype=torch.int64)
+        nrep = torch.zeros(self.E, dtype=torch.int64)
+        for e in range(self.E):
+            nrep[e] = len(self.owners[e])
+            for j in range(self.max_rep):
+                r = self.owners[e][j % len(self.owners[e])]
+                dest[e, j] = r
+                lid[e, j] = self.lidx[(e, r)]
+        return dest.to(device), lid.to(device), nrep.to(device)
+
+    def imbalance(self):
+        """max over mean of the expected per-rank loads"""
+        m = self.rank_load.mean()
+        return float(self.rank_load.max() / m) if m > 0 else 1.0
+
+
+class ExpertParallelMoE:
+    """One expert-parallel MoE layer on this rank.
+
+    expert_fn(rows [R][H] (send dtype), lidx [R] int64, n_local) -> [R][H] fp32: the local experts applied to the
+    received rows; rows whose lidx == n_local are padding and may hold anything.
+    combine_fn(mo [pairs][H] fp32, rw [T][topk] fp32, shared [T][H] fp32 or None) -> [T][H] fp32; b200q_combine by
+    default.  shared_fn(x) -> [T][H] fp32 or None: the shared expert on this rank's tokens."""
+
+    def __init__(self, placement, rank, world, H, topk, expert_fn, shared_fn=None, combine_fn=None, group=None,
+                 layout="capacity", send_dtype=torch.bfloat16, device=None):
+        self.p, self.rank, self.world, self.H, self.topk = placement, rank, world, H, topk
+        self.n_local = len(placement.local[rank])
+        self.expert_fn, self.shared_fn = expert_fn, shared_fn
+        self.combine_fn = combine_fn or _gpu_combine(topk)
+        self.group, self.layout, self.send_dtype = group, layout, send_dtype
+        self.device = device or torch.device("cpu")
+        self.dest_t, self.lidx_t, self.nrep_t = placement.tables(self.device)
+        self.timing = None   # optional: a list of 4 CUDA events (dispatch start/end, return start/end)
+
+    # -- the pieces ----------------------------------------------------------------------------------------
+    def _route(self, ridx):
+        """per pair: destination rank, local expert index there, the order that sorts pairs by destination, and
+        the pair's position inside its destination's block"""
+        e = ridx.reshape(-1).to(torch.int64)
+        pairs = e.numel()
+        tok = torch.arange(pairs, device=e.device) // self.topk
+        rep = tok % self.nrep_t[e]
+        dest = self.dest_t[e, rep]
+        lidx = self.lidx_t[e, rep]
+        order = torch.sort(dest, stable=True).indices
+        counts = torch.zeros(self.world, dtype=torch.int64, device=e.device).scatter_add_(0, dest, torch.ones_like(dest))
+        starts = torch.cumsum(counts, 0) - counts
+        pos = torch.arange(pairs, device=e.device) - starts[dest[order]]
+        return dest, lidx, order, counts, pos, tok
+
+    def _a2a(self, out, inp, out_splits=None, in_splits=None, async_op=False):
+        if self.world == 1:   # one rank: the exchange is a copy (no process group needed)
+            out.copy_(inp)
+            return _Done()
+        return dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group, async_op=async_op)
+
+    def __call__(self, x, ridx, rw):
+        """x [T][H] (this rank's tokens), ridx [T][topk] global expert ids, rw [T][topk] -> out [T][H] fp32"""
+        T, H, topk = x.shape[0], self.H, self.topk
+        pairs = T * topk
+        dest, lidx, order, counts, pos, tok = self._route(ridx)
+        xs = x.to(self.send_dtype)
+        ev = self.timing
+        if self.layout == "capacity":
+            cap = pairs
+            slot = dest[order] * cap + pos                       # where each sorted pair sits in the send buffer
+            send = torch.empty(self.world * cap, H, dtype=self.send_dtype, device=x.device)
+            send_l = torch.full((self.world * cap,), self.n_local_max_peer(), dtype=torch.int64, device=x.device)
+            send.index_copy_(0, slot, xs.index_select(0, tok[order]))
+            send_l.index_copy_(0, slot, lidx[order])
+            recv = torch.empty_like(send)
+            recv_l = torch.empty_like(send_l)
+            if ev:
+                ev[0].record()
+            w1 = self._a2a(recv, send, async_op=True)
+            w2 = self._a2a(recv_l, send_l, async_op=True)
+            shared = self.shared_fn(x) if self.shared_fn else None   # overlaps the dispatch
+            w1.wait()
+            w2.wait()
+            if ev:
+                ev[1].record()
+            recv_l = torch.where(recv_l >= self.n_local, torch.full_like(recv_l, self.n_local), recv_l)
+            y = self.expert_fn(recv, recv_l, self.n_local).to(self.send_dtype)
+            back = torch.empty_like(y)
+            if ev:
+                ev[2].record()
+            self._a2a(back, y)
+            if ev:
+                ev[3].record()
+            got = back.index_select(0, slot)                     # sorted pair order
+        else:
+            rc = torch.empty_like(counts)
+            self._a2a(rc, counts)
+            send_splits = counts.tolist()
+            recv_splits = rc.tolist()
+            send = xs.index_select(0, tok[order])
+            send_l = lidx[order]
+            recv = torch.empty(sum(recv_splits), H, dtype=self.send_dtype, device=x.device)
+            recv_l = torch.empty(sum(recv_splits), dtype=torch.int64, device=x.device)
+            if ev:
+                ev[0].record()
+            w1 = self._a2a(recv, send, recv_splits, send_splits, async_op=True)
+            w2 = self._a2a(recv_l, send_l, recv_splits, send_splits, async_op=True)
+            shared = self.shared_fn(x) if self.shared_fn else None   # overlaps the dispatch
+            w1.wait()
+            w2.wait()
+            if ev:
+                ev[1].record()
+            y = self.expert_fn(recv, recv_l, self.n_local).to(self.send_dtype)
+            got = torch.empty(pairs, H, dtype=self.send_dtype, device=x.device)
+            if ev:
+                ev[2].record()
+            self._a2a(got, y, send_splits, recv_splits)
+            if ev:
+                ev[3].record()
+        mo = torch.empty(pairs, H, dtype=torch.float32, device=x.device)
+        mo.index_copy_(0, order, got.to(torch.float32))
+        return self.combine_fn(mo, rw, shared)
+
+    def n_local_max_peer(self):
+        """the discard index every receiver maps to its own n_local (any index >= its expert count)"""
+        return max(len(l) for l in self.p.local)
+
+
+class _Done:
+    def wait(self):
+        pass
+
+
+def _gpu_combine(topk):
+    def f(mo, rw, shared):
+        import b200q
+        return b200q.k_combine(mo, rw.reshape(-1).contiguous(), topk, shared=shared)
+    return f
+
+
+class LocalExperts:
+    """The routed experts one rank holds (packed rt32 slabs of its local experts, in local order) and their grouped
+    GEMMs on received rows; lidx == n_local marks padding rows, which are grouped but never computed."""
+
+    def __init__(self, up, down, n_local, H, F):
+        self.up, self.down, self.n, self.H, self.F = up, down, n_local, H, F
+
+    def decode(self, rows, lidx, n_local):
+        import b200q
+        if rows.shape[0] == 0 or self.n == 0:
+            return torch.zeros(rows.shape[0], self.H, dtype=torch.float32, device=rows.device)
+        xq, xs = b200q.k_quant_rows(rows)
+        counts, offsets, order = b200q.k_moe_group(lidx.to(torch.int32), n_local + 1)
+        aq, as_ = b200q.moe_up_q8(self.up, n_local, self.F, self.H, counts, offsets, order, 1, xq, xs)
+        return b200q.moe_down(self.down, n_local, self.H, self.F, counts, offsets, order, aq, as_)
+
+    def prompt(self, rows, lidx, n_local):
+        import b200q
+        out = torch.zeros(rows.shape[0], self.H, dtype=torch.float32, device=rows.device)
+        if rows.shape[0] == 0 or self.n == 0:
+            return out
+        counts, offsets, order = b200q.k_moe_group_large(lidx.to(torch.int32), n_local + 1)
+        return b200q.moe_prompt(self.up, self.down, n_local, self.H, self.F, counts, offsets, order, 1, rows, mo=out)
+
+
+def slice_slab(slab, experts, expert_bytes):
+    """the packed rt32 matrices of `experts` (in that order) out of a full slab, as one local slab"""
+    if len(experts) == 0:
+        return slab[:0].clone()
+    return torch.cat([slab[e * expert_bytes:(e + 1) * expert_bytes] for e in experts])
+
+
+class SharedExpert:
+    """The shared expert on a rank's own decode tokens: the int8 GEMV pair over one group of all T rows."""
+
+    def __init__(self, up, down, H, F, T, device):
+        self.up, self.down, self.H, self.F = up, down, H, F
+        self.counts = torch.tensor([T], dtype=torch.int32, device=device)
+        self.offsets = torch.tensor([0, T], dtype=torch.int32, device=device)
+        self.order = torch.arange(T, dtype=torch.int32, device=device)
+
+    def __call__(self, x):
+        import b200q
+        T = x.shape[0]
+        if T != int(self.order.numel()):
+            raise ValueError(f"SharedExpert was built for {int(self.order.numel())} tokens, got {T}")
+        xq, xs = b200q.k_quant_rows(x)
+        aq, as_ = b200q.moe_up_q8(self.up, 1, self.F, self.H, self.counts, self.offsets, self.order[:T], 1, xq, xs)
+        return b200q.moe_down(self.down, 1, self.H, self.F, self.counts, self.offsets, self.order[:T], aq, as_)
