@@ -356,6 +356,71 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
     return res
 
 
+def nvfp4_bench(b200q, device, iters=20):
+    """the NVFP4 Mamba-2 projections, in_proj 4096 -> 18560 and out_proj 8192 -> 4096 (e2m1 codes
+    U{0..15}, e4m3 scales U[0.5, 2] per 16, an fp32 tensor scale), activations bf16 N(0, 1).  M <= 16: the t16 decode
+    GEMV, GB/s over weights + x + y, rotating 4 weight copies (246 MB, larger than L2).  M >= 512: quant_nv4_rows +
+    the block-scaled fp4 tcgen05 GEMM, TFLOPS of the GEMM alone and of quantiser + GEMM."""
+    shapes = {"in_proj": (18560, 4096), "out_proj": (4096, 8192)}
+    copies = 4
+    g = torch.Generator(device="cpu").manual_seed(31)
+    W = {}
+    for name, (n, k) in shapes.items():
+        W[name] = []
+        for c in range(copies):
+            q = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, generator=g).to(device)
+            sc = (torch.rand(n, k // 16, generator=g) * 1.5 + 0.5).to(torch.float8_e4m3fn).view(torch.uint8).to(device)
+            W[name].append((b200q.tile_nv4(q, sc, n, k), b200q.tile_nv4w(q, sc, n, k) if c == 0 else None))
+    s2 = 0.01
+    out = {}
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for name, (n, k) in shapes.items():
+        for M in (1, 16):
+            x = torch.randn(M, k, generator=g).to(torch.bfloat16).to(device)
+            y = torch.empty(M, n, device=device)
+            for i in range(3):
+                b200q.mma_nv4(W[name][i % copies][0], s2, n, k, x, y=y)
+            torch.cuda.synchronize()
+            e0.record()
+            for i in range(iters):
+                b200q.mma_nv4(W[name][i % copies][0], s2, n, k, x, y=y)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / iters
+            nbytes = n * k // 2 + n * k // 16 + M * k * 2 + M * n * 4
+            out[f"{name}_M{M}_gbs"] = round(nbytes / (ms * 1e-3) / 1e9, 1)
+        for M in (512, 4096):
+            x = torch.randn(M, k, generator=g).to(torch.bfloat16).to(device)
+            rows = b200q.quant_nv4_rows(x)
+            y = torch.empty(M, n, device=device)
+            wt = W[name][0][1]
+            for _ in range(3):
+                b200q.mma_nv4_fp4(wt, s2, n, k, rows, M, y=y)
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(iters):
+                b200q.mma_nv4_fp4(wt, s2, n, k, rows, M, y=y)
+            e1.record()
+            torch.cuda.synchronize()
+            gemm_ms = e0.elapsed_time(e1) / iters
+            e0.record()
+            for _ in range(iters):
+                b200q.quant_nv4_rows(x, out=rows)
+                b200q.mma_nv4_fp4(wt, s2, n, k, rows, M, y=y)
+            e1.record()
+            torch.cuda.synchronize()
+            both_ms = e0.elapsed_time(e1) / iters
+            fl = 2.0 * M * n * k
+            out[f"{name}_M{M}_tflops"] = round(fl / (gemm_ms * 1e-3) / 1e12, 1)
+            out[f"{name}_M{M}_with_quant_tflops"] = round(fl / (both_ms * 1e-3) / 1e12, 1)
+    out["device_error"] = b200q.device_error()
+    out["fp4_peak_tflops"] = 9000.0
+    out["fp4_peak_kind"] = "nominal dense FP4 (no measured FP4 figure on this pool)"
+    out["workload"] = ("BASELINE config 3: NVFP4 in_proj 4096->18560 and out_proj 8192->4096; M 1/16 on the decode "
+                       "GEMV (fp16 mma.sync, exact e2m1*e4m3 operands), M 512/4096 on tcgen05.mma kind::mxf4nvf4")
+    return out
+
+
 def make_batches(rank, device):
     g = torch.Generator().manual_seed(77 + rank)
     xs = [torch.randn(T, H, generator=g).to(torch.bfloat16) for _ in range(BATCHES)]
@@ -549,6 +614,8 @@ def run_ours(args, rank, world, local_rank):
         if pre:
             line["prefill"] = pre
         line["ep"] = ep_bench(b200q, 0, 1, device, min(args.steps, 500), args.warmup, prefill=args.prefill)
+        if args.prefill:
+            line["nvfp4"] = nvfp4_bench(b200q, device)
     if dist:
         torch.distributed.destroy_process_group()
     return line
@@ -619,6 +686,8 @@ def main():
     ap.add_argument("--layers", type=int, default=4, help="layer copies rotated to defeat L2 (1 for small profiles)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="length of the CPU-baseline sample")
     ap.add_argument("--no-prefill", dest="prefill", action="store_false", help="skip the config-4 prefill GEMMs")
+    ap.add_argument("--only", choices=["prefill", "nvfp4", "ep"], default=None,
+                    help="run one sub-measurement on one GPU and print its object (for profiling)")
     args = ap.parse_args()
     global LAYERS
     LAYERS = max(1, args.layers)
@@ -626,7 +695,18 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
-    if args.impl == "reference":
+    if args.only:
+        import b200q
+        device = torch.device("cuda", local_rank)
+        torch.cuda.set_device(device)
+        if args.only == "prefill":
+            up, down, _, _ = full_layer(b200q, device, 0)
+            line = prefill_bench(b200q, type("L", (), {"up": up, "down": down}), device)
+        elif args.only == "nvfp4":
+            line = nvfp4_bench(b200q, device)
+        else:
+            line = ep_bench(b200q, 0, 1, device, min(args.steps, 500), args.warmup)
+    elif args.impl == "reference":
         line = run_reference(args, rank, world)
     else:
         line = run_ours(args, rank, world, local_rank)

@@ -6,11 +6,12 @@
 // columns), so every dequantised weight feeds 256 rows.  Per 32-k stage of a 5-stage shared-memory ring:
 //   A        the two 128-row halves (8 KB each), bulk-copied (cp.async.bulk, no tensor map) from an fp16 rows image
 //            by one lane of warp 0;
-//   B        256 weight rows x 32 k in fp16, written by 8 dequantising warps (warp w: rows 32w..32w+31, lane = row)
-//            from the packed weights, which each lane prefetches into registers ahead of use.  IQ2_XXS: a prmt picks
-//            every fp16 value out of its chunk's three scaled magnitudes and a xor sets its sign, with the selectors and
-//            sign masks read from lane-replicated shared-memory tables (conflict-free).  Q8_0: a magic-number prmt
-//            makes the int8 exact in fp16 and one hmul2 applies the scale;
+//   B        256 weight rows x 32 k in fp16, written by 16 dequantising warps in two sets of 8 that take alternate
+//            stages (warp w of a set: rows 32w..32w+31, lane = row), from the packed weights, which each lane
+//            prefetches into registers ahead of use.  IQ2_XXS: a prmt picks every fp16 pair out of its chunk's three
+//            scaled magnitudes and a xor sets its signs, the selectors and masks read as 128-bit entries from
+//            replicated shared-memory tables (conflict-free).  Q8_0: a magic-number prmt makes the int8 exact in fp16
+//            and one hmul2 applies the scale;
 //   MMA      one lane of warp 1 issues the m128n256k16 MMAs of both halves and commits them to the stage's barrier;
 //   epilogue 8 warps drain the accumulators (tcgen05.ld), hand them back to the MMA warp, and write the outputs.
 // Tiles (up to 256 rows of one group x 256 weight rows) are handed out persistently, one CTA per SM.
@@ -37,12 +38,12 @@ constexpr int kXM = 128;                        // rows of a slot and of an MMA 
 constexpr int kXN = 256;                        // weight rows of a tile
 constexpr int kXRec = kXM * 64;                 // 8 KB: a rows-image record (128 rows x 32 fp16)
 constexpr int kXB = kXN * 64;                   // 16 KB: the B tile of a stage
-constexpr int kXStage = 2 * kXRec + kXB;        // 32 KB
+constexpr int kXStage = 2 * kXRec + kXB;        // 32 KB: the two A halves, then the B tile
 constexpr int kXStages = 5;
-constexpr int kDeqWarps = 8, kXEpiWarps = 8;
-constexpr int kXThreads = (2 + kDeqWarps + kXEpiWarps) * 32;   // 576
-constexpr int kGridTbl = 256 * 16 * 8;          // 32 KB: grid-entry prmt selectors, 16 copies
-constexpr int kSignTbl = 128 * 32 * 4;          // 16 KB: sign masks, 32 copies
+constexpr int kDeqWarps = 16, kXEpiWarps = 8;  // dequantisers: two sets of 8 taking alternate stages
+constexpr int kXThreads = (2 + kDeqWarps + kXEpiWarps) * 32;   // 832
+constexpr int kGridTbl = 256 * 8 * 16;          // 32 KB: grid entry -> four prmt selectors, 8 copies
+constexpr int kSignTbl = 128 * 8 * 16;          // 16 KB: sign index -> four xor masks, 8 copies
 constexpr size_t kXSmem = (size_t)kXStages * kXStage + kGridTbl + kSignTbl + 1024 /*align*/ + 256 /*barriers*/;
 constexpr uint32_t kXTmemCols = 512;            // two 256-column accumulators
 
@@ -73,19 +74,19 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
     asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(s));
     return d;
 }
-__device__ __forceinline__ uint2 lds64(uint32_t addr) {
-    uint2 v;
-    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
-    return v;
-}
-__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-    return v;
-}
 __device__ __forceinline__ uint4 ldg_nc(const void* p) {
     uint4 v;
     asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint2 ldg_nc64(const void* p) {
+    uint2 v;
+    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
     return v;
 }
 __device__ __forceinline__ uint32_t ldg_u16(const void* p) {
@@ -154,79 +155,84 @@ struct EpiImg {              // fp16(relu(v)^2) into the next GEMM's rows image 
 };
 
 // ---------------------------------------------------------------------------------------------------------
-// B dequantisers.  run() produces every stage of one tile for the calling warp's 32 rows (lane = row): for each 32-k
-// block it waits for the stage to be free, writes the row's 64 B, and arrives on the stage's "full" barrier.
+// B dequantisers.  run() produces its phase's stages of one tile for the calling warp's 32 rows (lane = row): for
+// each of those 32-k blocks it waits for the stage to be free, writes the row's 64 B, and arrives on the stage's "full"
+// barrier.
 // ---------------------------------------------------------------------------------------------------------
 struct XRing {               // stage bookkeeping shared by the warps of one CTA
     uint32_t sbase, bars;
-    __device__ uint32_t full(int s) const { return bars + 8u * s; }
-    __device__ uint32_t empty(int s) const { return bars + 8u * (kXStages + s); }
-    __device__ uint32_t stage(int s) const { return sbase + (uint32_t)(s * kXStage); }
+    __device__ uint32_t full(int it) const { return bars + 8u * (it % kXStages); }
+    __device__ uint32_t empty(int it) const { return bars + 8u * (kXStages + it % kXStages); }
+    __device__ uint32_t stage(int it) const { return sbase + (uint32_t)((it % kXStages) * kXStage); }
+    static constexpr int kBars = 2 * kXStages;
 };
 
 // waits (lane 0) for the stage of iteration `it` to be free; false on a timeout (warp-uniform)
 __device__ __forceinline__ bool x_wait_free(const XRing& R, int it, int lane) {
-    const int s = it % kXStages, use = it / kXStages;
+    const int use = it / kXStages;
     int ok = 1;
-    if (use > 0 && lane == 0) ok = tc_mbar_wait(R.empty(s), (uint32_t)((use - 1) & 1)) ? 1 : 0;
+    if (use > 0 && lane == 0) ok = tc_mbar_wait(R.empty(it), (uint32_t)((use - 1) & 1)) ? 1 : 0;
     return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 __device__ __forceinline__ void x_stage_done(const XRing& R, int it, int lane) {
     tc_fence_proxy_async();   // the generic-proxy writes are visible to the tensor core
     __syncwarp();
-    if (lane == 0) tc_mbar_arrive(R.full(it % kXStages));
+    if (lane == 0) tc_mbar_arrive(R.full(it));
 }
 
 struct DeqIQ2 {              // IQ2_XXS rt32 layout (common.cuh); sign words re-encoded by the packer
     static constexpr bool kTables = true;
     uint32_t gtbl, stbl;     // shared-memory tables (set in the kernel)
-    // 8 fp16 of one 8-element group: magnitudes by prmt from {h8, h25, h43}, then the signs
-    __device__ __forceinline__ uint4 group(uint32_t P0, uint32_t P1, uint32_t gi, uint32_t si, int lane) const {
-        const uint2 sel = lds64(gtbl + ((gi * 16u + (uint32_t)(lane & 15)) << 3));
-        const uint32_t sp = lds32(stbl + ((si * 32u + (uint32_t)lane) << 2));
-        uint4 o;
-        o.x = prmt(P0, P1, sel.x) ^ ((sp << 15) & 0x80008000u);
-        o.y = prmt(P0, P1, sel.x >> 16) ^ ((sp << 14) & 0x80008000u);
-        o.z = prmt(P0, P1, sel.y) ^ ((sp << 13) & 0x80008000u);
-        o.w = prmt(P0, P1, sel.y >> 16) ^ ((sp << 12) & 0x80008000u);
-        return o;
+    // 8 fp16 of one 8-element group: each pair's magnitudes by prmt from {h8, h25, h43}, then its signs by xor.  A
+    // 128-bit table entry per grid index (selectors) and per sign index (masks), 8 copies so that the 8 lanes of a
+    // quarter-warp read 8 different bank groups.
+    __device__ __forceinline__ uint4 group(uint32_t P0, uint32_t P1, uint32_t gi, uint32_t si, uint32_t lane8) const {
+        const uint4 sel = lds128(gtbl + ((gi << 7) | lane8));
+        const uint4 sg = lds128(stbl + ((si << 7) | lane8));
+        return make_uint4(prmt(P0, P1, sel.x) ^ sg.x, prmt(P0, P1, sel.y) ^ sg.y, prmt(P0, P1, sel.z) ^ sg.z,
+                          prmt(P0, P1, sel.w) ^ sg.w);
     }
     __device__ __forceinline__ void chunk(uint32_t qx, uint32_t qy, float d, uint32_t row_addr, int lane) const {
         const uint32_t s4 = ((qy >> 7) & 1u) | ((qy >> 14) & 2u) | ((qy >> 21) & 4u) | ((qy >> 28) & 8u);
-        const float db = d * (0.5f + (float)s4) * 0.25f;
+        // (float)s4 without a conversion instruction: s4 in the mantissa of 2^23, minus 2^23 (exact)
+        const float fs4 = __uint_as_float(0x4B000000u | s4) - 8388608.f;
+        const float db = d * (0.5f + fs4) * 0.25f;
         const uint32_t P0 = h2u(__floats2half2_rn(8.f * db, 25.f * db));
-        const uint32_t P1 = (uint32_t)__half_as_ushort(__float2half_rn(43.f * db));
+        const uint32_t P1 = h2u(__floats2half2_rn(43.f * db, 0.f));
         const int sw = (lane >> 1) & 3;
+        const uint32_t lane8 = (uint32_t)(lane & 7) << 4;
 #pragma unroll
         for (int g = 0; g < 4; g++)
-            sts128(row_addr + (uint32_t)((g ^ sw) << 4), group(P0, P1, (qx >> (8 * g)) & 255u, (qy >> (8 * g)) & 127u, lane));
+            sts128(row_addr + (uint32_t)((g ^ sw) << 4), group(P0, P1, (qx >> (8 * g)) & 255u, (qy >> (8 * g)) & 127u, lane8));
     }
-    // rows of row tile rt of the group's matrix wm (n x K); valid: rt's rows exist
-    __device__ bool run(const XRing& R, int& it, const uint8_t* wm, int K, int rt, bool valid, int wd, int lane) const {
+    // the stages kk = phase, phase + 2, ... of one tile for the rows of row tile rt of the group's matrix wm (n x K);
+    // stage kk is ring iteration it0 + kk.  valid: rt's rows exist.
+    __device__ bool run(const XRing& R, int it0, const uint8_t* wm, int K, int rt, bool valid, int wd, int phase,
+                        int lane) const {
         const int nb = K >> 8;
-        const uint8_t* base = wm + (size_t)rt * nb * kIq2Unit;
-        uint4 c[4], n[4];
+        const uint8_t* base = wm + (size_t)rt * nb * kIq2Unit + lane * 16 + phase * 8;
+        uint2 c[4], n[4];   // this lane's chunks 2j + phase of the current / next super-block
         uint32_t dc = 0, dn = 0;
         if (valid) {
 #pragma unroll
-            for (int j = 0; j < 4; j++) c[j] = ldg_nc(base + j * 512 + lane * 16);
-            dc = ldg_u16(base + 2048 + lane * 2);
+            for (int j = 0; j < 4; j++) c[j] = ldg_nc64(base + j * 512);
+            dc = ldg_u16(wm + (size_t)rt * nb * kIq2Unit + 2048 + lane * 2);
         }
         for (int sb = 0; sb < nb; sb++) {
             if (valid && sb + 1 < nb) {
                 const uint8_t* u = base + (size_t)(sb + 1) * kIq2Unit;
 #pragma unroll
-                for (int j = 0; j < 4; j++) n[j] = ldg_nc(u + j * 512 + lane * 16);
-                dn = ldg_u16(u + 2048 + lane * 2);
+                for (int j = 0; j < 4; j++) n[j] = ldg_nc64(u + j * 512);
+                dn = ldg_u16(wm + ((size_t)rt * nb + sb + 1) * kIq2Unit + 2048 + lane * 2);
             }
             const float d = __half2float(__ushort_as_half((unsigned short)dc));
 #pragma unroll
-            for (int ch = 0; ch < 8; ch++, it++) {
+            for (int j = 0; j < 4; j++) {
+                const int it = it0 + sb * 8 + 2 * j + phase;
                 if (!x_wait_free(R, it, lane)) return false;
-                const uint32_t row_addr = R.stage(it % kXStages) + 2 * kXRec + (uint32_t)((wd * 32 + lane) * 64);
+                const uint32_t row_addr = R.stage(it) + 2 * kXRec + (uint32_t)((wd * 32 + lane) * 64);
                 if (valid) {
-                    const uint4 u = c[ch >> 1];
-                    chunk((ch & 1) ? u.z : u.x, (ch & 1) ? u.w : u.y, d, row_addr, lane);
+                    chunk(c[j].x, c[j].y, d, row_addr, lane);
                 } else {
 #pragma unroll
                     for (int g = 0; g < 4; g++) sts128(row_addr + g * 16, make_uint4(0, 0, 0, 0));
@@ -259,7 +265,9 @@ struct DeqQ8 {
         const uint32_t x0 = w0 ^ 0x80808080u, x1 = w1 ^ 0x80808080u;
         return make_uint4(pair(x0, 0x4140u, d2), pair(x0, 0x4342u, d2), pair(x1, 0x4140u, d2), pair(x1, 0x4342u, d2));
     }
-    __device__ bool run(const XRing& R, int& it, const uint8_t* wm, int K, int rt, bool valid, int wd, int lane) const {
+    // the stages kk = phase, phase + 2, ... of one tile (32-k blocks), prefetched three of this warp's blocks ahead
+    __device__ bool run(const XRing& R, int it0, const uint8_t* wm, int K, int rt, bool valid, int wd, int phase,
+                        int lane) const {
         const int nk = K >> 5;   // a multiple of 8
         const uint8_t* base = wm + (size_t)rt * nk * kQ8Unit;
         uint4 qa[4], qb[4];
@@ -267,24 +275,25 @@ struct DeqQ8 {
         if (valid) {
 #pragma unroll
             for (int u = 0; u < 3; u++) {
-                const uint8_t* p = base + (size_t)u * kQ8Unit;
+                const uint8_t* p = base + (size_t)(2 * u + phase) * kQ8Unit;
                 qa[u] = ldg_nc(p + lane * 32);
                 qb[u] = ldg_nc(p + lane * 32 + 16);
                 dd[u] = ldg_u16(p + 1024 + lane * 2);
             }
         }
-        for (int k0 = 0; k0 < nk; k0 += 4) {
+        for (int m0 = 0; m0 < nk / 2; m0 += 4) {
 #pragma unroll
-            for (int u = 0; u < 4; u++, it++) {
-                const int kb = k0 + u, nx = kb + 3;
-                if (valid && nx < nk) {   // prefetch three blocks ahead into the ring slot of block kb + 3
-                    const uint8_t* p = base + (size_t)nx * kQ8Unit;
+            for (int u = 0; u < 4; u++) {
+                const int m = m0 + u, kb = 2 * m + phase, nx = m + 3;
+                if (valid && nx < nk / 2) {   // prefetch this warp's block m + 3 into its ring slot
+                    const uint8_t* p = base + (size_t)(2 * nx + phase) * kQ8Unit;
                     qa[(u + 3) & 3] = ldg_nc(p + lane * 32);
                     qb[(u + 3) & 3] = ldg_nc(p + lane * 32 + 16);
                     dd[(u + 3) & 3] = ldg_u16(p + 1024 + lane * 2);
                 }
+                const int it = it0 + kb;
                 if (!x_wait_free(R, it, lane)) return false;
-                const uint32_t row_addr = R.stage(it % kXStages) + 2 * kXRec + (uint32_t)((wd * 32 + lane) * 64);
+                const uint32_t row_addr = R.stage(it) + 2 * kXRec + (uint32_t)((wd * 32 + lane) * 64);
                 const int sw = (lane >> 1) & 3;
                 if (valid) {
                     const __half2 d2 = __half2half2(__ushort_as_half((unsigned short)dd[u]));
@@ -315,35 +324,35 @@ __global__ void __launch_bounds__(kXThreads, 1) tcx_gemm_k(XArgs a, Epi epi) {
     R.sbase = (raw + 1023u) & ~1023u;
     const uint32_t gtbl = R.sbase + kXStages * kXStage, stbl = gtbl + kGridTbl;
     R.bars = stbl + kSignTbl;
-    const uint32_t acc_full = R.bars + 8u * (2 * kXStages), acc_empty = acc_full + 8u, drain = acc_full + 16u;
+    const uint32_t acc_full = R.bars + 8u * XRing::kBars, acc_empty = acc_full + 8u, drain = acc_full + 16u;
     const uint32_t tmem_slot = acc_full + 24u;
     unsigned char* tmem_slot_ptr = x_dyn + (tmem_slot - raw);
 
     if (Deq::kTables) {
-        // grid selectors: entry g, copy c (lanes c and c + 16): two words of four prmt selectors over {h8, h25, h43}
-        for (int i = tid; i < 256 * 16; i += kXThreads) {
-            const unsigned long long gr = iq2xxs_grid[i >> 4];
-            uint32_t w[2] = {0u, 0u};
+        // grid selectors: entry g, copy c at (g * 8 + c) * 16: for each pair p of elements (2p, 2p + 1) the prmt
+        // selector of their fp16 magnitudes out of {h8, h25, h43} (bytes 0-1, 2-3, 4-5)
+        for (int i = tid; i < 256 * 8; i += kXThreads) {
+            const unsigned long long gr = iq2xxs_grid[i >> 3];
+            uint32_t w[4];
 #pragma unroll
             for (int p = 0; p < 4; p++) {
                 const uint32_t m0 = (uint32_t)((gr >> (16 * p)) & 255), m1 = (uint32_t)((gr >> (16 * p + 8)) & 255);
                 const uint32_t a0 = m0 == 8 ? 0u : m0 == 25 ? 2u : 4u, a1 = m1 == 8 ? 0u : m1 == 25 ? 2u : 4u;
-                const uint32_t sel = a0 | (a0 + 1) << 4 | a1 << 8 | (a1 + 1) << 12;
-                w[p >> 1] |= sel << (16 * (p & 1));
+                w[p] = a0 | (a0 + 1) << 4 | a1 << 8 | (a1 + 1) << 12;
             }
-            asm volatile("st.shared.v2.u32 [%0], {%1,%2};" ::"r"(gtbl + (uint32_t)i * 8u), "r"(w[0]), "r"(w[1]) : "memory");
+            sts128(gtbl + (uint32_t)i * 16u, make_uint4(w[0], w[1], w[2], w[3]));
         }
-        // sign masks: sign index i, copy l: the 8 sign bits with element 2p at bit p and 2p + 1 at bit 16 + p
-        for (int i = tid; i < 128 * 32; i += kXThreads) {
-            const uint32_t s = ksigns_iq2xs[i >> 5];
-            uint32_t sp = 0;
+        // sign masks: sign index i, copy c: for each pair p the fp16x2 sign bits of elements 2p (bit 15), 2p + 1 (bit 31)
+        for (int i = tid; i < 128 * 8; i += kXThreads) {
+            const uint32_t s = ksigns_iq2xs[i >> 3];
+            uint32_t w[4];
 #pragma unroll
-            for (int p = 0; p < 4; p++) sp |= ((s >> (2 * p)) & 1u) << p | ((s >> (2 * p + 1)) & 1u) << (16 + p);
-            asm volatile("st.shared.u32 [%0], %1;" ::"r"(stbl + (uint32_t)i * 4u), "r"(sp) : "memory");
+            for (int p = 0; p < 4; p++) w[p] = ((s >> (2 * p)) & 1u) << 15 | ((s >> (2 * p + 1)) & 1u) << 31;
+            sts128(stbl + (uint32_t)i * 16u, make_uint4(w[0], w[1], w[2], w[3]));
         }
     }
     if (tid == 0) {
-        for (int s = 0; s < kXStages; s++) { tc_mbar_init(R.full(s), 1 + kDeqWarps); tc_mbar_init(R.empty(s), 1); }
+        for (int s = 0; s < kXStages; s++) { tc_mbar_init(R.full(s), 1 + kDeqWarps / 2); tc_mbar_init(R.empty(s), 1); }
         tc_mbar_init(acc_full, 1);
         tc_mbar_init(acc_empty, kXEpiWarps);
         tc_mbar_init(drain, 1);
@@ -373,17 +382,17 @@ __global__ void __launch_bounds__(kXThreads, 1) tcx_gemm_k(XArgs a, Epi epi) {
                 const int halves = t.w > kXM ? 2 : 1;
                 const uint8_t* a0 = a.a + (size_t)t.y * KK * kXRec;
                 for (int kk = 0; kk < KK; kk++, it++) {
-                    const int s = it % kXStages, use = it / kXStages;
-                    if (use > 0 && !tc_mbar_wait(R.empty(s), (uint32_t)((use - 1) & 1))) { healthy = false; break; }
-                    const uint32_t st = R.stage(s);
-                    tc_mbar_arrive_tx(R.full(s), (uint32_t)(halves * kXRec));
-                    tc_bulk_g2s(st, a0 + (size_t)kk * kXRec, (uint32_t)kXRec, R.full(s));
-                    if (halves == 2) tc_bulk_g2s(st + kXRec, a0 + ((size_t)KK + kk) * kXRec, (uint32_t)kXRec, R.full(s));
+                    const int use = it / kXStages;
+                    if (use > 0 && !tc_mbar_wait(R.empty(it), (uint32_t)((use - 1) & 1))) { healthy = false; break; }
+                    const uint32_t st = R.stage(it);
+                    tc_mbar_arrive_tx(R.full(it), (uint32_t)(halves * kXRec));
+                    tc_bulk_g2s(st, a0 + (size_t)kk * kXRec, (uint32_t)kXRec, R.full(it));
+                    if (halves == 2) tc_bulk_g2s(st + kXRec, a0 + ((size_t)KK + kk) * kXRec, (uint32_t)kXRec, R.full(it));
                 }
             }
             // the copies of the last uses of every stage have landed before the CTA may exit
             for (int i = it - kXStages > 0 ? it - kXStages : 0; i < it; i++)
-                if (!tc_mbar_wait(R.full(i % kXStages), (uint32_t)((i / kXStages) & 1))) healthy = false;
+                if (!tc_mbar_wait(R.full(i), (uint32_t)((i / kXStages) & 1))) healthy = false;
             if (!healthy) atomicOr(&g_tc_error, 1);
         }
         __syncwarp();
@@ -398,10 +407,9 @@ __global__ void __launch_bounds__(kXThreads, 1) tcx_gemm_k(XArgs a, Epi epi) {
                 if (tl > 0 && !tc_mbar_wait(acc_empty, (uint32_t)((tl - 1) & 1))) { healthy = false; break; }
                 tc_fence_after();
                 for (int kk = 0; kk < KK; kk++, it++) {
-                    const int s = it % kXStages;
-                    if (!tc_mbar_wait(R.full(s), (uint32_t)((it / kXStages) & 1))) { healthy = false; break; }
+                    if (!tc_mbar_wait(R.full(it), (uint32_t)((it / kXStages) & 1))) { healthy = false; break; }
                     tc_fence_after();
-                    const uint32_t st = R.stage(s), bt = st + 2 * kXRec;
+                    const uint32_t st = R.stage(it), bt = st + 2 * kXRec;
 #pragma unroll
                     for (int ki = 0; ki < 2; ki++)
                         umma_f16(tmem, umma_desc_sw64(st + ki * 32), umma_desc_sw64(bt + ki * 32), (kk | ki) ? 1u : 0u);
@@ -410,7 +418,7 @@ __global__ void __launch_bounds__(kXThreads, 1) tcx_gemm_k(XArgs a, Epi epi) {
                         for (int ki = 0; ki < 2; ki++)
                             umma_f16(tmem + 256u, umma_desc_sw64(st + kXRec + ki * 32), umma_desc_sw64(bt + ki * 32), (kk | ki) ? 1u : 0u);
                     }
-                    umma_commit(R.empty(s));
+                    umma_commit(R.empty(it));
                 }
                 if (healthy) umma_commit(acc_full);
             }
@@ -421,17 +429,18 @@ __global__ void __launch_bounds__(kXThreads, 1) tcx_gemm_k(XArgs a, Epi epi) {
         }
         __syncwarp();
     } else if (warp < 2 + kDeqWarps) {
-        // dequantisers: warp wd owns weight rows 32 wd .. 32 wd + 31 of every tile
-        const int wd = warp - 2;
+        // dequantisers: warp 2 + 8 phase + wd owns weight rows 32 wd .. 32 wd + 31 of the even (phase 0) or odd
+        // (phase 1) stages of every tile
+        const int wd = (warp - 2) & 7, phase = (warp - 2) >> 3;
         Deq dq;
         dq.gtbl = gtbl;
         dq.stbl = stbl;
-        int it = 0;
-        for (int L = blockIdx.x; L < total; L += gridDim.x) {
+        int it0 = 0;
+        for (int L = blockIdx.x; L < total; L += gridDim.x, it0 += KK) {
             const int4 t = x_tile(a, L / NT);
             const int n0 = (L % NT) * kXN + wd * 32;
             const uint8_t* wm = a.w + (size_t)t.x * a.wstride;
-            if (!dq.run(R, it, wm, a.K, n0 >> 5, n0 < a.N, wd, lane)) {
+            if (!dq.run(R, it0, wm, a.K, n0 >> 5, n0 < a.N, wd, phase, lane)) {
                 if (lane == 0) atomicOr(&g_tc_error, 1);
                 break;
             }
