@@ -35,6 +35,7 @@ METRIC = "IQ2_XXS MoE decode GB/s"
 T, H, F, E, TOPK = 16, 4096, 2048, 128, 6
 LAYERS, BATCHES = 4, 8
 EXPERT_BYTES = 2 * (F * (H // 256) * 66)      # up [F][H] + down [H][F]: 4,325,376 B
+GEMV_UP_TRAFFIC = 149706496 + 4285696          # DRAM bytes of one captured up-GEMV launch (ncu, config 2)
 
 
 def peaks():
@@ -603,7 +604,10 @@ def run_ours(args, rank, world, local_rank):
             "hbm_fraction": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "kernel": names[dom], "achieved": round(achieved, 1) if achieved else None,
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None,
-                         "traffic": None, "peak_kind": peak_kind,
+                         "traffic": GEMV_UP_TRAFFIC if dom == 1 else None,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one up launch at this "
+                                           "config (profiles/iq2_gemv_config2_ncu.md)",
+                         "algorithmic_bytes": round(dom_bytes), "peak_kind": peak_kind,
                          "stage_ms": {n: round(float(v), 5) for n, v in zip(names, stage_ms)}},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": T * H * 2 + T * E * 2,
