@@ -2,8 +2,10 @@
 // kind::f16 (fp16 operands, fp32 accumulation in TMEM), the weights dequantised inside the kernel.
 //
 // C[m][n] = sum_k A[m][k] B[n][k]: A the activation rows (tokens, or the expert-sorted pairs of the MoE), B the weight
-// rows.  A CTA computes a 256 x 256 tile as two 128-row halves that share one B tile (two accumulators of 256 TMEM
-// columns), so every dequantised weight feeds 256 rows.  Per 32-k stage of a 5-stage shared-memory ring:
+// rows.  A CTA computes a tile of up to 256 rows x 256 weight rows as two MMAs per k-step, each with M = 128 weight
+// rows (one half of the dequantised weight tile) and N = the tile's rows (both 128-row activation records): two
+// accumulators of 256 TMEM columns whose TMEM lanes are weight rows, so every dequantised weight feeds 256 rows and
+// the epilogue's lanes hold 32 consecutive outputs of one row (each store a contiguous line).  Per 32-k stage of a 5-stage shared-memory ring:
 //   A        the two 128-row halves (8 KB each), bulk-copied (cp.async.bulk, no tensor map) from an fp16 rows image
 //            by one lane of warp 0;
 //   B        256 weight rows x 32 k in fp16, written by 16 dequantising warps in two sets of 8 that take alternate
@@ -12,7 +14,8 @@
 //            scaled magnitudes and a xor sets its signs, the selectors and masks read as 128-bit entries from
 //            replicated shared-memory tables (conflict-free).  Q8_0: a magic-number prmt makes the int8 exact in fp16
 //            and one hmul2 applies the scale;
-//   MMA      one lane of warp 1 issues the m128n256k16 MMAs of both halves and commits them to the stage's barrier;
+//   MMA      one lane of warp 1 issues the m128n256k16 (or n128 for tiles of at most 128 rows) MMAs of both weight
+//            halves and commits them to the stage's barrier;
 //   epilogue 8 warps drain the accumulators (tcgen05.ld), hand them back to the MMA warp, and write the outputs.
 // Tiles (up to 256 rows of one group x 256 weight rows) are handed out persistently, one CTA per SM.
 //
@@ -59,14 +62,15 @@ int tc_error_read(int clear) {
     return v;
 }
 
-// instruction descriptor, kind::f16: fp32 accumulator, fp16 A and B, both K-major, N = 256, M = 128
-constexpr uint32_t kIdescF16 = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(kXN >> 3) << 17) | ((uint32_t)(kXM >> 4) << 24);
+// instruction descriptors, kind::f16: fp32 accumulator, fp16 A and B, both K-major, M = 128, N = 256 or 128
+constexpr uint32_t kIdescF16N256 = (1u << 4) | (256u >> 3) << 17 | ((uint32_t)(kXM >> 4) << 24);
+constexpr uint32_t kIdescF16N128 = (1u << 4) | (128u >> 3) << 17 | ((uint32_t)(kXM >> 4) << 24);
 
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p; }"
-        ::"r"(tmem_d), "l"(a), "l"(b), "r"(kIdescF16), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+        ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
@@ -115,41 +119,39 @@ __device__ __forceinline__ int4 x_tile(const XArgs& a, int mt) {
     return make_int4(0, 2 * mt, m0, min(2 * kXM, a.T - m0));
 }
 
-// epilogues: v = 32 accumulator columns [col, col + 32) of row r (0..127) of half h of tile t
-struct EpiRows {             // fp32 y[orow][col]; orow = rowmap[row0[g] + m0 + 128 h + r] (or the dense row)
+// epilogues: v[j] = the accumulator of weight row n (the calling lane's) and token tok0 + j of tile t, j < 32; the 32
+// lanes of a warp hold 32 consecutive weight rows, so each token's store is one contiguous line.
+struct EpiRows {             // fp32 y[orow][n]; orow = rowmap[row0[g] + m0 + token] (or the dense row)
     float* y;
     int ldy;
     const int* row0;         // per-group first row in the row list (offsets), nullptr: 0
     const int* rowmap;       // nullptr: identity
-    __device__ void put(int4 t, int h, int r, int col, int N, const uint32_t (&v)[32]) const {
-        const int grow = (row0 ? row0[t.x] : 0) + t.z + h * kXM + r;
-        const int orow = rowmap ? rowmap[grow] : grow;
-        float* o = y + (size_t)orow * ldy + col;
-        if (col + 32 <= N && ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0)) {
+    __device__ void put(int4 t, int n, int tok0, int lane, const uint32_t (&v)[32]) const {
+        const int grow = (row0 ? row0[t.x] : 0) + t.z + tok0 + lane;
+        const int mine = tok0 + lane < t.w ? (rowmap ? rowmap[grow] : grow) : -1;
+        float* yn = y + n;
 #pragma unroll
-            for (int i = 0; i < 32; i += 4)
-                *reinterpret_cast<float4*>(o + i) =
-                    make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]), __uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
-        } else {
-#pragma unroll
-            for (int i = 0; i < 32; i++)
-                if (col + i < N) o[i] = __uint_as_float(v[i]);
+        for (int j = 0; j < 32; j++) {
+            const int orow = __shfl_sync(0xffffffffu, mine, j);
+            if (orow >= 0) yn[(size_t)orow * ldy] = __uint_as_float(v[j]);
         }
     }
 };
 struct EpiImg {              // fp16(relu(v)^2) into the next GEMM's rows image (its K = this GEMM's N)
     uint8_t* img;
-    __device__ void put(int4 t, int h, int r, int col, int N, const uint32_t (&v)[32]) const {
-        uint8_t* rec = img + ((size_t)(t.y + h) * (N / 32) + col / 32) * kXRec;
+    int N;
+    __device__ void put(int4 t, int n, int tok0, int lane, const uint32_t (&v)[32]) const {
+        const size_t kk = (size_t)(n >> 5), nkk = (size_t)(N >> 5);
+        const uint32_t within = (uint32_t)((lane & 7) * 2);
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-            uint32_t o[4];
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const float a0 = __uint_as_float(v[8 * c + 2 * j]), a1 = __uint_as_float(v[8 * c + 2 * j + 1]);
-                o[j] = h2u(__floats2half2_rn(a0 > 0.f ? a0 * a0 : 0.f, a1 > 0.f ? a1 * a1 : 0.f));
+        for (int j = 0; j < 32; j++) {
+            const int tok = tok0 + j;
+            if (tok < t.w) {
+                const int r = tok & (kXM - 1);
+                uint8_t* rec = img + ((size_t)(t.y + (tok >> 7)) * nkk + kk) * kXRec;
+                const float a0 = __uint_as_float(v[j]);
+                *reinterpret_cast<__half*>(rec + sw64_off(r, lane >> 3) + within) = __float2half_rn(a0 > 0.f ? a0 * a0 : 0.f);
             }
-            *reinterpret_cast<uint4*>(rec + sw64_off(r, c)) = make_uint4(o[0], o[1], o[2], o[3]);
         }
     }
 };
@@ -403,20 +405,23 @@ __global__ void __launch_bounds__(kXThreads, 1) tcx_gemm_k(XArgs a, Epi epi) {
             int it = 0, tl = 0;
             for (int L = blockIdx.x; L < total && healthy; L += gridDim.x, tl++) {
                 const int4 t = x_tile(a, L / NT);
-                const bool two = t.w > kXM;
+                const uint32_t idesc = t.w > kXM ? kIdescF16N256 : kIdescF16N128;   // tokens: the MMAs' N
+                const bool w2 = (L % NT) * kXN + kXM < a.N;                         // the second weight half exists
                 if (tl > 0 && !tc_mbar_wait(acc_empty, (uint32_t)((tl - 1) & 1))) { healthy = false; break; }
                 tc_fence_after();
                 for (int kk = 0; kk < KK; kk++, it++) {
                     if (!tc_mbar_wait(R.full(it), (uint32_t)((it / kXStages) & 1))) { healthy = false; break; }
                     tc_fence_after();
                     const uint32_t st = R.stage(it), bt = st + 2 * kXRec;
+                    // M = 128 weight rows (half h of the B tile), N = the tile's tokens (both A records, contiguous)
 #pragma unroll
                     for (int ki = 0; ki < 2; ki++)
-                        umma_f16(tmem, umma_desc_sw64(st + ki * 32), umma_desc_sw64(bt + ki * 32), (kk | ki) ? 1u : 0u);
-                    if (two) {
+                        umma_f16(tmem, umma_desc_sw64(bt + ki * 32), umma_desc_sw64(st + ki * 32), idesc, (kk | ki) ? 1u : 0u);
+                    if (w2) {
 #pragma unroll
                         for (int ki = 0; ki < 2; ki++)
-                            umma_f16(tmem + 256u, umma_desc_sw64(st + kXRec + ki * 32), umma_desc_sw64(bt + ki * 32), (kk | ki) ? 1u : 0u);
+                            umma_f16(tmem + 256u, umma_desc_sw64(bt + kXRec + ki * 32), umma_desc_sw64(st + ki * 32), idesc,
+                                     (kk | ki) ? 1u : 0u);
                     }
                     umma_commit(R.empty(it));
                 }
@@ -446,32 +451,31 @@ __global__ void __launch_bounds__(kXThreads, 1) tcx_gemm_k(XArgs a, Epi epi) {
             }
         }
     } else {
-        // epilogue: warp w reads TMEM lanes 32 (w % 4).. of accumulator h = (w - 10) / 4
+        // epilogue: warp w reads TMEM lanes 32 (w % 4).. (weight rows) of accumulator h = (w - 18) / 4, whose
+        // columns are the tile's tokens
         const int q = warp & 3, h = (warp - 2 - kDeqWarps) >> 2;
-        const int r = q * 32 + lane;
         int tl = 0;
         for (int L = blockIdx.x; L < total; L += gridDim.x, tl++) {
             const int4 t = x_tile(a, L / NT);
-            const int n0 = (L % NT) * kXN;
+            const int n = (L % NT) * kXN + h * kXM + q * 32 + lane;   // this lane's weight row
             if (!tc_mbar_wait(acc_full, (uint32_t)(tl & 1))) {
                 if (lane == 0) atomicOr(&g_tc_error, 1);
                 break;
             }
             tc_fence_after();
-            if (h == 0 || t.w > kXM) {
-                const bool row_ok = h * kXM + r < t.w;
+            if ((L % NT) * kXN + h * kXM < a.N) {
+                const int ncb = t.w > kXM ? 8 : 4;   // 32-token column blocks the MMAs wrote
 #pragma unroll 1
-                for (int cb = 0; cb < kXN / 32; cb++) {
+                for (int cb = 0; cb < ncb; cb++) {
                     uint32_t v[32];
                     tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 256 + cb * 32), v);
                     tmem_ld_wait();
-                    if (cb == kXN / 32 - 1) {
+                    if (cb == ncb - 1) {
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) tc_mbar_arrive(acc_empty);   // the accumulators may be overwritten now
                     }
-                    const int col = n0 + cb * 32;
-                    if (row_ok && col < a.N) epi.put(t, h, r, col, a.N, v);
+                    if (cb * 32 < t.w && n < a.N) epi.put(t, n, cb * 32, lane, v);
                 }
             } else {
                 tc_fence_before();
@@ -732,7 +736,7 @@ int b200q_moe_prompt(const void* up, const void* down, int E, int H, int F, cons
     a.tiles = tiles;
     a.ntiles = meta;
     a.max_mtiles = L.max_tiles;
-    e = launch_x<DeqIQ2>(a, EpiImg{actimg}, s);
+    e = launch_x<DeqIQ2>(a, EpiImg{actimg, F}, s);
     if (e != cudaSuccess) return status_from(e);
     if (act_rows) {
         th = (size_t)L.max_slots * kXM * (F / 8);
