@@ -10,9 +10,9 @@
 //
 // Mapping: a lane owns one weight row and walks K in order, so every output is the reference's own chunk-ordered
 // sum, reproducible bit for bit by a scalar loop.  A warp owns 32 rows of one expert ("slot") and up to 4 of the
-// slot's tokens: a work unit.  CTAs are persistent (one of 12 warps per SM); every warp takes a contiguous range of
-// units weighted by their cost (weights streamed + tokens dotted), and neighbouring ranges go to different SMs, so a
-// slot with many tokens (the shared expert) is spread out instead of holding up the tail.
+// slot's tokens: a work unit.  CTAs are persistent (one of 16 warps per SM); warps take units from a global counter
+// as they go, the slots with the most tokens first, so the expensive units start early and every warp stays busy
+// until the last units are handed out.
 //
 // Streaming: the (32-row tile, 256-k super-block) pieces of the layout are contiguous 2112-byte units, so each warp
 // runs its own ring of kStages shared-memory stages filled by TMA bulk copies (cp.async.bulk, completion on an
@@ -32,6 +32,7 @@
 // the spare top bit selects the table's second, identical half of sign words.
 #include "iq2.cuh"
 
+#include <atomic>
 #include <cstring>
 
 namespace b200q {
@@ -144,17 +145,22 @@ constexpr int kMaxSlots = 520;
 // (table base, index byte, lane offset) with no add.  Below it: the ring barriers, the slot counts and prefix, and
 // the first stages; above it, the remaining stages.  The layout holds for a dynamic-memory base below 1 KB.
 constexpr uint32_t kTblAddr = 0x10000;
-constexpr uint32_t kHdrBytes = kGemvWarps * kStages * 8 + (2 * kMaxSlots + 1) * 4 + 12;   // barriers, counts, prefix
+constexpr int kQueue = kStages + 1;         // a warp's queue of units grabbed ahead (its producer is <= kStages ahead)
+constexpr int kQEntry = 1 + 4;              // unit index, then its token ids
+// barriers, slot counts / order / unit prefix, the warps' unit queues
+constexpr uint32_t kHdrBytes = kGemvWarps * kStages * 8 + (3 * kMaxSlots + 1) * 4 + kGemvWarps * kQueue * kQEntry * 4 + 12;
 constexpr int kNumStages = kGemvWarps * kStages;
 constexpr uint32_t kMaxDynBase = 1024;
 constexpr int kStagesBelowMin = (int)((kTblAddr - kMaxDynBase - kHdrBytes - 16) / kStageBytes);
 constexpr size_t kGemvSmem = (size_t)kTblAddr * 2 + (size_t)(kNumStages - kStagesBelowMin) * kStageBytes;
-constexpr int kCostRows = 3;                // a unit costs kCostRows (its weights) + its token count
+constexpr int kUnitCtrs = 64;               // launch slots of the unit counters (launches in flight at once)
 constexpr unsigned long long kWaitNs = 2000000000ull;   // a ring stage not filled within 2 s: give up
 
 enum Epi { kStore = 0, kRelu2 = 1, kRelu2Q8 = 2, kDots = 3 };
 
 __device__ int g_iq2_error;   // bit 0: a ring wait timed out; bit 1: the shared-memory layout did not fit
+// per launch slot: the next unit to hand out, and the CTAs done (the last one resets both for the slot's next launch)
+__device__ int g_unit_ctr[kUnitCtrs][2];
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
     uint32_t d;
@@ -243,47 +249,28 @@ __device__ __forceinline__ void group_weights(uint32_t lane_c, uint32_t lane_s, 
     hi = prmt(0xF82B1908u, 0x0000D5E7u, sel >> 16);
 }
 
-// The walk over a warp's units: slot-major (slots with tokens only), then token batch b0 (kUnitTok tokens), then
-// 32-row group g; unit (s, b0, g) starts at cost start(s, b0) + g * (kCostRows + nt) and belongs to the warp whose
-// cost range [lo, hi) holds that start.
-struct Walk {
-    const int* cnt;
-    const int* pre;
-    int nslots, G;
-    long long lo, hi;
-    int s, b0, g, g1;
-    long long start;
-    bool ok;
-
-    __device__ void begin() {
-        s = 0;
-        while (s < nslots && pre[s + 1] <= lo) s++;
-        b0 = 0;
-        start = s < nslots ? pre[s] : 0;
-        enter();
-    }
-    __device__ void enter() {
-        for (;;) {
-            if (s >= nslots || pre[s] >= hi) { ok = false; return; }
-            const int c = cnt[s];
-            if (b0 >= c) { s++; b0 = 0; if (s < nslots) start = pre[s]; continue; }
-            const int cost = kCostRows + min(kUnitTok, c - b0);
-            long long g0 = lo > start ? (lo - start + cost - 1) / cost : 0;
-            long long e = hi > start ? (hi - start + cost - 1) / cost : 0;
-            if (e > G) e = G;
-            if (g0 < e) { g = (int)g0; g1 = (int)e; ok = true; return; }
-            start += (long long)G * cost;
-            b0 += kUnitTok;
-        }
-    }
-    __device__ void next() {
-        if (++g < g1) return;
-        start += (long long)G * (kCostRows + min(kUnitTok, cnt[s] - b0));
-        b0 += kUnitTok;
-        enter();
-    }
-    __device__ int nt() const { return min(kUnitTok, cnt[s] - b0); }
+// Units: (slot s, token batch b0 of kUnitTok tokens, 32-row group g).  Every CTA orders the slots by token count,
+// largest first, and numbers their units in that order (batch-major, then row group); warps take unit numbers from
+// a global counter as they go, so the expensive units go first and the tail is short and shared by all warps.
+struct Unit {
+    int s, b0, g, nt;
 };
+__device__ __forceinline__ Unit decode_unit(int u, const int* s_order, const int* s_upre, const int* s_cnt, int nslots,
+                                            int G) {
+    int lo = 0, hi = nslots;   // the last ordered slot whose first unit is <= u
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (s_upre[mid] <= u) lo = mid;
+        else hi = mid;
+    }
+    Unit w;
+    w.s = s_order[lo];
+    const int r = u - s_upre[lo], b = r / G;
+    w.b0 = b * kUnitTok;
+    w.g = r - b * G;
+    w.nt = min(kUnitTok, s_cnt[w.s] - w.b0);
+    return w;
+}
 
 struct Ring {
     uint32_t bar0, a0;       // the CTA's barriers; its first stage below the table
@@ -302,11 +289,11 @@ struct Toks {
     int arow[kUnitTok];
 };
 
-__device__ __forceinline__ void unit_tokens(const GemvArgs& a, const Walk& w, int nt, Toks& t) {
+__device__ __forceinline__ void unit_tokens(const GemvArgs& a, const Unit& w, Toks& t) {
     const int base = a.counts ? a.offsets[w.s] : 0;
 #pragma unroll
     for (int m = 0; m < kUnitTok; m++) {
-        const int mm = m < nt ? m : 0;
+        const int mm = m < w.nt ? m : 0;
         const int id = a.counts ? a.order[base + w.b0 + mm] : w.b0 + mm;
         t.id[m] = id;
         t.arow[m] = id < a.act_split ? id / a.act_div : id - a.act_split + a.act_base;
@@ -317,30 +304,57 @@ __device__ __forceinline__ const uint8_t* slot_weights(const GemvArgs& a, int s)
     return (a.counts == nullptr || s < a.nslot_routed) ? a.slab + (size_t)s * a.expert_bytes : a.extra_w;
 }
 
-// Lane 0: fill the next ring stage with the producer walk's next super-block (weights, tokens' rows and scales).
-__device__ void issue_next(const GemvArgs& a, Walk& pw, int& psb, Toks& pt, Ring& r, int nsb) {
-    if (!pw.ok) return;
-    const int nt = pw.nt();
-    if (psb == 0) unit_tokens(a, pw, nt, pt);
-    const uint8_t* src = slot_weights(a, pw.s) + ((size_t)pw.g * nsb + psb) * kIq2Unit;
-    const uint32_t st = r.stage(r.issued), bar = r.bar(r.issued);
-    const bool scales = a.xs != nullptr;
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the warp's reads of the stage come first
-    mbar_expect_tx(bar, (uint32_t)(kIq2Unit + nt * 256 + (scales ? nt * 32 : 0)));
-    bulk_g2s(st, src, kIq2Unit, bar);
-    for (int m = 0; m < nt; m++) {
-        bulk_g2s(st + kStageAct + m * 256, a.xq + (size_t)pt.arow[m] * a.k + psb * 256, 256, bar);
-        if (scales) bulk_g2s(st + kStageScl + m * 32, a.xs + (size_t)pt.arow[m] * (a.k >> 5) + psb * 8, 32, bar);
+// Lane 0's producer: takes units from the launch's counter, queues them for its warp (unit number and token ids), and
+// fills the warp's ring with their super-blocks (weights, the tokens' int8 rows and scales).
+struct Producer {
+    const int *s_order, *s_upre, *s_cnt;
+    int nslots, G, U, nsb, ctr;
+    int* queue;              // this warp's kQueue entries of kQEntry ints
+    Unit pu;
+    Toks pt;
+    int psb, pn;
+    bool ok;
+
+    __device__ __forceinline__ void grab(const GemvArgs& a) {
+        const int u = atomicAdd(&g_unit_ctr[ctr][0], 1);
+        int* e = queue + (pn % kQueue) * kQEntry;
+        pn++;
+        if (u >= U) { ok = false; e[0] = -1; return; }
+        pu = decode_unit(u, s_order, s_upre, s_cnt, nslots, G);
+        unit_tokens(a, pu, pt);
+        e[0] = u;
+#pragma unroll
+        for (int m = 0; m < kUnitTok; m++) e[1 + m] = pt.id[m];
+        psb = 0;
+        ok = true;
     }
-    r.issued++;
-    if (++psb == nsb) { psb = 0; pw.next(); }
-}
+    // the next super-block into the next ring stage
+    __device__ __forceinline__ void issue_next(const GemvArgs& a, Ring& r) {
+        if (!ok) return;
+        const int nt = pu.nt;
+        const uint8_t* src = slot_weights(a, pu.s) + ((size_t)pu.g * nsb + psb) * kIq2Unit;
+        const uint32_t st = r.stage(r.issued), bar = r.bar(r.issued);
+        const bool scales = a.xs != nullptr;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the warp's reads of the stage come first
+        mbar_expect_tx(bar, (uint32_t)(kIq2Unit + nt * 256 + (scales ? nt * 32 : 0)));
+        bulk_g2s(st, src, kIq2Unit, bar);
+#pragma unroll
+        for (int m = 0; m < kUnitTok; m++) {
+            if (m < nt) {
+                bulk_g2s(st + kStageAct + m * 256, a.xq + (size_t)pt.arow[m] * a.k + psb * 256, 256, bar);
+                if (scales) bulk_g2s(st + kStageScl + m * 32, a.xs + (size_t)pt.arow[m] * (a.k >> 5) + psb * 8, 32, bar);
+            }
+        }
+        r.issued++;
+        if (++psb == nsb) grab(a);
+    }
+};
 
 // One unit: its 32 rows (a lane each) over K in chunk order, NT token rows (nt <= NT real; nt == NT for NT <= 2).
 // Returns false when a ring wait timed out.
 template <int NT, int EPI>
-__device__ bool unit_rows(const GemvArgs& a, const Walk& w, const Toks& t, int nt, int lane, Ring& r, Walk& pw, int& psb,
-                          Toks& pt, int nsb) {
+__device__ __forceinline__ bool unit_rows(const GemvArgs& a, const Unit& w, const Toks& t, int nt, int lane, Ring& r, Producer& pr,
+                          int nsb) {
     const uint32_t lane_c = kTblAddr | ((uint32_t)lane * 4u), lane_s = lane_c | 128u;
     const int row = w.g * kIq2Tile + lane, nc = a.k >> 5;
     // exact int -> float without a conversion instruction: an integer i with |i| < 2^22 added to the bits of 1.5 * 2^23
@@ -397,7 +411,7 @@ __device__ bool unit_rows(const GemvArgs& a, const Walk& w, const Toks& t, int n
         }
         __syncwarp();   // every lane is done with the stage: lane 0 refills it
         r.consumed++;
-        if (lane == 0) issue_next(a, pw, psb, pt, r, nsb);
+        if (lane == 0) pr.issue_next(a, r);
         __syncwarp();
     }
     if constexpr (EPI != kDots) {
@@ -431,7 +445,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) iq2_gemv_k(GemvArgs a, int
     // the layout around the table at kTblAddr (see kTblAddr): barriers, counts, prefix, stages below; stages above
     const uint32_t base = (uint32_t)__cvta_generic_to_shared(dyn);
     int* s_cnt = reinterpret_cast<int*>(dyn + kNumStages * 8);
-    int* s_pre = s_cnt + kMaxSlots;
+    int* s_order = s_cnt + kMaxSlots;
+    int* s_upre = s_order + kMaxSlots;
+    int* s_queue = s_upre + kMaxSlots + 1;
     Ring r;
     r.bar0 = base;
     r.a0 = (base + kHdrBytes + 15u) & ~15u;
@@ -457,37 +473,55 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) iq2_gemv_k(GemvArgs a, int
         s_cnt[s] = cnt;
     }
     __syncthreads();
-    if (tid == 0) {   // exclusive prefix of slot costs (nslots <= 520: a serial loop is cheap)
-        long long acc = 0;
-        for (int s = 0; s < nslots; s++) {
-            s_pre[s] = (int)acc;
-            const int cnt = s_cnt[s];
-            const int nb = (cnt + kUnitTok - 1) / kUnitTok;
-            acc += (long long)G * (nb * kCostRows + cnt);
+    // the slots by token count, largest first (ties by index), and the exclusive prefix of their unit counts
+    for (int s = tid; s < nslots; s += blockDim.x) {
+        const int c = s_cnt[s];
+        int rank = 0;
+        for (int o = 0; o < nslots; o++) {
+            const int co = s_cnt[o];
+            rank += (co > c || (co == c && o < s)) ? 1 : 0;
         }
-        s_pre[nslots] = (int)acc;
+        s_order[rank] = s;
     }
     __syncthreads();
-    const long long total = s_pre[nslots];
-    const int nwarps = gridDim.x * kGemvWarps;
-    const int gw = warp * gridDim.x + blockIdx.x;   // neighbouring cost ranges go to different SMs
-    Walk w{s_cnt, s_pre, nslots, G, total * gw / nwarps, total * (gw + 1) / nwarps, 0, 0, 0, 0, 0, false};
-    w.begin();
-    Walk pw = w;       // lane 0's producer walk: the ring is refilled as soon as a stage is consumed
-    int psb = 0;
-    Toks pt{};
-    if (lane == 0)
-        for (int i = 0; i < kStages; i++) issue_next(a, pw, psb, pt, r, nsb);
-    __syncwarp();
+    if (tid == 0) {
+        int acc = 0;
+        for (int i = 0; i < nslots; i++) {
+            s_upre[i] = acc;
+            acc += G * ((s_cnt[s_order[i]] + kUnitTok - 1) / kUnitTok);
+        }
+        s_upre[nslots] = acc;
+    }
+    __syncthreads();
+    Producer pr;
+    pr.s_order = s_order;
+    pr.s_upre = s_upre;
+    pr.s_cnt = s_cnt;
+    pr.nslots = nslots;
+    pr.G = G;
+    pr.U = s_upre[nslots];
+    pr.nsb = nsb;
+    pr.ctr = a.ctr;
+    pr.queue = s_queue + warp * kQueue * kQEntry;
+    pr.pn = 0;
+    pr.ok = false;
+    if (lane == 0) {
+        pr.grab(a);
+        for (int i = 0; i < kStages; i++) pr.issue_next(a, r);
+    }
     bool healthy = true;
-    while (w.ok && healthy) {
-        const int nt = w.nt();
+    for (int cn = 0; healthy; cn++) {
+        __syncwarp();   // lane 0's queue writes are visible to the warp
+        const int* e = pr.queue + (cn % kQueue) * kQEntry;
+        const int u = e[0];
+        if (u < 0) break;
+        const Unit w = decode_unit(u, s_order, s_upre, s_cnt, nslots, G);
         Toks t;
-        unit_tokens(a, w, nt, t);
-        if (nt == 1) healthy = unit_rows<1, EPI>(a, w, t, nt, lane, r, pw, psb, pt, nsb);
-        else if (nt == 2) healthy = unit_rows<2, EPI>(a, w, t, nt, lane, r, pw, psb, pt, nsb);
-        else healthy = unit_rows<4, EPI>(a, w, t, nt, lane, r, pw, psb, pt, nsb);
-        w.next();
+#pragma unroll
+        for (int m = 0; m < kUnitTok; m++) t.id[m] = e[1 + m];
+        if (w.nt == 1) healthy = unit_rows<1, EPI>(a, w, t, w.nt, lane, r, pr, nsb);
+        else if (w.nt == 2) healthy = unit_rows<2, EPI>(a, w, t, w.nt, lane, r, pr, nsb);
+        else healthy = unit_rows<4, EPI>(a, w, t, w.nt, lane, r, pr, nsb);
     }
     if (!healthy) {
         // a stage never filled: flag it, and let this warp's copies in flight land before the CTA's memory goes away
@@ -496,6 +530,16 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) iq2_gemv_k(GemvArgs a, int
             for (int i = r.consumed; i < r.issued; i++) mbar_wait(r.bar(i), (uint32_t)((i / kStages) & 1), kWaitNs);
         }
         __syncwarp();
+    }
+    // the last CTA out resets this launch slot's counters for the slot's next launch
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(&g_unit_ctr[a.ctr][1], 1) == (int)gridDim.x - 1) {
+            g_unit_ctr[a.ctr][0] = 0;
+            g_unit_ctr[a.ctr][1] = 0;
+            __threadfence();
+        }
     }
     pdl_trigger();
 }
@@ -524,8 +568,13 @@ static cudaError_t launch_gemv_e(const GemvArgs& a, int nslots, cudaStream_t s) 
     return launch(iq2_gemv_k<EPI>, dim3(num_sms()), dim3(kGemvWarps * 32), kGemvSmem, s, a, nslots);
 }
 
-cudaError_t launch_iq2_gemv(const GemvArgs& a, int nslots, int /*maxcnt*/, int epi, cudaStream_t s) {
+cudaError_t launch_iq2_gemv(const GemvArgs& a0, int nslots, int /*maxcnt*/, int epi, cudaStream_t s) {
     if (nslots <= 0 || nslots > kMaxSlots) return cudaErrorInvalidValue;
+    // launches take the counter slots in turn: kUnitCtrs launches can be in flight (on any streams) before a slot is
+    // reused, and a slot is back to zero when its launch ends
+    static std::atomic<unsigned> next_slot{0};
+    GemvArgs a = a0;
+    a.ctr = (int)(next_slot.fetch_add(1u) % kUnitCtrs);
     switch (epi) {
         case kStore: return launch_gemv_e<kStore>(a, nslots, s);
         case kRelu2: return launch_gemv_e<kRelu2>(a, nslots, s);

@@ -27,6 +27,7 @@ struct GemvArgs {
     int8_t* aq;         // epi 2: relu^2 rows quantised, [ids][n] int8 and as [ids][n/32]
     float* as;
     int32_t* dots;      // epi 3: [ids][n][k/32] int32 chunk dots
+    int ctr;            // the launch slot of the unit counter (set by launch_iq2_gemv)
 };
 
 // epi: 0 store, 1 relu^2, 2 relu^2 + int8 per 32, 3 chunk dots.  maxcnt bounds a slot's ids (the staging size).
