@@ -48,14 +48,15 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi sampled every 200 ms in the background during the timed region."""
+    """nvidia-smi sampled every 50 ms in the background during the timed region (one query after it if the region was
+    shorter than that)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index):
-        self.gpu = gpu_index
+        self.gpu = gpu_index          # an int, or a comma-separated list of indices (one sampler for all the ranks)
         self.proc = None
         self.path = os.path.join("/tmp", f"b200q_clocks_{os.getpid()}.csv")
 
@@ -63,7 +64,7 @@ class Clocks:
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                          "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.f,
                                          stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -77,6 +78,11 @@ class Clocks:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
             self.f.close()
+            if os.path.exists(self.path) and os.path.getsize(self.path) == 0:
+                # a timed region shorter than the polling interval: one query right after it
+                with open(self.path, "w") as f:
+                    subprocess.run(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                    "--format=csv,noheader,nounits"], stdout=f, stderr=subprocess.DEVNULL, timeout=30)
 
     def summary(self):
         if self.proc is None or not os.path.exists(self.path):
@@ -200,7 +206,7 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
     own tokens.  decode: 16 tokens a rank, uniform placement, fixed-capacity exchange, shared expert on every rank;
     GB/s = the touched experts' bytes over all ranks (+ activations) / the slowest rank's step time.  prefill: 8192
     tokens a rank, Zipf(1.1) routing, LPT placement with the hottest experts split; TFLOPS over all ranks."""
-    from ep import ExpertParallelMoE, LocalExperts, Placement, SharedExpert, slice_slab
+    from ep import ExpertParallelMoE, GraphedStep, LocalExperts, Placement, SharedExpert, slice_slab
     dist = world > 1
     up_b, down_b = b200q.iq2_bytes(F, H), b200q.iq2_bytes(H, F)
 
@@ -233,9 +239,32 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
     xs = [x.to(device) for x in xs_h]
     ls = [l.to(device) for l in ls_h]
 
+    xin = torch.empty(T, H, dtype=torch.bfloat16, device=device)   # the step's tokens and logits (graph inputs)
+    lin = torch.empty(T, E, dtype=torch.bfloat16, device=device)
+
+    def eager_on(L, x, lg):
+        ridx, rw = b200q.k_route(lg, TOPK)
+        return layers[L](x, ridx, rw)
+
+    def eager_step(L, b):
+        return eager_on(L, xs[b], ls[b])
+
+    # the step as a CUDA graph per layer copy over fixed input buffers: no host read in the capacity exchange, so the
+    # whole step (router, packing, NCCL all-to-alls, expert kernels, combine) replays as one launch
+    graphs = []
+    if os.environ.get("B200Q_EP_GRAPH", "1") != "0":
+        xin.copy_(xs[0])
+        lin.copy_(ls[0])
+        graphs = [GraphedStep(lambda L=L: eager_on(L, xin, lin), world) for L in range(LAYERS)]
+    graphed = bool(graphs) and all(g.ok for g in graphs)
+
     def step(i):
-        ridx, rw = b200q.k_route(ls[i % BATCHES], TOPK)
-        return layers[i % LAYERS](xs[i % BATCHES], ridx, rw)
+        L, b = i % LAYERS, i % BATCHES
+        if graphed:
+            xin.copy_(xs[b])
+            lin.copy_(ls[b])
+            return graphs[L]()
+        return eager_step(L, b)
 
     # bytes of a step of batch b over all ranks: every rank's touched local experts + its shared expert + activations
     step_bytes_b, rank_hits = [], []
@@ -273,7 +302,7 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
         e.record()
     acc = np.zeros(3)
     nprof = min(steps, 50)
-    for i in range(nprof):
+    for i in range(nprof):   # eager, with events between the pieces
         moe = layers[(warmup + i) % LAYERS]
         moe.timing = evs[:4]
         inner = moe.expert_fn
@@ -284,7 +313,7 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
             evs[5].record()
             return y
         moe.expert_fn = timed
-        step(warmup + i)
+        eager_step((warmup + i) % LAYERS, (warmup + i) % BATCHES)
         moe.expert_fn, moe.timing = inner, None
         torch.cuda.synchronize()
         acc += [evs[0].elapsed_time(evs[1]), evs[2].elapsed_time(evs[3]), evs[4].elapsed_time(evs[5])]
@@ -293,17 +322,15 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
     xh = [x.pin_memory() for x in xs_h]
     lh = [l.pin_memory() for l in ls_h]
     oh = torch.empty(T, H, dtype=torch.float32).pin_memory()
-    xd = torch.empty(T, H, dtype=torch.bfloat16, device=device)
-    ld = torch.empty(T, E, dtype=torch.bfloat16, device=device)
     barrier()
     torch.cuda.synchronize()
     ev0.record()
     for i in range(steps):
         b = (warmup + i) % BATCHES
-        xd.copy_(xh[b], non_blocking=True)
-        ld.copy_(lh[b], non_blocking=True)
-        ridx, rw = b200q.k_route(ld, TOPK)
-        oh.copy_(layers[(warmup + i) % LAYERS](xd, ridx, rw), non_blocking=True)
+        xin.copy_(xh[b], non_blocking=True)
+        lin.copy_(lh[b], non_blocking=True)
+        L = (warmup + i) % LAYERS
+        oh.copy_(graphs[L]() if graphed else eager_on(L, xin, lin), non_blocking=True)
     ev1.record()
     torch.cuda.synchronize()
     barrier()
@@ -314,8 +341,12 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
                      "local_experts_ms": round(float(acc[2]), 5), "step_bytes_mean": float(np.mean(step_bytes_b)),
                      "rank_local_expert_bytes": float(np.mean(rank_hits)) * EXPERT_BYTES,
                      "e2e_gbs": round(nbytes / (e2e_ms * 1e-3) / 1e9, 2),
-                     "h2d_bytes_per_step": T * H * 2 + T * E * 2, "d2h_bytes_per_step": T * H * 4}
-    del layers
+                     "h2d_bytes_per_step": T * H * 2 + T * E * 2, "d2h_bytes_per_step": T * H * 4,
+                     "cuda_graph": graphed}
+    del graphs, layers
+    import gc
+    gc.collect()
+    torch.cuda.synchronize()
     torch.cuda.empty_cache()
 
     # ---- prefill -------------------------------------------------------------------------------------------
@@ -442,7 +473,8 @@ def run_ep(args, rank, world, local_rank):
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
-    clk = Clocks(local_rank)
+    # one nvidia-smi sampler (on local rank 0) for all the node's ranks: a poller per rank stalls the launches
+    clk = Clocks(",".join(str(i) for i in range(int(os.environ.get("LOCAL_WORLD_SIZE", world))))) if local_rank == 0 else None
     r = ep_bench(b200q, rank, world, device, args.steps, args.warmup, prefill=args.prefill, clk=clk)
     line = None
     if rank == 0:
@@ -467,7 +499,7 @@ def run_ep(args, rank, world, local_rank):
             "e2e": {"value": d["e2e_gbs"], "unit": "GB/s", "h2d_bytes_per_step": d["h2d_bytes_per_step"],
                     "d2h_bytes_per_step": d["d2h_bytes_per_step"]},
             "gpu_launches": 9 * args.steps,
-            "clocks": clk.summary(),
+            "clocks": clk.summary() if clk else None,
             "ep": r,
         }
         if "prefill" in r:

@@ -96,10 +96,14 @@ def _check(status, what):
         raise B200QError(status, what)
 
 
-def _dev(t, name):
+def _dev(t, name, rows=False):
+    """a CUDA tensor, contiguous (rows=True: each row contiguous, rows at any 16-byte-multiple stride)"""
     if not (isinstance(t, torch.Tensor) and t.is_cuda):
         raise B200QError(EINVAL, f"{name} must be a CUDA tensor")
-    if not t.is_contiguous():
+    if rows:
+        if t.dim() != 2 or t.stride(1) != 1 or (t.stride(0) * t.element_size()) % 16:
+            raise B200QError(EINVAL, f"{name} must be rows with contiguous elements and a 16-byte row stride")
+    elif not t.is_contiguous():
         raise B200QError(EINVAL, f"{name} must be contiguous")
     return t
 
@@ -146,12 +150,13 @@ def synth_iq2_host(seed, nblocks):
 # router, grouping, activation quantisation, combine
 # -------------------------------------------------------------------------------------------------------------
 def k_quant_rows(x, q=None, s=None):
-    """int8 per 32 (quant_rows_k): x [rows][k] fp32/bf16 -> q [rows][k] int8, s [rows][k/32] fp32."""
-    _dev(x, "x")
+    """int8 per 32 (quant_rows_k): x [rows][k] fp32/bf16 (rows may be strided) -> q [rows][k] int8, s [rows][k/32]."""
+    _dev(x, "x", rows=True)
     rows, k = x.shape
     q = torch.empty(rows, k, dtype=torch.int8, device=x.device) if q is None else q
     s = torch.empty(rows, k // 32, dtype=torch.float32, device=x.device) if s is None else s
-    _check(lib().b200q_quant_rows(_p(x), _dtype_code(x), k, _p(q), k, _p(s), k // 32, rows, k, _s()), "k_quant_rows")
+    _check(lib().b200q_quant_rows(_p(x), _dtype_code(x), x.stride(0), _p(q), k, _p(s), k // 32, rows, k, _s()),
+           "k_quant_rows")
     return q, s
 
 

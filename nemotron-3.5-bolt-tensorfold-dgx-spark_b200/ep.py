@@ -138,23 +138,24 @@ class ExpertParallelMoE:
         if self.layout == "capacity":
             cap = pairs
             slot = dest[order] * cap + pos                       # where each sorted pair sits in the send buffer
-            send = torch.empty(self.world * cap, H, dtype=self.send_dtype, device=x.device)
-            send_l = torch.full((self.world * cap,), self.n_local_max_peer(), dtype=torch.int64, device=x.device)
-            send.index_copy_(0, slot, xs.index_select(0, tok[order]))
+            # one exchange: each row is the token's H values, then 16 bytes whose first 8 hold the local expert index
+            pad = 16 // xs.element_size()
+            send = torch.empty(self.world * cap, H + pad, dtype=self.send_dtype, device=x.device)
+            send_l = _index_view(send, H)
+            send_l.fill_(self.n_local_max_peer())
+            send[:, :H].index_copy_(0, slot, xs.index_select(0, tok[order]))
             send_l.index_copy_(0, slot, lidx[order])
             recv = torch.empty_like(send)
-            recv_l = torch.empty_like(send_l)
             if ev:
                 ev[0].record()
             w1 = self._a2a(recv, send, async_op=True)
-            w2 = self._a2a(recv_l, send_l, async_op=True)
             shared = self.shared_fn(x) if self.shared_fn else None   # overlaps the dispatch
             w1.wait()
-            w2.wait()
             if ev:
                 ev[1].record()
+            recv_l = _index_view(recv, H)
             recv_l = torch.where(recv_l >= self.n_local, torch.full_like(recv_l, self.n_local), recv_l)
-            y = self.expert_fn(recv, recv_l, self.n_local).to(self.send_dtype)
+            y = self.expert_fn(recv[:, :H], recv_l, self.n_local).to(self.send_dtype)
             back = torch.empty_like(y)
             if ev:
                 ev[2].record()
@@ -194,6 +195,12 @@ class ExpertParallelMoE:
     def n_local_max_peer(self):
         """the discard index every receiver maps to its own n_local (any index >= its expert count)"""
         return max(len(l) for l in self.p.local)
+
+
+def _index_view(buf, H):
+    """the int64 stored in bytes 0..7 after the H values of every row of buf [R][H + pad], as an [R] view"""
+    n = 8 // buf.element_size()
+    return buf[:, H:H + n].view(torch.int64).view(-1)
 
 
 class _Done:
@@ -257,3 +264,42 @@ class SharedExpert:
         xq, xs = b200q.k_quant_rows(x)
         aq, as_ = b200q.moe_up_q8(self.up, 1, self.F, self.H, self.counts, self.offsets, self.order[:T], 1, xq, xs)
         return b200q.moe_down(self.down, 1, self.H, self.F, self.counts, self.offsets, self.order[:T], aq, as_)
+
+
+class GraphedStep:
+    """A decode step captured once as a CUDA graph and replayed.  With the capacity exchange the expert-parallel layer
+    reads nothing back to the host, so router, packing, the NCCL all-to-alls, the expert kernels and the combine
+    capture as one graph, which removes the per-launch host latency that dominates a 16-token step.  Every rank must
+    build the same GraphedSteps in the same order (the warm-up runs the collectives eagerly); `ok` is agreed across
+    the ranks before any replay, so either all ranks replay or all run eagerly.  Drop the object (and with it the
+    graph's NCCL work) before destroying the process group."""
+
+    def __init__(self, fn, world, group=None, warm=2):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize()
+        ok = 1
+        self.g, self.out = None, None
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                out = fn()
+            self.g, self.out = g, out
+        except Exception:   # a capture the runtime refuses: this rank falls back, and so do the others below
+            ok = 0
+        torch.cuda.synchronize()
+        if world > 1:
+            t = torch.tensor([ok], dtype=torch.int32, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
+            ok = int(t.item())
+        self.ok = bool(ok)
+        self.fn = fn
+        if self.ok:   # the first replay carries one-time setup (the captured collectives'); keep it out of any timing
+            self.g.replay()
+            torch.cuda.synchronize()
+
+    def __call__(self):
+        if self.ok:
+            self.g.replay()
+            return self.out
+        return self.fn()
