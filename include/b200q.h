@@ -201,7 +201,12 @@ size_t b200q_nv4_tc_bytes(int64_t n, int k);
 int b200q_nv4_tc_pack(const void* q, const void* sc, void* packed, int64_t n, int k, void* stream);
 size_t b200q_nv4_rows_bytes(int T, int k);
 int b200q_quant_nv4_rows(const void* x, int x_dtype, int ldx, int T, int k, void* rows, void* stream);
-int b200q_nv4_gemm(const void* w, int n, int k, float s2, const void* rows, int T, float* y, int ldy, void* stream);
+/* A launch with at most a quarter of the SMs' worth of 128 x 256 tiles cuts K into slices; their fp32 partial sums go to
+ * `workspace` (>= b200q_nv4_gemm_workspace_bytes, 0 when no split is needed) and are added in slice order.  A NULL
+ * or small workspace runs without the split. */
+size_t b200q_nv4_gemm_workspace_bytes(int n, int k, int T);
+int b200q_nv4_gemm(const void* w, int n, int k, float s2, const void* rows, int T, float* y, int ldy, void* workspace,
+                   size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------
  * One decode MoE layer, the sequence enqueue_block runs for a MoE block

@@ -74,7 +74,8 @@ def lib():
             "b200q_nv4_tc_pack": (i32, [vp, vp, vp, i64, i32, vp]),
             "b200q_nv4_rows_bytes": (sz, [i32, i32]),
             "b200q_quant_nv4_rows": (i32, [vp, i32, i32, i32, i32, vp, vp]),
-            "b200q_nv4_gemm": (i32, [vp, i32, i32, f32, vp, i32, vp, i32, vp]),
+            "b200q_nv4_gemm_workspace_bytes": (sz, [i32, i32, i32]),
+            "b200q_nv4_gemm": (i32, [vp, i32, i32, f32, vp, i32, vp, i32, vp, sz, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -335,7 +336,9 @@ def quant_nv4_rows(x, k=None, out=None):
 def mma_nv4_fp4(w_tc, s2, n, k, rows, T, y=None):
     """y [T][n] fp32 = s2 * (NVFP4 rows) . (NVFP4 weights) on the block-scaled fp4 tensor cores (mma_nv4_fp4)."""
     y = torch.empty(T, n, dtype=torch.float32, device=rows.device) if y is None else y
-    _check(lib().b200q_nv4_gemm(_p(w_tc), n, k, float(s2), _p(rows), T, _p(y), y.stride(0), _s()), "mma_nv4_fp4")
+    ws, wb = _WS.get(lib().b200q_nv4_gemm_workspace_bytes(n, k, T), rows.device)
+    _check(lib().b200q_nv4_gemm(_p(w_tc), n, k, float(s2), _p(rows), T, _p(y), y.stride(0), ws, wb, _s()),
+           "mma_nv4_fp4")
     return y
 
 

@@ -184,6 +184,8 @@ struct F4Args {
     float* y;
     int n, k, T, ldy;
     float s2;
+    int ksplit;              // K slices a tile's sum is cut into (1: none)
+    float* part;             // ksplit > 1: unscaled partial sums [ksplit][T][n]
 };
 
 __global__ void __launch_bounds__(kF4Threads, 1) nv4_gemm_k(F4Args a) {
@@ -199,7 +201,15 @@ __global__ void __launch_bounds__(kF4Threads, 1) nv4_gemm_k(F4Args a) {
     unsigned char* tmem_slot_ptr = f4_dyn + (tmem_slot - raw);
 
     const int MT = (a.T + kF4M - 1) / kF4M, NT = (a.n + kF4N - 1) / kF4N, KS = a.k / kF4K;
-    const int tiles = MT * NT;
+    const int tiles = MT * NT * a.ksplit;   // work items: (tile, K slice)
+    // item -> tile (m fastest within an n-tile), K slice; stage range [ks0, ks1)
+    auto item = [&](int i, int& mt, int& nt, int& ks0, int& ks1) {
+        const int t = i / a.ksplit, sl = i - t * a.ksplit;
+        nt = t / MT;
+        mt = t - nt * MT;
+        ks0 = sl * KS / a.ksplit;
+        ks1 = (sl + 1) * KS / a.ksplit;
+    };
 
     if (tid == 0) {
         for (int s = 0; s < kF4Stages; s++) { tc_mbar_init(full(s), 1); tc_mbar_init(empty(s), 1); }
@@ -224,10 +234,11 @@ __global__ void __launch_bounds__(kF4Threads, 1) nv4_gemm_k(F4Args a) {
             bool healthy = true;
             int it = 0;
             for (int tile = blockIdx.x; tile < tiles && healthy; tile += gridDim.x) {
-                const int nt = tile / MT, mt = tile % MT;
+                int mt, nt, ks0, ks1;
+                item(tile, mt, nt, ks0, ks1);
                 const uint8_t* ap = a.a + (size_t)mt * KS * kF4ARec;
                 const uint8_t* bp = a.w + (size_t)nt * KS * kF4BRec;
-                for (int ks = 0; ks < KS; ks++, it++) {
+                for (int ks = ks0; ks < ks1; ks++, it++) {
                     const int s = it % kF4Stages, use = it / kF4Stages;
                     if (use > 0 && !tc_mbar_wait(empty(s), (uint32_t)((use - 1) & 1))) { healthy = false; break; }
                     const uint32_t st = sbase + (uint32_t)(s * kF4Stage);
@@ -248,9 +259,11 @@ __global__ void __launch_bounds__(kF4Threads, 1) nv4_gemm_k(F4Args a) {
             bool healthy = true;
             int it = 0, tl = 0;
             for (int tile = blockIdx.x; tile < tiles && healthy; tile += gridDim.x, tl++) {
+                int mt, nt, ks0, ks1;
+                item(tile, mt, nt, ks0, ks1);
                 if (tl > 0 && !tc_mbar_wait(acc_empty, (uint32_t)((tl - 1) & 1))) { healthy = false; break; }
                 tc_fence_after();
-                for (int ks = 0; ks < KS; ks++, it++) {
+                for (int ks = ks0; ks < ks1; ks++, it++) {
                     const int s = it % kF4Stages;
                     if (!tc_mbar_wait(full(s), (uint32_t)((it / kF4Stages) & 1))) { healthy = false; break; }
                     tc_fence_after();
@@ -265,8 +278,8 @@ __global__ void __launch_bounds__(kF4Threads, 1) nv4_gemm_k(F4Args a) {
                     }
 #pragma unroll
                     for (int kb = 0; kb < 4; kb++)
-                        umma_f4(tmem, umma_desc_sw128(at + kb * 32), umma_desc_sw128(bt + kb * 32), (ks | kb) ? 1u : 0u,
-                                sfa + 4u * kb, sfb + 8u * kb);
+                        umma_f4(tmem, umma_desc_sw128(at + kb * 32), umma_desc_sw128(bt + kb * 32),
+                                (ks > ks0 || kb > 0) ? 1u : 0u, sfa + 4u * kb, sfb + 8u * kb);
                     umma_commit(empty(s));
                 }
                 if (healthy) umma_commit(acc_full);
@@ -280,10 +293,15 @@ __global__ void __launch_bounds__(kF4Threads, 1) nv4_gemm_k(F4Args a) {
     } else {
         // epilogue: warp w reads TMEM lanes 32 (w % 4).. (tile rows) and columns 128 ((w - 2) / 4)..
         const int q = warp & 3, half = (warp - 2) >> 2;
-        const bool vec = ((a.ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.y) & 15) == 0);
+        const bool split = a.ksplit > 1;
+        const int ld = split ? a.n : a.ldy;
+        const float sc = split ? 1.f : a.s2;
+        const bool vec = ((ld & 3) == 0) && ((reinterpret_cast<uintptr_t>(split ? a.part : a.y) & 15) == 0);
         int tl = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, tl++) {
-            const int nt = tile / MT, mt = tile % MT;
+            int mt, nt, ks0, ks1;
+            item(tile, mt, nt, ks0, ks1);
+            float* dst = split ? a.part + (size_t)(tile % a.ksplit) * a.T * a.n : a.y;
             if (!tc_mbar_wait(acc_full, (uint32_t)(tl & 1))) {
                 if (lane == 0) atomicOr(&g_nv4_error, 1);
                 break;
@@ -300,14 +318,14 @@ __global__ void __launch_bounds__(kF4Threads, 1) nv4_gemm_k(F4Args a) {
             const int row = mt * kF4M + q * 32 + lane;
             const int col0 = nt * kF4N + half * 128;
             if (row < a.T) {
-                float* yr = a.y + (size_t)row * a.ldy;
+                float* yr = dst + (size_t)row * ld;
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
 #pragma unroll
                     for (int e = 0; e < 32; e += 4) {
                         const int col = col0 + 32 * j + e;
-                        const float f0 = __uint_as_float(v[j][e]) * a.s2, f1 = __uint_as_float(v[j][e + 1]) * a.s2;
-                        const float f2 = __uint_as_float(v[j][e + 2]) * a.s2, f3 = __uint_as_float(v[j][e + 3]) * a.s2;
+                        const float f0 = __uint_as_float(v[j][e]) * sc, f1 = __uint_as_float(v[j][e + 1]) * sc;
+                        const float f2 = __uint_as_float(v[j][e + 2]) * sc, f3 = __uint_as_float(v[j][e + 3]) * sc;
                         if (vec && col + 4 <= a.n) {
                             *reinterpret_cast<float4*>(yr + col) = make_float4(f0, f1, f2, f3);
                         } else {
@@ -328,6 +346,31 @@ __global__ void __launch_bounds__(kF4Threads, 1) nv4_gemm_k(F4Args a) {
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kF4TmemCols));
     }
     pdl_trigger();
+}
+
+// y[t][c] = s2 * (part[0][t][c] + part[1][t][c] + ...), the slices added in order
+__global__ void f4_splitk_sum_k(const float* __restrict__ part, int ksplit, int T, int n, float s2, float* __restrict__ y,
+                                int ldy) {
+    pdl_wait();
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < (size_t)T * n) {
+        const int t = (int)(i / n), c = (int)(i % n);
+        float acc = part[i];
+        for (int sl = 1; sl < ksplit; sl++) acc += part[(size_t)sl * T * n + i];
+        y[(size_t)t * ldy + c] = acc * s2;
+    }
+    pdl_trigger();
+}
+
+// K slices for a launch with at most a quarter of the SMs' worth of tiles (up to 4, at least 2 stages a slice).  A
+// CTA's ring is bound by the latency of its bulk copies, so slicing pays only when most SMs would otherwise idle (out_proj
+// at M = 512, 64 tiles on 148 SMs, measured slower sliced in two).
+static int f4_ksplit(int tiles, int KS, int sms) {
+    if (tiles * 4 > sms) return 1;
+    int s = sms / tiles;
+    if (s > 4) s = 4;
+    if (s > KS / 2) s = KS / 2;
+    return s < 2 ? 1 : s;
 }
 
 static int f4_num_sms() {
@@ -379,7 +422,15 @@ int b200q_quant_nv4_rows(const void* x, int x_dtype, int ldx, int T, int k, void
                               x, x_dtype, ldx, T, k, Mp, (uint8_t*)rows));
 }
 
-int b200q_nv4_gemm(const void* w, int n, int k, float s2, const void* rows, int T, float* y, int ldy, void* stream) {
+size_t b200q_nv4_gemm_workspace_bytes(int n, int k, int T) {
+    if (n <= 0 || T <= 0 || k <= 0 || k % kF4K) return 0;
+    const int tiles = ((T + kF4M - 1) / kF4M) * ((n + kF4N - 1) / kF4N);
+    const int ks = f4_ksplit(tiles, k / kF4K, f4_num_sms());
+    return ks > 1 ? (size_t)ks * T * n * sizeof(float) : 0;
+}
+
+int b200q_nv4_gemm(const void* w, int n, int k, float s2, const void* rows, int T, float* y, int ldy, void* workspace,
+                   size_t workspace_bytes, void* stream) {
     if (!w || !rows || !y || n <= 0 || T <= 0 || k <= 0 || k % kF4K || ldy < n || !a16(w) || !a16(rows)) return B200Q_EINVAL;
     static bool opted = false;
     if (!opted) {
@@ -388,9 +439,16 @@ int b200q_nv4_gemm(const void* w, int n, int k, float s2, const void* rows, int 
         opted = true;
     }
     const int tiles = ((T + kF4M - 1) / kF4M) * ((n + kF4N - 1) / kF4N);
-    const int grid = tiles < f4_num_sms() ? tiles : f4_num_sms();
-    F4Args a{(const uint8_t*)w, (const uint8_t*)rows, y, n, k, T, ldy, s2};
-    return status_from(launch(nv4_gemm_k, dim3(grid), dim3(kF4Threads), kF4Smem, (cudaStream_t)stream, a));
+    int ks = f4_ksplit(tiles, k / kF4K, f4_num_sms());
+    if (!workspace || workspace_bytes < (size_t)ks * T * n * sizeof(float) || !a16(workspace)) ks = 1;
+    const int items = tiles * ks;
+    const int grid = items < f4_num_sms() ? items : f4_num_sms();
+    F4Args a{(const uint8_t*)w, (const uint8_t*)rows, y, n, k, T, ldy, s2, ks, (float*)workspace};
+    cudaError_t e = launch(nv4_gemm_k, dim3(grid), dim3(kF4Threads), kF4Smem, (cudaStream_t)stream, a);
+    if (e != cudaSuccess || ks == 1) return status_from(e);
+    const size_t th = (size_t)T * n;
+    return status_from(launch(f4_splitk_sum_k, dim3((unsigned)((th + 255) / 256)), dim3(256), 0, (cudaStream_t)stream,
+                              (const float*)workspace, ks, T, n, s2, y, ldy));
 }
 
 }  // extern "C"

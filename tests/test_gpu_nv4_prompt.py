@@ -126,3 +126,24 @@ def test_nv4_prompt_gemm_ldy_and_repeat():
     assert torch.all(big[:, n:] == 7.0)
     q4, sf = O.quant_nv4_rows(x, k)
     assert rel_l2(big[:, :n].cpu().numpy(), O.nv4_gemm_q4(q, sc, 1.0, n, k, q4, sf)) < 1e-5
+
+
+def test_nv4_prompt_gemm_split_k():
+    """a launch with few tiles cuts K into slices (partials in the workspace, added in slice order): the same sums as
+    the oracle's, and as the unsplit launch up to fp32 reassociation"""
+    T, n, k = 130, 512, 2048   # 2 x 2 tiles: 4 slices of K
+    q, sc = nv4_weights(11, n, k)
+    x = np.random.default_rng(12).standard_normal((T, k)).astype(np.float32)
+    w = b200q.tile_nv4w(dev(q), dev(sc), n, k)
+    rows = b200q.quant_nv4_rows(dev(x))
+    assert b200q.lib().b200q_nv4_gemm_workspace_bytes(n, k, T) == 4 * T * n * 4
+    y = b200q.mma_nv4_fp4(w, 0.5, n, k, rows, T)
+    y1 = torch.empty_like(y)
+    st = b200q.lib().b200q_nv4_gemm(b200q._p(w), n, k, 0.5, b200q._p(rows), T, b200q._p(y1), n, None, 0, b200q._s())
+    assert st == 0
+    y, y1 = y.cpu().numpy(), y1.cpu().numpy()
+    assert b200q.device_error() == 0
+    q4, sf = O.quant_nv4_rows(x, k)
+    ref = O.nv4_gemm_q4(q, sc, 0.5, n, k, q4, sf)
+    assert rel_l2(y, ref) < 1e-5 and rel_l2(y1, ref) < 1e-5
+    assert rel_l2(y, y1) < 1e-6
