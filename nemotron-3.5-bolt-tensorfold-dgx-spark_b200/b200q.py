@@ -13,7 +13,8 @@ import os
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libb200q.so")
+# the library: B200Q_LIB if set (like libbolt's TENSORFOLD_BOLT_LIB lookup, bolt_api.zig:128-140), else the in-place build
+LIB_PATH = os.environ.get("B200Q_LIB") or os.path.join(HERE, "libb200q.so")
 
 OK, EINVAL, ENOSPACE, ECUDA = 0, -1, -2, -3
 F32, BF16 = 0, 1

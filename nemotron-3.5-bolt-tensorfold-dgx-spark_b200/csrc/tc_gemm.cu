@@ -16,7 +16,8 @@
 //            and one hmul2 applies the scale;
 //   MMA      one lane of warp 1 issues the m128n256k16 (or n128 for tiles of at most 128 rows) MMAs of both weight
 //            halves and commits them to the stage's barrier;
-//   epilogue 8 warps drain the accumulators (tcgen05.ld), hand them back to the MMA warp, and write the outputs.
+//   epilogue 8 warps drain the accumulators (tcgen05.ld: warp w reads lane quarter w % 4 of one accumulator), hand
+//            them back to the MMA warp, and write the outputs.
 // Tiles (up to 256 rows of one group x 256 weight rows) are handed out persistently, one CTA per SM.
 //
 // Shared-memory tiles are K-major with the 64-byte swizzle of the UMMA descriptors: rows of 64 B (32 fp16), 8-row
@@ -43,7 +44,9 @@ constexpr int kXRec = kXM * 64;                 // 8 KB: a rows-image record (12
 constexpr int kXB = kXN * 64;                   // 16 KB: the B tile of a stage
 constexpr int kXStage = 2 * kXRec + kXB;        // 32 KB: the two A halves, then the B tile
 constexpr int kXStages = 5;
-constexpr int kDeqWarps = 16, kXEpiWarps = 8;  // dequantisers: two sets of 8 taking alternate stages
+constexpr int kDeqWarps = 16, kXEpiWarps = 8;  // dequantisers (8 a stage: kDeqWarps / 8 sets taking stages in turn)
+constexpr int kPhases = kDeqWarps / 8;
+constexpr int kEpiParts = kXEpiWarps / 8;       // epilogue warps an (accumulator, lane quarter), splitting the tokens
 constexpr int kXThreads = (2 + kDeqWarps + kXEpiWarps) * 32;   // 832
 constexpr int kGridTbl = 256 * 8 * 16;          // 32 KB: grid entry -> four prmt selectors, 8 copies
 constexpr int kSignTbl = 128 * 8 * 16;          // 16 KB: sign index -> four xor masks, 8 copies
@@ -182,6 +185,15 @@ __device__ __forceinline__ void x_stage_done(const XRing& R, int it, int lane) {
     if (lane == 0) tc_mbar_arrive(R.full(it));
 }
 
+// a lane's 16 bytes of a chunk pair (one phase: both chunks; two phases: only its own 8 bytes, in .x and .y)
+__device__ __forceinline__ uint4 ld_pair(const uint8_t* p) {
+    if (kPhases == 2) {
+        const uint2 v = ldg_nc64(p);
+        return make_uint4(v.x, v.y, 0u, 0u);
+    }
+    return ldg_nc(p);
+}
+
 struct DeqIQ2 {              // IQ2_XXS rt32 layout (common.cuh); sign words re-encoded by the packer
     static constexpr bool kTables = true;
     uint32_t gtbl, stbl;     // shared-memory tables (set in the kernel)
@@ -212,34 +224,40 @@ struct DeqIQ2 {              // IQ2_XXS rt32 layout (common.cuh); sign words re-
     __device__ bool run(const XRing& R, int it0, const uint8_t* wm, int K, int rt, bool valid, int wd, int phase,
                         int lane) const {
         const int nb = K >> 8;
-        const uint8_t* base = wm + (size_t)rt * nb * kIq2Unit + lane * 16 + phase * 8;
-        uint2 c[4], n[4];   // this lane's chunks 2j + phase of the current / next super-block
+        const uint8_t* base = wm + (size_t)rt * nb * kIq2Unit + lane * 16 + (kPhases == 2 ? phase * 8 : 0);
+        // this lane's chunk pairs j of the current / next super-block (with two phases only chunk 2j + phase)
+        uint4 c[4], n[4];
         uint32_t dc = 0, dn = 0;
         if (valid) {
 #pragma unroll
-            for (int j = 0; j < 4; j++) c[j] = ldg_nc64(base + j * 512);
+            for (int j = 0; j < 4; j++) c[j] = ld_pair(base + j * 512);
             dc = ldg_u16(wm + (size_t)rt * nb * kIq2Unit + 2048 + lane * 2);
         }
         for (int sb = 0; sb < nb; sb++) {
             if (valid && sb + 1 < nb) {
                 const uint8_t* u = base + (size_t)(sb + 1) * kIq2Unit;
 #pragma unroll
-                for (int j = 0; j < 4; j++) n[j] = ldg_nc64(u + j * 512);
+                for (int j = 0; j < 4; j++) n[j] = ld_pair(u + j * 512);
                 dn = ldg_u16(wm + ((size_t)rt * nb + sb + 1) * kIq2Unit + 2048 + lane * 2);
             }
             const float d = __half2float(__ushort_as_half((unsigned short)dc));
 #pragma unroll
             for (int j = 0; j < 4; j++) {
-                const int it = it0 + sb * 8 + 2 * j + phase;
-                if (!x_wait_free(R, it, lane)) return false;
-                const uint32_t row_addr = R.stage(it) + 2 * kXRec + (uint32_t)((wd * 32 + lane) * 64);
-                if (valid) {
-                    chunk(c[j].x, c[j].y, d, row_addr, lane);
-                } else {
 #pragma unroll
-                    for (int g = 0; g < 4; g++) sts128(row_addr + g * 16, make_uint4(0, 0, 0, 0));
+                for (int hh = 0; hh < 2 / kPhases; hh++) {
+                    const int ch = kPhases == 2 ? 2 * j + phase : 2 * j + hh;
+                    const int it = it0 + sb * 8 + ch;
+                    if (!x_wait_free(R, it, lane)) return false;
+                    const uint32_t row_addr = R.stage(it) + 2 * kXRec + (uint32_t)((wd * 32 + lane) * 64);
+                    if (valid) {
+                        if (hh == 0) chunk(c[j].x, c[j].y, d, row_addr, lane);
+                        else chunk(c[j].z, c[j].w, d, row_addr, lane);
+                    } else {
+#pragma unroll
+                        for (int g = 0; g < 4; g++) sts128(row_addr + g * 16, make_uint4(0, 0, 0, 0));
+                    }
+                    x_stage_done(R, it, lane);
                 }
-                x_stage_done(R, it, lane);
             }
 #pragma unroll
             for (int j = 0; j < 4; j++) c[j] = n[j];
@@ -277,18 +295,18 @@ struct DeqQ8 {
         if (valid) {
 #pragma unroll
             for (int u = 0; u < 3; u++) {
-                const uint8_t* p = base + (size_t)(2 * u + phase) * kQ8Unit;
+                const uint8_t* p = base + (size_t)(kPhases * u + phase) * kQ8Unit;
                 qa[u] = ldg_nc(p + lane * 32);
                 qb[u] = ldg_nc(p + lane * 32 + 16);
                 dd[u] = ldg_u16(p + 1024 + lane * 2);
             }
         }
-        for (int m0 = 0; m0 < nk / 2; m0 += 4) {
+        for (int m0 = 0; m0 < nk / kPhases; m0 += 4) {
 #pragma unroll
             for (int u = 0; u < 4; u++) {
-                const int m = m0 + u, kb = 2 * m + phase, nx = m + 3;
-                if (valid && nx < nk / 2) {   // prefetch this warp's block m + 3 into its ring slot
-                    const uint8_t* p = base + (size_t)(2 * nx + phase) * kQ8Unit;
+                const int m = m0 + u, kb = kPhases * m + phase, nx = m + 3;
+                if (valid && nx < nk / kPhases) {   // prefetch this warp's block m + 3 into its ring slot
+                    const uint8_t* p = base + (size_t)(kPhases * nx + phase) * kQ8Unit;
                     qa[(u + 3) & 3] = ldg_nc(p + lane * 32);
                     qb[(u + 3) & 3] = ldg_nc(p + lane * 32 + 16);
                     dd[(u + 3) & 3] = ldg_u16(p + 1024 + lane * 2);
@@ -354,7 +372,7 @@ __global__ void __launch_bounds__(kXThreads, 1) tcx_gemm_k(XArgs a, Epi epi) {
         }
     }
     if (tid == 0) {
-        for (int s = 0; s < kXStages; s++) { tc_mbar_init(R.full(s), 1 + kDeqWarps / 2); tc_mbar_init(R.empty(s), 1); }
+        for (int s = 0; s < kXStages; s++) { tc_mbar_init(R.full(s), 1 + kDeqWarps / kPhases); tc_mbar_init(R.empty(s), 1); }
         tc_mbar_init(acc_full, 1);
         tc_mbar_init(acc_empty, kXEpiWarps);
         tc_mbar_init(drain, 1);
@@ -436,7 +454,7 @@ __global__ void __launch_bounds__(kXThreads, 1) tcx_gemm_k(XArgs a, Epi epi) {
     } else if (warp < 2 + kDeqWarps) {
         // dequantisers: warp 2 + 8 phase + wd owns weight rows 32 wd .. 32 wd + 31 of the even (phase 0) or odd
         // (phase 1) stages of every tile
-        const int wd = (warp - 2) & 7, phase = (warp - 2) >> 3;
+        const int wd = (warp - 2) & 7, phase = (warp - 2) >> 3;   // phase 0 with one set
         Deq dq;
         dq.gtbl = gtbl;
         dq.stbl = stbl;
@@ -451,9 +469,9 @@ __global__ void __launch_bounds__(kXThreads, 1) tcx_gemm_k(XArgs a, Epi epi) {
             }
         }
     } else {
-        // epilogue: warp w reads TMEM lanes 32 (w % 4).. (weight rows) of accumulator h = (w - 18) / 4, whose
-        // columns are the tile's tokens
-        const int q = warp & 3, h = (warp - 2 - kDeqWarps) >> 2;
+        // epilogue: warp w reads TMEM lanes 32 (w % 4).. (weight rows) of accumulator h, whose columns are the tile's
+        // tokens; kEpiParts warps share an (h, lane quarter), each a contiguous part of the token blocks
+        const int e = warp - 2 - kDeqWarps, q = warp & 3, h = (e >> 2) & 1, cpart = e >> 3;
         int tl = 0;
         for (int L = blockIdx.x; L < total; L += gridDim.x, tl++) {
             const int4 t = x_tile(a, L / NT);
@@ -463,10 +481,13 @@ __global__ void __launch_bounds__(kXThreads, 1) tcx_gemm_k(XArgs a, Epi epi) {
                 break;
             }
             tc_fence_after();
-            if ((L % NT) * kXN + h * kXM < a.N) {
-                const int ncb = t.w > kXM ? 8 : 4;   // 32-token column blocks the MMAs wrote
+            // this warp's 32-token column blocks [cb0, cb1) of the tile's 8 (4 for a tile of at most 128 tokens)
+            const int nblk = t.w > kXM ? 8 : 4;
+            const int cb0 = min(cpart * (8 / kEpiParts), nblk), cb1 = min(cb0 + 8 / kEpiParts, nblk);
+            if ((L % NT) * kXN + h * kXM < a.N && cb0 < cb1) {
+                const int ncb = cb1;
 #pragma unroll 1
-                for (int cb = 0; cb < ncb; cb++) {
+                for (int cb = cb0; cb < ncb; cb++) {
                     uint32_t v[32];
                     tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 256 + cb * 32), v);
                     tmem_ld_wait();
