@@ -122,9 +122,13 @@ __device__ __forceinline__ int4 x_tile(const XArgs& a, int mt) {
     return make_int4(0, 2 * mt, m0, min(2 * kXM, a.T - m0));
 }
 
-// epilogues: v[j] = the accumulator of weight row n (the calling lane's) and token tok0 + j of tile t, j < 32; the 32
-// lanes of a warp hold 32 consecutive weight rows, so each token's store is one contiguous line.
+// Epilogues.  kTokensM picks the MMA's orientation, and so which index a TMEM lane carries:
+//   false: weights are M, tokens N.  put(t, n, tok0, lane, v): v[j] = (weight row n, the lane's; token tok0 + j); the
+//          32 lanes hold 32 consecutive weight rows, so a token's store is one contiguous line, one element a lane.
+//   true:  tokens are M, weights N.  put(t, h, r, col, N, v): v[j] = (token 128 h + r, the lane's; weight row col + j);
+//          a lane holds 32 consecutive outputs of one row and stores them 16 bytes at a time.
 struct EpiRows {             // fp32 y[orow][n]; orow = rowmap[row0[g] + m0 + token] (or the dense row)
+    static constexpr bool kTokensM = false;
     float* y;
     int ldy;
     const int* row0;         // per-group first row in the row list (offsets), nullptr: 0
@@ -140,7 +144,49 @@ struct EpiRows {             // fp32 y[orow][n]; orow = rowmap[row0[g] + m0 + to
         }
     }
 };
-struct EpiImg {              // fp16(relu(v)^2) into the next GEMM's rows image (its K = this GEMM's N)
+struct EpiRowsT {            // EpiRows with tokens as M: a lane's 32 outputs of its row as eight 16-byte stores
+    static constexpr bool kTokensM = true;
+    float* y;
+    int ldy;
+    const int* row0;
+    const int* rowmap;
+    __device__ void put(int4 t, int h, int r, int col, int N, const uint32_t (&v)[32]) const {
+        const int grow = (row0 ? row0[t.x] : 0) + t.z + h * kXM + r;
+        const int orow = rowmap ? rowmap[grow] : grow;
+        float* o = y + (size_t)orow * ldy + col;
+        if (col + 32 <= N && ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0)) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+                *reinterpret_cast<float4*>(o + i) =
+                    make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]), __uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; i++)
+                if (col + i < N) o[i] = __uint_as_float(v[i]);
+        }
+    }
+};
+struct EpiImg {              // fp16(relu(v)^2) into the next GEMM's rows image (its K = this GEMM's N), tokens as M:
+    // a lane's 32 outputs are one 64-byte row of a record, and a warp's 32 lanes write 2 KB of it contiguously
+    static constexpr bool kTokensM = true;
+    uint8_t* img;
+    int N;
+    __device__ void put(int4 t, int h, int r, int col, int N_, const uint32_t (&v)[32]) const {
+        uint8_t* rec = img + ((size_t)(t.y + h) * (N / 32) + col / 32) * kXRec;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const float a0 = __uint_as_float(v[8 * c + 2 * j]), a1 = __uint_as_float(v[8 * c + 2 * j + 1]);
+                o[j] = h2u(__floats2half2_rn(a0 > 0.f ? a0 * a0 : 0.f, a1 > 0.f ? a1 * a1 : 0.f));
+            }
+            *reinterpret_cast<uint4*>(rec + sw64_off(r, c)) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    }
+};
+struct EpiImgW {             // EpiImg with weights as M (one fp16 a lane per token row)
+    static constexpr bool kTokensM = false;
     uint8_t* img;
     int N;
     __device__ void put(int4 t, int n, int tok0, int lane, const uint32_t (&v)[32]) const {
@@ -431,15 +477,29 @@ __global__ void __launch_bounds__(kXThreads, 1) tcx_gemm_k(XArgs a, Epi epi) {
                     if (!tc_mbar_wait(R.full(it), (uint32_t)((it / kXStages) & 1))) { healthy = false; break; }
                     tc_fence_after();
                     const uint32_t st = R.stage(it), bt = st + 2 * kXRec;
-                    // M = 128 weight rows (half h of the B tile), N = the tile's tokens (both A records, contiguous)
-#pragma unroll
-                    for (int ki = 0; ki < 2; ki++)
-                        umma_f16(tmem, umma_desc_sw64(bt + ki * 32), umma_desc_sw64(st + ki * 32), idesc, (kk | ki) ? 1u : 0u);
-                    if (w2) {
+                    if constexpr (Epi::kTokensM) {
+                        // M = 128 tokens (A record h), N = the 256 weight rows of the B tile
 #pragma unroll
                         for (int ki = 0; ki < 2; ki++)
-                            umma_f16(tmem + 256u, umma_desc_sw64(bt + kXRec + ki * 32), umma_desc_sw64(st + ki * 32), idesc,
+                            umma_f16(tmem, umma_desc_sw64(st + ki * 32), umma_desc_sw64(bt + ki * 32), kIdescF16N256,
                                      (kk | ki) ? 1u : 0u);
+                        if (t.w > kXM) {
+#pragma unroll
+                            for (int ki = 0; ki < 2; ki++)
+                                umma_f16(tmem + 256u, umma_desc_sw64(st + kXRec + ki * 32), umma_desc_sw64(bt + ki * 32),
+                                         kIdescF16N256, (kk | ki) ? 1u : 0u);
+                        }
+                    } else {
+                        // M = 128 weight rows (half h of the B tile), N = the tile's tokens (both A records, contiguous)
+#pragma unroll
+                        for (int ki = 0; ki < 2; ki++)
+                            umma_f16(tmem, umma_desc_sw64(bt + ki * 32), umma_desc_sw64(st + ki * 32), idesc, (kk | ki) ? 1u : 0u);
+                        if (w2) {
+#pragma unroll
+                            for (int ki = 0; ki < 2; ki++)
+                                umma_f16(tmem + 256u, umma_desc_sw64(bt + kXRec + ki * 32), umma_desc_sw64(st + ki * 32), idesc,
+                                         (kk | ki) ? 1u : 0u);
+                        }
                     }
                     umma_commit(R.empty(it));
                 }
@@ -469,39 +529,65 @@ __global__ void __launch_bounds__(kXThreads, 1) tcx_gemm_k(XArgs a, Epi epi) {
             }
         }
     } else {
-        // epilogue: warp w reads TMEM lanes 32 (w % 4).. (weight rows) of accumulator h, whose columns are the tile's
-        // tokens; kEpiParts warps share an (h, lane quarter), each a contiguous part of the token blocks
+        // epilogue: warp w reads TMEM lanes 32 (w % 4).. of accumulator h; kEpiParts warps share an (h, lane quarter),
+        // each a contiguous part of its column blocks
         const int e = warp - 2 - kDeqWarps, q = warp & 3, h = (e >> 2) & 1, cpart = e >> 3;
         int tl = 0;
         for (int L = blockIdx.x; L < total; L += gridDim.x, tl++) {
             const int4 t = x_tile(a, L / NT);
-            const int n = (L % NT) * kXN + h * kXM + q * 32 + lane;   // this lane's weight row
+            const int n = (L % NT) * kXN + h * kXM + q * 32 + lane;   // the lane's weight row (weights as M)
             if (!tc_mbar_wait(acc_full, (uint32_t)(tl & 1))) {
                 if (lane == 0) atomicOr(&g_tc_error, 1);
                 break;
             }
             tc_fence_after();
-            // this warp's 32-token column blocks [cb0, cb1) of the tile's 8 (4 for a tile of at most 128 tokens)
-            const int nblk = t.w > kXM ? 8 : 4;
-            const int cb0 = min(cpart * (8 / kEpiParts), nblk), cb1 = min(cb0 + 8 / kEpiParts, nblk);
-            if ((L % NT) * kXN + h * kXM < a.N && cb0 < cb1) {
-                const int ncb = cb1;
+            if constexpr (Epi::kTokensM) {
+                // lanes are tokens 128 h + 32 q + lane; columns the tile's weight rows, 8 blocks of 32 (split by part)
+                const int r = q * 32 + lane, n0 = (L % NT) * kXN;
+                const int cb0 = cpart * (8 / kEpiParts), cb1 = cb0 + 8 / kEpiParts;
+                if (h == 0 || t.w > kXM) {
+                    const bool row_ok = h * kXM + r < t.w;
 #pragma unroll 1
-                for (int cb = cb0; cb < ncb; cb++) {
-                    uint32_t v[32];
-                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 256 + cb * 32), v);
-                    tmem_ld_wait();
-                    if (cb == ncb - 1) {
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) tc_mbar_arrive(acc_empty);   // the accumulators may be overwritten now
+                    for (int cb = cb0; cb < cb1; cb++) {
+                        uint32_t v[32];
+                        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 256 + cb * 32), v);
+                        tmem_ld_wait();
+                        if (cb == cb1 - 1) {
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) tc_mbar_arrive(acc_empty);   // the accumulators may be overwritten now
+                        }
+                        const int col = n0 + cb * 32;
+                        if (row_ok && col < a.N) epi.put(t, h, r, col, a.N, v);
                     }
-                    if (cb * 32 < t.w && n < a.N) epi.put(t, n, cb * 32, lane, v);
+                } else {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) tc_mbar_arrive(acc_empty);
                 }
             } else {
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) tc_mbar_arrive(acc_empty);
+                // lanes are weight rows; this warp's 32-token column blocks [cb0, cb1) of the tile's 8 (4 for a tile of
+                // at most 128 tokens)
+                const int nblk = t.w > kXM ? 8 : 4;
+                const int cb0 = min(cpart * (8 / kEpiParts), nblk), cb1 = min(cb0 + 8 / kEpiParts, nblk);
+                if ((L % NT) * kXN + h * kXM < a.N && cb0 < cb1) {
+#pragma unroll 1
+                    for (int cb = cb0; cb < cb1; cb++) {
+                        uint32_t v[32];
+                        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 256 + cb * 32), v);
+                        tmem_ld_wait();
+                        if (cb == cb1 - 1) {
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) tc_mbar_arrive(acc_empty);   // the accumulators may be overwritten now
+                        }
+                        if (cb * 32 < t.w && n < a.N) epi.put(t, n, cb * 32, lane, v);
+                    }
+                } else {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) tc_mbar_arrive(acc_empty);
+                }
             }
         }
     }
