@@ -146,9 +146,8 @@ constexpr int kMaxSlots = 520;
 // the first stages; above it, the remaining stages.  The layout holds for a dynamic-memory base below 1 KB.
 constexpr uint32_t kTblAddr = 0x10000;
 constexpr int kQueue = kStages + 1;         // a warp's queue of units grabbed ahead (its producer is <= kStages ahead)
-constexpr int kQEntry = 1 + 4;              // unit index, then its token ids
-// barriers, slot counts / order / unit prefix, the warps' unit queues
-constexpr uint32_t kHdrBytes = kGemvWarps * kStages * 8 + (3 * kMaxSlots + 1) * 4 + kGemvWarps * kQueue * kQEntry * 4 + 12;
+// barriers, slot counts / order / unit prefix, the warps' unit queues, the two magnitude words (8-byte aligned)
+constexpr uint32_t kHdrBytes = kGemvWarps * kStages * 8 + (3 * kMaxSlots + 1) * 4 + kGemvWarps * kQueue * (2 + kUnitTok) * 4 + 12 + 16;
 constexpr int kNumStages = kGemvWarps * kStages;
 constexpr uint32_t kMaxDynBase = 1024;
 constexpr int kStagesBelowMin = (int)((kTblAddr - kMaxDynBase - kHdrBytes - 16) / kStageBytes);
@@ -272,166 +271,221 @@ __device__ __forceinline__ Unit decode_unit(int u, const int* s_order, const int
     return w;
 }
 
+// A warp's ring: kStages shared-memory stages used in turn.  `slot` is the stage the warp reads next and `par` the
+// parity of its barrier's next phase; consumed / issued count super-blocks (for the drain after a timeout).
 struct Ring {
-    uint32_t bar0, a0;       // the CTA's barriers; its first stage below the table
-    int q0, nA;              // this warp's first stage index; stages below the table
-    int issued, consumed;    // super-blocks issued into / consumed from the ring
-    __device__ uint32_t stage(int i) const {
-        const int q = q0 + (i % kStages);
-        return q < nA ? a0 + (uint32_t)(q * kStageBytes) : 2u * kTblAddr + (uint32_t)((q - nA) * kStageBytes);
+    uint32_t st[kStages];    // the stages' shared addresses
+    uint32_t bar0;           // the first stage's barrier (the others 8 bytes apart)
+    int slot, consumed, issued;
+    uint32_t par;
+    static_assert(kStages == 3, "stage() selects among three stages");
+    __device__ __forceinline__ uint32_t stage() const { return slot == 0 ? st[0] : slot == 1 ? st[1] : st[2]; }
+    __device__ __forceinline__ uint32_t bar() const { return bar0 + 8u * (uint32_t)slot; }
+    __device__ __forceinline__ void advance() {
+        consumed++;
+        if (++slot == kStages) {
+            slot = 0;
+            par ^= 1u;
+        }
     }
-    __device__ uint32_t bar(int i) const { return bar0 + (uint32_t)((q0 + (i % kStages)) * 8); }
 };
-
-// a unit's token ids and activation rows
-struct Toks {
-    int id[kUnitTok];
-    int arow[kUnitTok];
-};
-
-__device__ __forceinline__ void unit_tokens(const GemvArgs& a, const Unit& w, Toks& t) {
-    const int base = a.counts ? a.offsets[w.s] : 0;
-#pragma unroll
-    for (int m = 0; m < kUnitTok; m++) {
-        const int mm = m < w.nt ? m : 0;
-        const int id = a.counts ? a.order[base + w.b0 + mm] : w.b0 + mm;
-        t.id[m] = id;
-        t.arow[m] = id < a.act_split ? id / a.act_div : id - a.act_split + a.act_base;
-    }
-}
 
 __device__ __forceinline__ const uint8_t* slot_weights(const GemvArgs& a, int s) {
     return (a.counts == nullptr || s < a.nslot_routed) ? a.slab + (size_t)s * a.expert_bytes : a.extra_w;
 }
 
-// Lane 0's producer: takes units from the launch's counter, queues them for its warp (unit number and token ids), and
-// fills the warp's ring with their super-blocks (weights, the tokens' int8 rows and scales).
-struct Producer {
-    const int *s_order, *s_upre, *s_cnt;
-    int nslots, G, U, nsb, ctr;
-    int* queue;              // this warp's kQueue entries of kQEntry ints
-    Unit pu;
-    Toks pt;
-    int psb, pn;
-    bool ok;
+// A queue entry: the unit's row group (-1: no more units), its token count, then its token ids.
+constexpr int kQEntry = 2 + kUnitTok;
 
-    __device__ __forceinline__ void grab(const GemvArgs& a) {
-        const int u = atomicAdd(&g_unit_ctr[ctr][0], 1);
+// Lane 0's producer: takes units from the launch's counter, queues them for its warp (row group, token count and
+// ids), and fills the warp's ring with their super-blocks (weights, the tokens' int8 rows and, unless the launch
+// returns chunk dots, their scales).  Every source pointer is set once a unit and advanced by a constant a stage.
+// The CTA's unit bookkeeping in shared memory: the slots by token count and the exclusive prefix of their units.
+struct Sched {
+    const int *cnt, *order, *upre;
+    int nslots, G, U;
+    uint32_t kc;             // shared address of the two words of signed magnitudes (prmt sources)
+};
+
+template <bool kScl>
+struct Producer {
+    int* queue;              // this warp's kQueue entries of kQEntry ints
+    int pn;                  // units grabbed
+    int nt, left;            // the unit being issued: its tokens, and its super-blocks not yet issued (0: none)
+    const uint8_t* wsrc;     // its next super-block of weights
+    int xoff[kUnitTok];      // element offsets of its tokens' next int8 blocks (from a.xq) and scales (from a.xs)
+    int soff[kUnitTok];
+
+    __device__ __forceinline__ void grab(const GemvArgs& a, const Sched& sc) {
+        const int u = atomicAdd(&g_unit_ctr[a.ctr][0], 1);
         int* e = queue + (pn % kQueue) * kQEntry;
         pn++;
-        if (u >= U) { ok = false; e[0] = -1; return; }
-        pu = decode_unit(u, s_order, s_upre, s_cnt, nslots, G);
-        unit_tokens(a, pu, pt);
-        e[0] = u;
+        if (u >= sc.U) {
+            e[0] = -1;
+            left = 0;
+            return;
+        }
+        const Unit w = decode_unit(u, sc.order, sc.upre, sc.cnt, sc.nslots, sc.G);
+        const int base = a.counts ? a.offsets[w.s] : 0;
+        e[0] = w.g;
+        e[1] = w.nt;
 #pragma unroll
-        for (int m = 0; m < kUnitTok; m++) e[1 + m] = pt.id[m];
-        psb = 0;
-        ok = true;
+        for (int m = 0; m < kUnitTok; m++) {
+            const int mm = m < w.nt ? m : 0;
+            const int id = a.counts ? a.order[base + w.b0 + mm] : w.b0 + mm;
+            const int arow = id < a.act_split ? id / a.act_div : id - a.act_split + a.act_base;
+            e[2 + m] = id;
+            xoff[m] = arow * a.k;
+            if (kScl) soff[m] = arow * (a.k >> 5);
+        }
+        wsrc = slot_weights(a, w.s) + (size_t)w.g * (a.k >> 8) * kIq2Unit;
+        nt = w.nt;
+        left = a.k >> 8;
     }
-    // the next super-block into the next ring stage
-    __device__ __forceinline__ void issue_next(const GemvArgs& a, Ring& r) {
-        if (!ok) return;
-        const int nt = pu.nt;
-        const uint8_t* src = slot_weights(a, pu.s) + ((size_t)pu.g * nsb + psb) * kIq2Unit;
-        const uint32_t st = r.stage(r.issued), bar = r.bar(r.issued);
-        const bool scales = a.xs != nullptr;
+    // the unit's next super-block into the stage at st (barrier bar), which the warp has finished reading
+    __device__ __forceinline__ void issue(const GemvArgs& a, const Sched& sc, uint32_t st, uint32_t bar, Ring& r) {
+        if (left == 0) return;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the warp's reads of the stage come first
-        mbar_expect_tx(bar, (uint32_t)(kIq2Unit + nt * 256 + (scales ? nt * 32 : 0)));
-        bulk_g2s(st, src, kIq2Unit, bar);
+        mbar_expect_tx(bar, (uint32_t)(kIq2Unit + nt * (kScl ? 288 : 256)));
+        bulk_g2s(st, wsrc, kIq2Unit, bar);
+        wsrc += kIq2Unit;
 #pragma unroll
         for (int m = 0; m < kUnitTok; m++) {
             if (m < nt) {
-                bulk_g2s(st + kStageAct + m * 256, a.xq + (size_t)pt.arow[m] * a.k + psb * 256, 256, bar);
-                if (scales) bulk_g2s(st + kStageScl + m * 32, a.xs + (size_t)pt.arow[m] * (a.k >> 5) + psb * 8, 32, bar);
+                bulk_g2s(st + kStageAct + m * 256, a.xq + xoff[m], 256, bar);
+                xoff[m] += 256;
+                if (kScl) {
+                    bulk_g2s(st + kStageScl + m * 32, a.xs + soff[m], 32, bar);
+                    soff[m] += 8;
+                }
             }
         }
         r.issued++;
-        if (++psb == nsb) grab(a);
+        if (--left == 0) grab(a, sc);
     }
 };
 
-// One unit: its 32 rows (a lane each) over K in chunk order, NT token rows (nt <= NT real; nt == NT for NT <= 2).
-// Returns false when a ring wait timed out.
+// the table words are written once before the first barrier and never change: a plain (reorderable) load
+__device__ __forceinline__ uint32_t lds_tbl(uint32_t addr) {
+    uint32_t v;
+    asm("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+
+// dA = d (0.5 + s4) / 4 = (2 s4 + 1) d / 8 of a chunk, exactly.  s4 is the top bits of its four sign bytes: one
+// multiply gathers bits 7, 15, 23, 31 into 28..31 (every partial product lands on its own bit, so nothing carries)
+// and the added bit 27 is the +1; a funnel shift puts 2 s4 + 1 under the exponent of 2^23, f = 2^23 + 2 s4 + 1, and
+// one fma gives f * d/8 - 2^23 * d/8 with no rounding (the result has at most 16 significant bits).
+__device__ __forceinline__ float chunk_scale(uint32_t qy, float dh8, float dh8m) {
+    const uint32_t p = (qy & 0x80808080u) * 0x00204081u + 0x08000000u;
+    return fmaf(__uint_as_float(__funnelshift_r(p, 0x02580000u, 27)), dh8, dh8m);
+}
+
+// One unit: its 32 rows (a lane each) over K in chunk order, exactly NT token rows.  Every stage is one super-block,
+// read as four chunk pairs (a loop kept rolled: the unrolled stage outgrows the instruction cache).  Returns false
+// when a ring wait timed out.
+struct Ids {
+    int v[kUnitTok];
+};
+
 template <int NT, int EPI>
-__device__ __forceinline__ bool unit_rows(const GemvArgs& a, const Unit& w, const Toks& t, int nt, int lane, Ring& r, Producer& pr,
-                          int nsb) {
+__device__ __forceinline__ bool unit_rows(const GemvArgs& a, int g, const Ids& ids, int lane, Ring& r,
+                                          Producer<EPI != kDots>& pr, const Sched& sc, int nsb) {
+    constexpr bool kScl = EPI != kDots;
+    const int* id = ids.v;
     const uint32_t lane_c = kTblAddr | ((uint32_t)lane * 4u), lane_s = lane_c | 128u;
-    const int row = w.g * kIq2Tile + lane, nc = a.k >> 5;
+    const int row = g * kIq2Tile + lane, nc = a.k >> 5;
     // exact int -> float without a conversion instruction: an integer i with |i| < 2^22 added to the bits of 1.5 * 2^23
-    // gives the float 1.5 * 2^23 + i (the dot's bound is 32 * 43 * 127 = 174752); likewise 2 s4 + 1 in 2^23's mantissa
+    // gives the float 1.5 * 2^23 + i (the dot's bound is 32 * 43 * 127 = 174752)
     constexpr int kBias = 0x4B400000;
     constexpr float kBiasF = 12582912.f;
     float acc[NT];
 #pragma unroll
     for (int m = 0; m < NT; m++) acc[m] = 0.f;
     for (int sb = 0; sb < nsb; sb++) {
-        const uint32_t st = r.stage(r.consumed);
-        const bool ok = mbar_wait(r.bar(r.consumed), (uint32_t)((r.consumed / kStages) & 1), kWaitNs);
+        const uint32_t st = r.stage(), bar = r.bar();
+        const bool ok = mbar_wait(bar, r.par, kWaitNs);
         if (__any_sync(0xffffffffu, !ok)) return false;
         const float dh8 = __half2float(__ushort_as_half(lds16(st + 2048 + lane * 2))) * 0.125f;
         const float dh8m = -8388608.f * dh8;   // exact: a power-of-two scaling
+        // the signed magnitudes {8, 25, 43, -8 | -25, -43} as two words, loaded rather than written as immediates:
+        // held in registers they cost two, rebuilt at each use they cost an instruction a prmt
+        const uint2 tb = lds64(sc.kc);
 #pragma unroll 1
         for (int j = 0; j < 4; j++) {
             const uint4 q = lds128(st + j * 512 + lane * 16);
+            float se[NT], so[NT];   // the tokens' scales of chunks 2j, 2j + 1
+#pragma unroll
+            for (int m = 0; m < NT; m++) {
+                if constexpr (kScl) {
+                    const uint2 v = lds64(st + kStageScl + m * 32 + j * 8);
+                    se[m] = __uint_as_float(v.x);
+                    so[m] = __uint_as_float(v.y);
+                } else {
+                    se[m] = so[m] = 0.f;
+                }
+            }
 #pragma unroll
             for (int h = 0; h < 2; h++) {
                 const int c8 = 2 * j + h;
                 const uint32_t qx = h ? q.z : q.x, qy = h ? q.w : q.y;
-                // s4 from the four spare bits (bits 7, 15, 23, 31 -> 28..31); dA = (d/8) * (2 s4 + 1), one exact fma:
-                // (2^23 + 2 s4 + 1) * d/8 - 2^23 * d/8
-                const uint32_t s4f = ((((qy & 0x80808080u) * 0x00204081u) >> 27) & 0x1eu) | 0x4B000001u;
-                const float dA = fmaf(__uint_as_float(s4f), dh8, dh8m);
+                const float dA = chunk_scale(qy, dh8, dh8m);
                 uint32_t wq[8];
 #pragma unroll
-                for (int g = 0; g < 4; g++) group_weights(lane_c, lane_s, qx, qy, g, wq[2 * g], wq[2 * g + 1]);
+                for (int gg = 0; gg < 4; gg++) {
+                    // address = kTblAddr | (index byte << 8) | lane * 4 (| 128 for the sign half)
+                    const uint32_t sel_b = 0x7604u | ((uint32_t)gg << 4);
+                    const uint32_t sel = lds_tbl(prmt(qx, lane_c, sel_b)) + lds_tbl(prmt(qy, lane_s, sel_b));
+                    wq[2 * gg] = prmt(tb.x, tb.y, sel);
+                    wq[2 * gg + 1] = prmt(tb.x, tb.y, sel >> 16);
+                }
 #pragma unroll
                 for (int m = 0; m < NT; m++) {
-                    if (NT <= 2 || m < nt) {
-                        const uint32_t xa = st + kStageAct + m * 256 + c8 * 32;
-                        const uint4 x0 = lds128(xa), x1 = lds128(xa + 16);
-                        // two independent chains of four (half the dependent latency), joined by one add
-                        int da = __dp4a((int)wq[0], (int)x0.x, kBias);
-                        int db = __dp4a((int)wq[4], (int)x1.x, 0);
-                        da = __dp4a((int)wq[1], (int)x0.y, da);
-                        db = __dp4a((int)wq[5], (int)x1.y, db);
-                        da = __dp4a((int)wq[2], (int)x0.z, da);
-                        db = __dp4a((int)wq[6], (int)x1.z, db);
-                        da = __dp4a((int)wq[3], (int)x0.w, da);
-                        db = __dp4a((int)wq[7], (int)x1.w, db);
-                        const int dot = da + db;
-                        if constexpr (EPI == kDots) {
-                            a.dots[((size_t)t.id[m] * a.n + row) * nc + sb * 8 + c8] = dot - kBias;
-                        } else {
-                            const float s = __uint_as_float(lds32(st + kStageScl + m * 32 + c8 * 4));
-                            acc[m] = fmaf(dA * s, __int_as_float(dot) - kBiasF, acc[m]);
-                        }
+                    const uint32_t xa = st + kStageAct + m * 256 + c8 * 32;
+                    const uint4 x0 = lds128(xa), x1 = lds128(xa + 16);
+                    // one chain of eight: the other tokens and the next chunk's dequantisation hide its latency
+                    int da = __dp4a((int)wq[0], (int)x0.x, kBias);
+                    da = __dp4a((int)wq[1], (int)x0.y, da);
+                    da = __dp4a((int)wq[2], (int)x0.z, da);
+                    da = __dp4a((int)wq[3], (int)x0.w, da);
+                    da = __dp4a((int)wq[4], (int)x1.x, da);
+                    da = __dp4a((int)wq[5], (int)x1.y, da);
+                    da = __dp4a((int)wq[6], (int)x1.z, da);
+                    da = __dp4a((int)wq[7], (int)x1.w, da);
+                    const int dot = da;
+                    if constexpr (EPI == kDots) {
+                        a.dots[((size_t)id[m] * a.n + row) * nc + sb * 8 + c8] = dot - kBias;
+                    } else {
+                        const float s = h ? so[m] : se[m];
+                        acc[m] = fmaf(dA * s, __int_as_float(dot) - kBiasF, acc[m]);
                     }
                 }
             }
         }
         __syncwarp();   // every lane is done with the stage: lane 0 refills it
-        r.consumed++;
-        if (lane == 0) pr.issue_next(a, r);
-        __syncwarp();
+        if (lane == 0) pr.issue(a, sc, st, bar, r);
+        r.advance();
     }
     if constexpr (EPI != kDots) {
 #pragma unroll
         for (int m = 0; m < NT; m++) {
-            if (NT <= 2 || m < nt) {
-                float v = acc[m];
-                if constexpr (EPI != kStore) v = v > 0.f ? v * v : 0.f;
-                const int id = t.id[m];
-                if constexpr (EPI == kRelu2Q8) {
-                    // quant_rows_k over this warp's 32 consecutive outputs (one 32-group of the output row)
-                    float am = v;   // v >= 0 after relu^2
+            float v = acc[m];
+            if constexpr (EPI != kStore) v = v > 0.f ? v * v : 0.f;
+            if constexpr (EPI == kRelu2Q8) {
+                // quant_rows_k over this warp's 32 consecutive outputs (one 32-group of the output row)
+                float am = v;   // v >= 0 after relu^2
 #pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-                    const float inv = am > 0.f ? 127.f / am : 0.f;
-                    a.aq[(size_t)id * a.n + row] = (int8_t)__float2int_rn(v * inv);
-                    if (lane == 0) a.as[(size_t)id * (a.n >> 5) + w.g] = am / 127.f;
-                } else {
-                    a.y[(size_t)id * a.ldy + row] = v;
-                }
+                for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+                const float inv = am > 0.f ? 127.f / am : 0.f;
+                a.aq[(size_t)id[m] * a.n + row] = (int8_t)__float2int_rn(v * inv);
+                if (lane == 0) a.as[(size_t)id[m] * (a.n >> 5) + g] = am / 127.f;
+            } else {
+                a.y[(size_t)id[m] * a.ldy + row] = v;
             }
         }
     }
@@ -448,23 +502,30 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) iq2_gemv_k(GemvArgs a, int
     int* s_order = s_cnt + kMaxSlots;
     int* s_upre = s_order + kMaxSlots;
     int* s_queue = s_upre + kMaxSlots + 1;
+    const uint32_t a0 = (base + kHdrBytes + 15u) & ~15u;
+    int nA = a0 <= kTblAddr ? (int)((kTblAddr - a0) / kStageBytes) : 0;
+    if (nA > kNumStages) nA = kNumStages;
     Ring r;
-    r.bar0 = base;
-    r.a0 = (base + kHdrBytes + 15u) & ~15u;
-    r.nA = r.a0 <= kTblAddr ? (int)((kTblAddr - r.a0) / kStageBytes) : 0;
-    if (r.nA > kNumStages) r.nA = kNumStages;
-    r.q0 = warp * kStages;
-    r.issued = r.consumed = 0;
-    const uint32_t end = 2u * kTblAddr + (uint32_t)((kNumStages - r.nA) * kStageBytes);
+    r.bar0 = base + 8u * (uint32_t)(warp * kStages);
+#pragma unroll
+    for (int i = 0; i < kStages; i++) {
+        const int q = warp * kStages + i;
+        r.st[i] = q < nA ? a0 + (uint32_t)(q * kStageBytes) : 2u * kTblAddr + (uint32_t)((q - nA) * kStageBytes);
+    }
+    r.slot = r.consumed = r.issued = 0;
+    r.par = 0;
+    const uint32_t end = 2u * kTblAddr + (uint32_t)((kNumStages - nA) * kStageBytes);
     if (base + kHdrBytes > kTblAddr || (size_t)end > (size_t)base + kGemvSmem) {
         if (tid == 0) atomicOr(&g_iq2_error, 2);   // the dynamic shared memory does not start low enough
         return;
     }
     if (lane == 0) {
-        for (int i = 0; i < kStages; i++) mbar_init(r.bar0 + 8u * (uint32_t)(r.q0 + i), 1);
+        for (int i = 0; i < kStages; i++) mbar_init(r.bar0 + 8u * (uint32_t)i, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     build_table(reinterpret_cast<uint32_t*>(dyn + (kTblAddr - base)));
+    const uint32_t kc = (base + (uint32_t)((const unsigned char*)(s_queue + kGemvWarps * kQueue * kQEntry) - dyn) + 7u) & ~7u;
+    if (tid == 0) asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(kc), "r"(0xF82B1908u), "r"(0x0000D5E7u) : "memory");
     pdl_wait();
     const int G = a.n / kIq2Tile, nsb = a.k >> 8;
     for (int s = tid; s < nslots; s += blockDim.x) {
@@ -484,50 +545,64 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) iq2_gemv_k(GemvArgs a, int
         s_order[rank] = s;
     }
     __syncthreads();
-    if (tid == 0) {
-        int acc = 0;
-        for (int i = 0; i < nslots; i++) {
-            s_upre[i] = acc;
-            acc += G * ((s_cnt[s_order[i]] + kUnitTok - 1) / kUnitTok);
+    if (warp == 0) {
+        // warp-wide exclusive scan of the ordered slots' unit counts
+        int carry = 0;
+        for (int i0 = 0; i0 < nslots; i0 += 32) {
+            const int i = i0 + lane;
+            const int v = i < nslots ? G * ((s_cnt[s_order[i]] + kUnitTok - 1) / kUnitTok) : 0;
+            int incl = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            if (i < nslots) s_upre[i] = carry + incl - v;
+            carry += __shfl_sync(0xffffffffu, incl, 31);
         }
-        s_upre[nslots] = acc;
+        if (lane == 0) s_upre[nslots] = carry;
     }
     __syncthreads();
-    Producer pr;
-    pr.s_order = s_order;
-    pr.s_upre = s_upre;
-    pr.s_cnt = s_cnt;
-    pr.nslots = nslots;
-    pr.G = G;
-    pr.U = s_upre[nslots];
-    pr.nsb = nsb;
-    pr.ctr = a.ctr;
+    Sched sc;
+    sc.cnt = s_cnt;
+    sc.order = s_order;
+    sc.upre = s_upre;
+    sc.nslots = nslots;
+    sc.G = G;
+    sc.U = s_upre[nslots];
+    sc.kc = kc;
+    Producer<EPI != kDots> pr;
     pr.queue = s_queue + warp * kQueue * kQEntry;
     pr.pn = 0;
-    pr.ok = false;
+    pr.left = 0;
     if (lane == 0) {
-        pr.grab(a);
-        for (int i = 0; i < kStages; i++) pr.issue_next(a, r);
+        pr.grab(a, sc);
+#pragma unroll
+        for (int i = 0; i < kStages; i++) pr.issue(a, sc, r.st[i], r.bar0 + 8u * (uint32_t)i, r);
     }
     bool healthy = true;
     for (int cn = 0; healthy; cn++) {
         __syncwarp();   // lane 0's queue writes are visible to the warp
         const int* e = pr.queue + (cn % kQueue) * kQEntry;
-        const int u = e[0];
-        if (u < 0) break;
-        const Unit w = decode_unit(u, s_order, s_upre, s_cnt, nslots, G);
-        Toks t;
+        const int g = e[0];
+        if (g < 0) break;
+        const int nt = e[1];
+        Ids id;
 #pragma unroll
-        for (int m = 0; m < kUnitTok; m++) t.id[m] = e[1 + m];
-        if (w.nt == 1) healthy = unit_rows<1, EPI>(a, w, t, w.nt, lane, r, pr, nsb);
-        else if (w.nt == 2) healthy = unit_rows<2, EPI>(a, w, t, w.nt, lane, r, pr, nsb);
-        else healthy = unit_rows<4, EPI>(a, w, t, w.nt, lane, r, pr, nsb);
+        for (int m = 0; m < kUnitTok; m++) id.v[m] = e[2 + m];
+        switch (nt) {
+            case 1: healthy = unit_rows<1, EPI>(a, g, id, lane, r, pr, sc, nsb); break;
+            case 2: healthy = unit_rows<2, EPI>(a, g, id, lane, r, pr, sc, nsb); break;
+            case 3: healthy = unit_rows<3, EPI>(a, g, id, lane, r, pr, sc, nsb); break;
+            default: healthy = unit_rows<4, EPI>(a, g, id, lane, r, pr, sc, nsb); break;
+        }
     }
     if (!healthy) {
         // a stage never filled: flag it, and let this warp's copies in flight land before the CTA's memory goes away
         if (lane == 0) {
             atomicOr(&g_iq2_error, 1);
-            for (int i = r.consumed; i < r.issued; i++) mbar_wait(r.bar(i), (uint32_t)((i / kStages) & 1), kWaitNs);
+            for (int i = r.consumed; i < r.issued; i++)
+                mbar_wait(r.bar0 + 8u * (uint32_t)(i % kStages), (uint32_t)((i / kStages) & 1), kWaitNs);
         }
         __syncwarp();
     }
