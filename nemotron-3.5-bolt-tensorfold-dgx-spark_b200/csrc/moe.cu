@@ -58,12 +58,13 @@ __global__ void quant_rows_k(const void* __restrict__ x, int dtype, int ldx, int
 //   softmax: w_i = exp(z_i - max) / sum over the picked of exp(z_j - max)   (softmax, top-k, renormalised)
 //   sigmoid: route_k's form: pick by sigmoid(z) + bias, w = sigmoid / (1e-20 + sum of picked) * scale
 // ---------------------------------------------------------------------------------------------------------
+template <int NJ>   // logits a lane holds: E <= 32 NJ
 __device__ void route_token(const void* logits, int dtype, int ldl, const float* bias, int E, int topk, int mode,
-                           float scale, int t, int lane, int* ridx, float* rw) {
-    float val[16], key[16];
+                            float scale, int t, int lane, int* ridx, float* rw, int* ridx_s) {
+    float val[NJ], key[NJ];
     float mx = -3.0e38f;
 #pragma unroll
-    for (int j = 0; j < 16; j++) {
+    for (int j = 0; j < NJ; j++) {
         const int i = lane + 32 * j;
         if (i < E) {
             const float z = load_act(logits, dtype, (size_t)t * ldl + i);
@@ -88,7 +89,7 @@ __device__ void route_token(const void* logits, int dtype, int ldl, const float*
         float bv = -3.4e38f;
         int bi = 0x7fffffff;
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
+        for (int j = 0; j < NJ; j++) {
             const int i = lane + 32 * j;
             if (i < E && key[j] > bv) { bv = key[j]; bi = i; }
         }
@@ -100,7 +101,7 @@ __device__ void route_token(const void* logits, int dtype, int ldl, const float*
         }
         float pv = 0.f;
 #pragma unroll
-        for (int j = 0; j < 16; j++)
+        for (int j = 0; j < NJ; j++)
             if (lane + 32 * j == bi) { pv = val[j]; key[j] = -3.4e38f; }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) pv += __shfl_xor_sync(0xffffffffu, pv, o);   // only one lane is non-zero
@@ -110,6 +111,7 @@ __device__ void route_token(const void* logits, int dtype, int ldl, const float*
     }
     if (lane < topk) {
         ridx[t * topk + lane] = pick_i;
+        if (ridx_s) ridx_s[t * topk + lane] = pick_i;
         rw[t * topk + lane] = mode == B200Q_ROUTE_SOFTMAX ? picked / sum : picked / sum * scale;
     }
 }
@@ -118,37 +120,67 @@ __global__ void route_k(const void* __restrict__ logits, int dtype, int ldl, con
                         int topk, int mode, float scale, int* __restrict__ ridx, float* __restrict__ rw) {
     pdl_wait();
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (t < T) route_token(logits, dtype, ldl, bias, E, topk, mode, scale, t, threadIdx.x & 31, ridx, rw);
+    if (t < T) {
+        if (E <= 128) route_token<4>(logits, dtype, ldl, bias, E, topk, mode, scale, t, threadIdx.x & 31, ridx, rw, nullptr);
+        else route_token<16>(logits, dtype, ldl, bias, E, topk, mode, scale, t, threadIdx.x & 31, ridx, rw, nullptr);
+    }
     pdl_trigger();
 }
 
 // ---------------------------------------------------------------------------------------------------------
-// grouping (moe_group_k's counting sort, bolt_kernels.cu:275-325), deterministic: thread e collects the pairs of
-// expert e in increasing pair order.  One CTA of 512 threads, E <= 512, pairs <= 4096.  extra > 0 appends a slot
-// E with ids pairs .. pairs + extra - 1 (the shared expert over every token).
+// grouping (moe_group_k's counting sort, bolt_kernels.cu:275-325), deterministic: the pairs of expert e in
+// increasing pair order.  One CTA of 512 threads, E <= 512, pairs <= 4096.  extra > 0 appends a slot E with ids
+// pairs .. pairs + extra - 1 (the shared expert over every token).
+//   1. warp 0 walks the pairs 32 at a time in order: match_any finds the lanes of the same expert, a pair's place in
+//      its expert is that expert's running count plus its rank among those lanes, and the lowest such lane adds
+//      their number to the running count;
+//   2. an exclusive scan of the counts (warp shuffles, then the warps' totals) gives the offsets;
+//   3. every pair writes its index to order[offset + place].
+// Shared memory: ridx_s[pairs] (the routing), place_s[pairs], run_s[512], warp_s[16].
 // ---------------------------------------------------------------------------------------------------------
 __device__ void group_pairs(const int* ridx_s, int pairs, int E, int extra, int* counts, int* offsets, int* order,
-                            int* scan_s) {
-    const int tid = threadIdx.x;
-    int c = 0;
-    if (tid < E)
-        for (int p = 0; p < pairs; p++) c += ridx_s[p] == tid;
-    scan_s[tid] = tid < E ? c : 0;
+                            int* place_s, int* run_s, int* warp_s) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    run_s[tid] = 0;
     __syncthreads();
-    for (int off = 1; off < 512; off <<= 1) {
-        const int v = tid >= off ? scan_s[tid - off] : 0;
-        __syncthreads();
-        scan_s[tid] += v;
-        __syncthreads();
+    if (warp == 0) {
+        for (int p0 = 0; p0 < pairs; p0 += 32) {
+            const int p = p0 + lane;
+            const bool valid = p < pairs;
+            const unsigned vm = __ballot_sync(0xffffffffu, valid);
+            if (valid) {
+                const int e = ridx_s[p];
+                const unsigned peers = __match_any_sync(vm, e);
+                const unsigned below = peers & ((1u << lane) - 1u);
+                place_s[p] = run_s[e] + __popc(below);
+                __syncwarp(vm);
+                if (below == 0) run_s[e] += __popc(peers);
+            }
+            __syncwarp();
+        }
     }
-    const int start = scan_s[tid] - (tid < E ? c : 0);
+    __syncthreads();
+    // exclusive scan of run_s[0 .. 512) (zero past E)
+    const int c = tid < E ? run_s[tid] : 0;
+    int incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_s[warp] = incl;
+    __syncthreads();
+    int before = 0;
+    for (int w = 0; w < warp; w++) before += warp_s[w];
+    const int start = before + incl - c;
     if (tid < E) {
         counts[tid] = c;
         offsets[tid] = start;
-        int w = start;
-        for (int p = 0; p < pairs; p++)
-            if (ridx_s[p] == tid) order[w++] = p;
     }
+    __syncthreads();
+    run_s[tid] = start;   // reused: the offsets, for the scatter
+    __syncthreads();
+    for (int p = tid; p < pairs; p += blockDim.x) order[run_s[ridx_s[p]] + place_s[p]] = p;
     if (tid == 0) {
         offsets[E] = pairs;
         if (extra > 0) { counts[E] = extra; offsets[E + 1] = pairs + extra; }
@@ -159,11 +191,10 @@ __device__ void group_pairs(const int* ridx_s, int pairs, int E, int extra, int*
 __global__ void __launch_bounds__(512) group_k(const int* __restrict__ ridx, int pairs, int E, int* __restrict__ counts,
                                                int* __restrict__ offsets, int* __restrict__ order) {
     pdl_wait();
-    __shared__ int ridx_s[4096];
-    __shared__ int scan_s[512];
+    __shared__ int ridx_s[4096], place_s[4096], run_s[512], warp_s[16];
     for (int i = threadIdx.x; i < pairs; i += blockDim.x) ridx_s[i] = ridx[i];
     __syncthreads();
-    group_pairs(ridx_s, pairs, E, 0, counts, offsets, order, scan_s);
+    group_pairs(ridx_s, pairs, E, 0, counts, offsets, order, place_s, run_s, warp_s);
     pdl_trigger();
 }
 
@@ -217,16 +248,15 @@ __global__ void __launch_bounds__(512) moe_prep_k(const void* __restrict__ x, co
                                                   int* __restrict__ counts, int* __restrict__ offsets, int* __restrict__ order,
                                                   int8_t* __restrict__ xq, float* __restrict__ xs) {
     pdl_wait();
-    __shared__ int ridx_s[4096];
-    __shared__ int scan_s[512];
+    __shared__ int ridx_s[1024], place_s[1024], run_s[512], warp_s[16];   // T * topk <= 64 * 16
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (blockIdx.x == 0) {
-        for (int t = warp; t < T; t += 16) route_token(logits, B200Q_BF16, E, bias, E, topk, route, scale, t, lane, ridx, rw);
+        for (int t = warp; t < T; t += 16) {
+            if (E <= 128) route_token<4>(logits, B200Q_BF16, E, bias, E, topk, route, scale, t, lane, ridx, rw, ridx_s);
+            else route_token<16>(logits, B200Q_BF16, E, bias, E, topk, route, scale, t, lane, ridx, rw, ridx_s);
+        }
         __syncthreads();
-        __threadfence_block();
-        for (int i = threadIdx.x; i < T * topk; i += blockDim.x) ridx_s[i] = ridx[i];
-        __syncthreads();
-        group_pairs(ridx_s, T * topk, E, extra, counts, offsets, order, scan_s);
+        group_pairs(ridx_s, T * topk, E, extra, counts, offsets, order, place_s, run_s, warp_s);
     } else {
         const int groups = H >> 5;
         const int gw = (blockIdx.x - 1) * 16 + warp;
