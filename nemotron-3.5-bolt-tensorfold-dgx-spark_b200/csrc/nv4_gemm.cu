@@ -5,7 +5,7 @@
 // y[t][n] = s2 * sum_k e2m1(x4[t][k]) e4m3(sx[t][k/16]) e2m1(w[n][k]) e4m3(sw[n][k/16])
 //
 // Both operands live in HBM as "tile images": the exact bytes a pipeline stage holds in shared memory, so one
-// cp.async.bulk per operand fills a stage (no tensor map, no multicast, no register staging):
+// cp.async.bulk per operand fills a stage (no tensor map, one destination, no register staging):
 //   weights  (b200q_nv4_tc_pack)      record (n-tile of 256 rows, 256 k): 32 KB of e2m1 then 4 KB of scales
 //   rows     (b200q_quant_nv4_rows)   record (m-tile of 128 rows, 256 k): 16 KB of e2m1 then 2 KB of scales
 // e2m1 part: row r's 128 bytes (k = 2b low nibble, 2b + 1 high nibble of byte b) at r * 128 with the 16-byte chunk c

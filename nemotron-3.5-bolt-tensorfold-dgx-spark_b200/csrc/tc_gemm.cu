@@ -1,24 +1,29 @@
 // Prompt-length GEMMs of the IQ2_XXS experts and the Q8_0 projections on the sm_100a tensor cores: tcgen05.mma
-// kind::f16 (fp16 operands, fp32 accumulation in TMEM), the weights dequantised inside the kernel.
+// kind::f16 (fp16 operands, fp32 accumulation in TMEM), the weights dequantised inside the kernel, on SM pairs.
 //
-// C[m][n] = sum_k A[m][k] B[n][k]: A the activation rows (tokens, or the expert-sorted pairs of the MoE), B the weight
-// rows.  A CTA computes a tile of up to 256 rows x 256 weight rows as two MMAs per k-step, each with M = 128 weight
-// rows (one half of the dequantised weight tile) and N = the tile's rows (both 128-row activation records): two
-// accumulators of 256 TMEM columns whose TMEM lanes are weight rows, so every dequantised weight feeds 256 rows and
-// the epilogue's lanes hold 32 consecutive outputs of one row (each store a contiguous line).  Per 32-k stage of a 5-stage shared-memory ring:
-//   A        the two 128-row halves (8 KB each), bulk-copied (cp.async.bulk, no tensor map) from an fp16 rows image
-//            by one lane of warp 0;
-//   B        256 weight rows x 32 k in fp16, written by 16 dequantising warps in two sets of 8 that take alternate
-//            stages (warp w of a set: rows 32w..32w+31, lane = row), from the packed weights, which each lane
-//            prefetches into registers ahead of use.  IQ2_XXS: a prmt picks every fp16 pair out of its chunk's three
-//            scaled magnitudes and a xor sets its signs, the selectors and masks read as 128-bit entries from
+// C[n][m] = sum_k W[n][k] X[m][k]: W the weight rows (the MMA's M), X the activation rows (tokens, or the
+// expert-sorted pairs of the MoE; the MMA's N).  A cluster of two CTAs computes a pair tile of 256 weight rows x 256
+// rows (128 for a tile of at most 128 rows) with tcgen05.mma.cta_group::2 m256n256k16: CTA r of the pair holds
+// weight rows 128 r .. 128 r + 127 (its half of A) and X rows 128 r .. (its half of B, 64 rows for N = 128), and its
+// TMEM holds the accumulator of its 128 weight rows x all N columns.  So every SM dequantises 128 weight rows that
+// feed 256 rows, each SM's tensor core reads only half of the B tile from its own shared memory, and the accumulator
+// (256 columns) is double-buffered in the SM's 512 TMEM columns: the epilogue drains one tile while the MMAs of the
+// next fill the other buffer.  Per 64-k stage of a 5-stage ring in each CTA (32 KB, identical offsets in both), two
+// 32-k blocks of each operand:
+//   X        the CTA's X rows (2 x 8 KB, or 2 x 4 KB for N = 128), bulk-copied (cp.async.bulk, no tensor map, one
+//            destination) from an fp16 rows image by one lane of warp 0;
+//   W        the CTA's 128 weight rows x 64 k in fp16, written by 16 dequantising warps in four sets of 4 that take
+//            the stages in turn (warp w of a set: rows 32w..32w+31, lane = row), from the packed weights, which each
+//            lane prefetches into registers ahead of use.  IQ2_XXS: a prmt picks every fp16 pair out of its chunk's
+//            three scaled magnitudes and a xor sets its signs, the selectors and masks read as 128-bit entries from
 //            replicated shared-memory tables (conflict-free).  Q8_0: a magic-number prmt makes the int8 exact in fp16
 //            and one hmul2 applies the scale;
-//   MMA      one lane of warp 1 issues the m128n256k16 (or n128 for tiles of at most 128 rows) MMAs of both weight
-//            halves and commits them to the stage's barrier;
-//   epilogue 8 warps drain the accumulators (tcgen05.ld: warp w reads lane quarter w % 4 of one accumulator), hand
-//            them back to the MMA warp, and write the outputs.
-// Tiles (up to 256 rows of one group x 256 weight rows) are handed out persistently, one CTA per SM.
+//   MMA      one lane of the leader CTA's warp 1 waits until both CTAs' stages are full, issues the four m256 MMAs
+//            of the stage and commits them to both CTAs' "empty" barriers (one tcgen05.commit, multicast to the
+//            pair); in the peer CTA warp 1 relays "stage full" to the leader (a remote mbarrier arrive);
+//   epilogue 8 warps a CTA drain their accumulator buffer (tcgen05.ld: warp w reads lane quarter w % 4, half of the
+//            columns), release it to the leader, and write the outputs.
+// Pair tiles are handed out persistently, one cluster per SM pair.
 //
 // Shared-memory tiles are K-major with the 64-byte swizzle of the UMMA descriptors: rows of 64 B (32 fp16), 8-row
 // atoms of 512 B, the 16-byte chunk c of row r at position c ^ ((r >> 1) & 3).
@@ -29,29 +34,29 @@
 // projection's rows image.
 //
 // Numerics (libbolt's prompt fold, PQ8 bolt_mma.cu:234-254 and PIQ2 bolt_mma.cu:380-397, in fp16):
-//   Q8_0   B = fp16(q * d), the scale folded and rounded once.
-//   IQ2    B = fp16(d (0.5 + s4) / 4 * signed grid), rounded once.  (FP8 cannot hold the grid magnitudes 25 and 43.)
-//   A      activations rounded to fp16 once; the MoE's intermediate act = fp16(relu(v)^2).
+//   Q8_0   W = fp16(q * d), the scale folded and rounded once.
+//   IQ2    W = fp16(d (0.5 + s4) / 4 * signed grid), rounded once.  (FP8 cannot hold the grid magnitudes 25 and 43.)
+//   X      activations rounded to fp16 once; the MoE's intermediate act = fp16(relu(v)^2).
 // Every barrier wait is bounded (%globaltimer); on a timeout the kernel records an error (b200q_device_error bit 4),
-// waits for its own copies and MMAs, frees its TMEM and returns.
+// waits for its own copies and MMAs, frees its TMEM and returns.  Every copy has one destination, its own CTA.
 #include "tcgen05.cuh"
 
 namespace b200q {
 
-constexpr int kXM = 128;                        // rows of a slot and of an MMA half
-constexpr int kXN = 256;                        // weight rows of a tile
+constexpr int kXM = 128;                        // rows of a slot, and weight rows of a CTA
+constexpr int kXN = 256;                        // weight rows of a pair tile
 constexpr int kXRec = kXM * 64;                 // 8 KB: a rows-image record (128 rows x 32 fp16)
-constexpr int kXB = kXN * 64;                   // 16 KB: the B tile of a stage
-constexpr int kXStage = 2 * kXRec + kXB;        // 32 KB: the two A halves, then the B tile
+constexpr int kXStage = 4 * kXRec;              // 32 KB: the CTA's X rows (two 32-k blocks), then its W rows (two)
+constexpr int kXWOff = 2 * kXRec;               // the W blocks' offset in a stage
 constexpr int kXStages = 5;
-constexpr int kDeqWarps = 16, kXEpiWarps = 8;  // dequantisers (8 a stage: kDeqWarps / 8 sets taking stages in turn)
-constexpr int kPhases = kDeqWarps / 8;
-constexpr int kEpiParts = kXEpiWarps / 8;       // epilogue warps an (accumulator, lane quarter), splitting the tokens
+constexpr int kDeqWarps = 16, kXEpiWarps = 8;   // dequantisers (4 a stage, in kPhases sets taking stages in turn)
+constexpr int kPhases = kDeqWarps / 4;
 constexpr int kXThreads = (2 + kDeqWarps + kXEpiWarps) * 32;   // 832
 constexpr int kGridTbl = 256 * 8 * 16;          // 32 KB: grid entry -> four prmt selectors, 8 copies
 constexpr int kSignTbl = 128 * 8 * 16;          // 16 KB: sign index -> four xor masks, 8 copies
 constexpr size_t kXSmem = (size_t)kXStages * kXStage + kGridTbl + kSignTbl + 1024 /*align*/ + 256 /*barriers*/;
-constexpr uint32_t kXTmemCols = 512;            // two 256-column accumulators
+constexpr uint32_t kXTmemCols = 512;            // two 256-column accumulator buffers
+static_assert(kPhases == 4, "the dequantisers' chunk assignment assumes four sets");
 
 __device__ int g_tc_error;   // bit 0: a barrier wait timed out (reported by b200q_device_error)
 
@@ -65,15 +70,42 @@ int tc_error_read(int clear) {
     return v;
 }
 
-// instruction descriptors, kind::f16: fp32 accumulator, fp16 A and B, both K-major, M = 128, N = 256 or 128
-constexpr uint32_t kIdescF16N256 = (1u << 4) | (256u >> 3) << 17 | ((uint32_t)(kXM >> 4) << 24);
-constexpr uint32_t kIdescF16N128 = (1u << 4) | (128u >> 3) << 17 | ((uint32_t)(kXM >> 4) << 24);
+// instruction descriptors, kind::f16: fp32 accumulator, fp16 A and B, both K-major, M = 256 (a CTA pair), N = 256 / 128
+constexpr uint32_t kIdesc2N256 = (1u << 4) | (256u >> 3) << 17 | (256u >> 4) << 24;
+constexpr uint32_t kIdesc2N128 = (1u << 4) | (128u >> 3) << 17 | (256u >> 4) << 24;
 
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+// one m256 MMA of a CTA pair, issued by the leader: A and B descriptors address the same offsets in both CTAs
+__device__ __forceinline__ void umma2_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p; }"
-        ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p; }"
+        ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0),
+          "r"(0), "r"(0));
+}
+// the completion of the leader's MMAs so far arrives on the barrier at offset `bar` in both CTAs of the pair (a
+// tcgen05.commit multicast: a signal, not a load)
+__device__ __forceinline__ void umma2_commit_pair(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 ::"r"(bar), "h"((unsigned short)3) : "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// the shared::cluster address of `addr` (a shared::cta address) in the CTA of rank `rank`
+__device__ __forceinline__ uint32_t peer_addr(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+// an arrive on the other CTA's barrier (default semantics: no cluster-wide fence before it, which would stall the
+// relay a round trip per stage)
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
@@ -122,13 +154,9 @@ __device__ __forceinline__ int4 x_tile(const XArgs& a, int mt) {
     return make_int4(0, 2 * mt, m0, min(2 * kXM, a.T - m0));
 }
 
-// Epilogues.  kTokensM picks the MMA's orientation, and so which index a TMEM lane carries:
-//   false: weights are M, tokens N.  put(t, n, tok0, lane, v): v[j] = (weight row n, the lane's; token tok0 + j); the
-//          32 lanes hold 32 consecutive weight rows, so a token's store is one contiguous line, one element a lane.
-//   true:  tokens are M, weights N.  put(t, h, r, col, N, v): v[j] = (token 128 h + r, the lane's; weight row col + j);
-//          a lane holds 32 consecutive outputs of one row and stores them 16 bytes at a time.
-struct EpiRows {             // fp32 y[orow][n]; orow = rowmap[row0[g] + m0 + token] (or the dense row)
-    static constexpr bool kTokensM = false;
+// Epilogues.  put(t, n, tok0, lane, v): v[j] = (weight row n, the lane's; row tok0 + j of the tile); the 32 lanes of
+// a warp hold 32 consecutive weight rows, so every row's outputs from one warp are one contiguous line.
+struct EpiRows {             // fp32 y[orow][n]; orow = rowmap[row0[g] + m0 + row] (or the dense row)
     float* y;
     int ldy;
     const int* row0;         // per-group first row in the row list (offsets), nullptr: 0
@@ -144,49 +172,8 @@ struct EpiRows {             // fp32 y[orow][n]; orow = rowmap[row0[g] + m0 + to
         }
     }
 };
-struct EpiRowsT {            // EpiRows with tokens as M: a lane's 32 outputs of its row as eight 16-byte stores
-    static constexpr bool kTokensM = true;
-    float* y;
-    int ldy;
-    const int* row0;
-    const int* rowmap;
-    __device__ void put(int4 t, int h, int r, int col, int N, const uint32_t (&v)[32]) const {
-        const int grow = (row0 ? row0[t.x] : 0) + t.z + h * kXM + r;
-        const int orow = rowmap ? rowmap[grow] : grow;
-        float* o = y + (size_t)orow * ldy + col;
-        if (col + 32 <= N && ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0)) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 4)
-                *reinterpret_cast<float4*>(o + i) =
-                    make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]), __uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
-        } else {
-#pragma unroll
-            for (int i = 0; i < 32; i++)
-                if (col + i < N) o[i] = __uint_as_float(v[i]);
-        }
-    }
-};
-struct EpiImg {              // fp16(relu(v)^2) into the next GEMM's rows image (its K = this GEMM's N), tokens as M:
-    // a lane's 32 outputs are one 64-byte row of a record, and a warp's 32 lanes write 2 KB of it contiguously
-    static constexpr bool kTokensM = true;
-    uint8_t* img;
-    int N;
-    __device__ void put(int4 t, int h, int r, int col, int N_, const uint32_t (&v)[32]) const {
-        uint8_t* rec = img + ((size_t)(t.y + h) * (N / 32) + col / 32) * kXRec;
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-            uint32_t o[4];
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const float a0 = __uint_as_float(v[8 * c + 2 * j]), a1 = __uint_as_float(v[8 * c + 2 * j + 1]);
-                o[j] = h2u(__floats2half2_rn(a0 > 0.f ? a0 * a0 : 0.f, a1 > 0.f ? a1 * a1 : 0.f));
-            }
-            *reinterpret_cast<uint4*>(rec + sw64_off(r, c)) = make_uint4(o[0], o[1], o[2], o[3]);
-        }
-    }
-};
-struct EpiImgW {             // EpiImg with weights as M (one fp16 a lane per token row)
-    static constexpr bool kTokensM = false;
+struct EpiImg {              // fp16(relu(v)^2) into the next GEMM's rows image (its K = this GEMM's N): for each row
+    // the warp's 32 weight rows are one 64-byte row of a record (2 bytes a lane)
     uint8_t* img;
     int N;
     __device__ void put(int4 t, int n, int tok0, int lane, const uint32_t (&v)[32]) const {
@@ -206,7 +193,7 @@ struct EpiImgW {             // EpiImg with weights as M (one fp16 a lane per to
 };
 
 // ---------------------------------------------------------------------------------------------------------
-// B dequantisers.  run() produces its phase's stages of one tile for the calling warp's 32 rows (lane = row): for
+// W dequantisers.  run() produces its phase's stages of one tile for the calling warp's 32 rows (lane = row): for
 // each of those 32-k blocks it waits for the stage to be free, writes the row's 64 B, and arrives on the stage's "full"
 // barrier.
 // ---------------------------------------------------------------------------------------------------------
@@ -229,15 +216,6 @@ __device__ __forceinline__ void x_stage_done(const XRing& R, int it, int lane) {
     tc_fence_proxy_async();   // the generic-proxy writes are visible to the tensor core
     __syncwarp();
     if (lane == 0) tc_mbar_arrive(R.full(it));
-}
-
-// a lane's 16 bytes of a chunk pair (one phase: both chunks; two phases: only its own 8 bytes, in .x and .y)
-__device__ __forceinline__ uint4 ld_pair(const uint8_t* p) {
-    if (kPhases == 2) {
-        const uint2 v = ldg_nc64(p);
-        return make_uint4(v.x, v.y, 0u, 0u);
-    }
-    return ldg_nc(p);
 }
 
 struct DeqIQ2 {              // IQ2_XXS rt32 layout (common.cuh); sign words re-encoded by the packer
@@ -265,49 +243,50 @@ struct DeqIQ2 {              // IQ2_XXS rt32 layout (common.cuh); sign words re-
         for (int g = 0; g < 4; g++)
             sts128(row_addr + (uint32_t)((g ^ sw) << 4), group(P0, P1, (qx >> (8 * g)) & 255u, (qy >> (8 * g)) & 127u, lane8));
     }
-    // the stages kk = phase, phase + 2, ... of one tile for the rows of row tile rt of the group's matrix wm (n x K);
-    // stage kk is ring iteration it0 + kk.  valid: rt's rows exist.
+    // the stages kk = phase, phase + 4, ... of one tile for the rows of row tile rt of the group's matrix wm (n x K):
+    // stage kk (64 k) is chunk pair kk & 3 of super-block kk >> 2, so this warp reads chunk pair `phase` (16 bytes)
+    // of every super-block, two super-blocks ahead of use.  Stage kk is ring iteration it0 + kk.  valid: rt's rows
+    // exist.
     __device__ bool run(const XRing& R, int it0, const uint8_t* wm, int K, int rt, bool valid, int wd, int phase,
                         int lane) const {
         const int nb = K >> 8;
-        const uint8_t* base = wm + (size_t)rt * nb * kIq2Unit + lane * 16 + (kPhases == 2 ? phase * 8 : 0);
-        // this lane's chunk pairs j of the current / next super-block (with two phases only chunk 2j + phase)
-        uint4 c[4], n[4];
-        uint32_t dc = 0, dn = 0;
+        const uint8_t* unit0 = wm + (size_t)rt * nb * kIq2Unit;
+        const uint32_t o = (uint32_t)(phase * 512 + lane * 16);
+        uint4 c = make_uint4(0, 0, 0, 0), m = c, n = c;
+        uint32_t dc = 0, dm = 0, dn = 0;
         if (valid) {
-#pragma unroll
-            for (int j = 0; j < 4; j++) c[j] = ld_pair(base + j * 512);
-            dc = ldg_u16(wm + (size_t)rt * nb * kIq2Unit + 2048 + lane * 2);
+            c = ldg_nc(unit0 + o);
+            dc = ldg_u16(unit0 + 2048 + lane * 2);
+            if (nb > 1) {
+                m = ldg_nc(unit0 + kIq2Unit + o);
+                dm = ldg_u16(unit0 + kIq2Unit + 2048 + lane * 2);
+            }
         }
         for (int sb = 0; sb < nb; sb++) {
-            if (valid && sb + 1 < nb) {
-                const uint8_t* u = base + (size_t)(sb + 1) * kIq2Unit;
-#pragma unroll
-                for (int j = 0; j < 4; j++) n[j] = ld_pair(u + j * 512);
-                dn = ldg_u16(wm + ((size_t)rt * nb + sb + 1) * kIq2Unit + 2048 + lane * 2);
+            if (valid && sb + 2 < nb) {
+                const uint8_t* u = unit0 + (size_t)(sb + 2) * kIq2Unit;
+                n = ldg_nc(u + o);
+                dn = ldg_u16(u + 2048 + lane * 2);
             }
             const float d = __half2float(__ushort_as_half((unsigned short)dc));
+            const int it = it0 + sb * 4 + phase;
+            if (!x_wait_free(R, it, lane)) return false;
+            const uint32_t row_addr = R.stage(it) + kXWOff + (uint32_t)((wd * 32 + lane) * 64);
+            if (valid) {
+                chunk(c.x, c.y, d, row_addr, lane);
+                chunk(c.z, c.w, d, row_addr + kXRec, lane);
+            } else {
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-#pragma unroll
-                for (int hh = 0; hh < 2 / kPhases; hh++) {
-                    const int ch = kPhases == 2 ? 2 * j + phase : 2 * j + hh;
-                    const int it = it0 + sb * 8 + ch;
-                    if (!x_wait_free(R, it, lane)) return false;
-                    const uint32_t row_addr = R.stage(it) + 2 * kXRec + (uint32_t)((wd * 32 + lane) * 64);
-                    if (valid) {
-                        if (hh == 0) chunk(c[j].x, c[j].y, d, row_addr, lane);
-                        else chunk(c[j].z, c[j].w, d, row_addr, lane);
-                    } else {
-#pragma unroll
-                        for (int g = 0; g < 4; g++) sts128(row_addr + g * 16, make_uint4(0, 0, 0, 0));
-                    }
-                    x_stage_done(R, it, lane);
+                for (int g = 0; g < 4; g++) {
+                    sts128(row_addr + g * 16, make_uint4(0, 0, 0, 0));
+                    sts128(row_addr + kXRec + g * 16, make_uint4(0, 0, 0, 0));
                 }
             }
-#pragma unroll
-            for (int j = 0; j < 4; j++) c[j] = n[j];
-            dc = dn;
+            x_stage_done(R, it, lane);
+            c = m;
+            dc = dm;
+            m = n;
+            dm = dn;
         }
         return true;
     }
@@ -331,45 +310,55 @@ struct DeqQ8 {
         const uint32_t x0 = w0 ^ 0x80808080u, x1 = w1 ^ 0x80808080u;
         return make_uint4(pair(x0, 0x4140u, d2), pair(x0, 0x4342u, d2), pair(x1, 0x4140u, d2), pair(x1, 0x4342u, d2));
     }
-    // the stages kk = phase, phase + 2, ... of one tile (32-k blocks), prefetched three of this warp's blocks ahead
+    __device__ __forceinline__ static void put_block(uint32_t row_addr, uint4 qa, uint4 qb, uint32_t d, int lane) {
+        const int sw = (lane >> 1) & 3;
+        const __half2 d2 = __half2half2(__ushort_as_half((unsigned short)d));
+        sts128(row_addr + (uint32_t)((0 ^ sw) << 4), quad(qa.x, qa.y, d2));
+        sts128(row_addr + (uint32_t)((1 ^ sw) << 4), quad(qa.z, qa.w, d2));
+        sts128(row_addr + (uint32_t)((2 ^ sw) << 4), quad(qb.x, qb.y, d2));
+        sts128(row_addr + (uint32_t)((3 ^ sw) << 4), quad(qb.z, qb.w, d2));
+    }
+    // the stages kk = phase, phase + 4, ... of one tile (64 k: 32-k blocks 2kk, 2kk + 1), each prefetched one of
+    // this warp's stages (four stages) ahead (two would not fit the registers of an 832-thread CTA)
     __device__ bool run(const XRing& R, int it0, const uint8_t* wm, int K, int rt, bool valid, int wd, int phase,
                         int lane) const {
-        const int nk = K >> 5;   // a multiple of 8
-        const uint8_t* base = wm + (size_t)rt * nk * kQ8Unit;
-        uint4 qa[4], qb[4];
-        uint32_t dd[4];
-        if (valid) {
+        constexpr int kAhead = 1, kRing = kAhead + 1;
+        const int nm = (K >> 6) / kPhases;   // this warp's stages (K % 256 == 0: at least 1)
+        const uint8_t* base = wm + (size_t)rt * (K >> 5) * kQ8Unit + lane * 32;
+        const uint8_t* dbase = wm + (size_t)rt * (K >> 5) * kQ8Unit + 1024 + lane * 2;
+        uint4 qa[kRing][2], qb[kRing][2];
+        uint32_t dd[kRing][2];
+        auto fetch = [&](int slot, int mm) {
 #pragma unroll
-            for (int u = 0; u < 3; u++) {
-                const uint8_t* p = base + (size_t)(kPhases * u + phase) * kQ8Unit;
-                qa[u] = ldg_nc(p + lane * 32);
-                qb[u] = ldg_nc(p + lane * 32 + 16);
-                dd[u] = ldg_u16(p + 1024 + lane * 2);
+            for (int h = 0; h < 2; h++) {
+                const size_t off = (size_t)(2 * (kPhases * mm + phase) + h) * kQ8Unit;
+                qa[slot][h] = ldg_nc(base + off);
+                qb[slot][h] = ldg_nc(base + off + 16);
+                dd[slot][h] = ldg_u16(dbase + off);
             }
-        }
-        for (int m0 = 0; m0 < nk / kPhases; m0 += 4) {
+        };
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int m = m0 + u, kb = kPhases * m + phase, nx = m + 3;
-                if (valid && nx < nk / kPhases) {   // prefetch this warp's block m + 3 into its ring slot
-                    const uint8_t* p = base + (size_t)(kPhases * nx + phase) * kQ8Unit;
-                    qa[(u + 3) & 3] = ldg_nc(p + lane * 32);
-                    qb[(u + 3) & 3] = ldg_nc(p + lane * 32 + 16);
-                    dd[(u + 3) & 3] = ldg_u16(p + 1024 + lane * 2);
-                }
-                const int it = it0 + kb;
+        for (int u = 0; u < kAhead; u++) {
+            if (valid && u < nm) fetch(u, u);
+        }
+        for (int m0 = 0; m0 < nm; m0 += kRing) {
+#pragma unroll
+            for (int u = 0; u < kRing; u++) {
+                const int m = m0 + u;
+                if (m >= nm) break;
+                if (valid && m + kAhead < nm) fetch((u + kAhead) % kRing, m + kAhead);
+                const int it = it0 + kPhases * m + phase;
                 if (!x_wait_free(R, it, lane)) return false;
-                const uint32_t row_addr = R.stage(it) + 2 * kXRec + (uint32_t)((wd * 32 + lane) * 64);
-                const int sw = (lane >> 1) & 3;
+                const uint32_t row_addr = R.stage(it) + kXWOff + (uint32_t)((wd * 32 + lane) * 64);
                 if (valid) {
-                    const __half2 d2 = __half2half2(__ushort_as_half((unsigned short)dd[u]));
-                    sts128(row_addr + (uint32_t)((0 ^ sw) << 4), quad(qa[u].x, qa[u].y, d2));
-                    sts128(row_addr + (uint32_t)((1 ^ sw) << 4), quad(qa[u].z, qa[u].w, d2));
-                    sts128(row_addr + (uint32_t)((2 ^ sw) << 4), quad(qb[u].x, qb[u].y, d2));
-                    sts128(row_addr + (uint32_t)((3 ^ sw) << 4), quad(qb[u].z, qb[u].w, d2));
+                    put_block(row_addr, qa[u][0], qb[u][0], dd[u][0], lane);
+                    put_block(row_addr + kXRec, qa[u][1], qb[u][1], dd[u][1], lane);
                 } else {
 #pragma unroll
-                    for (int g = 0; g < 4; g++) sts128(row_addr + g * 16, make_uint4(0, 0, 0, 0));
+                    for (int g = 0; g < 4; g++) {
+                        sts128(row_addr + g * 16, make_uint4(0, 0, 0, 0));
+                        sts128(row_addr + kXRec + g * 16, make_uint4(0, 0, 0, 0));
+                    }
                 }
                 x_stage_done(R, it, lane);
             }
@@ -379,19 +368,21 @@ struct DeqQ8 {
 };
 
 // ---------------------------------------------------------------------------------------------------------
-// the GEMM
+// the GEMM: one cluster of two CTAs per SM pair
 // ---------------------------------------------------------------------------------------------------------
 template <class Deq, class Epi>
-__global__ void __launch_bounds__(kXThreads, 1) tcx_gemm_k(XArgs a, Epi epi) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kXThreads, 1) tcx_gemm_k(XArgs a, Epi epi) {
     extern __shared__ __align__(1024) unsigned char x_dyn[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t rank = cluster_rank();   // 0: the leader, which issues the pair's MMAs; 1: the peer
     const uint32_t raw = (uint32_t)__cvta_generic_to_shared(x_dyn);
     XRing R;
     R.sbase = (raw + 1023u) & ~1023u;
     const uint32_t gtbl = R.sbase + kXStages * kXStage, stbl = gtbl + kGridTbl;
     R.bars = stbl + kSignTbl;
-    const uint32_t acc_full = R.bars + 8u * XRing::kBars, acc_empty = acc_full + 8u, drain = acc_full + 16u;
-    const uint32_t tmem_slot = acc_full + 24u;
+    const uint32_t acc_full = R.bars + 8u * XRing::kBars;   // [2]
+    const uint32_t acc_empty = acc_full + 16u;              // [2], arrived on in the leader by both CTAs' epilogues
+    const uint32_t drain = acc_full + 32u, tmem_slot = acc_full + 40u;
     unsigned char* tmem_slot_ptr = x_dyn + (tmem_slot - raw);
 
     if (Deq::kTables) {
@@ -418,110 +409,128 @@ __global__ void __launch_bounds__(kXThreads, 1) tcx_gemm_k(XArgs a, Epi epi) {
         }
     }
     if (tid == 0) {
-        for (int s = 0; s < kXStages; s++) { tc_mbar_init(R.full(s), 1 + kDeqWarps / kPhases); tc_mbar_init(R.empty(s), 1); }
-        tc_mbar_init(acc_full, 1);
-        tc_mbar_init(acc_empty, kXEpiWarps);
+        // full: this CTA's producer (arrive + bytes) and the stage's 4 dequantising warps, and in the leader the peer's
+        // relay; empty, acc_full, drain: one commit of the leader's MMAs; acc_empty (used in the leader): both CTAs'
+        // epilogue warps
+        for (int s = 0; s < kXStages; s++) {
+            tc_mbar_init(R.full(s), 1 + 4 + (rank == 0 ? 1 : 0));
+            tc_mbar_init(R.empty(s), 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            tc_mbar_init(acc_full + 8u * b, 1);
+            tc_mbar_init(acc_empty + 8u * b, 2 * kXEpiWarps);
+        }
         tc_mbar_init(drain, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot), "r"(kXTmemCols));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        // both CTAs' warp 1 take the pair's TMEM: 512 columns in each SM
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot), "r"(kXTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
     }
     tc_fence_before();
     __syncthreads();
+    cluster_sync_all();   // both CTAs' barriers exist before either arrives on the other's
     tc_fence_after();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot_ptr);
     pdl_wait();
 
-    const int NT = (a.N + kXN - 1) / kXN, KK = a.K / 32;
+    const int NT = (a.N + kXN - 1) / kXN, KK = a.K / 64;   // 64-k stages a tile
     const int mtiles = a.tiles ? min(*a.ntiles, a.max_mtiles) : a.max_mtiles;
     const int total = mtiles * NT;
+    const int cl = (int)(blockIdx.x >> 1), ncl = (int)(gridDim.x >> 1);
 
     if (warp == 0) {
-        // rows producer: one lane bulk-copies each stage's A records
+        // X producer: one lane bulk-copies this CTA's rows of each stage (its 128-row slot, or half of the tile's one
+        // slot when the tile has at most 128 rows): the two 32-k records of a stage are adjacent in the image
         if (lane == 0) {
             bool healthy = true;
             int it = 0;
-            for (int L = blockIdx.x; L < total && healthy; L += gridDim.x) {
+            for (int L = cl; L < total && healthy; L += ncl) {
                 const int4 t = x_tile(a, L / NT);
-                const int halves = t.w > kXM ? 2 : 1;
-                const uint8_t* a0 = a.a + (size_t)t.y * KK * kXRec;
+                const bool wide = t.w > kXM;
+                const uint8_t* src = wide ? a.a + (size_t)(t.y + (int)rank) * (2 * KK) * kXRec
+                                          : a.a + (size_t)t.y * (2 * KK) * kXRec + rank * (kXRec / 2);
                 for (int kk = 0; kk < KK; kk++, it++) {
                     const int use = it / kXStages;
                     if (use > 0 && !tc_mbar_wait(R.empty(it), (uint32_t)((use - 1) & 1))) { healthy = false; break; }
-                    const uint32_t st = R.stage(it);
-                    tc_mbar_arrive_tx(R.full(it), (uint32_t)(halves * kXRec));
-                    tc_bulk_g2s(st, a0 + (size_t)kk * kXRec, (uint32_t)kXRec, R.full(it));
-                    if (halves == 2) tc_bulk_g2s(st + kXRec, a0 + ((size_t)KK + kk) * kXRec, (uint32_t)kXRec, R.full(it));
+                    const uint8_t* blk = src + (size_t)(2 * kk) * kXRec;
+                    if (wide) {
+                        tc_mbar_arrive_tx(R.full(it), 2u * kXRec);
+                        tc_bulk_g2s(R.stage(it), blk, 2u * kXRec, R.full(it));
+                    } else {
+                        tc_mbar_arrive_tx(R.full(it), (uint32_t)kXRec);
+                        tc_bulk_g2s(R.stage(it), blk, (uint32_t)(kXRec / 2), R.full(it));
+                        tc_bulk_g2s(R.stage(it) + kXRec, blk + kXRec, (uint32_t)(kXRec / 2), R.full(it));
+                    }
                 }
             }
-            // the copies of the last uses of every stage have landed before the CTA may exit
+            // every stage's last release (the leader's commits land in this CTA's barriers too) before the CTA may exit
             for (int i = it - kXStages > 0 ? it - kXStages : 0; i < it; i++)
-                if (!tc_mbar_wait(R.full(i), (uint32_t)((i / kXStages) & 1))) healthy = false;
+                if (!tc_mbar_wait(R.empty(i), (uint32_t)((i / kXStages) & 1))) healthy = false;
             if (!healthy) atomicOr(&g_tc_error, 1);
         }
         __syncwarp();
     } else if (warp == 1) {
-        // MMA issuer
         if (lane == 0) {
             bool healthy = true;
-            int it = 0, tl = 0;
-            for (int L = blockIdx.x; L < total && healthy; L += gridDim.x, tl++) {
-                const int4 t = x_tile(a, L / NT);
-                const uint32_t idesc = t.w > kXM ? kIdescF16N256 : kIdescF16N128;   // tokens: the MMAs' N
-                const bool w2 = (L % NT) * kXN + kXM < a.N;                         // the second weight half exists
-                if (tl > 0 && !tc_mbar_wait(acc_empty, (uint32_t)((tl - 1) & 1))) { healthy = false; break; }
-                tc_fence_after();
-                for (int kk = 0; kk < KK; kk++, it++) {
-                    if (!tc_mbar_wait(R.full(it), (uint32_t)((it / kXStages) & 1))) { healthy = false; break; }
-                    tc_fence_after();
-                    const uint32_t st = R.stage(it), bt = st + 2 * kXRec;
-                    if constexpr (Epi::kTokensM) {
-                        // M = 128 tokens (A record h), N = the 256 weight rows of the B tile
-#pragma unroll
-                        for (int ki = 0; ki < 2; ki++)
-                            umma_f16(tmem, umma_desc_sw64(st + ki * 32), umma_desc_sw64(bt + ki * 32), kIdescF16N256,
-                                     (kk | ki) ? 1u : 0u);
-                        if (t.w > kXM) {
-#pragma unroll
-                            for (int ki = 0; ki < 2; ki++)
-                                umma_f16(tmem + 256u, umma_desc_sw64(st + kXRec + ki * 32), umma_desc_sw64(bt + ki * 32),
-                                         kIdescF16N256, (kk | ki) ? 1u : 0u);
-                        }
-                    } else {
-                        // M = 128 weight rows (half h of the B tile), N = the tile's tokens (both A records, contiguous)
-#pragma unroll
-                        for (int ki = 0; ki < 2; ki++)
-                            umma_f16(tmem, umma_desc_sw64(bt + ki * 32), umma_desc_sw64(st + ki * 32), idesc, (kk | ki) ? 1u : 0u);
-                        if (w2) {
-#pragma unroll
-                            for (int ki = 0; ki < 2; ki++)
-                                umma_f16(tmem + 256u, umma_desc_sw64(bt + kXRec + ki * 32), umma_desc_sw64(st + ki * 32), idesc,
-                                         (kk | ki) ? 1u : 0u);
-                        }
+            if (rank == 0) {
+                // MMA issuer: per stage four m256 MMAs (k 16 each) into the tile's accumulator buffer
+                int it = 0, tl = 0;
+                for (int L = cl; L < total && healthy; L += ncl, tl++) {
+                    const int4 t = x_tile(a, L / NT);
+                    const uint32_t idesc = t.w > kXM ? kIdesc2N256 : kIdesc2N128;
+                    const int b = tl & 1;
+                    if (tl >= 2 && !tc_mbar_wait(acc_empty + 8u * b, (uint32_t)(((tl >> 1) - 1) & 1))) {
+                        healthy = false;
+                        break;
                     }
-                    umma_commit(R.empty(it));
+                    tc_fence_after();
+                    const uint32_t dacc = tmem + (uint32_t)(b * 256);
+                    for (int kk = 0; kk < KK; kk++, it++) {
+                        if (!tc_mbar_wait(R.full(it), (uint32_t)((it / kXStages) & 1))) { healthy = false; break; }
+                        tc_fence_after();
+                        const uint32_t st = R.stage(it);
+#pragma unroll
+                        for (int ki = 0; ki < 4; ki++) {
+                            const uint32_t o = (uint32_t)((ki >> 1) * kXRec + (ki & 1) * 32);
+                            umma2_f16(dacc, umma_desc_sw64(st + kXWOff + o), umma_desc_sw64(st + o), idesc,
+                                      (kk | ki) ? 1u : 0u);
+                        }
+                        umma2_commit_pair(R.empty(it));
+                    }
+                    if (healthy) umma2_commit_pair(acc_full + 8u * b);
                 }
-                if (healthy) umma_commit(acc_full);
+                // the epilogues' last releases have landed before the leader may exit
+                for (int j = tl - 2 > 0 ? tl - 2 : 0; j < tl && healthy; j++)
+                    if (!tc_mbar_wait(acc_empty + 8u * (j & 1), (uint32_t)((j >> 1) & 1))) healthy = false;
+                // every MMA issued has completed (and so no longer reads either CTA's stages) before TMEM is freed
+                umma2_commit_pair(drain);
+            } else {
+                // relay: each stage of this CTA full (its X rows landed, its W rows written) -> the leader's barrier
+                const uint32_t lead_full0 = peer_addr(R.full(0), 0);
+                int it = 0;
+                for (int L = cl; L < total && healthy; L += ncl)
+                    for (int kk = 0; kk < KK; kk++, it++) {
+                        if (!tc_mbar_wait(R.full(it), (uint32_t)((it / kXStages) & 1))) { healthy = false; break; }
+                        mbar_arrive_cluster(lead_full0 + 8u * (uint32_t)(it % kXStages));
+                    }
             }
-            // every MMA this thread issued has completed before the TMEM is freed
-            umma_commit(drain);
             if (!tc_mbar_wait(drain, 0)) healthy = false;
             if (!healthy) atomicOr(&g_tc_error, 1);
         }
         __syncwarp();
     } else if (warp < 2 + kDeqWarps) {
-        // dequantisers: warp 2 + 8 phase + wd owns weight rows 32 wd .. 32 wd + 31 of the even (phase 0) or odd
-        // (phase 1) stages of every tile
-        const int wd = (warp - 2) & 7, phase = (warp - 2) >> 3;   // phase 0 with one set
+        // dequantisers: warp 2 + 4 phase + wd owns this CTA's weight rows 32 wd .. 32 wd + 31 of the stages
+        // kk = phase (mod 4) of every tile
+        const int wd = (warp - 2) & 3, phase = (warp - 2) >> 2;
         Deq dq;
         dq.gtbl = gtbl;
         dq.stbl = stbl;
         int it0 = 0;
-        for (int L = blockIdx.x; L < total; L += gridDim.x, it0 += KK) {
+        for (int L = cl; L < total; L += ncl, it0 += KK) {
             const int4 t = x_tile(a, L / NT);
-            const int n0 = (L % NT) * kXN + wd * 32;
+            const int n0 = (L % NT) * kXN + (int)rank * kXM + wd * 32;
             const uint8_t* wm = a.w + (size_t)t.x * a.wstride;
             if (!dq.run(R, it0, wm, a.K, n0 >> 5, n0 < a.N, wd, phase, lane)) {
                 if (lane == 0) atomicOr(&g_tc_error, 1);
@@ -529,73 +538,45 @@ __global__ void __launch_bounds__(kXThreads, 1) tcx_gemm_k(XArgs a, Epi epi) {
             }
         }
     } else {
-        // epilogue: warp w reads TMEM lanes 32 (w % 4).. of accumulator h; kEpiParts warps share an (h, lane quarter),
-        // each a contiguous part of its column blocks
-        const int e = warp - 2 - kDeqWarps, q = warp & 3, h = (e >> 2) & 1, cpart = e >> 3;
+        // epilogue: warp w reads TMEM lane quarter w % 4 (32 weight rows) and one half of the tile's 32-row column
+        // blocks, from the tile's buffer; the last read releases the buffer to the leader's MMA
+        const int e = warp - 2 - kDeqWarps, q = warp & 3, ch = e >> 2;
+        const uint32_t lead_empty = rank == 0 ? 0u : peer_addr(acc_empty, 0);
         int tl = 0;
-        for (int L = blockIdx.x; L < total; L += gridDim.x, tl++) {
+        for (int L = cl; L < total; L += ncl, tl++) {
             const int4 t = x_tile(a, L / NT);
-            const int n = (L % NT) * kXN + h * kXM + q * 32 + lane;   // the lane's weight row (weights as M)
-            if (!tc_mbar_wait(acc_full, (uint32_t)(tl & 1))) {
+            const int b = tl & 1;
+            if (!tc_mbar_wait(acc_full + 8u * b, (uint32_t)((tl >> 1) & 1))) {
                 if (lane == 0) atomicOr(&g_tc_error, 1);
                 break;
             }
             tc_fence_after();
-            if constexpr (Epi::kTokensM) {
-                // lanes are tokens 128 h + 32 q + lane; columns the tile's weight rows, 8 blocks of 32 (split by part)
-                const int r = q * 32 + lane, n0 = (L % NT) * kXN;
-                const int cb0 = cpart * (8 / kEpiParts), cb1 = cb0 + 8 / kEpiParts;
-                if (h == 0 || t.w > kXM) {
-                    const bool row_ok = h * kXM + r < t.w;
+            const int nbase = (L % NT) * kXN + (int)rank * kXM;   // this CTA's first weight row
+            const int n = nbase + q * 32 + lane;
+            const int nblk = t.w > kXM ? 8 : 4, cb0 = ch * (nblk / 2), cb1 = cb0 + nblk / 2;
 #pragma unroll 1
-                    for (int cb = cb0; cb < cb1; cb++) {
-                        uint32_t v[32];
-                        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 256 + cb * 32), v);
-                        tmem_ld_wait();
-                        if (cb == cb1 - 1) {
-                            tc_fence_before();
-                            __syncwarp();
-                            if (lane == 0) tc_mbar_arrive(acc_empty);   // the accumulators may be overwritten now
-                        }
-                        const int col = n0 + cb * 32;
-                        if (row_ok && col < a.N) epi.put(t, h, r, col, a.N, v);
-                    }
-                } else {
+            for (int cb = cb0; cb < cb1; cb++) {
+                uint32_t v[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * 256 + cb * 32), v);
+                tmem_ld_wait();
+                if (cb == cb1 - 1) {
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) tc_mbar_arrive(acc_empty);
-                }
-            } else {
-                // lanes are weight rows; this warp's 32-token column blocks [cb0, cb1) of the tile's 8 (4 for a tile of
-                // at most 128 tokens)
-                const int nblk = t.w > kXM ? 8 : 4;
-                const int cb0 = min(cpart * (8 / kEpiParts), nblk), cb1 = min(cb0 + 8 / kEpiParts, nblk);
-                if ((L % NT) * kXN + h * kXM < a.N && cb0 < cb1) {
-#pragma unroll 1
-                    for (int cb = cb0; cb < cb1; cb++) {
-                        uint32_t v[32];
-                        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 256 + cb * 32), v);
-                        tmem_ld_wait();
-                        if (cb == cb1 - 1) {
-                            tc_fence_before();
-                            __syncwarp();
-                            if (lane == 0) tc_mbar_arrive(acc_empty);   // the accumulators may be overwritten now
-                        }
-                        if (cb * 32 < t.w && n < a.N) epi.put(t, n, cb * 32, lane, v);
+                    if (lane == 0) {
+                        if (rank == 0) tc_mbar_arrive(acc_empty + 8u * b);
+                        else mbar_arrive_cluster(lead_empty + 8u * b);
                     }
-                } else {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) tc_mbar_arrive(acc_empty);
                 }
+                if (nbase < a.N && cb * 32 < t.w && n < a.N) epi.put(t, n, cb * 32, lane, v);
             }
         }
     }
     tc_fence_before();
     __syncthreads();
+    cluster_sync_all();   // neither CTA leaves while the other may still arrive on its barriers
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kXTmemCols));
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kXTmemCols));
     }
     pdl_trigger();
 }
@@ -615,16 +596,32 @@ static int x_num_sms() {
 
 template <class Deq, class Epi>
 static cudaError_t launch_x(const XArgs& a, const Epi& epi, cudaStream_t s) {
-    static bool opted = false;
-    if (!opted) {
+    static int max_clusters = 0;   // SM pairs that can hold one cluster each
+    if (!max_clusters) {
         const cudaError_t e = cudaFuncSetAttribute(tcx_gemm_k<Deq, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kXSmem);
         if (e != cudaSuccess) return e;
-        opted = true;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (x_num_sms() / 2));
+        cfg.blockDim = dim3(kXThreads);
+        cfg.dynamicSmemBytes = kXSmem;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 2;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, tcx_gemm_k<Deq, Epi>, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = x_num_sms() / 2;
+        }
+        max_clusters = n;
     }
     const long long work = (long long)a.max_mtiles * ((a.N + kXN - 1) / kXN);
-    const int grid = (int)(work < x_num_sms() ? work : x_num_sms());
-    if (grid <= 0) return cudaSuccess;
-    return launch(tcx_gemm_k<Deq, Epi>, dim3(grid), dim3(kXThreads), kXSmem, s, a, epi);
+    const int clusters = (int)(work < max_clusters ? work : max_clusters);
+    if (clusters <= 0) return cudaSuccess;
+    return launch(tcx_gemm_k<Deq, Epi>, dim3(2 * clusters), dim3(kXThreads), kXSmem, s, a, epi);
 }
 
 // ---------------------------------------------------------------------------------------------------------

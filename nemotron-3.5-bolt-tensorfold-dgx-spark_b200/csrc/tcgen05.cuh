@@ -39,7 +39,7 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// global -> shared bulk copy (no tensor map, no multicast) completing `bytes` on the barrier; 16-byte aligned, size a
+// global -> shared bulk copy (no tensor map, one destination) completing `bytes` on the barrier; 16-byte aligned, size a
 // multiple of 16
 __device__ __forceinline__ void tc_bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
