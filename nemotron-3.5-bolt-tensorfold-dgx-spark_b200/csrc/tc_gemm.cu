@@ -48,13 +48,18 @@ constexpr int kXN = 256;                        // weight rows of a pair tile
 constexpr int kXRec = kXM * 64;                 // 8 KB: a rows-image record (128 rows x 32 fp16)
 constexpr int kXStage = 4 * kXRec;              // 32 KB: the CTA's X rows (two 32-k blocks), then its W rows (two)
 constexpr int kXWOff = 2 * kXRec;               // the W blocks' offset in a stage
-constexpr int kXStages = 5;
+#ifndef B200Q_TC_COPIES
+#define B200Q_TC_COPIES 8
+#endif
+#ifndef B200Q_TC_IQ2_STAGES
+#define B200Q_TC_IQ2_STAGES 5
+#endif
 constexpr int kDeqWarps = 16, kXEpiWarps = 8;   // dequantisers (4 a stage, in kPhases sets taking stages in turn)
 constexpr int kPhases = kDeqWarps / 4;
 constexpr int kXThreads = (2 + kDeqWarps + kXEpiWarps) * 32;   // 832
-constexpr int kGridTbl = 256 * 8 * 16;          // 32 KB: grid entry -> four prmt selectors, 8 copies
-constexpr int kSignTbl = 128 * 8 * 16;          // 16 KB: sign index -> four xor masks, 8 copies
-constexpr size_t kXSmem = (size_t)kXStages * kXStage + kGridTbl + kSignTbl + 1024 /*align*/ + 256 /*barriers*/;
+// shared memory of a CTA: the ring, the dequantiser's tables, alignment slack and the barriers
+template <class Deq>
+constexpr size_t x_smem() { return (size_t)Deq::kStages * kXStage + Deq::kTableBytes + 1024 + 256; }
 constexpr uint32_t kXTmemCols = 512;            // two 256-column accumulator buffers
 static_assert(kPhases == 4, "the dequantisers' chunk assignment assumes four sets");
 
@@ -197,22 +202,26 @@ struct EpiImg {              // fp16(relu(v)^2) into the next GEMM's rows image 
 // each of those 32-k blocks it waits for the stage to be free, writes the row's 64 B, and arrives on the stage's "full"
 // barrier.
 // ---------------------------------------------------------------------------------------------------------
-struct XRing {               // stage bookkeeping shared by the warps of one CTA
+template <int S>
+struct XRing {               // stage bookkeeping shared by the warps of one CTA: S stages
+    static constexpr int kStages = S;
     uint32_t sbase, bars;
-    __device__ uint32_t full(int it) const { return bars + 8u * (it % kXStages); }
-    __device__ uint32_t empty(int it) const { return bars + 8u * (kXStages + it % kXStages); }
-    __device__ uint32_t stage(int it) const { return sbase + (uint32_t)((it % kXStages) * kXStage); }
-    static constexpr int kBars = 2 * kXStages;
+    __device__ uint32_t full(int it) const { return bars + 8u * (it % S); }
+    __device__ uint32_t empty(int it) const { return bars + 8u * (S + it % S); }
+    __device__ uint32_t stage(int it) const { return sbase + (uint32_t)((it % S) * kXStage); }
+    static constexpr int kBars = 2 * S;
 };
 
 // waits (lane 0) for the stage of iteration `it` to be free; false on a timeout (warp-uniform)
-__device__ __forceinline__ bool x_wait_free(const XRing& R, int it, int lane) {
-    const int use = it / kXStages;
+template <class Ring>
+__device__ __forceinline__ bool x_wait_free(const Ring& R, int it, int lane) {
+    const int use = it / Ring::kStages;
     int ok = 1;
     if (use > 0 && lane == 0) ok = tc_mbar_wait(R.empty(it), (uint32_t)((use - 1) & 1)) ? 1 : 0;
     return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
-__device__ __forceinline__ void x_stage_done(const XRing& R, int it, int lane) {
+template <class Ring>
+__device__ __forceinline__ void x_stage_done(const Ring& R, int it, int lane) {
     tc_fence_proxy_async();   // the generic-proxy writes are visible to the tensor core
     __syncwarp();
     if (lane == 0) tc_mbar_arrive(R.full(it));
@@ -220,13 +229,18 @@ __device__ __forceinline__ void x_stage_done(const XRing& R, int it, int lane) {
 
 struct DeqIQ2 {              // IQ2_XXS rt32 layout (common.cuh); sign words re-encoded by the packer
     static constexpr bool kTables = true;
+    static constexpr int kCopies = B200Q_TC_COPIES;            // replicas of each table entry
+    static constexpr int kGridTbl = 256 * kCopies * 16;       // grid entry -> four prmt selectors
+    static constexpr int kSignTbl = 128 * kCopies * 16;       // sign index -> four xor masks
+    static constexpr int kTableBytes = kGridTbl + kSignTbl;
+    static constexpr int kStages = B200Q_TC_IQ2_STAGES;
     uint32_t gtbl, stbl;     // shared-memory tables (set in the kernel)
     // 8 fp16 of one 8-element group: each pair's magnitudes by prmt from {h8, h25, h43}, then its signs by xor.  A
-    // 128-bit table entry per grid index (selectors) and per sign index (masks), 8 copies so that the 8 lanes of a
-    // quarter-warp read 8 different bank groups.
+    // 128-bit table entry per grid index (selectors) and per sign index (masks), kCopies copies so that the lanes of a
+    // quarter-warp read different bank groups.
     __device__ __forceinline__ uint4 group(uint32_t P0, uint32_t P1, uint32_t gi, uint32_t si, uint32_t lane8) const {
-        const uint4 sel = lds128(gtbl + ((gi << 7) | lane8));
-        const uint4 sg = lds128(stbl + ((si << 7) | lane8));
+        const uint4 sel = lds128(gtbl + ((gi * kCopies) << 4 | lane8));
+        const uint4 sg = lds128(stbl + ((si * kCopies) << 4 | lane8));
         return make_uint4(prmt(P0, P1, sel.x) ^ sg.x, prmt(P0, P1, sel.y) ^ sg.y, prmt(P0, P1, sel.z) ^ sg.z,
                           prmt(P0, P1, sel.w) ^ sg.w);
     }
@@ -238,7 +252,7 @@ struct DeqIQ2 {              // IQ2_XXS rt32 layout (common.cuh); sign words re-
         const uint32_t P0 = h2u(__floats2half2_rn(8.f * db, 25.f * db));
         const uint32_t P1 = h2u(__floats2half2_rn(43.f * db, 0.f));
         const int sw = (lane >> 1) & 3;
-        const uint32_t lane8 = (uint32_t)(lane & 7) << 4;
+        const uint32_t lane8 = (uint32_t)(lane & (kCopies - 1)) << 4;
 #pragma unroll
         for (int g = 0; g < 4; g++)
             sts128(row_addr + (uint32_t)((g ^ sw) << 4), group(P0, P1, (qx >> (8 * g)) & 255u, (qy >> (8 * g)) & 127u, lane8));
@@ -247,7 +261,8 @@ struct DeqIQ2 {              // IQ2_XXS rt32 layout (common.cuh); sign words re-
     // stage kk (64 k) is chunk pair kk & 3 of super-block kk >> 2, so this warp reads chunk pair `phase` (16 bytes)
     // of every super-block, two super-blocks ahead of use.  Stage kk is ring iteration it0 + kk.  valid: rt's rows
     // exist.
-    __device__ bool run(const XRing& R, int it0, const uint8_t* wm, int K, int rt, bool valid, int wd, int phase,
+    template <class Ring>
+    __device__ bool run(const Ring& R, int it0, const uint8_t* wm, int K, int rt, bool valid, int wd, int phase,
                         int lane) const {
         const int nb = K >> 8;
         const uint8_t* unit0 = wm + (size_t)rt * nb * kIq2Unit;
@@ -297,6 +312,8 @@ struct DeqIQ2 {              // IQ2_XXS rt32 layout (common.cuh); sign words re-
 constexpr int kQ8Unit = 1088;
 struct DeqQ8 {
     static constexpr bool kTables = false;
+    static constexpr int kCopies = 1, kGridTbl = 0, kSignTbl = 0, kTableBytes = 0;
+    static constexpr int kStages = 7;
     uint32_t gtbl, stbl;
     // 0x64XX as fp16 is 1024 + XX exactly; with the int8's sign bit flipped XX = q + 128, so minus 1152 gives q exactly,
     // and one fp16 multiply by d rounds q * d once
@@ -320,7 +337,8 @@ struct DeqQ8 {
     }
     // the stages kk = phase, phase + 4, ... of one tile (64 k: 32-k blocks 2kk, 2kk + 1), each prefetched one of
     // this warp's stages (four stages) ahead (two would not fit the registers of an 832-thread CTA)
-    __device__ bool run(const XRing& R, int it0, const uint8_t* wm, int K, int rt, bool valid, int wd, int phase,
+    template <class Ring>
+    __device__ bool run(const Ring& R, int it0, const uint8_t* wm, int K, int rt, bool valid, int wd, int phase,
                         int lane) const {
         constexpr int kAhead = 1, kRing = kAhead + 1;
         const int nm = (K >> 6) / kPhases;   // this warp's stages (K % 256 == 0: at least 1)
@@ -376,11 +394,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kXThreads, 1) tcx_ge
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t rank = cluster_rank();   // 0: the leader, which issues the pair's MMAs; 1: the peer
     const uint32_t raw = (uint32_t)__cvta_generic_to_shared(x_dyn);
-    XRing R;
+    constexpr int kXStages = Deq::kStages;
+    using Ring = XRing<kXStages>;
+    Ring R;
     R.sbase = (raw + 1023u) & ~1023u;
-    const uint32_t gtbl = R.sbase + kXStages * kXStage, stbl = gtbl + kGridTbl;
-    R.bars = stbl + kSignTbl;
-    const uint32_t acc_full = R.bars + 8u * XRing::kBars;   // [2]
+    const uint32_t gtbl = R.sbase + kXStages * kXStage, stbl = gtbl + Deq::kGridTbl;
+    R.bars = stbl + Deq::kSignTbl;
+    const uint32_t acc_full = R.bars + 8u * Ring::kBars;   // [2]
     const uint32_t acc_empty = acc_full + 16u;              // [2], arrived on in the leader by both CTAs' epilogues
     const uint32_t drain = acc_full + 32u, tmem_slot = acc_full + 40u;
     unsigned char* tmem_slot_ptr = x_dyn + (tmem_slot - raw);
@@ -388,8 +408,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kXThreads, 1) tcx_ge
     if (Deq::kTables) {
         // grid selectors: entry g, copy c at (g * 8 + c) * 16: for each pair p of elements (2p, 2p + 1) the prmt
         // selector of their fp16 magnitudes out of {h8, h25, h43} (bytes 0-1, 2-3, 4-5)
-        for (int i = tid; i < 256 * 8; i += kXThreads) {
-            const unsigned long long gr = iq2xxs_grid[i >> 3];
+        for (int i = tid; i < 256 * Deq::kCopies; i += kXThreads) {
+            const unsigned long long gr = iq2xxs_grid[i / Deq::kCopies];
             uint32_t w[4];
 #pragma unroll
             for (int p = 0; p < 4; p++) {
@@ -400,8 +420,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kXThreads, 1) tcx_ge
             sts128(gtbl + (uint32_t)i * 16u, make_uint4(w[0], w[1], w[2], w[3]));
         }
         // sign masks: sign index i, copy c: for each pair p the fp16x2 sign bits of elements 2p (bit 15), 2p + 1 (bit 31)
-        for (int i = tid; i < 128 * 8; i += kXThreads) {
-            const uint32_t s = ksigns_iq2xs[i >> 3];
+        for (int i = tid; i < 128 * Deq::kCopies; i += kXThreads) {
+            const uint32_t s = ksigns_iq2xs[i / Deq::kCopies];
             uint32_t w[4];
 #pragma unroll
             for (int p = 0; p < 4; p++) w[p] = ((s >> (2 * p)) & 1u) << 15 | ((s >> (2 * p + 1)) & 1u) << 31;
@@ -598,12 +618,12 @@ template <class Deq, class Epi>
 static cudaError_t launch_x(const XArgs& a, const Epi& epi, cudaStream_t s) {
     static int max_clusters = 0;   // SM pairs that can hold one cluster each
     if (!max_clusters) {
-        const cudaError_t e = cudaFuncSetAttribute(tcx_gemm_k<Deq, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kXSmem);
+        const cudaError_t e = cudaFuncSetAttribute(tcx_gemm_k<Deq, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)x_smem<Deq>());
         if (e != cudaSuccess) return e;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * (x_num_sms() / 2));
         cfg.blockDim = dim3(kXThreads);
-        cfg.dynamicSmemBytes = kXSmem;
+        cfg.dynamicSmemBytes = x_smem<Deq>();
         cudaLaunchAttribute at[1];
         at[0].id = cudaLaunchAttributeClusterDimension;
         at[0].val.clusterDim.x = 2;
@@ -621,7 +641,7 @@ static cudaError_t launch_x(const XArgs& a, const Epi& epi, cudaStream_t s) {
     const long long work = (long long)a.max_mtiles * ((a.N + kXN - 1) / kXN);
     const int clusters = (int)(work < max_clusters ? work : max_clusters);
     if (clusters <= 0) return cudaSuccess;
-    return launch(tcx_gemm_k<Deq, Epi>, dim3(2 * clusters), dim3(kXThreads), kXSmem, s, a, epi);
+    return launch(tcx_gemm_k<Deq, Epi>, dim3(2 * clusters), dim3(kXThreads), x_smem<Deq>(), s, a, epi);
 }
 
 // ---------------------------------------------------------------------------------------------------------
