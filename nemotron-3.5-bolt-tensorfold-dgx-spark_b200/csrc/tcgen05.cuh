@@ -22,10 +22,14 @@ __device__ __forceinline__ void tc_mbar_arrive(uint32_t bar) {
 __device__ __forceinline__ void tc_mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
+// One test of the phase.  A thread whose phase is not complete is suspended until it completes or kTcSuspendNs
+// pass: a waiting warp then takes no issue slots from the working ones (without the hint try_wait returns at once
+// and a waiting warp spins).
+constexpr uint32_t kTcSuspendNs = 100000;
 __device__ __forceinline__ bool tc_mbar_try(uint32_t bar, uint32_t parity) {
     uint32_t ok;
-    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(ok) : "r"(bar), "r"(parity), "r"(kTcSuspendNs) : "memory");
     return ok != 0;
 }
 __device__ __forceinline__ bool tc_mbar_wait(uint32_t bar, uint32_t parity) {
