@@ -321,6 +321,9 @@ struct Producer {
         int* e = queue + (pn % kQueue) * kQEntry;
         pn++;
         if (u >= sc.U) {
+            // no units left for this warp: the next launch on the stream may be scheduled now (it still waits for
+            // this grid's completion before it reads anything), so its CTAs build their tables during this tail
+            pdl_trigger();
             e[0] = -1;
             left = 0;
             return;
