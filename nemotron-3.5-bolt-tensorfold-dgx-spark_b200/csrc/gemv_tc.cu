@@ -61,8 +61,8 @@ __device__ __forceinline__ uint32_t ldg_stream1(const void* p) {
 // layouts ("t16"): rows in tiles of 16; lane (g, t) = (lane / 4, lane % 4) holds the m16n8k16 A fragment
 //   a0 = (row g, k 2t..2t+1)  a1 = (row g+8, k 2t..)  a2 = (row g, k 2t+8..)  a3 = (row g+8, k 2t+8..)
 // NVFP4: unit (tile, 64-k step s) = 576 B: [32 lanes][4 words] then [8 g][8 B].  Word j of a lane covers k16
-//   step j: nibble i (i < 4) is the low element of a_i and nibble i+4 its high element.  The 8 bytes of group g
-//   are the e4m3 scales of row g for the step's four 16-blocks, then those of row g+8.
+//   step j: byte i is a_i, its low element in the low nibble (so one cvt.f16x2.e2m1x2 makes a_i).  The 8 bytes of
+//   group g are the e4m3 scales of row g for the step's four 16-blocks, then those of row g+8.
 // Q8_0: unit (tile, 32-k block b) = 544 B: [32 lanes][16 B] then [8 g][2 x fp16].  Bytes 8u..8u+7 of a lane are
 //   a0, a1, a2, a3 (two int8 each, low k first) of k16 step u; group g's word holds d of row g, then of row g+8.
 // ---------------------------------------------------------------------------------------------------------
@@ -84,7 +84,7 @@ __global__ void nv4_pack_k(const uint8_t* __restrict__ q, const uint8_t* __restr
             const int rr[4] = {16 * tile + g, 16 * tile + g + 8, 16 * tile + g, 16 * tile + g + 8};
             const int kk[4] = {k0, k0, k0 + 8, k0 + 8};
             uint32_t v = 0;
-            for (int r = 0; r < 4; r++) v |= nib(rr[r], kk[r]) << (4 * r) | nib(rr[r], kk[r] + 1) << (4 * (r + 4));
+            for (int r = 0; r < 4; r++) v |= (nib(rr[r], kk[r]) | nib(rr[r], kk[r] + 1) << 4) << (8 * r);
             w[j] = v;
         }
         uint8_t* u = out + (size_t)unit * kNv4Unit;
@@ -145,19 +145,19 @@ struct TcArgs {
 constexpr int kTcWarps = 8;
 enum { kFmtNv4 = 0, kFmtQ8 = 1 };
 
-// the four A fragments of one NVFP4 k16 step from word `w`, scaled by (sg, sg8) = the step's scales of rows g, g+8
+// two e2m1 codes (low nibble -> low half) to f16x2, exact (every e2m1 value is an fp16)
+__device__ __forceinline__ uint32_t e2m1x2_f16x2(uint32_t v) {
+    uint32_t d;
+    asm("{ .reg .b8 t; cvt.u8.u32 t, %1; cvt.rn.f16x2.e2m1x2 %0, t; }" : "=r"(d) : "r"(v));
+    return d;
+}
+// the four A fragments of one NVFP4 k16 step from word `w` (byte i = a_i), scaled by (hg, hg8) = the step's scales
+// of rows g, g+8
 __device__ __forceinline__ void nv4_frag(uint32_t w, uint32_t hg, uint32_t hg8, uint32_t (&a)[4]) {
-    // fp16 high bytes of the magnitudes 0, .5, 1, 1.5, 2, 3, 4, 6 (low bytes are zero)
-    const uint32_t ml = prmt(0x3E3C3800u, 0x46444240u, w & 0x7777u);
-    const uint32_t mh = prmt(0x3E3C3800u, 0x46444240u, (w >> 16) & 0x7777u);
-    // a_i = half2(nibble i, nibble i + 4): bytes [0, ml.i, 0, mh.i]; the zero bytes come from prmt's sign-replicate
-    // mode on a byte whose top bit is clear; the signs (bit 3 of the nibbles) move to bits 15 and 31
-    a[0] = prmt(ml, mh, 0x4808u) | ((w << 12) & 0x80008000u);
-    a[1] = prmt(ml, mh, 0x5919u) | ((w << 8) & 0x80008000u);
-    a[2] = prmt(ml, mh, 0x6A2Au) | ((w << 4) & 0x80008000u);
-    a[3] = prmt(ml, mh, 0x7B3Bu) | (w & 0x80008000u);
-    a[0] = hmul2(a[0], hg); a[2] = hmul2(a[2], hg);
-    a[1] = hmul2(a[1], hg8); a[3] = hmul2(a[3], hg8);
+    a[0] = hmul2(e2m1x2_f16x2(w), hg);
+    a[1] = hmul2(e2m1x2_f16x2(w >> 8), hg8);
+    a[2] = hmul2(e2m1x2_f16x2(w >> 16), hg);
+    a[3] = hmul2(e2m1x2_f16x2(w >> 24), hg8);
 }
 
 // int8 pairs -> f16x2 exactly: 1152 + b as fp16 (0x64 high byte, b ^ 0x80 low byte), minus 1152

@@ -46,7 +46,7 @@ def np_nv4_t16(q, sc, n, k):
             for r in range(4):
                 lo = nib.reshape(n // 16, 16, k // 64, 64)[:, rows[r], :, ks[r]]
                 hi = nib.reshape(n // 16, 16, k // 64, 64)[:, rows[r], :, ks[r] + 1]
-                w |= lo << (4 * r) | hi << (4 * (r + 4))
+                w |= (lo | hi << 4) << (8 * r)
             out[:, :, 16 * lane + 4 * j:16 * lane + 4 * j + 4] = w[..., None].view(np.uint8).reshape(n // 16, k // 64, 4)
     s = sc.reshape(n // 16, 16, k // 64, 4)
     for g in range(8):
