@@ -181,6 +181,32 @@ def prefill_bench(b200q, layer, device, iters=5):
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / iters
         res[name] = (ms, flops / (ms * 1e-3) / 1e12)
+    # the same GQA projections at decode sizes (M = 1 / 16 rows) on the t16 Q8_0 GEMV, GB/s over weights + x + y,
+    # rotating 6 weight copies of q/k/v (160 MB, larger than L2)
+    dec = {}
+    copies = 6
+    wd = []
+    for c in range(copies):
+        r = np.random.default_rng(40 + c)
+        raw = np.concatenate([r.uniform(1e-3, 1e-2, (6144, H // 32)).astype(np.float16).view(np.uint8).reshape(6144, H // 32, 2),
+                              r.integers(-127, 128, (6144, H // 32, 32), dtype=np.int8).view(np.uint8)], -1).reshape(-1)
+        wd.append(b200q.tile_q8(torch.from_numpy(raw).to(device), 6144, H))
+    for M in (1, 16):
+        xd = torch.randn(M, H, generator=g).to(torch.bfloat16).to(device)
+        yd = torch.empty(M, 6144, dtype=torch.float32, device=device)
+        for i in range(3):
+            b200q.mma_q8(wd[i % copies], 6144, H, xd, y=yd)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(s)
+        n_it = 30
+        for i in range(n_it):
+            b200q.mma_q8(wd[i % copies], 6144, H, xd, y=yd)
+        e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / n_it
+        nbytes = 6144 * H * 34 // 32 + M * H * 2 + M * 6144 * 4
+        dec[f"gqa_qkv_decode_M{M}_gbs"] = round(nbytes / (ms * 1e-3) / 1e9, 1)
     err = b200q.device_error()
     cnt = counts.cpu().numpy()
     return {"workload": "BASELINE config 4: 8192 tokens x top-6 = 49152 rows over 128 IQ2_XXS experts (Zipf 1.1, "
@@ -188,7 +214,7 @@ def prefill_bench(b200q, layer, device, iters=5):
                         "same 8192 tokens",
             "arithmetic": "fp16 operands (scales folded, rounded once), fp32 accumulation: tcgen05.mma kind::f16",
             "moe_ms": round(res["moe"][0], 4), "moe_tflops": round(res["moe"][1], 1),
-            "gqa_ms": round(res["gqa"][0], 4), "gqa_tflops": round(res["gqa"][1], 1),
+            "gqa_ms": round(res["gqa"][0], 4), "gqa_tflops": round(res["gqa"][1], 1), **dec,
             "hottest_expert_rows": int(cnt.max()), "device_error": err}
 
 

@@ -19,8 +19,8 @@
 //            replicated shared-memory tables (conflict-free).  Q8_0: a magic-number prmt makes the int8 exact in fp16
 //            and one hmul2 applies the scale;
 //   MMA      one lane of the leader CTA's warp 1 waits until both CTAs' stages are full, issues the four m256 MMAs
-//            of the stage and commits them to both CTAs' "empty" barriers (one tcgen05.commit, multicast to the
-//            pair); in the peer CTA warp 1 relays "stage full" to the leader (a remote mbarrier arrive);
+//            of the stage and commits them to both CTAs' "empty" barriers (a tcgen05.commit to each); in the peer CTA
+//            warp 1 relays "stage full" to the leader (a remote mbarrier arrive);
 //   epilogue 8 warps a CTA drain their accumulator buffer (tcgen05.ld: warp w reads lane quarter w % 4, half of the
 //            columns), release it to the leader, and write the outputs.
 // Pair tiles are handed out persistently, one cluster per SM pair.
@@ -87,11 +87,10 @@ __device__ __forceinline__ void umma2_f16(uint32_t tmem_d, uint64_t a, uint64_t 
         ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0),
           "r"(0), "r"(0));
 }
-// the completion of the leader's MMAs so far arrives on the barrier at offset `bar` in both CTAs of the pair (a
-// tcgen05.commit multicast: a signal, not a load)
-__device__ __forceinline__ void umma2_commit_pair(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
-                 ::"r"(bar), "h"((unsigned short)3) : "memory");
+// the completion of the leader's MMAs so far arrives on the barrier at `bar` (a shared::cluster address: the
+// leader's own barrier, or the peer's from peer_addr); the leader commits to each CTA's copy of a barrier in turn
+__device__ __forceinline__ void umma2_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
@@ -496,6 +495,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kXThreads, 1) tcx_ge
             bool healthy = true;
             if (rank == 0) {
                 // MMA issuer: per stage four m256 MMAs (k 16 each) into the tile's accumulator buffer
+                const uint32_t p_empty0 = peer_addr(R.empty(0), 1), p_acc_full = peer_addr(acc_full, 1);
                 int it = 0, tl = 0;
                 for (int L = cl; L < total && healthy; L += ncl, tl++) {
                     const int4 t = x_tile(a, L / NT);
@@ -517,15 +517,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kXThreads, 1) tcx_ge
                             umma2_f16(dacc, umma_desc_sw64(st + kXWOff + o), umma_desc_sw64(st + o), idesc,
                                       (kk | ki) ? 1u : 0u);
                         }
-                        umma2_commit_pair(R.empty(it));
+                        umma2_commit(R.empty(it));
+                        umma2_commit(p_empty0 + 8u * (uint32_t)(it % kXStages));
                     }
-                    if (healthy) umma2_commit_pair(acc_full + 8u * b);
+                    if (healthy) {
+                        umma2_commit(acc_full + 8u * b);
+                        umma2_commit(p_acc_full + 8u * b);
+                    }
                 }
                 // the epilogues' last releases have landed before the leader may exit
                 for (int j = tl - 2 > 0 ? tl - 2 : 0; j < tl && healthy; j++)
                     if (!tc_mbar_wait(acc_empty + 8u * (j & 1), (uint32_t)((j >> 1) & 1))) healthy = false;
                 // every MMA issued has completed (and so no longer reads either CTA's stages) before TMEM is freed
-                umma2_commit_pair(drain);
+                umma2_commit(drain);
+                umma2_commit(peer_addr(drain, 1));
             } else {
                 // relay: each stage of this CTA full (its X rows landed, its W rows written) -> the leader's barrier
                 const uint32_t lead_full0 = peer_addr(R.full(0), 0);
