@@ -10,7 +10,7 @@
 //
 // Mapping: a lane owns one weight row and walks K in order, so every output is the reference's own chunk-ordered
 // sum, reproducible bit for bit by a scalar loop.  A warp owns 32 rows of one expert ("slot") and up to 4 of the
-// slot's tokens: a work unit.  CTAs are persistent (one of 16 warps per SM); warps take units from a global counter
+// slot's tokens: a work unit.  CTAs are persistent (one of 24 warps per SM); warps take units from a global counter
 // as they go, the slots with the most tokens first, so the expensive units start early and every warp stays busy
 // until the last units are handed out.
 //
@@ -134,9 +134,9 @@ __global__ void iq2_pack_k(const uint8_t* __restrict__ raw, uint8_t* __restrict_
 // ---------------------------------------------------------------------------------------------------------
 // the GEMV
 // ---------------------------------------------------------------------------------------------------------
-constexpr int kGemvWarps = 16;              // one persistent CTA of 16 warps an SM
-constexpr int kStages = 3;                  // ring stages a warp (kStages - 1 super-blocks in flight)
-constexpr int kUnitTok = 4;                 // most tokens a work unit dots
+constexpr int kGemvWarps = 24;              // one persistent CTA of 24 warps an SM (80 registers a thread)
+constexpr int kStages = 2;                  // ring stages a warp (one super-block in flight while one is read)
+constexpr int kUnitTok = kIq2UnitTok;       // most tokens a work unit dots
 constexpr int kStageAct = kIq2Unit;                       // 2112: tokens' int8 rows (kUnitTok x 256 B)
 constexpr int kStageScl = kStageAct + kUnitTok * 256;     // 3136: their scales (kUnitTok x 32 B)
 constexpr int kStageBytes = kStageScl + kUnitTok * 32;    // 3264
@@ -278,8 +278,11 @@ struct Ring {
     uint32_t bar0;           // the first stage's barrier (the others 8 bytes apart)
     int slot, consumed, issued;
     uint32_t par;
-    static_assert(kStages == 3, "stage() selects among three stages");
-    __device__ __forceinline__ uint32_t stage() const { return slot == 0 ? st[0] : slot == 1 ? st[1] : st[2]; }
+    static_assert(kStages == 2 || kStages == 3, "stage() selects among two or three stages");
+    __device__ __forceinline__ uint32_t stage() const {
+        if constexpr (kStages == 2) return slot == 0 ? st[0] : st[1];
+        else return slot == 0 ? st[0] : slot == 1 ? st[1] : st[2];
+    }
     __device__ __forceinline__ uint32_t bar() const { return bar0 + 8u * (uint32_t)slot; }
     __device__ __forceinline__ void advance() {
         consumed++;
@@ -316,8 +319,12 @@ struct Producer {
     int xoff[kUnitTok];      // element offsets of its tokens' next int8 blocks (from a.xq) and scales (from a.xs)
     int soff[kUnitTok];
 
+    // A warp's first unit is fixed, warp w of CTA b taking unit w * gridDim + b (consecutive units, the heaviest
+    // first, land on different SMs), so a launch does not open with every warp of the GPU contending for one
+    // counter; the counter hands out the units after those.
     __device__ __forceinline__ void grab(const GemvArgs& a, const Sched& sc) {
-        const int u = atomicAdd(&g_unit_ctr[a.ctr][0], 1);
+        const int u = pn == 0 ? (int)(threadIdx.x >> 5) * (int)gridDim.x + (int)blockIdx.x
+                              : (int)gridDim.x * kGemvWarps + atomicAdd(&g_unit_ctr[a.ctr][0], 1);
         int* e = queue + (pn % kQueue) * kQEntry;
         pn++;
         if (u >= sc.U) {
@@ -329,13 +336,14 @@ struct Producer {
             return;
         }
         const Unit w = decode_unit(u, sc.order, sc.upre, sc.cnt, sc.nslots, sc.G);
-        const int base = a.counts ? a.offsets[w.s] : 0;
+        // offsets and order are read at L2 (cg): they may be taken before this grid waits for its predecessor
+        const int base = a.counts ? __ldcg(a.offsets + w.s) : 0;
         e[0] = w.g;
         e[1] = w.nt;
 #pragma unroll
         for (int m = 0; m < kUnitTok; m++) {
             const int mm = m < w.nt ? m : 0;
-            const int id = a.counts ? a.order[base + w.b0 + mm] : w.b0 + mm;
+            const int id = a.counts ? __ldcg(a.order + base + w.b0 + mm) : w.b0 + mm;
             const int arow = id < a.act_split ? id / a.act_div : id - a.act_split + a.act_base;
             e[2 + m] = id;
             xoff[m] = arow * a.k;
@@ -529,42 +537,27 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) iq2_gemv_k(GemvArgs a, int
     build_table(reinterpret_cast<uint32_t*>(dyn + (kTblAddr - base)));
     const uint32_t kc = (base + (uint32_t)((const unsigned char*)(s_queue + kGemvWarps * kQueue * kQEntry) - dyn) + 7u) & ~7u;
     if (tid == 0) asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(kc), "r"(0xF82B1908u), "r"(0x0000D5E7u) : "memory");
-    pdl_wait();
+    // With a schedule whose inputs an earlier launch wrote, the schedule and each warp's first unit are taken while
+    // the preceding launch still runs; only the bulk copies wait for it.
+    const bool early = a.sched != nullptr && a.sched_early;
+    if (!early) pdl_wait();
     const int G = a.n / kIq2Tile, nsb = a.k >> 8;
     for (int s = tid; s < nslots; s += blockDim.x) {
-        int cnt = a.counts ? a.counts[s] : a.dense_rows;
+        int cnt = a.counts ? __ldcg(a.counts + s) : a.dense_rows;
         if (slot_weights(a, s) == nullptr) cnt = 0;
         s_cnt[s] = cnt;
     }
-    __syncthreads();
-    // the slots by token count, largest first (ties by index), and the exclusive prefix of their unit counts
-    for (int s = tid; s < nslots; s += blockDim.x) {
-        const int c = s_cnt[s];
-        int rank = 0;
-        for (int o = 0; o < nslots; o++) {
-            const int co = s_cnt[o];
-            rank += (co > c || (co == c && o < s)) ? 1 : 0;
+    if (a.sched) {
+        for (int i = tid; i <= nslots; i += blockDim.x) {
+            if (i < nslots) s_order[i] = __ldcg(a.sched + i);
+            s_upre[i] = __ldcg(a.sched + nslots + i);
         }
-        s_order[rank] = s;
+    } else {
+        __syncthreads();
+        iq2_schedule_slots(s_cnt, nslots, s_order, s_upre, s_order);
     }
     __syncthreads();
-    if (warp == 0) {
-        // warp-wide exclusive scan of the ordered slots' unit counts
-        int carry = 0;
-        for (int i0 = 0; i0 < nslots; i0 += 32) {
-            const int i = i0 + lane;
-            const int v = i < nslots ? G * ((s_cnt[s_order[i]] + kUnitTok - 1) / kUnitTok) : 0;
-            int incl = v;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += y;
-            }
-            if (i < nslots) s_upre[i] = carry + incl - v;
-            carry += __shfl_sync(0xffffffffu, incl, 31);
-        }
-        if (lane == 0) s_upre[nslots] = carry;
-    }
+    for (int i = tid; i <= nslots; i += blockDim.x) s_upre[i] *= G;   // batches -> units (batch, row group)
     __syncthreads();
     Sched sc;
     sc.cnt = s_cnt;
@@ -578,8 +571,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) iq2_gemv_k(GemvArgs a, int
     pr.queue = s_queue + warp * kQueue * kQEntry;
     pr.pn = 0;
     pr.left = 0;
+    if (lane == 0) pr.grab(a, sc);
+    if (early) pdl_wait();
     if (lane == 0) {
-        pr.grab(a, sc);
 #pragma unroll
         for (int i = 0; i < kStages; i++) pr.issue(a, sc, r.st[i], r.bar0 + 8u * (uint32_t)i, r);
     }

@@ -28,7 +28,57 @@ struct GemvArgs {
     float* as;
     int32_t* dots;      // epi 3: [ids][n][k/32] int32 chunk dots
     int ctr;            // the launch slot of the unit counter (set by launch_iq2_gemv)
+    // Optional schedule (iq2_schedule_slots): sched[0 .. nslots) the slots by token count, largest first,
+    // sched[nslots .. 2 nslots] the exclusive prefix of their batch counts.  nullptr: the kernel derives it.
+    const int* sched;
+    // 1: counts, offsets, order and sched were written by an earlier launch on the stream than the one this launch
+    // follows, so the kernel takes its schedule and first unit before waiting for that launch
+    int sched_early;
 };
+
+constexpr int kIq2UnitTok = 4;   // tokens a GEMV work unit dots at most (a slot's tokens come in batches of this many)
+
+// The GEMVs' slot schedule, computed by one CTA (all its threads call it; counts readable by all of them):
+// order[0 .. nslots) the slots by token count, largest first (ties to the lower index), and bpre[0 .. nslots] the
+// exclusive prefix of their batch counts ceil(count / kIq2UnitTok) in that order.  rank_tmp: nslots ints of shared
+// memory (it may be order itself when order is in shared memory).
+__device__ inline void iq2_schedule_slots(const int* counts, int nslots, int* order, int* bpre, int* rank_tmp) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    // a slot's rank is counted by a warp, 32 other slots a ballot
+    for (int s = warp; s < nslots; s += nw) {
+        const int c = counts[s];
+        int rank = 0;
+        for (int o0 = 0; o0 < nslots; o0 += 32) {
+            const int o = o0 + lane;
+            const int co = o < nslots ? counts[o] : -1;
+            rank += __popc(__ballot_sync(0xffffffffu, co > c || (co == c && o < s)));
+        }
+        if (lane == 0) rank_tmp[rank] = s;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        // warp-wide exclusive scan of the ordered slots' batch counts
+        int carry = 0;
+        for (int i0 = 0; i0 < nslots; i0 += 32) {
+            const int i = i0 + lane;
+            const int s = i < nslots ? rank_tmp[i] : 0;
+            const int v = i < nslots ? (counts[s] + kIq2UnitTok - 1) / kIq2UnitTok : 0;
+            int incl = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            if (i < nslots) {
+                order[i] = s;
+                bpre[i] = carry + incl - v;
+            }
+            carry += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (lane == 0) bpre[nslots] = carry;
+    }
+}
+
 
 // epi: 0 store, 1 relu^2, 2 relu^2 + int8 per 32, 3 chunk dots.  maxcnt bounds a slot's ids (the staging size).
 cudaError_t launch_iq2_gemv(const GemvArgs& a, int nslots, int maxcnt, int epi, cudaStream_t s);

@@ -239,14 +239,14 @@ __global__ void group_scatter_k(const int* __restrict__ ridx, int pairs, const i
 }
 
 // ---------------------------------------------------------------------------------------------------------
-// decode prologue, one launch: block 0 routes every token (a warp per token) and groups the pairs; the other
-// blocks write the int8 rows of x (a warp per 32-group).
+// decode prologue, one launch: block 0 routes every token (a warp per token), groups the pairs and orders the
+// expert GEMVs' slots (iq2_schedule_slots); the other blocks write the int8 rows of x (a warp per 32-group).
 // ---------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(512) moe_prep_k(const void* __restrict__ x, const void* __restrict__ logits, int T, int H,
                                                   int E, int topk, int route, const float* __restrict__ bias, float scale,
                                                   int extra, int* __restrict__ ridx, float* __restrict__ rw,
                                                   int* __restrict__ counts, int* __restrict__ offsets, int* __restrict__ order,
-                                                  int8_t* __restrict__ xq, float* __restrict__ xs) {
+                                                  int8_t* __restrict__ xq, float* __restrict__ xs, int* __restrict__ sched) {
     pdl_wait();
     __shared__ int ridx_s[1024], place_s[1024], run_s[512], warp_s[16];   // T * topk <= 64 * 16
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -257,6 +257,13 @@ __global__ void __launch_bounds__(512) moe_prep_k(const void* __restrict__ x, co
         }
         __syncthreads();
         group_pairs(ridx_s, T * topk, E, extra, counts, offsets, order, place_s, run_s, warp_s);
+        // the expert GEMVs' schedule, once for both, from the counts this block wrote (visible after the barrier)
+        // copied into shared memory
+        const int nsl = E + (extra > 0 ? 1 : 0);
+        __syncthreads();
+        for (int i = threadIdx.x; i < nsl; i += blockDim.x) place_s[i] = counts[i];
+        __syncthreads();
+        iq2_schedule_slots(place_s, nsl, sched, sched + nsl, ridx_s);
     } else {
         const int groups = H >> 5;
         const int gw = (blockIdx.x - 1) * 16 + warp;
@@ -306,6 +313,7 @@ __global__ void combine_k(const float* __restrict__ mo, const float* __restrict_
 struct DecodeWs {
     int* ridx; float* rw; int* counts; int* offsets; int* order;
     int8_t* xq; float* xs; int8_t* aq; float* as; float* mo;
+    int* sched;   // the expert GEMVs' slot schedule (2 nslots + 1 ints)
     size_t bytes;
 };
 static size_t al(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -323,6 +331,7 @@ static DecodeWs decode_ws(char* base, int T, int H, int F, int E, int topk) {
     w.aq = (int8_t*)(base + o); o += al(ids * F);
     w.as = (float*)(base + o); o += al(ids * (F / 32) * 4);
     w.mo = (float*)(base + o); o += al(ids * H * 4);
+    w.sched = (int*)(base + o); o += al((size_t)(2 * (E + 1) + 1) * 4);
     w.bytes = o;
     return w;
 }
@@ -433,7 +442,7 @@ int b200q_moe_decode(const void* x, const void* logits, const void* up, const vo
     // 1. router + grouping (block 0) and the int8 rows of x (the rest)
     const int qwarps = T * (H / 32);
     launch(moe_prep_k, dim3(1 + (qwarps + 15) / 16), dim3(512), 0, s, x, logits, T, H, E, topk, route, bias, scale, extra,
-           w.ridx, w.rw, w.counts, w.offsets, w.order, w.xq, w.xs);
+           w.ridx, w.rw, w.counts, w.offsets, w.order, w.xq, w.xs, w.sched);
     if ((st = launched()) != B200Q_OK) return st;
     if ((st = mark(1)) != B200Q_OK) return st;
 
@@ -442,6 +451,7 @@ int b200q_moe_decode(const void* x, const void* logits, const void* up, const vo
     a.slab = (const uint8_t*)up; a.expert_bytes = iq2_bytes(F, H); a.extra_w = (const uint8_t*)shared_up;
     a.nslot_routed = E; a.n = F; a.k = H; a.counts = w.counts; a.offsets = w.offsets; a.order = w.order;
     a.act_div = topk; a.act_split = pairs; a.act_base = 0; a.xq = w.xq; a.xs = w.xs; a.aq = w.aq; a.as = w.as;
+    a.sched = w.sched;   // written by the prologue, the launch this one follows: read after the wait
     if ((st = status_from(launch_iq2_gemv(a, nslots, maxcnt, 2, s))) != B200Q_OK) return st;
     if ((st = mark(2)) != B200Q_OK) return st;
 
@@ -450,6 +460,9 @@ int b200q_moe_decode(const void* x, const void* logits, const void* up, const vo
     b.slab = (const uint8_t*)down; b.expert_bytes = iq2_bytes(H, F); b.extra_w = (const uint8_t*)shared_down;
     b.nslot_routed = E; b.n = H; b.k = F; b.counts = w.counts; b.offsets = w.offsets; b.order = w.order;
     b.act_div = 1; b.act_split = 1 << 30; b.xq = w.aq; b.xs = w.as; b.y = w.mo; b.ldy = H;
+    // the prologue's schedule and grouping are two launches back: the down GEMV takes its schedule and first unit
+    // while the up GEMV finishes
+    b.sched = w.sched; b.sched_early = 1;
     if ((st = status_from(launch_iq2_gemv(b, nslots, maxcnt, 0, s))) != B200Q_OK) return st;
     if ((st = mark(3)) != B200Q_OK) return st;
 
