@@ -9,8 +9,9 @@
 // acc = fma(dA * s, (float)dot, acc).
 //
 // Mapping: a lane owns one weight row and walks K in order, so every output is the reference's own chunk-ordered
-// sum, reproducible bit for bit by a scalar loop.  A warp owns 32 rows of one expert ("slot") and up to 4 of the
-// slot's tokens: a work unit.  CTAs are persistent (one of 24 warps per SM); warps take units from a global counter
+// sum, reproducible bit for bit by a scalar loop.  A warp owns 32 rows of one expert ("slot") and up to 3 of the
+// slot's tokens: a work unit (at three, not four, the units of the 16-token shared expert no longer outlast the
+// routed experts' second wave of units).  CTAs are persistent (one of 24 warps per SM); warps take units from a global counter
 // as they go, the slots with the most tokens first, so the expensive units start early and every warp stays busy
 // until the last units are handed out.
 //
@@ -138,8 +139,8 @@ constexpr int kGemvWarps = 24;              // one persistent CTA of 24 warps an
 constexpr int kStages = 2;                  // ring stages a warp (one super-block in flight while one is read)
 constexpr int kUnitTok = kIq2UnitTok;       // most tokens a work unit dots
 constexpr int kStageAct = kIq2Unit;                       // 2112: tokens' int8 rows (kUnitTok x 256 B)
-constexpr int kStageScl = kStageAct + kUnitTok * 256;     // 3136: their scales (kUnitTok x 32 B)
-constexpr int kStageBytes = kStageScl + kUnitTok * 32;    // 3264
+constexpr int kStageScl = kStageAct + kUnitTok * 256;     // their scales (kUnitTok x 32 B)
+constexpr int kStageBytes = kStageScl + kUnitTok * 32;    // 2976 at three tokens
 constexpr int kMaxSlots = 520;
 // Shared memory: the 64 KB table sits at the fixed shared address kTblAddr, so one prmt builds a lookup address
 // (table base, index byte, lane offset) with no add.  Below it: the ring barriers, the slot counts and prefix, and
@@ -587,12 +588,11 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) iq2_gemv_k(GemvArgs a, int
         Ids id;
 #pragma unroll
         for (int m = 0; m < kUnitTok; m++) id.v[m] = e[2 + m];
-        switch (nt) {
-            case 1: healthy = unit_rows<1, EPI>(a, g, id, lane, r, pr, sc, nsb); break;
-            case 2: healthy = unit_rows<2, EPI>(a, g, id, lane, r, pr, sc, nsb); break;
-            case 3: healthy = unit_rows<3, EPI>(a, g, id, lane, r, pr, sc, nsb); break;
-            default: healthy = unit_rows<4, EPI>(a, g, id, lane, r, pr, sc, nsb); break;
-        }
+        static_assert(kUnitTok >= 2 && kUnitTok <= 4, "one code path per token count 1 .. kUnitTok");
+        if (nt == 1) healthy = unit_rows<1, EPI>(a, g, id, lane, r, pr, sc, nsb);
+        else if (nt == 2 || kUnitTok == 2) healthy = unit_rows<2, EPI>(a, g, id, lane, r, pr, sc, nsb);
+        else if (nt == 3 || kUnitTok == 3) healthy = unit_rows<(kUnitTok < 3 ? 2 : 3), EPI>(a, g, id, lane, r, pr, sc, nsb);
+        else healthy = unit_rows<kUnitTok, EPI>(a, g, id, lane, r, pr, sc, nsb);
     }
     if (!healthy) {
         // a stage never filled: flag it, and let this warp's copies in flight land before the CTA's memory goes away

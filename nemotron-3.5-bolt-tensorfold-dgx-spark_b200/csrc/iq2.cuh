@@ -36,7 +36,7 @@ struct GemvArgs {
     int sched_early;
 };
 
-constexpr int kIq2UnitTok = 4;   // tokens a GEMV work unit dots at most (a slot's tokens come in batches of this many)
+constexpr int kIq2UnitTok = 3;   // tokens a GEMV work unit dots at most (a slot's tokens come in batches of this many)
 
 // The GEMVs' slot schedule, computed by one CTA (all its threads call it; counts readable by all of them):
 // order[0 .. nslots) the slots by token count, largest first (ties to the lower index), and bpre[0 .. nslots] the

@@ -139,7 +139,7 @@ __global__ void route_k(const void* __restrict__ logits, int dtype, int ldl, con
 // Shared memory: ridx_s[pairs] (the routing), place_s[pairs], run_s[512], warp_s[16].
 // ---------------------------------------------------------------------------------------------------------
 __device__ void group_pairs(const int* ridx_s, int pairs, int E, int extra, int* counts, int* offsets, int* order,
-                            int* place_s, int* run_s, int* warp_s) {
+                            int* place_s, int* run_s, int* warp_s, int* counts_s = nullptr) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     run_s[tid] = 0;
     __syncthreads();
@@ -176,7 +176,9 @@ __device__ void group_pairs(const int* ridx_s, int pairs, int E, int extra, int*
     if (tid < E) {
         counts[tid] = c;
         offsets[tid] = start;
+        if (counts_s) counts_s[tid] = c;   // a shared-memory copy for the caller (slot E: extra)
     }
+    if (counts_s && tid == 0) counts_s[E] = extra;
     __syncthreads();
     run_s[tid] = start;   // reused: the offsets, for the scatter
     __syncthreads();
@@ -248,7 +250,7 @@ __global__ void __launch_bounds__(512) moe_prep_k(const void* __restrict__ x, co
                                                   int* __restrict__ counts, int* __restrict__ offsets, int* __restrict__ order,
                                                   int8_t* __restrict__ xq, float* __restrict__ xs, int* __restrict__ sched) {
     pdl_wait();
-    __shared__ int ridx_s[1024], place_s[1024], run_s[512], warp_s[16];   // T * topk <= 64 * 16
+    __shared__ int ridx_s[1024], place_s[1024], run_s[512], warp_s[16], cnt_s[513];   // T * topk <= 64 * 16
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (blockIdx.x == 0) {
         for (int t = warp; t < T; t += 16) {
@@ -256,14 +258,11 @@ __global__ void __launch_bounds__(512) moe_prep_k(const void* __restrict__ x, co
             else route_token<16>(logits, B200Q_BF16, E, bias, E, topk, route, scale, t, lane, ridx, rw, ridx_s);
         }
         __syncthreads();
-        group_pairs(ridx_s, T * topk, E, extra, counts, offsets, order, place_s, run_s, warp_s);
-        // the expert GEMVs' schedule, once for both, from the counts this block wrote (visible after the barrier)
-        // copied into shared memory
+        group_pairs(ridx_s, T * topk, E, extra, counts, offsets, order, place_s, run_s, warp_s, cnt_s);
+        // the expert GEMVs' schedule, once for both, from the counts kept in shared memory
         const int nsl = E + (extra > 0 ? 1 : 0);
         __syncthreads();
-        for (int i = threadIdx.x; i < nsl; i += blockDim.x) place_s[i] = counts[i];
-        __syncthreads();
-        iq2_schedule_slots(place_s, nsl, sched, sched + nsl, ridx_s);
+        iq2_schedule_slots(cnt_s, nsl, sched, sched + nsl, ridx_s);
     } else {
         const int groups = H >> 5;
         const int gw = (blockIdx.x - 1) * 16 + warp;
