@@ -227,6 +227,19 @@ int b200q_moe_decode(const void* x, const void* logits, const void* up, const vo
                      float scale, void* out, int out_dtype, void* workspace, size_t workspace_bytes, int* ridx_out,
                      float* rw_out, void* const* stage_events, void* stream);
 
+/* The routed experts of one rank of the expert-parallel decode layer over the rows it received (no counterpart in
+ * libbolt, which is single-GPU; the operators are moe_up / moe_down of bolt_kernels.cu:682-695 with libbolt's grouping,
+ * k_moe_group :275-344, fused as b200q_moe_decode fuses them): row r goes through local expert lidx[r] (up, relu^2,
+ * int8 rows, down) into y[r]; an lidx outside 0 .. n_local - 1 marks a padding row, left unwritten.  Three launches:
+ * grouping + slot schedule + int8 rows of the input, the up GEMV, the down GEMV.
+ *   rows [R][ldr] fp32 or bf16, R <= 4096; lidx [R] int32; up [n_local] x [F][H], down [n_local] x [H][F] packed
+ *   rt32, n_local <= 511; y [R][ldy] fp32.  workspace >= b200q_moe_experts_workspace_bytes(R, H, F, n_local),
+ *   256-byte aligned. */
+size_t b200q_moe_experts_workspace_bytes(int R, int H, int F, int n_local);
+int b200q_moe_experts_decode(const void* rows, int rows_dtype, int ldr, int R, int H, int F, const int* lidx,
+                             int n_local, const void* up, const void* down, float* y, int ldy, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
 /* The decode MoE layer without a caller-provided workspace, for callers that cannot allocate device memory (a host
  * whose allocator owns the GPU's memory, a plugin that receives only tensors, a loop that must not take cudaMalloc's
  * implicit synchronisation).  No counterpart in the reference: libbolt allocates its own scratch at bolt_open.

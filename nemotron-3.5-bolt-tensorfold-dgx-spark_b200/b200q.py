@@ -53,6 +53,8 @@ def lib():
             "b200q_moe_up_q8": (i32, [vp, i32, i32, i32, vp, vp, vp, i32, vp, vp, vp, vp, vp]),
             "b200q_moe_down": (i32, [vp, i32, i32, i32, vp, vp, vp, vp, vp, vp, i32, vp]),
             "b200q_moe_decode_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
+            "b200q_moe_experts_workspace_bytes": (sz, [i32, i32, i32, i32]),
+            "b200q_moe_experts_decode": (i32, [vp, i32, i32, i32, i32, i32, vp, i32, vp, vp, vp, i32, vp, sz, vp]),
             "b200q_moe_decode": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, f32, vp, i32, vp, sz,
                                        vp, vp, vp, vp]),
             "b200q_synth_iq2_host": (None, [ctypes.c_uint64, i64, vp]),
@@ -235,6 +237,35 @@ def moe_down(slab, E, n, k, counts, offsets, order, aq, as_):
     _check(lib().b200q_moe_down(_p(slab), E, n, k, _p(counts), _p(offsets), _p(order), _p(aq), _p(as_), _p(y), n, _s()),
            "moe_down")
     return y[:pairs]
+
+
+class ExpertsDecode:
+    """The routed experts of one rank of the expert-parallel decode layer (b200q_moe_experts_decode): the received
+    rows through their local experts, up, relu^2, down.  The workspace grows to the largest row count seen."""
+
+    def __init__(self, up, down, n_local, H, F):
+        self.up, self.down, self.n, self.H, self.F = up, down, n_local, H, F
+        self.buf, self.ptr, self.nbytes = None, None, 0
+
+    def __call__(self, rows, lidx, y=None):
+        """rows [R][H] fp32 or bf16 (each row contiguous, any row stride), lidx [R] int32 (n_local or more: padding)
+        -> y [R][H] fp32 (padding rows unwritten)"""
+        _dev(rows, "rows", rows=True)
+        R = rows.shape[0]
+        y = torch.empty(R, self.H, dtype=torch.float32, device=rows.device) if y is None else y
+        if R == 0:
+            return y
+        need = lib().b200q_moe_experts_workspace_bytes(R, self.H, self.F, self.n)
+        if self.buf is None or self.nbytes < need or self.buf.device != rows.device:
+            self.buf = torch.empty(need + 256, dtype=torch.uint8, device=rows.device)
+            self.ptr = self.buf.data_ptr() + (-self.buf.data_ptr()) % 256
+            self.nbytes = need
+        li = (lidx if lidx.dtype == torch.int32 else lidx.to(torch.int32)).contiguous()
+        _check(lib().b200q_moe_experts_decode(_p(rows), _dtype_code(rows), rows.stride(0), R, self.H, self.F,
+                                              _p(li), self.n, _p(self.up), _p(self.down), _p(y),
+                                              y.stride(0), ctypes.c_void_p(self.ptr), self.nbytes, _s()),
+               "moe_experts_decode")
+        return y
 
 
 # -------------------------------------------------------------------------------------------------------------

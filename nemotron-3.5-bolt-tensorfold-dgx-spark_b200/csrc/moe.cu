@@ -276,6 +276,40 @@ __global__ void __launch_bounds__(512) moe_prep_k(const void* __restrict__ x, co
 }
 
 // ---------------------------------------------------------------------------------------------------------
+// the expert-parallel prologue over a rank's received rows, one launch: block 0 groups the rows by their local expert
+// (lidx; an index outside 0 .. n_local - 1 is padding, grouped into slot n_local and never computed) and orders the
+// GEMVs' slots; the other blocks write the int8 rows.
+// ---------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(512) moe_local_prep_k(const void* __restrict__ rows, int dtype, int ldr, int R, int H,
+                                                        const int* __restrict__ lidx, int n_local,
+                                                        int* __restrict__ counts, int* __restrict__ offsets,
+                                                        int* __restrict__ order, int8_t* __restrict__ xq,
+                                                        float* __restrict__ xs, int* __restrict__ sched) {
+    pdl_wait();
+    __shared__ int ridx_s[4096], place_s[4096], run_s[512], warp_s[16], cnt_s[513];   // R <= 4096
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (blockIdx.x == 0) {
+        for (int i = threadIdx.x; i < R; i += blockDim.x) {
+            const int l = lidx[i];
+            ridx_s[i] = (l < 0 || l > n_local) ? n_local : l;
+        }
+        __syncthreads();
+        group_pairs(ridx_s, R, n_local + 1, 0, counts, offsets, order, place_s, run_s, warp_s, cnt_s);
+        __syncthreads();
+        iq2_schedule_slots(cnt_s, n_local, sched, sched + n_local, ridx_s);
+    } else {
+        const int groups = H >> 5;
+        const int gw = (blockIdx.x - 1) * 16 + warp;
+        if (gw < R * groups) {
+            const int r = gw / groups, g = gw - r * groups;
+            const float v = load_act(rows, dtype, (size_t)r * ldr + g * 32 + lane);
+            quant_group(v, lane, xq + (size_t)r * H + g * 32, xs + (size_t)r * (H >> 5) + g);
+        }
+    }
+    pdl_trigger();
+}
+
+// ---------------------------------------------------------------------------------------------------------
 // combine (combine_k, bolt_kernels.cu:1714-1727): out[t][h] = sum_k rw[t][k] mo[t*topk+k][h] (+ shared[t][h])
 // ---------------------------------------------------------------------------------------------------------
 __global__ void combine_k(const float* __restrict__ mo, const float* __restrict__ rw, const float* __restrict__ shared, int T,
@@ -331,6 +365,25 @@ static DecodeWs decode_ws(char* base, int T, int H, int F, int E, int topk) {
     w.as = (float*)(base + o); o += al(ids * (F / 32) * 4);
     w.mo = (float*)(base + o); o += al(ids * H * 4);
     w.sched = (int*)(base + o); o += al((size_t)(2 * (E + 1) + 1) * 4);
+    w.bytes = o;
+    return w;
+}
+
+struct ExpertsWs {
+    int* counts; int* offsets; int* order; int8_t* xq; float* xs; int8_t* aq; float* as; int* sched;
+    size_t bytes;
+};
+static ExpertsWs experts_ws(char* base, int R, int H, int F, int n_local) {
+    ExpertsWs w;
+    size_t o = 0;
+    w.counts = (int*)(base + o); o += al((size_t)(n_local + 1) * 4);
+    w.offsets = (int*)(base + o); o += al((size_t)(n_local + 2) * 4);
+    w.order = (int*)(base + o); o += al((size_t)R * 4);
+    w.xq = (int8_t*)(base + o); o += al((size_t)R * H);
+    w.xs = (float*)(base + o); o += al((size_t)R * (H / 32) * 4);
+    w.aq = (int8_t*)(base + o); o += al((size_t)R * F);
+    w.as = (float*)(base + o); o += al((size_t)R * (F / 32) * 4);
+    w.sched = (int*)(base + o); o += al((size_t)(2 * n_local + 1) * 4);
     w.bytes = o;
     return w;
 }
@@ -408,6 +461,44 @@ int b200q_combine(const float* mo, const float* rw, const float* shared, int T, 
     launch(combine_k, dim3((H / 4 + 255) / 256, T), dim3(256), 0, (cudaStream_t)stream, mo, rw, shared, T, topk, H, out,
            out_dtype);
     return launched();
+}
+
+size_t b200q_moe_experts_workspace_bytes(int R, int H, int F, int n_local) {
+    if (R <= 0 || H <= 0 || F <= 0 || n_local <= 0) return 0;
+    return experts_ws(nullptr, R, H, F, n_local).bytes;
+}
+
+int b200q_moe_experts_decode(const void* rows, int rows_dtype, int ldr, int R, int H, int F, const int* lidx,
+                             int n_local, const void* up, const void* down, float* y, int ldy, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+    if (R < 0 || R > 4096 || n_local <= 0 || n_local > 511 || !iq2_shape_ok(F, H) || !iq2_shape_ok(H, F) ||
+        (rows_dtype != B200Q_F32 && rows_dtype != B200Q_BF16))
+        return B200Q_EINVAL;
+    if (R == 0) return B200Q_OK;
+    if (!rows || !lidx || !up || !down || !y || !workspace || ldr < H || ldy < H || ((uintptr_t)workspace & 255) ||
+        ((uintptr_t)up & 15) || ((uintptr_t)down & 15) || ((uintptr_t)y & 15))
+        return B200Q_EINVAL;
+    ExpertsWs w = experts_ws((char*)workspace, R, H, F, n_local);
+    if (workspace_bytes < w.bytes) return B200Q_ENOSPACE;
+    cudaStream_t s = (cudaStream_t)stream;
+    int st;
+    // 1. grouping by local expert, the slot schedule, the int8 rows
+    const int qwarps = R * (H / 32);
+    launch(moe_local_prep_k, dim3(1 + (qwarps + 15) / 16), dim3(512), 0, s, rows, rows_dtype, ldr, R, H, lidx, n_local,
+           w.counts, w.offsets, w.order, w.xq, w.xs, w.sched);
+    if ((st = launched()) != B200Q_OK) return st;
+    // 2. up with relu^2 and the int8 rows of the result, row id = received row
+    GemvArgs a = {};
+    a.slab = (const uint8_t*)up; a.expert_bytes = iq2_bytes(F, H); a.nslot_routed = n_local; a.n = F; a.k = H;
+    a.counts = w.counts; a.offsets = w.offsets; a.order = w.order; a.act_div = 1; a.act_split = 1 << 30;
+    a.xq = w.xq; a.xs = w.xs; a.aq = w.aq; a.as = w.as; a.sched = w.sched;
+    if ((st = status_from(launch_iq2_gemv(a, n_local, 16, 2, s))) != B200Q_OK) return st;
+    // 3. down: the prologue's schedule is two launches back, taken before the down GEMV waits for the up GEMV
+    GemvArgs b = {};
+    b.slab = (const uint8_t*)down; b.expert_bytes = iq2_bytes(H, F); b.nslot_routed = n_local; b.n = H; b.k = F;
+    b.counts = w.counts; b.offsets = w.offsets; b.order = w.order; b.act_div = 1; b.act_split = 1 << 30;
+    b.xq = w.aq; b.xs = w.as; b.y = y; b.ldy = ldy; b.sched = w.sched; b.sched_early = 1;
+    return status_from(launch_iq2_gemv(b, n_local, 16, 0, s));
 }
 
 size_t b200q_moe_decode_workspace_bytes(int T, int H, int F, int E, int topk) {

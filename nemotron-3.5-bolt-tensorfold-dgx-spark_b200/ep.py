@@ -221,15 +221,16 @@ class LocalExperts:
 
     def __init__(self, up, down, n_local, H, F):
         self.up, self.down, self.n, self.H, self.F = up, down, n_local, H, F
+        self._dec = None
 
     def decode(self, rows, lidx, n_local):
+        """b200q_moe_experts_decode: grouping, slot schedule and int8 rows in one launch, then the two GEMVs"""
         import b200q
         if rows.shape[0] == 0 or self.n == 0:
             return torch.zeros(rows.shape[0], self.H, dtype=torch.float32, device=rows.device)
-        xq, xs = b200q.k_quant_rows(rows)
-        counts, offsets, order = b200q.k_moe_group(lidx.to(torch.int32), n_local + 1)
-        aq, as_ = b200q.moe_up_q8(self.up, n_local, self.F, self.H, counts, offsets, order, 1, xq, xs)
-        return b200q.moe_down(self.down, n_local, self.H, self.F, counts, offsets, order, aq, as_)
+        if self._dec is None:
+            self._dec = b200q.ExpertsDecode(self.up, self.down, self.n, self.H, self.F)
+        return self._dec(rows, lidx)
 
     def prompt(self, rows, lidx, n_local):
         import b200q
@@ -248,22 +249,22 @@ def slice_slab(slab, experts, expert_bytes):
 
 
 class SharedExpert:
-    """The shared expert on a rank's own decode tokens: the int8 GEMV pair over one group of all T rows."""
+    """The shared expert on a rank's own decode tokens: the int8 GEMV pair over all T rows as one expert
+    (b200q_moe_experts_decode with every row's local index 0)."""
 
     def __init__(self, up, down, H, F, T, device):
-        self.up, self.down, self.H, self.F = up, down, H, F
-        self.counts = torch.tensor([T], dtype=torch.int32, device=device)
-        self.offsets = torch.tensor([0, T], dtype=torch.int32, device=device)
-        self.order = torch.arange(T, dtype=torch.int32, device=device)
+        self.up, self.down, self.H, self.F, self.T = up, down, H, F, T
+        self.lidx = torch.zeros(T, dtype=torch.int32, device=device)
+        self._dec = None
 
     def __call__(self, x):
         import b200q
         T = x.shape[0]
-        if T != int(self.order.numel()):
-            raise ValueError(f"SharedExpert was built for {int(self.order.numel())} tokens, got {T}")
-        xq, xs = b200q.k_quant_rows(x)
-        aq, as_ = b200q.moe_up_q8(self.up, 1, self.F, self.H, self.counts, self.offsets, self.order[:T], 1, xq, xs)
-        return b200q.moe_down(self.down, 1, self.H, self.F, self.counts, self.offsets, self.order[:T], aq, as_)
+        if T != self.T:
+            raise ValueError(f"SharedExpert was built for {self.T} tokens, got {T}")
+        if self._dec is None:
+            self._dec = b200q.ExpertsDecode(self.up, self.down, 1, self.H, self.F)
+        return self._dec(x, self.lidx)
 
 
 class GraphedStep:

@@ -52,3 +52,42 @@ def test_ep_one_rank_matches_fused_layer(layout, form, dt):
     ref, _, _ = O.moe_layer(xb, lb, up.reshape(-1), down.reshape(-1), su.reshape(-1), sd.reshape(-1), T, H, F, E, topk,
                             mode=0)
     assert_tolerance(got, ref)
+
+
+@pytest.mark.parametrize("R,H,F,n_local,dt", [(40, 512, 256, 5, "bfloat16"), (96, 1024, 2048, 16, "float32"),
+                                              (7, 256, 512, 3, "bfloat16")])
+def test_experts_decode_matches_grouped_gemvs(R, H, F, n_local, dt):
+    """b200q_moe_experts_decode (one prologue: grouping, slot schedule, int8 rows; then the two GEMVs) against the
+    grouped operators it fuses (k_quant_rows, k_moe_group, moe_up_q8, moe_down): the same arithmetic, so the same
+    bytes; padding rows (local index n_local or above) are left alone, one expert gets no rows, and the rows sit at a
+    padded stride as the exchange leaves them"""
+    rng = np.random.default_rng(R + H)
+    up = iq2_blocks(21, n_local * F, H)
+    down = iq2_blocks(22, n_local * H, F)
+    pu = b200q.repack_iq2(dev(up.reshape(-1)), n_local * F, H)
+    pd = b200q.repack_iq2(dev(down.reshape(-1)), n_local * H, F)
+    lidx = rng.integers(0, n_local - 1, R).astype(np.int32)   # expert n_local - 1 gets none
+    lidx[::5] = n_local                                        # padding rows
+    lidx[1::11] = n_local + 7
+    buf = torch.randn(R, H + 64, device=DEV).to(getattr(torch, dt))
+    rows = buf[:, :H]
+    li = dev(lidx)
+    sentinel = torch.full((R, H), 12345.0, device=DEV)
+    got = b200q.ExpertsDecode(pu, pd, n_local, H, F)(rows, li, y=sentinel.clone()).cpu().numpy()
+    # the grouped operators on the same rows (padding grouped into slot n_local and not computed)
+    xq, xs = b200q.k_quant_rows(rows.contiguous())
+    gl = torch.where(li >= n_local, torch.full_like(li, n_local), li)
+    counts, offsets, order = b200q.k_moe_group(gl, n_local + 1)
+    aq, as_ = b200q.moe_up_q8(pu, n_local, F, H, counts, offsets, order, 1, xq, xs)
+    want = b200q.moe_down(pd, n_local, H, F, counts, offsets, order, aq, as_).cpu().numpy()
+    real = lidx < n_local
+    assert np.array_equal(got[real], want[real])
+    assert (got[~real] == 12345.0).all()
+    # and the oracle's int8 arithmetic, row by row
+    xq_n, xs_n = xq.cpu().numpy(), xs.cpu().numpy()
+    ub, db = up.reshape(n_local, -1), down.reshape(n_local, -1)
+    for r in np.nonzero(real)[0][:6]:
+        a = O.iq2_gemm_i8(ub[lidx[r]], F, H, xq_n[r], xs_n[r], 1)
+        aq_r, as_r = O.quant_rows(a, F)
+        assert np.array_equal(got[r], O.iq2_gemm_i8(db[lidx[r]], H, F, aq_r, as_r, 0)[0])
+    assert b200q.device_error() == 0
