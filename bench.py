@@ -333,9 +333,9 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
         moe.timing = evs[:4]
         inner = moe.expert_fn
 
-        def timed(rows, lidx, n, inner=inner):
+        def timed(rows, lidx, n, inner=inner, **kw):
             evs[4].record()
-            y = inner(rows, lidx, n)
+            y = inner(rows, lidx, n, **kw)
             evs[5].record()
             return y
         moe.expert_fn = timed

@@ -232,13 +232,31 @@ int b200q_moe_decode(const void* x, const void* logits, const void* up, const vo
  * k_moe_group :275-344, fused as b200q_moe_decode fuses them): row r goes through local expert lidx[r] (up, relu^2,
  * int8 rows, down) into y[r]; an lidx outside 0 .. n_local - 1 marks a padding row, left unwritten.  Three launches:
  * grouping + slot schedule + int8 rows of the input, the up GEMV, the down GEMV.
- *   rows [R][ldr] fp32 or bf16, R <= 4096; lidx [R] int32; up [n_local] x [F][H], down [n_local] x [H][F] packed
- *   rt32, n_local <= 511; y [R][ldy] fp32.  workspace >= b200q_moe_experts_workspace_bytes(R, H, F, n_local),
- *   256-byte aligned. */
+ *   rows [R][ldr] fp32 or bf16, R <= 4096; lidx: R int32, lidx_stride ints apart (1: an array; b200q_ep_pack's send
+ *   rows carry theirs after the row's values); up [n_local] x [F][H], down [n_local] x [H][F] packed rt32,
+ *   n_local <= 511; y [R][ldy] fp32 or bf16 (y_dtype; bf16 rounded to nearest even).
+ *   workspace >= b200q_moe_experts_workspace_bytes(R, H, F, n_local), 256-byte aligned. */
 size_t b200q_moe_experts_workspace_bytes(int R, int H, int F, int n_local);
 int b200q_moe_experts_decode(const void* rows, int rows_dtype, int ldr, int R, int H, int F, const int* lidx,
-                             int n_local, const void* up, const void* down, float* y, int ldy, void* workspace,
-                             size_t workspace_bytes, void* stream);
+                             int lidx_stride, int n_local, const void* up, const void* down, void* y, int y_dtype,
+                             int ldy, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The expert-parallel decode exchange in its fixed-capacity layout (no counterpart in libbolt), around
+ * b200q_moe_experts_decode and one all-to-all each way:
+ * b200q_ep_pack writes this rank's send buffer: pair p = (t, k) of expert e = ridx[p] goes to rank
+ * d = dest[e * max_rep + t % nrep[e]] as local expert lidx[e * max_rep + t % nrep[e]], into send row d * cap + pos,
+ * pos = its place among the pairs bound for d in pair order (pos < cap is the caller's guarantee: cap = T * topk).
+ * A send row is ldsend elements of send_dtype: x[t]'s H values (converted, bf16 rounded to nearest even), then the
+ * local index as an int32 at element H (2 elements of bf16, 1 of fp32; ldsend >= H + 16 bytes' worth); rows no pair
+ * takes get the index `discard` (>= every rank's local expert count).  slot[p] = the pair's send row.
+ *   x [T][H] fp32 or bf16; ridx [T][topk] int32; dest, lidx [E][max_rep], nrep [E] int32; world * cap send rows.
+ * b200q_ep_combine: out[t] = sum over k in order of rw[t][k] * back[slot[t * topk + k]] (fma, combine_k's order)
+ * (+ shared[t]); back rows ldb elements of back_dtype (the exchange's return buffer), out fp32 or bf16. */
+int b200q_ep_pack(const void* x, int x_dtype, int T, int H, const int* ridx, int topk, const int* dest,
+                  const int* lidx, const int* nrep, int max_rep, int world, int cap, int discard, void* send,
+                  int send_dtype, int ldsend, int* slot, void* stream);
+int b200q_ep_combine(const void* back, int back_dtype, int ldb, const int* slot, const float* rw, const float* shared,
+                     int T, int topk, int H, void* out, int out_dtype, void* stream);
 
 /* The decode MoE layer without a caller-provided workspace, for callers that cannot allocate device memory (a host
  * whose allocator owns the GPU's memory, a plugin that receives only tensors, a loop that must not take cudaMalloc's

@@ -54,7 +54,10 @@ def lib():
             "b200q_moe_down": (i32, [vp, i32, i32, i32, vp, vp, vp, vp, vp, vp, i32, vp]),
             "b200q_moe_decode_workspace_bytes": (sz, [i32, i32, i32, i32, i32]),
             "b200q_moe_experts_workspace_bytes": (sz, [i32, i32, i32, i32]),
-            "b200q_moe_experts_decode": (i32, [vp, i32, i32, i32, i32, i32, vp, i32, vp, vp, vp, i32, vp, sz, vp]),
+            "b200q_moe_experts_decode": (i32, [vp, i32, i32, i32, i32, i32, vp, i32, i32, vp, vp, vp, i32, i32, vp, sz,
+                                               vp]),
+            "b200q_ep_pack": (i32, [vp, i32, i32, i32, vp, i32, vp, vp, vp, i32, i32, i32, i32, vp, i32, i32, vp, vp]),
+            "b200q_ep_combine": (i32, [vp, i32, i32, vp, vp, vp, i32, i32, i32, vp, i32, vp]),
             "b200q_moe_decode": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, f32, vp, i32, vp, sz,
                                        vp, vp, vp, vp]),
             "b200q_synth_iq2_host": (None, [ctypes.c_uint64, i64, vp]),
@@ -247,12 +250,12 @@ class ExpertsDecode:
         self.up, self.down, self.n, self.H, self.F = up, down, n_local, H, F
         self.buf, self.ptr, self.nbytes = None, None, 0
 
-    def __call__(self, rows, lidx, y=None):
-        """rows [R][H] fp32 or bf16 (each row contiguous, any row stride), lidx [R] int32 (n_local or more: padding)
-        -> y [R][H] fp32 (padding rows unwritten)"""
+    def __call__(self, rows, lidx, y=None, out_dtype=torch.float32):
+        """rows [R][H] fp32 or bf16 (each row contiguous, any row stride), lidx [R] int32 at any stride (n_local or
+        more: padding) -> y [R][H] fp32 or bf16 (out_dtype; padding rows unwritten)"""
         _dev(rows, "rows", rows=True)
         R = rows.shape[0]
-        y = torch.empty(R, self.H, dtype=torch.float32, device=rows.device) if y is None else y
+        y = torch.empty(R, self.H, dtype=out_dtype, device=rows.device) if y is None else y
         if R == 0:
             return y
         need = lib().b200q_moe_experts_workspace_bytes(R, self.H, self.F, self.n)
@@ -260,12 +263,48 @@ class ExpertsDecode:
             self.buf = torch.empty(need + 256, dtype=torch.uint8, device=rows.device)
             self.ptr = self.buf.data_ptr() + (-self.buf.data_ptr()) % 256
             self.nbytes = need
-        li = (lidx if lidx.dtype == torch.int32 else lidx.to(torch.int32)).contiguous()
+        li = lidx if lidx.dtype == torch.int32 else lidx.to(torch.int32)
+        if li.dim() != 1 or li.numel() != R:
+            raise B200QError(EINVAL, "lidx must hold one index a row")
         _check(lib().b200q_moe_experts_decode(_p(rows), _dtype_code(rows), rows.stride(0), R, self.H, self.F,
-                                              _p(li), self.n, _p(self.up), _p(self.down), _p(y),
-                                              y.stride(0), ctypes.c_void_p(self.ptr), self.nbytes, _s()),
-               "moe_experts_decode")
+                                              _p(li), max(li.stride(0), 1), self.n, _p(self.up), _p(self.down), _p(y),
+                                              _dtype_code(y), y.stride(0), ctypes.c_void_p(self.ptr), self.nbytes,
+                                              _s()), "moe_experts_decode")
         return y
+
+
+def ep_pack(x, ridx, dest, lidx, nrep, world, cap, discard, send_dtype=torch.bfloat16):
+    """The expert-parallel send buffer (b200q_ep_pack): x [T][H], ridx [T][topk] int32, placement tables dest / lidx
+    [E][max_rep] and nrep [E] (int32) -> send [world * cap][H + 16 bytes] of send_dtype, each row's local index as an
+    int32 after its H values, and slot [T * topk] int32 (each pair's send row)."""
+    _dev(x, "x")
+    T, H = x.shape
+    topk = ridx.shape[-1]
+    pad = 16 // torch.empty(0, dtype=send_dtype).element_size()
+    send = torch.empty(world * cap, H + pad, dtype=send_dtype, device=x.device)
+    slot = torch.empty(T * topk, dtype=torch.int32, device=x.device)
+    _check(lib().b200q_ep_pack(_p(x), _dtype_code(x), T, H, _p(_dev(ridx, "ridx")), topk, _p(_dev(dest, "dest")),
+                               _p(_dev(lidx, "lidx")), _p(_dev(nrep, "nrep")), dest.shape[1], world, cap, int(discard),
+                               _p(send), _dtype_code(send), send.stride(0), _p(slot), _s()), "ep_pack")
+    return send, slot
+
+
+def ep_index_view(buf, H):
+    """the int32 local index b200q_ep_pack stores after the H values of each row of buf, as an [R] strided view"""
+    return buf.view(torch.int32)[:, H * buf.element_size() // 4]
+
+
+def ep_combine(back, slot, rw, topk, shared=None, out_dtype=torch.float32):
+    """out[t] = sum_k rw[t][k] back[slot[t * topk + k]] (+ shared[t]) (b200q_ep_combine): the return buffer's rows
+    weighted in combine_k's order"""
+    _dev(back, "back", rows=True)
+    T = rw.numel() // topk
+    H = back.shape[1]
+    out = torch.empty(T, H, dtype=out_dtype, device=back.device)
+    rwc = rw.contiguous()
+    _check(lib().b200q_ep_combine(_p(back), _dtype_code(back), back.stride(0), _p(slot), _p(rwc), _p(shared), T,
+                                  topk, H, _p(out), _dtype_code(out), _s()), "ep_combine")
+    return out
 
 
 # -------------------------------------------------------------------------------------------------------------

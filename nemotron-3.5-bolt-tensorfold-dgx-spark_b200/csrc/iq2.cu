@@ -497,7 +497,8 @@ __device__ __forceinline__ bool unit_rows(const GemvArgs& a, int g, const Ids& i
                 a.aq[(size_t)id[m] * a.n + row] = (int8_t)__float2int_rn(v * inv);
                 if (lane == 0) a.as[(size_t)id[m] * (a.n >> 5) + g] = am / 127.f;
             } else {
-                a.y[(size_t)id[m] * a.ldy + row] = v;
+                if (a.y_bf16) reinterpret_cast<__nv_bfloat16*>(a.y)[(size_t)id[m] * a.ldy + row] = __float2bfloat16_rn(v);
+                else a.y[(size_t)id[m] * a.ldy + row] = v;
             }
         }
     }

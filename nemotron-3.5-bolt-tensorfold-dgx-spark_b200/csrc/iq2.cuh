@@ -22,7 +22,8 @@ struct GemvArgs {
     int act_split, act_base;
     const int8_t* xq;   // [rows][k] int8
     const float* xs;    // [rows][k/32]
-    float* y;           // [ids][ldy] fp32 (epi 0, 1)
+    float* y;           // [ids][ldy] fp32 (epi 0, 1); bf16 elements when y_bf16
+    int y_bf16;
     int ldy;
     int8_t* aq;         // epi 2: relu^2 rows quantised, [ids][n] int8 and as [ids][n/32]
     float* as;

@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(512) moe_prep_k(const void* __restrict__ x, co
 // GEMVs' slots; the other blocks write the int8 rows.
 // ---------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(512) moe_local_prep_k(const void* __restrict__ rows, int dtype, int ldr, int R, int H,
-                                                        const int* __restrict__ lidx, int n_local,
+                                                        const int* __restrict__ lidx, int lidx_stride, int n_local,
                                                         int* __restrict__ counts, int* __restrict__ offsets,
                                                         int* __restrict__ order, int8_t* __restrict__ xq,
                                                         float* __restrict__ xs, int* __restrict__ sched) {
@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(512) moe_local_prep_k(const void* __restrict__
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (blockIdx.x == 0) {
         for (int i = threadIdx.x; i < R; i += blockDim.x) {
-            const int l = lidx[i];
+            const int l = lidx[(size_t)i * lidx_stride];
             ridx_s[i] = (l < 0 || l > n_local) ? n_local : l;
         }
         __syncthreads();
@@ -469,14 +469,14 @@ size_t b200q_moe_experts_workspace_bytes(int R, int H, int F, int n_local) {
 }
 
 int b200q_moe_experts_decode(const void* rows, int rows_dtype, int ldr, int R, int H, int F, const int* lidx,
-                             int n_local, const void* up, const void* down, float* y, int ldy, void* workspace,
-                             size_t workspace_bytes, void* stream) {
+                             int lidx_stride, int n_local, const void* up, const void* down, void* y, int y_dtype,
+                             int ldy, void* workspace, size_t workspace_bytes, void* stream) {
     if (R < 0 || R > 4096 || n_local <= 0 || n_local > 511 || !iq2_shape_ok(F, H) || !iq2_shape_ok(H, F) ||
-        (rows_dtype != B200Q_F32 && rows_dtype != B200Q_BF16))
+        (rows_dtype != B200Q_F32 && rows_dtype != B200Q_BF16) || (y_dtype != B200Q_F32 && y_dtype != B200Q_BF16))
         return B200Q_EINVAL;
     if (R == 0) return B200Q_OK;
-    if (!rows || !lidx || !up || !down || !y || !workspace || ldr < H || ldy < H || ((uintptr_t)workspace & 255) ||
-        ((uintptr_t)up & 15) || ((uintptr_t)down & 15) || ((uintptr_t)y & 15))
+    if (!rows || !lidx || lidx_stride < 1 || !up || !down || !y || !workspace || ldr < H || ldy < H ||
+        ((uintptr_t)workspace & 255) || ((uintptr_t)up & 15) || ((uintptr_t)down & 15))
         return B200Q_EINVAL;
     ExpertsWs w = experts_ws((char*)workspace, R, H, F, n_local);
     if (workspace_bytes < w.bytes) return B200Q_ENOSPACE;
@@ -484,8 +484,8 @@ int b200q_moe_experts_decode(const void* rows, int rows_dtype, int ldr, int R, i
     int st;
     // 1. grouping by local expert, the slot schedule, the int8 rows
     const int qwarps = R * (H / 32);
-    launch(moe_local_prep_k, dim3(1 + (qwarps + 15) / 16), dim3(512), 0, s, rows, rows_dtype, ldr, R, H, lidx, n_local,
-           w.counts, w.offsets, w.order, w.xq, w.xs, w.sched);
+    launch(moe_local_prep_k, dim3(1 + (qwarps + 15) / 16), dim3(512), 0, s, rows, rows_dtype, ldr, R, H, lidx,
+           lidx_stride, n_local, w.counts, w.offsets, w.order, w.xq, w.xs, w.sched);
     if ((st = launched()) != B200Q_OK) return st;
     // 2. up with relu^2 and the int8 rows of the result, row id = received row
     GemvArgs a = {};
@@ -497,7 +497,8 @@ int b200q_moe_experts_decode(const void* rows, int rows_dtype, int ldr, int R, i
     GemvArgs b = {};
     b.slab = (const uint8_t*)down; b.expert_bytes = iq2_bytes(H, F); b.nslot_routed = n_local; b.n = H; b.k = F;
     b.counts = w.counts; b.offsets = w.offsets; b.order = w.order; b.act_div = 1; b.act_split = 1 << 30;
-    b.xq = w.aq; b.xs = w.as; b.y = y; b.ldy = ldy; b.sched = w.sched; b.sched_early = 1;
+    b.xq = w.aq; b.xs = w.as; b.y = (float*)y; b.ldy = ldy; b.y_bf16 = y_dtype == B200Q_BF16;
+    b.sched = w.sched; b.sched_early = 1;
     return status_from(launch_iq2_gemv(b, n_local, 16, 0, s));
 }
 

@@ -90,8 +90,10 @@ class Placement:
 class ExpertParallelMoE:
     """One expert-parallel MoE layer on this rank.
 
-    expert_fn(rows [R][H] (send dtype), lidx [R] int64, n_local) -> [R][H] fp32: the local experts applied to the
-    received rows; rows whose lidx == n_local are padding and may hold anything.
+    expert_fn(rows [R][H] (send dtype), lidx [R], n_local[, out_dtype]) -> [R][H]: the local experts applied to the
+    received rows; rows whose lidx >= n_local are padding and may hold anything.  The tensor-operation form passes
+    lidx as int64 and takes fp32 back; the fused CUDA form (capacity layout) passes an int32 index view of the received
+    rows and asks for out_dtype = the send dtype.
     combine_fn(mo [pairs][H] fp32, rw [T][topk] fp32, shared [T][H] fp32 or None) -> [T][H] fp32; b200q_combine by
     default.  shared_fn(x) -> [T][H] fp32 or None: the shared expert on this rank's tokens."""
 
@@ -101,10 +103,16 @@ class ExpertParallelMoE:
         self.n_local = len(placement.local[rank])
         self.expert_fn, self.shared_fn = expert_fn, shared_fn
         self.combine_fn = combine_fn or _gpu_combine(topk)
+        self._own_combine = combine_fn is None
         self.group, self.layout, self.send_dtype = group, layout, send_dtype
         self.device = device or torch.device("cpu")
         self.dest_t, self.lidx_t, self.nrep_t = placement.tables(self.device)
+        # int32 copies for the fused capacity exchange on CUDA (b200q_ep_pack)
+        self.dest_32, self.lidx_32, self.nrep_32 = (t.to(torch.int32) for t in (self.dest_t, self.lidx_t, self.nrep_t))
         self.timing = None   # optional: a list of 4 CUDA events (dispatch start/end, return start/end)
+        # on CUDA the capacity exchange runs as the fused kernels (expert_fn then takes an int32 index view and an
+        # out_dtype keyword); False keeps the tensor-operation form, which the CPU tests use
+        self.fused = True
 
     # -- the pieces ----------------------------------------------------------------------------------------
     def _route(self, ridx):
@@ -128,10 +136,40 @@ class ExpertParallelMoE:
             return _Done()
         return dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group, async_op=async_op)
 
+    def _capacity_fused(self, x, ridx, rw):
+        """the capacity exchange on CUDA in four kernels around the two all-to-alls: b200q_ep_pack (route lookup,
+        places, rows and local indices into the send buffer), the local experts on the received rows (their indices
+        read from the rows; outputs written in the send dtype), b200q_ep_combine (the pairs' outputs gathered from the
+        return buffer, weighted, plus the shared expert).  Same values as the tensor-operation form below."""
+        import b200q
+        T, H, topk = x.shape[0], self.H, self.topk
+        cap = T * topk
+        send, slot = b200q.ep_pack(x, ridx.to(torch.int32), self.dest_32, self.lidx_32, self.nrep_32, self.world, cap,
+                                   self.n_local_max_peer(), self.send_dtype)
+        recv = torch.empty_like(send)
+        ev = self.timing
+        if ev:
+            ev[0].record()
+        w1 = self._a2a(recv, send, async_op=True)
+        shared = self.shared_fn(x) if self.shared_fn else None   # overlaps the dispatch
+        w1.wait()
+        if ev:
+            ev[1].record()
+        y = self.expert_fn(recv[:, :H], b200q.ep_index_view(recv, H), self.n_local, out_dtype=self.send_dtype)
+        back = torch.empty_like(y)
+        if ev:
+            ev[2].record()
+        self._a2a(back, y)
+        if ev:
+            ev[3].record()
+        return b200q.ep_combine(back, slot, rw, topk, shared)
+
     def __call__(self, x, ridx, rw):
         """x [T][H] (this rank's tokens), ridx [T][topk] global expert ids, rw [T][topk] -> out [T][H] fp32"""
         T, H, topk = x.shape[0], self.H, self.topk
         pairs = T * topk
+        if self.layout == "capacity" and x.is_cuda and self.fused and self._own_combine:
+            return self._capacity_fused(x, ridx, rw)
         dest, lidx, order, counts, pos, tok = self._route(ridx)
         xs = x.to(self.send_dtype)
         ev = self.timing
@@ -223,14 +261,14 @@ class LocalExperts:
         self.up, self.down, self.n, self.H, self.F = up, down, n_local, H, F
         self._dec = None
 
-    def decode(self, rows, lidx, n_local):
+    def decode(self, rows, lidx, n_local, out_dtype=torch.float32):
         """b200q_moe_experts_decode: grouping, slot schedule and int8 rows in one launch, then the two GEMVs"""
         import b200q
         if rows.shape[0] == 0 or self.n == 0:
-            return torch.zeros(rows.shape[0], self.H, dtype=torch.float32, device=rows.device)
+            return torch.zeros(rows.shape[0], self.H, dtype=out_dtype, device=rows.device)
         if self._dec is None:
             self._dec = b200q.ExpertsDecode(self.up, self.down, self.n, self.H, self.F)
-        return self._dec(rows, lidx)
+        return self._dec(rows, lidx, out_dtype=out_dtype)
 
     def prompt(self, rows, lidx, n_local):
         import b200q

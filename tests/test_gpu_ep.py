@@ -91,3 +91,41 @@ def test_experts_decode_matches_grouped_gemvs(R, H, F, n_local, dt):
         aq_r, as_r = O.quant_rows(a, F)
         assert np.array_equal(got[r], O.iq2_gemm_i8(db[lidx[r]], H, F, aq_r, as_r, 0)[0])
     assert b200q.device_error() == 0
+
+
+@pytest.mark.parametrize("dt", ["bfloat16", "float32"])
+def test_fused_capacity_exchange_matches_tensor_form(dt):
+    """the capacity exchange as b200q_ep_pack + the local experts + b200q_ep_combine against its tensor-operation
+    form on the same inputs: the same values reach the same places, so the same bytes come out; and the send buffer
+    itself: every pair's row in its destination block at its place in pair order, indices after the values"""
+    T, H, F, E, topk = 16, 512, 256, 16, 4
+    up = iq2_blocks(31, E * F, H)
+    down = iq2_blocks(32, E * H, F)
+    su, sd = iq2_blocks(33, F, H), iq2_blocks(34, H, F)
+    xb, _ = normal_bf16(35, (T, H))
+    lb, _ = normal_bf16(36, (T, E))
+    pu = b200q.repack_iq2(dev(up.reshape(-1)), E * F, H)
+    pd = b200q.repack_iq2(dev(down.reshape(-1)), E * H, F)
+    psu, psd = b200q.repack_iq2(dev(su.reshape(-1)), F, H), b200q.repack_iq2(dev(sd.reshape(-1)), H, F)
+    xt, lt = dev(xb).view(torch.bfloat16), dev(lb).view(torch.bfloat16)
+    pl = Placement(E, 1, seed=5)
+    loc = pl.local[0]
+    ex = LocalExperts(slice_slab(pu, loc, b200q.iq2_bytes(F, H)), slice_slab(pd, loc, b200q.iq2_bytes(H, F)), len(loc),
+                      H, F)
+    moe = ExpertParallelMoE(pl, 0, 1, H, topk, ex.decode, shared_fn=SharedExpert(psu, psd, H, F, T, DEV),
+                            layout="capacity", send_dtype=getattr(torch, dt), device=torch.device(DEV))
+    ridx, rw = b200q.k_route(lt, topk)
+    fused = moe(xt, ridx, rw).cpu().numpy()
+    moe.fused = False
+    plain = moe(xt, ridx, rw).cpu().numpy()
+    assert np.array_equal(fused, plain)
+    # the send buffer
+    cap = T * topk
+    send, slot = b200q.ep_pack(xt, ridx, moe.dest_32, moe.lidx_32, moe.nrep_32, 1, cap, len(loc), getattr(torch, dt))
+    r = ridx.reshape(-1).cpu().numpy()
+    s = slot.cpu().numpy()
+    assert np.array_equal(np.sort(s), np.arange(cap))            # one rank: every pair in order of the pairs
+    assert np.array_equal(s, np.arange(cap))
+    idx = b200q.ep_index_view(send, H).cpu().numpy()
+    assert np.array_equal(idx, np.array([pl.lidx[(int(e), 0)] for e in r]))
+    assert np.array_equal(send[:, :H].float().cpu().numpy(), xt.float().repeat_interleave(topk, 0).cpu().numpy())
