@@ -168,7 +168,8 @@ int b200q_moe_group_large(const int* ridx, int pairs, int E, int* counts, int* o
 
 /* One prompt MoE projection pair over the expert-sorted pairs (replaces moe_up_tile / moe_down_tile, moe_tile_k
  * bolt_kernels.cu:697-862, and the shared expert's moe_tile_dense, :881-893):
- *   act[p] = fp16(relu(W_up[e] . x[p / topk])^2),   mo[p][0..H) = W_down[e] . act[p]   (fp32, pair-indexed)
+ *   act[p] = fp16(relu(W_up[e] . x[p / topk])^2),   mo[p][0..H) = W_down[e] . act[p]   (pair-indexed; fp32, or bf16
+ *   rounded to nearest even when mo_dtype is B200Q_BF16, as the expert-parallel return exchange sends it)
  * for every pair p of expert e, given b200q_moe_group_large's counts / offsets / order of the pairs' experts.
  * up: slab of E experts [F][H], down: slab of E experts [H][F] (packed rt32); x [T][H] fp32 or bf16 (ldx = H).
  * act_rows: NULL, or [pairs][F] fp16 receiving act (inspection only; it costs one extra pass).
@@ -176,8 +177,8 @@ int b200q_moe_group_large(const int* ridx, int pairs, int E, int* counts, int* o
  * aligned.  H % 256 == 0, F % 256 == 0, E <= 512. */
 size_t b200q_moe_prompt_workspace_bytes(int pairs, int E, int H, int F);
 int b200q_moe_prompt(const void* up, const void* down, int E, int H, int F, const int* counts, const int* offsets,
-                     const int* order, int topk, int pairs, const void* x, int x_dtype, float* mo, void* act_rows,
-                     void* workspace, size_t workspace_bytes, void* stream);
+                     const int* order, int topk, int pairs, const void* x, int x_dtype, void* mo, int mo_dtype,
+                     void* act_rows, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Q8_0 prompt GEMM (replaces mma_q8 / mma_q8_multi at prompt row counts, mma_big_k bolt_mma.cu:611-696):
  * y[t][n] = sum_k fp16(q * d) x[t][k] for any T.  Weights in the "q8 tc" layout (b200q_q8_tc_pack: units of 32 rows x

@@ -70,7 +70,7 @@ def lib():
             "b200q_q8_gemv": (i32, [vp, i32, i32, vp, i32, i32, i32, vp, i32, vp, sz, vp]),
             "b200q_moe_group_large": (i32, [vp, i32, i32, vp, vp, vp, vp, vp]),
             "b200q_moe_prompt_workspace_bytes": (sz, [i32, i32, i32, i32]),
-            "b200q_moe_prompt": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, i32, i32, vp, i32, vp, vp, vp, sz, vp]),
+            "b200q_moe_prompt": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, i32, i32, vp, i32, vp, i32, vp, vp, sz, vp]),
             "b200q_q8_tc_bytes": (sz, [i64, i32]),
             "b200q_q8_tc_pack": (i32, [vp, vp, i64, i32, vp]),
             "b200q_q8_gemm_workspace_bytes": (sz, [i32, i32]),
@@ -426,20 +426,22 @@ def k_moe_group_large(ridx, E):
     return counts, offsets, order[:pairs]
 
 
-def moe_prompt(up, down, E, H, F, counts, offsets, order, topk, x, mo=None, act=None, workspace=None):
-    """Prompt path of the routed experts (moe_up_tile + moe_down_tile): mo [pairs][H] fp32 = W_down[e] . act[p],
-    act[p] = fp16(relu(W_up[e] . x[p / topk])^2); act (optional, [pairs][F] fp16) receives the intermediate."""
+def moe_prompt(up, down, E, H, F, counts, offsets, order, topk, x, mo=None, act=None, workspace=None,
+               out_dtype=torch.float32):
+    """Prompt path of the routed experts (moe_up_tile + moe_down_tile): mo [pairs][H] (fp32, or bf16 with out_dtype /
+    a bf16 mo) = W_down[e] . act[p], act[p] = fp16(relu(W_up[e] . x[p / topk])^2); act (optional, [pairs][F] fp16)
+    receives the intermediate."""
     _dev(x, "x")
     pairs = order.numel()
-    mo = torch.empty(pairs, H, dtype=torch.float32, device=x.device) if mo is None else mo
+    mo = torch.empty(pairs, H, dtype=out_dtype, device=x.device) if mo is None else mo
     nb = lib().b200q_moe_prompt_workspace_bytes(pairs, E, H, F)
     if workspace is None:
         ws, wb = _WS.get(nb, x.device)
     else:
         ws, wb = _p(workspace), workspace.numel()
     _check(lib().b200q_moe_prompt(_p(up), _p(down), E, H, F, _p(counts), _p(offsets), _p(order), topk, pairs, _p(x),
-                                  _dtype_code(x), _p(mo), _p(act) if act is not None else None, ws, wb, _s()),
-           "moe_prompt")
+                                  _dtype_code(x), _p(mo), _dtype_code(mo), _p(act) if act is not None else None, ws, wb,
+                                  _s()), "moe_prompt")
     return mo
 
 

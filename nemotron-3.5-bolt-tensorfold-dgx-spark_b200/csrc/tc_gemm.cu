@@ -176,6 +176,22 @@ struct EpiRows {             // fp32 y[orow][n]; orow = rowmap[row0[g] + m0 + ro
         }
     }
 };
+struct EpiRows16 {           // EpiRows with bf16 outputs (rounded to nearest even): a 64-byte line a row
+    __nv_bfloat16* y;
+    int ldy;
+    const int* row0;
+    const int* rowmap;
+    __device__ void put(int4 t, int n, int tok0, int lane, const uint32_t (&v)[32]) const {
+        const int grow = (row0 ? row0[t.x] : 0) + t.z + tok0 + lane;
+        const int mine = tok0 + lane < t.w ? (rowmap ? rowmap[grow] : grow) : -1;
+        __nv_bfloat16* yn = y + n;
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const int orow = __shfl_sync(0xffffffffu, mine, j);
+            if (orow >= 0) yn[(size_t)orow * ldy] = __float2bfloat16_rn(__uint_as_float(v[j]));
+        }
+    }
+};
 struct EpiImg {              // fp16(relu(v)^2) into the next GEMM's rows image (its K = this GEMM's N): for each row
     // the warp's 32 weight rows are one 64-byte row of a record (2 bytes a lane)
     uint8_t* img;
@@ -833,10 +849,11 @@ size_t b200q_moe_prompt_workspace_bytes(int pairs, int E, int H, int F) {
 }
 
 int b200q_moe_prompt(const void* up, const void* down, int E, int H, int F, const int* counts, const int* offsets,
-                     const int* order, int topk, int pairs, const void* x, int x_dtype, float* mo, void* act_rows,
-                     void* workspace, size_t workspace_bytes, void* stream) {
+                     const int* order, int topk, int pairs, const void* x, int x_dtype, void* mo, int mo_dtype,
+                     void* act_rows, void* workspace, size_t workspace_bytes, void* stream) {
     if (!up || !down || !counts || !offsets || !order || !x || !mo || !workspace || E <= 0 || E > 512 || topk <= 0 ||
         pairs <= 0 || H % 256 || F % 256 || H <= 0 || F <= 0 || (x_dtype != B200Q_F32 && x_dtype != B200Q_BF16) ||
+        (mo_dtype != B200Q_F32 && mo_dtype != B200Q_BF16) ||
         !x16(up) || !x16(down) || !x16(x) || !x16(workspace) || (act_rows && !x16(act_rows)))
         return B200Q_EINVAL;
     const MoeWs L = moe_ws(pairs, E, H, F);
@@ -878,7 +895,9 @@ int b200q_moe_prompt(const void* up, const void* down, int E, int H, int F, cons
     a.a = actimg;
     a.N = H;
     a.K = F;
-    return status_from(launch_x<DeqIQ2>(a, EpiRows{mo, H, offsets, order}, s));
+    if (mo_dtype == B200Q_BF16)
+        return status_from(launch_x<DeqIQ2>(a, EpiRows16{(__nv_bfloat16*)mo, H, offsets, order}, s));
+    return status_from(launch_x<DeqIQ2>(a, EpiRows{(float*)mo, H, offsets, order}, s));
 }
 
 }  // extern "C"

@@ -110,8 +110,9 @@ class ExpertParallelMoE:
         # int32 copies for the fused capacity exchange on CUDA (b200q_ep_pack)
         self.dest_32, self.lidx_32, self.nrep_32 = (t.to(torch.int32) for t in (self.dest_t, self.lidx_t, self.nrep_t))
         self.timing = None   # optional: a list of 4 CUDA events (dispatch start/end, return start/end)
-        # on CUDA the capacity exchange runs as the fused kernels (expert_fn then takes an int32 index view and an
-        # out_dtype keyword); False keeps the tensor-operation form, which the CPU tests use
+        # on CUDA the exchanges run in their fused forms (expert_fn then takes an out_dtype keyword, an int32 index view
+        # in the capacity layout, and a topk keyword on one rank in the exact layout); False keeps the
+        # tensor-operation form, which the CPU tests use
         self.fused = True
 
     # -- the pieces ----------------------------------------------------------------------------------------
@@ -164,12 +165,56 @@ class ExpertParallelMoE:
             ev[3].record()
         return b200q.ep_combine(back, slot, rw, topk, shared)
 
+    def _exact_fused(self, x, ridx, rw):
+        """the exact exchange on CUDA: the expert outputs come back in the send dtype and b200q_ep_combine gathers,
+        weights and sums them from the return buffer.  On one rank nothing is exchanged: the local experts run on the
+        tokens' pairs in place (expert_fn with topk) and b200q_combine sums their fp32 outputs."""
+        import b200q
+        T, H, topk = x.shape[0], self.H, self.topk
+        pairs = T * topk
+        dest, lidx, order, counts, pos, tok = self._route(ridx)
+        shared = None
+        if self.world == 1:
+            shared = self.shared_fn(x) if self.shared_fn else None
+            mo = self.expert_fn(x, lidx, self.n_local, topk=topk)
+            return b200q.k_combine(mo, rw.reshape(-1).contiguous(), topk, shared=shared)
+        rc = torch.empty_like(counts)
+        self._a2a(rc, counts)
+        send_splits = counts.tolist()
+        recv_splits = rc.tolist()
+        send = x.to(self.send_dtype).index_select(0, tok[order])
+        send_l = lidx[order]
+        recv = torch.empty(sum(recv_splits), H, dtype=self.send_dtype, device=x.device)
+        recv_l = torch.empty(sum(recv_splits), dtype=torch.int64, device=x.device)
+        ev = self.timing
+        if ev:
+            ev[0].record()
+        w1 = self._a2a(recv, send, recv_splits, send_splits, async_op=True)
+        w2 = self._a2a(recv_l, send_l, recv_splits, send_splits, async_op=True)
+        shared = self.shared_fn(x) if self.shared_fn else None   # overlaps the dispatch
+        w1.wait()
+        w2.wait()
+        if ev:
+            ev[1].record()
+        y = self.expert_fn(recv, recv_l, self.n_local, out_dtype=self.send_dtype)
+        got = torch.empty(pairs, H, dtype=self.send_dtype, device=x.device)
+        if ev:
+            ev[2].record()
+        self._a2a(got, y, send_splits, recv_splits)
+        if ev:
+            ev[3].record()
+        slot = torch.empty(pairs, dtype=torch.int32, device=x.device)
+        slot.scatter_(0, order, torch.arange(pairs, dtype=torch.int32, device=x.device))   # pair p's row in got
+        return b200q.ep_combine(got, slot, rw, topk, shared)
+
     def __call__(self, x, ridx, rw):
         """x [T][H] (this rank's tokens), ridx [T][topk] global expert ids, rw [T][topk] -> out [T][H] fp32"""
         T, H, topk = x.shape[0], self.H, self.topk
         pairs = T * topk
-        if self.layout == "capacity" and x.is_cuda and self.fused and self._own_combine:
-            return self._capacity_fused(x, ridx, rw)
+        if x.is_cuda and self.fused and self._own_combine:
+            if self.layout == "capacity":
+                return self._capacity_fused(x, ridx, rw)
+            return self._exact_fused(x, ridx, rw)
         dest, lidx, order, counts, pos, tok = self._route(ridx)
         xs = x.to(self.send_dtype)
         ev = self.timing
@@ -261,22 +306,28 @@ class LocalExperts:
         self.up, self.down, self.n, self.H, self.F = up, down, n_local, H, F
         self._dec = None
 
-    def decode(self, rows, lidx, n_local, out_dtype=torch.float32):
-        """b200q_moe_experts_decode: grouping, slot schedule and int8 rows in one launch, then the two GEMVs"""
+    def decode(self, rows, lidx, n_local, out_dtype=torch.float32, topk=1):
+        """b200q_moe_experts_decode: grouping, slot schedule and int8 rows in one launch, then the two GEMVs; with
+        topk > 1, pair p (one lidx each) reads row p // topk"""
         import b200q
+        if topk > 1:
+            rows = rows.index_select(0, torch.arange(lidx.numel(), device=rows.device) // topk)
         if rows.shape[0] == 0 or self.n == 0:
             return torch.zeros(rows.shape[0], self.H, dtype=out_dtype, device=rows.device)
         if self._dec is None:
             self._dec = b200q.ExpertsDecode(self.up, self.down, self.n, self.H, self.F)
         return self._dec(rows, lidx, out_dtype=out_dtype)
 
-    def prompt(self, rows, lidx, n_local):
+    def prompt(self, rows, lidx, n_local, out_dtype=torch.float32, topk=1):
+        """the tcgen05 prompt GEMMs over pairs: pair p (one lidx each, all local: the exact layout has no padding)
+        reads row p // topk of rows; -> [pairs][H] in out_dtype"""
         import b200q
-        out = torch.zeros(rows.shape[0], self.H, dtype=torch.float32, device=rows.device)
-        if rows.shape[0] == 0 or self.n == 0:
-            return out
+        pairs = lidx.numel()
+        if pairs == 0 or self.n == 0:
+            return torch.zeros(pairs, self.H, dtype=out_dtype, device=rows.device)
+        out = torch.empty(pairs, self.H, dtype=out_dtype, device=rows.device)
         counts, offsets, order = b200q.k_moe_group_large(lidx.to(torch.int32), n_local + 1)
-        return b200q.moe_prompt(self.up, self.down, n_local, self.H, self.F, counts, offsets, order, 1, rows, mo=out)
+        return b200q.moe_prompt(self.up, self.down, n_local, self.H, self.F, counts, offsets, order, topk, rows, mo=out)
 
 
 def slice_slab(slab, experts, expert_bytes):
