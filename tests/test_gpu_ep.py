@@ -129,3 +129,48 @@ def test_fused_capacity_exchange_matches_tensor_form(dt):
     idx = b200q.ep_index_view(send, H).cpu().numpy()
     assert np.array_equal(idx, np.array([pl.lidx[(int(e), 0)] for e in r]))
     assert np.array_equal(send[:, :H].float().cpu().numpy(), xt.float().repeat_interleave(topk, 0).cpu().numpy())
+
+
+def test_ep_pack_and_combine_layout_four_ranks():
+    """b200q_ep_pack for a 4-rank placement (with a replicated expert) against a numpy statement of the send layout:
+    destination blocks of cap rows, each holding its pairs in pair order with their values and local indices, the rest
+    carrying the discard index; b200q_ep_combine against the weighted sum it restates"""
+    T, H, E, topk, world = 16, 256, 16, 6, 4
+    rng = np.random.default_rng(41)
+    loads = rng.uniform(1, 10, E)
+    loads[3] = 200.0
+    pl = Placement(E, world, loads=loads, replicate=1)
+    assert max(len(o) for o in pl.owners) > 1
+    dest_t, lidx_t, nrep_t = (t.to(torch.int32) for t in pl.tables(torch.device(DEV)))
+    x = torch.randn(T, H, device=DEV)
+    ridx = torch.from_numpy(rng.integers(0, E, (T, topk)).astype(np.int32)).to(DEV)
+    cap = T * topk
+    discard = max(len(l) for l in pl.local)
+    send, slot = b200q.ep_pack(x, ridx, dest_t, lidx_t, nrep_t, world, cap, discard, torch.float32)
+    s_np, idx = send[:, :H].cpu().numpy(), b200q.ep_index_view(send, H).cpu().numpy()
+    slot_np, x_np, r = slot.cpu().numpy(), x.cpu().numpy(), ridx.cpu().numpy().reshape(-1)
+    fill = np.zeros(world, int)
+    seen = np.zeros(world * cap, bool)
+    for p in range(cap):
+        e, t = int(r[p]), p // topk
+        owner = pl.owners[e][t % len(pl.owners[e])]
+        row = owner * cap + fill[owner]
+        fill[owner] += 1
+        assert slot_np[p] == row
+        assert idx[row] == pl.lidx[(e, owner)]
+        assert np.array_equal(s_np[row], x_np[t])
+        seen[row] = True
+    assert (idx[~seen] == discard).all()
+    # the combine over a return buffer holding anything in the unused rows
+    back = torch.randn(world * cap, H, device=DEV).to(torch.bfloat16)
+    rw = torch.rand(T, topk, device=DEV)
+    shared = torch.randn(T, H, device=DEV)
+    got = b200q.ep_combine(back, slot, rw, topk, shared).cpu().numpy()
+    b, w = back.float().cpu().numpy(), rw.cpu().numpy()
+    want = np.zeros((T, H), np.float32)
+    for t in range(T):
+        acc = np.zeros(H, np.float32)
+        for k in range(topk):
+            acc = (np.float64(w[t, k]) * b[slot_np[t * topk + k]] + acc).astype(np.float32)   # fma: one rounding
+        want[t] = acc + shared[t].cpu().numpy()
+    assert np.array_equal(got, want)
