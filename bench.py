@@ -138,6 +138,31 @@ def zipf_routing(seed, tokens, topk, s=1.1, perm_seed=None):
     return ridx
 
 
+def graph_ms(call, n, reps=5):
+    """ms per call of call(i), i = 0 .. n-1, captured once as a CUDA graph and replayed `reps` times: the decode GEMVs
+    take some 10-60 us of GPU time, less than a Python-side launch, so timing them launch by launch would time the
+    host.  The caller has run call(i) eagerly first (warm-up, workspaces sized)."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(g, stream=side):
+            for i in range(n):
+                call(i)
+    torch.cuda.current_stream().wait_stream(side)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / (reps * n)
+    del g
+    return ms
+
+
 def prefill_bench(b200q, layer, device, iters=5):
     """BASELINE config 4 on the tcgen05 prompt GEMMs: the routed experts' grouped up (ReLU^2) and down GEMMs over
     8192 tokens x top-6 (Zipf 1.1), and the Q8_0 GQA projections (q/k/v fused, then o) on the same 8192 tokens."""
@@ -182,9 +207,9 @@ def prefill_bench(b200q, layer, device, iters=5):
         ms = e0.elapsed_time(e1) / iters
         res[name] = (ms, flops / (ms * 1e-3) / 1e12)
     # the same GQA projections at decode sizes (M = 1 / 16 rows) on the t16 Q8_0 GEMV, GB/s over weights + x + y,
-    # rotating 6 weight copies of q/k/v (160 MB, larger than L2)
+    # rotating 10 weight copies of q/k/v (267 MB, twice the L2), timed as a CUDA graph of 60 calls
     dec = {}
-    copies = 6
+    copies = 10
     wd = []
     for c in range(copies):
         r = np.random.default_rng(40 + c)
@@ -196,15 +221,8 @@ def prefill_bench(b200q, layer, device, iters=5):
         yd = torch.empty(M, 6144, dtype=torch.float32, device=device)
         for i in range(3):
             b200q.mma_q8(wd[i % copies], 6144, H, xd, y=yd)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
-        e0.record(s)
-        n_it = 30
-        for i in range(n_it):
-            b200q.mma_q8(wd[i % copies], 6144, H, xd, y=yd)
-        e1.record(s)
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / n_it
+        ms = graph_ms(lambda i: b200q.mma_q8(wd[i % copies], 6144, H, xd, y=yd), 60)
         nbytes = 6144 * H * 34 // 32 + M * H * 2 + M * 6144 * 4
         dec[f"gqa_qkv_decode_M{M}_gbs"] = round(nbytes / (ms * 1e-3) / 1e9, 1)
     err = b200q.device_error()
@@ -417,15 +435,16 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
 def nvfp4_bench(b200q, device, iters=20):
     """the NVFP4 Mamba-2 projections, in_proj 4096 -> 18560 and out_proj 8192 -> 4096 (e2m1 codes
     U{0..15}, e4m3 scales U[0.5, 2] per 16, an fp32 tensor scale), activations bf16 N(0, 1).  M <= 16: the t16 decode
-    GEMV, GB/s over weights + x + y, rotating 4 weight copies (246 MB, larger than L2).  M >= 512: quant_nv4_rows +
-    the block-scaled fp4 tcgen05 GEMM, TFLOPS of the GEMM alone and of quantiser + GEMM."""
+    GEMV, GB/s over weights + x + y, rotating weight copies of twice the L2 (6 of in_proj, 14 of out_proj), timed as a
+    CUDA graph of 60 calls.  M >= 512: quant_nv4_rows + the block-scaled fp4 tcgen05 GEMM, TFLOPS of the GEMM alone
+    and of quantiser + GEMM."""
     shapes = {"in_proj": (18560, 4096), "out_proj": (4096, 8192)}
-    copies = 4
+    ncopies = {"in_proj": 6, "out_proj": 14}
     g = torch.Generator(device="cpu").manual_seed(31)
     W = {}
     for name, (n, k) in shapes.items():
         W[name] = []
-        for c in range(copies):
+        for c in range(ncopies[name]):
             q = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, generator=g).to(device)
             sc = (torch.rand(n, k // 16, generator=g) * 1.5 + 0.5).to(torch.float8_e4m3fn).view(torch.uint8).to(device)
             W[name].append((b200q.tile_nv4(q, sc, n, k), b200q.tile_nv4w(q, sc, n, k) if c == 0 else None))
@@ -433,18 +452,14 @@ def nvfp4_bench(b200q, device, iters=20):
     out = {}
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     for name, (n, k) in shapes.items():
+        copies = ncopies[name]
         for M in (1, 16):
             x = torch.randn(M, k, generator=g).to(torch.bfloat16).to(device)
             y = torch.empty(M, n, device=device)
             for i in range(3):
                 b200q.mma_nv4(W[name][i % copies][0], s2, n, k, x, y=y)
             torch.cuda.synchronize()
-            e0.record()
-            for i in range(iters):
-                b200q.mma_nv4(W[name][i % copies][0], s2, n, k, x, y=y)
-            e1.record()
-            torch.cuda.synchronize()
-            ms = e0.elapsed_time(e1) / iters
+            ms = graph_ms(lambda i: b200q.mma_nv4(W[name][i % copies][0], s2, n, k, x, y=y), 60)
             nbytes = n * k // 2 + n * k // 16 + M * k * 2 + M * n * 4
             out[f"{name}_M{M}_gbs"] = round(nbytes / (ms * 1e-3) / 1e9, 1)
         for M in (512, 4096):
