@@ -1,0 +1,141 @@
+// libbolt's operator launchers over this engine (include/b200q_bolt.h): the names, signatures and view structs of the
+// reference's engine/bolt_common.h:77-161, so its host code links here for the routed-expert MoE block.  Each shim
+// maps libbolt's arguments onto the engine's kernels; libbolt's model constants (latent 1024, TOPN 9) are the fixed
+// shapes its launchers assume.
+#include "iq2.cuh"
+#include "../../include/b200q_bolt.h"
+
+#include <cstdio>
+
+namespace b200q {
+
+constexpr int kBoltLatent = 1024;   // moe_up's k, moe_down's n, k_combine's width (bolt_kernels.cu:682-695, 1714-1727)
+constexpr int kBoltTopN = 9;        // routed experts a token (bolt_common.h:25)
+constexpr int kBoltSlots = 512;     // experts a router output can name (moe_group_k's 512 counters, bolt_kernels.cu:278)
+
+static void report(const char* what, cudaError_t e) {
+    if (e != cudaSuccess) fprintf(stderr, "b200q shim: %s failed: %s\n", what, cudaGetErrorString(e));
+}
+static void report(const char* what, int status) {
+    if (status != B200Q_OK) fprintf(stderr, "b200q shim: %s failed: %s\n", what, b200q_strerror(status));
+}
+
+// the one-item-per-slot work list: expert[e] = e, n_work = kBoltSlots
+__global__ void work_slots_k(int* __restrict__ work_exp, int* __restrict__ n_work, const int* __restrict__ counts,
+                             int* __restrict__ stat) {
+    pdl_wait();
+    const int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e < kBoltSlots) {
+        work_exp[e] = e;
+        if (stat && counts[e] > 0) atomicAdd(stat, 1);   // libbolt's profile counters: active experts, items
+    }
+    if (e == 0) {
+        *n_work = kBoltSlots;
+        if (stat) atomicAdd(stat + 1, kBoltSlots);
+    }
+    pdl_trigger();
+}
+
+// a grouped launch over libbolt's slab (split rt32 planes) and this engine's one-item-per-slot MoeWork
+static GemvArgs slab_args(const IQ2Slab& slab, const MoeWork& w, int n, int k, int act_div) {
+    GemvArgs a = {};
+    a.slab = slab.qs;
+    a.expert_bytes = slab.qs_stride;
+    a.dplane = (const uint8_t*)slab.d;
+    a.dplane_stride = slab.d_stride * 2;   // halves -> bytes
+    a.nslot_routed = kBoltSlots;
+    a.n = n;
+    a.k = k;
+    a.counts = w.count;
+    a.offsets = w.first;
+    a.order = w.order;
+    a.act_div = act_div;
+    a.act_split = 1 << 30;
+    return a;
+}
+
+}  // namespace b200q
+
+using namespace b200q;
+
+// repack_iq2 (bolt_kernels.cu:1053-1068): the checkpoint's blocks into the qs / d buffers load_slab allocates
+// (rows * k/256 * 64 and * 2 bytes), as this engine's split rt32 layout; rows % 32 == 0
+void repack_iq2(cudaStream_t s, const uint8_t* src, uint8_t* qs, void* d, size_t rows, int k) {
+    if (!src || !qs || !d || rows % kIq2Tile || k % 256 || k <= 0) {
+        report("repack_iq2", B200Q_EINVAL);
+        return;
+    }
+    report("repack_iq2", launch_iq2_pack_split(src, qs, (uint8_t*)d, (int64_t)rows, k, s));
+}
+
+// route_k (bolt_kernels.cu:1653-1712): sigmoid + bias top-9, weights normalised and scaled
+void k_route(cudaStream_t s, const float* logits, int ldl, const float* bias, int* ridx, float* rw, int E, float scale, int T) {
+    report("k_route", b200q_route(logits, B200Q_F32, ldl, bias, T, E, kBoltTopN, B200Q_ROUTE_SIGMOID, scale, ridx, rw, s));
+}
+
+// moe_group_k (bolt_kernels.cu:275-344): the pairs in expert order, and the work list as one item per expert slot
+void k_moe_group(cudaStream_t s, const int* ridx, int pairs, int* order, int* work_first, int* work_n, int* work_exp,
+                 int* n_work, int* stat) {
+    // work_n / work_first take the slots' counts and offsets (libbolt sizes them TMAX * TOPN >= 513 entries);
+    // work_exp is the large-count grouping's fill scratch before it becomes the slot list
+    const int st = pairs <= 4096 ? b200q_moe_group(ridx, pairs, kBoltSlots, work_n, work_first, order, s)
+                                 : b200q_moe_group_large(ridx, pairs, kBoltSlots, work_n, work_first, order, work_exp, s);
+    report("k_moe_group", st);
+    if (st == B200Q_OK)
+        report("k_moe_group", launch(work_slots_k, dim3((kBoltSlots + 255) / 256), dim3(256), 0, s, work_exp, n_work,
+                                     (const int*)work_n, stat));
+}
+
+// quant_rows_k (bolt_kernels.cu:347-363)
+void k_quant_rows(cudaStream_t s, const float* x, int ldx, int8_t* q, int ldq, float* sc, int ldsc, int rows, int k) {
+    report("k_quant_rows", b200q_quant_rows(x, B200Q_F32, ldx, q, ldq, sc, ldsc, rows, k, s));
+}
+
+// moe_up (bolt_kernels.cu:682-688): act[p][0 .. width) = relu(W_up[e] . x[p / 9])^2 over the latent (k 1024)
+void moe_up(cudaStream_t s, const IQ2Slab& up, const MoeWork& w, const int8_t* xq, const float* xs, float* act, int width,
+            int pairs) {
+    if (pairs <= 0) return;
+    GemvArgs a = slab_args(up, w, width, kBoltLatent, kBoltTopN);
+    a.xq = xq;
+    a.xs = xs;
+    a.y = act;
+    a.ldy = width;
+    report("moe_up", launch_iq2_gemv(a, kBoltSlots, 16, 1, s));
+}
+
+// moe_down (bolt_kernels.cu:689-695): out[p][0 .. 1024) = W_down[e] . act[p] (k = width)
+void moe_down(cudaStream_t s, const IQ2Slab& down, const MoeWork& w, const int8_t* xq, const float* xs, float* out,
+              int width, int pairs) {
+    if (pairs <= 0) return;
+    GemvArgs a = slab_args(down, w, kBoltLatent, width, 1);
+    a.xq = xq;
+    a.xs = xs;
+    a.y = out;
+    a.ldy = kBoltLatent;
+    report("moe_down", launch_iq2_gemv(a, kBoltSlots, 16, 0, s));
+}
+
+// moe_coop_dense (bolt_kernels.cu:881-887): one IQ2 matrix (n rows, a slab of one) over T rows, epi 1 relu^2
+void moe_coop_dense(cudaStream_t s, const IQ2Slab& w, const MoeWork& mw, int T, const int8_t* xq, const float* xs, float* y,
+                    int ldy, int n, int k, int epi) {
+    (void)mw;   // libbolt's one-expert work list: the dense launch needs none
+    if (T <= 0) return;
+    GemvArgs a = {};
+    a.slab = w.qs;
+    a.dplane = (const uint8_t*)w.d;
+    a.n = n;
+    a.k = k;
+    a.dense_rows = T;
+    a.act_div = 1;
+    a.act_split = 1 << 30;
+    a.xq = xq;
+    a.xs = xs;
+    a.y = y;
+    a.ldy = ldy;
+    report("moe_coop_dense", launch_iq2_gemv(a, 1, T, epi ? 1 : 0, s));
+}
+
+// combine_k (bolt_kernels.cu:1714-1727): out[t][0 .. 1024) = sum over the 9 picks of rw * o[t * 9 + k]
+void k_combine(cudaStream_t s, const float* o, const float* rw, float* out, int T) {
+    report("k_combine", b200q_combine(o, rw, nullptr, T, kBoltTopN, kBoltLatent, out, B200Q_F32, s));
+}

@@ -108,6 +108,32 @@ __host__ __device__ inline uint32_t iq2_sign_bytes(uint32_t qy) {
 // packer: ggml blocks [n][k/256][66] -> rt32 units (see common.cuh), one thread per (row, chunk pair); the sign
 // word of every chunk is re-encoded by iq2_sign_bytes
 // ---------------------------------------------------------------------------------------------------------
+// the split form: a unit's 2048 chunk bytes into qs (2048 a unit), its 32 rows' d into dq (64 bytes a unit)
+__global__ void iq2_pack_split_k(const uint8_t* __restrict__ raw, uint8_t* __restrict__ qs, uint8_t* __restrict__ dq,
+                                 int64_t n, int k) {
+    pdl_wait();
+    const int npair = k / 64, nb = k / 256;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n * npair) {
+        const int64_t row = i / npair;
+        const int j = (int)(i - row * npair);
+        const uint8_t* blk = raw + ((size_t)row * nb + j / 4) * 66;
+        const uint8_t* src = blk + 2 + 16 * (j % 4);
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+            w[q] = (uint32_t)src[4 * q] | (uint32_t)src[4 * q + 1] << 8 | (uint32_t)src[4 * q + 2] << 16 | (uint32_t)src[4 * q + 3] << 24;
+        w[1] = iq2_sign_bytes(w[1]);
+        w[3] = iq2_sign_bytes(w[3]);
+        const int64_t rt = row / kIq2Tile;
+        const int lane = (int)(row % kIq2Tile);
+        const size_t unit = (size_t)rt * nb + j / 4;
+        reinterpret_cast<uint4*>(qs + unit * 2048)[(j & 3) * kIq2Tile + lane] = make_uint4(w[0], w[1], w[2], w[3]);
+        if ((j & 3) == 0) reinterpret_cast<uint16_t*>(dq + unit * 64)[lane] = (uint16_t)(blk[0] | blk[1] << 8);
+    }
+    pdl_trigger();
+}
+
 __global__ void iq2_pack_k(const uint8_t* __restrict__ raw, uint8_t* __restrict__ out, int64_t n, int k) {
     pdl_wait();
     const int npair = k / 64, nb = k / 256;
@@ -317,6 +343,7 @@ struct Producer {
     int pn;                  // units grabbed
     int nt, left;            // the unit being issued: its tokens, and its super-blocks not yet issued (0: none)
     const uint8_t* wsrc;     // its next super-block of weights
+    const uint8_t* dsrc;     // the split layout: its next 64 bytes of d
     int xoff[kUnitTok];      // element offsets of its tokens' next int8 blocks (from a.xq) and scales (from a.xs)
     int soff[kUnitTok];
 
@@ -350,7 +377,14 @@ struct Producer {
             xoff[m] = arow * a.k;
             if (kScl) soff[m] = arow * (a.k >> 5);
         }
-        wsrc = slot_weights(a, w.s) + (size_t)w.g * (a.k >> 8) * kIq2Unit;
+        const size_t unit0 = (size_t)w.g * (a.k >> 8);   // the unit's first (tile, super-block)
+        if (a.dplane) {
+            const bool routed = a.counts == nullptr || w.s < a.nslot_routed;   // as slot_weights
+            wsrc = slot_weights(a, w.s) + unit0 * 2048;
+            dsrc = (routed ? a.dplane + (size_t)w.s * a.dplane_stride : a.dplane_extra) + unit0 * 64;
+        } else {
+            wsrc = slot_weights(a, w.s) + unit0 * kIq2Unit;
+        }
         nt = w.nt;
         left = a.k >> 8;
     }
@@ -359,8 +393,15 @@ struct Producer {
         if (left == 0) return;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the warp's reads of the stage come first
         mbar_expect_tx(bar, (uint32_t)(kIq2Unit + nt * (kScl ? 288 : 256)));
-        bulk_g2s(st, wsrc, kIq2Unit, bar);
-        wsrc += kIq2Unit;
+        if (a.dplane) {
+            bulk_g2s(st, wsrc, 2048, bar);
+            bulk_g2s(st + 2048, dsrc, 64, bar);
+            wsrc += 2048;
+            dsrc += 64;
+        } else {
+            bulk_g2s(st, wsrc, kIq2Unit, bar);
+            wsrc += kIq2Unit;
+        }
 #pragma unroll
         for (int m = 0; m < kUnitTok; m++) {
             if (m < nt) {
@@ -654,6 +695,11 @@ cudaError_t launch_iq2_gemv(const GemvArgs& a0, int nslots, int /*maxcnt*/, int 
         case kRelu2Q8: return launch_gemv_e<kRelu2Q8>(a, nslots, s);
         default: return launch_gemv_e<kDots>(a, nslots, s);
     }
+}
+
+cudaError_t launch_iq2_pack_split(const uint8_t* raw, uint8_t* qs, uint8_t* dq, int64_t n, int k, cudaStream_t s) {
+    const int64_t th = n * (k / 64);
+    return launch(iq2_pack_split_k, dim3((unsigned)((th + 255) / 256)), dim3(256), 0, s, raw, qs, dq, n, k);
 }
 
 bool iq2_shape_ok(int64_t n, int k) { return n > 0 && n % kIq2Tile == 0 && n <= (1 << 24) && k > 0 && k % 256 == 0 && k <= 8192; }

@@ -24,6 +24,11 @@ struct GemvArgs {
     const float* xs;    // [rows][k/32]
     float* y;           // [ids][ldy] fp32 (epi 0, 1); bf16 elements when y_bf16
     int y_bf16;
+    // The split form of the layout (libbolt's allocation: qs and d planes, iq2_pack_split): slab / extra_w hold the
+    // units' 2048 chunk bytes (expert_bytes apart), dplane / dplane_extra their 64 bytes of d (dplane_stride apart).
+    const uint8_t* dplane;
+    const uint8_t* dplane_extra;
+    size_t dplane_stride;
     int ldy;
     int8_t* aq;         // epi 2: relu^2 rows quantised, [ids][n] int8 and as [ids][n/32]
     float* as;
@@ -83,6 +88,8 @@ __device__ inline void iq2_schedule_slots(const int* counts, int nslots, int* or
 
 // epi: 0 store, 1 relu^2, 2 relu^2 + int8 per 32, 3 chunk dots.  maxcnt bounds a slot's ids (the staging size).
 cudaError_t launch_iq2_gemv(const GemvArgs& a, int nslots, int maxcnt, int epi, cudaStream_t s);
+// ggml blocks [n][k/256][66] -> the split rt32 layout: qs [units][2048], dq [units][64] (units = n/32 * k/256)
+cudaError_t launch_iq2_pack_split(const uint8_t* raw, uint8_t* qs, uint8_t* dq, int64_t n, int k, cudaStream_t s);
 bool iq2_shape_ok(int64_t n, int k);
 
 }  // namespace b200q

@@ -1,0 +1,50 @@
+// TEST INFRASTRUCTURE: C entry points that call libb200q's libbolt-signature shims (include/b200q_bolt.h) the way
+// libbolt's host code does, building IQ2Slab / MoeWork from plain pointers, so tests/test_gpu_bolt_shim.py can drive
+// them through ctypes.  Built by tests/build_harness.py into tests/_build/libbolt_shim_harness.so.
+#include "b200q_bolt.h"
+
+extern "C" {
+
+void hs_repack_iq2(void* s, const void* src, void* qs, void* d, size_t rows, int k) {
+    repack_iq2((cudaStream_t)s, (const uint8_t*)src, (uint8_t*)qs, d, rows, k);
+}
+
+void hs_k_route(void* s, const float* logits, int ldl, const float* bias, int* ridx, float* rw, int E, float scale, int T) {
+    k_route((cudaStream_t)s, logits, ldl, bias, ridx, rw, E, scale, T);
+}
+
+void hs_k_moe_group(void* s, const int* ridx, int pairs, int* order, int* first, int* count, int* exp, int* nwork) {
+    k_moe_group((cudaStream_t)s, ridx, pairs, order, first, count, exp, nwork, nullptr);
+}
+
+void hs_k_quant_rows(void* s, const float* x, int ldx, int8_t* q, int ldq, float* sc, int ldsc, int rows, int k) {
+    k_quant_rows((cudaStream_t)s, x, ldx, q, ldq, sc, ldsc, rows, k);
+}
+
+// moe_up / moe_down with the slab and work list as enqueue_block builds them (bolt_host.cu:700-713)
+void hs_moe_up(void* s, const void* qs, const void* d, size_t qs_stride, size_t d_stride, int* order, int* first,
+               int* count, int* exp, int* nwork, const int8_t* xq, const float* xs, float* act, int width, int pairs) {
+    const IQ2Slab up{(const uint8_t*)qs, d, qs_stride, d_stride};
+    const MoeWork w{order, first, count, exp, nwork};
+    moe_up((cudaStream_t)s, up, w, xq, xs, act, width, pairs);
+}
+
+void hs_moe_down(void* s, const void* qs, const void* d, size_t qs_stride, size_t d_stride, int* order, int* first,
+                 int* count, int* exp, int* nwork, const int8_t* xq, const float* xs, float* out, int width, int pairs) {
+    const IQ2Slab down{(const uint8_t*)qs, d, qs_stride, d_stride};
+    const MoeWork w{order, first, count, exp, nwork};
+    moe_down((cudaStream_t)s, down, w, xq, xs, out, width, pairs);
+}
+
+void hs_moe_coop_dense(void* s, const void* qs, const void* d, int T, const int8_t* xq, const float* xs, float* y, int ldy,
+                       int n, int k, int epi) {
+    const IQ2Slab w{(const uint8_t*)qs, d, 0, 0};
+    const MoeWork mw{nullptr, nullptr, nullptr, nullptr, nullptr};
+    moe_coop_dense((cudaStream_t)s, w, mw, T, xq, xs, y, ldy, n, k, epi);
+}
+
+void hs_k_combine(void* s, const float* o, const float* rw, float* out, int T) {
+    k_combine((cudaStream_t)s, o, rw, out, T);
+}
+
+}  // extern "C"

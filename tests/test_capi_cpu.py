@@ -66,3 +66,20 @@ def test_host_generator_is_deterministic_and_in_range():
     assert s4.min() == 0 and s4.max() == 15
     # block i depends only on (seed, i)
     assert np.array_equal(b200q.synth_iq2_host(7, 10), a[:660])
+
+
+def test_library_exports_the_libbolt_signature_shims():
+    """include/b200q_bolt.h's launchers (libbolt's C++ names and signatures) are defined in the library"""
+    import shutil
+    import subprocess
+    import pytest
+    nm = shutil.which("nm")
+    if nm is None:
+        pytest.skip("nm not available")
+    text = open(os.path.join(ROOT, "include", "b200q_bolt.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = sorted(set(re.findall(r"^void (\w+)\(", text, flags=re.M)))
+    assert {"moe_up", "moe_down", "k_moe_group", "repack_iq2"} <= set(names)
+    out = subprocess.run([nm, "-DC", "--defined-only", b200q.LIB_PATH], capture_output=True, text=True).stdout
+    missing = [n for n in names if not re.search(r"\b" + n + r"\(CUstream_st\*", out)]
+    assert not missing, missing
