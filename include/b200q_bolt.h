@@ -4,6 +4,11 @@
  *   load time   repack_iq2 (into the same qs / d buffers load_slab allocates, in this engine's split rt32 layout);
  *   per block   k_route, k_moe_group, k_quant_rows, moe_up, moe_down, k_combine; moe_coop_dense for the shared
  *               expert.
+ * and for the Mamba and attention projections (load_nv4 / load_q8, bolt_host.cu:198-264, and their decode calls):
+ *   load time   tile_bytes_nv4, tile_scale_bytes_nv4, tile_bytes_q8, tile_scale_bytes_q8, tile_nv4, tile_q8 (the same
+ *               buffer sizes as libbolt's tiles, holding this engine's t16 units split into a code plane and a scale
+ *               plane);
+ *   per step    mma_nv4, mma_q8, mma_q8_multi.
  * The structs repeat libbolt's member order and types so the bytes match.  libbolt's fixed model shapes stay fixed
  * here: the latent width 1024 (moe_up's k, moe_down's n, k_combine's width) and TOPN = 9 routed experts a token.
  * As in libbolt the launchers are asynchronous on the given stream and return nothing; a launch error is printed
@@ -32,3 +37,25 @@ void moe_down(cudaStream_t s, const IQ2Slab& down, const MoeWork& w, const int8_
 void moe_coop_dense(cudaStream_t s, const IQ2Slab& w, const MoeWork& mw, int T, const int8_t* xq, const float* xs, float* y,
                     int ldy, int n, int k, int epi);
 void k_combine(cudaStream_t s, const float* o, const float* rw, float* out, int T);
+
+/* an NVFP4 matrix (n rows, k): q = the 512 code bytes of each 16-row x 64-k unit, sc = its 64 e4m3 scale bytes,
+ * s2 = the tensor's second-level scale (bolt_common.h:43) */
+struct TNV4 { const uint4* q; const uint2* sc; float s2; int n, k; };
+/* a Q8_0 matrix: q = the 512 int8 bytes of each 16-row x 32-k unit, d = its 16 fp16 scales (bolt_common.h:47) */
+struct TQ8 { const uint4* q; const uint32_t* d; int n, k; };
+/* up to three Q8_0 matrices over the same rows (the attention q / k / v, bolt_common.h:125) */
+struct TQ8Multi { TQ8 w[3]; float* y[3]; int ldy[3]; };
+
+size_t tile_bytes_nv4(int n, int k);
+size_t tile_scale_bytes_nv4(int n, int k);
+size_t tile_bytes_q8(int n, int k);
+size_t tile_scale_bytes_q8(int n, int k);
+/* q [n][k/2] (low nibble first), sc [n][k/16] e4m3 -> qt, sct; raw = ggml Q8_0 blocks [n][k/32][34] -> qt, dt.
+ * n % 16 == 0, k % 256 == 0 */
+void tile_nv4(cudaStream_t s, const uint8_t* q, const uint8_t* sc, void* qt, void* sct, int n, int k);
+void tile_q8(cudaStream_t s, const uint8_t* raw, void* qt, void* dt, int n, int k);
+/* y[t][0 .. n) = W x[t] for t < T (fp32 rows; 16-row pieces at a time, each one decode GEMV) */
+void mma_nv4(cudaStream_t s, const TNV4& w, const float* x, int ldx, float* y, int ldy, int T);
+void mma_q8(cudaStream_t s, const TQ8& w, const float* x, int ldx, float* y, int ldy, int T);
+/* each matrix with n > 0 (libbolt leaves an unused one zeroed) into its own y */
+void mma_q8_multi(cudaStream_t s, const TQ8Multi& m, const float* x, int ldx, int T);

@@ -6,8 +6,19 @@
 #include "../../include/b200q_bolt.h"
 
 #include <cstdio>
+#include <mutex>
 
 namespace b200q {
+
+// the split forms of the t16 decode layouts (gemv_tc.cu)
+cudaError_t launch_nv4_pack_split(const uint8_t* q, const uint8_t* sc, uint8_t* qt, uint8_t* sct, int n, int k,
+                                  cudaStream_t s);
+cudaError_t launch_q8_pack_split(const uint8_t* raw, uint8_t* qt, uint8_t* dt, int n, int k, cudaStream_t s);
+int tc_gemv_split(int fmt, const uint8_t* qt, const uint8_t* sct, float s2, int n, int k, const float* x, int ldx, int T,
+                  float* y, int ldy, void* ws, size_t ws_bytes, cudaStream_t s);
+size_t tc_split_ws(int n, int k, int T);
+constexpr int kTcNv4 = 0, kTcQ8 = 1;
+constexpr int kTcRows = 16;   // rows a decode GEMV launch takes
 
 constexpr int kBoltLatent = 1024;   // moe_up's k, moe_down's n, k_combine's width (bolt_kernels.cu:682-695, 1714-1727)
 constexpr int kBoltTopN = 9;        // routed experts a token (bolt_common.h:25)
@@ -52,6 +63,68 @@ static GemvArgs slab_args(const IQ2Slab& slab, const MoeWork& w, int n, int k, i
     a.act_div = act_div;
     a.act_split = 1 << 30;
     return a;
+}
+
+// The K-slice partials of the shims' decode GEMVs, one buffer a (device, stream) as libbolt's mma_pack_buffer keeps
+// its per-stream row scratch (bolt_mma.cu:1183-1187): launches on one stream are ordered, so they share it.  It grows
+// only outside stream capture; a capture that needs more than it holds runs the GEMV as one K slice (same sums).
+struct ShimWs { int dev; cudaStream_t s; void* p; size_t bytes; };
+static ShimWs g_ws[16];
+static std::mutex g_ws_mu;
+
+static void* shim_ws(cudaStream_t s, size_t need, size_t* have) {
+    *have = 0;
+    if (need == 0) return nullptr;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(g_ws_mu);
+    ShimWs* slot = nullptr;
+    for (auto& w : g_ws)
+        if (w.p && w.dev == dev && w.s == s) { slot = &w; break; }
+    if (!slot)
+        for (auto& w : g_ws)
+            if (!w.p) { slot = &w; break; }
+    if (!slot) return nullptr;
+    if (slot->p && slot->bytes >= need) {
+        *have = slot->bytes;
+        return slot->p;
+    }
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+        *have = slot->p ? slot->bytes : 0;
+        return slot->p;
+    }
+    const size_t bytes = need > (size_t(16) << 20) ? need : (size_t(16) << 20);
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        *have = slot->p ? slot->bytes : 0;
+        return slot->p;
+    }
+    if (slot->p) {
+        cudaStreamSynchronize(s);   // the old buffer's last readers
+        cudaFree(slot->p);
+    }
+    *slot = {dev, s, p, bytes};
+    *have = bytes;
+    return p;
+}
+
+// W x for T rows in 16-row pieces, libbolt's mma_* over the split planes
+static void tc_rows(const char* what, int fmt, const uint8_t* qt, const uint8_t* sct, float s2, int n, int k,
+                    const float* x, int ldx, float* y, int ldy, int T, cudaStream_t s) {
+    if (T <= 0) return;
+    size_t have = 0;
+    void* ws = shim_ws(s, tc_split_ws(n, k, T < kTcRows ? T : kTcRows), &have);
+    for (int t0 = 0; t0 < T; t0 += kTcRows) {
+        const int rows = T - t0 < kTcRows ? T - t0 : kTcRows;
+        const int st = tc_gemv_split(fmt, qt, sct, s2, n, k, x + (size_t)t0 * ldx, ldx, rows, y + (size_t)t0 * ldy, ldy,
+                                     ws, have, s);
+        if (st != B200Q_OK) {
+            report(what, st);
+            return;
+        }
+    }
 }
 
 }  // namespace b200q
@@ -138,4 +211,42 @@ void moe_coop_dense(cudaStream_t s, const IQ2Slab& w, const MoeWork& mw, int T, 
 // combine_k (bolt_kernels.cu:1714-1727): out[t][0 .. 1024) = sum over the 9 picks of rw * o[t * 9 + k]
 void k_combine(cudaStream_t s, const float* o, const float* rw, float* out, int T) {
     report("k_combine", b200q_combine(o, rw, nullptr, T, kBoltTopN, kBoltLatent, out, B200Q_F32, s));
+}
+
+// tile_bytes_* (bolt_mma.cu:1221-1224): ceil(n/16) units of 16 rows a 64 (NVFP4) or 32 (Q8_0) k, 512 code bytes each,
+// and 64 / 32 scale bytes each
+size_t tile_bytes_nv4(int n, int k) { return (size_t)((n + 15) / 16) * (k / 64) * 512; }
+size_t tile_scale_bytes_nv4(int n, int k) { return (size_t)((n + 15) / 16) * (k / 64) * 64; }
+size_t tile_bytes_q8(int n, int k) { return (size_t)((n + 15) / 16) * (k / 32) * 512; }
+size_t tile_scale_bytes_q8(int n, int k) { return (size_t)((n + 15) / 16) * (k / 32) * 32; }
+
+// tile_nv4 / tile_q8 (bolt_mma.cu:1365-1366, via load_nv4 / load_q8 bolt_host.cu:198-264)
+void tile_nv4(cudaStream_t s, const uint8_t* q, const uint8_t* sc, void* qt, void* sct, int n, int k) {
+    if (!q || !sc || !qt || !sct || n <= 0 || n % 16 || k <= 0 || k % 256) {
+        report("tile_nv4", B200Q_EINVAL);
+        return;
+    }
+    report("tile_nv4", launch_nv4_pack_split(q, sc, (uint8_t*)qt, (uint8_t*)sct, n, k, s));
+}
+void tile_q8(cudaStream_t s, const uint8_t* raw, void* qt, void* dt, int n, int k) {
+    if (!raw || !qt || !dt || n <= 0 || n % 16 || k <= 0 || k % 256) {
+        report("tile_q8", B200Q_EINVAL);
+        return;
+    }
+    report("tile_q8", launch_q8_pack_split(raw, (uint8_t*)qt, (uint8_t*)dt, n, k, s));
+}
+
+// mma_nv4 / mma_q8 (bolt_mma.cu:1190-1194): y = s2 * sum e2m1 * e4m3 * x, y = sum (q * d) * x, fp32 rows
+void mma_nv4(cudaStream_t s, const TNV4& w, const float* x, int ldx, float* y, int ldy, int T) {
+    tc_rows("mma_nv4", kTcNv4, (const uint8_t*)w.q, (const uint8_t*)w.sc, w.s2, w.n, w.k, x, ldx, y, ldy, T, s);
+}
+void mma_q8(cudaStream_t s, const TQ8& w, const float* x, int ldx, float* y, int ldy, int T) {
+    tc_rows("mma_q8", kTcQ8, (const uint8_t*)w.q, (const uint8_t*)w.d, 1.f, w.n, w.k, x, ldx, y, ldy, T, s);
+}
+// mma_q8_multi (bolt_mma.cu:1204-1217): each matrix over the same rows
+void mma_q8_multi(cudaStream_t s, const TQ8Multi& m, const float* x, int ldx, int T) {
+    for (int i = 0; i < 3; i++)
+        if (m.w[i].n > 0)
+            tc_rows("mma_q8_multi", kTcQ8, (const uint8_t*)m.w[i].q, (const uint8_t*)m.w[i].d, 1.f, m.w[i].n,
+                    m.w[i].k, x, ldx, m.y[i], m.ldy[i], T, s);
 }

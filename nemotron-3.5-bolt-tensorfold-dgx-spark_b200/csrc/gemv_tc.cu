@@ -68,7 +68,10 @@ __device__ __forceinline__ uint32_t ldg_stream1(const void* p) {
 // ---------------------------------------------------------------------------------------------------------
 constexpr int kNv4Unit = 576, kQ8Unit = 544;
 
-__global__ void nv4_pack_k(const uint8_t* __restrict__ q, const uint8_t* __restrict__ sc, uint8_t* __restrict__ out, int n, int k) {
+// qo / so: a unit's 512 code bytes and 64 scale bytes, units qstride / sstride apart (the t16 unit: out, out + 512,
+// both 576; the split form: two planes, 512 and 64)
+__global__ void nv4_pack_k(const uint8_t* __restrict__ q, const uint8_t* __restrict__ sc, uint8_t* __restrict__ qo,
+                           uint8_t* __restrict__ so, int qstride, int sstride, int n, int k) {
     pdl_wait();
     const int steps = k / 64;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -87,17 +90,20 @@ __global__ void nv4_pack_k(const uint8_t* __restrict__ q, const uint8_t* __restr
             for (int r = 0; r < 4; r++) v |= (nib(rr[r], kk[r]) | nib(rr[r], kk[r] + 1) << 4) << (8 * r);
             w[j] = v;
         }
-        uint8_t* u = out + (size_t)unit * kNv4Unit;
-        reinterpret_cast<uint4*>(u)[lane] = make_uint4(w[0], w[1], w[2], w[3]);
+        reinterpret_cast<uint4*>(qo + (size_t)unit * qstride)[lane] = make_uint4(w[0], w[1], w[2], w[3]);
+        uint8_t* us = so + (size_t)unit * sstride;
         if (t == 0) {
             for (int h = 0; h < 2; h++)
-                for (int j = 0; j < 4; j++) u[512 + 8 * g + 4 * h + j] = sc[(size_t)(16 * tile + g + 8 * h) * (k / 16) + 4 * s + j];
+                for (int j = 0; j < 4; j++) us[8 * g + 4 * h + j] = sc[(size_t)(16 * tile + g + 8 * h) * (k / 16) + 4 * s + j];
         }
     }
     pdl_trigger();
 }
 
-__global__ void q8_pack_k(const uint8_t* __restrict__ raw, uint8_t* __restrict__ out, int n, int k) {
+// qo / so: a unit's 512 int8 bytes and 32 scale bytes, units qstride / sstride apart (t16: out, out + 512, both 544;
+// the split form: two planes, 512 and 32)
+__global__ void q8_pack_k(const uint8_t* __restrict__ raw, uint8_t* __restrict__ qo, uint8_t* __restrict__ so,
+                          int qstride, int sstride, int n, int k) {
     pdl_wait();
     const int nb = k / 32;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -107,7 +113,8 @@ __global__ void q8_pack_k(const uint8_t* __restrict__ raw, uint8_t* __restrict__
         const int tile = (int)(unit / nb), b = (int)(unit % nb);
         const int g = lane >> 2, t = lane & 3;
         auto val = [&](int row, int kk) { return raw[((size_t)row * nb + b) * 34 + 2 + kk]; };
-        uint8_t* u = out + (size_t)unit * kQ8Unit;
+        uint8_t* u = qo + (size_t)unit * qstride;
+        uint8_t* us = so + (size_t)unit * sstride;
         for (int uu = 0; uu < 2; uu++) {
             const int k0 = 16 * uu + 2 * t;
             const int rr[4] = {16 * tile + g, 16 * tile + g + 8, 16 * tile + g, 16 * tile + g + 8};
@@ -120,8 +127,8 @@ __global__ void q8_pack_k(const uint8_t* __restrict__ raw, uint8_t* __restrict__
         if (t == 0) {
             for (int h = 0; h < 2; h++) {
                 const uint8_t* blk = raw + ((size_t)(16 * tile + g + 8 * h) * nb + b) * 34;
-                u[512 + 4 * g + 2 * h] = blk[0];
-                u[512 + 4 * g + 2 * h + 1] = blk[1];
+                us[4 * g + 2 * h] = blk[0];
+                us[4 * g + 2 * h + 1] = blk[1];
             }
         }
     }
@@ -140,6 +147,7 @@ struct TcArgs {
     float s2;       // NVFP4 tensor scale (1 for Q8_0)
     float* out;     // KS == 1: y [T][ldy]; else partials [KS][T][n]
     int ldo;
+    const uint8_t* wsc;   // the split layout (libbolt's tile buffers): w holds the units' 512 code bytes, wsc their scales
 };
 
 constexpr int kTcWarps = 8;
@@ -170,7 +178,7 @@ __device__ __forceinline__ void q8_frag(uint32_t w0, uint32_t w1, uint32_t (&a)[
     a[3] = hsub2(prmt(x1, 0x64646464u, 0x7362u), bias);
 }
 
-template <int FMT, int NT>
+template <int FMT, int NT, bool SPLIT>
 __global__ void __launch_bounds__(kTcWarps * 32) tc_gemv_k(TcArgs a) {
     pdl_wait();
     extern __shared__ __align__(16) unsigned char dyn[];
@@ -207,15 +215,19 @@ __global__ void __launch_bounds__(kTcWarps * 32) tc_gemv_k(TcArgs a) {
         };
         if constexpr (FMT == kFmtNv4) {
             const int steps = a.k / 64, s0 = k0 / 64, ns = len / 64;
-            const uint8_t* base = a.w + ((size_t)tile * steps + s0) * kNv4Unit;
+            // a unit's codes and scales: one 576-byte unit, or the two planes of the split layout
+            constexpr int QS = SPLIT ? 512 : kNv4Unit, SS = SPLIT ? 64 : kNv4Unit;
+            const size_t u0 = (size_t)tile * steps + s0;
+            const uint8_t* base = a.w + u0 * QS;
+            const uint8_t* sbase = SPLIT ? a.wsc + u0 * SS : base + 512;
             constexpr int PF = 4;
             uint4 qb[PF];
             uint2 sb[PF];
 #pragma unroll
             for (int i = 0; i < PF; i++) {
                 if (i < ns) {
-                    qb[i] = ldg_stream(base + (size_t)i * kNv4Unit + 16 * lane);
-                    sb[i] = ldg_stream2(base + (size_t)i * kNv4Unit + 512 + 8 * g);
+                    qb[i] = ldg_stream(base + (size_t)i * QS + 16 * lane);
+                    sb[i] = ldg_stream2(sbase + (size_t)i * SS + 8 * g);
                 }
             }
             for (int s = 0; s < ns; s += PF) {
@@ -225,8 +237,8 @@ __global__ void __launch_bounds__(kTcWarps * 32) tc_gemv_k(TcArgs a) {
                         const uint4 q = qb[i];
                         const uint2 sc = sb[i];
                         if (s + i + PF < ns) {
-                            qb[i] = ldg_stream(base + (size_t)(s + i + PF) * kNv4Unit + 16 * lane);
-                            sb[i] = ldg_stream2(base + (size_t)(s + i + PF) * kNv4Unit + 512 + 8 * g);
+                            qb[i] = ldg_stream(base + (size_t)(s + i + PF) * QS + 16 * lane);
+                            sb[i] = ldg_stream2(sbase + (size_t)(s + i + PF) * SS + 8 * g);
                         }
                         // the step's scales: half2 (row g, row g + 8) for blocks 0,1 and 2,3, duplicated per row
                         const uint32_t h01 = e4m3x2_f16x2(prmt(sc.x, sc.y, 0x5140u));   // bytes g.0, g8.0 | g.1, g8.1
@@ -253,15 +265,18 @@ __global__ void __launch_bounds__(kTcWarps * 32) tc_gemv_k(TcArgs a) {
             }
         } else {
             const int nbk = a.k / 32, b0i = k0 / 32, nblk = len / 32;
-            const uint8_t* base = a.w + ((size_t)tile * nbk + b0i) * kQ8Unit;
+            constexpr int QS = SPLIT ? 512 : kQ8Unit, SS = SPLIT ? 32 : kQ8Unit;
+            const size_t u0 = (size_t)tile * nbk + b0i;
+            const uint8_t* base = a.w + u0 * QS;
+            const uint8_t* sbase = SPLIT ? a.wsc + u0 * SS : base + 512;
             constexpr int PF = 4;
             uint4 qb[PF];
             uint32_t db[PF];
 #pragma unroll
             for (int i = 0; i < PF; i++) {
                 if (i < nblk) {
-                    qb[i] = ldg_stream(base + (size_t)i * kQ8Unit + 16 * lane);
-                    db[i] = ldg_stream1(base + (size_t)i * kQ8Unit + 512 + 4 * g);
+                    qb[i] = ldg_stream(base + (size_t)i * QS + 16 * lane);
+                    db[i] = ldg_stream1(sbase + (size_t)i * SS + 4 * g);
                 }
             }
             for (int b = 0; b < nblk; b += PF) {
@@ -271,8 +286,8 @@ __global__ void __launch_bounds__(kTcWarps * 32) tc_gemv_k(TcArgs a) {
                         const uint4 q = qb[i];
                         const uint32_t dd = db[i];
                         if (b + i + PF < nblk) {
-                            qb[i] = ldg_stream(base + (size_t)(b + i + PF) * kQ8Unit + 16 * lane);
-                            db[i] = ldg_stream1(base + (size_t)(b + i + PF) * kQ8Unit + 512 + 4 * g);
+                            qb[i] = ldg_stream(base + (size_t)(b + i + PF) * QS + 16 * lane);
+                            db[i] = ldg_stream1(sbase + (size_t)(b + i + PF) * SS + 4 * g);
                         }
                         const float dg = __half2float(__ushort_as_half((unsigned short)(dd & 0xffff)));
                         const float dg8 = __half2float(__ushort_as_half((unsigned short)(dd >> 16)));
@@ -346,25 +361,28 @@ static size_t splitk_ws(int n, int k, int T) {
     return KS > 1 ? (size_t)KS * T * n * sizeof(float) : 0;
 }
 
+template <int FMT, int NT, bool SPLIT>
+static cudaError_t launch_tc(const TcArgs& a, dim3 grid, size_t smem, cudaStream_t s) {
+    static size_t opted = 0;
+    if (smem > 48 * 1024 && smem > opted) {
+        cudaFuncSetAttribute(tc_gemv_k<FMT, NT, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        opted = smem;
+    }
+    return launch(tc_gemv_k<FMT, NT, SPLIT>, grid, dim3(kTcWarps * 32), smem, s, a);
+}
+
 template <int FMT>
 static int run_tc(const uint8_t* w, float s2, int n, int k, const void* x, int x_dtype, int ldx, int T, float* y, int ldy,
-                  void* ws, size_t ws_bytes, cudaStream_t s) {
+                  void* ws, size_t ws_bytes, cudaStream_t s, const uint8_t* wsc = nullptr) {
     int L = slice_len(n, k);
     int KS = (k + L - 1) / L;
     if (KS > 1 && (!ws || ws_bytes < (size_t)KS * T * n * sizeof(float))) { L = k; KS = 1; }   // no workspace: one slice
-    TcArgs a{w, n, k, x, x_dtype, ldx, T, L, s2, KS > 1 ? (float*)ws : y, ldy};
+    TcArgs a{w, n, k, x, x_dtype, ldx, T, L, s2, KS > 1 ? (float*)ws : y, ldy, wsc};
     const size_t smem = (size_t)(T > 8 ? 16 : 8) * (L + 8) * 2;
     const dim3 grid((n / 16 + kTcWarps - 1) / kTcWarps, KS);
     cudaError_t e;
-    if (T > 8) {
-        static size_t opted = 0;
-        if (smem > 48 * 1024 && smem > opted) { cudaFuncSetAttribute(tc_gemv_k<FMT, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); opted = smem; }
-        e = launch(tc_gemv_k<FMT, 2>, grid, dim3(kTcWarps * 32), smem, s, a);
-    } else {
-        static size_t opted = 0;
-        if (smem > 48 * 1024 && smem > opted) { cudaFuncSetAttribute(tc_gemv_k<FMT, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); opted = smem; }
-        e = launch(tc_gemv_k<FMT, 1>, grid, dim3(kTcWarps * 32), smem, s, a);
-    }
+    if (wsc) e = T > 8 ? launch_tc<FMT, 2, true>(a, grid, smem, s) : launch_tc<FMT, 1, true>(a, grid, smem, s);
+    else e = T > 8 ? launch_tc<FMT, 2, false>(a, grid, smem, s) : launch_tc<FMT, 1, false>(a, grid, smem, s);
     if (e != cudaSuccess) return status_from(e);
     if (KS > 1) {
         const int64_t tot = (int64_t)T * n;
@@ -375,6 +393,25 @@ static int run_tc(const uint8_t* w, float s2, int n, int k, const void* x, int x
 }
 
 static bool tc_shape_ok(int64_t n, int k) { return n > 0 && n % 16 == 0 && k > 0 && k % 256 == 0; }
+
+// the split forms of the t16 layouts, for libbolt's tile buffers (bolt_shim.cu)
+cudaError_t launch_nv4_pack_split(const uint8_t* q, const uint8_t* sc, uint8_t* qt, uint8_t* sct, int n, int k,
+                                  cudaStream_t s) {
+    const int64_t th = (int64_t)(n / 16) * (k / 64) * 32;
+    return launch(nv4_pack_k, dim3((unsigned)((th + 255) / 256)), dim3(256), 0, s, q, sc, qt, sct, 512, 64, n, k);
+}
+cudaError_t launch_q8_pack_split(const uint8_t* raw, uint8_t* qt, uint8_t* dt, int n, int k, cudaStream_t s) {
+    const int64_t th = (int64_t)(n / 16) * (k / 32) * 32;
+    return launch(q8_pack_k, dim3((unsigned)((th + 255) / 256)), dim3(256), 0, s, raw, qt, dt, 512, 32, n, k);
+}
+// the decode GEMVs over split planes; ws may be null (one K slice)
+int tc_gemv_split(int fmt, const uint8_t* qt, const uint8_t* sct, float s2, int n, int k, const float* x, int ldx, int T,
+                  float* y, int ldy, void* ws, size_t ws_bytes, cudaStream_t s) {
+    if (!qt || !sct || !x || !y || !tc_shape_ok(n, k) || T <= 0 || T > 16 || ldx < k || ldy < n) return B200Q_EINVAL;
+    return fmt == kFmtNv4 ? run_tc<kFmtNv4>(qt, s2, n, k, x, B200Q_F32, ldx, T, y, ldy, ws, ws_bytes, s, sct)
+                          : run_tc<kFmtQ8>(qt, 1.f, n, k, x, B200Q_F32, ldx, T, y, ldy, ws, ws_bytes, s, sct);
+}
+size_t tc_split_ws(int n, int k, int T) { return tc_shape_ok(n, k) && T > 0 ? splitk_ws(n, k, T) : 0; }
 
 }  // namespace b200q
 
@@ -389,7 +426,7 @@ int b200q_nv4_pack(const void* q, const void* sc, void* packed, int64_t n, int k
     if (!q || !sc || !packed || !tc_shape_ok(n, k) || n > (1 << 30)) return B200Q_EINVAL;
     const int64_t th = (n / 16) * (k / 64) * 32;
     launch(nv4_pack_k, dim3((unsigned)((th + 255) / 256)), dim3(256), 0, (cudaStream_t)stream, (const uint8_t*)q,
-           (const uint8_t*)sc, (uint8_t*)packed, (int)n, k);
+           (const uint8_t*)sc, (uint8_t*)packed, (uint8_t*)packed + 512, kNv4Unit, kNv4Unit, (int)n, k);
     return launched();
 }
 
@@ -397,7 +434,7 @@ int b200q_q8_pack(const void* raw, void* packed, int64_t n, int k, void* stream)
     if (!raw || !packed || !tc_shape_ok(n, k) || n > (1 << 30)) return B200Q_EINVAL;
     const int64_t th = (n / 16) * (k / 32) * 32;
     launch(q8_pack_k, dim3((unsigned)((th + 255) / 256)), dim3(256), 0, (cudaStream_t)stream, (const uint8_t*)raw,
-           (uint8_t*)packed, (int)n, k);
+           (uint8_t*)packed, (uint8_t*)packed + 512, kQ8Unit, kQ8Unit, (int)n, k);
     return launched();
 }
 

@@ -47,4 +47,39 @@ void hs_k_combine(void* s, const float* o, const float* rw, float* out, int T) {
     k_combine((cudaStream_t)s, o, rw, out, T);
 }
 
+size_t hs_tile_bytes(int fmt, int scales, int n, int k) {
+    return fmt == 0 ? (scales ? tile_scale_bytes_nv4(n, k) : tile_bytes_nv4(n, k))
+                    : (scales ? tile_scale_bytes_q8(n, k) : tile_bytes_q8(n, k));
+}
+
+void hs_tile_nv4(void* s, const uint8_t* q, const uint8_t* sc, void* qt, void* sct, int n, int k) {
+    tile_nv4((cudaStream_t)s, q, sc, qt, sct, n, k);
+}
+
+void hs_tile_q8(void* s, const uint8_t* raw, void* qt, void* dt, int n, int k) { tile_q8((cudaStream_t)s, raw, qt, dt, n, k); }
+
+// mma_nv4 / mma_q8 with the views load_nv4 / load_q8 return (bolt_host.cu:198-264)
+void hs_mma_nv4(void* s, const void* qt, const void* sct, float s2, int n, int k, const float* x, int ldx, float* y,
+                int ldy, int T) {
+    const TNV4 w{(const uint4*)qt, (const uint2*)sct, s2, n, k};
+    mma_nv4((cudaStream_t)s, w, x, ldx, y, ldy, T);
+}
+
+void hs_mma_q8(void* s, const void* qt, const void* dt, int n, int k, const float* x, int ldx, float* y, int ldy, int T) {
+    const TQ8 w{(const uint4*)qt, (const uint32_t*)dt, n, k};
+    mma_q8((cudaStream_t)s, w, x, ldx, y, ldy, T);
+}
+
+// three matrices: q* / d* / n* / y* / ldy* for each (n = 0 leaves one unused)
+void hs_mma_q8_multi(void* s, const void* const* qt, const void* const* dt, const int* n, int k, const float* x, int ldx,
+                     float* const* y, const int* ldy, int T) {
+    TQ8Multi m{};
+    for (int i = 0; i < 3; i++) {
+        m.w[i] = TQ8{(const uint4*)qt[i], (const uint32_t*)dt[i], n[i], n[i] ? k : 0};
+        m.y[i] = y[i];
+        m.ldy[i] = ldy[i];
+    }
+    mma_q8_multi((cudaStream_t)s, m, x, ldx, T);
+}
+
 }  // extern "C"

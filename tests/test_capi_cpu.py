@@ -83,3 +83,7 @@ def test_library_exports_the_libbolt_signature_shims():
     out = subprocess.run([nm, "-DC", "--defined-only", b200q.LIB_PATH], capture_output=True, text=True).stdout
     missing = [n for n in names if not re.search(r"\b" + n + r"\(CUstream_st\*", out)]
     assert not missing, missing
+    sizes = sorted(set(re.findall(r"^size_t (\w+)\(int n, int k\)", text, flags=re.M)))
+    assert {"tile_bytes_nv4", "tile_scale_bytes_q8"} <= set(sizes)
+    missing = [n for n in sizes if not re.search(r"\b" + n + r"\(int, int\)", out)]
+    assert not missing, missing

@@ -31,9 +31,15 @@ def _harness():
         "hs_moe_down": [vp, vp, vp, sz, sz, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32],
         "hs_moe_coop_dense": [vp, vp, vp, i32, vp, vp, vp, i32, i32, i32, i32],
         "hs_k_combine": [vp, vp, vp, vp, i32],
+        "hs_tile_nv4": [vp, vp, vp, vp, vp, i32, i32],
+        "hs_tile_q8": [vp, vp, vp, vp, i32, i32],
+        "hs_mma_nv4": [vp, vp, vp, f32, i32, i32, vp, i32, vp, i32, i32],
+        "hs_mma_q8": [vp, vp, vp, i32, i32, vp, i32, vp, i32, i32],
+        "hs_mma_q8_multi": [vp, vp, vp, vp, i32, vp, i32, vp, vp, i32],
     }
     for n, a in sig.items():
         getattr(L, n).restype, getattr(L, n).argtypes = None, a
+    L.hs_tile_bytes.restype, L.hs_tile_bytes.argtypes = sz, [i32, i32, i32, i32]
     return L
 
 
@@ -125,3 +131,116 @@ def test_shim_coop_dense_and_combine_match_libbolt():
     out = torch.empty(T, 1024, device=DEV)
     L.hs_k_combine(s(), p(d(i["o"])), p(d(i["rw"])), p(out), T)
     assert np.array_equal(out.cpu().numpy(), o["out"])
+
+
+def nv4_tiles(L, q, sc, n, k):
+    """the qt / sct buffers load_nv4 allocates (tile_bytes_nv4, tile_scale_bytes_nv4), filled by tile_nv4"""
+    qt = torch.empty(L.hs_tile_bytes(0, 0, n, k), dtype=torch.uint8, device=DEV)
+    sct = torch.empty(L.hs_tile_bytes(0, 1, n, k), dtype=torch.uint8, device=DEV)
+    L.hs_tile_nv4(s(), p(d(q)), p(d(sc)), p(qt), p(sct), n, k)
+    _KEEP.extend([qt, sct])
+    return qt, sct
+
+
+def q8_tiles(L, blocks, n, k):
+    qt = torch.empty(L.hs_tile_bytes(1, 0, n, k), dtype=torch.uint8, device=DEV)
+    dt = torch.empty(L.hs_tile_bytes(1, 1, n, k), dtype=torch.uint8, device=DEV)
+    L.hs_tile_q8(s(), p(d(blocks)), p(qt), p(dt), n, k)
+    _KEEP.extend([qt, dt])
+    return qt, dt
+
+
+def golden_q8_blocks(i):
+    n, k = i["q"].shape
+    blocks = np.concatenate([i["d"].view(np.uint8).reshape(n, k // 32, 2), i["q"].view(np.uint8).reshape(n, k // 32, 32)],
+                            -1)
+    return blocks.reshape(n, -1)
+
+
+def test_shim_nv4_q8_decode_match_libbolt():
+    """tile_nv4 + mma_nv4 and tile_q8 + mma_q8 on the golden cases' inputs.  libbolt's mma_nv4 / mma_q8 round the fp32
+    rows to fp16 before the tensor cores (PNV4 / PQ8 kBF = false, bolt_mma.cu:103, 182), as the shims do: against
+    the oracle on those rounded rows 1e-5 (fp32 sums in another order); against the fixtures, which hold libbolt's
+    fp32-row gemv_nv4 / gemv_q8, within the rows' fp16 rounding (relative L2 1e-3)."""
+    import oracle as O
+    from helpers import rel_l2
+    L = _harness()
+    i, o = golden("gemv_nv4")
+    n, k = i["q"].shape[0], i["q"].shape[1] * 2
+    T = i["x"].shape[0]
+    x16 = i["x"].astype(np.float16).astype(np.float32)
+    qt, sct = nv4_tiles(L, i["q"], i["sc"], n, k)
+    y = torch.full((T, n), -1.0, device=DEV)
+    L.hs_mma_nv4(s(), p(qt), p(sct), float(i["s2"]), n, k, p(d(i["x"])), k, p(y), n, T)
+    y = y.cpu().numpy()
+    ref = O.nv4_gemm_exact(i["q"], i["sc"], float(i["s2"]), n, k, x16)
+    assert np.allclose(y, ref, rtol=1e-5, atol=1e-5 * np.abs(ref).max())
+    assert rel_l2(y, o["y"]) < 1e-3
+    i, o = golden("gemv_q8")
+    n, k = i["q"].shape
+    x16 = i["x"].astype(np.float16).astype(np.float32)
+    blocks = golden_q8_blocks(i)
+    qt, dt = q8_tiles(L, blocks, n, k)
+    y = torch.full((T, n), -1.0, device=DEV)
+    L.hs_mma_q8(s(), p(qt), p(dt), n, k, p(d(i["x"])), k, p(y), n, T)
+    y = y.cpu().numpy()
+    ref = O.q8_gemm_exact(blocks, n, k, x16)
+    assert np.allclose(y, ref, rtol=1e-5, atol=1e-5 * np.abs(ref).max())
+    assert rel_l2(y, o["y"]) < 1e-3
+    assert b200q.device_error() == 0
+
+
+@pytest.mark.parametrize("n,k", [(64, 256), (4096, 2048)])
+def test_shim_tiles_are_the_split_t16_units(n, k):
+    """libbolt's two tile buffers hold this engine's t16 units split in two: the 512 code bytes of each unit in qt,
+    its 64 (NVFP4) or 32 (Q8_0) scale bytes in sct / dt, in unit order"""
+    from test_gpu_nv4_q8 import nv4_weights, q8_blocks
+    L = _harness()
+    q, sc = nv4_weights(n + 1, n, k)
+    qt, sct = nv4_tiles(L, q, sc, n, k)
+    units = b200q.tile_nv4(d(q), d(sc), n, k).view(-1, 576)
+    assert torch.equal(qt.view(-1, 512), units[:, :512]) and torch.equal(sct.view(-1, 64), units[:, 512:])
+    blocks = q8_blocks(n + 2, n, k)
+    qt, dt = q8_tiles(L, blocks, n, k)
+    units = b200q.tile_q8(d(blocks), n, k).view(-1, 544)
+    assert torch.equal(qt.view(-1, 512), units[:, :512]) and torch.equal(dt.view(-1, 32), units[:, 512:])
+
+
+def test_shim_mma_rows_and_multi_match_engine_gemv():
+    """mma_nv4 / mma_q8 over T = 37 fp32 rows run 16-row decode GEMVs on the split planes: bit for bit the engine's
+    GEMV on the joined units, piece by piece; mma_q8_multi (q, k, v and a zeroed slot) is each mma_q8 alone"""
+    from test_gpu_nv4_q8 import nv4_weights, q8_blocks
+    L = _harness()
+    n, k, T = 4096, 4096, 37
+    x = torch.randn(T, k, device=DEV)
+    q, sc = nv4_weights(5, n, k)
+    qt, sct = nv4_tiles(L, q, sc, n, k)
+    w = b200q.tile_nv4(d(q), d(sc), n, k)
+    y = torch.full((T, n), -1.0, device=DEV)
+    L.hs_mma_nv4(s(), p(qt), p(sct), 0.37, n, k, p(x), k, p(y), n, T)
+    ref = torch.cat([b200q.mma_nv4(w, 0.37, n, k, x[t0:t0 + 16]) for t0 in range(0, T, 16)])
+    assert torch.equal(y, ref)
+    ns = [4096, 1024, 1024]
+    tiles = [q8_tiles(L, q8_blocks(20 + j, nj, k), nj, k) for j, nj in enumerate(ns)]
+    refs = []
+    for j, nj in enumerate(ns):
+        yj = torch.full((T, nj), -1.0, device=DEV)
+        L.hs_mma_q8(s(), p(tiles[j][0]), p(tiles[j][1]), nj, k, p(x), k, p(yj), nj, T)
+        wj = b200q.tile_q8(d(q8_blocks(20 + j, nj, k)), nj, k)
+        assert torch.equal(yj, torch.cat([b200q.mma_q8(wj, nj, k, x[t0:t0 + 16]) for t0 in range(0, T, 16)]))
+        refs.append(yj)
+    for used in ([0, 1, 2], [0, 2]):
+        ys = [torch.full((T, nj), -1.0, device=DEV) for nj in ns]
+        arr = lambda vals, ty: (ty * 3)(*vals)
+        qv = arr([tiles[j][0].data_ptr() if j in used else 0 for j in range(3)], ctypes.c_void_p)
+        dv = arr([tiles[j][1].data_ptr() if j in used else 0 for j in range(3)], ctypes.c_void_p)
+        nv = arr([ns[j] if j in used else 0 for j in range(3)], ctypes.c_int)
+        yv = arr([ys[j].data_ptr() for j in range(3)], ctypes.c_void_p)
+        lv = arr(ns, ctypes.c_int)
+        L.hs_mma_q8_multi(s(), qv, dv, nv, k, p(x), k, yv, lv, T)
+        for j in range(3):
+            if j in used:
+                assert torch.equal(ys[j], refs[j])
+            else:
+                assert bool((ys[j] == -1.0).all())
+    assert b200q.device_error() == 0
