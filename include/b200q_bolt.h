@@ -8,7 +8,9 @@
  *   load time   tile_bytes_nv4, tile_scale_bytes_nv4, tile_bytes_q8, tile_scale_bytes_q8, tile_nv4, tile_q8 (the same
  *               buffer sizes as libbolt's tiles, holding this engine's t16 units split into a code plane and a scale
  *               plane);
- *   per step    mma_nv4, mma_q8, mma_q8_multi.
+ *   per step    mma_nv4, mma_q8, mma_q8_multi;
+ * and for the shared expert (load_iq2, bolt_host.cu:266-283, and bolt_host.cu:680-681): tile_bytes_iq2,
+ * tile_scale_bytes_iq2, tile_iq2, mma_iq2.
  * The structs repeat libbolt's member order and types so the bytes match.  libbolt's fixed model shapes stay fixed
  * here: the latent width 1024 (moe_up's k, moe_down's n, k_combine's width) and TOPN = 9 routed experts a token.
  * As in libbolt the launchers are asynchronous on the given stream and return nothing; a launch error is printed
@@ -59,3 +61,12 @@ void mma_nv4(cudaStream_t s, const TNV4& w, const float* x, int ldx, float* y, i
 void mma_q8(cudaStream_t s, const TQ8& w, const float* x, int ldx, float* y, int ldy, int T);
 /* each matrix with n > 0 (libbolt leaves an unused one zeroed) into its own y */
 void mma_q8_multi(cudaStream_t s, const TQ8Multi& m, const float* x, int ldx, int T);
+
+/* an IQ2_XXS matrix: q = 64 code bytes a row and 256 k, d = one fp16 scale a row and 256 k (bolt_common.h:49); with
+ * this engine's tile_iq2 they hold the split rt32 planes (n % 32 == 0) */
+struct TIQ2 { const uint4* q; const uint16_t* d; int n, k; };
+size_t tile_bytes_iq2(int n, int k);
+size_t tile_scale_bytes_iq2(int n, int k);
+void tile_iq2(cudaStream_t s, const uint8_t* raw, void* qt, void* dt, int n, int k);
+/* y[t][0 .. n) = W x[t] (epi 1: relu(.)^2) for fp32 rows, computed on the rows quantised to int8 per 32 */
+void mma_iq2(cudaStream_t s, const TIQ2& w, const float* x, int ldx, float* y, int ldy, int T, int epi = 0);

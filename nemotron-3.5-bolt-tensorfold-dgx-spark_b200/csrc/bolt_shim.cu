@@ -65,14 +65,16 @@ static GemvArgs slab_args(const IQ2Slab& slab, const MoeWork& w, int n, int k, i
     return a;
 }
 
-// The K-slice partials of the shims' decode GEMVs, one buffer a (device, stream) as libbolt's mma_pack_buffer keeps
-// its per-stream row scratch (bolt_mma.cu:1183-1187): launches on one stream are ordered, so they share it.  It grows
-// only outside stream capture; a capture that needs more than it holds runs the GEMV as one K slice (same sums).
-struct ShimWs { int dev; cudaStream_t s; void* p; size_t bytes; };
-static ShimWs g_ws[16];
+// The shims' scratch, one buffer a (device, stream, use) as libbolt's mma_pack_buffer keeps its per-stream row
+// scratch (bolt_mma.cu:1183-1187): launches on one stream are ordered, so they share it.  It grows only outside stream
+// capture.  Uses: the K-slice partials of the decode GEMVs (a capture that needs more than the buffer holds runs the
+// GEMV as one K slice, the same sums), and mma_iq2's int8 rows.
+enum { kWsPartials = 0, kWsRows = 1 };
+struct ShimWs { int dev; cudaStream_t s; int use; void* p; size_t bytes; };
+static ShimWs g_ws[32];
 static std::mutex g_ws_mu;
 
-static void* shim_ws(cudaStream_t s, size_t need, size_t* have) {
+static void* shim_ws(cudaStream_t s, size_t need, size_t* have, int use = kWsPartials) {
     *have = 0;
     if (need == 0) return nullptr;
     int dev = 0;
@@ -80,7 +82,7 @@ static void* shim_ws(cudaStream_t s, size_t need, size_t* have) {
     std::lock_guard<std::mutex> lock(g_ws_mu);
     ShimWs* slot = nullptr;
     for (auto& w : g_ws)
-        if (w.p && w.dev == dev && w.s == s) { slot = &w; break; }
+        if (w.p && w.dev == dev && w.s == s && w.use == use) { slot = &w; break; }
     if (!slot)
         for (auto& w : g_ws)
             if (!w.p) { slot = &w; break; }
@@ -105,7 +107,7 @@ static void* shim_ws(cudaStream_t s, size_t need, size_t* have) {
         cudaStreamSynchronize(s);   // the old buffer's last readers
         cudaFree(slot->p);
     }
-    *slot = {dev, s, p, bytes};
+    *slot = {dev, s, use, p, bytes};
     *have = bytes;
     return p;
 }
@@ -249,4 +251,58 @@ void mma_q8_multi(cudaStream_t s, const TQ8Multi& m, const float* x, int ldx, in
         if (m.w[i].n > 0)
             tc_rows("mma_q8_multi", kTcQ8, (const uint8_t*)m.w[i].q, (const uint8_t*)m.w[i].d, 1.f, m.w[i].n,
                     m.w[i].k, x, ldx, m.y[i], m.ldy[i], T, s);
+}
+
+// tile_bytes_iq2 / tile_scale_bytes_iq2 (bolt_mma.cu:1226-1227): 64 code bytes and one fp16 scale a row and 256 k,
+// the byte counts of this engine's split rt32 planes (2048 + 64 bytes a 32-row unit)
+size_t tile_bytes_iq2(int n, int k) { return (size_t)((n + 15) / 16) * (k / 64) * 256; }
+size_t tile_scale_bytes_iq2(int n, int k) { return (size_t)((n + 15) / 16) * (k / 256) * 32; }
+
+// tile_iq2 (bolt_mma.cu:1336-1361, via load_iq2 bolt_host.cu:266-283): the checkpoint's blocks [n][k/256][66] into qt
+// (codes) and dt (scales) as the split rt32 layout; n % 32 == 0
+void tile_iq2(cudaStream_t s, const uint8_t* raw, void* qt, void* dt, int n, int k) {
+    if (!raw || !qt || !dt || n <= 0 || n % kIq2Tile || k <= 0 || k % 256) {
+        report("tile_iq2", B200Q_EINVAL);
+        return;
+    }
+    report("tile_iq2", launch_iq2_pack_split(raw, (uint8_t*)qt, (uint8_t*)dt, n, k, s));
+}
+
+// mma_iq2 (bolt_mma.cu:1196-1203), the shared expert (bolt_host.cu:680-681): y[t] = W x[t], epi 1 = relu(.)^2.  The
+// rows are quantised to int8 per 32 (quant_rows_k) into a per-stream scratch and the dense expert GEMV runs on them,
+// the arithmetic libbolt's moe_coop_dense / moe_tile_dense use for the shared expert; libbolt's mma_iq2 rounds the
+// rows to bf16 instead, and the two agree to the rows' rounding.
+void mma_iq2(cudaStream_t s, const TIQ2& w, const float* x, int ldx, float* y, int ldy, int T, int epi) {
+    if (T <= 0) return;
+    if (!w.q || !w.d || !x || !y || w.n <= 0 || w.n % kIq2Tile || w.k <= 0 || w.k % 256 || ldx < w.k || ldy < w.n) {
+        report("mma_iq2", B200Q_EINVAL);
+        return;
+    }
+    const size_t qbytes = ((size_t)T * w.k + 255) / 256 * 256;
+    size_t have = 0;
+    uint8_t* rows = (uint8_t*)shim_ws(s, qbytes + (size_t)T * (w.k / 32) * sizeof(float), &have, kWsRows);
+    if (!rows || have < qbytes + (size_t)T * (w.k / 32) * sizeof(float)) {
+        report("mma_iq2", B200Q_ENOSPACE);   // first grown inside a stream capture
+        return;
+    }
+    int8_t* xq = (int8_t*)rows;
+    float* xs = (float*)(rows + qbytes);
+    const int st = b200q_quant_rows(x, B200Q_F32, ldx, xq, w.k, xs, w.k / 32, T, w.k, s);
+    if (st != B200Q_OK) {
+        report("mma_iq2", st);
+        return;
+    }
+    GemvArgs a = {};
+    a.slab = (const uint8_t*)w.q;
+    a.dplane = (const uint8_t*)w.d;
+    a.n = w.n;
+    a.k = w.k;
+    a.dense_rows = T;
+    a.act_div = 1;
+    a.act_split = 1 << 30;
+    a.xq = xq;
+    a.xs = xs;
+    a.y = y;
+    a.ldy = ldy;
+    report("mma_iq2", launch_iq2_gemv(a, 1, T, epi ? 1 : 0, s));
 }

@@ -47,9 +47,20 @@ void hs_k_combine(void* s, const float* o, const float* rw, float* out, int T) {
     k_combine((cudaStream_t)s, o, rw, out, T);
 }
 
+// fmt 0 NVFP4, 1 Q8_0, 2 IQ2_XXS
 size_t hs_tile_bytes(int fmt, int scales, int n, int k) {
-    return fmt == 0 ? (scales ? tile_scale_bytes_nv4(n, k) : tile_bytes_nv4(n, k))
-                    : (scales ? tile_scale_bytes_q8(n, k) : tile_bytes_q8(n, k));
+    if (fmt == 0) return scales ? tile_scale_bytes_nv4(n, k) : tile_bytes_nv4(n, k);
+    if (fmt == 1) return scales ? tile_scale_bytes_q8(n, k) : tile_bytes_q8(n, k);
+    return scales ? tile_scale_bytes_iq2(n, k) : tile_bytes_iq2(n, k);
+}
+
+void hs_tile_iq2(void* s, const uint8_t* raw, void* qt, void* dt, int n, int k) { tile_iq2((cudaStream_t)s, raw, qt, dt, n, k); }
+
+// the shared expert's up (epi 1) and down as enqueue_block calls them (bolt_host.cu:680-681)
+void hs_mma_iq2(void* s, const void* qt, const void* dt, int n, int k, const float* x, int ldx, float* y, int ldy, int T,
+                int epi) {
+    const TIQ2 w{(const uint4*)qt, (const uint16_t*)dt, n, k};
+    mma_iq2((cudaStream_t)s, w, x, ldx, y, ldy, T, epi);
 }
 
 void hs_tile_nv4(void* s, const uint8_t* q, const uint8_t* sc, void* qt, void* sct, int n, int k) {

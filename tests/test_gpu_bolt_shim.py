@@ -36,6 +36,8 @@ def _harness():
         "hs_mma_nv4": [vp, vp, vp, f32, i32, i32, vp, i32, vp, i32, i32],
         "hs_mma_q8": [vp, vp, vp, i32, i32, vp, i32, vp, i32, i32],
         "hs_mma_q8_multi": [vp, vp, vp, vp, i32, vp, i32, vp, vp, i32],
+        "hs_tile_iq2": [vp, vp, vp, vp, i32, i32],
+        "hs_mma_iq2": [vp, vp, vp, i32, i32, vp, i32, vp, i32, i32, i32],
     }
     for n, a in sig.items():
         getattr(L, n).restype, getattr(L, n).argtypes = None, a
@@ -243,4 +245,62 @@ def test_shim_mma_rows_and_multi_match_engine_gemv():
                 assert torch.equal(ys[j], refs[j])
             else:
                 assert bool((ys[j] == -1.0).all())
+    assert b200q.device_error() == 0
+
+
+def iq2_tiles(L, blocks, n, k):
+    """the qt / dt buffers load_iq2 allocates (tile_bytes_iq2, tile_scale_bytes_iq2), filled by tile_iq2"""
+    qt = torch.empty(L.hs_tile_bytes(2, 0, n, k), dtype=torch.uint8, device=DEV)
+    dt = torch.empty(L.hs_tile_bytes(2, 1, n, k), dtype=torch.uint8, device=DEV)
+    L.hs_tile_iq2(s(), p(d(blocks.reshape(-1))), p(qt), p(dt), n, k)
+    _KEEP.extend([qt, dt])
+    return qt, dt
+
+
+def test_shim_iq2_tiles_are_repack_iq2_planes():
+    """tile_iq2 fills libbolt's tile buffers (the same byte counts as load_slab's qs / d) exactly as repack_iq2"""
+    L = _harness()
+    n, k = 256, 1024
+    blocks = iq2_blocks(41, n, k)
+    assert L.hs_tile_bytes(2, 0, n, k) == n * (k // 256) * 64 and L.hs_tile_bytes(2, 1, n, k) == n * (k // 256) * 2
+    qt, dt = iq2_tiles(L, blocks, n, k)
+    qs, dd = slab(L, blocks, n, k)
+    assert torch.equal(qt, qs) and torch.equal(dt, dd.view(torch.uint8))
+
+
+def test_shim_mma_iq2_shared_expert():
+    """mma_iq2 (the shared expert's up with relu^2, then down): bit for bit the oracle's int8-row arithmetic
+    (quant_rows_k, int32 chunk dots, fp32 chunk-order sums); against libbolt's fp32-row gemv_iq2 fixture and the
+    exact dequantised product within the tolerance BASELINE states for fp32 outputs (relative L2 1e-2)"""
+    import oracle as O
+    from helpers import rel_l2
+    L = _harness()
+    i, o = golden("gemv_iq2")
+    n, k = int(i["n"]), int(i["k"])
+    T = i["x"].shape[0]
+    blocks = iq2_blocks(int(i["seed"]), n, k)
+    qt, dt = iq2_tiles(L, blocks, n, k)
+    y = torch.full((T, n), -1.0, device=DEV)
+    L.hs_mma_iq2(s(), p(qt), p(dt), n, k, p(d(i["x"])), k, p(y), n, T, 0)
+    y = y.cpu().numpy()
+    xq, xs = O.quant_rows(i["x"], k)
+    assert np.array_equal(y, O.iq2_gemm_i8(blocks, n, k, xq, xs, 0))
+    assert rel_l2(y, o["y"]) < 1e-2
+    # the model's shared expert shapes: latent 1024 -> 5376 (relu^2) -> 1024, T = 21 rows
+    H, F, T = 1024, 5376, 21
+    up, down = iq2_blocks(42, F, H), iq2_blocks(43, H, F)
+    uqt, udt = iq2_tiles(L, up, F, H)
+    dqt, ddt = iq2_tiles(L, down, H, F)
+    x = np.random.default_rng(44).standard_normal((T, H)).astype(np.float32)
+    act = torch.full((T, F), -1.0, device=DEV)
+    L.hs_mma_iq2(s(), p(uqt), p(udt), F, H, p(d(x)), H, p(act), F, T, 1)
+    out = torch.full((T, H), -1.0, device=DEV)
+    L.hs_mma_iq2(s(), p(dqt), p(ddt), H, F, p(act), F, p(out), H, T, 0)
+    act_ref = O.iq2_gemm_i8(up, F, H, *O.quant_rows(x, H), 1)
+    assert np.array_equal(act.cpu().numpy(), act_ref)
+    out_ref = O.iq2_gemm_i8(down, H, F, *O.quant_rows(act_ref, F), 0)
+    assert np.array_equal(out.cpu().numpy(), out_ref)
+    # each projection against the exact product of its own input rows
+    assert rel_l2(act_ref, O.iq2_gemm_exact(up, F, H, x, 1)) < 1e-2
+    assert rel_l2(out_ref, O.iq2_gemm_exact(down, H, F, act_ref, 0)) < 1e-2
     assert b200q.device_error() == 0
