@@ -87,3 +87,28 @@ def test_library_exports_the_libbolt_signature_shims():
     assert {"tile_bytes_nv4", "tile_scale_bytes_q8"} <= set(sizes)
     missing = [n for n in sizes if not re.search(r"\b" + n + r"\(int, int\)", out)]
     assert not missing, missing
+
+
+def test_libbolt_shims_reject_bad_shapes_before_any_launch(capfd):
+    """the libbolt-signature shims return nothing, as libbolt's launchers do: a bad shape is reported on stderr
+    (prefix "b200q shim") before any CUDA call, so these run without a GPU"""
+    import build_harness
+    L = ctypes.CDLL(build_harness.build())
+    vp = ctypes.c_void_p
+    buf = ctypes.create_string_buffer(256)
+    p = ctypes.cast(buf, vp)
+    L.hs_tile_nv4.argtypes = [vp, vp, vp, vp, vp, ctypes.c_int, ctypes.c_int]
+    L.hs_tile_nv4(None, p, p, p, p, 20, 256)                  # n % 16
+    L.hs_tile_q8.argtypes = [vp, vp, vp, vp, ctypes.c_int, ctypes.c_int]
+    L.hs_tile_q8(None, p, p, p, 32, 300)                      # k % 256
+    L.hs_tile_iq2.argtypes = [vp, vp, vp, vp, ctypes.c_int, ctypes.c_int]
+    L.hs_tile_iq2(None, p, p, p, 48, 256)                     # n % 32
+    L.hs_repack_iq2.argtypes = [vp, vp, vp, vp, ctypes.c_size_t, ctypes.c_int]
+    L.hs_repack_iq2(None, p, p, p, 31, 256)                   # rows % 32
+    L.hs_mma_iq2.argtypes = [vp, vp, vp] + [ctypes.c_int] * 2 + [vp, ctypes.c_int, vp] + [ctypes.c_int] * 3
+    L.hs_mma_iq2(None, p, p, 48, 256, p, 256, p, 48, 4, 1)   # n % 32
+    L.hs_mma_nv4.argtypes = [vp, vp, vp, ctypes.c_float] + [ctypes.c_int] * 2 + [vp, ctypes.c_int, vp] + [ctypes.c_int] * 2
+    L.hs_mma_nv4(None, p, p, 1.0, 20, 256, p, 256, p, 20, 2)  # n % 16
+    err = capfd.readouterr().err
+    for name in ("tile_nv4", "tile_q8", "tile_iq2", "repack_iq2", "mma_iq2", "mma_nv4"):
+        assert f"b200q shim: {name} failed: invalid" in err, (name, err)
