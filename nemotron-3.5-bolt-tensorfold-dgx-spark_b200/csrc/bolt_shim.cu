@@ -16,7 +16,7 @@ cudaError_t launch_nv4_pack_split(const uint8_t* q, const uint8_t* sc, uint8_t* 
 cudaError_t launch_q8_pack_split(const uint8_t* raw, uint8_t* qt, uint8_t* dt, int n, int k, cudaStream_t s);
 int tc_gemv_split(int fmt, const uint8_t* qt, const uint8_t* sct, float s2, int n, int k, const float* x, int ldx, int T,
                   float* y, int ldy, void* ws, size_t ws_bytes, cudaStream_t s);
-size_t tc_split_ws(int n, int k, int T);
+size_t tc_split_ws(int fmt, int n, int k, int T);
 constexpr int kTcNv4 = 0, kTcQ8 = 1;
 constexpr int kTcRows = 16;   // rows a decode GEMV launch takes
 
@@ -117,7 +117,7 @@ static void tc_rows(const char* what, int fmt, const uint8_t* qt, const uint8_t*
                     const float* x, int ldx, float* y, int ldy, int T, cudaStream_t s) {
     if (T <= 0) return;
     size_t have = 0;
-    void* ws = shim_ws(s, tc_split_ws(n, k, T < kTcRows ? T : kTcRows), &have);
+    void* ws = shim_ws(s, tc_split_ws(fmt, n, k, T < kTcRows ? T : kTcRows), &have);
     for (int t0 = 0; t0 < T; t0 += kTcRows) {
         const int rows = T - t0 < kTcRows ? T - t0 : kTcRows;
         const int st = tc_gemv_split(fmt, qt, sct, s2, n, k, x + (size_t)t0 * ldx, ldx, rows, y + (size_t)t0 * ldy, ldy,

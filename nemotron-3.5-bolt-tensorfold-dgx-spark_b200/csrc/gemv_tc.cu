@@ -152,6 +152,12 @@ struct TcArgs {
 
 constexpr int kTcWarps = 8;
 enum { kFmtNv4 = 0, kFmtQ8 = 1 };
+// units a lane keeps in flight, and the CTAs an SM the K split aims at, per format (measured on B200 over 4 / 8 / 16
+// units and 4 / 8 CTAs at config 3's and the GQA projections' shapes, M 1 and 16: NVFP4 is fastest at 4 and 4, Q8_0
+// at 8 and 8)
+template <int FMT> struct TcTune;
+template <> struct TcTune<kFmtNv4> { static constexpr int kPf = 4, kCtasPerSm = 4; };
+template <> struct TcTune<kFmtQ8> { static constexpr int kPf = 8, kCtasPerSm = 8; };
 
 // two e2m1 codes (low nibble -> low half) to f16x2, exact (every e2m1 value is an fp16)
 __device__ __forceinline__ uint32_t e2m1x2_f16x2(uint32_t v) {
@@ -220,7 +226,7 @@ __global__ void __launch_bounds__(kTcWarps * 32) tc_gemv_k(TcArgs a) {
             const size_t u0 = (size_t)tile * steps + s0;
             const uint8_t* base = a.w + u0 * QS;
             const uint8_t* sbase = SPLIT ? a.wsc + u0 * SS : base + 512;
-            constexpr int PF = 4;
+            constexpr int PF = TcTune<FMT>::kPf;
             uint4 qb[PF];
             uint2 sb[PF];
 #pragma unroll
@@ -269,7 +275,7 @@ __global__ void __launch_bounds__(kTcWarps * 32) tc_gemv_k(TcArgs a) {
             const size_t u0 = (size_t)tile * nbk + b0i;
             const uint8_t* base = a.w + u0 * QS;
             const uint8_t* sbase = SPLIT ? a.wsc + u0 * SS : base + 512;
-            constexpr int PF = 4;
+            constexpr int PF = TcTune<FMT>::kPf;
             uint4 qb[PF];
             uint32_t db[PF];
 #pragma unroll
@@ -347,17 +353,18 @@ __global__ void splitk_sum_k(const float* __restrict__ part, int KS, int T, int 
     pdl_trigger();
 }
 
-// K slice: about four CTAs an SM over the row tiles, slices a multiple of 256
-static int slice_len(int n, int k) {
+// K slice: about TcTune<FMT>::kCtasPerSm CTAs an SM over the row tiles, slices a multiple of 256
+static int slice_len(int fmt, int n, int k) {
     const int ctas_x = (n / 16 + kTcWarps - 1) / kTcWarps;
-    const int want = (4 * 148 + ctas_x - 1) / ctas_x;
+    const int per_sm = fmt == kFmtNv4 ? TcTune<kFmtNv4>::kCtasPerSm : TcTune<kFmtQ8>::kCtasPerSm;
+    const int want = (per_sm * 148 + ctas_x - 1) / ctas_x;
     int L = (k + want - 1) / want;
     L = ((L + 255) / 256) * 256;
     return L > k ? k : L;
 }
 
-static size_t splitk_ws(int n, int k, int T) {
-    const int L = slice_len(n, k), KS = (k + L - 1) / L;
+static size_t splitk_ws(int fmt, int n, int k, int T) {
+    const int L = slice_len(fmt, n, k), KS = (k + L - 1) / L;
     return KS > 1 ? (size_t)KS * T * n * sizeof(float) : 0;
 }
 
@@ -374,7 +381,7 @@ static cudaError_t launch_tc(const TcArgs& a, dim3 grid, size_t smem, cudaStream
 template <int FMT>
 static int run_tc(const uint8_t* w, float s2, int n, int k, const void* x, int x_dtype, int ldx, int T, float* y, int ldy,
                   void* ws, size_t ws_bytes, cudaStream_t s, const uint8_t* wsc = nullptr) {
-    int L = slice_len(n, k);
+    int L = slice_len(FMT, n, k);
     int KS = (k + L - 1) / L;
     if (KS > 1 && (!ws || ws_bytes < (size_t)KS * T * n * sizeof(float))) { L = k; KS = 1; }   // no workspace: one slice
     TcArgs a{w, n, k, x, x_dtype, ldx, T, L, s2, KS > 1 ? (float*)ws : y, ldy, wsc};
@@ -411,7 +418,7 @@ int tc_gemv_split(int fmt, const uint8_t* qt, const uint8_t* sct, float s2, int 
     return fmt == kFmtNv4 ? run_tc<kFmtNv4>(qt, s2, n, k, x, B200Q_F32, ldx, T, y, ldy, ws, ws_bytes, s, sct)
                           : run_tc<kFmtQ8>(qt, 1.f, n, k, x, B200Q_F32, ldx, T, y, ldy, ws, ws_bytes, s, sct);
 }
-size_t tc_split_ws(int n, int k, int T) { return tc_shape_ok(n, k) && T > 0 ? splitk_ws(n, k, T) : 0; }
+size_t tc_split_ws(int fmt, int n, int k, int T) { return tc_shape_ok(n, k) && T > 0 ? splitk_ws(fmt, n, k, T) : 0; }
 
 }  // namespace b200q
 
@@ -438,8 +445,8 @@ int b200q_q8_pack(const void* raw, void* packed, int64_t n, int k, void* stream)
     return launched();
 }
 
-size_t b200q_nv4_gemv_workspace_bytes(int n, int k, int T) { return tc_shape_ok(n, k) && T > 0 ? splitk_ws(n, k, T) : 0; }
-size_t b200q_q8_gemv_workspace_bytes(int n, int k, int T) { return tc_shape_ok(n, k) && T > 0 ? splitk_ws(n, k, T) : 0; }
+size_t b200q_nv4_gemv_workspace_bytes(int n, int k, int T) { return tc_split_ws(kFmtNv4, n, k, T); }
+size_t b200q_q8_gemv_workspace_bytes(int n, int k, int T) { return tc_split_ws(kFmtQ8, n, k, T); }
 
 int b200q_nv4_gemv(const void* w, float s2, int n, int k, const void* x, int x_dtype, int ldx, int T, float* y, int ldy,
                    void* workspace, size_t workspace_bytes, void* stream) {
