@@ -14,7 +14,10 @@
  * The structs repeat libbolt's member order and types so the bytes match.  libbolt's fixed model shapes stay fixed
  * here: the latent width 1024 (moe_up's k, moe_down's n, k_combine's width) and TOPN = 9 routed experts a token.
  * As in libbolt the launchers are asynchronous on the given stream and return nothing; a launch error is printed
- * (prefix "b200q shim") and left for the caller's cudaGetLastError. */
+ * (prefix "b200q shim") and left for the caller's cudaGetLastError.  mma_nv4, mma_q8, mma_q8_multi and mma_iq2
+ * take no scratch argument (libbolt's keep a row scratch a stream, mma_pack_buffer): they keep one buffer a
+ * (device, stream), allocated at the first call outside stream capture, so a captured sequence should be run once
+ * before it is captured. */
 #pragma once
 #include <cuda_runtime.h>
 #include <cstddef>
