@@ -36,7 +36,8 @@ def _stale(target, deps):
 def _compile(src, verbose=False):
     obj = os.path.join(OBJ, os.path.basename(src)[:-3] + ".o")
     headers = [os.path.join(CSRC, h) for h in os.listdir(CSRC) if h.endswith((".cuh", ".h"))]
-    headers.append(os.path.join(ROOT, "include", "b200q.h"))
+    inc = os.path.join(ROOT, "include")
+    headers += [os.path.join(inc, h) for h in os.listdir(inc) if h.endswith(".h")]
     if not _stale(obj, [src, __file__] + headers):
         return obj
     cmd = [NVCC, *ARCH, *FLAGS, "-c", src, "-o", obj]
