@@ -54,7 +54,7 @@ int b200q_last_cuda_error(void);
 const char* b200q_strerror(int status);
 /* Errors the kernels recorded on the current device (a bitmask, 0 if none; bit 0: a streaming GEMV's bounded wait for
  * its copies ran out, so its outputs are incomplete; bit 4: the same in an fp16 tensor-core GEMM; bit 8: in the NVFP4
- * tensor-core GEMM); synchronous.  clear != 0 resets it.  No counterpart in libbolt,
+ * tensor-core GEMM; bit 12: in the Q8_0 decode GEMV); synchronous.  clear != 0 resets it.  No counterpart in libbolt,
  * whose kernels do not wait on barriers. */
 int b200q_device_error(int clear);
 
@@ -84,7 +84,8 @@ int b200q_nv4_pack(const void* q, const void* sc, void* packed, int64_t n, int k
  * and verify row counts.  Q8_0: y = sum (q * d) * x, replacing mma_q8 (bolt_mma.cu:1194) and gemv_q8
  * (bolt_kernels.cu:228-231).  K is split across CTAs; the fp32 partials go to `workspace`
  * (>= b200q_*_gemv_workspace_bytes, 0 when no split is needed) and are summed in a fixed order.  A NULL or small
- * workspace runs without the split (slower, same result order).
+ * workspace runs without the split (slower, same result order).  w must be 16-byte aligned (the packers' output in
+ * any device allocation is).
  * --------------------------------------------------------------------------------------------------------- */
 size_t b200q_nv4_gemv_workspace_bytes(int n, int k, int T);
 int b200q_nv4_gemv(const void* w, float s2, int n, int k, const void* x, int x_dtype, int ldx, int T, float* y, int ldy,

@@ -153,11 +153,11 @@ struct TcArgs {
 constexpr int kTcWarps = 8;
 enum { kFmtNv4 = 0, kFmtQ8 = 1 };
 // units a lane keeps in flight, and the CTAs an SM the K split aims at, per format (measured on B200 over 4 / 8 / 16
-// units and 4 / 8 CTAs at config 3's and the GQA projections' shapes, M 1 and 16: NVFP4 is fastest at 4 and 4, Q8_0
-// at 8 and 8)
+// units and 4 / 8 CTAs at config 3's and the GQA projections' shapes, M 1 and 16: tc_gemv_k is fastest for NVFP4 at
+// 4 and 4; Q8_0 runs the ring form at 3 CTAs an SM, all its shared memory admits)
 template <int FMT> struct TcTune;
 template <> struct TcTune<kFmtNv4> { static constexpr int kPf = 4, kCtasPerSm = 4; };
-template <> struct TcTune<kFmtQ8> { static constexpr int kPf = 8, kCtasPerSm = 8; };
+template <> struct TcTune<kFmtQ8> { static constexpr int kPf = 8, kCtasPerSm = 3; };   // the ring form (below)
 
 // two e2m1 codes (low nibble -> low half) to f16x2, exact (every e2m1 value is an fp16)
 __device__ __forceinline__ uint32_t e2m1x2_f16x2(uint32_t v) {
@@ -341,6 +341,228 @@ __global__ void __launch_bounds__(kTcWarps * 32) tc_gemv_k(TcArgs a) {
     pdl_trigger();
 }
 
+// ---------------------------------------------------------------------------------------------------------
+// The ring form, used for Q8_0: each warp's units reach shared memory by bulk copies into a ring of kRingStages
+// stages of kRingUnits units (one mbarrier a stage, lane 0 refilling a stage once the warp has read it), so a warp
+// keeps its slice's units in flight without holding them in registers.  The arithmetic is tc_gemv_k's, unit by unit.
+// Measured on B200 against tc_gemv_k (CUDA graphs of 60 calls): Q8_0 q/k/v 6144 x 4096 at 2287 / 1638 GB/s (M 1 / 16)
+// against 2118 / 1532; NVFP4 slower (in_proj M=1 2017 against 2071, M=16 1152 against 1450), so NVFP4 keeps
+// tc_gemv_k.  Every wait is bounded: on a timeout the kernel records bit 0 of g_gemv_error (b200q_device_error bit
+// 12), lets its copies in flight land and returns.
+// ---------------------------------------------------------------------------------------------------------
+constexpr int kRingStages = 3, kRingUnits = 4;
+constexpr unsigned long long kRingWaitNs = 2000000000ull;   // a stage not filled within 2 s: give up
+__device__ int g_gemv_error;                                // bit 0: a ring wait timed out
+
+__device__ __forceinline__ void ring_init(uint32_t bar) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void ring_expect(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool ring_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ unsigned long long ring_clock() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ bool ring_wait(uint32_t bar, uint32_t parity) {
+    if (ring_try(bar, parity)) return true;
+    const unsigned long long t0 = ring_clock();
+    while (!ring_try(bar, parity))
+        if (ring_clock() - t0 > kRingWaitNs) return false;
+    return true;
+}
+__device__ __forceinline__ void ring_copy(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+__device__ __forceinline__ uint4 ring_lds128(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint2 ring_lds64(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint32_t ring_lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
+template <int FMT>
+struct RingGeom {
+    static constexpr int kKu = FMT == kFmtNv4 ? 64 : 32;                 // k a unit
+    static constexpr int kUb = FMT == kFmtNv4 ? kNv4Unit : kQ8Unit;      // bytes a unit, joined
+    static constexpr int kSsz = kUb - 512;                                // its scale bytes
+    static constexpr int kStage = kRingUnits * kUb;                       // bytes a stage
+};
+// dynamic shared memory of a ring launch: barriers, the staged rows, the warps' rings
+template <int FMT>
+__host__ __device__ inline size_t ring_x_offset() { return 256; }
+template <int FMT>
+__host__ __device__ inline size_t ring_offset(int rows, int L) {
+    return (ring_x_offset<FMT>() + (size_t)rows * (L + 8) * 2 + 127) / 128 * 128;
+}
+template <int FMT>
+__host__ __device__ inline size_t ring_smem(int rows, int L) {
+    return ring_offset<FMT>(rows, L) + (size_t)kTcWarps * kRingStages * RingGeom<FMT>::kStage;
+}
+
+template <int FMT, int NT, bool SPLIT>
+__global__ void __launch_bounds__(kTcWarps * 32) tc_ring_k(TcArgs a) {
+    static_assert(FMT == kFmtQ8, "the ring form is the Q8_0 decode GEMV");
+    using G = RingGeom<FMT>;
+    extern __shared__ __align__(16) unsigned char dyn[];
+    const int L = a.L, stride = L + 8;
+    const int ks = blockIdx.y, k0 = ks * L, len = min(L, a.k - k0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int tile = blockIdx.x * kTcWarps + warp;
+    const bool live = tile * 16 < a.n;
+    const uint32_t sb0 = (uint32_t)__cvta_generic_to_shared(dyn);
+    const uint32_t bar0 = sb0 + 8u * (uint32_t)(warp * kRingStages);
+    const uint32_t ring = sb0 + (uint32_t)ring_offset<FMT>(NT * 8, L) + (uint32_t)(warp * kRingStages * G::kStage);
+    __half* xs = reinterpret_cast<__half*>(dyn + ring_x_offset<FMT>());
+    // the warp's units: nun consecutive units from u0, in stages of kRingUnits
+    const int nun = live ? len / G::kKu : 0;
+    const int nst = (nun + kRingUnits - 1) / kRingUnits;
+    const size_t u0 = (size_t)tile * (a.k / G::kKu) + k0 / G::kKu;
+    // smem of unit i of a stage: codes at st + i * CQ, scales at st + SOFF + i * CS
+    constexpr int CQ = SPLIT ? 512 : G::kUb, SOFF = SPLIT ? kRingUnits * 512 : 512, CS = SPLIT ? G::kSsz : G::kUb;
+    auto issue = [&](int q) {   // stage q of the slice into its ring slot (lane 0)
+        const int u = q * kRingUnits, n = min(kRingUnits, nun - u);
+        const uint32_t st = ring + (uint32_t)((q % kRingStages) * G::kStage), bar = bar0 + 8u * (uint32_t)(q % kRingStages);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        ring_expect(bar, (uint32_t)(n * G::kUb));
+        if constexpr (SPLIT) {
+            ring_copy(st, a.w + (u0 + u) * 512, (uint32_t)(n * 512), bar);
+            ring_copy(st + SOFF, a.wsc + (u0 + u) * G::kSsz, (uint32_t)(n * G::kSsz), bar);
+        } else {
+            ring_copy(st, a.w + (u0 + u) * G::kUb, (uint32_t)(n * G::kUb), bar);
+        }
+    };
+    if (lane == 0 && nst > 0) {
+        for (int i = 0; i < kRingStages; i++) ring_init(bar0 + 8u * (uint32_t)i);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    pdl_wait();
+    if (lane == 0)
+        for (int q = 0; q < kRingStages && q < nst; q++) issue(q);
+    for (int i = threadIdx.x; i < NT * 8 * (len / 2); i += blockDim.x) {
+        const int r = i / (len / 2), c = 2 * (i - r * (len / 2));
+        float v0 = 0.f, v1 = 0.f;
+        if (r < a.T) {
+            const size_t off = (size_t)r * a.ldx + k0 + c;
+            if (a.x_dtype == B200Q_BF16) {
+                const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(reinterpret_cast<const __nv_bfloat16*>(a.x) + off);
+                v0 = __low2float(b); v1 = __high2float(b);
+            } else {
+                const float2 f = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(a.x) + off);
+                v0 = f.x; v1 = f.y;
+            }
+        }
+        *reinterpret_cast<__half2*>(xs + (size_t)r * stride + c) = __floats2half2_rn(v0, v1);
+    }
+    __syncthreads();
+    if (nst > 0) {
+        float acc[NT][4];
+#pragma unroll
+        for (int i = 0; i < NT; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+        const __half* xb = xs + (size_t)g * stride + 2 * t;
+        auto bfrag = [&](int nt, int kk, uint32_t& b0, uint32_t& b1) {
+            const __half* p = xb + (size_t)nt * 8 * stride + kk;
+            b0 = *reinterpret_cast<const uint32_t*>(p);
+            b1 = *reinterpret_cast<const uint32_t*>(p + 8);
+        };
+        bool healthy = true;
+        int q = 0;
+        for (; q < nst; q++) {
+            const uint32_t st = ring + (uint32_t)((q % kRingStages) * G::kStage), bar = bar0 + 8u * (uint32_t)(q % kRingStages);
+            const bool ok = ring_wait(bar, (uint32_t)((q / kRingStages) & 1));
+            if (__any_sync(0xffffffffu, !ok)) {
+                healthy = false;
+                break;
+            }
+            const int n = min(kRingUnits, nun - q * kRingUnits);
+#pragma unroll 1
+            for (int i = 0; i < n; i++) {
+                const uint4 qv = ring_lds128(st + (uint32_t)(i * CQ + 16 * lane));
+                const int ku = (q * kRingUnits + i) * G::kKu;   // the unit's first k within the slice
+                const uint32_t dd = ring_lds32(st + (uint32_t)(SOFF + i * CS + 4 * g));
+                const float dg = __half2float(__ushort_as_half((unsigned short)(dd & 0xffff)));
+                const float dg8 = __half2float(__ushort_as_half((unsigned short)(dd >> 16)));
+                float part[NT][4];
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++) part[nt][0] = part[nt][1] = part[nt][2] = part[nt][3] = 0.f;
+#pragma unroll
+                for (int u = 0; u < 2; u++) {
+                    uint32_t af[4];
+                    q8_frag(u ? qv.z : qv.x, u ? qv.w : qv.y, af);
+                    const int kk = ku + 16 * u;
+#pragma unroll
+                    for (int nt = 0; nt < NT; nt++) {
+                        uint32_t b0, b1;
+                        bfrag(nt, kk, b0, b1);
+                        mma16816(part[nt], af[0], af[1], af[2], af[3], b0, b1);
+                    }
+                }
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++) {
+                    acc[nt][0] = fmaf(dg, part[nt][0], acc[nt][0]);
+                    acc[nt][1] = fmaf(dg, part[nt][1], acc[nt][1]);
+                    acc[nt][2] = fmaf(dg8, part[nt][2], acc[nt][2]);
+                    acc[nt][3] = fmaf(dg8, part[nt][3], acc[nt][3]);
+                }
+            }
+            __syncwarp();   // every lane is done with the stage: lane 0 refills it
+            if (lane == 0 && q + kRingStages < nst) issue(q + kRingStages);
+        }
+        if (!healthy) {
+            // a stage never filled: flag it, and let this warp's copies in flight land before the CTA's memory goes
+            if (lane == 0) {
+                atomicOr(&g_gemv_error, 1);
+                for (int i = q; i < nst && i < q + kRingStages; i++)
+                    ring_wait(bar0 + 8u * (uint32_t)(i % kRingStages), (uint32_t)((i / kRingStages) & 1));
+            }
+            __syncwarp();
+        } else {
+            const bool partial = gridDim.y > 1;
+            const float sc = partial ? 1.f : a.s2;
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int tok = nt * 8 + 2 * t + (j & 1);
+                    const int row = tile * 16 + g + ((j >> 1) ? 8 : 0);
+                    if (tok < a.T && row < a.n) {
+                        float* o = partial ? a.out + ((size_t)ks * a.T + tok) * a.n + row : a.out + (size_t)tok * a.ldo + row;
+                        *o = acc[nt][j] * sc;
+                    }
+                }
+        }
+    }
+    pdl_trigger();
+}
+
+int gemv_error_read(int clear) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_gemv_error, sizeof(int)) != cudaSuccess) return -1;
+    if (clear) {
+        const int z = 0;
+        cudaMemcpyToSymbol(g_gemv_error, &z, sizeof(int));
+    }
+    return v;
+}
+
 __global__ void splitk_sum_k(const float* __restrict__ part, int KS, int T, int n, float s2, float* __restrict__ y, int ldy) {
     pdl_wait();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -368,14 +590,26 @@ static size_t splitk_ws(int fmt, int n, int k, int T) {
     return KS > 1 ? (size_t)KS * T * n * sizeof(float) : 0;
 }
 
+// dynamic shared memory of a launch over `rows` staged rows (8 or 16) and slices of L
+template <int FMT>
+static size_t tc_smem(int rows, int L) {
+    return FMT == kFmtQ8 ? ring_smem<FMT>(rows, L) : (size_t)rows * (L + 8) * 2;
+}
+constexpr size_t kMaxSmem = 232448;   // 227 KB, the opt-in limit a CTA
+
 template <int FMT, int NT, bool SPLIT>
-static cudaError_t launch_tc(const TcArgs& a, dim3 grid, size_t smem, cudaStream_t s) {
+static cudaError_t launch_tc(const TcArgs& a, dim3 grid, cudaStream_t s) {
     static size_t opted = 0;
+    const size_t smem = tc_smem<FMT>(NT * 8, a.L);
+    void (*kern)(TcArgs);
+    if constexpr (FMT == kFmtQ8) kern = tc_ring_k<FMT, NT, SPLIT>;
+    else kern = tc_gemv_k<FMT, NT, SPLIT>;
     if (smem > 48 * 1024 && smem > opted) {
-        cudaFuncSetAttribute(tc_gemv_k<FMT, NT, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
         opted = smem;
     }
-    return launch(tc_gemv_k<FMT, NT, SPLIT>, grid, dim3(kTcWarps * 32), smem, s, a);
+    return launch(kern, grid, dim3(kTcWarps * 32), smem, s, a);
 }
 
 template <int FMT>
@@ -384,12 +618,20 @@ static int run_tc(const uint8_t* w, float s2, int n, int k, const void* x, int x
     int L = slice_len(FMT, n, k);
     int KS = (k + L - 1) / L;
     if (KS > 1 && (!ws || ws_bytes < (size_t)KS * T * n * sizeof(float))) { L = k; KS = 1; }   // no workspace: one slice
+    if (((uintptr_t)w | (uintptr_t)wsc) & 15) return B200Q_EINVAL;   // the ring's bulk copies start on 16-byte boundaries
+    if (T > 8 && tc_smem<FMT>(16, L) > kMaxSmem) {
+        // one slice's 16 staged rows do not fit (a long K without a workspace): two passes of at most 8 rows
+        const size_t xe = x_dtype == B200Q_BF16 ? 2 : 4;
+        const int st = run_tc<FMT>(w, s2, n, k, x, x_dtype, ldx, 8, y, ldy, ws, ws_bytes, s, wsc);
+        if (st != B200Q_OK) return st;
+        return run_tc<FMT>(w, s2, n, k, (const char*)x + 8 * (size_t)ldx * xe, x_dtype, ldx, T - 8, y + 8 * (size_t)ldy, ldy,
+                           ws, ws_bytes, s, wsc);
+    }
     TcArgs a{w, n, k, x, x_dtype, ldx, T, L, s2, KS > 1 ? (float*)ws : y, ldy, wsc};
-    const size_t smem = (size_t)(T > 8 ? 16 : 8) * (L + 8) * 2;
     const dim3 grid((n / 16 + kTcWarps - 1) / kTcWarps, KS);
     cudaError_t e;
-    if (wsc) e = T > 8 ? launch_tc<FMT, 2, true>(a, grid, smem, s) : launch_tc<FMT, 1, true>(a, grid, smem, s);
-    else e = T > 8 ? launch_tc<FMT, 2, false>(a, grid, smem, s) : launch_tc<FMT, 1, false>(a, grid, smem, s);
+    if (wsc) e = T > 8 ? launch_tc<FMT, 2, true>(a, grid, s) : launch_tc<FMT, 1, true>(a, grid, s);
+    else e = T > 8 ? launch_tc<FMT, 2, false>(a, grid, s) : launch_tc<FMT, 1, false>(a, grid, s);
     if (e != cudaSuccess) return status_from(e);
     if (KS > 1) {
         const int64_t tot = (int64_t)T * n;

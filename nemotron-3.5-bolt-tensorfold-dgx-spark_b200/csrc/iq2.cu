@@ -709,6 +709,7 @@ static bool a16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
 int tc_error_read(int clear);   // tc_gemm.cu
 int nv4_error_read(int clear);  // nv4_gemm.cu
+int gemv_error_read(int clear); // gemv_tc.cu
 
 }  // namespace b200q
 
@@ -745,9 +746,9 @@ int b200q_device_error(int clear) {
         const int z = 0;
         cudaMemcpyToSymbol(g_iq2_error, &z, sizeof(int));
     }
-    const int t = b200q::tc_error_read(clear), f = b200q::nv4_error_read(clear);
-    if (t < 0 || f < 0) return -1;
-    return v | (t << 4) | (f << 8);
+    const int t = b200q::tc_error_read(clear), f = b200q::nv4_error_read(clear), d = b200q::gemv_error_read(clear);
+    if (t < 0 || f < 0 || d < 0) return -1;
+    return v | (t << 4) | (f << 8) | (d << 12);
 }
 
 int b200q_iq2_gemv(const void* w, int n, int k, const int8_t* xq, const float* xs, int T, float* y, int ldy, int epi,
