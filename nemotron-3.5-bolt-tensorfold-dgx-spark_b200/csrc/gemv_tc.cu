@@ -154,10 +154,10 @@ constexpr int kTcWarps = 8;
 enum { kFmtNv4 = 0, kFmtQ8 = 1 };
 // units a lane keeps in flight, and the CTAs an SM the K split aims at, per format (measured on B200 over 4 / 8 / 16
 // units and 4 / 8 CTAs at config 3's and the GQA projections' shapes, M 1 and 16: tc_gemv_k is fastest for NVFP4 at
-// 4 and 4; Q8_0 runs the ring form at 3 CTAs an SM, all its shared memory admits)
+// 4 and 4; Q8_0 runs the ring form, two stages at 4 CTAs an SM)
 template <int FMT> struct TcTune;
 template <> struct TcTune<kFmtNv4> { static constexpr int kPf = 4, kCtasPerSm = 4; };
-template <> struct TcTune<kFmtQ8> { static constexpr int kPf = 8, kCtasPerSm = 3; };   // the ring form (below)
+template <> struct TcTune<kFmtQ8> { static constexpr int kPf = 8, kCtasPerSm = 4; };   // the ring form (below)
 
 // two e2m1 codes (low nibble -> low half) to f16x2, exact (every e2m1 value is an fp16)
 __device__ __forceinline__ uint32_t e2m1x2_f16x2(uint32_t v) {
@@ -346,11 +346,12 @@ __global__ void __launch_bounds__(kTcWarps * 32) tc_gemv_k(TcArgs a) {
 // stages of kRingUnits units (one mbarrier a stage, lane 0 refilling a stage once the warp has read it), so a warp
 // keeps its slice's units in flight without holding them in registers.  The arithmetic is tc_gemv_k's, unit by unit.
 // Measured on B200 against tc_gemv_k (CUDA graphs of 60 calls): Q8_0 q/k/v 6144 x 4096 at 2287 / 1638 GB/s (M 1 / 16)
-// against 2118 / 1532; NVFP4 slower (in_proj M=1 2017 against 2071, M=16 1152 against 1450), so NVFP4 keeps
+// with three stages at 3 CTAs an SM against 2118 / 1532, and 2378 / 1690 with two stages at 4; NVFP4 mixed (two
+// stages: in_proj M=1 2199 against 2072, M=16 1190 against 1452, out_proj M=1 1424 against 1513), so NVFP4 keeps
 // tc_gemv_k.  Every wait is bounded: on a timeout the kernel records bit 0 of g_gemv_error (b200q_device_error bit
 // 12), lets its copies in flight land and returns.
 // ---------------------------------------------------------------------------------------------------------
-constexpr int kRingStages = 3, kRingUnits = 4;
+constexpr int kRingStages = 2, kRingUnits = 4;
 constexpr unsigned long long kRingWaitNs = 2000000000ull;   // a stage not filled within 2 s: give up
 __device__ int g_gemv_error;                                // bit 0: a ring wait timed out
 
