@@ -1,5 +1,5 @@
 """Expert-parallel MoE host logic on CPU: placement, and the dispatch / expert / return / combine exchange as
-world_size-2 gloo ranks against a single-process computation of the same layer.
+world_size-2, 4 and 8 gloo ranks against a single-process computation of the same layer.
 
 The experts here are small dense fp32 matrices applied one row at a time (the same operations in both computations),
 so with fp32 transfers the expert-parallel result must equal the single-process one exactly; with bf16 transfers
@@ -106,6 +106,15 @@ def _run(layout, dtype_name, replicate=0, world=2):
 @pytest.mark.parametrize("layout", ["capacity", "exact"])
 def test_ep_matches_single_process_fp32(layout):
     got = _run(layout, "float32")
+    for r, out in got.items():
+        assert np.array_equal(out, _reference(r).numpy())
+
+
+@pytest.mark.parametrize("layout,world", [("capacity", 4), ("exact", 4), ("capacity", 8)])
+def test_ep_matches_single_process_more_ranks(layout, world):
+    """the scaling run's rank counts: 8 experts over 4 ranks (2 each) and 8 ranks (1 each), fp32 transfers"""
+    got = _run(layout, "float32", world=world)
+    assert sorted(got) == list(range(world))
     for r, out in got.items():
         assert np.array_equal(out, _reference(r).numpy())
 
