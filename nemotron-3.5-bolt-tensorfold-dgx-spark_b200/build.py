@@ -2,7 +2,7 @@
 and linked into one shared library beside this file.
 
 The ggml IQ2_XXS tables are compiled in from the reference's own table file, found by path (B200Q_IQ2_TABLES, default
-/root/reference/engine/iq2_tables.inc); they are not copied into the sources.  Where that file is absent (a GPU box),
+the reference checkout's engine/iq2_tables.inc); they are not copied into the sources.  Where that file is absent (a GPU box),
 the prebuilt library is used as is.
 """
 import concurrent.futures

@@ -2,7 +2,7 @@
 
 The oracle is the checker of the B200 kernels; only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg
 load it.  The ggml IQ2_XXS tables are compiled in from the reference's table file by path (B200Q_IQ2_TABLES, default
-/root/reference/engine/iq2_tables.inc).  Where that file is absent (a GPU box) the prebuilt library is used.
+the reference checkout's engine/iq2_tables.inc).  Where that file is absent (a GPU box) the prebuilt library is used.
 
 With --ref it also builds oracle/_ref/libbolt_ref.so: the reference's own kernels (engine/bolt_kernels.cu, compiled
 from where it lies) for sm_100a, with oracle/ref_shim.cu giving them extern "C" entry points.  That library lets the
