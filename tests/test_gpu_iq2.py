@@ -9,7 +9,7 @@ import torch
 
 import b200q
 import oracle as O
-from helpers import assert_tolerance, iq2_blocks, normal_bf16
+from helpers import assert_tolerance, bf16_bits, iq2_blocks, normal_bf16
 
 pytestmark = pytest.mark.gpu
 
@@ -104,6 +104,26 @@ def test_route(mode, T, E, topk):
     else:
         oi, ow = O.route_sigmoid(lg, bias, topk, 2.5)
     assert np.array_equal(ridx.cpu().numpy(), oi)
+    assert np.allclose(rw.cpu().numpy(), ow, rtol=2e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("mode", [b200q.ROUTE_SOFTMAX, b200q.ROUTE_SIGMOID])
+def test_route_ties_go_to_the_lower_index(mode):
+    """logits from {0, 1, 2, 3}: most picks are ties, which route_k's warp argmax breaks towards the lower expert
+    index (bolt_kernels.cu:1676-1692); the oracle does the same"""
+    T, E, topk = 16, 128, 6
+    lg = np.random.default_rng(77).integers(0, 4, (T, E)).astype(np.float32)
+    bits = bf16_bits(lg)
+    ridx, rw = b200q.k_route(dev(bits).view(torch.bfloat16), topk, mode, None, 1.0)
+    if mode == b200q.ROUTE_SOFTMAX:
+        oi, ow = O.route_softmax(lg, topk)
+    else:
+        oi, ow = O.route_sigmoid(lg, None, topk, 1.0)
+    assert np.array_equal(ridx.cpu().numpy(), oi)
+    # every token's picks: its highest value's experts in index order
+    for t in range(T):
+        order = sorted(range(E), key=lambda i: (-lg[t, i], i))[:topk]
+        assert oi[t].tolist() == order
     assert np.allclose(rw.cpu().numpy(), ow, rtol=2e-6, atol=1e-7)
 
 
