@@ -2,8 +2,8 @@
  * names, signatures and view structs and backed by libb200q (csrc/bolt_shim.cu), so that libbolt's host code
  * (bolt_host.cu's enqueue_block and load_slab) links against this engine for the routed-expert MoE block:
  *   load time   repack_iq2 (into the same qs / d buffers load_slab allocates, in this engine's split rt32 layout);
- *   per block   k_route, k_moe_group, k_quant_rows, moe_up, moe_down, k_combine; moe_coop_dense for the shared
- *               expert.
+ *   per block   k_route, k_moe_group, k_quant_rows, moe_up, moe_down, k_combine; moe_coop_dense / moe_tile_dense
+ *               for the shared expert; moe_bf16 (false) and the reporting stubs moe_up_bf / moe_down_bf.
  * and for the Mamba and attention projections (load_nv4 / load_q8, bolt_host.cu:198-264, and their decode calls):
  *   load time   tile_bytes_nv4, tile_scale_bytes_nv4, tile_bytes_q8, tile_scale_bytes_q8, tile_nv4, tile_q8 (the same
  *               buffer sizes as libbolt's tiles, holding this engine's t16 units split into a code plane and a scale
@@ -41,6 +41,15 @@ void moe_down(cudaStream_t s, const IQ2Slab& down, const MoeWork& w, const int8_
               int width, int pairs);
 void moe_coop_dense(cudaStream_t s, const IQ2Slab& w, const MoeWork& mw, int T, const int8_t* xq, const float* xs, float* y,
                     int ldy, int n, int k, int epi);
+/* the same for prompt row counts (enqueue_block's choice at T >= 256) */
+void moe_tile_dense(cudaStream_t s, const IQ2Slab& w, const MoeWork& mw, int T, const int8_t* xq, const float* xs, float* y,
+                    int ldy, int n, int k, int epi);
+/* libbolt's opt-in bf16 routed path (BOLT_MOE_BF=1) is not provided: moe_bf16() is false, and moe_up_bf /
+ * moe_down_bf only report (they exist so that libbolt's host links) */
+bool moe_bf16();
+void moe_up_bf(cudaStream_t s, const IQ2Slab& up, const MoeWork& w, const float* x, int ldx, float* act, int width, int pairs);
+void moe_down_bf(cudaStream_t s, const IQ2Slab& down, const MoeWork& w, const float* act, int ldx, float* out, int width,
+                 int pairs);
 void k_combine(cudaStream_t s, const float* o, const float* rw, float* out, int T);
 
 /* an NVFP4 matrix (n rows, k): q = the 512 code bytes of each 16-row x 64-k unit, sc = its 64 e4m3 scale bytes,

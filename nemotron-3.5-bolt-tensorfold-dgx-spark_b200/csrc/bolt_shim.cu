@@ -210,6 +210,24 @@ void moe_coop_dense(cudaStream_t s, const IQ2Slab& w, const MoeWork& mw, int T, 
     report("moe_coop_dense", launch_iq2_gemv(a, 1, T, epi ? 1 : 0, s));
 }
 
+// moe_tile_dense (bolt_kernels.cu:888-893): libbolt's shared expert at prompt row counts (enqueue_block picks it for
+// T >= 256, bolt_host.cu:674), on the int8 rows like moe_coop_dense; here the same dense expert GEMV, which takes any T
+void moe_tile_dense(cudaStream_t s, const IQ2Slab& w, const MoeWork& mw, int T, const int8_t* xq, const float* xs, float* y,
+                    int ldy, int n, int k, int epi) {
+    moe_coop_dense(s, w, mw, T, xq, xs, y, ldy, n, k, epi);
+}
+
+// moe_bf16 (bolt_kernels.cu:1040): whether enqueue_block takes libbolt's opt-in bf16 routed path (BOLT_MOE_BF=1,
+// bolt_host.cu:702) instead of its default int8 one.  That path is not provided here, so the answer is always no, and
+// moe_up_bf / moe_down_bf exist so that libbolt's host links; called anyway, they report and do nothing.
+bool moe_bf16() { return false; }
+void moe_up_bf(cudaStream_t, const IQ2Slab&, const MoeWork&, const float*, int, float*, int, int) {
+    fprintf(stderr, "b200q shim: moe_up_bf failed: the bf16 routed path is not provided (moe_bf16() is false)\n");
+}
+void moe_down_bf(cudaStream_t, const IQ2Slab&, const MoeWork&, const float*, int, float*, int, int) {
+    fprintf(stderr, "b200q shim: moe_down_bf failed: the bf16 routed path is not provided (moe_bf16() is false)\n");
+}
+
 // combine_k (bolt_kernels.cu:1714-1727): out[t][0 .. 1024) = sum over the 9 picks of rw * o[t * 9 + k]
 void k_combine(cudaStream_t s, const float* o, const float* rw, float* out, int T) {
     report("k_combine", b200q_combine(o, rw, nullptr, T, kBoltTopN, kBoltLatent, out, B200Q_F32, s));

@@ -43,6 +43,22 @@ void hs_moe_coop_dense(void* s, const void* qs, const void* d, int T, const int8
     moe_coop_dense((cudaStream_t)s, w, mw, T, xq, xs, y, ldy, n, k, epi);
 }
 
+void hs_moe_tile_dense(void* s, const void* qs, const void* d, int T, const int8_t* xq, const float* xs, float* y, int ldy,
+                       int n, int k, int epi) {
+    const IQ2Slab w{(const uint8_t*)qs, d, 0, 0};
+    const MoeWork mw{nullptr, nullptr, nullptr, nullptr, nullptr};
+    moe_tile_dense((cudaStream_t)s, w, mw, T, xq, xs, y, ldy, n, k, epi);
+}
+
+int hs_moe_bf16(void) { return moe_bf16() ? 1 : 0; }
+
+void hs_moe_up_bf(void* s) {
+    const IQ2Slab w{nullptr, nullptr, 0, 0};
+    const MoeWork mw{nullptr, nullptr, nullptr, nullptr, nullptr};
+    moe_up_bf((cudaStream_t)s, w, mw, nullptr, 0, nullptr, 0, 0);
+    moe_down_bf((cudaStream_t)s, w, mw, nullptr, 0, nullptr, 0, 0);
+}
+
 void hs_k_combine(void* s, const float* o, const float* rw, float* out, int T) {
     k_combine((cudaStream_t)s, o, rw, out, T);
 }

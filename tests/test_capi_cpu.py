@@ -112,3 +112,10 @@ def test_libbolt_shims_reject_bad_shapes_before_any_launch(capfd):
     err = capfd.readouterr().err
     for name in ("tile_nv4", "tile_q8", "tile_iq2", "repack_iq2", "mma_iq2", "mma_nv4"):
         assert f"b200q shim: {name} failed: invalid" in err, (name, err)
+    # libbolt's opt-in bf16 routed path is not provided: moe_bf16() says so, and its launchers only report
+    L.hs_moe_bf16.restype = ctypes.c_int
+    assert L.hs_moe_bf16() == 0
+    L.hs_moe_up_bf.argtypes = [vp]
+    L.hs_moe_up_bf(None)
+    err = capfd.readouterr().err
+    assert "b200q shim: moe_up_bf failed" in err and "b200q shim: moe_down_bf failed" in err

@@ -31,6 +31,7 @@ def _harness():
         "hs_moe_down": [vp, vp, vp, sz, sz, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32],
         "hs_moe_coop_dense": [vp, vp, vp, i32, vp, vp, vp, i32, i32, i32, i32],
         "hs_k_combine": [vp, vp, vp, vp, i32],
+        "hs_moe_tile_dense": [vp, vp, vp, i32, vp, vp, vp, i32, i32, i32, i32],
         "hs_tile_nv4": [vp, vp, vp, vp, vp, i32, i32],
         "hs_tile_q8": [vp, vp, vp, vp, i32, i32],
         "hs_mma_nv4": [vp, vp, vp, f32, i32, i32, vp, i32, vp, i32, i32],
@@ -128,6 +129,9 @@ def test_shim_coop_dense_and_combine_match_libbolt():
     y = torch.full((T, n), -1.0, device=DEV)
     L.hs_moe_coop_dense(s(), p(qs), p(dd), T, p(d(i["xq"])), p(d(i["xs"])), p(y), n, n, k, 1)
     assert np.array_equal(y.cpu().numpy(), o["y"])
+    y2 = torch.full((T, n), -1.0, device=DEV)   # moe_tile_dense, enqueue_block's choice at prompt row counts
+    L.hs_moe_tile_dense(s(), p(qs), p(dd), T, p(d(i["xq"])), p(d(i["xs"])), p(y2), n, n, k, 1)
+    assert np.array_equal(y2.cpu().numpy(), o["y"])
     i, o = golden("combine")
     T = o["out"].shape[0]
     out = torch.empty(T, 1024, device=DEV)
