@@ -91,7 +91,13 @@ def lib():
 
 
 def _p(t):
-    return None if t is None else ctypes.c_void_p(t.data_ptr())
+    """the device address of a CUDA tensor for the C ABI (None -> NULL).  Anything else is refused before any launch:
+    a host tensor's address would reach a kernel."""
+    if t is None:
+        return None
+    if not (isinstance(t, torch.Tensor) and t.is_cuda):
+        raise B200QError(EINVAL, "operands of the C ABI must be CUDA tensors")
+    return ctypes.c_void_p(t.data_ptr())
 
 
 def _s(stream=None):
