@@ -280,6 +280,40 @@ int b200q_moe_decode_noalloc(const void* x, const void* logits, const void* up, 
 /* IQ2_XXS ggml blocks [nblocks][66]: d fp16 ~ U[1e-3, 1e-2], grid indices U{0..255}, sign indices U{0..127},
  * sub-scales U{0..15}; block i depends on (seed, i) only. */
 void b200q_synth_iq2_host(uint64_t seed, int64_t nblocks, void* out);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Checkpoint ingestion (replaces libbolt's Store / open_store / lookup and load_slab / load_nv4 / load_q8,
+ * bolt_host.cu:61-345).  b200q_ckpt_open reads dir/model.safetensors.index.json ({"weight_map": {tensor: shard}})
+ * or, without one, dir/model.safetensors; shards are memory-mapped on first use and their JSON headers checked (every
+ * data offset inside the file, byte counts matching dtype and shape).  NULL when the directory holds neither or the
+ * index does not parse.  A handle is used from one thread at a time or under the caller's lock (lookups lock
+ * internally); b200q_ckpt_close unmaps.
+ * b200q_ckpt_tensor: a tensor's host bytes inside the mapping (valid until close), shape (up to 8 dims), dtype
+ * (safetensors' name, up to 15 characters); EINVAL if absent or malformed.
+ * The packers copy raw checkpoint bytes into `staging` (device, 16-byte aligned, >= b200q_ckpt_staging_bytes: fmt 0
+ * one expert's IQ2_XXS blocks of n rows, 1 NVFP4, 2 Q8_0) and pack from there on `stream` into this library's
+ * layouts, exactly as b200q_iq2_pack / b200q_nv4_pack / b200q_q8_pack of the same bytes:
+ *   _iq2_slab  names[e] = expert e's [rows][k/256][66] blocks -> packed expert e at e * b200q_iq2_bytes(rows, k)
+ *              (load_slab);
+ *   _nv4       prefix.weight [n][k/2], prefix.weight_scale [n][k/16] e4m3, prefix.weight_scale_2 (fp32) -> the t16
+ *              layout, *s2 = the tensor scale (load_nv4);
+ *   _q8        name [n][k/32][34] -> the t16 layout (load_q8).
+ * Every name and byte count is checked before the first copy (EINVAL), the staging size too (ENOSPACE).  The
+ * copies read pageable host memory, so each returns once its bytes are staged.
+ * --------------------------------------------------------------------------------------------------------- */
+typedef struct b200q_ckpt b200q_ckpt;
+b200q_ckpt* b200q_ckpt_open(const char* dir);
+void b200q_ckpt_close(b200q_ckpt* c);
+int64_t b200q_ckpt_count(b200q_ckpt* c);
+int b200q_ckpt_tensor(b200q_ckpt* c, const char* name, const void** data, size_t* bytes, int64_t* shape, int* ndim,
+                      char* dtype);
+size_t b200q_ckpt_staging_bytes(int fmt, int n, int k);
+int b200q_ckpt_pack_iq2_slab(b200q_ckpt* c, const char* const* names, int experts, int rows, int k, void* packed,
+                             void* staging, size_t staging_bytes, void* stream);
+int b200q_ckpt_pack_nv4(b200q_ckpt* c, const char* prefix, int n, int k, void* packed, float* s2, void* staging,
+                        size_t staging_bytes, void* stream);
+int b200q_ckpt_pack_q8(b200q_ckpt* c, const char* name, int n, int k, void* packed, void* staging,
+                       size_t staging_bytes, void* stream);
 int b200q_synth_iq2(uint64_t seed, int64_t nblocks, void* out, void* stream);
 
 #ifdef __cplusplus

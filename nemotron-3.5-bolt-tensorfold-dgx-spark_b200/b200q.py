@@ -82,6 +82,15 @@ def lib():
             "b200q_quant_nv4_rows": (i32, [vp, i32, i32, i32, i32, vp, vp]),
             "b200q_nv4_gemm_workspace_bytes": (sz, [i32, i32, i32]),
             "b200q_nv4_gemm": (i32, [vp, i32, i32, f32, vp, i32, vp, i32, vp, sz, vp]),
+            "b200q_ckpt_open": (vp, [ctypes.c_char_p]),
+            "b200q_ckpt_close": (None, [vp]),
+            "b200q_ckpt_count": (i64, [vp]),
+            "b200q_ckpt_tensor": (i32, [vp, ctypes.c_char_p, ctypes.POINTER(vp), ctypes.POINTER(sz),
+                                        ctypes.POINTER(i64), ctypes.POINTER(i32), ctypes.c_char_p]),
+            "b200q_ckpt_staging_bytes": (sz, [i32, i32, i32]),
+            "b200q_ckpt_pack_iq2_slab": (i32, [vp, ctypes.POINTER(ctypes.c_char_p), i32, i32, i32, vp, vp, sz, vp]),
+            "b200q_ckpt_pack_nv4": (i32, [vp, ctypes.c_char_p, i32, i32, vp, ctypes.POINTER(f32), vp, sz, vp]),
+            "b200q_ckpt_pack_q8": (i32, [vp, ctypes.c_char_p, i32, i32, vp, vp, sz, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -449,6 +458,80 @@ def moe_prompt(up, down, E, H, F, counts, offsets, order, topk, x, mo=None, act=
                                   _dtype_code(x), _p(mo), _dtype_code(mo), _p(act) if act is not None else None, ws, wb,
                                   _s()), "moe_prompt")
     return mo
+
+
+# -------------------------------------------------------------------------------------------------------------
+# checkpoint ingestion (open_store / lookup / load_slab / load_nv4 / load_q8, bolt_host.cu:61-345)
+# -------------------------------------------------------------------------------------------------------------
+class Checkpoint:
+    """A model directory of safetensors shards (model.safetensors.index.json, or one model.safetensors), mapped by the
+    library; tensors are read in place and packed into this library's device layouts through a device staging
+    buffer."""
+
+    def __init__(self, path):
+        self._h = lib().b200q_ckpt_open(os.fsencode(path))
+        if not self._h:
+            raise B200QError(EINVAL, f"no readable safetensors checkpoint at {path}")
+        self._staging = None
+
+    def close(self):
+        if self._h:
+            lib().b200q_ckpt_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __len__(self):
+        return int(lib().b200q_ckpt_count(self._h))
+
+    def tensor(self, name):
+        """(a read-only uint8 numpy view of the tensor's bytes in the mapping, shape, safetensors dtype)"""
+        import numpy as np
+        data, nbytes = ctypes.c_void_p(), ctypes.c_size_t()
+        shape, ndim, dtype = (ctypes.c_int64 * 8)(), ctypes.c_int(), ctypes.create_string_buffer(16)
+        _check(lib().b200q_ckpt_tensor(self._h, name.encode(), ctypes.byref(data), ctypes.byref(nbytes), shape,
+                                       ctypes.byref(ndim), dtype), f"tensor {name}")
+        if nbytes.value:
+            view = np.ctypeslib.as_array(ctypes.cast(data, ctypes.POINTER(ctypes.c_uint8)), shape=(nbytes.value,))
+        else:
+            view = np.zeros(0, np.uint8)
+        view.flags.writeable = False
+        return view, tuple(shape[i] for i in range(ndim.value)), dtype.value.decode()
+
+    def _stage(self, fmt, n, k, device):
+        need = lib().b200q_ckpt_staging_bytes(fmt, n, k)
+        if self._staging is None or self._staging.numel() < need or self._staging.device != torch.device(device):
+            self._staging = torch.empty(need, dtype=torch.uint8, device=device)
+        return self._staging
+
+    def pack_iq2_slab(self, names, rows, k, device="cuda"):
+        """the experts' IQ2_XXS tensors (names[e]: [rows][k/256][66] blocks) -> one packed slab (load_slab)"""
+        st = self._stage(0, rows, k, device)
+        out = torch.empty(len(names) * iq2_bytes(rows, k), dtype=torch.uint8, device=device)
+        arr = (ctypes.c_char_p * len(names))(*[n.encode() for n in names])
+        _check(lib().b200q_ckpt_pack_iq2_slab(self._h, arr, len(names), rows, k, _p(out), _p(st), st.numel(), _s()),
+               "pack_iq2_slab")
+        return out
+
+    def pack_nv4(self, prefix, n, k, device="cuda"):
+        """prefix.weight / .weight_scale / .weight_scale_2 -> (the t16 layout, the tensor scale s2) (load_nv4)"""
+        st = self._stage(1, n, k, device)
+        out = torch.empty(lib().b200q_nv4_bytes(n, k), dtype=torch.uint8, device=device)
+        s2 = ctypes.c_float()
+        _check(lib().b200q_ckpt_pack_nv4(self._h, prefix.encode(), n, k, _p(out), ctypes.byref(s2), _p(st), st.numel(),
+                                         _s()), "pack_nv4")
+        return out, s2.value
+
+    def pack_q8(self, name, n, k, device="cuda"):
+        """a Q8_0 tensor ([n][k/32][34] blocks) -> the t16 layout (load_q8)"""
+        st = self._stage(2, n, k, device)
+        out = torch.empty(lib().b200q_q8_bytes(n, k), dtype=torch.uint8, device=device)
+        _check(lib().b200q_ckpt_pack_q8(self._h, name.encode(), n, k, _p(out), _p(st), st.numel(), _s()), "pack_q8")
+        return out
 
 
 # -------------------------------------------------------------------------------------------------------------

@@ -10,3 +10,6 @@ for p in (os.path.join(ROOT, "tests"), os.path.join(ROOT, "oracle"), PKG):
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (a B200); run with -m gpu")
+    # tmp_path directories (the checkpoint tests' shards) stay inside the repository, under the ignored tests/_build
+    if not config.option.basetemp:
+        config.option.basetemp = os.path.join(ROOT, "tests", "_build", "tmp")

@@ -1,0 +1,155 @@
+"""CPU tests of checkpoint ingestion (b200q_ckpt_*, csrc/ckpt.cu): safetensors shards written here, opened through the
+index or as one file, looked up by name (bytes, shape and dtype exactly as written), and every malformed or missing
+piece refused with EINVAL (a NULL handle for the directory itself) before anything reaches the GPU.  The packers'
+checks (staging size, names, byte counts) run before their first copy, so they are tested here too."""
+import ctypes
+import json
+import os
+import struct
+
+import numpy as np
+import pytest
+
+import b200q
+
+
+def write_safetensors(path, tensors, header_extra=None, raw_header=None):
+    """tensors: {name: (dtype, shape, bytes)} -> a safetensors file (8-byte little-endian header length, the JSON
+    header padded with spaces to 8 bytes, then the data in order)"""
+    header, off, blobs = {}, 0, []
+    for name, (dt, shape, data) in tensors.items():
+        header[name] = {"dtype": dt, "shape": list(shape), "data_offsets": [off, off + len(data)]}
+        off += len(data)
+        blobs.append(data)
+    if header_extra:
+        header.update(header_extra)
+    h = raw_header if raw_header is not None else json.dumps(header).encode()
+    h += b" " * ((8 - len(h) % 8) % 8)
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(h)))
+        f.write(h)
+        for b in blobs:
+            f.write(b)
+
+
+def write_index(d, weight_map):
+    with open(os.path.join(d, "model.safetensors.index.json"), "w") as f:
+        json.dump({"metadata": {"total_size": 0}, "weight_map": weight_map}, f)
+
+
+def synthetic_model(d, seed=0, rows=64, k=512, experts=3, n=64):
+    """a two-shard model: IQ2_XXS experts, an NVFP4 projection and a Q8_0 projection of the given sizes; returns
+    {name: (dtype, shape, bytes)}"""
+    rng = np.random.default_rng(seed)
+    t = {}
+    for e in range(experts):
+        blocks = b200q.synth_iq2_host(seed * 100 + e, rows * (k // 256))
+        t[f"layers.1.mixer.experts.{e}.up_proj.weight"] = ("U8", (rows, k // 256, 66), blocks.tobytes())
+    t["layers.0.mixer.in_proj.weight"] = ("U8", (n, k // 2), rng.integers(0, 256, n * k // 2, dtype=np.uint8).tobytes())
+    sc = rng.integers(0x30, 0x40, n * k // 16, dtype=np.uint8)   # e4m3 codes between 0.5 and 1.9
+    t["layers.0.mixer.in_proj.weight_scale"] = ("F8_E4M3", (n, k // 16), sc.tobytes())
+    t["layers.0.mixer.in_proj.weight_scale_2"] = ("F32", (), np.float32(0.375).tobytes())
+    qv = rng.integers(-127, 128, (n, k // 32, 32), dtype=np.int8)
+    dq = rng.uniform(1e-3, 1e-2, (n, k // 32)).astype(np.float16)
+    q8 = np.concatenate([dq.view(np.uint8).reshape(n, k // 32, 2), qv.view(np.uint8)], -1)
+    t["layers.2.self_attn.q_proj.weight"] = ("U8", (n, k // 32, 34), q8.tobytes())
+    t["layers.3.norm.weight"] = ("F32", (4,), np.arange(4, dtype=np.float32).tobytes())
+    names = list(t)
+    a, b = names[: experts], names[experts:]
+    write_safetensors(os.path.join(d, "model-00001-of-00002.safetensors"), {x: t[x] for x in a},
+                      header_extra={"__metadata__": {"format": "pt"}})
+    write_safetensors(os.path.join(d, "model-00002-of-00002.safetensors"), {x: t[x] for x in b})
+    write_index(d, {**{x: "model-00001-of-00002.safetensors" for x in a},
+                    **{x: "model-00002-of-00002.safetensors" for x in b}})
+    return t
+
+
+def test_open_index_and_read_tensors(tmp_path):
+    t = synthetic_model(str(tmp_path))
+    ck = b200q.Checkpoint(str(tmp_path))
+    assert len(ck) == len(t)
+    for name, (dt, shape, data) in t.items():
+        view, shp, dtype = ck.tensor(name)
+        assert view.tobytes() == data and shp == tuple(shape) and dtype == dt
+    with pytest.raises(b200q.B200QError):
+        ck.tensor("layers.9.missing.weight")
+    ck.close()
+
+
+def test_single_file_without_index(tmp_path):
+    data = np.arange(24, dtype=np.int32).tobytes()
+    write_safetensors(str(tmp_path / "model.safetensors"),
+                      {"a": ("I32", (2, 3, 4), data), "café \"q\"": ("U8", (3,), b"xyz")})
+    ck = b200q.Checkpoint(str(tmp_path))
+    assert len(ck) == 2
+    view, shp, dt = ck.tensor("a")
+    assert view.tobytes() == data and shp == (2, 3, 4) and dt == "I32"
+    assert ck.tensor("café \"q\"")[0].tobytes() == b"xyz"   # escapes and UTF-8 in the JSON header
+
+
+def test_empty_directory_and_bad_index_are_refused(tmp_path):
+    with pytest.raises(b200q.B200QError):
+        b200q.Checkpoint(str(tmp_path))
+    (tmp_path / "model.safetensors.index.json").write_text('{"weight_map": {"a": "s.safetensors",}}')
+    with pytest.raises(b200q.B200QError):
+        b200q.Checkpoint(str(tmp_path))
+    write_index(str(tmp_path), {"a": "../outside.safetensors"})   # a shard outside the directory
+    with pytest.raises(b200q.B200QError):
+        b200q.Checkpoint(str(tmp_path))
+
+
+@pytest.mark.parametrize("case", ["offset past the file", "bytes not dtype x shape", "header longer than the file",
+                                  "header not JSON", "offsets reversed"])
+def test_malformed_shards_are_refused(tmp_path, case):
+    d = str(tmp_path)
+    path = os.path.join(d, "s.safetensors")
+    good = {"a": ("F32", (2,), np.zeros(2, np.float32).tobytes())}
+    if case == "offset past the file":
+        write_safetensors(path, good, raw_header=json.dumps(
+            {"a": {"dtype": "F32", "shape": [4], "data_offsets": [0, 16]}}).encode())
+    elif case == "bytes not dtype x shape":
+        write_safetensors(path, {"a": ("F32", (3,), np.zeros(2, np.float32).tobytes())})
+    elif case == "header longer than the file":
+        write_safetensors(path, good)
+        with open(path, "r+b") as f:
+            f.write(struct.pack("<Q", 1 << 20))
+    elif case == "header not JSON":
+        write_safetensors(path, good, raw_header=b'{"a": {"dtype": "F32", "shape": [2], "data_offsets": [0, 8]')
+    else:
+        write_safetensors(path, good, raw_header=json.dumps(
+            {"a": {"dtype": "F32", "shape": [2], "data_offsets": [8, 0]}}).encode())
+    write_index(d, {"a": "s.safetensors"})
+    ck = b200q.Checkpoint(d)   # the index opens; the shard is read at the first lookup
+    with pytest.raises(b200q.B200QError):
+        ck.tensor("a")
+
+
+def test_packers_check_everything_before_the_first_copy(tmp_path):
+    """staging too small, a missing expert among present ones, a tensor of the wrong size, an NVFP4 prefix without
+    its scale: refused before any copy (fake device pointers, never touched)"""
+    t = synthetic_model(str(tmp_path), rows=64, k=512, experts=3, n=64)
+    L = b200q.lib()
+    h = L.b200q_ckpt_open(os.fsencode(str(tmp_path)))
+    assert h
+    fake, null = ctypes.c_void_p(1 << 20), ctypes.c_void_p()
+    rows, k = 64, 512
+    need = L.b200q_ckpt_staging_bytes(0, rows, k)
+    assert need == rows * (k // 256) * 66
+    names = [n for n in t if ".experts." in n]
+    arr = lambda xs: (ctypes.c_char_p * len(xs))(*[x.encode() for x in xs])
+    assert L.b200q_ckpt_pack_iq2_slab(h, arr(names), 3, rows, k, fake, fake, need - 16, null) == b200q.ENOSPACE
+    assert L.b200q_ckpt_pack_iq2_slab(h, arr(names[:2] + ["no.such.weight"]), 3, rows, k, fake, fake, need,
+                                      null) == b200q.EINVAL
+    assert L.b200q_ckpt_pack_iq2_slab(h, arr(names), 3, rows, 256, fake, fake, need, null) == b200q.EINVAL   # sizes
+    assert L.b200q_ckpt_pack_iq2_slab(h, arr(names), 3, 48, k, fake, fake, need, null) == b200q.EINVAL      # rows % 32
+    s2 = ctypes.c_float()
+    nv = L.b200q_ckpt_staging_bytes(1, 64, 512)
+    assert L.b200q_ckpt_pack_nv4(h, b"layers.0.mixer.in_proj", 64, 512, fake, ctypes.byref(s2), fake, nv - 1,
+                                 null) == b200q.ENOSPACE
+    assert L.b200q_ckpt_pack_nv4(h, b"layers.0.mixer.out_proj", 64, 512, fake, ctypes.byref(s2), fake, nv,
+                                 null) == b200q.EINVAL
+    q8 = L.b200q_ckpt_staging_bytes(2, 64, 512)
+    assert q8 == 64 * 16 * 34
+    assert L.b200q_ckpt_pack_q8(h, b"layers.2.self_attn.q_proj.weight", 64, 256, fake, fake, q8, null) == b200q.EINVAL
+    assert L.b200q_ckpt_pack_q8(h, b"layers.3.norm.weight", 64, 512, fake, fake, q8, null) == b200q.EINVAL
+    L.b200q_ckpt_close(h)
