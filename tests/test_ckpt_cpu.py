@@ -153,3 +153,44 @@ def test_packers_check_everything_before_the_first_copy(tmp_path):
     assert L.b200q_ckpt_pack_q8(h, b"layers.2.self_attn.q_proj.weight", 64, 256, fake, fake, q8, null) == b200q.EINVAL
     assert L.b200q_ckpt_pack_q8(h, b"layers.3.norm.weight", 64, 512, fake, fake, q8, null) == b200q.EINVAL
     L.b200q_ckpt_close(h)
+
+
+def test_mutated_headers_never_escape_the_file(tmp_path):
+    """300 seeded mutations (byte flips, cuts, duplications) of a valid header: every lookup either fails with EINVAL
+    or returns a tensor that lies inside the file with a byte count matching its dtype and shape; nothing crashes"""
+    rng = np.random.default_rng(11)
+    tensors = {"w": ("F32", (3, 5), np.arange(15, dtype=np.float32).tobytes()),
+               "b": ("BF16", (7,), bytes(14)), "s": ("U8", (2, 2, 2), bytes(range(8)))}
+    base = json.dumps({n: {"dtype": dt, "shape": list(sh), "data_offsets": [o, o + len(b)]}
+                       for (n, (dt, sh, b)), o in zip(tensors.items(), [0, 60, 74])}).encode()
+    data = b"".join(b for _, _, b in tensors.values())
+    elt = {"F32": 4, "BF16": 2, "U8": 1}
+    for i in range(300):
+        h = bytearray(base)
+        for _ in range(int(rng.integers(1, 4))):
+            op, at = int(rng.integers(0, 3)), int(rng.integers(0, len(h)))
+            if op == 0:
+                h[at] = int(rng.integers(0, 256))
+            elif op == 1:
+                del h[at:at + int(rng.integers(1, 8))]
+            else:
+                h[at:at] = h[max(0, at - 8):at]
+        d = tmp_path / f"m{i}"
+        d.mkdir()
+        hb = bytes(h) + b" " * ((8 - len(h) % 8) % 8)
+        with open(d / "model.safetensors", "wb") as f:
+            f.write(struct.pack("<Q", len(hb)) + hb + data)
+        try:
+            ck = b200q.Checkpoint(str(d))
+        except b200q.B200QError:
+            continue
+        size = os.path.getsize(d / "model.safetensors")
+        for name in ["w", "b", "s", "x"]:
+            try:
+                view, shape, dt = ck.tensor(name)
+            except b200q.B200QError:
+                continue
+            n = int(np.prod(shape)) if shape else 1
+            assert dt not in elt or view.nbytes == n * elt[dt]
+            assert view.nbytes <= size - 8 - len(hb)
+        ck.close()
