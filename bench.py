@@ -754,6 +754,60 @@ def run_reference(args, rank, world):
             "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def ckpt_bench(b200q, device, reps=3):
+    """Checkpoint ingestion (b200q_ckpt_*): one MoE layer at the model's own shapes (layer 1 of its schedule: 240
+    IQ2_XXS experts, width 2048, latent 1024; up and down in two safetensors shards, 260 MB) written to disk, then
+    packed from the mapped shards into the device slabs.  GB/s = raw checkpoint bytes / wall time of the two packs,
+    best of `reps` with the shards in the page cache (the pageable host-to-device copies run one expert at a time)."""
+    import shutil
+    experts, width, latent = 240, 2048, 1024
+    d = os.path.join(ROOT, "_build", "ckpt_bench")
+    shutil.rmtree(d, ignore_errors=True)
+    os.makedirs(d)
+    try:
+        weight_map = {}
+        for proj, rows, k in (("up_proj", width, latent), ("down_proj", latent, width)):
+            nb = rows * (k // 256)
+            header, blobs, off = {}, [], 0
+            for e in range(experts):
+                name = f"backbone.layers.1.mixer.experts.{e}.{proj}.weight"
+                blob = b200q.synth_iq2_host(7000 + e + (experts if proj == "down_proj" else 0), nb).tobytes()
+                header[name] = {"dtype": "U8", "shape": [rows, k // 256, 66], "data_offsets": [off, off + len(blob)]}
+                off += len(blob)
+                blobs.append(blob)
+                weight_map[name] = f"{proj}.safetensors"
+            h = json.dumps(header).encode()
+            h += b" " * ((8 - len(h) % 8) % 8)
+            with open(os.path.join(d, f"{proj}.safetensors"), "wb") as f:
+                f.write(len(h).to_bytes(8, "little"))
+                f.write(h)
+                for blob in blobs:
+                    f.write(blob)
+        with open(os.path.join(d, "model.safetensors.index.json"), "w") as f:
+            json.dump({"weight_map": weight_map}, f)
+        ck = b200q.Checkpoint(d)
+        up_names = [n for n in weight_map if n.endswith("up_proj.weight")]
+        down_names = [n for n in weight_map if n.endswith("down_proj.weight")]
+        nbytes = 2 * experts * width * (latent // 256) * 66
+        best = None
+        for _ in range(reps + 1):   # the first pass maps the shards and faults their pages in
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            su = ck.pack_iq2_slab(up_names, width, latent, device)
+            sd = ck.pack_iq2_slab(down_names, latent, width, device)
+            torch.cuda.synchronize()
+            dt = time.perf_counter() - t0
+            best = dt if best is None or dt < best else best
+            del su, sd
+        ck.close()
+        return {"ckpt": {"workload": "one MoE layer of the model's schedule: 240 IQ2_XXS experts, width 2048, latent "
+                                     "1024, up and down (safetensors, page-cache resident)",
+                         "bytes": nbytes, "ms": round(best * 1e3, 2), "gbs": round(nbytes / best / 1e9, 2),
+                         "device_error": b200q.device_error()}}
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -763,7 +817,7 @@ def main():
     ap.add_argument("--layers", type=int, default=4, help="layer copies rotated to defeat L2 (1 for small profiles)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="length of the CPU-baseline sample")
     ap.add_argument("--no-prefill", dest="prefill", action="store_false", help="skip the config-4 prefill GEMMs")
-    ap.add_argument("--only", choices=["prefill", "nvfp4", "ep"], default=None,
+    ap.add_argument("--only", choices=["prefill", "nvfp4", "ep", "ckpt"], default=None,
                     help="run one sub-measurement on one GPU and print its object (for profiling)")
     args = ap.parse_args()
     global LAYERS
@@ -781,6 +835,8 @@ def main():
             line = prefill_bench(b200q, type("L", (), {"up": up, "down": down}), device)
         elif args.only == "nvfp4":
             line = nvfp4_bench(b200q, device)
+        elif args.only == "ckpt":
+            line = ckpt_bench(b200q, device)
         else:
             line = ep_bench(b200q, 0, 1, device, min(args.steps, 500), args.warmup)
     elif args.impl == "reference":
