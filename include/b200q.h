@@ -266,8 +266,10 @@ int b200q_ep_combine(const void* back, int back_dtype, int ldb, const int* slot,
  * Arguments and results are those of b200q_moe_decode.  Scratch is a library-resident device array of
  * b200q_moe_decode_noalloc_max_bytes() bytes (3 MiB: enough for T <= 16, H <= 4096, F <= 2048, E <= 128,
  * topk <= 8), held by every GPU that loads the library until exit; larger shapes return B200Q_ENOSPACE.  The first
- * call on a device looks up the array's device address, so make it before any stream capture.  All calls share the
- * array: calls that overlap on the GPU race.  It allocates nothing. */
+ * call on a device looks up the array's device address, so make it before any stream capture.  The address is kept
+ * for the life of the process; after cudaDeviceReset the array may sit elsewhere, so a process that resets a device
+ * must not call this entry point on it again.  All calls share the array: calls that overlap on the GPU race.  It
+ * allocates nothing. */
 size_t b200q_moe_decode_noalloc_max_bytes(void);
 int b200q_moe_decode_noalloc(const void* x, const void* logits, const void* up, const void* down, const void* shared_up,
                              const void* shared_down, int T, int H, int F, int E, int topk, int route, const float* bias,

@@ -463,40 +463,65 @@ def moe_prompt(up, down, E, H, F, counts, offsets, order, topk, x, mo=None, act=
 # -------------------------------------------------------------------------------------------------------------
 # checkpoint ingestion (open_store / lookup / load_slab / load_nv4 / load_q8, bolt_host.cu:61-345)
 # -------------------------------------------------------------------------------------------------------------
-class Checkpoint:
-    """A model directory of safetensors shards (model.safetensors.index.json, or one model.safetensors), mapped by the
-    library; tensors are read in place and packed into this library's device layouts through a device staging
-    buffer."""
+class _Mapping:
+    """The library's handle of an opened checkpoint.  The shards stay mapped while this object lives: the Checkpoint
+    and every tensor view it handed out hold a reference, so a view never outlives the memory it reads."""
 
-    def __init__(self, path):
-        self._h = lib().b200q_ckpt_open(os.fsencode(path))
-        if not self._h:
-            raise B200QError(EINVAL, f"no readable safetensors checkpoint at {path}")
-        self._staging = None
-
-    def close(self):
-        if self._h:
-            lib().b200q_ckpt_close(self._h)
-            self._h = None
+    def __init__(self, h):
+        self.h = h
 
     def __del__(self):
         try:
-            self.close()
+            if self.h:
+                lib().b200q_ckpt_close(self.h)
+                self.h = None
         except Exception:
             pass
+
+
+class Checkpoint:
+    """A model directory of safetensors shards (model.safetensors.index.json, or one model.safetensors), mapped by the
+    library; tensors are read in place and packed into this library's device layouts through a device staging
+    buffer.
+
+    The packs of one Checkpoint share one staging buffer; a pack on a different stream from the previous one first
+    makes its stream wait for the previous stream's work, so the staging bytes are never overwritten while a pack
+    kernel still reads them."""
+
+    def __init__(self, path):
+        h = lib().b200q_ckpt_open(os.fsencode(path))
+        if not h:
+            raise B200QError(EINVAL, f"no readable safetensors checkpoint at {path}")
+        self._map = _Mapping(h)
+        self._staging = None
+        self._staging_stream = None
+
+    @property
+    def _h(self):
+        if self._map is None:
+            raise B200QError(EINVAL, "checkpoint is closed")
+        return self._map.h
+
+    def close(self):
+        """Drop this object's hold on the mapping; views handed out by tensor() keep it mapped until they go."""
+        self._map = None
+        self._staging = None
 
     def __len__(self):
         return int(lib().b200q_ckpt_count(self._h))
 
     def tensor(self, name):
-        """(a read-only uint8 numpy view of the tensor's bytes in the mapping, shape, safetensors dtype)"""
+        """(a read-only uint8 numpy view of the tensor's bytes in the mapping, shape, safetensors dtype).  The view
+        keeps the mapping alive: it stays valid after close() or after this Checkpoint is gone."""
         import numpy as np
         data, nbytes = ctypes.c_void_p(), ctypes.c_size_t()
         shape, ndim, dtype = (ctypes.c_int64 * 8)(), ctypes.c_int(), ctypes.create_string_buffer(16)
         _check(lib().b200q_ckpt_tensor(self._h, name.encode(), ctypes.byref(data), ctypes.byref(nbytes), shape,
                                        ctypes.byref(ndim), dtype), f"tensor {name}")
         if nbytes.value:
-            view = np.ctypeslib.as_array(ctypes.cast(data, ctypes.POINTER(ctypes.c_uint8)), shape=(nbytes.value,))
+            buf = (ctypes.c_uint8 * nbytes.value).from_address(data.value)
+            buf._mapping = self._map   # the numpy array below holds buf, buf holds the mapping
+            view = np.frombuffer(buf, dtype=np.uint8)
         else:
             view = np.zeros(0, np.uint8)
         view.flags.writeable = False
@@ -504,8 +529,15 @@ class Checkpoint:
 
     def _stage(self, fmt, n, k, device):
         need = lib().b200q_ckpt_staging_bytes(fmt, n, k)
+        cur = torch.cuda.current_stream(torch.device(device))
         if self._staging is None or self._staging.numel() < need or self._staging.device != torch.device(device):
+            if self._staging is not None and self._staging_stream is not None:
+                # the old buffer's memory is reused only after the work its last pack enqueued
+                self._staging.record_stream(self._staging_stream)
             self._staging = torch.empty(need, dtype=torch.uint8, device=device)
+        elif self._staging_stream is not None and self._staging_stream != cur:
+            cur.wait_stream(self._staging_stream)   # the previous pack's kernel has read the staging bytes
+        self._staging_stream = cur
         return self._staging
 
     def pack_iq2_slab(self, names, rows, k, device="cuda"):

@@ -17,7 +17,9 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <cstdio>
+#include <initializer_list>
 #include <cstdlib>
 #include <cstring>
 #include <memory>
@@ -363,10 +365,16 @@ struct b200q_ckpt : Ckpt {};
 
 namespace {
 
-// a tensor of exactly `bytes` bytes, or null
-const Tensor* sized(b200q_ckpt* c, const std::string& name, size_t bytes, const uint8_t** data) {
+// a tensor of exactly `bytes` bytes and, when `shape` is given, exactly that shape, or null.  The byte count alone
+// would accept a tensor whose rows and k are swapped (the same count, another layout); the reference's loaders read n
+// and k from the shape and check its last dimension (load_iq2 / load_q8 / load_nv4, engine/bolt_host.cu:198-283).
+const Tensor* sized(b200q_ckpt* c, const std::string& name, size_t bytes, const uint8_t** data,
+                    std::initializer_list<int64_t> shape = {}) {
     const Tensor* t = c->find(name, data);
-    return t && t->end - t->begin == bytes ? t : nullptr;
+    if (!t || t->end - t->begin != bytes) return nullptr;
+    if (shape.size() && (t->shape.size() != shape.size() || !std::equal(shape.begin(), shape.end(), t->shape.begin())))
+        return nullptr;
+    return t;
 }
 
 inline size_t up16(size_t v) { return (v + 15) & ~size_t(15); }
@@ -438,7 +446,7 @@ int b200q_ckpt_pack_iq2_slab(b200q_ckpt* c, const char* const* names, int expert
     if (staging_bytes < raw) return B200Q_ENOSPACE;
     std::vector<const uint8_t*> src((size_t)experts);
     for (int e = 0; e < experts; e++)   // every expert found and of the right size before the first copy
-        if (!names[e] || !sized(c, names[e], raw, &src[(size_t)e])) return B200Q_EINVAL;
+        if (!names[e] || !sized(c, names[e], raw, &src[(size_t)e], {rows, k / 256, 66})) return B200Q_EINVAL;
     const size_t per = iq2_bytes(rows, k);
     for (int e = 0; e < experts; e++) {
         int st = h2d(staging, src[(size_t)e], raw, stream);
@@ -456,7 +464,7 @@ int b200q_ckpt_pack_nv4(b200q_ckpt* c, const char* prefix, int n, int k, void* p
     const std::string p(prefix);
     const uint8_t *q = nullptr, *sc = nullptr, *g = nullptr;
     const size_t qb = (size_t)n * (k / 2), sb = (size_t)n * (k / 16);
-    if (!sized(c, p + ".weight", qb, &q) || !sized(c, p + ".weight_scale", sb, &sc) ||
+    if (!sized(c, p + ".weight", qb, &q, {n, k / 2}) || !sized(c, p + ".weight_scale", sb, &sc, {n, k / 16}) ||
         !sized(c, p + ".weight_scale_2", 4, &g))
         return B200Q_EINVAL;
     memcpy(s2, g, 4);
@@ -474,7 +482,7 @@ int b200q_ckpt_pack_q8(b200q_ckpt* c, const char* name, int n, int k, void* pack
     const size_t raw = b200q_ckpt_staging_bytes(2, n, k);
     if (staging_bytes < raw) return B200Q_ENOSPACE;
     const uint8_t* src = nullptr;
-    if (!sized(c, name, raw, &src)) return B200Q_EINVAL;
+    if (!sized(c, name, raw, &src, {n, k / 32, 34})) return B200Q_EINVAL;
     int st = h2d(staging, src, raw, stream);
     if (st == B200Q_OK) st = b200q_q8_pack(staging, packed, n, k, stream);
     return st;

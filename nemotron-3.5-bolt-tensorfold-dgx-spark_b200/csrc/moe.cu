@@ -583,7 +583,9 @@ int b200q_moe_decode(const void* x, const void* logits, const void* up, const vo
 // __device__ array of kNoAllocScratchBytes, which every GPU that loads the library holds until the process exits.
 // Host code cannot use the array's name as a device address (it is a host-side stand-in), so the first call on each
 // device, with that device current, asks the runtime for the address (cudaGetSymbolAddress) and keeps it; that first
-// call should therefore come before any stream capture.  Every call shares the one array: the layer writes every
+// call should therefore come before any stream capture.  The address is kept for the process's life: a
+// cudaDeviceReset rebuilds the context and may move the array, so the entry point is not for devices that get reset.
+// Every call shares the one array: the layer writes every
 // byte of scratch it reads before reading it, so nothing has to start at zero, but calls that overlap on the GPU
 // (two streams, two threads) race on it.  Shapes whose scratch would exceed the array are refused with
 // B200Q_ENOSPACE.

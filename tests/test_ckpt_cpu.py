@@ -155,6 +155,55 @@ def test_packers_check_everything_before_the_first_copy(tmp_path):
     L.b200q_ckpt_close(h)
 
 
+def test_packers_refuse_a_swapped_shape(tmp_path):
+    """rows and k swapped give the same byte count in another layout: the packers read the shape, as the reference's
+    loaders do (load_iq2 / load_q8 / load_nv4 take n and k from it), and refuse before any copy"""
+    rng = np.random.default_rng(4)
+    iq2 = b200q.synth_iq2_host(3, 64 * 4).tobytes()                       # 64 rows, k 1024
+    q8 = rng.integers(0, 256, 64 * 16 * 34, dtype=np.uint8).tobytes()      # n 64, k 512
+    nq = rng.integers(0, 256, 64 * 256, dtype=np.uint8).tobytes()          # n 64, k 512
+    ns = rng.integers(0x30, 0x40, 64 * 32, dtype=np.uint8).tobytes()
+    write_safetensors(os.path.join(str(tmp_path), "model.safetensors"), {
+        "e.weight": ("U8", (64, 4, 66), iq2), "q.weight": ("U8", (64, 16, 34), q8),
+        "p.weight": ("U8", (64, 256), nq), "p.weight_scale": ("F8_E4M3", (64, 32), ns),
+        "p.weight_scale_2": ("F32", (), np.float32(1).tobytes()),
+    })
+    L = b200q.lib()
+    h = L.b200q_ckpt_open(os.fsencode(str(tmp_path)))
+    assert h
+    fake, null = ctypes.c_void_p(1 << 20), ctypes.c_void_p()
+    arr = lambda xs: (ctypes.c_char_p * len(xs))(*[x.encode() for x in xs])
+    # each request below has the tensor's byte count but not its shape
+    need = L.b200q_ckpt_staging_bytes(0, 256, 256)
+    assert need == len(iq2)
+    assert L.b200q_ckpt_pack_iq2_slab(h, arr(["e.weight"]), 1, 256, 256, fake, fake, need, null) == b200q.EINVAL
+    q8b = L.b200q_ckpt_staging_bytes(2, 16, 2048)
+    assert q8b == len(q8)
+    assert L.b200q_ckpt_pack_q8(h, b"q.weight", 16, 2048, fake, fake, q8b, null) == b200q.EINVAL
+    s2 = ctypes.c_float()
+    nv = L.b200q_ckpt_staging_bytes(1, 128, 256)
+    assert L.b200q_ckpt_pack_nv4(h, b"p", 128, 256, fake, ctypes.byref(s2), fake, nv, null) == b200q.EINVAL
+    L.b200q_ckpt_close(h)
+
+
+def test_tensor_view_outlives_the_checkpoint(tmp_path):
+    """a view from tensor() keeps the shard mapped: reading it after close() or after the Checkpoint is collected
+    returns the bytes (it used to read unmapped memory)"""
+    import gc
+    t = synthetic_model(str(tmp_path))
+    name = "layers.2.self_attn.q_proj.weight"
+    ck = b200q.Checkpoint(str(tmp_path))
+    v1 = ck.tensor(name)[0]
+    ck.close()
+    with pytest.raises(b200q.B200QError):
+        ck.tensor(name)
+    v2 = b200q.Checkpoint(str(tmp_path)).tensor(name)[0]   # the Checkpoint object is dropped at once
+    gc.collect()
+    assert v1.tobytes() == t[name][2] and v2.tobytes() == t[name][2]
+    del v1, v2
+    gc.collect()
+
+
 def test_mutated_headers_never_escape_the_file(tmp_path):
     """300 seeded mutations (byte flips, cuts, duplications) of a valid header: every lookup either fails with EINVAL
     or returns a tensor that lies inside the file with a byte count matching its dtype and shape; nothing crashes"""
