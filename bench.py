@@ -38,6 +38,16 @@ EXPERT_BYTES = 2 * (F * (H // 256) * 66)      # up [F][H] + down [H][F]: 4,325,3
 GEMV_UP_TRAFFIC = 149383424 + 4151040          # DRAM bytes of one captured up-GEMV launch (ncu, config 2)
 
 
+def config2():
+    """the config object of the headline line, the same in both arms"""
+    return {"workload": "BASELINE config 2: decode MoE layer, 16 tokens, hidden 4096, 128 IQ2_XXS experts top-6 "
+                        "(softmax, renormalised) + 1 shared, FFN 2048, ReLU^2",
+            "tokens": T, "hidden": H, "experts": E, "topk": TOPK, "ffn": F, "shared_experts": 1,
+            "l2": f"inputs larger than L2: {LAYERS} rotating layer copies "
+                  f"({LAYERS * (E + 1) * EXPERT_BYTES / 1e9:.2f} GB) and {BATCHES} token batches (the 126 MB L2)",
+            "parallelism": "single"}
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -586,20 +596,34 @@ def run_ours(args, rank, world, local_rank):
 
     # ---- the timed region: K steps, device-timed with events, barrier + synchronize on both sides
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
+    # the K-step region is repeated R times (R chosen so the repeats span about half a second, at least 5) and the
+    # median is the value; the clock sampler runs across all of them
+    ev0.record(stream)
+    for i in range(args.steps):
+        step(args.warmup + i)
+    ev1.record(stream)
     torch.cuda.synchronize()
+    est = max(ev0.elapsed_time(ev1), 1e-3)
+    reps = int(min(500, max(5, 500.0 / est)))
+    runs = []
     with Clocks(local_rank) as clk:
-        ev0.record(stream)
-        for i in range(args.steps):
-            step(args.warmup + i)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-    barrier()
-    ms = ev0.elapsed_time(ev1)
+        for _ in range(reps):
+            barrier()
+            torch.cuda.synchronize()
+            ev0.record(stream)
+            for i in range(args.steps):
+                step(args.warmup + i)
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            barrier()
+            runs.append(ev0.elapsed_time(ev1))
+    ms = float(np.median(runs))
     if dist:
         t = torch.tensor([ms], device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
+    timed = {"repeats": reps, "steps_each": args.steps, "ms_median": round(ms, 5), "ms_min": round(min(runs), 5),
+             "ms_max": round(max(runs), 5), "value_is": "the median repeat"}
     total_bytes = sum(byts[(args.warmup + i) % BATCHES][0] for i in range(args.steps))
     gbs_rank = total_bytes / (ms * 1e-3) / 1e9
     value = gbs_rank * world      # every rank does the same amount of work; the time is the max over ranks
@@ -662,18 +686,15 @@ def run_ours(args, rank, world, local_rank):
             pre["peak_kind"] = "measured cuBLAS bf16 burst (fp16 runs at the same dense rate)"
             pre["moe_frac"] = round(pre["moe_tflops"] / bf16_peak, 4)
             pre["gqa_frac"] = round(pre["gqa_tflops"] / bf16_peak, 4)
-        cpu = cpu_baseline(threads=os.cpu_count() or 1, min_seconds=args.cpu_seconds)
+        cpu = cpu_baseline(threads=os.cpu_count() or 1, min_seconds=args.cpu_seconds,
+                           single_seconds=max(1.0, args.cpu_seconds / 2))
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "BASELINE config 2: decode MoE layer, 16 tokens, hidden 4096, 128 IQ2_XXS experts "
-                                   "top-6 (softmax, renormalised) + 1 shared, FFN 2048, ReLU^2",
-                       "tokens": T, "hidden": H, "experts": E, "topk": TOPK, "ffn": F, "shared_experts": 1,
-                       "mean_distinct_experts": round(float(mean_distinct), 2),
-                       "l2": f"{LAYERS} rotating layer copies ({LAYERS * (E + 1) * EXPERT_BYTES / 1e9:.2f} GB) and "
-                             f"{BATCHES} token batches, larger than the 126 MB L2",
-                       "parallelism": f"replicas{world}" if world > 1 else "single"},
+            "config": config2(),
+            "routing": {"mean_distinct_experts": round(float(mean_distinct), 2)},
+            "timed_region": timed,
             "hbm_fraction": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "kernel": names[dom], "achieved": round(achieved, 1) if achieved else None,
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None,
@@ -701,26 +722,40 @@ def run_ours(args, rank, world, local_rank):
 _CPU_LAYER = {}
 
 
+def _oracle():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    return O
+
+
 def _cpu_layer():
-    """A config-2 layer for the CPU oracle (all 128 experts + the shared one, host-generated once)."""
+    """The config-2 layer for the CPU oracle: all 128 experts + the shared one of layer copy 0, made by the oracle's
+    statement of the seeded generator from the GPU arm's seeds (the same bytes), without the product library."""
     if not _CPU_LAYER:
-        import b200q
-        _CPU_LAYER["up"] = b200q.synth_iq2_host(50, E * F * (H // 256))
-        _CPU_LAYER["down"] = b200q.synth_iq2_host(51, E * H * (F // 256))
-        _CPU_LAYER["su"] = b200q.synth_iq2_host(52, F * (H // 256))
-        _CPU_LAYER["sd"] = b200q.synth_iq2_host(53, H * (F // 256))
+        O = _oracle()
+        _CPU_LAYER["up"] = O.synth_iq2(1000, E * F * (H // 256))
+        _CPU_LAYER["down"] = O.synth_iq2(1001, E * H * (F // 256))
+        _CPU_LAYER["su"] = O.synth_iq2(1002, F * (H // 256))
+        _CPU_LAYER["sd"] = O.synth_iq2(1003, H * (F // 256))
     return _CPU_LAYER
 
 
-def cpu_baseline(threads, min_seconds=10.0, max_passes=1000):
-    """The CPU oracle (the int8-per-32 arithmetic of libbolt's expert kernels, OpenMP over rows with every host
-    thread) on the config-2 layer: whole 16-token passes repeated until `min_seconds` have gone by; GB/s over each
-    pass's touched experts, as the GPU line counts them."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
-    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def _cpu_passes(threads, min_seconds, max_passes, seed=5):
+    O = _oracle()
+    O.set_threads(threads)
     L = _cpu_layer()
-    g = torch.Generator().manual_seed(5)
+    g = torch.Generator().manual_seed(seed)
     nbytes, passes, t0 = 0, 0, time.perf_counter()
     while passes < max_passes and (passes == 0 or time.perf_counter() - t0 < min_seconds):
         x = torch.randn(T, H, generator=g).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
@@ -728,10 +763,23 @@ def cpu_baseline(threads, min_seconds=10.0, max_passes=1000):
         _, ridx, _ = O.moe_layer(x, lg, L["up"], L["down"], L["su"], L["sd"], T, H, F, E, TOPK, mode=0)
         nbytes += (len(np.unique(ridx)) + 1) * EXPERT_BYTES + T * H * 2 + T * E * 2 + T * H * 4
         passes += 1
-    dt = time.perf_counter() - t0
-    return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{passes} passes of the 16-token config-2 layer in {dt:.1f} s (CPU oracle, int8-per-32 "
-                      f"arithmetic, OpenMP over rows)"}
+    return nbytes, passes, time.perf_counter() - t0
+
+
+def cpu_baseline(threads, min_seconds=10.0, max_passes=1000, single_seconds=None):
+    """The CPU oracle (the int8-per-32 arithmetic of libbolt's expert kernels) on the config-2 layer: whole 16-token
+    passes repeated until `min_seconds` have gone by, OpenMP over rows with `threads` threads; GB/s over each pass's
+    touched experts, as the GPU line counts them.  With single_seconds, also one thread alone for that long."""
+    nbytes, passes, dt = _cpu_passes(threads, min_seconds, max_passes)
+    out = {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+           "sample": f"{passes} passes of the 16-token config-2 layer in {dt:.1f} s (CPU oracle, int8-per-32 "
+                     f"arithmetic, OpenMP over rows, {threads} threads)",
+           "nproc": os.cpu_count(), "cpu_model": cpu_model()}
+    if single_seconds:
+        nb1, p1, dt1 = _cpu_passes(1, single_seconds, max_passes, seed=6)
+        out["single_thread"] = {"value": round(nb1 / dt1 / 1e9, 3), "unit": "GB/s", "cores": 1,
+                                "sample": f"{p1} passes in {dt1:.1f} s on one thread"}
+    return out
 
 
 def run_reference(args, rank, world):
@@ -747,9 +795,7 @@ def run_reference(args, rank, world):
     return {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": "BASELINE config 2: decode MoE layer, 16 tokens, hidden 4096, 128 IQ2_XXS experts "
-                                   "top-6 (softmax, renormalised) + 1 shared, FFN 2048, ReLU^2",
-                       "tokens": T, "hidden": H, "experts": E, "topk": TOPK, "ffn": F, "shared_experts": 1},
+            "config": config2(),
             "cpu_baseline": c,
             "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 

@@ -1,9 +1,10 @@
 """Build libb200q.so in place: every csrc/*.cu compiled by nvcc for sm_100a (-gencode arch=compute_100a,code=sm_100a)
 and linked into one shared library beside this file.
 
-The ggml IQ2_XXS tables are compiled in from the reference's own table file, found by path (B200Q_IQ2_TABLES, default
-the reference checkout's engine/iq2_tables.inc); they are not copied into the sources.  Where that file is absent (a GPU box),
-the prebuilt library is used as is.
+The ggml IQ2_XXS tables are compiled in from the reference's own table file, found by path (B200Q_IQ2_TABLES, else
+engine/iq2_tables.inc of a reference checkout named "reference" beside this repository); they are not copied into the
+sources.  Where that file is absent (a GPU box), the prebuilt library is used, and only if it is newer than every
+source: a stale prebuilt library is an error, never silently reused.
 """
 import concurrent.futures
 import os
@@ -15,7 +16,8 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libb200q.so")
 OBJ = os.path.join(HERE, "_build")
-TABLES = os.environ.get("B200Q_IQ2_TABLES", "/root/reference/engine/iq2_tables.inc")
+TABLES = os.environ.get("B200Q_IQ2_TABLES",
+                        os.path.join(os.path.dirname(ROOT), "reference", "engine", "iq2_tables.inc"))
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
@@ -24,6 +26,12 @@ FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxe
 
 def sources():
     return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cu"))
+
+
+def _all_sources():
+    inc = os.path.join(ROOT, "include")
+    return (sources() + [os.path.join(CSRC, h) for h in os.listdir(CSRC) if h.endswith((".cuh", ".h"))] +
+            [os.path.join(inc, h) for h in os.listdir(inc) if h.endswith(".h")])
 
 
 def _stale(target, deps):
@@ -54,9 +62,9 @@ def _compile(src, verbose=False):
 def build(force=False, verbose=False):
     """Compile and link libb200q.so; returns its path."""
     if not os.path.exists(TABLES):
-        if os.path.exists(OUT):
+        if os.path.exists(OUT) and not _stale(OUT, _all_sources()):
             return OUT
-        raise RuntimeError(f"IQ2_XXS table file not found at {TABLES} and no prebuilt {OUT}")
+        raise RuntimeError(f"IQ2_XXS table file not found at {TABLES} and no prebuilt {OUT} newer than its sources")
     os.makedirs(OBJ, exist_ok=True)
     if force:
         for f in os.listdir(OBJ):

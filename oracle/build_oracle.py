@@ -1,8 +1,10 @@
 """Build the CPU oracle (oracle.c -> oracle/liboracle.so) -- TEST INFRASTRUCTURE ONLY.
 
 The oracle is the checker of the B200 kernels; only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg
-load it.  The ggml IQ2_XXS tables are compiled in from the reference's table file by path (B200Q_IQ2_TABLES, default
-the reference checkout's engine/iq2_tables.inc).  Where that file is absent (a GPU box) the prebuilt library is used.
+load it.  The ggml IQ2_XXS tables are compiled in from the reference's table file by path (B200Q_IQ2_TABLES, else
+engine/iq2_tables.inc of the reference checkout: B200Q_REF_ENGINE, else a checkout named "reference" beside this
+repository).  Where that file is absent (a GPU box) the prebuilt library is used, and only if it is newer than its
+sources: a stale prebuilt library is an error, never silently reused.
 
 With --ref it also builds oracle/_ref/libbolt_ref.so: the reference's own kernels (engine/bolt_kernels.cu, compiled
 from where it lies) for sm_100a, with oracle/ref_shim.cu giving them extern "C" entry points.  That library lets the
@@ -16,7 +18,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "liboracle.so")
 REF_DIR = os.path.join(HERE, "_ref")
 REF_OUT = os.path.join(REF_DIR, "libbolt_ref.so")
-ENGINE = os.environ.get("B200Q_REF_ENGINE", "/root/reference/engine")
+ENGINE = os.environ.get("B200Q_REF_ENGINE",
+                        os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference", "engine"))
 TABLES = os.environ.get("B200Q_IQ2_TABLES", os.path.join(ENGINE, "iq2_tables.inc"))
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
@@ -28,9 +31,9 @@ def _stale(target, deps):
 def build():
     src = os.path.join(HERE, "oracle.c")
     if not os.path.exists(TABLES):
-        if os.path.exists(OUT):
+        if os.path.exists(OUT) and not _stale(OUT, [src]):
             return OUT
-        raise RuntimeError(f"IQ2_XXS table file not found at {TABLES} and no prebuilt {OUT}")
+        raise RuntimeError(f"IQ2_XXS table file not found at {TABLES} and no up-to-date prebuilt {OUT}")
     if _stale(OUT, [src, __file__]):
         cmd = ["gcc", "-O3", "-march=x86-64-v3", "-fopenmp", "-ffp-contract=off", "-fPIC", "-shared",
                f"-DB200Q_IQ2_TABLES=\"{TABLES}\"", src, "-o", OUT, "-lm"]
@@ -45,7 +48,7 @@ def build_ref():
     kern = os.path.join(ENGINE, "bolt_kernels.cu")
     shim = os.path.join(HERE, "ref_shim.cu")
     if not os.path.exists(kern):
-        if os.path.exists(REF_OUT):
+        if os.path.exists(REF_OUT) and not _stale(REF_OUT, [shim]):
             return REF_OUT
         return None
     os.makedirs(REF_DIR, exist_ok=True)

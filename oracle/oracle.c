@@ -558,3 +558,48 @@ EXPORT void or_iq2_gemm_f16fold(const uint8_t* blocks, int N, int K, const float
         free(w);
     }
 }
+
+/* ------------------------------------------------------------------------------------------------------ */
+/* inputs and threads of the timed CPU arm                                                                 */
+/* ------------------------------------------------------------------------------------------------------ */
+
+/* BASELINE's seeded IQ2_XXS generator (d fp16 ~ U[1e-3, 1e-2], grid indices U{0..255}, sign indices U{0..127},
+ * sub-scales U{0..15}; block i depends on (seed, i) only), stated here so that the CPU arm of the benchmark makes
+ * the weights the GPU arm makes from the same seed without loading the product library.  A CPU test checks the bytes
+ * against the library's host generator. */
+static uint64_t or_splitmix64(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+
+EXPORT void or_synth_iq2(uint64_t seed, int64_t nblocks, uint8_t* out) {
+    int64_t i;
+#pragma omp parallel for schedule(static)
+    for (i = 0; i < nblocks; i++) {
+        uint8_t* b = out + i * 66;
+        uint64_t h = or_splitmix64(seed ^ or_splitmix64((uint64_t)i * 0x100000001B3ull + 0x51ED27ull));
+        const float u = (float)(h >> 40) * (1.f / 16777216.f);
+        const uint16_t d = or_f2h(1e-3f + 9e-3f * u);
+        int c;
+        b[0] = (uint8_t)(d & 255);
+        b[1] = (uint8_t)(d >> 8);
+        for (c = 0; c < 8; c++) {
+            uint32_t grid, aux, s4, hi;
+            uint8_t* p = b + 2 + 8 * c;
+            h = or_splitmix64(h + (uint64_t)c);
+            grid = (uint32_t)h;
+            aux = (uint32_t)(h >> 32);
+            s4 = (uint32_t)(or_splitmix64(h ^ 0xA5A5ull) & 15u);
+            hi = (aux & 0x0fffffffu) | (s4 << 28);
+            p[0] = (uint8_t)grid; p[1] = (uint8_t)(grid >> 8); p[2] = (uint8_t)(grid >> 16); p[3] = (uint8_t)(grid >> 24);
+            p[4] = (uint8_t)hi; p[5] = (uint8_t)(hi >> 8); p[6] = (uint8_t)(hi >> 16); p[7] = (uint8_t)(hi >> 24);
+        }
+    }
+}
+
+/* the OpenMP thread count of the oracle's parallel loops (1: the scalar single-thread baseline) */
+#include <omp.h>
+EXPORT void or_set_threads(int n) { omp_set_num_threads(n > 0 ? n : 1); }
+EXPORT int or_max_threads(void) { return omp_get_max_threads(); }

@@ -44,6 +44,8 @@ def lib():
             "or_q8_gemm_exact": (None, [vp, i32, i32, vp, i32, vp]),
             "or_q8_gemm_f16fold": (None, [vp, i32, i32, vp, i32, vp]),
             "or_iq2_gemm_f16fold": (None, [vp, i32, i32, vp, i32, vp, i32]),
+            "or_synth_iq2": (None, [ctypes.c_uint64, i64, vp]),
+            "or_set_threads": (None, [i32]), "or_max_threads": (i32, []),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -207,6 +209,18 @@ def iq2_gemm_f16fold(blocks, n, k, x, epi=0):
     b = _c(blocks, np.uint8)
     lib().or_iq2_gemm_f16fold(_p(b), n, k, _p(x), x.shape[0], _p(y), epi)
     return y
+
+
+def synth_iq2(seed, nblocks):
+    """BASELINE's seeded IQ2_XXS blocks [nblocks][66] (the same bytes as the library's generator for the seed)"""
+    out = np.empty((nblocks, 66), np.uint8)
+    lib().or_synth_iq2(seed, nblocks, _p(out))
+    return out
+
+
+def set_threads(n):
+    """the OpenMP threads of the oracle's loops (1: single-thread)"""
+    lib().or_set_threads(int(n))
 
 
 def scalar(name, *args):

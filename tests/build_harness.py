@@ -1,6 +1,6 @@
 """Build tests/_build/libbolt_shim_harness.so (TEST INFRASTRUCTURE): tests/bolt_shim_harness.cu linked against the
 package's libb200q.so (nvcc, sm_100a host code only; the shims it calls live in libb200q).  Where nvcc or the
-library is missing (a GPU box with the prebuilt files), an existing build is kept."""
+library is missing (a GPU box with the prebuilt files), an existing build is kept if it is newer than its source."""
 import os
 import subprocess
 
@@ -17,9 +17,9 @@ def build():
     if os.path.exists(OUT) and os.path.getmtime(OUT) >= max(os.path.getmtime(SRC), os.path.getmtime(lib)):
         return OUT
     if not os.path.exists(NVCC):
-        if os.path.exists(OUT):
+        if os.path.exists(OUT) and os.path.getmtime(OUT) >= os.path.getmtime(SRC):
             return OUT
-        raise RuntimeError("nvcc not found and no prebuilt harness")
+        raise RuntimeError("nvcc not found and no prebuilt harness newer than its source")
     os.makedirs(os.path.dirname(OUT), exist_ok=True)
     cmd = [NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-O2", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
            "-I", os.path.join(ROOT, "include"), SRC, "-o", OUT, "-L", PKG, "-lb200q",

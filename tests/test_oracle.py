@@ -263,3 +263,12 @@ def test_q8_gemm_exact():
     assert np.allclose(O.q8_gemm_exact(blocks, n, k, x), x.astype(np.float64) @ w.T, rtol=1e-6, atol=1e-6)
     wf = (qv.astype(np.float32) * d.astype(np.float32)[..., None]).astype(np.float16).astype(np.float32).reshape(n, k)
     assert np.allclose(O.q8_gemm_f16fold(blocks, n, k, x), x.astype(np.float64) @ wf.T, rtol=1e-6, atol=1e-6)
+
+
+def test_oracle_generator_matches_the_library():
+    """the bench's CPU arm makes its weights with the oracle's statement of the seeded generator: the same bytes as
+    the library's host generator for the same seed"""
+    import b200q
+    a = O.synth_iq2(1001, 3000)
+    b = np.asarray(b200q.synth_iq2_host(1001, 3000)).reshape(a.shape)
+    assert np.array_equal(a, b)
