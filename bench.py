@@ -800,6 +800,30 @@ def run_reference(args, rank, world):
             "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def decode_only(b200q, device, steps, warmup):
+    """The config-2 decode layer alone, `warmup` then `steps` steps over the --layers copies, timed with events (the
+    small case the profiling commands capture)."""
+    layers = make_layers(b200q, device)
+    xs_h, ls_h = make_batches(0, device)
+    xs = [x.to(device) for x in xs_h]
+    ls = [l.to(device) for l in ls_h]
+    out = torch.empty(T, H, dtype=torch.float32, device=device)
+    ridx = [torch.empty(T, TOPK, dtype=torch.int32, device=device) for _ in range(BATCHES)]
+    for i in range(warmup):
+        layers[i % LAYERS](xs[i % BATCHES], ls[i % BATCHES], out=out, ridx=ridx[i % BATCHES])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        layers[i % LAYERS](xs[i % BATCHES], ls[i % BATCHES], out=out, ridx=ridx[i % BATCHES])
+    e1.record()
+    torch.cuda.synchronize()
+    nb = sum(step_bytes(ridx[i % BATCHES].cpu().numpy())[0] for i in range(steps))
+    ms = e0.elapsed_time(e1)
+    return {"decode": {"gbs": round(nb / (ms * 1e-3) / 1e9, 1), "ms_per_step": round(ms / steps, 5),
+                       "layers": LAYERS, "device_error": b200q.device_error()}}
+
+
 def ckpt_bench(b200q, device, reps=3):
     """Checkpoint ingestion (b200q_ckpt_*): one MoE layer at the model's own shapes (layer 1 of its schedule: 240
     IQ2_XXS experts, width 2048, latent 1024; up and down in two safetensors shards, 260 MB) written to disk, then
@@ -863,7 +887,7 @@ def main():
     ap.add_argument("--layers", type=int, default=4, help="layer copies rotated to defeat L2 (1 for small profiles)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="length of the CPU-baseline sample")
     ap.add_argument("--no-prefill", dest="prefill", action="store_false", help="skip the config-4 prefill GEMMs")
-    ap.add_argument("--only", choices=["prefill", "nvfp4", "ep", "ckpt"], default=None,
+    ap.add_argument("--only", choices=["decode", "prefill", "nvfp4", "ep", "ckpt"], default=None,
                     help="run one sub-measurement on one GPU and print its object (for profiling)")
     args = ap.parse_args()
     global LAYERS
@@ -876,7 +900,9 @@ def main():
         import b200q
         device = torch.device("cuda", local_rank)
         torch.cuda.set_device(device)
-        if args.only == "prefill":
+        if args.only == "decode":
+            line = decode_only(b200q, device, args.steps, args.warmup)
+        elif args.only == "prefill":
             up, down, _, _ = full_layer(b200q, device, 0)
             line = prefill_bench(b200q, type("L", (), {"up": up, "down": down}), device)
         elif args.only == "nvfp4":

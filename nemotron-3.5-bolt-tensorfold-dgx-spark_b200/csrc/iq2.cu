@@ -469,7 +469,11 @@ __device__ __forceinline__ bool unit_rows(const GemvArgs& a, int g, const Ids& i
         // the signed magnitudes {8, 25, 43, -8 | -25, -43} as two words, loaded rather than written as immediates:
         // held in registers they cost two, rebuilt at each use they cost an instruction a prmt
         const uint2 tb = lds64(sc.kc);
+#ifdef B200Q_X_UNROLL_J
+#pragma unroll
+#else
 #pragma unroll 1
+#endif
         for (int j = 0; j < 4; j++) {
             const uint4 q = lds128(st + j * 512 + lane * 16);
             float se[NT], so[NT];   // the tokens' scales of chunks 2j, 2j + 1
@@ -495,7 +499,11 @@ __device__ __forceinline__ bool unit_rows(const GemvArgs& a, int g, const Ids& i
                     const uint32_t sel_b = 0x7604u | ((uint32_t)gg << 4);
                     const uint32_t sel = lds_tbl(prmt(qx, lane_c, sel_b)) + lds_tbl(prmt(qy, lane_s, sel_b));
                     wq[2 * gg] = prmt(tb.x, tb.y, sel);
+#ifdef B200Q_X_UMULHI
+                    wq[2 * gg + 1] = prmt(tb.x, tb.y, __umulhi(sel, 0x10000u));
+#else
                     wq[2 * gg + 1] = prmt(tb.x, tb.y, sel >> 16);
+#endif
                 }
 #pragma unroll
                 for (int m = 0; m < NT; m++) {
