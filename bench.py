@@ -35,7 +35,10 @@ METRIC = "IQ2_XXS MoE decode GB/s"
 T, H, F, E, TOPK = 16, 4096, 2048, 128, 6
 LAYERS, BATCHES = 4, 8
 EXPERT_BYTES = 2 * (F * (H // 256) * 66)      # up [F][H] + down [H][F]: 4,325,376 B
-GEMV_UP_TRAFFIC = 149383424 + 4151040          # DRAM bytes of one captured up-GEMV launch (ncu, config 2)
+# DRAM bytes (read + write) of one captured decode_layer_k launch at config 2, per the ncu summary in profiles/
+# (None until captured for the current kernel)
+LAYER_TRAFFIC = None
+LAYER_TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum of one decode_layer_k launch at config 2"
 
 
 def config2():
@@ -628,24 +631,24 @@ def run_ours(args, rank, world, local_rank):
     gbs_rank = total_bytes / (ms * 1e-3) / 1e9
     value = gbs_rank * world      # every rank does the same amount of work; the time is the max over ranks
 
-    # ---- per-kernel durations (a second pass with events between the four launches)
+    # ---- the layer kernel's own duration: the layer is one launch (decode_layer_k: router, grouping, the int8 rows
+    # of x, up with relu^2, down, combine); a second pass with events around each launch (events between launches stop
+    # the programmatic overlap with the next step, so this is the kernel alone, ramp included)
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
     for e in evs:
         e.record(stream)      # torch creates the CUDA event on its first record
-    stage_ms = np.zeros(4)
+    kern_ms, kern_bytes = [], []
     nprof = max(args.steps, 4)
     for i in range(nprof):
         step(args.warmup + i, stage_events=evs)
         torch.cuda.synchronize()
-        stage_ms += [evs[j].elapsed_time(evs[j + 1]) for j in range(4)]
-    stage_ms /= nprof
-    names = ["prep (router+group+quant)", "up GEMV (relu^2 + int8)", "down GEMV", "combine"]
-    dom = int(np.argmax(stage_ms))
+        kern_ms.append(evs[0].elapsed_time(evs[4]))
+        kern_bytes.append(byts[(args.warmup + i) % BATCHES][0])
     mean_distinct = np.mean([byts[(args.warmup + i) % BATCHES][1] for i in range(nprof)])
-    half = (mean_distinct + 1) * EXPERT_BYTES / 2
-    dom_bytes = {1: half + T * H + (T * TOPK + T) * F * 1.125, 2: half + (T * TOPK + T) * (F * 1.125 + H * 4)}.get(dom, 0)
+    dom_ms = float(np.mean(kern_ms))
+    dom_bytes = float(np.mean(kern_bytes))
     peak, peak_kind = peaks()
-    achieved = dom_bytes / (stage_ms[dom] * 1e-3) / 1e9 if dom_bytes else None
+    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
 
     # ---- e2e: the public API with host buffers (pinned), H2D of x and logits, D2H of the output, every step
     xh = [x.pin_memory() for x in xs_h]
@@ -696,17 +699,16 @@ def run_ours(args, rank, world, local_rank):
             "routing": {"mean_distinct_experts": round(float(mean_distinct), 2)},
             "timed_region": timed,
             "hbm_fraction": round(value / world / peak, 4),
-            "roofline": {"bound": "hbm", "kernel": names[dom], "achieved": round(achieved, 1) if achieved else None,
-                         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None,
-                         "traffic": GEMV_UP_TRAFFIC if dom == 1 else None,
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one up launch at this "
-                                           "config (profiles/iq2_gemv_config2_ncu.md)",
+            "roofline": {"bound": "hbm", "kernel": "decode_layer_k (the whole layer, one launch)",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": LAYER_TRAFFIC,
+                         "traffic_source": LAYER_TRAFFIC_SOURCE,
                          "algorithmic_bytes": round(dom_bytes), "peak_kind": peak_kind,
-                         "stage_ms": {n: round(float(v), 5) for n, v in zip(names, stage_ms)}},
+                         "kernel_ms": round(dom_ms, 5)},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": T * H * 2 + T * E * 2,
                     "d2h_bytes_per_step": T * H * 4},
-            "gpu_launches": 4 * args.steps,
+            "gpu_launches": args.steps,   # one decode_layer_k launch a step
             "clocks": clk.summary(),
         }
         if pre:

@@ -32,6 +32,7 @@
 // re-encodes ggml's sign word (four 7-bit fields, s4 in bits 28-31) as four bytes, byte g = field g | bit g of s4 << 7;
 // the spare top bit selects the table's second, identical half of sign words.
 #include "iq2.cuh"
+#include "moe.cuh"
 
 #include <atomic>
 #include <cstring>
@@ -174,7 +175,11 @@ constexpr int kMaxSlots = 520;
 constexpr uint32_t kTblAddr = 0x10000;
 constexpr int kQueue = kStages + 1;         // a warp's queue of units grabbed ahead (its producer is <= kStages ahead)
 // barriers, slot counts / order / unit prefix, the warps' unit queues, the two magnitude words (8-byte aligned)
-constexpr uint32_t kHdrBytes = kGemvWarps * kStages * 8 + (3 * kMaxSlots + 1) * 4 + kGemvWarps * kQueue * (2 + kUnitTok) * 4 + 12 + 16;
+// the one-launch decode layer keeps its own schedule in shared memory: at most kLayerSlots slots and kLayerIds ids
+// (pairs + shared-expert rows, also the most batches); larger layers take the three-launch path
+constexpr int kLayerSlots = 257, kLayerIds = 512;
+constexpr uint32_t kHdrBytes = kGemvWarps * kStages * 8 + (3 * kMaxSlots + 1) * 4 + kGemvWarps * kQueue * (3 + kUnitTok) * 4 +
+                               (kLayerSlots + 1 + 2 * kLayerIds) * 4 + 12 + 16;
 constexpr int kNumStages = kGemvWarps * kStages;
 constexpr uint32_t kMaxDynBase = 1024;
 constexpr int kStagesBelowMin = (int)((kTblAddr - kMaxDynBase - kHdrBytes - 16) / kStageBytes);
@@ -184,9 +189,25 @@ constexpr unsigned long long kWaitNs = 2000000000ull;   // a ring stage not fill
 
 enum Epi { kStore = 0, kRelu2 = 1, kRelu2Q8 = 2, kDots = 3 };
 
-__device__ int g_iq2_error;   // bit 0: a ring wait timed out; bit 1: the shared-memory layout did not fit
-// per launch slot: the next unit to hand out, and the CTAs done (the last one resets both for the slot's next launch)
-__device__ int g_unit_ctr[kUnitCtrs][2];
+// bit 0: a ring wait timed out; bit 1: the shared-memory layout did not fit; bit 3: a fused launch's down unit
+// waited more than 2 s for its batch's up rows; bit 4: a fused launch's batch order held an index out of range;
+// bit 5: a wait of the one-launch decode layer (schedule, x's rows, the CTAs' units) gave up
+__device__ int g_iq2_error;
+#ifdef B200Q_X_TRACE
+__device__ unsigned long long g_x_trace[160][16];   // per CTA: %globaltimer at the layer's phase points
+#define XTRACE(i) do { if (threadIdx.x == 0) g_x_trace[blockIdx.x][i] = globaltimer(); } while (0)
+#else
+#define XTRACE(i) do { } while (0)
+#endif
+#ifdef B200Q_X_STATS
+__device__ unsigned long long g_x_stats[4];   // pending waits, their ns, pending units taken, down units taken
+#endif
+// per launch slot: [0] the next unit to hand out, [1] the CTAs done (the last one resets the slot for its next
+// launch), [6] set when a wait of the launch gave up (the other waits of the launch then give up at once); the
+// one-launch decode layer also uses [4] the CTAs done quantising x and [5] the CTAs done with their units
+__device__ int g_unit_ctr[kUnitCtrs][8];
+// the one-launch decode layer's readiness counters per launch slot (one a batch), zero between the slot's launches
+__device__ int g_layer_ready[kUnitCtrs][kLayerIds];
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
     uint32_t d;
@@ -233,6 +254,17 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
         if (globaltimer() - t0 > ns) return false;
     return true;
 }
+// A weight copy, read once a step: marked to leave L2 first (an evict_first policy), so that the step's streamed
+// weights do not push out what is read again (the code, the tables, the activation rows between the projections).
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void bulk_g2s_stream(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar, uint64_t pol) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(pol) : "memory");
+}
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
@@ -278,38 +310,61 @@ __device__ __forceinline__ void group_weights(uint32_t lane_c, uint32_t lane_s, 
 // Units: (slot s, token batch b0 of kUnitTok tokens, 32-row group g).  Every CTA orders the slots by token count,
 // largest first, and numbers their units in that order (batch-major, then row group); warps take unit numbers from
 // a global counter as they go, so the expensive units go first and the tail is short and shared by all warps.
+//
+// A fused launch runs two phases over the same slots and schedule: the up projection's units (ReLU^2 and the int8
+// rows of the result), then the down projection's units over those rows.  A down unit of (slot, batch) needs the
+// batch's up rows for every row group of the up output, so each up unit adds one to its batch's readiness counter
+// once its rows are stored, and the producer of a down unit waits (bounded) for the counter to reach the up phase's
+// row-group count before it issues the unit's first copy.  Units are handed out in order, so every up unit a down unit
+// waits for is already held by a running warp, and nothing an up unit does waits on a down unit: the waits end.
 struct Unit {
-    int s, b0, g, nt;
+    int s, b0, g, nt, bidx;   // slot, first token, row group, tokens, the batch's index in schedule order
 };
-__device__ __forceinline__ Unit decode_unit(int u, const int* s_order, const int* s_upre, const int* s_cnt, int nslots,
-                                            int G) {
-    int lo = 0, hi = nslots;   // the last ordered slot whose first unit is <= u
+
+// The CTA's unit bookkeeping in shared memory: the slots by token count and the exclusive prefix of their batches.
+struct Sched {
+    const int *cnt, *order, *bpre;
+    int nslots;
+    int G, U;                // the (first) phase: row groups, units
+    int G2, U2;              // a fused launch's down phase (U2 = 0 otherwise)
+    const int* dorder;       // its order of batches
+    const int* offs;         // the one-launch layer: the slots' offsets and the ids in slot order (shared memory;
+    const int* ord;          // nullptr: read the arguments' offsets and order from global memory)
+    uint32_t kc;             // shared address of the two words of signed magnitudes (prmt sources)
+};
+
+// unit u of a phase of G row groups
+__device__ __forceinline__ Unit decode_unit(int u, const Sched& sc, int G) {
+    int lo = 0, hi = sc.nslots;   // the last ordered slot whose first unit is <= u
     while (hi - lo > 1) {
         const int mid = (lo + hi) >> 1;
-        if (s_upre[mid] <= u) lo = mid;
+        if (sc.bpre[mid] * G <= u) lo = mid;
         else hi = mid;
     }
     Unit w;
-    w.s = s_order[lo];
-    const int r = u - s_upre[lo], b = r / G;
+    w.s = sc.order[lo];
+    const int r = u - sc.bpre[lo] * G, b = r / G;
+    w.bidx = sc.bpre[lo] + b;
     w.b0 = b * kUnitTok;
     w.g = r - b * G;
-    w.nt = min(kUnitTok, s_cnt[w.s] - w.b0);
+    w.nt = min(kUnitTok, sc.cnt[w.s] - w.b0);
     return w;
 }
 
 // A warp's ring: kStages shared-memory stages used in turn.  `slot` is the stage the warp reads next and `par` the
-// parity of its barrier's next phase; consumed / issued count super-blocks (for the drain after a timeout).
+// parity of its barrier's next phase; consumed / issued count super-blocks (for the drain after a timeout, and for
+// lane 0 to see that the ring ran empty).
 struct Ring {
     uint32_t st[kStages];    // the stages' shared addresses
     uint32_t bar0;           // the first stage's barrier (the others 8 bytes apart)
     int slot, consumed, issued;
     uint32_t par;
     static_assert(kStages == 2 || kStages == 3, "stage() selects among two or three stages");
-    __device__ __forceinline__ uint32_t stage() const {
-        if constexpr (kStages == 2) return slot == 0 ? st[0] : st[1];
-        else return slot == 0 ? st[0] : slot == 1 ? st[1] : st[2];
+    __device__ __forceinline__ uint32_t stage_at(int sl) const {   // selects, so st stays in registers
+        if constexpr (kStages == 2) return sl == 0 ? st[0] : st[1];
+        else return sl == 0 ? st[0] : sl == 1 ? st[1] : st[2];
     }
+    __device__ __forceinline__ uint32_t stage() const { return stage_at(slot); }
     __device__ __forceinline__ uint32_t bar() const { return bar0 + 8u * (uint32_t)slot; }
     __device__ __forceinline__ void advance() {
         consumed++;
@@ -324,38 +379,79 @@ __device__ __forceinline__ const uint8_t* slot_weights(const GemvArgs& a, int s)
     return (a.counts == nullptr || s < a.nslot_routed) ? a.slab + (size_t)s * a.expert_bytes : a.extra_w;
 }
 
-// A queue entry: the unit's row group (-1: no more units), its token count, then its token ids.
-constexpr int kQEntry = 2 + kUnitTok;
+// A queue entry: the unit's row group (-1: no more units), its token count, its phase and batch index
+// (phase | bidx << 1), then its token ids.
+constexpr int kQEntry = 3 + kUnitTok;
 
-// Lane 0's producer: takes units from the launch's counter, queues them for its warp (row group, token count and
-// ids), and fills the warp's ring with their super-blocks (weights, the tokens' int8 rows and, unless the launch
-// returns chunk dots, their scales).  Every source pointer is set once a unit and advanced by a constant a stage.
-// The CTA's unit bookkeeping in shared memory: the slots by token count and the exclusive prefix of their units.
-struct Sched {
-    const int *cnt, *order, *upre;
-    int nslots, G, U;
-    uint32_t kc;             // shared address of the two words of signed magnitudes (prmt sources)
-};
+__device__ __forceinline__ int ld_acquire(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 
+// Lane 0's producer: takes units from the launch's counter, queues them for its warp (row group, token count, phase,
+// ids), and fills the warp's ring with their super-blocks (weights, the tokens' int8 rows and, with kScl, their
+// scales).  Every source pointer is set once a unit and advanced by a constant a stage.
+//
+// A fused launch's down unit whose batch is not complete when it is taken is `pending`: the producer issues nothing
+// for it and never waits (its warp may still be reading an up unit that others wait for); the warp waits, bounded, only
+// when its ring has run empty (force), when it holds no unfinished up unit.
 template <bool kScl>
 struct Producer {
     int* queue;              // this warp's kQueue entries of kQEntry ints
     int pn;                  // units grabbed
     int nt, left;            // the unit being issued: its tokens, and its super-blocks not yet issued (0: none)
+    int pending;             // 1 + the batch index a pending down unit waits for, or 0
+    bool split;              // its weights in the split layout
     const uint8_t* wsrc;     // its next super-block of weights
     const uint8_t* dsrc;     // the split layout: its next 64 bytes of d
-    int xoff[kUnitTok];      // element offsets of its tokens' next int8 blocks (from a.xq) and scales (from a.xs)
+    const int8_t* xq;        // its phase's int8 rows and scales
+    const float* xs;
+    int xoff[kUnitTok];      // element offsets of its tokens' next int8 blocks (from xq) and scales (from xs)
     int soff[kUnitTok];
+
+    // the unit's queue entry and source pointers, from its phase's arguments
+    __device__ __forceinline__ void fill(const GemvArgs& p, const Sched& sc, const Unit& w, int phase, int* e) {
+        // offsets and order are read at L2 (cg): they may be taken before this grid waits for its predecessor
+        const int base = sc.offs ? sc.offs[w.s] : p.counts ? __ldcg(p.offsets + w.s) : 0;
+        e[0] = w.g;
+        e[1] = w.nt;
+        e[2] = phase | (w.bidx << 1);
+#pragma unroll
+        for (int m = 0; m < kUnitTok; m++) {
+            const int mm = m < w.nt ? m : 0;
+            const int id = sc.ord ? sc.ord[base + w.b0 + mm] : p.counts ? __ldcg(p.order + base + w.b0 + mm) : w.b0 + mm;
+            const int arow = id < p.act_split ? id / p.act_div : id - p.act_split + p.act_base;
+            e[3 + m] = id;
+            xoff[m] = arow * p.k;
+            if (kScl) soff[m] = arow * (p.k >> 5);
+        }
+        const size_t unit0 = (size_t)w.g * (p.k >> 8);   // the unit's first (tile, super-block)
+        split = p.dplane != nullptr;
+        if (split) {
+            const bool routed = p.counts == nullptr || w.s < p.nslot_routed;   // as slot_weights
+            wsrc = slot_weights(p, w.s) + unit0 * 2048;
+            dsrc = (routed ? p.dplane + (size_t)w.s * p.dplane_stride : p.dplane_extra) + unit0 * 64;
+        } else {
+            wsrc = slot_weights(p, w.s) + unit0 * kIq2Unit;
+        }
+        xq = p.xq;
+        xs = p.xs;
+        nt = w.nt;
+        left = p.k >> 8;
+    }
 
     // A warp's first unit is fixed, warp w of CTA b taking unit w * gridDim + b (consecutive units, the heaviest
     // first, land on different SMs), so a launch does not open with every warp of the GPU contending for one
     // counter; the counter hands out the units after those.
-    __device__ __forceinline__ void grab(const GemvArgs& a, const Sched& sc) {
+    template <bool FUSED>
+    __device__ __forceinline__ void grab(const GemvArgs& a, const GemvArgs& b, const Sched& sc, const int* ready,
+                                         int ctr) {
         const int u = pn == 0 ? (int)(threadIdx.x >> 5) * (int)gridDim.x + (int)blockIdx.x
-                              : (int)gridDim.x * kGemvWarps + atomicAdd(&g_unit_ctr[a.ctr][0], 1);
+                              : (int)gridDim.x * kGemvWarps + atomicAdd(&g_unit_ctr[ctr][0], 1);
         int* e = queue + (pn % kQueue) * kQEntry;
         pn++;
-        if (u >= sc.U) {
+        if (u >= sc.U + sc.U2) {
             // no units left for this warp: the next launch on the stream may be scheduled now (it still waits for
             // this grid's completion before it reads anything), so its CTAs build their tables during this tail
             pdl_trigger();
@@ -363,58 +459,98 @@ struct Producer {
             left = 0;
             return;
         }
-        const Unit w = decode_unit(u, sc.order, sc.upre, sc.cnt, sc.nslots, sc.G);
-        // offsets and order are read at L2 (cg): they may be taken before this grid waits for its predecessor
-        const int base = a.counts ? __ldcg(a.offsets + w.s) : 0;
-        e[0] = w.g;
-        e[1] = w.nt;
-#pragma unroll
-        for (int m = 0; m < kUnitTok; m++) {
-            const int mm = m < w.nt ? m : 0;
-            const int id = a.counts ? __ldcg(a.order + base + w.b0 + mm) : w.b0 + mm;
-            const int arow = id < a.act_split ? id / a.act_div : id - a.act_split + a.act_base;
-            e[2 + m] = id;
-            xoff[m] = arow * a.k;
-            if (kScl) soff[m] = arow * (a.k >> 5);
+        if (!FUSED || u < sc.U) {
+            fill(a, sc, decode_unit(u, sc, sc.G), 0, e);
+            return;
         }
-        const size_t unit0 = (size_t)w.g * (a.k >> 8);   // the unit's first (tile, super-block)
-        if (a.dplane) {
-            const bool routed = a.counts == nullptr || w.s < a.nslot_routed;   // as slot_weights
-            wsrc = slot_weights(a, w.s) + unit0 * 2048;
-            dsrc = (routed ? a.dplane + (size_t)w.s * a.dplane_stride : a.dplane_extra) + unit0 * 64;
-        } else {
-            wsrc = slot_weights(a, w.s) + unit0 * kIq2Unit;
+        // the down phase runs batch by batch in the prologue's order (iq2_schedule_batches), each batch's row groups
+        // in turn
+        const int uu = u - sc.U, p = uu / sc.G2;
+        Unit w;
+        w.bidx = sc.offs ? sc.dorder[p] : __ldcg(sc.dorder + p);
+        if ((unsigned)w.bidx >= (unsigned)sc.bpre[sc.nslots]) {   // never, with a whole order: refuse, not read past it
+            atomicOr(&g_iq2_error, 16);
+            e[0] = -1;
+            left = 0;
+            return;
         }
-        nt = w.nt;
-        left = a.k >> 8;
+        const int i = iq2_batch_slot(sc.bpre, sc.nslots, w.bidx);
+        w.s = sc.order[i];
+        w.b0 = (w.bidx - sc.bpre[i]) * kUnitTok;
+        w.g = uu - p * sc.G2;
+        w.nt = min(kUnitTok, sc.cnt[w.s] - w.b0);
+        fill(b, sc, w, 1, e);
+#ifdef B200Q_X_STATS
+        atomicAdd(&g_x_stats[3], 1ull);
+#endif
+        if (ld_acquire(ready + w.bidx) < sc.G) pending = 1 + w.bidx;   // the batch's up rows are not all in
+        else asm volatile("fence.proxy.async.global;" ::: "memory");   // rows read by the async proxy (bulk copies)
     }
+
     // the unit's next super-block into the stage at st (barrier bar), which the warp has finished reading
-    __device__ __forceinline__ void issue(const GemvArgs& a, const Sched& sc, uint32_t st, uint32_t bar, Ring& r) {
-        if (left == 0) return;
+    template <bool FUSED>
+    __device__ __forceinline__ void issue(const GemvArgs& a, const GemvArgs& b, const Sched& sc, const int* ready,
+                                          int ctr, uint32_t st, uint32_t bar, Ring& r) {
+        if (left == 0 || (FUSED && pending)) return;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the warp's reads of the stage come first
         mbar_expect_tx(bar, (uint32_t)(kIq2Unit + nt * (kScl ? 288 : 256)));
-        if (a.dplane) {
-            bulk_g2s(st, wsrc, 2048, bar);
-            bulk_g2s(st + 2048, dsrc, 64, bar);
+        if (split) {
+            bulk_g2s_stream(st, wsrc, 2048, bar, evict_first_policy());
+            bulk_g2s_stream(st + 2048, dsrc, 64, bar, evict_first_policy());
             wsrc += 2048;
             dsrc += 64;
         } else {
-            bulk_g2s(st, wsrc, kIq2Unit, bar);
+            bulk_g2s_stream(st, wsrc, kIq2Unit, bar, evict_first_policy());
             wsrc += kIq2Unit;
         }
 #pragma unroll
         for (int m = 0; m < kUnitTok; m++) {
             if (m < nt) {
-                bulk_g2s(st + kStageAct + m * 256, a.xq + xoff[m], 256, bar);
+                bulk_g2s(st + kStageAct + m * 256, xq + xoff[m], 256, bar);
                 xoff[m] += 256;
                 if (kScl) {
-                    bulk_g2s(st + kStageScl + m * 32, a.xs + soff[m], 32, bar);
+                    bulk_g2s(st + kStageScl + m * 32, xs + soff[m], 32, bar);
                     soff[m] += 8;
                 }
             }
         }
         r.issued++;
-        if (--left == 0) grab(a, sc);
+        if (--left == 0) grab<FUSED>(a, b, sc, ready, ctr);
+    }
+
+    // The ring is empty (every issued stage read): wait, bounded, for a pending unit's batch, then fill the ring from
+    // the stage the warp reads next.  False when the wait timed out.
+    template <bool FUSED>
+    __device__ __forceinline__ bool force(const GemvArgs& a, const GemvArgs& b, const Sched& sc, const int* ready,
+                                          int ctr, Ring& r) {
+        if (FUSED && pending) {
+            const int* c = ready + (pending - 1);
+            const unsigned long long t0 = globaltimer();
+#ifdef B200Q_X_STATS
+            atomicAdd(&g_x_stats[0], 1ull);
+#endif
+            while (ld_acquire(c) < sc.G) {
+                // give up after 2 s, or at once when another wait of this launch has (rows may never be released)
+                if (globaltimer() - t0 > kWaitNs || *(volatile int*)&g_unit_ctr[ctr][6]) {
+                    atomicOr(&g_iq2_error, 8);
+                    atomicExch(&g_unit_ctr[ctr][6], 1);
+                    return false;
+                }
+                __nanosleep(128);
+            }
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+#ifdef B200Q_X_STATS
+            atomicAdd(&g_x_stats[1], globaltimer() - t0);
+#endif
+            pending = 0;
+        }
+#pragma unroll
+        for (int i = 0; i < kStages; i++) {
+            int sl = r.slot + i;
+            if (sl >= kStages) sl -= kStages;
+            issue<FUSED>(a, b, sc, ready, ctr, r.stage_at(sl), r.bar0 + 8u * (uint32_t)sl, r);
+        }
+        return true;
     }
 };
 
@@ -441,15 +577,17 @@ __device__ __forceinline__ float chunk_scale(uint32_t qy, float dh8, float dh8m)
 
 // One unit: its 32 rows (a lane each) over K in chunk order, exactly NT token rows.  Every stage is one super-block,
 // read as four chunk pairs (a loop kept rolled: the unrolled stage outgrows the instruction cache).  Returns false
-// when a ring wait timed out.
+// when a ring wait timed out.  `ready`: a fused launch's up unit adds one to its batch's counter once its rows are
+// stored (nullptr otherwise).
 struct Ids {
     int v[kUnitTok];
 };
 
-template <int NT, int EPI>
-__device__ __forceinline__ bool unit_rows(const GemvArgs& a, int g, const Ids& ids, int lane, Ring& r,
-                                          Producer<EPI != kDots>& pr, const Sched& sc, int nsb) {
-    constexpr bool kScl = EPI != kDots;
+template <int NT, int EPI, bool FUSED, bool kScl>
+__device__ __forceinline__ bool unit_rows(const GemvArgs& a, const GemvArgs& pa, const GemvArgs& pb, int g,
+                                          const Ids& ids, int lane, Ring& r, Producer<kScl>& pr, const Sched& sc,
+                                          const int* ready, int* release, int ctr, int nsb) {
+    static_assert(kScl == (EPI != kDots), "scales travel with every epilogue but the chunk dots");
     const int* id = ids.v;
     const uint32_t lane_c = kTblAddr | ((uint32_t)lane * 4u), lane_s = lane_c | 128u;
     const int row = g * kIq2Tile + lane, nc = a.k >> 5;
@@ -461,6 +599,12 @@ __device__ __forceinline__ bool unit_rows(const GemvArgs& a, int g, const Ids& i
 #pragma unroll
     for (int m = 0; m < NT; m++) acc[m] = 0.f;
     for (int sb = 0; sb < nsb; sb++) {
+        if (FUSED) {
+            // a pending unit reaches the front with nothing in flight: only now may the warp wait for its batch
+            int fok = 1;
+            if (lane == 0 && r.issued == r.consumed) fok = pr.template force<FUSED>(pa, pb, sc, ready, ctr, r);
+            if (!__shfl_sync(0xffffffffu, fok, 0)) return false;
+        }
         const uint32_t st = r.stage(), bar = r.bar();
         const bool ok = mbar_wait(bar, r.par, kWaitNs);
         if (__any_sync(0xffffffffu, !ok)) return false;
@@ -529,7 +673,7 @@ __device__ __forceinline__ bool unit_rows(const GemvArgs& a, int g, const Ids& i
             }
         }
         __syncwarp();   // every lane is done with the stage: lane 0 refills it
-        if (lane == 0) pr.issue(a, sc, st, bar, r);
+        if (lane == 0) pr.template issue<FUSED>(pa, pb, sc, ready, ctr, st, bar, r);
         r.advance();
     }
     if constexpr (EPI != kDots) {
@@ -551,19 +695,278 @@ __device__ __forceinline__ bool unit_rows(const GemvArgs& a, int g, const Ids& i
             }
         }
     }
+    if (FUSED && EPI == kRelu2Q8 && release != nullptr) {
+        // this unit's rows are stored: release them to the down units of its batch (bulk copies read them, so the
+        // proxy fence orders the stores before the async proxy's reads as well)
+        __syncwarp();
+        if (lane == 0) {
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            __threadfence();
+            atomicAdd(release, 1);
+        }
+    }
     return true;
 }
 
-template <int EPI>
-__global__ void __launch_bounds__(kGemvWarps * 32, 1) iq2_gemv_k(GemvArgs a, int nslots) {
+__device__ __forceinline__ void st_release(int* p, int v) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// a bounded wait of one thread until *p >= v; false (and an error bit) when it gave up, after 2 s or at once when
+// another wait of the launch (slot ctr) has given up
+__device__ __forceinline__ bool wait_at_least(const int* p, int v, int ctr) {
+    if (ld_acquire(p) >= v) return true;
+    const unsigned long long t0 = globaltimer();
+    while (ld_acquire(p) < v) {
+        if (globaltimer() - t0 > kWaitNs || *(volatile int*)&g_unit_ctr[ctr][6]) {
+            atomicOr(&g_iq2_error, 32);
+            atomicExch(&g_unit_ctr[ctr][6], 1);
+            return false;
+        }
+        __nanosleep(256);
+    }
+    return true;
+}
+
+// Softmax top-k of one token over bf16 logits, E <= 128 (a lane holds logits lane + 32 j), by a warp: route_token's
+// selection, weights and rounding (larger logit first, ties to the lower index; w = exp(z - max) / the sum over the
+// picked, in pick order), with each pick one redux over packed keys: a bf16 logit maps to 16 bits that order as its
+// value, above 16 bits that order as the reversed index.
+__device__ __forceinline__ void route_softmax_bf16(const __nv_bfloat16* lg, int E, int topk, int t, int lane,
+                                                   int* ridx, float* rw, int* ridx_s) {
+    uint32_t key[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int i = lane + 32 * j;
+        uint32_t b = i < E ? (uint32_t)__bfloat16_as_ushort(lg[(size_t)t * E + i]) : 0u;
+        if (b == 0x8000u) b = 0u;   // -0 ties with +0, as the float compare has it
+        const uint32_t ord = (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+        key[j] = i < E ? (ord << 16) | (0xFFFFu - (uint32_t)i) : 0u;
+    }
+    float mx = 0.f, sum = 0.f, picked = 0.f;
+    int pick_i = 0;
+    for (int kk = 0; kk < topk; kk++) {
+        const uint32_t best = __reduce_max_sync(0xffffffffu, max(max(key[0], key[1]), max(key[2], key[3])));
+        const int bi = (int)(0xFFFFu - (best & 0xFFFFu));
+        const uint32_t o = best >> 16;
+        const uint32_t b = (o & 0x8000u) ? (o & 0x7FFFu) : (~o & 0xFFFFu);
+        const float z = __uint_as_float(b << 16);
+        if (kk == 0) mx = z;   // the first pick is the largest logit
+        const float pv = expf(z - mx);
+        sum += pv;
+        if (lane == kk) { picked = pv; pick_i = bi; }
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            if (lane + 32 * j == bi) key[j] = 0u;
+    }
+    if (lane < topk) {
+        ridx[t * topk + lane] = pick_i;
+        ridx_s[t * topk + lane] = pick_i;
+        rw[t * topk + lane] = picked / sum;
+    }
+}
+
+// sum of a[0 .. n) (shared memory, 16-byte aligned): four words a load, several loads in flight
+__device__ __forceinline__ int smem_sum(const int* a, int n) {
+    const int4* v = reinterpret_cast<const int4*>(a);
+    int s0 = 0, s1 = 0;
+    int j = 0;
+#pragma unroll 4
+    for (; j + 8 <= n; j += 8) {
+        const int4 x = v[j >> 2], y = v[(j >> 2) + 1];
+        s0 += (x.x + x.y) + (x.z + x.w);
+        s1 += (y.x + y.y) + (y.z + y.w);
+    }
+    for (; j < n; j++) s0 += a[j];
+    return s0 + s1;
+}
+
+// #{j < n : a[j] > c, or a[j] == c and j < self} (ties to the lower index): the rank of element `self` of value c in
+// an order by value, largest first (desc) or smallest first (!desc)
+template <bool DESC>
+__device__ __forceinline__ int smem_rank(const int* a, int n, int c, int self) {
+    const int4* v = reinterpret_cast<const int4*>(a);
+    int r = 0;
+    int j = 0;
+    auto before = [&](int x, int idx) { return (DESC ? x > c : x < c) | ((x == c) & (idx < self)); };
+#pragma unroll 4
+    for (; j + 4 <= n; j += 4) {
+        const int4 x = v[j >> 2];
+        r += before(x.x, j) + before(x.y, j + 1) + before(x.z, j + 2) + before(x.w, j + 3);
+    }
+    for (; j < n; j++) r += before(a[j], j);
+    return r;
+}
+
+// The layer's grouping and GEMV schedule from the routing in shared memory, every thread of the CTA, each output by
+// a direct count (the arrays are small): counts by expert (slot E: the shared expert's `extra` rows); offsets; the
+// ids of each slot in increasing pair order (group_pairs' order); the slots by count, largest first, ties to the lower
+// index (iq2_schedule_slots' order) with the exclusive prefix of their batches; and the down phase's batch order of
+// iq2_schedule_batches.  tmp: kLayerIds ints.  All arrays 16-byte aligned.
+__device__ void layer_schedule(const int* ridx_s, int pairs, int E, int extra, int G, int W, int* s_cnt, int* s_offs,
+                               int* s_ord, int* s_order, int* s_bpre, int* s_dord, int* tmp) {
+    const int tid = threadIdx.x, nth = blockDim.x;
+    const int nslots = E + (extra ? 1 : 0);
+    for (int i = tid; i < E; i += nth) s_cnt[i] = 0;
+    __syncthreads();
+    for (int p = tid; p < pairs; p += nth) atomicAdd(&s_cnt[ridx_s[p]], 1);
+    if (tid == 0 && extra) s_cnt[E] = extra;
+    __syncthreads();
+    XTRACE(11);
+    for (int e = tid; e <= nslots; e += nth) s_offs[e] = smem_sum(s_cnt, e);
+    for (int s = tid; s < nslots; s += nth) s_order[smem_rank<true>(s_cnt, nslots, s_cnt[s], s)] = s;
+    __syncthreads();
+    XTRACE(12);
+    for (int p = tid; p < pairs; p += nth) {
+        const int e = ridx_s[p];
+        int r = 0;
+#pragma unroll 8
+        for (int q = 0; q < p; q++) r += ridx_s[q] == e;
+        s_ord[s_offs[e] + r] = p;
+    }
+    for (int i = tid; i < extra; i += nth) s_ord[pairs + i] = pairs + i;
+    for (int i = tid; i < nslots; i += nth) tmp[i] = (s_cnt[s_order[i]] + kIq2UnitTok - 1) / kIq2UnitTok;
+    __syncthreads();
+    XTRACE(14);
+    for (int i = tid; i <= nslots; i += nth) s_bpre[i] = smem_sum(tmp, i);
+    __syncthreads();
+    XTRACE(15);
+    const int nb = s_bpre[nslots];
+    // each batch's key: first-wave batches (all up units numbered below W) before the rest, fewer tokens first
+    for (int i = tid; i < nslots; i += nth) {
+        const int c = s_cnt[s_order[i]];
+        for (int bidx = s_bpre[i]; bidx < s_bpre[i + 1]; bidx++) {
+            const int ntok = min(kIq2UnitTok, c - kIq2UnitTok * (bidx - s_bpre[i]));
+            tmp[bidx] = ((bidx + 1) * G - 1 >= W ? 4 : 0) + ntok;
+        }
+    }
+    __syncthreads();
+    for (int bidx = tid; bidx < nb; bidx += nth) s_dord[smem_rank<false>(tmp, nb, tmp[bidx], bidx)] = bidx;
+    __syncthreads();
+}
+
+// The layer's prologue, every thread of the CTA.  After the wait for the preceding launch, the CTA quantises its
+// share of x to int8 rows (a warp per 32-group) and counts itself done; then it routes every token, groups the pairs
+// by expert and computes the GEMVs' schedule on its own, into shared memory (every CTA gets the same bytes; only CTA 0
+// writes the routing to the caller's buffers); then it waits (bounded) until every CTA's share of x is written.
+// Scratch: the ring stages, unused until the units start.  False when the wait gave up: the CTA takes no units.
+__device__ bool layer_prologue(const LayerArgs& L, const GemvArgs& a, int nslots, int* scr, int ctr, int* s_cnt,
+                               int* s_order, int* s_bpre, int* s_offs, int* s_ord, int* s_dord) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    XTRACE(1);
+    pdl_wait();
+    XTRACE(2);
+    // route (a warp a token) and quantise this CTA's share of x (a warp a 32-group) at once: with fewer tokens than
+    // warps, the quantising warps are those without a token
+    int* ridx_s = scr;                 // kLayerIds: the routing
+    int* place_s = ridx_s + kLayerIds; // kLayerIds: the schedule's scratch
+    float* rw_s = reinterpret_cast<float*>(place_s + kLayerIds);   // kLayerIds: the routing of CTAs other than 0
+    const int pairs = L.T * L.topk;
+    int* ridx_o = blockIdx.x == 0 ? L.ridx : reinterpret_cast<int*>(rw_s);   // CTA 0 writes the caller's buffers
+    float* rw_o = blockIdx.x == 0 ? L.rw : rw_s;   // (the others write a scratch nobody reads)
+    const int groups = L.H >> 5, ng = L.T * groups;
+    const int qw0 = L.T < nw ? L.T : 0, nqw = nw - qw0;   // the quantising warps
+    if (warp >= qw0)
+        for (int gw = (int)blockIdx.x * nqw + (warp - qw0); gw < ng; gw += (int)gridDim.x * nqw) {
+            const int r = gw / groups, g = gw - r * groups;
+            const float v = load_act(L.x, B200Q_BF16, (size_t)r * L.H + g * 32 + lane);
+            quant_group(v, lane, const_cast<int8_t*>(a.xq) + (size_t)r * L.H + g * 32,
+                        const_cast<float*>(a.xs) + (size_t)r * groups + g);
+        }
+    for (int t = warp; t < L.T; t += nw) {
+        if (L.route == B200Q_ROUTE_SOFTMAX && L.E <= 128)
+            route_softmax_bf16(reinterpret_cast<const __nv_bfloat16*>(L.logits), L.E, L.topk, t, lane, ridx_o, rw_o,
+                               ridx_s);
+        else if (L.E <= 128) route_token<4>(L.logits, B200Q_BF16, L.E, L.bias, L.E, L.topk, L.route, L.scale, t, lane,
+                                            ridx_o, rw_o, ridx_s);
+        else route_token<16>(L.logits, B200Q_BF16, L.E, L.bias, L.E, L.topk, L.route, L.scale, t, lane, ridx_o, rw_o,
+                             ridx_s);
+    }
+    __syncthreads();
+    if (tid == 0) {   // this CTA's share of x is written
+        __threadfence();
+        atomicAdd(&g_unit_ctr[ctr][4], 1);
+    }
+    XTRACE(10);
+    layer_schedule(ridx_s, pairs, L.E, L.extra, a.n >> 5, (int)gridDim.x * kGemvWarps, s_cnt, s_offs, s_ord, s_order,
+                   s_bpre, s_dord, place_s);
+    XTRACE(13);
+    if (tid == 0) {
+        const bool ok = wait_at_least(&g_unit_ctr[ctr][4], (int)gridDim.x, ctr);
+        asm volatile("fence.proxy.async.global;" ::: "memory");   // x's rows are read by bulk copies
+        scr[0] = ok ? 1 : 0;
+    }
+    __syncthreads();
+    XTRACE(5);
+    const bool ok = scr[0] != 0;
+    __syncthreads();
+    return ok;
+}
+
+// The layer's epilogue: once every CTA is done with its units (a bounded count), this CTA's share of
+// out[t] = sum_k rw[t][k] mo[t * topk + k] (+ the shared expert's row), in combine_k's order.
+__device__ void layer_epilogue(const LayerArgs& L, const GemvArgs& b, int ctr) {
+    const int tid = threadIdx.x;
+    __syncthreads();
+    XTRACE(7);
+    if (tid == 0) {
+        __threadfence();
+        atomicAdd(&g_unit_ctr[ctr][5], 1);
+        wait_at_least(&g_unit_ctr[ctr][5], (int)gridDim.x, ctr);
+    }
+    __syncthreads();
+    XTRACE(8);
+    const int h4n = L.H >> 2, total = L.T * h4n, topk = L.topk;
+    const float* mo = b.y;
+    for (int i = (int)blockIdx.x + (int)gridDim.x * tid; i < total; i += (int)gridDim.x * blockDim.x) {   // every CTA a share
+        const int t = i / h4n, h4 = i - t * h4n;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        float wk[16];
+        float4 v[16];
+#pragma unroll
+        for (int kk = 0; kk < 16; kk++)   // every load issued before the sums (topk <= 16)
+            if (kk < topk) {
+                wk[kk] = __ldcg(L.rw + t * topk + kk);
+                v[kk] = __ldcg(reinterpret_cast<const float4*>(mo + ((size_t)t * topk + kk) * L.H) + h4);
+            }
+#pragma unroll
+        for (int kk = 0; kk < 16; kk++)
+            if (kk < topk) {
+                acc.x = fmaf(wk[kk], v[kk].x, acc.x); acc.y = fmaf(wk[kk], v[kk].y, acc.y);
+                acc.z = fmaf(wk[kk], v[kk].z, acc.z); acc.w = fmaf(wk[kk], v[kk].w, acc.w);
+            }
+        if (L.extra) {
+            const float4 sv = __ldcg(reinterpret_cast<const float4*>(mo + ((size_t)L.T * topk + t) * L.H) + h4);
+            acc.x += sv.x; acc.y += sv.y; acc.z += sv.z; acc.w += sv.w;
+        }
+        if (L.out_dtype == B200Q_BF16) {
+            __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(L.out) + (size_t)t * L.H) + 2 * h4;
+            o[0] = __floats2bfloat162_rn(acc.x, acc.y);
+            o[1] = __floats2bfloat162_rn(acc.z, acc.w);
+        } else {
+            reinterpret_cast<float4*>(reinterpret_cast<float*>(L.out) + (size_t)t * L.H)[h4] = acc;
+        }
+    }
+}
+
+// One launch: the units of one phase (EPI), or a fused up (kRelu2Q8, args a) + down (kStore, args b) pair over the
+// same slots, whose schedule the fused form requires (a.sched); LAYER: the whole decode layer around the fused pair.
+template <int EPI, bool FUSED, bool LAYER>
+__device__ __forceinline__ void gemv_body(const GemvArgs& a, const GemvArgs& b, int* ready, int nslots,
+                                          const LayerArgs& L) {
+    static_assert(!FUSED || EPI == kRelu2Q8, "a fused launch is up (relu^2 + int8 rows) then down");
+    static_assert(!LAYER || FUSED, "the layer runs the fused projections");
     extern __shared__ __align__(128) unsigned char dyn[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // the layout around the table at kTblAddr (see kTblAddr): barriers, counts, prefix, stages below; stages above
     const uint32_t base = (uint32_t)__cvta_generic_to_shared(dyn);
     int* s_cnt = reinterpret_cast<int*>(dyn + kNumStages * 8);
     int* s_order = s_cnt + kMaxSlots;
-    int* s_upre = s_order + kMaxSlots;
-    int* s_queue = s_upre + kMaxSlots + 1;
+    int* s_bpre = s_order + kMaxSlots;
+    int* s_queue = s_bpre + kMaxSlots + 1;
+    int* s_offs = s_queue + kGemvWarps * kQueue * kQEntry;   // the one-launch layer's schedule
+    int* s_ord = s_offs + kLayerSlots + 1;
+    int* s_dord = s_ord + kLayerIds;
     const uint32_t a0 = (base + kHdrBytes + 15u) & ~15u;
     int nA = a0 <= kTblAddr ? (int)((kTblAddr - a0) / kStageBytes) : 0;
     if (nA > kNumStages) nA = kNumStages;
@@ -585,49 +988,68 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) iq2_gemv_k(GemvArgs a, int
         for (int i = 0; i < kStages; i++) mbar_init(r.bar0 + 8u * (uint32_t)i, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    XTRACE(0);
     build_table(reinterpret_cast<uint32_t*>(dyn + (kTblAddr - base)));
-    const uint32_t kc = (base + (uint32_t)((const unsigned char*)(s_queue + kGemvWarps * kQueue * kQEntry) - dyn) + 7u) & ~7u;
+    const uint32_t kc = (base + (uint32_t)((const unsigned char*)(s_dord + kLayerIds) - dyn) + 7u) & ~7u;
     if (tid == 0) asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(kc), "r"(0xF82B1908u), "r"(0x0000D5E7u) : "memory");
+    bool layer_ok = true;
+    if constexpr (LAYER) {
+        ready = &g_layer_ready[a.ctr][0];
+        layer_ok = layer_prologue(L, a, nslots, reinterpret_cast<int*>(dyn + (2u * kTblAddr - base)), a.ctr, s_cnt,
+                                  s_order, s_bpre, s_offs, s_ord, s_dord);
+    }
     // With a schedule whose inputs an earlier launch wrote, the schedule and each warp's first unit are taken while
     // the preceding launch still runs; only the bulk copies wait for it.
-    const bool early = a.sched != nullptr && a.sched_early;
-    if (!early) pdl_wait();
-    const int G = a.n / kIq2Tile, nsb = a.k >> 8;
-    for (int s = tid; s < nslots; s += blockDim.x) {
-        int cnt = a.counts ? __ldcg(a.counts + s) : a.dense_rows;
-        if (slot_weights(a, s) == nullptr) cnt = 0;
-        s_cnt[s] = cnt;
-    }
-    if (a.sched) {
+    const bool early = !FUSED && a.sched != nullptr && a.sched_early;
+    if (!early && !LAYER) pdl_wait();
+    if (!LAYER)
+        for (int s = tid; s < nslots; s += blockDim.x) {
+            int cnt = a.counts ? __ldcg(a.counts + s) : a.dense_rows;
+            if (slot_weights(a, s) == nullptr) cnt = 0;
+            s_cnt[s] = cnt;
+        }
+    if (LAYER) {
+        // the prologue computed the schedule in shared memory
+    } else if (a.sched) {
         for (int i = tid; i <= nslots; i += blockDim.x) {
             if (i < nslots) s_order[i] = __ldcg(a.sched + i);
-            s_upre[i] = __ldcg(a.sched + nslots + i);
+            s_bpre[i] = __ldcg(a.sched + nslots + i);
         }
     } else {
         __syncthreads();
-        iq2_schedule_slots(s_cnt, nslots, s_order, s_upre, s_order);
+        iq2_schedule_slots(s_cnt, nslots, s_order, s_bpre, s_order);
     }
-    __syncthreads();
-    for (int i = tid; i <= nslots; i += blockDim.x) s_upre[i] *= G;   // batches -> units (batch, row group)
     __syncthreads();
     Sched sc;
     sc.cnt = s_cnt;
     sc.order = s_order;
-    sc.upre = s_upre;
+    sc.bpre = s_bpre;
     sc.nslots = nslots;
-    sc.G = G;
-    sc.U = s_upre[nslots];
+    sc.G = a.n / kIq2Tile;
+    sc.U = s_bpre[nslots] * sc.G;
+    sc.G2 = FUSED ? b.n / kIq2Tile : 0;
+    sc.U2 = FUSED ? s_bpre[nslots] * sc.G2 : 0;
+    sc.dorder = LAYER ? s_dord : a.sched + 2 * nslots + 1;
+    sc.offs = LAYER ? s_offs : nullptr;
+    sc.ord = LAYER ? s_ord : nullptr;
+    if (!layer_ok) sc.U = sc.U2 = 0;   // a prologue wait gave up: no units (the error bit is set)
     sc.kc = kc;
-    Producer<EPI != kDots> pr;
+    const int ctr = a.ctr;
+    constexpr bool kScl = EPI != kDots;
+    Producer<kScl> pr;
     pr.queue = s_queue + warp * kQueue * kQEntry;
     pr.pn = 0;
     pr.left = 0;
-    if (lane == 0) pr.grab(a, sc);
+    pr.pending = 0;
+    XTRACE(6);
+    if (lane == 0) pr.template grab<FUSED>(a, b, sc, ready, ctr);
     if (early) pdl_wait();
     if (lane == 0) {
 #pragma unroll
-        for (int i = 0; i < kStages; i++) pr.issue(a, sc, r.st[i], r.bar0 + 8u * (uint32_t)i, r);
+        for (int i = 0; i < kStages; i++)
+            pr.template issue<FUSED>(a, b, sc, ready, ctr, r.st[i], r.bar0 + 8u * (uint32_t)i, r);
     }
+    const int nsb = a.k >> 8, nsb2 = FUSED ? b.k >> 8 : 0;
     bool healthy = true;
     for (int cn = 0; healthy; cn++) {
         __syncwarp();   // lane 0's queue writes are visible to the warp
@@ -635,14 +1057,27 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) iq2_gemv_k(GemvArgs a, int
         const int g = e[0];
         if (g < 0) break;
         const int nt = e[1];
+        const int ph = e[2] & 1;
+        int* rdy = FUSED ? ready + (e[2] >> 1) : nullptr;
         Ids id;
 #pragma unroll
-        for (int m = 0; m < kUnitTok; m++) id.v[m] = e[2 + m];
-        static_assert(kUnitTok >= 2 && kUnitTok <= 4, "one code path per token count 1 .. kUnitTok");
-        if (nt == 1) healthy = unit_rows<1, EPI>(a, g, id, lane, r, pr, sc, nsb);
-        else if (nt == 2 || kUnitTok == 2) healthy = unit_rows<2, EPI>(a, g, id, lane, r, pr, sc, nsb);
-        else if (nt == 3 || kUnitTok == 3) healthy = unit_rows<(kUnitTok < 3 ? 2 : 3), EPI>(a, g, id, lane, r, pr, sc, nsb);
-        else healthy = unit_rows<kUnitTok, EPI>(a, g, id, lane, r, pr, sc, nsb);
+        for (int m = 0; m < kUnitTok; m++) id.v[m] = e[3 + m];
+        static_assert(kUnitTok == 3, "one code path per token count 1 .. 3");
+        bool down_unit = false;
+        if constexpr (FUSED) down_unit = ph != 0;
+        if constexpr (FUSED) {
+            if (down_unit) {
+                if (nt == 1) healthy = unit_rows<1, kStore, FUSED, kScl>(b, a, b, g, id, lane, r, pr, sc, ready, nullptr, ctr, nsb2);
+                else if (nt == 2) healthy = unit_rows<2, kStore, FUSED, kScl>(b, a, b, g, id, lane, r, pr, sc, ready, nullptr, ctr, nsb2);
+                else healthy = unit_rows<3, kStore, FUSED, kScl>(b, a, b, g, id, lane, r, pr, sc, ready, nullptr, ctr, nsb2);
+                continue;
+            }
+        }
+        {
+            if (nt == 1) healthy = unit_rows<1, EPI, FUSED, kScl>(a, a, b, g, id, lane, r, pr, sc, ready, rdy, ctr, nsb);
+            else if (nt == 2) healthy = unit_rows<2, EPI, FUSED, kScl>(a, a, b, g, id, lane, r, pr, sc, ready, rdy, ctr, nsb);
+            else healthy = unit_rows<3, EPI, FUSED, kScl>(a, a, b, g, id, lane, r, pr, sc, ready, rdy, ctr, nsb);
+        }
     }
     if (!healthy) {
         // a stage never filled: flag it, and let this warp's copies in flight land before the CTA's memory goes away
@@ -653,17 +1088,36 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) iq2_gemv_k(GemvArgs a, int
         }
         __syncwarp();
     }
-    // the last CTA out resets this launch slot's counters for the slot's next launch
+    if constexpr (LAYER) layer_epilogue(L, b, ctr);
+    XTRACE(9);
+    // the last CTA out resets this launch slot's counters (and the layer's readiness counters) for its next launch
     __syncthreads();
     if (tid == 0) {
         __threadfence();
-        if (atomicAdd(&g_unit_ctr[a.ctr][1], 1) == (int)gridDim.x - 1) {
-            g_unit_ctr[a.ctr][0] = 0;
-            g_unit_ctr[a.ctr][1] = 0;
-            __threadfence();
+        const bool last = atomicAdd(&g_unit_ctr[ctr][1], 1) == (int)gridDim.x - 1;
+        if (last) {
+#pragma unroll
+            for (int i = 0; i < 8; i++) g_unit_ctr[ctr][i] = 0;
         }
+        s_queue[0] = last;
+    }
+    if constexpr (LAYER) {
+        __syncthreads();
+        if (s_queue[0])
+            for (int i = tid; i < kLayerIds; i += blockDim.x) g_layer_ready[ctr][i] = 0;
     }
     pdl_trigger();
+}
+
+template <int EPI, bool FUSED>
+__global__ void __launch_bounds__(kGemvWarps * 32, 1) iq2_gemv_k(GemvArgs a, GemvArgs b, int* ready, int nslots) {
+    const LayerArgs none = {};
+    gemv_body<EPI, FUSED, false>(a, b, ready, nslots, none);
+}
+
+__global__ void __launch_bounds__(kGemvWarps * 32, 1) decode_layer_k(GemvArgs a, GemvArgs b, int* ready, int nslots,
+                                                                     LayerArgs L) {
+    gemv_body<kRelu2Q8, true, true>(a, b, ready, nslots, L);
 }
 
 static int num_sms() {
@@ -679,30 +1133,63 @@ static int num_sms() {
     return sms[dev];
 }
 
-template <int EPI>
-static cudaError_t launch_gemv_e(const GemvArgs& a, int nslots, cudaStream_t s) {
+template <int EPI, bool FUSED>
+static cudaError_t launch_gemv_e(const GemvArgs& a, const GemvArgs& b, int* ready, int nslots, cudaStream_t s) {
     static bool opted = false;
     if (!opted) {
-        cudaError_t e = cudaFuncSetAttribute(iq2_gemv_k<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvSmem);
+        cudaError_t e = cudaFuncSetAttribute(iq2_gemv_k<EPI, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)kGemvSmem);
         if (e != cudaSuccess) return e;
         opted = true;
     }
-    return launch(iq2_gemv_k<EPI>, dim3(num_sms()), dim3(kGemvWarps * 32), kGemvSmem, s, a, nslots);
+    return launch(iq2_gemv_k<EPI, FUSED>, dim3(num_sms()), dim3(kGemvWarps * 32), kGemvSmem, s, a, b, ready, nslots);
+}
+
+// launches take the counter slots in turn: kUnitCtrs launches can be in flight (on any streams) before a slot is
+// reused, and a slot is back to zero when its launch ends
+static int next_ctr() {
+    static std::atomic<unsigned> next_slot{0};
+    return (int)(next_slot.fetch_add(1u) % kUnitCtrs);
 }
 
 cudaError_t launch_iq2_gemv(const GemvArgs& a0, int nslots, int /*maxcnt*/, int epi, cudaStream_t s) {
     if (nslots <= 0 || nslots > kMaxSlots) return cudaErrorInvalidValue;
-    // launches take the counter slots in turn: kUnitCtrs launches can be in flight (on any streams) before a slot is
-    // reused, and a slot is back to zero when its launch ends
-    static std::atomic<unsigned> next_slot{0};
     GemvArgs a = a0;
-    a.ctr = (int)(next_slot.fetch_add(1u) % kUnitCtrs);
+    a.ctr = next_ctr();
     switch (epi) {
-        case kStore: return launch_gemv_e<kStore>(a, nslots, s);
-        case kRelu2: return launch_gemv_e<kRelu2>(a, nslots, s);
-        case kRelu2Q8: return launch_gemv_e<kRelu2Q8>(a, nslots, s);
-        default: return launch_gemv_e<kDots>(a, nslots, s);
+        case kStore: return launch_gemv_e<kStore, false>(a, a, nullptr, nslots, s);
+        case kRelu2: return launch_gemv_e<kRelu2, false>(a, a, nullptr, nslots, s);
+        case kRelu2Q8: return launch_gemv_e<kRelu2Q8, false>(a, a, nullptr, nslots, s);
+        default: return launch_gemv_e<kDots, false>(a, a, nullptr, nslots, s);
     }
+}
+
+int iq2_first_wave() { return num_sms() * kGemvWarps; }
+
+bool layer_fits(int T, int E, int topk, bool shared) {
+    return T >= 1 && T <= 64 && E >= 1 && E + 1 <= kLayerSlots && T * topk + (shared ? T : 0) <= kLayerIds;
+}
+
+cudaError_t launch_decode_layer(const GemvArgs& up, const GemvArgs& down, int* ready, int nslots, const LayerArgs& L,
+                                cudaStream_t s) {
+    (void)ready;   // the launch keeps its readiness counters by launch slot
+    if (!layer_fits(L.T, L.E, L.topk, L.extra > 0) || nslots != L.E + (L.extra > 0 ? 1 : 0)) return cudaErrorInvalidValue;
+    static bool opted = false;
+    if (!opted) {
+        cudaError_t e = cudaFuncSetAttribute(decode_layer_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvSmem);
+        if (e != cudaSuccess) return e;
+        opted = true;
+    }
+    GemvArgs a = up;
+    a.ctr = next_ctr();
+    return launch(decode_layer_k, dim3(num_sms()), dim3(kGemvWarps * 32), kGemvSmem, s, a, down, ready, nslots, L);
+}
+
+cudaError_t launch_iq2_updown(const GemvArgs& up, const GemvArgs& down, int* ready, int nslots, cudaStream_t s) {
+    if (nslots <= 0 || nslots > kMaxSlots || up.sched == nullptr || ready == nullptr) return cudaErrorInvalidValue;
+    GemvArgs a = up;
+    a.ctr = next_ctr();
+    return launch_gemv_e<kRelu2Q8, true>(a, down, ready, nslots, s);
 }
 
 cudaError_t launch_iq2_pack_split(const uint8_t* raw, uint8_t* qs, uint8_t* dq, int64_t n, int k, cudaStream_t s) {
@@ -746,6 +1233,20 @@ int b200q_synth_iq2(uint64_t seed, int64_t nblocks, void* out, void* stream) {
     synth_iq2_k<<<(unsigned)((nblocks + 255) / 256), 256, 0, (cudaStream_t)stream>>>(seed, nblocks, (uint8_t*)out);
     return launched();
 }
+
+#ifdef B200Q_X_STATS
+extern "C" int b200q_x_stats(unsigned long long* out, int clear) {
+    cudaMemcpyFromSymbol(out, g_x_stats, sizeof(g_x_stats));
+    if (clear) { unsigned long long z[4] = {0, 0, 0, 0}; cudaMemcpyToSymbol(g_x_stats, z, sizeof(z)); }
+    return 0;
+}
+#endif
+
+#ifdef B200Q_X_TRACE
+extern "C" int b200q_x_trace(unsigned long long* out) {
+    return (int)cudaMemcpyFromSymbol(out, g_x_trace, sizeof(g_x_trace));
+}
+#endif
 
 int b200q_device_error(int clear) {
     int v = 0;

@@ -85,9 +85,101 @@ __device__ inline void iq2_schedule_slots(const int* counts, int nslots, int* or
     }
 }
 
+// The slot position holding batch bidx: the last i with bpre[i] <= bidx (slots without batches share their bpre with
+// the next slot, so the last such i is the slot that holds the batch).
+__device__ inline int iq2_batch_slot(const int* bpre, int nslots, int bidx) {
+    int lo = 0, hi = nslots;
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (bpre[mid] <= bidx) lo = mid;
+        else hi = mid;
+    }
+    return lo;
+}
+
+// The fused launch's order of the down phase's batches (launch_iq2_updown).  A batch's down units can start once all
+// its up units are done, and batches are ordered by when that is expected: first those whose up units all fall in the
+// launch's first wave (unit number < W: every warp starts on one unit), then the rest, each group by token count,
+// fewest (the shortest up units) first, ties by batch index.  Batch bidx's up units are bidx * G .. bidx * G + G - 1.
+// All threads of the CTA call it; cnt (by slot), order and bpre must be readable by all of them (shared memory);
+// tmp: 8 * ceil(batches / 32) ints of shared memory.  Writes dorder[0 .. batches).
+__device__ inline void iq2_schedule_batches(const int* cnt, const int* order, const int* bpre, int nslots, int G, int W,
+                                            int* dorder, int* tmp) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int nb = bpre[nslots], nch = (nb + 31) >> 5;
+    auto key_of = [&](int bidx) {
+        if (bidx >= nb) return 8;
+        const int i = iq2_batch_slot(bpre, nslots, bidx);
+        const int nt = min(kIq2UnitTok, cnt[order[i]] - kIq2UnitTok * (bidx - bpre[i]));
+        return ((bidx + 1) * G - 1 >= W ? 4 : 0) + nt;
+    };
+    // per chunk of 32 batches, the number of each key
+    for (int c = warp; c < nch; c += nw) {
+        const int key = key_of(32 * c + lane);
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int m = __popc(__ballot_sync(0xffffffffu, key == k));
+            if (lane == k) tmp[c * 8 + k] = m;
+        }
+    }
+    __syncthreads();
+    // each key's start in the order, and each chunk's start within its key
+    if (warp == 0) {
+        int run = 0;
+        if (lane < 8)
+            for (int c = 0; c < nch; c++) {
+                const int v = tmp[c * 8 + lane];
+                tmp[c * 8 + lane] = run;
+                run += v;
+            }
+        int incl = lane < 8 ? run : 0;
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        const int base = incl - (lane < 8 ? run : 0);
+        if (lane < 8)
+            for (int c = 0; c < nch; c++) tmp[c * 8 + lane] += base;
+    }
+    __syncthreads();
+    for (int c = warp; c < nch; c += nw) {
+        const int bidx = 32 * c + lane, key = key_of(bidx);
+        const unsigned m = __match_any_sync(0xffffffffu, key);
+        if (key < 8) dorder[tmp[c * 8 + key] + __popc(m & ((1u << lane) - 1u))] = bidx;
+    }
+}
 
 // epi: 0 store, 1 relu^2, 2 relu^2 + int8 per 32, 3 chunk dots.  maxcnt bounds a slot's ids (the staging size).
 cudaError_t launch_iq2_gemv(const GemvArgs& a, int nslots, int maxcnt, int epi, cudaStream_t s);
+// One launch of both expert projections over the same slots: up (a: relu^2 + int8 rows into a.aq / a.as, which must be
+// down's xq / xs) then down (b).  a.sched is required; ready: one int per batch of the schedule (at least its
+// pairs + extra), zero when the launch starts.
+// The decode layer in one launch (b200q_moe_decode): its router, grouping and schedule (done by the first CTA to
+// arrive), the int8 rows of x (every CTA a share), the fused expert projections, and the combine with the router
+// weights and the shared expert (every CTA a share, once every CTA is done with its units).
+struct LayerArgs {
+    const void* x;           // [T][H] bf16
+    const void* logits;      // [T][E] bf16
+    const float* bias;
+    float scale;
+    int T, H, E, topk, route, extra;   // extra: T with a shared expert (slot E), else 0
+    int* ridx;               // [T * topk] routing results
+    float* rw;
+    void* out;               // [T][H]
+    int out_dtype;
+};
+
+// a.sched must hold, after its 2 nslots + 1 ints, the down phase's batch order (iq2_schedule_batches with
+// W = iq2_first_wave()).
+cudaError_t launch_iq2_updown(const GemvArgs& up, const GemvArgs& down, int* ready, int nslots, cudaStream_t s);
+// the unit numbers a launch's warps start on (one a warp): the W of iq2_schedule_batches
+int iq2_first_wave();
+// The whole decode layer as one launch (see LayerArgs): up's xq / xs and down's y are written by the launch itself
+// (its schedule stays in shared memory); only for layers that layer_fits.
+bool layer_fits(int T, int E, int topk, bool shared);
+cudaError_t launch_decode_layer(const GemvArgs& up, const GemvArgs& down, int* ready, int nslots, const LayerArgs& L,
+                                cudaStream_t s);
 // ggml blocks [n][k/256][66] -> the split rt32 layout: qs [units][2048], dq [units][64] (units = n/32 * k/256)
 cudaError_t launch_iq2_pack_split(const uint8_t* raw, uint8_t* qs, uint8_t* dq, int64_t n, int k, cudaStream_t s);
 bool iq2_shape_ok(int64_t n, int k);

@@ -1,6 +1,7 @@
 // The MoE layer around the expert GEMVs: int8 rows of the activations, the router, the expert-sorted grouping,
 // the weighted combine, and the decode layer that chains them.
 #include "iq2.cuh"
+#include "moe.cuh"
 
 #include <cstdlib>
 
@@ -22,22 +23,6 @@ bool pdl_enabled() {
     return on;
 }
 
-__device__ __forceinline__ float load_act(const void* p, int dtype, size_t i) {
-    return dtype == B200Q_BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]) : reinterpret_cast<const float*>(p)[i];
-}
-
-// ---------------------------------------------------------------------------------------------------------
-// quant_rows_k's arithmetic (bolt_kernels.cu:347-360), a warp per 32-group: s = amax/127, q = rn(x * 127/amax)
-// ---------------------------------------------------------------------------------------------------------
-__device__ __forceinline__ void quant_group(float v, int lane, int8_t* q, float* s) {
-    float am = fabsf(v);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-    const float inv = am > 0.f ? 127.f / am : 0.f;
-    q[lane] = (int8_t)__float2int_rn(v * inv);
-    if (lane == 0) *s = am / 127.f;
-}
-
 __global__ void quant_rows_k(const void* __restrict__ x, int dtype, int ldx, int8_t* __restrict__ q, int ldq,
                              float* __restrict__ s, int lds, int rows, int k) {
     pdl_wait();
@@ -52,70 +37,6 @@ __global__ void quant_rows_k(const void* __restrict__ x, int dtype, int ldx, int
     pdl_trigger();
 }
 
-// ---------------------------------------------------------------------------------------------------------
-// router: a warp per token (route_k's shape, bolt_kernels.cu:1655-1712), E <= 512 so a lane holds 16 logits.
-// Top-k by repeated warp argmax, ties to the lower index.
-//   softmax: w_i = exp(z_i - max) / sum over the picked of exp(z_j - max)   (softmax, top-k, renormalised)
-//   sigmoid: route_k's form: pick by sigmoid(z) + bias, w = sigmoid / (1e-20 + sum of picked) * scale
-// ---------------------------------------------------------------------------------------------------------
-template <int NJ>   // logits a lane holds: E <= 32 NJ
-__device__ void route_token(const void* logits, int dtype, int ldl, const float* bias, int E, int topk, int mode,
-                            float scale, int t, int lane, int* ridx, float* rw, int* ridx_s) {
-    float val[NJ], key[NJ];
-    float mx = -3.0e38f;
-#pragma unroll
-    for (int j = 0; j < NJ; j++) {
-        const int i = lane + 32 * j;
-        if (i < E) {
-            const float z = load_act(logits, dtype, (size_t)t * ldl + i);
-            if (mode == B200Q_ROUTE_SOFTMAX) {
-                val[j] = z;
-                key[j] = z;
-            } else {
-                val[j] = 1.f / (1.f + expf(-z));
-                key[j] = val[j] + (bias ? bias[i] : 0.f);
-            }
-            mx = fmaxf(mx, z);
-        } else {
-            val[j] = 0.f;
-            key[j] = -3.0e38f;
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float picked = 0.f, sum = mode == B200Q_ROUTE_SOFTMAX ? 0.f : 1e-20f;
-    int pick_i = 0;
-    for (int kk = 0; kk < topk; kk++) {
-        float bv = -3.4e38f;
-        int bi = 0x7fffffff;
-#pragma unroll
-        for (int j = 0; j < NJ; j++) {
-            const int i = lane + 32 * j;
-            if (i < E && key[j] > bv) { bv = key[j]; bi = i; }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-        }
-        float pv = 0.f;
-#pragma unroll
-        for (int j = 0; j < NJ; j++)
-            if (lane + 32 * j == bi) { pv = val[j]; key[j] = -3.4e38f; }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) pv += __shfl_xor_sync(0xffffffffu, pv, o);   // only one lane is non-zero
-        if (mode == B200Q_ROUTE_SOFTMAX) pv = expf(pv - mx);
-        sum += pv;
-        if (lane == kk) { picked = pv; pick_i = bi; }
-    }
-    if (lane < topk) {
-        ridx[t * topk + lane] = pick_i;
-        if (ridx_s) ridx_s[t * topk + lane] = pick_i;
-        rw[t * topk + lane] = mode == B200Q_ROUTE_SOFTMAX ? picked / sum : picked / sum * scale;
-    }
-}
-
 __global__ void route_k(const void* __restrict__ logits, int dtype, int ldl, const float* __restrict__ bias, int T, int E,
                         int topk, int mode, float scale, int* __restrict__ ridx, float* __restrict__ rw) {
     pdl_wait();
@@ -125,69 +46,6 @@ __global__ void route_k(const void* __restrict__ logits, int dtype, int ldl, con
         else route_token<16>(logits, dtype, ldl, bias, E, topk, mode, scale, t, threadIdx.x & 31, ridx, rw, nullptr);
     }
     pdl_trigger();
-}
-
-// ---------------------------------------------------------------------------------------------------------
-// grouping (moe_group_k's counting sort, bolt_kernels.cu:275-325), deterministic: the pairs of expert e in
-// increasing pair order.  One CTA of 512 threads, E <= 512, pairs <= 4096.  extra > 0 appends a slot E with ids
-// pairs .. pairs + extra - 1 (the shared expert over every token).
-//   1. warp 0 walks the pairs 32 at a time in order: match_any finds the lanes of the same expert, a pair's place in
-//      its expert is that expert's running count plus its rank among those lanes, and the lowest such lane adds
-//      their number to the running count;
-//   2. an exclusive scan of the counts (warp shuffles, then the warps' totals) gives the offsets;
-//   3. every pair writes its index to order[offset + place].
-// Shared memory: ridx_s[pairs] (the routing), place_s[pairs], run_s[512], warp_s[16].
-// ---------------------------------------------------------------------------------------------------------
-__device__ void group_pairs(const int* ridx_s, int pairs, int E, int extra, int* counts, int* offsets, int* order,
-                            int* place_s, int* run_s, int* warp_s, int* counts_s = nullptr) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    run_s[tid] = 0;
-    __syncthreads();
-    if (warp == 0) {
-        for (int p0 = 0; p0 < pairs; p0 += 32) {
-            const int p = p0 + lane;
-            const bool valid = p < pairs;
-            const unsigned vm = __ballot_sync(0xffffffffu, valid);
-            if (valid) {
-                const int e = ridx_s[p];
-                const unsigned peers = __match_any_sync(vm, e);
-                const unsigned below = peers & ((1u << lane) - 1u);
-                place_s[p] = run_s[e] + __popc(below);
-                __syncwarp(vm);
-                if (below == 0) run_s[e] += __popc(peers);
-            }
-            __syncwarp();
-        }
-    }
-    __syncthreads();
-    // exclusive scan of run_s[0 .. 512) (zero past E)
-    const int c = tid < E ? run_s[tid] : 0;
-    int incl = c;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-    }
-    if (lane == 31) warp_s[warp] = incl;
-    __syncthreads();
-    int before = 0;
-    for (int w = 0; w < warp; w++) before += warp_s[w];
-    const int start = before + incl - c;
-    if (tid < E) {
-        counts[tid] = c;
-        offsets[tid] = start;
-        if (counts_s) counts_s[tid] = c;   // a shared-memory copy for the caller (slot E: extra)
-    }
-    if (counts_s && tid == 0) counts_s[E] = extra;
-    __syncthreads();
-    run_s[tid] = start;   // reused: the offsets, for the scatter
-    __syncthreads();
-    for (int p = tid; p < pairs; p += blockDim.x) order[run_s[ridx_s[p]] + place_s[p]] = p;
-    if (tid == 0) {
-        offsets[E] = pairs;
-        if (extra > 0) { counts[E] = extra; offsets[E + 1] = pairs + extra; }
-    }
-    for (int i = tid; i < extra; i += blockDim.x) order[pairs + i] = pairs + i;
 }
 
 __global__ void __launch_bounds__(512) group_k(const int* __restrict__ ridx, int pairs, int E, int* __restrict__ counts,
@@ -245,14 +103,16 @@ __global__ void group_scatter_k(const int* __restrict__ ridx, int pairs, const i
 // expert GEMVs' slots (iq2_schedule_slots); the other blocks write the int8 rows of x (a warp per 32-group).
 // ---------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(512) moe_prep_k(const void* __restrict__ x, const void* __restrict__ logits, int T, int H,
-                                                  int E, int topk, int route, const float* __restrict__ bias, float scale,
+                                                  int F, int E, int topk, int route, const float* __restrict__ bias, float scale,
                                                   int extra, int* __restrict__ ridx, float* __restrict__ rw,
                                                   int* __restrict__ counts, int* __restrict__ offsets, int* __restrict__ order,
-                                                  int8_t* __restrict__ xq, float* __restrict__ xs, int* __restrict__ sched) {
+                                                  int8_t* __restrict__ xq, float* __restrict__ xs, int* __restrict__ sched,
+                                                  int* __restrict__ ready, int wave) {
     pdl_wait();
     __shared__ int ridx_s[1024], place_s[1024], run_s[512], warp_s[16], cnt_s[513];   // T * topk <= 64 * 16
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (blockIdx.x == 0) {
+        for (int i = threadIdx.x; i < T * topk + (extra > 0 ? T : 0); i += blockDim.x) ready[i] = 0;
         for (int t = warp; t < T; t += 16) {
             if (E <= 128) route_token<4>(logits, B200Q_BF16, E, bias, E, topk, route, scale, t, lane, ridx, rw, ridx_s);
             else route_token<16>(logits, B200Q_BF16, E, bias, E, topk, route, scale, t, lane, ridx, rw, ridx_s);
@@ -263,6 +123,9 @@ __global__ void __launch_bounds__(512) moe_prep_k(const void* __restrict__ x, co
         const int nsl = E + (extra > 0 ? 1 : 0);
         __syncthreads();
         iq2_schedule_slots(cnt_s, nsl, sched, sched + nsl, ridx_s);
+        __syncthreads();
+        // the fused GEMV's down-phase order of batches (place_s is free after the grouping)
+        iq2_schedule_batches(cnt_s, sched, sched + nsl, nsl, F >> 5, wave, sched + 2 * nsl + 1, place_s);
     } else {
         const int groups = H >> 5;
         const int gw = (blockIdx.x - 1) * 16 + warp;
@@ -284,11 +147,13 @@ __global__ void __launch_bounds__(512) moe_local_prep_k(const void* __restrict__
                                                         const int* __restrict__ lidx, int lidx_stride, int n_local,
                                                         int* __restrict__ counts, int* __restrict__ offsets,
                                                         int* __restrict__ order, int8_t* __restrict__ xq,
-                                                        float* __restrict__ xs, int* __restrict__ sched) {
+                                                        float* __restrict__ xs, int* __restrict__ sched,
+                                                        int* __restrict__ ready, int F, int wave) {
     pdl_wait();
     __shared__ int ridx_s[4096], place_s[4096], run_s[512], warp_s[16], cnt_s[513];   // R <= 4096
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (blockIdx.x == 0) {
+        for (int i = threadIdx.x; i < R; i += blockDim.x) ready[i] = 0;
         for (int i = threadIdx.x; i < R; i += blockDim.x) {
             const int l = lidx[(size_t)i * lidx_stride];
             ridx_s[i] = (l < 0 || l > n_local) ? n_local : l;
@@ -297,6 +162,8 @@ __global__ void __launch_bounds__(512) moe_local_prep_k(const void* __restrict__
         group_pairs(ridx_s, R, n_local + 1, 0, counts, offsets, order, place_s, run_s, warp_s, cnt_s);
         __syncthreads();
         iq2_schedule_slots(cnt_s, n_local, sched, sched + n_local, ridx_s);
+        __syncthreads();
+        iq2_schedule_batches(cnt_s, sched, sched + n_local, n_local, F >> 5, wave, sched + 2 * n_local + 1, place_s);
     } else {
         const int groups = H >> 5;
         const int gw = (blockIdx.x - 1) * 16 + warp;
@@ -347,6 +214,7 @@ struct DecodeWs {
     int* ridx; float* rw; int* counts; int* offsets; int* order;
     int8_t* xq; float* xs; int8_t* aq; float* as; float* mo;
     int* sched;   // the expert GEMVs' slot schedule (2 nslots + 1 ints)
+    int* ready;   // the fused GEMV's readiness counter of each batch (pairs + T ints), zeroed by the prologue
     size_t bytes;
 };
 static size_t al(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -364,13 +232,15 @@ static DecodeWs decode_ws(char* base, int T, int H, int F, int E, int topk) {
     w.aq = (int8_t*)(base + o); o += al(ids * F);
     w.as = (float*)(base + o); o += al(ids * (F / 32) * 4);
     w.mo = (float*)(base + o); o += al(ids * H * 4);
-    w.sched = (int*)(base + o); o += al((size_t)(2 * (E + 1) + 1) * 4);
+    w.sched = (int*)(base + o); o += al(((size_t)(2 * (E + 1) + 1) + ids) * 4);   // + the down phase's batch order
+    w.ready = (int*)(base + o); o += al(ids * 4);
     w.bytes = o;
     return w;
 }
 
 struct ExpertsWs {
     int* counts; int* offsets; int* order; int8_t* xq; float* xs; int8_t* aq; float* as; int* sched;
+    int* ready;   // the fused GEMV's readiness counter of each batch (R ints), zeroed by the prologue
     size_t bytes;
 };
 static ExpertsWs experts_ws(char* base, int R, int H, int F, int n_local) {
@@ -383,7 +253,8 @@ static ExpertsWs experts_ws(char* base, int R, int H, int F, int n_local) {
     w.xs = (float*)(base + o); o += al((size_t)R * (H / 32) * 4);
     w.aq = (int8_t*)(base + o); o += al((size_t)R * F);
     w.as = (float*)(base + o); o += al((size_t)R * (F / 32) * 4);
-    w.sched = (int*)(base + o); o += al((size_t)(2 * n_local + 1) * 4);
+    w.sched = (int*)(base + o); o += al((size_t)(2 * n_local + 1 + R) * 4);   // + the down phase's batch order
+    w.ready = (int*)(base + o); o += al((size_t)R * 4);
     w.bytes = o;
     return w;
 }
@@ -485,21 +356,25 @@ int b200q_moe_experts_decode(const void* rows, int rows_dtype, int ldr, int R, i
     // 1. grouping by local expert, the slot schedule, the int8 rows
     const int qwarps = R * (H / 32);
     launch(moe_local_prep_k, dim3(1 + (qwarps + 15) / 16), dim3(512), 0, s, rows, rows_dtype, ldr, R, H, lidx,
-           lidx_stride, n_local, w.counts, w.offsets, w.order, w.xq, w.xs, w.sched);
+           lidx_stride, n_local, w.counts, w.offsets, w.order, w.xq, w.xs, w.sched, w.ready, F, iq2_first_wave());
     if ((st = launched()) != B200Q_OK) return st;
-    // 2. up with relu^2 and the int8 rows of the result, row id = received row
+    // 2. up with relu^2 and the int8 rows of the result (row id = received row), then down, in one launch
     GemvArgs a = {};
     a.slab = (const uint8_t*)up; a.expert_bytes = iq2_bytes(F, H); a.nslot_routed = n_local; a.n = F; a.k = H;
     a.counts = w.counts; a.offsets = w.offsets; a.order = w.order; a.act_div = 1; a.act_split = 1 << 30;
     a.xq = w.xq; a.xs = w.xs; a.aq = w.aq; a.as = w.as; a.sched = w.sched;
-    if ((st = status_from(launch_iq2_gemv(a, n_local, 16, 2, s))) != B200Q_OK) return st;
-    // 3. down: the prologue's schedule is two launches back, taken before the down GEMV waits for the up GEMV
     GemvArgs b = {};
     b.slab = (const uint8_t*)down; b.expert_bytes = iq2_bytes(H, F); b.nslot_routed = n_local; b.n = H; b.k = F;
     b.counts = w.counts; b.offsets = w.offsets; b.order = w.order; b.act_div = 1; b.act_split = 1 << 30;
     b.xq = w.aq; b.xs = w.as; b.y = (float*)y; b.ldy = ldy; b.y_bf16 = y_dtype == B200Q_BF16;
-    b.sched = w.sched; b.sched_early = 1;
+    b.sched = w.sched;
+#ifdef B200Q_X_NOFUSE
+    if ((st = status_from(launch_iq2_gemv(a, n_local, 16, 2, s))) != B200Q_OK) return st;
+    b.sched_early = 1;
     return status_from(launch_iq2_gemv(b, n_local, 16, 0, s));
+#else
+    return status_from(launch_iq2_updown(a, b, w.ready, n_local, s));
+#endif
 }
 
 size_t b200q_moe_decode_workspace_bytes(int T, int H, int F, int E, int topk) {
@@ -530,10 +405,36 @@ int b200q_moe_decode(const void* x, const void* logits, const void* up, const vo
     };
 
     if ((st = mark(0)) != B200Q_OK) return st;
+#ifndef B200Q_X_NOLAYER
+    if (layer_fits(T, E, topk, extra > 0)) {
+        // the whole layer as one launch: router, grouping and schedule, int8 rows of x, up (relu^2 + int8 rows) and
+        // down over every expert slot and the shared expert, combine
+        GemvArgs a = {};
+        a.slab = (const uint8_t*)up; a.expert_bytes = iq2_bytes(F, H); a.extra_w = (const uint8_t*)shared_up;
+        a.nslot_routed = E; a.n = F; a.k = H; a.counts = w.counts; a.offsets = w.offsets; a.order = w.order;
+        a.act_div = topk; a.act_split = pairs; a.act_base = 0; a.xq = w.xq; a.xs = w.xs; a.aq = w.aq; a.as = w.as;
+        a.sched = w.sched;
+        GemvArgs b = {};
+        b.slab = (const uint8_t*)down; b.expert_bytes = iq2_bytes(H, F); b.extra_w = (const uint8_t*)shared_down;
+        b.nslot_routed = E; b.n = H; b.k = F; b.counts = w.counts; b.offsets = w.offsets; b.order = w.order;
+        b.act_div = 1; b.act_split = 1 << 30; b.xq = w.aq; b.xs = w.as; b.y = w.mo; b.ldy = H; b.sched = w.sched;
+        LayerArgs L = {};
+        L.x = x; L.logits = logits; L.bias = bias; L.scale = scale; L.T = T; L.H = H; L.E = E; L.topk = topk;
+        // the routing goes straight to the caller's buffers when given (no copies after the launch)
+        L.route = route; L.extra = extra; L.ridx = ridx_out ? ridx_out : w.ridx; L.rw = rw_out ? rw_out : w.rw;
+        L.out = out; L.out_dtype = out_dtype;
+        (void)maxcnt;
+        if ((st = status_from(launch_decode_layer(a, b, w.ready, nslots, L, s))) != B200Q_OK) return st;
+        for (int i = 1; i <= 4; i++)
+            if ((st = mark(i)) != B200Q_OK) return st;   // one launch: the stage marks all follow it
+        return B200Q_OK;
+    } else
+#endif
+    {
     // 1. router + grouping (block 0) and the int8 rows of x (the rest)
     const int qwarps = T * (H / 32);
-    launch(moe_prep_k, dim3(1 + (qwarps + 15) / 16), dim3(512), 0, s, x, logits, T, H, E, topk, route, bias, scale, extra,
-           w.ridx, w.rw, w.counts, w.offsets, w.order, w.xq, w.xs, w.sched);
+    launch(moe_prep_k, dim3(1 + (qwarps + 15) / 16), dim3(512), 0, s, x, logits, T, H, F, E, topk, route, bias, scale, extra,
+           w.ridx, w.rw, w.counts, w.offsets, w.order, w.xq, w.xs, w.sched, w.ready, iq2_first_wave());
     if ((st = launched()) != B200Q_OK) return st;
     if ((st = mark(1)) != B200Q_OK) return st;
 
@@ -543,18 +444,24 @@ int b200q_moe_decode(const void* x, const void* logits, const void* up, const vo
     a.nslot_routed = E; a.n = F; a.k = H; a.counts = w.counts; a.offsets = w.offsets; a.order = w.order;
     a.act_div = topk; a.act_split = pairs; a.act_base = 0; a.xq = w.xq; a.xs = w.xs; a.aq = w.aq; a.as = w.as;
     a.sched = w.sched;   // written by the prologue, the launch this one follows: read after the wait
-    if ((st = status_from(launch_iq2_gemv(a, nslots, maxcnt, 2, s))) != B200Q_OK) return st;
-    if ((st = mark(2)) != B200Q_OK) return st;
 
-    // 3. down over the int8 rows of every id
+    // 3. down over the int8 rows of every id, in the same launch: a batch's down units start once its up rows are in
     GemvArgs b = {};
     b.slab = (const uint8_t*)down; b.expert_bytes = iq2_bytes(H, F); b.extra_w = (const uint8_t*)shared_down;
     b.nslot_routed = E; b.n = H; b.k = F; b.counts = w.counts; b.offsets = w.offsets; b.order = w.order;
     b.act_div = 1; b.act_split = 1 << 30; b.xq = w.aq; b.xs = w.as; b.y = w.mo; b.ldy = H;
-    // the prologue's schedule and grouping are two launches back: the down GEMV takes its schedule and first unit
-    // while the up GEMV finishes
-    b.sched = w.sched; b.sched_early = 1;
+    b.sched = w.sched;
+#ifdef B200Q_X_NOFUSE
+    (void)maxcnt;
+    if ((st = status_from(launch_iq2_gemv(a, nslots, maxcnt, 2, s))) != B200Q_OK) return st;
+    if ((st = mark(2)) != B200Q_OK) return st;
+    b.sched_early = 1;   // the prologue's schedule is two launches back: taken while the up GEMV finishes
     if ((st = status_from(launch_iq2_gemv(b, nslots, maxcnt, 0, s))) != B200Q_OK) return st;
+#else
+    (void)maxcnt;
+    if ((st = status_from(launch_iq2_updown(a, b, w.ready, nslots, s))) != B200Q_OK) return st;
+    if ((st = mark(2)) != B200Q_OK) return st;   // (stage 2 is both projections; stage 3 is empty)
+#endif
     if ((st = mark(3)) != B200Q_OK) return st;
 
     // 4. combine + the shared expert's rows
@@ -562,6 +469,7 @@ int b200q_moe_decode(const void* x, const void* logits, const void* up, const vo
            extra ? (const float*)(w.mo + (size_t)pairs * H) : (const float*)nullptr, T, topk, H, out, out_dtype);
     if ((st = launched()) != B200Q_OK) return st;
     if ((st = mark(4)) != B200Q_OK) return st;
+    }
     if (ridx_out) {
         if (cudaMemcpyAsync(ridx_out, w.ridx, sizeof(int) * pairs, cudaMemcpyDeviceToDevice, s) != cudaSuccess) return status_from(cudaGetLastError());
     }
