@@ -714,6 +714,7 @@ def run_ours(args, rank, world, local_rank):
         if pre:
             line["prefill"] = pre
         line["ep"] = ep_bench(b200q, 0, 1, device, min(args.steps, 500), args.warmup, prefill=args.prefill)
+        line["libbolt_shapes"] = libbolt_shapes("ours", device)
         if args.prefill:
             line["nvfp4"] = nvfp4_bench(b200q, device)
     if dist:
@@ -794,7 +795,14 @@ def run_reference(args, rank, world):
     cpu_baseline(threads, min_seconds=0.0, max_passes=min(args.warmup, 3))
     c = cpu_baseline(threads, min_seconds=60.0, max_passes=args.steps)
     v = c["value"]
+    lb = None
+    if torch.cuda.is_available() and os.path.exists(os.path.join(ROOT, "oracle", "_ref", "libbolt_ref.so")):
+        try:
+            lb = libbolt_shapes("reference", torch.device("cuda", 0))
+        except Exception as e:   # a measurement beside the line: its failure does not take the line down
+            lb = {"unavailable": f"{type(e).__name__}: {e}"}
     return {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "libbolt_gpu": lb,
             "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic", "impl": "reference",
             "config": config2(),
@@ -824,6 +832,139 @@ def decode_only(b200q, device, steps, warmup):
     ms = e0.elapsed_time(e1)
     return {"decode": {"gbs": round(nb / (ms * 1e-3) / 1e9, 1), "ms_per_step": round(ms / steps, 5),
                        "layers": LAYERS, "device_error": b200q.device_error()}}
+
+
+# libbolt's routed experts are compiled for its model: a latent of 1024 and TOPN = 9 (bolt_common.h:25,
+# bolt_kernels.cu:682-695); the comparison runs them there, with this layer's 128 experts and FFN width 2048
+LB_T, LB_E, LB_W, LB_LATENT, LB_TOPN = 16, 128, 2048, 1024, 9
+
+
+def libbolt_shapes(kind, device, iters=50):
+    """libbolt's operator launchers at libbolt's own shapes, on the B200: kind "reference" times libbolt's kernels
+    (engine/bolt_kernels.cu and bolt_mma.cu built for sm_100a into oracle/_ref, the reference arm only); "ours" times
+    this engine's shims of the same names and signatures (include/b200q_bolt.h, through the shim harness).  Both get the
+    same seeded inputs (weights from the seeded generator, routing from each side's k_route, which agree index for
+    index) and the same timed loop (`iters` launches on a stream, CUDA events, weight copies rotated past the L2).
+    Returns GB/s of weights streamed a launch for: moe_up / moe_down (16 tokens, 128 experts, top-9, width 2048,
+    latent 1024), mma_nv4 (in_proj 18560 x 4096, 1 and 16 rows), mma_q8 (q/k/v 6144 x 4096, 1 and 16 rows), mma_iq2
+    (the shared expert's up, 2048 x 4096, 16 rows)."""
+    import ctypes
+    vp, i32, f32, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+    if kind == "reference":
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        import refbind as R
+        L = R.lib()
+
+        def run(name, *a):
+            R.call("ref_" + name, *a)
+        synth = lambda seed, nb: torch.from_numpy(O.synth_iq2(seed, nb).reshape(-1)).to(device)
+        tile_bytes = lambda f, n, k: (L.ref_tile_bytes(f, n, k), L.ref_tile_scale_bytes(f, n, k))
+        time_moe, time_mma = L.ref_time_moe, L.ref_time_mma
+    else:
+        import b200q
+        path = os.path.join(ROOT, "tests", "_build", "libbolt_shim_harness.so")
+        if not os.path.exists(path):
+            return {"unavailable": "the shim harness is not built (tests/build_harness.py)"}
+        L = ctypes.CDLL(path)
+        L.hs_tile_bytes.restype, L.hs_tile_bytes.argtypes = sz, [i32, i32, i32, i32]
+        L.hs_time_moe.restype = L.hs_time_mma.restype = f32
+        L.hs_time_moe.argtypes = [i32, i32, i32, vp, vp, sz, sz, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32]
+        L.hs_time_mma.argtypes = [i32, i32, i32, vp, vp, f32, i32, i32, vp, vp, i32]
+        names = {"repack_iq2": ("hs_repack_iq2", [vp, vp, vp, vp, sz, i32]),
+                 "route": ("hs_k_route", [vp, vp, i32, vp, vp, vp, i32, f32, i32]),
+                 "moe_group": ("hs_k_moe_group", [vp, vp, i32, vp, vp, vp, vp, vp]),
+                 "quant_rows": ("hs_k_quant_rows", [vp, vp, i32, vp, i32, vp, i32, i32, i32]),
+                 "tile_nv4": ("hs_tile_nv4", [vp, vp, vp, vp, vp, i32, i32]),
+                 "tile_q8": ("hs_tile_q8", [vp, vp, vp, vp, i32, i32]),
+                 "tile_iq2": ("hs_tile_iq2", [vp, vp, vp, vp, i32, i32])}
+        for fn, args in names.values():
+            getattr(L, fn).restype, getattr(L, fn).argtypes = None, args
+
+        def run(name, *a):
+            getattr(L, names[name][0])(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), *a)
+            torch.cuda.synchronize()
+        synth = lambda seed, nb: b200q.synth_iq2(seed, nb, device)
+        tile_bytes = lambda f, n, k: (L.hs_tile_bytes(f, 0, n, k), L.hs_tile_bytes(f, 1, n, k))
+        time_moe, time_mma = L.hs_time_moe, L.hs_time_mma
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    ptrs = lambda ts: ctypes.cast((ctypes.c_void_p * len(ts))(*[t.data_ptr() for t in ts]), ctypes.c_void_p)
+    u8 = lambda n: torch.empty(n, dtype=torch.uint8, device=device)
+    out = {}
+    g = torch.Generator().manual_seed(61)
+    # ---- routed experts: libbolt's planar slabs (its repack_iq2 / the shim's, into the same buffers), two copies
+    T, E, W, K, topn = LB_T, LB_E, LB_W, LB_LATENT, LB_TOPN
+    pairs = T * topn
+    ups, downs = [], []
+    for c in range(2):
+        for proj, rows, k, dst in (("up", E * W, K, ups), ("down", E * K, W, downs)):
+            raw = synth(6100 + 2 * c + (proj == "down"), rows * (k // 256))
+            qs, d = u8(rows * (k // 256) * 64), u8(rows * (k // 256) * 2)
+            run("repack_iq2", P(raw), P(qs), P(d), rows, k)
+            dst.append((qs, d))
+            del raw
+    logits = torch.randn(T, E, generator=g).to(device)
+    bias = torch.zeros(E, device=device)
+    ridx = torch.empty(pairs, dtype=torch.int32, device=device)
+    rw = torch.empty(pairs, device=device)
+    run("route", P(logits), E, P(bias), P(ridx), P(rw), E, 1.0, T)
+    # the work lists at libbolt's own sizes (bolt_host.cu:1076: TMAX * TOPN entries; the shim writes one item a slot)
+    work = [torch.zeros(4096, dtype=torch.int32, device=device) for _ in range(4)] + \
+        [torch.zeros(1, dtype=torch.int32, device=device)]
+    run("moe_group", P(ridx), pairs, *[P(w) for w in work])
+    x = torch.randn(T, K, generator=g).to(device)
+    xq, xs = torch.empty(T, K, dtype=torch.int8, device=device), torch.empty(T, K // 32, device=device)
+    run("quant_rows", P(x), K, P(xq), K, P(xs), K // 32, T, K)
+    act = torch.empty(pairs, W, device=device)
+    distinct = len(torch.unique(ridx))
+    wbytes = distinct * W * (K // 256) * 66
+    ms = time_moe(0, iters, 2, ptrs([q for q, _ in ups]), ptrs([d for _, d in ups]), W * (K // 256) * 64,
+                  W * (K // 256), *[P(w) for w in work], P(xq), P(xs), P(act), W, pairs)
+    out["moe_up_gbs"] = round(wbytes / (ms * 1e-3) / 1e9, 1) if ms > 0 else None
+    aq, as_ = torch.empty(pairs, W, dtype=torch.int8, device=device), torch.empty(pairs, W // 32, device=device)
+    run("quant_rows", P(act), W, P(aq), W, P(as_), W // 32, pairs, W)
+    mo = torch.empty(pairs, K, device=device)
+    ms = time_moe(1, iters, 2, ptrs([q for q, _ in downs]), ptrs([d for _, d in downs]), K * (W // 256) * 64,
+                  K * (W // 256), *[P(w) for w in work], P(aq), P(as_), P(mo), W, pairs)
+    out["moe_down_gbs"] = round(wbytes / (ms * 1e-3) / 1e9, 1) if ms > 0 else None
+    out["moe_distinct_experts"] = distinct
+    del ups, downs
+    # ---- the tile GEMMs over weight copies past the L2
+    rng = np.random.default_rng(62)
+    for fmt, name, n, k, copies, rows_list in ((0, "mma_nv4", 18560, 4096, 4, (1, 16)), (1, "mma_q8", 6144, 4096, 6, (1, 16)),
+                                              (2, "mma_iq2", 2048, 4096, 32, (16,))):
+        cb, sb = tile_bytes(fmt, n, k)
+        qts, sts = [], []
+        for c in range(copies):
+            qt, st = u8(cb), u8(sb)
+            if fmt == 0:
+                q = torch.from_numpy(rng.integers(0, 256, (n, k // 2), dtype=np.uint8)).to(device)
+                sc = (torch.rand(n, k // 16, generator=g) * 1.5 + 0.5).to(torch.float8_e4m3fn).view(torch.uint8).to(device)
+                run("tile_nv4", P(q), P(sc), P(qt), P(st), n, k)
+                wb = n * k // 2 + n * k // 16
+            elif fmt == 1:
+                qv = rng.integers(-127, 128, (n, k // 32, 32), dtype=np.int8)
+                dv = rng.uniform(1e-3, 1e-2, (n, k // 32)).astype(np.float16)
+                raw = torch.from_numpy(np.concatenate([dv.view(np.uint8).reshape(n, k // 32, 2), qv.view(np.uint8)],
+                                                      -1).reshape(-1)).to(device)
+                run("tile_q8", P(raw), P(qt), P(st), n, k)
+                wb = n * k // 32 * 34
+            else:
+                raw = synth(6200 + c, n * (k // 256))
+                run("tile_iq2", P(raw), P(qt), P(st), n, k)
+                wb = n * k // 256 * 66
+            qts.append(qt)
+            sts.append(st)
+        for M in rows_list:
+            xm = torch.randn(M, k, generator=g).to(device)
+            ym = torch.empty(M, n, device=device)
+            ms = time_mma(fmt, iters, copies, ptrs(qts), ptrs(sts), 0.01, n, k, P(xm), P(ym), M)
+            out[f"{name}_M{M}_gbs"] = round(wb / (ms * 1e-3) / 1e9, 1) if ms > 0 else None
+        del qts, sts
+    out["shapes"] = ("moe_up/moe_down: 16 tokens, 128 experts, top-9, width 2048, latent 1024; mma_nv4 18560 x 4096; "
+                     "mma_q8 6144 x 4096; mma_iq2 2048 x 4096; GB/s of weights a launch")
+    torch.cuda.synchronize()
+    return out
 
 
 def ckpt_bench(b200q, device, reps=3):
@@ -889,7 +1030,7 @@ def main():
     ap.add_argument("--layers", type=int, default=4, help="layer copies rotated to defeat L2 (1 for small profiles)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="length of the CPU-baseline sample")
     ap.add_argument("--no-prefill", dest="prefill", action="store_false", help="skip the config-4 prefill GEMMs")
-    ap.add_argument("--only", choices=["decode", "prefill", "nvfp4", "ep", "ckpt"], default=None,
+    ap.add_argument("--only", choices=["decode", "prefill", "nvfp4", "ep", "ckpt", "libbolt"], default=None,
                     help="run one sub-measurement on one GPU and print its object (for profiling)")
     args = ap.parse_args()
     global LAYERS
@@ -902,7 +1043,9 @@ def main():
         import b200q
         device = torch.device("cuda", local_rank)
         torch.cuda.set_device(device)
-        if args.only == "decode":
+        if args.only == "libbolt":
+            line = {"libbolt_shapes": libbolt_shapes("ours", device)}
+        elif args.only == "decode":
             line = decode_only(b200q, device, args.steps, args.warmup)
         elif args.only == "prefill":
             up, down, _, _ = full_layer(b200q, device, 0)

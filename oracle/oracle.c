@@ -603,3 +603,44 @@ EXPORT void or_synth_iq2(uint64_t seed, int64_t nblocks, uint8_t* out) {
 #include <omp.h>
 EXPORT void or_set_threads(int n) { omp_set_num_threads(n > 0 ? n : 1); }
 EXPORT int or_max_threads(void) { return omp_get_max_threads(); }
+
+/* IQ2_XXS with the chunk scale folded into bf16 weights: the shared-expert GEMM of libbolt's mma_iq2 (PIQ2::step,
+ * bolt_mma.cu:372-397 over the tables of PIQ2::init, :310-324): dA = d * (0.5 + s4) * 0.25 rounded to bf16, each
+ * weight the bf16 product of that and the signed grid magnitude (round to nearest even), fp64 accumulation here (the
+ * kernel: fp32 on the tensor cores).  x is taken as given (the kernel rounds its rows to bf16; the caller does here).
+ * epi 1: relu^2. */
+EXPORT void or_iq2_gemm_bf16fold(const uint8_t* blocks, int N, int K, const float* x, int T, float* y, int epi) {
+    int n;
+#pragma omp parallel for schedule(dynamic, 16)
+    for (n = 0; n < N; n++) {
+        float* w = (float*)malloc(sizeof(float) * (size_t)K);
+        int b, c, l, j, t, k;
+        for (b = 0; b < K / 256; b++) {
+            const uint8_t* blk = blocks + ((size_t)n * (K / 256) + b) * 66;
+            const float d = or_h2f(rd16(blk));
+            for (c = 0; c < 8; c++) {
+                const uint32_t qx = rd32(blk + 2 + 8 * c), qy = rd32(blk + 2 + 8 * c + 4);
+                const float sa = or_bf2f(or_f2bf(d * (0.5f + (float)(qy >> 28)) * 0.25f));
+                for (l = 0; l < 4; l++) {
+                    const uint64_t g = iq2xxs_grid[(qx >> (8 * l)) & 255];
+                    const uint32_t sidx = (qy >> (7 * l)) & 127;
+                    const uint32_t sg = ksigns_iq2xs[sidx];
+                    for (j = 0; j < 8; j++) {
+                        float v = (float)((g >> (8 * j)) & 255);
+                        if ((sg >> j) & 1) v = -v;
+                        w[b * 256 + c * 32 + l * 8 + j] = or_bf2f(or_f2bf(v * sa));
+                    }
+                }
+            }
+        }
+        for (t = 0; t < T; t++) {
+            double acc = 0.0;
+            float v;
+            for (k = 0; k < K; k++) acc += (double)w[k] * (double)x[(size_t)t * K + k];
+            v = (float)acc;
+            if (epi == 1) v = v > 0.f ? v * v : 0.f;
+            y[(size_t)t * N + n] = v;
+        }
+        free(w);
+    }
+}

@@ -45,6 +45,7 @@ def lib():
             "or_q8_gemm_f16fold": (None, [vp, i32, i32, vp, i32, vp]),
             "or_iq2_gemm_f16fold": (None, [vp, i32, i32, vp, i32, vp, i32]),
             "or_synth_iq2": (None, [ctypes.c_uint64, i64, vp]),
+            "or_iq2_gemm_bf16fold": (None, [vp, i32, i32, vp, i32, vp, i32]),
             "or_set_threads": (None, [i32]), "or_max_threads": (i32, []),
         }
         for name, (res, args) in sig.items():
@@ -208,6 +209,15 @@ def iq2_gemm_f16fold(blocks, n, k, x, epi=0):
     y = np.zeros((x.shape[0], n), np.float32)
     b = _c(blocks, np.uint8)
     lib().or_iq2_gemm_f16fold(_p(b), n, k, _p(x), x.shape[0], _p(y), epi)
+    return y
+
+
+def iq2_gemm_bf16fold(blocks, n, k, x, epi=0):
+    """libbolt's mma_iq2 arithmetic (PIQ2): bf16(bf16(dA) x signed grid) weights; x as given (round it to bf16)"""
+    x = _c(x, np.float32).reshape(-1, k)
+    y = np.zeros((x.shape[0], n), np.float32)
+    b = _c(blocks, np.uint8)
+    lib().or_iq2_gemm_bf16fold(_p(b), n, k, _p(x), x.shape[0], _p(y), epi)
     return y
 
 

@@ -1,7 +1,7 @@
 """ctypes binding of oracle/_ref/libbolt_ref.so -- TEST INFRASTRUCTURE ONLY.
 
-libbolt's own kernels (engine/bolt_kernels.cu, compiled for sm_100a from where it lies by build_oracle.py --ref) behind
-oracle/ref_shim.cu.  The GPU tests run them on the same inputs as the CPU oracle to pin the oracle to the reference
+libbolt's own kernels (engine/bolt_kernels.cu compiled for sm_100a from where it lies, and engine/bolt_mma.cu from a
+guarded build copy, by build_oracle.py --ref) behind oracle/ref_shim.cu.  The GPU tests run them on the same inputs as the CPU oracle to pin the oracle to the reference
 itself, and tests/golden/make_golden.py records their outputs as fixtures.  All arguments are device pointers (ints).
 """
 import ctypes
@@ -34,10 +34,26 @@ def lib():
             "ref_gemv_iq2": [vp, vp, i32, i32, vp, i32, vp, i32, i32, i32],
             "ref_gemv_nv4": [vp, vp, f32, i32, i32, vp, i32, vp, i32, i32],
             "ref_gemv_q8": [vp, vp, i32, i32, vp, i32, vp, i32, i32],
+            "ref_tile_nv4": [vp, vp, vp, vp, i32, i32],
+            "ref_tile_q8": [vp, vp, vp, i32, i32],
+            "ref_tile_iq2": [vp, vp, vp, i32, i32],
+            "ref_mma_nv4": [vp, vp, f32, i32, i32, vp, i32, vp, i32, i32],
+            "ref_mma_q8": [vp, vp, i32, i32, vp, i32, vp, i32, i32],
+            "ref_mma_iq2": [vp, vp, i32, i32, vp, i32, vp, i32, i32, i32],
+            "ref_quant_nv4_rows": [vp, i32, vp, vp, i32, i32],
         }
         for name, args in sig.items():
             fn = getattr(L, name)
             fn.restype, fn.argtypes = ctypes.c_int, args
+        for name in ("ref_tile_bytes", "ref_tile_scale_bytes"):
+            fn = getattr(L, name)
+            fn.restype, fn.argtypes = sz, [i32, i32, i32]
+        fn = L.ref_time_moe
+        fn.restype = ctypes.c_float
+        fn.argtypes = [i32, i32, i32, vp, vp, sz, sz, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32]
+        fn = L.ref_time_mma
+        fn.restype = ctypes.c_float
+        fn.argtypes = [i32, i32, i32, vp, vp, f32, i32, i32, vp, vp, i32]
         _LIB = L
     return _LIB
 

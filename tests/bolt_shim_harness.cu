@@ -110,3 +110,52 @@ void hs_mma_q8_multi(void* s, const void* const* qt, const void* const* dt, cons
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------------------
+// Timed loops (bench.py's libbolt-shape measurement): `iters` launches of one shim on a stream of its own, timed with
+// events on that stream; ms a launch (negative on a CUDA error).  The same loop as oracle/ref_shim.cu's for libbolt's
+// own launchers, so the two are timed alike.
+// ---------------------------------------------------------------------------------------------------------
+template <class F>
+static float hs_timed(int iters, F f) {
+    cudaStream_t s;
+    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) return -1.f;
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    for (int i = 0; i < 3; i++) f(s, i);
+    cudaEventRecord(e0, s);
+    for (int i = 0; i < iters; i++) f(s, i);
+    cudaEventRecord(e1, s);
+    float ms = -1.f;
+    if (cudaEventSynchronize(e1) == cudaSuccess) cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaStreamDestroy(s);
+    return cudaGetLastError() == cudaSuccess ? ms / iters : -1.f;
+}
+
+extern "C" {
+
+float hs_time_moe(int which, int iters, int copies, const void* const* qs, const void* const* d, size_t qs_stride,
+                  size_t d_stride, int* order, int* first, int* count, int* exp, int* nwork, const int8_t* xq,
+                  const float* xs, float* y, int width, int pairs) {
+    const MoeWork w{order, first, count, exp, nwork};
+    return hs_timed(iters, [&](cudaStream_t s, int i) {
+        const IQ2Slab slab{(const uint8_t*)qs[i % copies], d[i % copies], qs_stride, d_stride};
+        if (which == 0) moe_up(s, slab, w, xq, xs, y, width, pairs);
+        else moe_down(s, slab, w, xq, xs, y, width, pairs);
+    });
+}
+
+float hs_time_mma(int fmt, int iters, int copies, const void* const* qt, const void* const* st, float s2, int n, int k,
+                  const float* x, float* y, int T) {
+    return hs_timed(iters, [&](cudaStream_t s, int i) {
+        const int c = i % copies;
+        if (fmt == 0) mma_nv4(s, TNV4{(const uint4*)qt[c], (const uint2*)st[c], s2, n, k}, x, k, y, n, T);
+        else if (fmt == 1) mma_q8(s, TQ8{(const uint4*)qt[c], (const uint32_t*)st[c], n, k}, x, k, y, n, T);
+        else mma_iq2(s, TIQ2{(const uint4*)qt[c], (const uint16_t*)st[c], n, k}, x, k, y, n, T, 0);
+    });
+}
+
+}  // extern "C"

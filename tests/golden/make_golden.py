@@ -1,7 +1,7 @@
 """Golden fixtures from libbolt's own kernels run on a B200 -- TEST INFRASTRUCTURE.
 
 The reference ships no golden vectors for its quantized GEMMs.  This script runs the reference's kernels
-(engine/bolt_kernels.cu compiled for sm_100a from where it lies, oracle/_ref/libbolt_ref.so) on seeded inputs and
+(engine/bolt_kernels.cu and engine/bolt_mma.cu compiled for sm_100a, oracle/_ref/libbolt_ref.so) on seeded inputs and
 writes their outputs to tests/golden/ref_<case>.npz; tests/test_golden.py then checks the CPU oracle against them on
 any machine.  Large weights are not stored: they are regenerated from their seed by the library's host generator
 (b200q.synth_iq2_host, deterministic per seed).
@@ -162,6 +162,76 @@ def case_gemv_q8():
     y = torch.zeros(T, n, dtype=torch.float32, device=DEV)
     R.call("ref_gemv_q8", _p(_d(qv)), _p(_d(dv)), n, k, _p(_d(x)), k, _p(y), n, T)
     return {"q": qv, "d": dv, "x": x}, {"y": y.cpu().numpy()}
+
+
+def _tiles(fmt, n, k):
+    code = torch.empty(R.lib().ref_tile_bytes(fmt, n, k), dtype=torch.uint8, device=DEV)
+    scale = torch.empty(R.lib().ref_tile_scale_bytes(fmt, n, k), dtype=torch.uint8, device=DEV)
+    return code, scale
+
+
+def case_mma_nv4():
+    """bolt_mma.cu's NVFP4 tile GEMM (tile_nv4 + mma_nv4: fp16 rows, the e4m3 scales folded exactly into fp16
+    operands), n 80 (five 16-row tiles), k 512, 5 rows."""
+    import oracle as O
+    n, k, T = 80, 512, 5
+    rng = np.random.default_rng(12)
+    q = rng.integers(0, 256, (n, k // 2), dtype=np.uint8)
+    sc = np.array([O.scalar("or_e4m3_enc", float(v)) for v in rng.uniform(0.5, 2, n * k // 16)], np.uint8).reshape(n, k // 16)
+    x = rng.standard_normal((T, k)).astype(np.float32)
+    qt, st = _tiles(0, n, k)
+    R.call("ref_tile_nv4", _p(_d(q)), _p(_d(sc)), _p(qt), _p(st), n, k)
+    y = torch.zeros(T, n, dtype=torch.float32, device=DEV)
+    R.call("ref_mma_nv4", _p(qt), _p(st), 0.375, n, k, _p(_d(x)), k, _p(y), n, T)
+    return {"q": q, "sc": sc, "s2": np.float32(0.375), "x": x}, {"y": y.cpu().numpy()}
+
+
+def case_mma_q8():
+    """bolt_mma.cu's Q8_0 tile GEMM (tile_q8 + mma_q8: fp16 rows, weights fp16(i8 d)), n 80, k 512, 5 rows."""
+    n, k, T = 80, 512, 5
+    rng = np.random.default_rng(13)
+    qv = rng.integers(-127, 128, (n, k // 32, 32), dtype=np.int8)
+    dv = rng.uniform(1e-3, 1e-2, (n, k // 32)).astype(np.float16)
+    blocks = np.concatenate([dv.view(np.uint8).reshape(n, k // 32, 2), qv.view(np.uint8)], -1).reshape(n, -1)
+    x = rng.standard_normal((T, k)).astype(np.float32)
+    qt, st = _tiles(1, n, k)
+    R.call("ref_tile_q8", _p(_d(blocks)), _p(qt), _p(st), n, k)
+    y = torch.zeros(T, n, dtype=torch.float32, device=DEV)
+    R.call("ref_mma_q8", _p(qt), _p(st), n, k, _p(_d(x)), k, _p(y), n, T)
+    return {"blocks": blocks, "x": x}, {"y": y.cpu().numpy()}
+
+
+def case_mma_iq2():
+    """bolt_mma.cu's IQ2_XXS tile GEMM, the shared expert's (tile_iq2 + mma_iq2: PIQ2's bf16 fold, bf16 rows), n 64,
+    k 512, 5 rows, without and with relu^2."""
+    n, k, T, seed = 64, 512, 5, 93
+    blocks = iq2_blocks(seed, n, k)
+    x = np.random.default_rng(14).standard_normal((T, k)).astype(np.float32)
+    qt, st = _tiles(2, n, k)
+    R.call("ref_tile_iq2", _p(_d(blocks)), _p(qt), _p(st), n, k)
+    out = {}
+    for epi in (0, 1):
+        y = torch.zeros(T, n, dtype=torch.float32, device=DEV)
+        R.call("ref_mma_iq2", _p(qt), _p(st), n, k, _p(_d(x)), k, _p(y), n, T, epi)
+        out[f"y{epi}"] = y.cpu().numpy()
+    return {"seed": np.int64(seed), "n": np.int32(n), "k": np.int32(k), "x": x}, out
+
+
+def case_quant_nv4_rows():
+    """bolt_mma.cu's row quantiser of the NVFP4 prompt path (quant_nv4_rows_k: e4m3 scale amax/6 a block of 16,
+    nearest e2m1), 37 rows of k 512 with per-block magnitudes from zero through e4m3 subnormal scales to saturation;
+    the scales are returned in [rows][k/16] order (the kernel stores them step-major, [k/64][(T+3)&~3][4])."""
+    T, k = 37, 512
+    rng = np.random.default_rng(15)
+    x = rng.standard_normal((T, k)).astype(np.float32)
+    mag = rng.choice(np.array([0.0, 1e-4, 3e-3, 0.05, 1.0, 30.0, 5000.0], np.float32), size=(T, k // 16, 1))
+    x = (x.reshape(T, k // 16, 16) * mag).reshape(T, k)
+    Tp = (T + 3) & ~3
+    q4 = torch.zeros(T, k // 2, dtype=torch.uint8, device=DEV)
+    sf = torch.zeros(k // 64, Tp, 4, dtype=torch.uint8, device=DEV)
+    R.call("ref_quant_nv4_rows", _p(_d(x)), k, _p(q4), _p(sf), T, k)
+    sf_rows = sf.cpu().numpy()[:, :T, :].transpose(1, 0, 2).reshape(T, k // 16)
+    return {"x": x}, {"q4": q4.cpu().numpy(), "sf": sf_rows}
 
 
 CASES = {name[5:]: fn for name, fn in dict(globals()).items() if name.startswith("case_")}

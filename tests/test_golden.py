@@ -70,3 +70,45 @@ def test_gemv_fp32():
     blocks = np.concatenate([i["d"].view(np.uint8).reshape(64, 8, 2), i["q"].view(np.uint8).reshape(64, 8, 32)], -1)
     y = O.q8_gemm_exact(blocks.reshape(64, -1), 64, 256, i["x"])
     assert np.allclose(y, o["y"], rtol=1e-5, atol=1e-5 * np.abs(y).max())
+
+
+def f16(a):
+    return np.asarray(a, np.float32).astype(np.float16).astype(np.float32)
+
+
+def bf16(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(torch.bfloat16).float().numpy()
+
+
+def test_mma_nv4_fold():
+    """libbolt's mma_nv4 (PNV4): fp16 rows, exact e2m1 x e4m3 operands: the oracle on fp16-rounded rows, 1e-5"""
+    i, o = load("mma_nv4")
+    n, k = o["y"].shape[1], i["x"].shape[1]
+    y = O.nv4_gemm_exact(i["q"], i["sc"], float(i["s2"]), n, k, f16(i["x"]))
+    assert np.allclose(o["y"], y, rtol=1e-5, atol=1e-5 * np.abs(y).max())
+
+
+def test_mma_q8_fold():
+    """libbolt's mma_q8 (PQ8): fp16 rows, weights fp16(i8 d): the oracle's fp16 fold on fp16-rounded rows, 1e-5"""
+    i, o = load("mma_q8")
+    n, k = o["y"].shape[1], i["x"].shape[1]
+    y = O.q8_gemm_f16fold(i["blocks"], n, k, f16(i["x"]))
+    assert np.allclose(o["y"], y, rtol=1e-5, atol=1e-5 * np.abs(y).max())
+
+
+def test_mma_iq2_bf16_fold():
+    """libbolt's mma_iq2 (PIQ2): bf16 rows, weights bf16(bf16(dA) x grid): or_iq2_gemm_bf16fold, 1e-5"""
+    i, o = load("mma_iq2")
+    n, k = int(i["n"]), int(i["k"])
+    blocks = iq2_blocks(int(i["seed"]), n, k)
+    for epi in (0, 1):
+        y = O.iq2_gemm_bf16fold(blocks, n, k, bf16(i["x"]), epi)
+        assert np.allclose(o[f"y{epi}"], y, rtol=1e-5, atol=1e-5 * np.abs(y).max()), epi
+
+
+def test_quant_nv4_rows_bytes():
+    """libbolt's NVFP4 row quantiser (quant_nv4_rows_k): the oracle's codes and scales, byte for byte"""
+    i, o = load("quant_nv4_rows")
+    q4, sf = O.quant_nv4_rows(i["x"], i["x"].shape[1])
+    assert np.array_equal(q4, o["q4"]) and np.array_equal(sf, o["sf"])
