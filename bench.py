@@ -715,6 +715,10 @@ def run_ours(args, rank, world, local_rank):
             line["prefill"] = pre
         line["ep"] = ep_bench(b200q, 0, 1, device, min(args.steps, 500), args.warmup, prefill=args.prefill)
         line["libbolt_shapes"] = libbolt_shapes("ours", device)
+        try:
+            line["ckpt"] = ckpt_bench(b200q, device)["ckpt"]
+        except OSError as e:   # a measurement beside the line (it needs 0.6 GB of scratch disk)
+            line["ckpt"] = {"unavailable": str(e)}
         if args.prefill:
             line["nvfp4"] = nvfp4_bench(b200q, device)
     if dist:
@@ -968,30 +972,36 @@ def libbolt_shapes(kind, device, iters=50):
 
 
 def ckpt_bench(b200q, device, reps=3):
-    """Checkpoint ingestion (b200q_ckpt_*): one MoE layer at the model's own shapes (layer 1 of its schedule: 240
-    IQ2_XXS experts, width 2048, latent 1024; up and down in two safetensors shards, 260 MB) written to disk, then
-    packed from the mapped shards into the device slabs.  GB/s = raw checkpoint bytes / wall time of the two packs,
-    best of `reps` with the shards in the page cache (the pageable host-to-device copies run one expert at a time)."""
+    """Checkpoint ingestion (b200q_ckpt_*, b200q.Checkpoint.pack_moe_layer): one MoE layer of the model's schedule
+    (layer 1: 240 IQ2_XXS experts, width 2048, latent 1024, and its shared expert, 5376 x 4096) under the model's own
+    tensor names (language_model.backbone.layers.1.mixer...), written to two safetensors shards, then packed from the
+    mapped shards into the device slabs.  GB/s = raw checkpoint bytes / wall time of the layer's packs, best of `reps`
+    with the shards in the page cache (the first pass maps the shards and faults their pages in)."""
     import shutil
-    experts, width, latent = 240, 2048, 1024
+    layer, experts, width, latent, hidden, sw = 1, 240, 2048, 1024, 4096, 5376
     d = os.path.join(ROOT, "_build", "ckpt_bench")
     shutil.rmtree(d, ignore_errors=True)
     os.makedirs(d)
     try:
-        weight_map = {}
-        for proj, rows, k in (("up_proj", width, latent), ("down_proj", latent, width)):
-            nb = rows * (k // 256)
+        names = b200q.moe_layer_tensor_names(layer, experts)
+        weight_map, nbytes = {}, 0
+        shards = {"experts": [], "shared": []}
+        for e in range(experts):
+            shards["experts"].append((names["up"][e], width, latent, 7000 + e))
+            shards["experts"].append((names["down"][e], latent, width, 7000 + experts + e))
+        shards["shared"] = [(names["shared_up"], sw, hidden, 7900), (names["shared_down"], hidden, sw, 7901)]
+        for shard, tensors in shards.items():
             header, blobs, off = {}, [], 0
-            for e in range(experts):
-                name = f"backbone.layers.1.mixer.experts.{e}.{proj}.weight"
-                blob = b200q.synth_iq2_host(7000 + e + (experts if proj == "down_proj" else 0), nb).tobytes()
+            for name, rows, k, seed in tensors:
+                blob = b200q.synth_iq2_host(seed, rows * (k // 256)).tobytes()
                 header[name] = {"dtype": "U8", "shape": [rows, k // 256, 66], "data_offsets": [off, off + len(blob)]}
                 off += len(blob)
                 blobs.append(blob)
-                weight_map[name] = f"{proj}.safetensors"
+                weight_map[name] = f"model-{shard}.safetensors"
+            nbytes += off
             h = json.dumps(header).encode()
             h += b" " * ((8 - len(h) % 8) % 8)
-            with open(os.path.join(d, f"{proj}.safetensors"), "wb") as f:
+            with open(os.path.join(d, f"model-{shard}.safetensors"), "wb") as f:
                 f.write(len(h).to_bytes(8, "little"))
                 f.write(h)
                 for blob in blobs:
@@ -999,22 +1009,19 @@ def ckpt_bench(b200q, device, reps=3):
         with open(os.path.join(d, "model.safetensors.index.json"), "w") as f:
             json.dump({"weight_map": weight_map}, f)
         ck = b200q.Checkpoint(d)
-        up_names = [n for n in weight_map if n.endswith("up_proj.weight")]
-        down_names = [n for n in weight_map if n.endswith("down_proj.weight")]
-        nbytes = 2 * experts * width * (latent // 256) * 66
         best = None
-        for _ in range(reps + 1):   # the first pass maps the shards and faults their pages in
+        for _ in range(reps + 1):
             torch.cuda.synchronize()
             t0 = time.perf_counter()
-            su = ck.pack_iq2_slab(up_names, width, latent, device)
-            sd = ck.pack_iq2_slab(down_names, latent, width, device)
+            packed = ck.pack_moe_layer(layer, experts, width, latent, device=device)
             torch.cuda.synchronize()
             dt = time.perf_counter() - t0
             best = dt if best is None or dt < best else best
-            del su, sd
+            del packed
         ck.close()
-        return {"ckpt": {"workload": "one MoE layer of the model's schedule: 240 IQ2_XXS experts, width 2048, latent "
-                                     "1024, up and down (safetensors, page-cache resident)",
+        return {"ckpt": {"workload": "one MoE layer of the model's schedule (layer 1: 240 IQ2_XXS experts, width 2048, "
+                                     "latent 1024, + the 5376-wide shared expert) under the model's tensor names, two "
+                                     "safetensors shards, page-cache resident",
                          "bytes": nbytes, "ms": round(best * 1e3, 2), "gbs": round(nbytes / best / 1e9, 2),
                          "device_error": b200q.device_error()}}
     finally:

@@ -8,6 +8,7 @@ returns void and logs; its C ABI returns -1/-3).  There is no CPU fallback: with
 every operator raises.
 """
 import ctypes
+import json
 import os
 
 import torch
@@ -463,6 +464,38 @@ def moe_prompt(up, down, E, H, F, counts, offsets, order, topk, x, mo=None, act=
 # -------------------------------------------------------------------------------------------------------------
 # checkpoint ingestion (open_store / lookup / load_slab / load_nv4 / load_q8, bolt_host.cu:61-345)
 # -------------------------------------------------------------------------------------------------------------
+# The model's checkpoint layout (libbolt's loader, bolt_host.cu:126, 959-1011): tensors named under
+# language_model.backbone.layers.<layer>, routed experts in the MoE latent space of 1024
+MODEL_PREFIX = "language_model.backbone.layers"
+MODEL_LATENT = 1024
+
+
+def moe_layer_tensor_names(layer, experts, prefix=MODEL_PREFIX):
+    """the tensor names libbolt's loader reads for MoE layer `layer` (bolt_host.cu:316, 994-995)"""
+    p = f"{prefix}.{layer}.mixer"
+    return {"up": [f"{p}.experts.{e}.up_proj.weight" for e in range(experts)],
+            "down": [f"{p}.experts.{e}.down_proj.weight" for e in range(experts)],
+            "shared_up": f"{p}.shared_experts.up_proj.weight",
+            "shared_down": f"{p}.shared_experts.down_proj.weight"}
+
+
+def read_moe_schedule(path):
+    """The model's MoE schedule from its contract file (a JSON object with "moe_schedule": [{"layer", "experts",
+    "width", "top_k"}...], "moe_latent_size", "shared_expert_width"): a list of (layer, experts, width, top_k) and a
+    dict of the shared sizes.  Every entry is checked (positive sizes, widths a multiple of 256)."""
+    with open(path) as f:
+        c = json.load(f)
+    sched = []
+    for m in c["moe_schedule"]:
+        L, e, w, k = int(m["layer"]), int(m["experts"]), int(m["width"]), int(m["top_k"])
+        if L < 0 or e <= 0 or k <= 0 or k > e or w <= 0 or w % 256:
+            raise B200QError(EINVAL, f"bad MoE schedule entry {m}")
+        sched.append((L, e, w, k))
+    info = {"latent": int(c.get("moe_latent_size", MODEL_LATENT)), "shared_width": int(c.get("shared_expert_width", 0)),
+            "hidden": int(c.get("hidden", 4096))}
+    return sched, info
+
+
 class _Mapping:
     """The library's handle of an opened checkpoint.  The shards stay mapped while this object lives: the Checkpoint
     and every tensor view it handed out hold a reference, so a view never outlives the memory it reads."""
@@ -547,6 +580,31 @@ class Checkpoint:
         arr = (ctypes.c_char_p * len(names))(*[n.encode() for n in names])
         _check(lib().b200q_ckpt_pack_iq2_slab(self._h, arr, len(names), rows, k, _p(out), _p(st), st.numel(), _s()),
                "pack_iq2_slab")
+        return out
+
+    def tensor_shape(self, name):
+        """a tensor's shape (the safetensors header's), without reading its bytes"""
+        return self.tensor(name)[1]
+
+    def pack_moe_layer(self, layer, experts, width, latent=MODEL_LATENT, prefix=MODEL_PREFIX, device="cuda"):
+        """One MoE layer of the model's checkpoint, as libbolt's loader takes it (bolt_host.cu:994-1003, load_slab
+        :306-328): the routed experts' up projections (prefix.<layer>.mixer.experts.<e>.up_proj.weight, [width][latent]
+        each) and down projections ([latent][width]) into one slab each, and the shared expert's up and down
+        (prefix.<layer>.mixer.shared_experts.{up,down}_proj.weight, their shapes read from the checkpoint).  Returns
+        {"up", "down", "shared_up", "shared_down": packed rt32 tensors, "shared_width", "hidden"}."""
+        names = moe_layer_tensor_names(layer, experts, prefix)
+        up = self.pack_iq2_slab(names["up"], width, latent, device)
+        down = self.pack_iq2_slab(names["down"], latent, width, device)
+        out = {"up": up, "down": down}
+        su, sd = self.tensor_shape(names["shared_up"]), self.tensor_shape(names["shared_down"])
+        if len(su) != 3 or len(sd) != 3 or su[2] != 66 or sd[2] != 66:
+            raise B200QError(EINVAL, f"layer {layer}: the shared expert is not IQ2_XXS ([rows][k/256][66])")
+        sw, hidden = int(su[0]), int(su[1]) * 256
+        if int(sd[0]) != hidden or int(sd[1]) * 256 != sw:
+            raise B200QError(EINVAL, f"layer {layer}: shared expert shapes {su} / {sd} do not chain")
+        out["shared_up"] = self.pack_iq2_slab([names["shared_up"]], sw, hidden, device)
+        out["shared_down"] = self.pack_iq2_slab([names["shared_down"]], hidden, sw, device)
+        out["shared_width"], out["hidden"] = sw, hidden
         return out
 
     def pack_nv4(self, prefix, n, k, device="cuda"):

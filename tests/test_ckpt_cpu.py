@@ -243,3 +243,72 @@ def test_mutated_headers_never_escape_the_file(tmp_path):
             assert dt not in elt or view.nbytes == n * elt[dt]
             assert view.nbytes <= size - 8 - len(hb)
         ck.close()
+
+
+def model_moe_checkpoint(d, layers=((1, 3, 512), (3, 2, 256)), latent=256, hidden=512, shared_width=768, seed=7):
+    """a checkpoint with the model's own tensor names (libbolt's loader, bolt_host.cu:316, 994-995) at small sizes:
+    MoE layers (layer, experts, width), each with its routed experts in the latent space and one shared expert on the
+    hidden size; returns {name: (dtype, shape, bytes)}"""
+    t = {}
+    for li, (layer, experts, width) in enumerate(layers):
+        names = b200q.moe_layer_tensor_names(layer, experts)
+        for e in range(experts):
+            for name, rows, k in ((names["up"][e], width, latent), (names["down"][e], latent, width)):
+                blob = b200q.synth_iq2_host(seed * 1000 + li * 100 + e * 2 + (rows == latent), rows * (k // 256)).tobytes()
+                t[name] = ("U8", (rows, k // 256, 66), blob)
+        for name, rows, k in ((names["shared_up"], shared_width, hidden), (names["shared_down"], hidden, shared_width)):
+            t[name] = ("U8", (rows, k // 256, 66), b200q.synth_iq2_host(seed + rows + k, rows * (k // 256)).tobytes())
+    t["language_model.backbone.norm_f.weight"] = ("F32", (4,), np.ones(4, np.float32).tobytes())
+    names = sorted(t)
+    half = len(names) // 2
+    for i, part in enumerate((names[:half], names[half:])):
+        write_safetensors(os.path.join(d, f"model-{i + 1:05d}-of-00002.safetensors"), {x: t[x] for x in part})
+    write_index(d, {x: f"model-{(0 if j < half else 1) + 1:05d}-of-00002.safetensors" for j, x in enumerate(names)})
+    return t
+
+
+def test_model_names_resolve(tmp_path):
+    """every tensor libbolt's loader asks for, by the model's naming, is found with its shape"""
+    t = model_moe_checkpoint(str(tmp_path))
+    ck = b200q.Checkpoint(str(tmp_path))
+    for layer, experts, width in ((1, 3, 512), (3, 2, 256)):
+        names = b200q.moe_layer_tensor_names(layer, experts)
+        for e in range(experts):
+            assert ck.tensor_shape(names["up"][e]) == (width, 1, 66)
+            assert ck.tensor_shape(names["down"][e]) == (256, width // 256, 66)
+        assert ck.tensor_shape(names["shared_up"]) == (768, 2, 66)
+        assert ck.tensor_shape(names["shared_down"]) == (512, 3, 66)
+    assert names["up"][0] == "language_model.backbone.layers.3.mixer.experts.0.up_proj.weight"
+    with pytest.raises(b200q.B200QError):
+        ck.tensor_shape(b200q.moe_layer_tensor_names(1, 4)["up"][3])   # layer 1 has three experts
+    ck.close()
+
+
+def test_moe_schedule_reader(tmp_path):
+    """the contract's MoE schedule: parsed and checked entry by entry"""
+    c = {"hidden": 4096, "moe_latent_size": 1024, "shared_expert_width": 5376,
+         "moe_schedule": [{"layer": 1, "experts": 240, "width": 2048, "top_k": 9},
+                          {"layer": 3, "experts": 240, "width": 1536, "top_k": 9}]}
+    p = tmp_path / "bolt.json"
+    p.write_text(json.dumps(c))
+    sched, info = b200q.read_moe_schedule(str(p))
+    assert sched == [(1, 240, 2048, 9), (3, 240, 1536, 9)]
+    assert info == {"latent": 1024, "shared_width": 5376, "hidden": 4096}
+    c["moe_schedule"].append({"layer": 5, "experts": 240, "width": 1000, "top_k": 9})   # not a multiple of 256
+    p.write_text(json.dumps(c))
+    with pytest.raises(b200q.B200QError):
+        b200q.read_moe_schedule(str(p))
+
+
+def test_real_contract_schedule():
+    """the reference's own contract, where its checkout is at hand: 40 MoE layers of 240 to 496 experts, widths 1536
+    to 2560, top-9, latent 1024, shared expert 5376 wide"""
+    here = os.path.dirname(os.path.abspath(__file__))
+    path = os.environ.get("B200Q_CONTRACT",
+                          os.path.join(os.path.dirname(os.path.dirname(here)), "reference", "contract", "bolt.json"))
+    if not os.path.exists(path):
+        pytest.skip("the model's contract file is not present")
+    sched, info = b200q.read_moe_schedule(path)
+    assert len(sched) == 40 and info["latent"] == 1024 and info["shared_width"] == 5376
+    assert {e for _, e, _, _ in sched} <= {240, 304, 368, 432, 496}
+    assert {w for _, _, w, _ in sched} <= {1536, 2048, 2304, 2560} and {k for *_, k in sched} == {9}
