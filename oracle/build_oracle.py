@@ -64,6 +64,10 @@ def guarded_mma_source(src_path, dst_path):
     end += 2
     guarded = (text[:at] + "\n#if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1200\n" + text[at:end] +
                "\n#endif\n" + text[end:])
+    if os.path.exists(dst_path):   # unchanged: keep its time stamp, so what is built from it is not rebuilt
+        with open(dst_path) as f:
+            if f.read() == guarded:
+                return dst_path
     with open(dst_path, "w") as f:
         f.write(guarded)
     return dst_path
@@ -91,7 +95,70 @@ def build_ref():
     return REF_OUT
 
 
+LINK_OUT = os.path.join(REF_DIR, "libbolt_b200.so")
+PKG = os.path.join(os.path.dirname(HERE), "nemotron-3.5-bolt-tensorfold-dgx-spark_b200")
+
+
+def build_bolt_link():
+    """libbolt as a whole, with its hot path from this engine: the reference's own engine/bolt_host.cu, bolt_kernels.cu,
+    bolt_draft.cu and (guarded) bolt_mma.cu compiled for sm_100a, every launcher that libb200q.so also defines (its
+    libbolt-signature shims, include/b200q_bolt.h) made local to the reference's objects (objcopy --localize-symbol),
+    and the result linked against libb200q.so -> oracle/_ref/libbolt_b200.so.  bolt_host.cu's calls of those launchers
+    are then undefined in the link and bound to libb200q.so at load time; the rest of libbolt (the Mamba scan,
+    attention, the drafter, the host logic behind the 45 exports of engine/bolt.def) is the reference's.  Returns the
+    path, or None where the reference checkout is absent."""
+    srcs = {n: os.path.join(ENGINE, n + ".cu") for n in ("bolt_host", "bolt_kernels", "bolt_draft")}
+    if not all(os.path.exists(v) for v in srcs.values()):
+        return LINK_OUT if os.path.exists(LINK_OUT) else None
+    lib = os.path.join(PKG, "libb200q.so")
+    obj_dir = os.path.join(REF_DIR, "obj")
+    os.makedirs(obj_dir, exist_ok=True)
+    srcs["bolt_mma"] = guarded_mma_source(os.path.join(ENGINE, "bolt_mma.cu"), os.path.join(REF_DIR, "bolt_mma_sm100.cu"))
+    objs = {}
+    import concurrent.futures
+
+    def compile_one(item):
+        name, src = item
+        obj = os.path.join(obj_dir, name + ".o")
+        if _stale(obj, [src, __file__]):
+            cmd = [NVCC, "-O2", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-Xcompiler", "-fPIC",
+                   "-diag-suppress", "177", "-I", ENGINE, "-c", src, "-o", obj]
+            r = subprocess.run(cmd, capture_output=True, text=True)
+            if r.returncode != 0:
+                raise RuntimeError(f"nvcc failed on {src}:\n{r.stderr}")
+        return name, obj
+    with concurrent.futures.ThreadPoolExecutor(4) as ex:
+        objs = dict(ex.map(compile_one, srcs.items()))
+    if not _stale(LINK_OUT, list(objs.values()) + [lib, __file__]):
+        return LINK_OUT
+    shims = set(_defined(lib)) - {x for x in _defined(lib) if x.startswith("b200q_")}
+    linked = [objs["bolt_host"], objs["bolt_draft"]]
+    for name in ("bolt_kernels", "bolt_mma"):
+        mine = sorted(shims & set(_defined(objs[name])))
+        out = os.path.join(obj_dir, name + ".local.o")
+        r = subprocess.run(["objcopy", *[f"--localize-symbol={x}" for x in mine], objs[name], out],
+                           capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"objcopy failed on {name}:\n{r.stderr}")
+        linked.append(out)
+    cmd = [NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", LINK_OUT, *linked, "-L", PKG, "-lb200q",
+           "-lcuda", "-Xlinker", "-rpath=$ORIGIN/../../nemotron-3.5-bolt-tensorfold-dgx-spark_b200"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"link failed:\n{r.stderr}")
+    return LINK_OUT
+
+
+def _defined(path):
+    """the global text symbols an object or library defines (mangled)"""
+    dyn = ["-D"] if path.endswith(".so") else []
+    r = subprocess.run(["nm", *dyn, "--defined-only", path], capture_output=True, text=True, check=True)
+    return [f[2] for f in (l.split() for l in r.stdout.splitlines()) if len(f) == 3 and f[1] == "T"]
+
+
 if __name__ == "__main__":
     print(build())
     if "--ref" in sys.argv:
         print(build_ref())
+    if "--link" in sys.argv:
+        print(build_bolt_link())
