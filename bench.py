@@ -35,10 +35,12 @@ METRIC = "IQ2_XXS MoE decode GB/s"
 T, H, F, E, TOPK = 16, 4096, 2048, 128, 6
 LAYERS, BATCHES = 4, 8
 EXPERT_BYTES = 2 * (F * (H // 256) * 66)      # up [F][H] + down [H][F]: 4,325,376 B
-# DRAM bytes (read + write) of one captured decode_layer_k launch at config 2, per the ncu summary in profiles/
-# (None until captured for the current kernel)
-LAYER_TRAFFIC = None
-LAYER_TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum of one decode_layer_k launch at config 2"
+# DRAM bytes (read + write) of one captured decode_layer_k launch at config 2, per the ncu summary in profiles/:
+# 281,733,632 read + 4,721,152 written for a launch whose batch routes to 63 distinct experts (277,221,376
+# algorithmic bytes).  Traffic grows with the experts read, so a launch's traffic is that ratio times its bytes.
+LAYER_TRAFFIC_CAPTURED = (281_733_632 + 4_721_152, 277_221_376)
+LAYER_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one decode_layer_k launch at config 2 "
+                        "(63 distinct experts), scaled by the algorithmic bytes to the timed launches' mean")
 
 
 def config2():
@@ -701,7 +703,8 @@ def run_ours(args, rank, world, local_rank):
             "hbm_fraction": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "kernel": "decode_layer_k (the whole layer, one launch)",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": LAYER_TRAFFIC,
+                         "frac": round(achieved / peak, 4),
+                         "traffic": round(dom_bytes * LAYER_TRAFFIC_CAPTURED[0] / LAYER_TRAFFIC_CAPTURED[1]),
                          "traffic_source": LAYER_TRAFFIC_SOURCE,
                          "algorithmic_bytes": round(dom_bytes), "peak_kind": peak_kind,
                          "kernel_ms": round(dom_ms, 5)},
