@@ -265,8 +265,10 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
     own tokens.  decode: 16 tokens a rank, uniform placement, fixed-capacity exchange, shared expert on every rank;
     GB/s = the touched experts' bytes over all ranks (+ activations) / the slowest rank's step time.  prefill: 8192
     tokens a rank, Zipf(1.1) routing, LPT placement with the hottest experts split; TFLOPS over all ranks."""
-    from ep import ExpertParallelMoE, GraphedStep, LocalExperts, Placement, SharedExpert, slice_slab
+    from ep import ExpertParallelMoE, GraphedStep, LocalExperts, PeerDecodeMoE, Placement, SharedExpert, slice_slab
     dist = world > 1
+    # decode exchange: "peer" (NVLink peer stores and loads, b200q_ep_peer_decode) or "nccl" (all-to-alls)
+    exchange = os.environ.get("B200Q_EP_EXCHANGE", "peer")
     up_b, down_b = b200q.iq2_bytes(F, H), b200q.iq2_bytes(H, F)
 
     def barrier():
@@ -287,11 +289,15 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
     layers, ex_ms = [], []
     for L in range(LAYERS):
         up, down, su, sd = full_layer(b200q, device, L)
-        ex = LocalExperts(slice_slab(up, loc, up_b), slice_slab(down, loc, down_b), len(loc), H, F)
+        if exchange == "peer":
+            moe = PeerDecodeMoE(pl, rank, world, H, F, T, TOPK, slice_slab(up, loc, up_b),
+                                slice_slab(down, loc, down_b), su, sd, device=device)
+        else:
+            ex = LocalExperts(slice_slab(up, loc, up_b), slice_slab(down, loc, down_b), len(loc), H, F)
+            moe = ExpertParallelMoE(pl, rank, world, H, TOPK, ex.decode,
+                                    shared_fn=SharedExpert(su, sd, H, F, T, device), layout="capacity", device=device)
+            moe.ex = ex
         del up, down
-        moe = ExpertParallelMoE(pl, rank, world, H, TOPK, ex.decode, shared_fn=SharedExpert(su, sd, H, F, T, device),
-                                layout="capacity", device=device)
-        moe.ex = ex
         layers.append(moe)
     torch.cuda.synchronize()
     xs_h, ls_h = make_batches(rank, device)
@@ -302,6 +308,8 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
     lin = torch.empty(T, E, dtype=torch.bfloat16, device=device)
 
     def eager_on(L, x, lg):
+        if exchange == "peer":
+            return layers[L](x, lg)
         ridx, rw = b200q.k_route(lg, TOPK)
         return layers[L](x, ridx, rw)
 
@@ -361,7 +369,31 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
         e.record()
     acc = np.zeros(3)
     nprof = min(steps, 50)
-    for i in range(nprof):   # eager, with events between the pieces
+
+    def alone(fn):
+        """one piece of a step timed alone: every rank ready first, the GPU kept busy while the host enqueues (no
+        launch gap inside the events)"""
+        barrier()
+        torch.cuda.synchronize()
+        torch.cuda._sleep(400000)
+        evs[4].record()
+        fn()
+        evs[5].record()
+        torch.cuda.synchronize()
+        return evs[4].elapsed_time(evs[5])
+
+    for i in range(nprof if exchange == "peer" else 0):
+        # after a full step every flag holds its epoch, so the local experts (with their flags) and the combine run
+        # again without waiting; the dispatch alone publishes the next epoch on every rank, and the next full step
+        # goes on from there
+        L, b = (warmup + i) % LAYERS, (warmup + i) % BATCHES
+        layers[L](xs[b], ls[b])
+        t_exp = alone(lambda: layers[L](xs[b], ls[b], phases=2))
+        t_comb = alone(lambda: layers[L](xs[b], ls[b], phases=4))
+        t_disp = alone(lambda: layers[L](xs[b], ls[b], phases=1))
+        acc += [t_disp, t_comb, t_exp]
+    barrier()
+    for i in range(nprof if exchange != "peer" else 0):   # eager, with events between the pieces
         moe = layers[(warmup + i) % LAYERS]
         moe.timing = evs[:4]
         inner = moe.expert_fn
@@ -394,15 +426,38 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_ms(ev0.elapsed_time(ev1))
+    if exchange == "peer" and dist:   # each piece's slowest rank
+        t = torch.tensor(acc, device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        acc = t.cpu().numpy()
+    errors = [m.error() for m in layers] if exchange == "peer" else []
+    if exchange == "peer":
+        pieces = {"exchange": "peer memory (NVLink stores and loads, no collective)",
+                  "dispatch_ms": round(float(acc[0]), 5),
+                  "combine_ms": round(float(acc[1]), 5),
+                  "comm_ms": round(float(acc[0] + acc[1]), 5),
+                  "comm_note": "each piece timed alone on every rank (no waiting on other ranks), the slowest rank's: "
+                               "dispatch = routing + the int8 row stores to the owners + the flags; local experts = "
+                               "prologue + fused up/down GEMVs + the flags; combine = the owners' output rows loaded "
+                               "and summed.  The step (CUDA graph) minus their sum is the ranks' waiting on one "
+                               "another and the launch overlap",
+                  "peer_errors": int(np.bitwise_or.reduce(errors)) if errors else 0}
+    else:
+        pieces = {"exchange": "NCCL all_to_all_single, fixed capacity", "layout": "capacity",
+                  "dispatch_plus_shared_ms": round(float(acc[0]), 5), "return_ms": round(float(acc[1]), 5),
+                  "comm_ms": round(float(acc[0] + acc[1]), 5)}
     res["decode"] = {"gbs": round(nbytes / (ms * 1e-3) / 1e9, 2), "ms_per_step": round(ms / steps, 5),
-                     "steps": steps, "experts_per_rank": len(loc), "layout": "capacity",
-                     "dispatch_plus_shared_ms": round(float(acc[0]), 5), "return_ms": round(float(acc[1]), 5),
+                     "steps": steps, "experts_per_rank": len(loc), **pieces,
                      "local_experts_ms": round(float(acc[2]), 5), "step_bytes_mean": float(np.mean(step_bytes_b)),
                      "rank_local_expert_bytes": float(np.mean(rank_hits)) * EXPERT_BYTES,
                      "e2e_gbs": round(nbytes / (e2e_ms * 1e-3) / 1e9, 2),
                      "h2d_bytes_per_step": T * H * 2 + T * E * 2, "d2h_bytes_per_step": T * H * 4,
                      "cuda_graph": graphed}
-    del graphs, layers
+    del graphs
+    if exchange == "peer":   # collective: every rank unmaps, then frees
+        for m in layers:
+            m.close()
+    del layers
     import gc
     gc.collect()
     torch.cuda.synchronize()
@@ -542,7 +597,9 @@ def run_ep(args, rank, world, local_rank):
             "warmup": args.warmup, "ms_per_step": d["ms_per_step"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": "BASELINE config 5 (decode): the config-2 MoE layer expert-parallel over N GPUs, "
-                                   "128/N experts a GPU, 16 tokens a GPU, NCCL all-to-all dispatch and combine (bf16)",
+                                   "128/N experts a GPU, 16 tokens a GPU, token rows dispatched (int8, the rows the "
+                                   "GEMVs read) and outputs combined (bf16) over NVLink peer memory (NCCL all-to-alls "
+                                   "of bf16 rows with B200Q_EP_EXCHANGE=nccl)",
                        "tokens_per_gpu": T, "hidden": H, "experts": E, "topk": TOPK, "ffn": F, "shared_experts": 1,
                        "l2": f"{LAYERS} rotating layer copies and {BATCHES} token batches",
                        "parallelism": f"ep{world}"},
@@ -554,7 +611,8 @@ def run_ep(args, rank, world, local_rank):
             "cpu_baseline_note": "the CPU oracle is timed at N=1 only",
             "e2e": {"value": d["e2e_gbs"], "unit": "GB/s", "h2d_bytes_per_step": d["h2d_bytes_per_step"],
                     "d2h_bytes_per_step": d["d2h_bytes_per_step"]},
-            "gpu_launches": 9 * args.steps,
+            # peer exchange: dispatch, expert prologue, fused up/down GEMV, combine a step
+            "gpu_launches": (4 if d.get("exchange", "").startswith("peer") else 9) * args.steps,
             "clocks": clk.summary() if clk else None,
             "ep": r,
         }

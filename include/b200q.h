@@ -260,6 +260,46 @@ int b200q_ep_pack(const void* x, int x_dtype, int T, int H, const int* ridx, int
 int b200q_ep_combine(const void* back, int back_dtype, int ldb, const int* slot, const float* rw, const float* shared,
                      int T, int topk, int H, void* out, int out_dtype, void* stream);
 
+/* The expert-parallel decode step with its exchange over NVLink peer memory (no counterpart in libbolt, which is
+ * single-GPU; the layer is the MoE block of enqueue_block, bolt_host.cu:665-720).  Every rank holds one region of
+ * b200q_ep_peer_region_bytes (allocated by b200q_peer_alloc, zeroed), exports it (b200q_peer_export), and maps every
+ * other rank's (b200q_peer_open); `peers` is a DEVICE array of the world regions as mapped in this process (its own
+ * at [rank], also passed as `region`).  Ranks must be on distinct GPUs of one box with peer access.
+ * A step is four launches on `stream` (phases: bit 0 the first, bit 1 the second and third, bit 2 the fourth; 7 all):
+ *   1. route x's tokens (logits [T][E], route_k's arithmetic), store each pair's token row into its owner's region as
+ *      the int8-per-32 row the GEMVs read (b200q_quant_rows' bytes; owner d = dest[e * max_rep + t % nrep[e]], local
+ *      expert lidx[...] there) and this rank's own rows for the shared expert, then publish the step in every owner's
+ *      flags;
+ *   2, 3. wait until every sender has published, then the local experts over the received rows
+ *      (b200q_moe_experts_decode's two launches: up [n_local + 1] x [F][H], down [n_local + 1] x [H][F], packed rt32,
+ *      the shared expert LAST), outputs in ret_dtype in this rank's region; the GEMV launch's last CTA publishes
+ *      them in every sender's flags;
+ *   4. wait for every owner, then out[t] = sum over k in order of rw[t][k] * (pair (t, k)'s output row, read from
+ *      its owner) (fma), + the shared expert's row; out [T][H] fp32 or bf16.
+ * With ret_dtype fp32 the result is b200q_moe_decode's to the bit (the same int8 rows, GEMVs and combine order).
+ * discard >= every rank's n_local + 1.  T * topk <= 1024, world * T * topk + T <= 4096, world <= 64.
+ * state: b200q_ep_peer_state_bytes, zeroed once (the step's epoch, error bits); workspace:
+ * b200q_ep_peer_workspace_bytes, 256-byte aligned.  ridx_out / rw_out (optional) receive the routing.
+ * Every wait is bounded (4 s): b200q_ep_peer_error returns the bits a step recorded (bit 0: senders did not arrive,
+ * bit 1: owners did not arrive, bit 2: a routing table entry out of range); synchronous, clear != 0 resets them.
+ * Once a bit is set, later waits give up after a few polls until it is cleared. */
+size_t b200q_ep_peer_region_bytes(int world, int T, int H, int topk, int ret_dtype);
+size_t b200q_ep_peer_state_bytes(int T, int topk);
+size_t b200q_ep_peer_workspace_bytes(int world, int T, int H, int F, int topk, int n_local);
+int b200q_peer_alloc(size_t bytes, void** ptr);
+int b200q_peer_free(void* ptr);
+size_t b200q_peer_handle_bytes(void);
+int b200q_peer_export(void* ptr, void* handle);
+int b200q_peer_open(const void* handle, void** ptr);
+int b200q_peer_close(void* ptr);
+int b200q_ep_peer_error(void* state, int clear);
+int b200q_ep_peer_decode(const void* x, int x_dtype, const void* logits, int logits_dtype, int T, int H, int F, int E,
+                         int topk, int route, const float* bias, float scale, const int* dest, const int* lidx,
+                         const int* nrep, int max_rep, void* region, void* const* peers, int world, int rank,
+                         int n_local, int discard, const void* up, const void* down, int ret_dtype, void* state,
+                         void* workspace, size_t workspace_bytes, void* out, int out_dtype, int* ridx_out,
+                         float* rw_out, int phases, void* stream);
+
 /* The decode MoE layer without a caller-provided workspace, for callers that cannot allocate device memory (a host
  * whose allocator owns the GPU's memory, a plugin that receives only tensors, a loop that must not take cudaMalloc's
  * implicit synchronisation).  No counterpart in the reference: libbolt allocates its own scratch at bolt_open.

@@ -59,6 +59,16 @@ def lib():
                                                vp]),
             "b200q_ep_pack": (i32, [vp, i32, i32, i32, vp, i32, vp, vp, vp, i32, i32, i32, i32, vp, i32, i32, vp, vp]),
             "b200q_ep_combine": (i32, [vp, i32, i32, vp, vp, vp, i32, i32, i32, vp, i32, vp]),
+            "b200q_ep_peer_region_bytes": (sz, [i32, i32, i32, i32, i32]),
+            "b200q_ep_peer_state_bytes": (sz, [i32, i32]),
+            "b200q_ep_peer_workspace_bytes": (sz, [i32, i32, i32, i32, i32, i32]),
+            "b200q_peer_alloc": (i32, [sz, ctypes.POINTER(vp)]), "b200q_peer_free": (i32, [vp]),
+            "b200q_peer_handle_bytes": (sz, []), "b200q_peer_export": (i32, [vp, ctypes.c_char_p]),
+            "b200q_peer_open": (i32, [ctypes.c_char_p, ctypes.POINTER(vp)]), "b200q_peer_close": (i32, [vp]),
+            "b200q_ep_peer_error": (i32, [vp, i32]),
+            "b200q_ep_peer_decode": (i32, [vp, i32, vp, i32, i32, i32, i32, i32, i32, i32, vp, f32, vp, vp, vp, i32,
+                                           vp, vp, i32, i32, i32, i32, vp, vp, i32, vp, vp, sz, vp, i32, vp, vp, i32,
+                                           vp]),
             "b200q_moe_decode": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, f32, vp, i32, vp, sz,
                                        vp, vp, vp, vp]),
             "b200q_synth_iq2_host": (None, [ctypes.c_uint64, i64, vp]),
@@ -321,6 +331,78 @@ def ep_combine(back, slot, rw, topk, shared=None, out_dtype=torch.float32):
     _check(lib().b200q_ep_combine(_p(back), _dtype_code(back), back.stride(0), _p(slot), _p(rwc), _p(shared), T,
                                   topk, H, _p(out), _dtype_code(out), _s()), "ep_combine")
     return out
+
+
+class PeerRegion:
+    """One rank's region of the expert-parallel exchange over peer memory (b200q_ep_peer_decode): a zeroed device
+    allocation of its own (not the caching allocator's: a CUDA IPC handle names a whole allocation), exported to the
+    other ranks of the box, and the other ranks' regions mapped into this process.  unmap() then free(): the caller
+    makes sure that no rank still uses a mapping when it is unmapped and that every rank has unmapped this region before
+    it is freed (ep.PeerDecodeMoE.close puts barriers between the steps)."""
+
+    def __init__(self, nbytes, device):
+        p = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            _check(lib().b200q_peer_alloc(nbytes, ctypes.byref(p)), "peer_alloc")
+        self.ptr, self.nbytes, self.device = p.value, nbytes, device
+        self.opened = []
+
+    def handle(self):
+        """the CUDA IPC handle of this region (bytes)"""
+        buf = ctypes.create_string_buffer(lib().b200q_peer_handle_bytes())
+        _check(lib().b200q_peer_export(self.ptr, buf), "peer_export")
+        return buf.raw
+
+    def open(self, handle):
+        """map another rank's region (its handle()) into this process; -> its device address here"""
+        p = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _check(lib().b200q_peer_open(handle, ctypes.byref(p)), "peer_open")
+        self.opened.append(p.value)
+        return p.value
+
+    def unmap(self):
+        """unmap the other ranks' regions"""
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize()
+            for q in self.opened:
+                lib().b200q_peer_close(q)
+        self.opened = []
+
+    def free(self):
+        """free this rank's region (after every other rank has unmapped it)"""
+        with torch.cuda.device(self.device):
+            if self.ptr:
+                lib().b200q_peer_free(self.ptr)
+        self.ptr = None
+
+
+def ep_peer_decode(x, logits, topk, dest, lidx, nrep, region, peers, world, rank, n_local, discard, up, down, state,
+                   workspace, H, F, ret_dtype=torch.bfloat16, out=None, out_dtype=torch.float32,
+                   route=ROUTE_SOFTMAX, bias=None, scale=1.0, ridx=None, rw=None, phases=7):
+    """b200q_ep_peer_decode: one rank's expert-parallel decode step with the exchange over peer memory (token rows go
+    out as int8 rows, outputs come back in ret_dtype).
+    x [T][H], logits [T][E] (bf16 or fp32); dest / lidx [E][max_rep], nrep [E] int32; region: this rank's PeerRegion
+    address; peers: int64 device tensor of every rank's region address in this process; up / down: the local slabs with
+    the shared expert last; state: int32 device tensor (b200q_ep_peer_state_bytes, zeroed once); workspace: (address,
+    bytes), 256-byte aligned.  -> out [T][H]"""
+    _dev(x, "x")
+    _dev(logits, "logits")
+    T, E = logits.shape
+    if out is None:
+        out = torch.empty(T, H, dtype=out_dtype, device=x.device)
+    _check(lib().b200q_ep_peer_decode(_p(x), _dtype_code(x), _p(logits), _dtype_code(logits), T, H, F, E, topk, route,
+                                      _p(bias), float(scale), _p(dest), _p(lidx), _p(nrep), dest.shape[1], region,
+                                      _p(peers), world, rank, n_local, discard, _p(up), _p(down),
+                                      BF16 if ret_dtype == torch.bfloat16 else F32, _p(state), workspace[0],
+                                      workspace[1], _p(out), _dtype_code(out), _p(ridx), _p(rw), phases, _s()),
+           "ep_peer_decode")
+    return out
+
+
+def ep_peer_error(state, clear=True):
+    """the error bits b200q_ep_peer_decode's bounded waits recorded in state (0: none); synchronous"""
+    return lib().b200q_ep_peer_error(_p(state), 1 if clear else 0)
 
 
 # -------------------------------------------------------------------------------------------------------------

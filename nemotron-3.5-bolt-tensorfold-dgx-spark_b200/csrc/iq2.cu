@@ -728,123 +728,6 @@ __device__ __forceinline__ bool wait_at_least(const int* p, int v, int ctr) {
     return true;
 }
 
-// Softmax top-k of one token over bf16 logits, E <= 128 (a lane holds logits lane + 32 j), by a warp: route_token's
-// selection, weights and rounding (larger logit first, ties to the lower index; w = exp(z - max) / the sum over the
-// picked, in pick order), with each pick one redux over packed keys: a bf16 logit maps to 16 bits that order as its
-// value, above 16 bits that order as the reversed index.
-__device__ __forceinline__ void route_softmax_bf16(const __nv_bfloat16* lg, int E, int topk, int t, int lane,
-                                                   int* ridx, float* rw, int* ridx_s) {
-    uint32_t key[4];
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-        const int i = lane + 32 * j;
-        uint32_t b = i < E ? (uint32_t)__bfloat16_as_ushort(lg[(size_t)t * E + i]) : 0u;
-        if (b == 0x8000u) b = 0u;   // -0 ties with +0, as the float compare has it
-        const uint32_t ord = (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
-        key[j] = i < E ? (ord << 16) | (0xFFFFu - (uint32_t)i) : 0u;
-    }
-    float mx = 0.f, sum = 0.f, picked = 0.f;
-    int pick_i = 0;
-    for (int kk = 0; kk < topk; kk++) {
-        const uint32_t best = __reduce_max_sync(0xffffffffu, max(max(key[0], key[1]), max(key[2], key[3])));
-        const int bi = (int)(0xFFFFu - (best & 0xFFFFu));
-        const uint32_t o = best >> 16;
-        const uint32_t b = (o & 0x8000u) ? (o & 0x7FFFu) : (~o & 0xFFFFu);
-        const float z = __uint_as_float(b << 16);
-        if (kk == 0) mx = z;   // the first pick is the largest logit
-        const float pv = expf(z - mx);
-        sum += pv;
-        if (lane == kk) { picked = pv; pick_i = bi; }
-#pragma unroll
-        for (int j = 0; j < 4; j++)
-            if (lane + 32 * j == bi) key[j] = 0u;
-    }
-    if (lane < topk) {
-        ridx[t * topk + lane] = pick_i;
-        ridx_s[t * topk + lane] = pick_i;
-        rw[t * topk + lane] = picked / sum;
-    }
-}
-
-// sum of a[0 .. n) (shared memory, 16-byte aligned): four words a load, several loads in flight
-__device__ __forceinline__ int smem_sum(const int* a, int n) {
-    const int4* v = reinterpret_cast<const int4*>(a);
-    int s0 = 0, s1 = 0;
-    int j = 0;
-#pragma unroll 4
-    for (; j + 8 <= n; j += 8) {
-        const int4 x = v[j >> 2], y = v[(j >> 2) + 1];
-        s0 += (x.x + x.y) + (x.z + x.w);
-        s1 += (y.x + y.y) + (y.z + y.w);
-    }
-    for (; j < n; j++) s0 += a[j];
-    return s0 + s1;
-}
-
-// #{j < n : a[j] > c, or a[j] == c and j < self} (ties to the lower index): the rank of element `self` of value c in
-// an order by value, largest first (desc) or smallest first (!desc)
-template <bool DESC>
-__device__ __forceinline__ int smem_rank(const int* a, int n, int c, int self) {
-    const int4* v = reinterpret_cast<const int4*>(a);
-    int r = 0;
-    int j = 0;
-    auto before = [&](int x, int idx) { return (DESC ? x > c : x < c) | ((x == c) & (idx < self)); };
-#pragma unroll 4
-    for (; j + 4 <= n; j += 4) {
-        const int4 x = v[j >> 2];
-        r += before(x.x, j) + before(x.y, j + 1) + before(x.z, j + 2) + before(x.w, j + 3);
-    }
-    for (; j < n; j++) r += before(a[j], j);
-    return r;
-}
-
-// The layer's grouping and GEMV schedule from the routing in shared memory, every thread of the CTA, each output by
-// a direct count (the arrays are small): counts by expert (slot E: the shared expert's `extra` rows); offsets; the
-// ids of each slot in increasing pair order (group_pairs' order); the slots by count, largest first, ties to the lower
-// index (iq2_schedule_slots' order) with the exclusive prefix of their batches; and the down phase's batch order of
-// iq2_schedule_batches.  tmp: kLayerIds ints.  All arrays 16-byte aligned.
-__device__ void layer_schedule(const int* ridx_s, int pairs, int E, int extra, int G, int W, int* s_cnt, int* s_offs,
-                               int* s_ord, int* s_order, int* s_bpre, int* s_dord, int* tmp) {
-    const int tid = threadIdx.x, nth = blockDim.x;
-    const int nslots = E + (extra ? 1 : 0);
-    for (int i = tid; i < E; i += nth) s_cnt[i] = 0;
-    __syncthreads();
-    for (int p = tid; p < pairs; p += nth) atomicAdd(&s_cnt[ridx_s[p]], 1);
-    if (tid == 0 && extra) s_cnt[E] = extra;
-    __syncthreads();
-    XTRACE(11);
-    for (int e = tid; e <= nslots; e += nth) s_offs[e] = smem_sum(s_cnt, e);
-    for (int s = tid; s < nslots; s += nth) s_order[smem_rank<true>(s_cnt, nslots, s_cnt[s], s)] = s;
-    __syncthreads();
-    XTRACE(12);
-    for (int p = tid; p < pairs; p += nth) {
-        const int e = ridx_s[p];
-        int r = 0;
-#pragma unroll 8
-        for (int q = 0; q < p; q++) r += ridx_s[q] == e;
-        s_ord[s_offs[e] + r] = p;
-    }
-    for (int i = tid; i < extra; i += nth) s_ord[pairs + i] = pairs + i;
-    for (int i = tid; i < nslots; i += nth) tmp[i] = (s_cnt[s_order[i]] + kIq2UnitTok - 1) / kIq2UnitTok;
-    __syncthreads();
-    XTRACE(14);
-    for (int i = tid; i <= nslots; i += nth) s_bpre[i] = smem_sum(tmp, i);
-    __syncthreads();
-    XTRACE(15);
-    const int nb = s_bpre[nslots];
-    // each batch's key: first-wave batches (all up units numbered below W) before the rest, fewer tokens first
-    for (int i = tid; i < nslots; i += nth) {
-        const int c = s_cnt[s_order[i]];
-        for (int bidx = s_bpre[i]; bidx < s_bpre[i + 1]; bidx++) {
-            const int ntok = min(kIq2UnitTok, c - kIq2UnitTok * (bidx - s_bpre[i]));
-            tmp[bidx] = ((bidx + 1) * G - 1 >= W ? 4 : 0) + ntok;
-        }
-    }
-    __syncthreads();
-    for (int bidx = tid; bidx < nb; bidx += nth) s_dord[smem_rank<false>(tmp, nb, tmp[bidx], bidx)] = bidx;
-    __syncthreads();
-}
-
 // The layer's prologue, every thread of the CTA.  After the wait for the preceding launch, the CTA quantises its
 // share of x to int8 rows (a warp per 32-group) and counts itself done; then it routes every token, groups the pairs
 // by expert and computes the GEMVs' schedule on its own, into shared memory (every CTA gets the same bytes; only CTA 0
@@ -1098,6 +981,13 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, const GemvArgs& b, 
         if (last) {
 #pragma unroll
             for (int i = 0; i < 8; i++) g_unit_ctr[ctr][i] = 0;
+            // every CTA wrote its outputs before its count (fence, then the add); this CTA's system-scope fence (the
+            // acquire of those counts, cumulative) orders them before the flags that publish them to other ranks
+            if (a.done_base) {
+                const int e = *reinterpret_cast<volatile const int*>(a.done_epoch);
+                fence_acq_rel_sys();
+                for (int j = 0; j < a.done_n; j++) st_relaxed_sys(reinterpret_cast<int*>(a.done_base[j] + a.done_off), e);
+            }
         }
         s_queue[0] = last;
     }

@@ -40,6 +40,13 @@ struct GemvArgs {
     // 1: counts, offsets, order and sched were written by an earlier launch on the stream than the one this launch
     // follows, so the kernel takes its schedule and first unit before waiting for that launch
     int sched_early;
+    // Optional (the expert-parallel exchange over peer memory): once every CTA is done, the last one stores
+    // *done_epoch into done_n flags, flag j at done_base[j] + done_off bytes (other GPUs' memory), after one
+    // system-scope fence, so that those ranks may read this launch's outputs.
+    unsigned char* const* done_base;
+    size_t done_off;
+    int done_n;
+    const int* done_epoch;
 };
 
 constexpr int kIq2UnitTok = 3;   // tokens a GEMV work unit dots at most (a slot's tokens come in batches of this many)
@@ -148,6 +155,86 @@ __device__ inline void iq2_schedule_batches(const int* cnt, const int* order, co
         const unsigned m = __match_any_sync(0xffffffffu, key);
         if (key < 8) dorder[tmp[c * 8 + key] + __popc(m & ((1u << lane) - 1u))] = bidx;
     }
+}
+
+// sum of a[0 .. n) (shared memory, 16-byte aligned): four words a load, several loads in flight
+__device__ __forceinline__ int smem_sum(const int* a, int n) {
+    const int4* v = reinterpret_cast<const int4*>(a);
+    int s0 = 0, s1 = 0;
+    int j = 0;
+#pragma unroll 4
+    for (; j + 8 <= n; j += 8) {
+        const int4 x = v[j >> 2], y = v[(j >> 2) + 1];
+        s0 += (x.x + x.y) + (x.z + x.w);
+        s1 += (y.x + y.y) + (y.z + y.w);
+    }
+    for (; j < n; j++) s0 += a[j];
+    return s0 + s1;
+}
+
+// #{j < n : a[j] > c, or a[j] == c and j < self} (ties to the lower index): the rank of element `self` of value c in
+// an order by value, largest first (desc) or smallest first (!desc)
+template <bool DESC>
+__device__ __forceinline__ int smem_rank(const int* a, int n, int c, int self) {
+    const int4* v = reinterpret_cast<const int4*>(a);
+    int r = 0;
+    int j = 0;
+    auto before = [&](int x, int idx) { return (DESC ? x > c : x < c) | ((x == c) & (idx < self)); };
+#pragma unroll 4
+    for (; j + 4 <= n; j += 4) {
+        const int4 x = v[j >> 2];
+        r += before(x.x, j) + before(x.y, j + 1) + before(x.z, j + 2) + before(x.w, j + 3);
+    }
+    for (; j < n; j++) r += before(a[j], j);
+    return r;
+}
+
+// The layer's grouping and GEMV schedule from the routing in shared memory, every thread of the CTA, each output by
+// a direct count (the arrays are small): counts by expert (slot E: the shared expert's `extra` rows); offsets; the
+// ids of each slot in increasing pair order (group_pairs' order); the slots by count, largest first, ties to the lower
+// index (iq2_schedule_slots' order) with the exclusive prefix of their batches; and the down phase's batch order of
+// iq2_schedule_batches.  An id whose expert is outside 0 .. E - 1 is left out.  tmp: an int a batch (kLayerIds in
+// the one-launch layer).  s_cnt, s_bpre and tmp 16-byte aligned shared memory; s_ord and s_dord may be global.
+__device__ inline void layer_schedule(const int* ridx_s, int pairs, int E, int extra, int G, int W, int* s_cnt, int* s_offs,
+                               int* s_ord, int* s_order, int* s_bpre, int* s_dord, int* tmp) {
+    const int tid = threadIdx.x, nth = blockDim.x;
+    const int nslots = E + (extra ? 1 : 0);
+    for (int i = tid; i < E; i += nth) s_cnt[i] = 0;
+    __syncthreads();
+    for (int p = tid; p < pairs; p += nth) {   // an expert outside 0 .. E - 1 marks an id to leave out
+        const int e = ridx_s[p];
+        if ((unsigned)e < (unsigned)E) atomicAdd(&s_cnt[e], 1);
+    }
+    if (tid == 0 && extra) s_cnt[E] = extra;
+    __syncthreads();
+    for (int e = tid; e <= nslots; e += nth) s_offs[e] = smem_sum(s_cnt, e);
+    for (int s = tid; s < nslots; s += nth) s_order[smem_rank<true>(s_cnt, nslots, s_cnt[s], s)] = s;
+    __syncthreads();
+    for (int p = tid; p < pairs; p += nth) {
+        const int e = ridx_s[p];
+        if ((unsigned)e >= (unsigned)E) continue;
+        int r = 0;
+#pragma unroll 8
+        for (int q = 0; q < p; q++) r += ridx_s[q] == e;
+        s_ord[s_offs[e] + r] = p;
+    }
+    for (int i = tid; i < extra; i += nth) s_ord[pairs + i] = pairs + i;
+    for (int i = tid; i < nslots; i += nth) tmp[i] = (s_cnt[s_order[i]] + kIq2UnitTok - 1) / kIq2UnitTok;
+    __syncthreads();
+    for (int i = tid; i <= nslots; i += nth) s_bpre[i] = smem_sum(tmp, i);
+    __syncthreads();
+    const int nb = s_bpre[nslots];
+    // each batch's key: first-wave batches (all up units numbered below W) before the rest, fewer tokens first
+    for (int i = tid; i < nslots; i += nth) {
+        const int c = s_cnt[s_order[i]];
+        for (int bidx = s_bpre[i]; bidx < s_bpre[i + 1]; bidx++) {
+            const int ntok = min(kIq2UnitTok, c - kIq2UnitTok * (bidx - s_bpre[i]));
+            tmp[bidx] = ((bidx + 1) * G - 1 >= W ? 4 : 0) + ntok;
+        }
+    }
+    __syncthreads();
+    for (int bidx = tid; bidx < nb; bidx += nth) s_dord[smem_rank<false>(tmp, nb, tmp[bidx], bidx)] = bidx;
+    __syncthreads();
 }
 
 // epi: 0 store, 1 relu^2, 2 relu^2 + int8 per 32, 3 chunk dots.  maxcnt bounds a slot's ids (the staging size).

@@ -139,36 +139,60 @@ __global__ void __launch_bounds__(512) moe_prep_k(const void* __restrict__ x, co
 }
 
 // ---------------------------------------------------------------------------------------------------------
-// the expert-parallel prologue over a rank's received rows, one launch: block 0 groups the rows by their local expert
-// (lidx; an index outside 0 .. n_local - 1 is padding, grouped into slot n_local and never computed) and orders the
-// GEMVs' slots; the other blocks write the int8 rows.
+// the expert-parallel prologue over a rank's received rows, one launch.  Block 0 groups the rows by their local expert
+// (lidx; an index outside 0 .. n_local - 1 is padding, left out and never computed) and orders the GEMVs' slots and
+// the down phase's batches, with the one-launch layer's direct counts (layer_schedule: the results of group_pairs,
+// iq2_schedule_slots and iq2_schedule_batches); the other blocks (none when rows is NULL: the rows came in int8 form)
+// write the int8 rows of the rows that are not padding.
+// With peer rows (the exchange over peer memory, ep_peer.cu), every block first waits until the wait_n senders'
+// flags in wait_flags have reached *wait_epoch (bounded; a timeout sets bit 0 of *wait_err).
 // ---------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(512) moe_local_prep_k(const void* __restrict__ rows, int dtype, int ldr, int R, int H,
                                                         const int* __restrict__ lidx, int lidx_stride, int n_local,
                                                         int* __restrict__ counts, int* __restrict__ offsets,
                                                         int* __restrict__ order, int8_t* __restrict__ xq,
                                                         float* __restrict__ xs, int* __restrict__ sched,
-                                                        int* __restrict__ ready, int F, int wave) {
+                                                        int* __restrict__ ready, int F, int wave, const int* wait_flags,
+                                                        int wait_n, const int* wait_epoch, int* wait_err) {
     pdl_wait();
-    __shared__ int ridx_s[4096], place_s[4096], run_s[512], warp_s[16], cnt_s[513];   // R <= 4096
+    if (wait_flags) {
+        if (threadIdx.x == 0) {
+            wait_epochs(wait_flags, wait_n, *wait_epoch, wait_err, 0);
+            asm volatile("fence.proxy.async.global;" ::: "memory");   // the GEMVs read the rows by bulk copies
+        }
+        __syncthreads();
+    }
+    // R <= 4096, n_local <= 511
+    __shared__ __align__(16) int ridx_s[4096], tmp_s[4096], cnt_s[516], offs_s[516], order_s[516], bpre_s[516];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (blockIdx.x == 0) {
         for (int i = threadIdx.x; i < R; i += blockDim.x) ready[i] = 0;
         for (int i = threadIdx.x; i < R; i += blockDim.x) {
             const int l = lidx[(size_t)i * lidx_stride];
-            ridx_s[i] = (l < 0 || l > n_local) ? n_local : l;
+            ridx_s[i] = (l < 0 || l >= n_local) ? n_local : l;   // padding: left out of the schedule
         }
         __syncthreads();
-        group_pairs(ridx_s, R, n_local + 1, 0, counts, offsets, order, place_s, run_s, warp_s, cnt_s);
-        __syncthreads();
-        iq2_schedule_slots(cnt_s, n_local, sched, sched + n_local, ridx_s);
-        __syncthreads();
-        iq2_schedule_batches(cnt_s, sched, sched + n_local, n_local, F >> 5, wave, sched + 2 * n_local + 1, place_s);
-    } else {
+        // counts by local expert, offsets, the ids of each expert in increasing row order (straight to `order`), the
+        // experts by count with their batch prefix, and the down phase's batch order (straight to `sched`)
+        layer_schedule(ridx_s, R, n_local, 0, F >> 5, wave, cnt_s, offs_s, order, order_s, bpre_s,
+                       sched + 2 * n_local + 1, tmp_s);
+        for (int e = threadIdx.x; e <= n_local; e += blockDim.x) {
+            if (e < n_local) {
+                counts[e] = cnt_s[e];
+                sched[e] = order_s[e];
+            } else {
+                counts[e] = R - offs_s[e];   // the padding rows
+            }
+            offsets[e] = offs_s[e];
+            sched[n_local + e] = bpre_s[e];
+        }
+    } else if (rows) {
+        // a warp a (row, 32-group), grid-stride; padding rows are skipped
         const int groups = H >> 5;
-        const int gw = (blockIdx.x - 1) * 16 + warp;
-        if (gw < R * groups) {
+        for (int gw = (blockIdx.x - 1) * 16 + warp; gw < R * groups; gw += (gridDim.x - 1) * 16) {
             const int r = gw / groups, g = gw - r * groups;
+            const int l = lidx[(size_t)r * lidx_stride];
+            if (l < 0 || l >= n_local) continue;
             const float v = load_act(rows, dtype, (size_t)r * ldr + g * 32 + lane);
             quant_group(v, lane, xq + (size_t)r * H + g * 32, xs + (size_t)r * (H >> 5) + g);
         }
@@ -342,40 +366,61 @@ size_t b200q_moe_experts_workspace_bytes(int R, int H, int F, int n_local) {
 int b200q_moe_experts_decode(const void* rows, int rows_dtype, int ldr, int R, int H, int F, const int* lidx,
                              int lidx_stride, int n_local, const void* up, const void* down, void* y, int y_dtype,
                              int ldy, void* workspace, size_t workspace_bytes, void* stream) {
+    return b200q::experts_decode(rows, rows_dtype, ldr, R, H, F, lidx, lidx_stride, n_local, up, down, y, y_dtype, ldy,
+                                 workspace, workspace_bytes, stream, nullptr);
+}
+
+}  // extern "C"
+
+int b200q::experts_decode(const void* rows, int rows_dtype, int ldr, int R, int H, int F, const int* lidx,
+                          int lidx_stride, int n_local, const void* up, const void* down, void* y, int y_dtype, int ldy,
+                          void* workspace, size_t workspace_bytes, void* stream, const ExpertsPeer* peer) {
+    const bool given = peer && peer->xq;   // the rows come in int8 form
     if (R < 0 || R > 4096 || n_local <= 0 || n_local > 511 || !iq2_shape_ok(F, H) || !iq2_shape_ok(H, F) ||
-        (rows_dtype != B200Q_F32 && rows_dtype != B200Q_BF16) || (y_dtype != B200Q_F32 && y_dtype != B200Q_BF16))
+        (!given && rows_dtype != B200Q_F32 && rows_dtype != B200Q_BF16) ||
+        (y_dtype != B200Q_F32 && y_dtype != B200Q_BF16))
         return B200Q_EINVAL;
     if (R == 0) return B200Q_OK;
-    if (!rows || !lidx || lidx_stride < 1 || !up || !down || !y || !workspace || ldr < H || ldy < H ||
-        ((uintptr_t)workspace & 255) || ((uintptr_t)up & 15) || ((uintptr_t)down & 15))
+    if ((!given && (!rows || ldr < H)) ||
+        (given && (!peer->xs || ((uintptr_t)peer->xq & 15) || ((uintptr_t)peer->xs & 15))) || !lidx ||
+        lidx_stride < 1 || !up || !down || !y || !workspace || ldy < H || ((uintptr_t)workspace & 255) ||
+        ((uintptr_t)up & 15) || ((uintptr_t)down & 15))
         return B200Q_EINVAL;
     ExpertsWs w = experts_ws((char*)workspace, R, H, F, n_local);
     if (workspace_bytes < w.bytes) return B200Q_ENOSPACE;
     cudaStream_t s = (cudaStream_t)stream;
     int st;
-    // 1. grouping by local expert, the slot schedule, the int8 rows
-    const int qwarps = R * (H / 32);
-    launch(moe_local_prep_k, dim3(1 + (qwarps + 15) / 16), dim3(512), 0, s, rows, rows_dtype, ldr, R, H, lidx,
-           lidx_stride, n_local, w.counts, w.offsets, w.order, w.xq, w.xs, w.sched, w.ready, F, iq2_first_wave());
+    // 1. grouping by local expert, the slot schedule, the int8 rows (unless given): at most one wave of quantiser
+    // blocks (148 SMs x 4 blocks of 512 threads), striding over the rows
+    const int qwarps = R * (H / 32), qblocks = (qwarps + 15) / 16 < 4 * 148 ? (qwarps + 15) / 16 : 4 * 148;
+    launch(moe_local_prep_k, dim3(given ? 1 : 1 + qblocks), dim3(512), 0, s, given ? nullptr : rows, rows_dtype, ldr,
+           R, H, lidx, lidx_stride, n_local, w.counts, w.offsets, w.order, w.xq, w.xs, w.sched, w.ready, F,
+           iq2_first_wave(), peer ? peer->wait_flags : nullptr, peer ? peer->wait_n : 0,
+           peer ? peer->epoch : nullptr, peer ? peer->err : nullptr);
     if ((st = launched()) != B200Q_OK) return st;
     // 2. up with relu^2 and the int8 rows of the result (row id = received row), then down, in one launch
     GemvArgs a = {};
     a.slab = (const uint8_t*)up; a.expert_bytes = iq2_bytes(F, H); a.nslot_routed = n_local; a.n = F; a.k = H;
     a.counts = w.counts; a.offsets = w.offsets; a.order = w.order; a.act_div = 1; a.act_split = 1 << 30;
-    a.xq = w.xq; a.xs = w.xs; a.aq = w.aq; a.as = w.as; a.sched = w.sched;
+    a.xq = given ? peer->xq : w.xq; a.xs = given ? peer->xs : w.xs; a.aq = w.aq; a.as = w.as; a.sched = w.sched;
     GemvArgs b = {};
     b.slab = (const uint8_t*)down; b.expert_bytes = iq2_bytes(H, F); b.nslot_routed = n_local; b.n = H; b.k = F;
     b.counts = w.counts; b.offsets = w.offsets; b.order = w.order; b.act_div = 1; b.act_split = 1 << 30;
     b.xq = w.aq; b.xs = w.as; b.y = (float*)y; b.ldy = ldy; b.y_bf16 = y_dtype == B200Q_BF16;
     b.sched = w.sched;
+    // the launch whose end publishes the outputs: the down launch, or the fused launch (whose args are up's)
 #ifdef B200Q_X_NOFUSE
+    if (peer) { b.done_base = peer->done_base; b.done_off = peer->done_off; b.done_n = peer->done_n; b.done_epoch = peer->epoch; }
     if ((st = status_from(launch_iq2_gemv(a, n_local, 16, 2, s))) != B200Q_OK) return st;
     b.sched_early = 1;
     return status_from(launch_iq2_gemv(b, n_local, 16, 0, s));
 #else
+    if (peer) { a.done_base = peer->done_base; a.done_off = peer->done_off; a.done_n = peer->done_n; a.done_epoch = peer->epoch; }
     return status_from(launch_iq2_updown(a, b, w.ready, n_local, s));
 #endif
 }
+
+extern "C" {
 
 size_t b200q_moe_decode_workspace_bytes(int T, int H, int F, int E, int topk) {
     if (T <= 0 || H <= 0 || F <= 0 || E <= 0 || topk <= 0) return 0;

@@ -10,6 +10,68 @@ __device__ __forceinline__ float load_act(const void* p, int dtype, size_t i) {
 }
 
 // ---------------------------------------------------------------------------------------------------------
+// Flags between GPUs (the expert-parallel exchange over peer memory, ep_peer.cu): a sender publishes an epoch after
+// its data stores and a system-scope fence; a receiver polls with system-scope acquire loads.  Every wait is bounded
+// in time and in polls: on a timeout the waiter sets bit `bit` of *err and goes on (its results are then wrong, and the
+// host reads the flag), so a rank that never arrives ends in an error, not a hang.  Measured on B200: a system-scope
+// fence about 2 us (3.5 when a hundred CTAs issue one at once), a GPU-scope one 0.2 us, a relaxed system-scope store
+// or an acquire load 0.1 us; so a flag set is one fence then relaxed stores.
+// ---------------------------------------------------------------------------------------------------------
+constexpr unsigned long long kPeerWaitNs = 4000000000ull;   // 4 s
+constexpr unsigned kPeerMaxPolls = 1u << 26;
+
+__device__ __forceinline__ unsigned long long peer_clock() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+    int v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void st_relaxed_sys(int* p, int v) {
+    asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// one thread: wait until flags[0 .. n) have all reached epoch (wrap-safe compare).  Once a waiter has given up (bit
+// `bit` of *err set), later waits give up after a few polls too, so a missing rank costs one timeout, not one a CTA;
+// the host clears the bits (b200q_ep_peer_error).
+__device__ inline void wait_epochs(const int* flags, int n, int epoch, int* err, int bit) {
+    const unsigned long long t0 = peer_clock();
+    unsigned polls = 0;
+    for (int i = 0; i < n; i++) {
+        while ((int)(ld_acquire_sys(flags + i) - epoch) < 0) {
+            if (++polls > kPeerMaxPolls || ((polls & 63) == 0 && (peer_clock() - t0 > kPeerWaitNs ||
+                                                                  ((*(volatile int*)err >> bit) & 1)))) {
+                atomicOr(err, 1 << bit);
+                return;
+            }
+            __nanosleep(32);
+        }
+    }
+}
+
+// The expert-parallel exchange over peer memory (ep_peer.cu) around b200q_moe_experts_decode: the received rows
+// arrive in int8 form (quantised by their senders, the same arithmetic), the prologue first waits for the senders'
+// flags, and the GEMV launch's last CTA publishes the outputs in the senders' flags.
+struct ExpertsPeer {
+    const int8_t* xq;                 // [R][H] int8 rows, [R][H/32] their scales: read by the GEMVs as they are
+    const float* xs;
+    const int* wait_flags;            // wait_n flags that must reach *epoch before the rows are read
+    int wait_n;
+    const int* epoch;
+    int* err;                         // bit 0 set when that wait gave up
+    unsigned char* const* done_base;  // GemvArgs::done_* (the value published is *epoch)
+    size_t done_off;
+    int done_n;
+};
+// b200q_moe_experts_decode; with peer, rows may be NULL (the int8 rows are peer->xq / xs).  Defined in moe.cu.
+int experts_decode(const void* rows, int rows_dtype, int ldr, int R, int H, int F, const int* lidx, int lidx_stride,
+                   int n_local, const void* up, const void* down, void* y, int y_dtype, int ldy, void* workspace,
+                   size_t workspace_bytes, void* stream, const ExpertsPeer* peer);
+
+// ---------------------------------------------------------------------------------------------------------
 // quant_rows_k's arithmetic (bolt_kernels.cu:347-360), a warp per 32-group: s = amax/127, q = rn(x * 127/amax)
 // ---------------------------------------------------------------------------------------------------------
 __device__ __forceinline__ void quant_group(float v, int lane, int8_t* q, float* s) {
@@ -82,6 +144,44 @@ __device__ void route_token(const void* logits, int dtype, int ldl, const float*
         ridx[t * topk + lane] = pick_i;
         if (ridx_s) ridx_s[t * topk + lane] = pick_i;
         rw[t * topk + lane] = mode == B200Q_ROUTE_SOFTMAX ? picked / sum : picked / sum * scale;
+    }
+}
+
+// Softmax top-k of one token over bf16 logits, E <= 128 (a lane holds logits lane + 32 j), by a warp: route_token's
+// selection, weights and rounding (larger logit first, ties to the lower index; w = exp(z - max) / the sum over the
+// picked, in pick order), with each pick one redux over packed keys: a bf16 logit maps to 16 bits that order as its
+// value, above 16 bits that order as the reversed index.
+__device__ __forceinline__ void route_softmax_bf16(const __nv_bfloat16* lg, int E, int topk, int t, int lane,
+                                                   int* ridx, float* rw, int* ridx_s) {
+    uint32_t key[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int i = lane + 32 * j;
+        uint32_t b = i < E ? (uint32_t)__bfloat16_as_ushort(lg[(size_t)t * E + i]) : 0u;
+        if (b == 0x8000u) b = 0u;   // -0 ties with +0, as the float compare has it
+        const uint32_t ord = (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+        key[j] = i < E ? (ord << 16) | (0xFFFFu - (uint32_t)i) : 0u;
+    }
+    float mx = 0.f, sum = 0.f, picked = 0.f;
+    int pick_i = 0;
+    for (int kk = 0; kk < topk; kk++) {
+        const uint32_t best = __reduce_max_sync(0xffffffffu, max(max(key[0], key[1]), max(key[2], key[3])));
+        const int bi = (int)(0xFFFFu - (best & 0xFFFFu));
+        const uint32_t o = best >> 16;
+        const uint32_t b = (o & 0x8000u) ? (o & 0x7FFFu) : (~o & 0xFFFFu);
+        const float z = __uint_as_float(b << 16);
+        if (kk == 0) mx = z;   // the first pick is the largest logit
+        const float pv = expf(z - mx);
+        sum += pv;
+        if (lane == kk) { picked = pv; pick_i = bi; }
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            if (lane + 32 * j == bi) key[j] = 0u;
+    }
+    if (lane < topk) {
+        ridx[t * topk + lane] = pick_i;
+        ridx_s[t * topk + lane] = pick_i;
+        rw[t * topk + lane] = picked / sum;
     }
 }
 

@@ -356,6 +356,84 @@ class SharedExpert:
         return self._dec(x, self.lidx)
 
 
+class PeerDecodeMoE:
+    """The expert-parallel decode layer with its exchange over NVLink peer memory (b200q_ep_peer_decode): per step four
+    launches on this rank's stream and no collective.  The dispatch stores each pair's token row straight into its
+    owner's region, as the int8 row the GEMVs read; the owner's expert prologue waits for every sender's flag; the
+    combine reads each pair's output row (ret_dtype: bf16, or fp32 for the fused layer's exact bytes) from its owner's
+    region.  Nothing is read back to the host, so a step captures as a CUDA graph.
+
+    The shared expert is the last local expert of every rank (run on that rank's own tokens inside the same GEMV
+    launches as the routed ones).  Construction is collective (the ranks exchange their regions' IPC handles and check
+    that they sit on distinct GPUs: ranks that wait on one another must never share a GPU); close() is collective too
+    and must run before the process group is destroyed.  T (tokens a rank a step) is fixed: the region's layout
+    depends on it, the same on every rank."""
+
+    def __init__(self, placement, rank, world, H, F, T, topk, up_local, down_local, shared_up, shared_down,
+                 group=None, ret_dtype=torch.bfloat16, device=None, route=0, bias=None, scale=1.0):
+        import b200q
+        self.p, self.rank, self.world, self.H, self.F, self.T, self.topk = placement, rank, world, H, F, T, topk
+        self.group, self.ret_dtype, self.route, self.bias, self.scale = group, ret_dtype, route, bias, scale
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.n_local = len(placement.local[rank])
+        self.discard = max(len(l) for l in placement.local) + 1   # above every rank's local experts + its shared one
+        self.up = torch.cat([up_local, shared_up]).contiguous()
+        self.down = torch.cat([down_local, shared_down]).contiguous()
+        dest, lidx, nrep = placement.tables(self.device)
+        self.dest, self.lidx, self.nrep = (t.to(torch.int32).contiguous() for t in (dest, lidx, nrep))
+        L = b200q.lib()
+        code = b200q.BF16 if ret_dtype == torch.bfloat16 else b200q.F32
+        if world > 1:
+            uuids = [None] * world
+            dist.all_gather_object(uuids, str(torch.cuda.get_device_properties(self.device).uuid), group=group)
+            if len(set(uuids)) != world:
+                raise RuntimeError("the peer-memory exchange needs every rank on its own GPU")
+        self.region = b200q.PeerRegion(L.b200q_ep_peer_region_bytes(world, T, H, topk, code), self.device)
+        handles = [self.region.handle()] * world
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, self.region.handle(), group=group)
+        ptrs = [self.region.ptr if r == rank else self.region.open(handles[r]) for r in range(world)]
+        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+        self.state = torch.zeros(L.b200q_ep_peer_state_bytes(T, topk) // 4, dtype=torch.int32, device=self.device)
+        nws = L.b200q_ep_peer_workspace_bytes(world, T, H, F, topk, self.n_local)
+        self._ws = torch.empty(nws + 256, dtype=torch.uint8, device=self.device)
+        self.ws = (self._ws.data_ptr() + (-self._ws.data_ptr()) % 256, nws)
+        if world > 1:   # every mapping in place before any rank's first step
+            dist.barrier(group=group)
+
+    def __call__(self, x, logits, out=None, ridx=None, rw=None, phases=7):
+        """x [T][H], logits [T][E] (this rank's tokens) -> out [T][H] fp32.  phases: the subset of the step's
+        launches (bit 0 dispatch, bit 1 local experts + their flags, bit 2 combine), for timing the pieces."""
+        import b200q
+        if x.shape[0] != self.T or logits.shape[0] != self.T:
+            raise ValueError(f"the layer was built for {self.T} tokens a step, got {x.shape[0]}")
+        return b200q.ep_peer_decode(x, logits, self.topk, self.dest, self.lidx, self.nrep, self.region.ptr,
+                                    self.peers, self.world, self.rank, self.n_local, self.discard, self.up, self.down,
+                                    self.state, self.ws, self.H, self.F, ret_dtype=self.ret_dtype, out=out,
+                                    route=self.route, bias=self.bias, scale=self.scale, ridx=ridx, rw=rw,
+                                    phases=phases)
+
+    def error(self, clear=True):
+        """the bits the step's bounded waits recorded (0: none; bit 0 senders, bit 1 owners did not arrive)"""
+        import b200q
+        return b200q.ep_peer_error(self.state, clear)
+
+    def close(self):
+        """collective: unmap the other ranks' regions once every rank is done with its steps, then free this one once
+        every rank has unmapped it"""
+        if self.region is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        self.region.unmap()
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        self.region.free()
+        self.region = None
+
+
 class GraphedStep:
     """A decode step captured once as a CUDA graph and replayed.  With the capacity exchange the expert-parallel layer
     reads nothing back to the host, so router, packing, the NCCL all-to-alls, the expert kernels and the combine

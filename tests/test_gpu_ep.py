@@ -8,7 +8,7 @@ import torch
 
 import b200q
 import oracle as O
-from ep import ExpertParallelMoE, LocalExperts, Placement, SharedExpert, slice_slab
+from ep import ExpertParallelMoE, LocalExperts, PeerDecodeMoE, Placement, SharedExpert, slice_slab
 from helpers import assert_tolerance, iq2_blocks, normal_bf16
 
 pytestmark = pytest.mark.gpu
@@ -174,3 +174,78 @@ def test_ep_pack_and_combine_layout_four_ranks():
             acc = (np.float64(w[t, k]) * b[slot_np[t * topk + k]] + acc).astype(np.float32)   # fma: one rounding
         want[t] = acc + shared[t].cpu().numpy()
     assert np.array_equal(got, want)
+
+
+def _peer_layer(T, H, F, E, topk, dt, seed=50):
+    up = iq2_blocks(seed + 1, E * F, H)
+    down = iq2_blocks(seed + 2, E * H, F)
+    su, sd = iq2_blocks(seed + 3, F, H), iq2_blocks(seed + 4, H, F)
+    pu = b200q.repack_iq2(dev(up.reshape(-1)), E * F, H)
+    pd = b200q.repack_iq2(dev(down.reshape(-1)), E * H, F)
+    psu, psd = b200q.repack_iq2(dev(su.reshape(-1)), F, H), b200q.repack_iq2(dev(sd.reshape(-1)), H, F)
+    pl = Placement(E, 1, seed=9)
+    loc = pl.local[0]
+    moe = PeerDecodeMoE(pl, 0, 1, H, F, T, topk, slice_slab(pu, loc, b200q.iq2_bytes(F, H)),
+                        slice_slab(pd, loc, b200q.iq2_bytes(H, F)), psu, psd, ret_dtype=getattr(torch, dt),
+                        device=torch.device(DEV))
+    fused = b200q.MoeDecodeLayer(pu, pd, psu, psd, H, F, E, topk, route=b200q.ROUTE_SOFTMAX, max_tokens=T)
+    return moe, fused, (up, down, su, sd)
+
+
+@pytest.mark.parametrize("T,H,F,E,topk,dt", [(16, 512, 256, 16, 4, "float32"), (16, 512, 256, 16, 4, "bfloat16"),
+                                             (16, 4096, 2048, 128, 6, "float32"), (3, 256, 512, 8, 2, "bfloat16")])
+def test_peer_decode_one_rank_matches_fused_layer(T, H, F, E, topk, dt):
+    """b200q_ep_peer_decode on one rank (its exchange stores into its own region): the rows go out as the int8 rows
+    the fused layer computes too, so with fp32 outputs returned the combine adds the fused layer's values in its
+    order: the same bytes; with bf16 outputs returned they round, within BASELINE's tolerance of the fused layer and
+    of the oracle.  Several steps in a row: the epochs advance and the region's rows are reused."""
+    moe, fused, (up, down, su, sd) = _peer_layer(T, H, F, E, topk, dt)
+    try:
+        for step in range(3):
+            xb, _ = normal_bf16(60 + step, (T, H))
+            lb, _ = normal_bf16(70 + step, (T, E))
+            xt, lt = dev(xb).view(torch.bfloat16), dev(lb).view(torch.bfloat16)
+            ridx = torch.empty(T, topk, dtype=torch.int32, device=DEV)
+            got = moe(xt, lt, ridx=ridx).cpu().numpy()
+            want_ridx = torch.empty(T, topk, dtype=torch.int32, device=DEV)
+            want = fused(xt, lt, ridx=want_ridx).cpu().numpy()
+            assert moe.error() == 0 and b200q.device_error() == 0
+            assert torch.equal(ridx, want_ridx)
+            if dt == "float32":
+                assert np.array_equal(got, want)
+            assert_tolerance(got, want)
+            if H <= 512:
+                ref, _, _ = O.moe_layer(xb, lb, up.reshape(-1), down.reshape(-1), su.reshape(-1), sd.reshape(-1), T,
+                                        H, F, E, topk, mode=0)
+                assert_tolerance(got, ref)
+        assert int(moe.state[0].item()) == 3   # one epoch a step
+    finally:
+        moe.close()
+
+
+def test_peer_decode_wait_runs_out_with_an_error_not_a_hang():
+    """A bounded wait that nothing satisfies: the step's epoch set ahead of every flag, so the local experts' prologue
+    (the senders' flags) and then the combine (the owners' flags) each give up after their time limit, record their
+    bit and return; the stream stays usable, and once the epoch is back where the flags are a full step is right."""
+    T, H, F, E, topk = 2, 256, 256, 4, 2
+    moe, fused, _ = _peer_layer(T, H, F, E, topk, "bfloat16", seed=80)
+    try:
+        xb, _ = normal_bf16(81, (T, H))
+        lb, _ = normal_bf16(82, (T, E))
+        xt, lt = dev(xb).view(torch.bfloat16), dev(lb).view(torch.bfloat16)
+        moe(xt, lt)
+        assert moe.error() == 0
+        moe.state[0] = 100                 # no sender has published step 100
+        moe(xt, lt, phases=2)
+        torch.cuda.synchronize()
+        assert moe.error() == 1
+        moe.state[0] = 200                 # no owner has published step 200 (the GEMVs above published 100)
+        moe(xt, lt, phases=4)
+        torch.cuda.synchronize()
+        assert moe.error() == 2
+        moe.state[0] = 100                 # where every flag now is: the next step publishes and waits for 101
+        got = moe(xt, lt).cpu().numpy()
+        assert moe.error() == 0
+        assert_tolerance(got, fused(xt, lt).cpu().numpy())
+    finally:
+        moe.close()

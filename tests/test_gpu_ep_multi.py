@@ -1,6 +1,8 @@
-"""The expert-parallel decode layer on two GPUs over NCCL (skipped with fewer): each rank's fused capacity exchange
-(b200q_ep_pack, the all-to-alls, b200q_moe_experts_decode on the received rows, b200q_ep_combine), with fp32
-transfers, gives the bytes the fused single-GPU layer gives for the same tokens with every expert on one GPU."""
+"""The expert-parallel decode layer on two GPUs (skipped with fewer), both exchanges: NCCL (each rank's fused capacity
+exchange: b200q_ep_pack, the all-to-alls, b200q_moe_experts_decode on the received rows, b200q_ep_combine) and peer
+memory (b200q_ep_peer_decode).  With fp32 outputs returned either gives the bytes the fused single-GPU layer gives
+for the same tokens with every expert on one GPU (the peer exchange sends the int8 rows the fused layer computes too);
+with bf16 outputs the peer exchange is within BASELINE's tolerance."""
 import os
 import socket
 
@@ -67,6 +69,79 @@ def test_two_rank_ep_decode_matches_fused_layer():
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(ok for _, ok, _ in res), res
+
+
+def _peer_worker(rank, world, port, q, dt, steps):
+    try:
+        import datetime
+        import sys
+        here = os.path.dirname(os.path.abspath(__file__))
+        root = os.path.dirname(here)
+        for p in (here, os.path.join(root, "oracle"), os.path.join(root, "nemotron-3.5-bolt-tensorfold-dgx-spark_b200")):
+            sys.path.insert(0, p)
+        import torch.distributed as dist
+        import b200q
+        from ep import PeerDecodeMoE, Placement, slice_slab
+        from helpers import assert_tolerance, iq2_blocks, normal_bf16
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+        T, H, F, E, topk = 16, 1024, 512, 16, 4
+        d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+        up, down = iq2_blocks(1, E * F, H), iq2_blocks(2, E * H, F)
+        su, sd = iq2_blocks(3, F, H), iq2_blocks(4, H, F)
+        pu, pd = b200q.repack_iq2(d(up.reshape(-1)), E * F, H), b200q.repack_iq2(d(down.reshape(-1)), E * H, F)
+        psu, psd = b200q.repack_iq2(d(su.reshape(-1)), F, H), b200q.repack_iq2(d(sd.reshape(-1)), H, F)
+        pl = Placement(E, world, seed=3)
+        loc = pl.local[rank]
+        moe = PeerDecodeMoE(pl, rank, world, H, F, T, topk, slice_slab(pu, loc, b200q.iq2_bytes(F, H)),
+                            slice_slab(pd, loc, b200q.iq2_bytes(H, F)), psu, psd, ret_dtype=getattr(torch, dt),
+                            device=dev)
+        ok, worst = True, 0.0
+        # nothing may raise between the region's construction and its collective close: a rank whose region is freed
+        # while the other still stores into it would take a fault on the GPU
+        try:
+            fused = b200q.MoeDecodeLayer(pu, pd, psu, psd, H, F, E, topk, max_tokens=T)
+            for step in range(steps):
+                xb, _ = normal_bf16(10 + rank + 2 * step, (T, H))
+                lb, _ = normal_bf16(20 + rank + 2 * step, (T, E))
+                xt, lt = d(xb).view(torch.bfloat16), d(lb).view(torch.bfloat16)
+                got = moe(xt, lt).cpu().numpy()
+                want = fused(xt, lt).cpu().numpy()
+                worst = max(worst, float(np.abs(got - want).max()))
+                if dt == "float32":
+                    ok = ok and bool(np.array_equal(got, want))
+                else:
+                    try:
+                        assert_tolerance(got, want)
+                    except AssertionError:
+                        ok = False
+            ok = ok and moe.error() == 0 and b200q.device_error() == 0
+        except Exception:
+            ok = False
+        finally:
+            moe.close()
+        dist.destroy_process_group()
+        q.put((rank, ok, worst))
+    except Exception as e:   # report, never hang the parent
+        q.put((rank, False, repr(e)))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("dt", ["float32", "bfloat16"])
+def test_two_rank_peer_decode_matches_fused_layer(dt):
+    ctx = torch.multiprocessing.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, q, dt, 4)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
