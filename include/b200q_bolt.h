@@ -9,6 +9,8 @@
  *               buffer sizes as libbolt's tiles, holding this engine's t16 units split into a code plane and a scale
  *               plane);
  *   per step    mma_nv4, mma_q8, mma_q8_multi;
+ * and for the prompt chunks' NVFP4 projections on the fp4 tensor cores (BOLT_NV4_FP4): tile_nv4w at load time,
+ *               quant_nv4_rows + mma_nv4_fp4 per chunk;
  * and for the shared expert (load_iq2, bolt_host.cu:266-283, and bolt_host.cu:680-681): tile_bytes_iq2,
  * tile_scale_bytes_iq2, tile_iq2, mma_iq2.
  * The structs repeat libbolt's member order and types so the bytes match.  libbolt's fixed model shapes stay fixed
@@ -73,6 +75,21 @@ void mma_nv4(cudaStream_t s, const TNV4& w, const float* x, int ldx, float* y, i
 void mma_q8(cudaStream_t s, const TQ8& w, const float* x, int ldx, float* y, int ldy, int T);
 /* each matrix with n > 0 (libbolt leaves an unused one zeroed) into its own y */
 void mma_q8_multi(cudaStream_t s, const TQ8Multi& m, const float* x, int ldx, int T);
+
+/* libbolt's BOLT_NV4_FP4 prompt path (bolt_common.h:115-121, load_nv4w bolt_host.cu:218-238, calls at
+ * bolt_host.cu:634,644): an NVFP4 matrix for the block-scaled fp4 tensor cores (bolt_common.h:46).  With this engine's
+ * tile_nv4w, q (libbolt's tile_bytes_nv4(n, k) buffer) and sf (its tile_scale_bytes_nv4 buffer) hold the code and
+ * scale planes of the tcgen05 GEMM's weight image (256-row tiles; a last tile of 128 rows when n % 256 == 128,
+ * in_proj's 18560), exactly libbolt's byte counts.  n % 128 == 0, k % 256 == 0. */
+struct TNV4W { const uint4* q; const uint32_t* sf; float s2; int n, k; };
+void tile_nv4w(cudaStream_t s, const uint8_t* q, const uint8_t* sc, void* qw, void* sfw, int n, int k);
+/* x fp32 [T][ldx] -> q4 [T][k/2] (e2m1, low nibble first), sf [T][k/16] (e4m3 of amax/6 a block of 16): libbolt's
+ * layout and bytes (quant_nv4_rows_k's steps) */
+void quant_nv4_rows(cudaStream_t s, const float* x, int ldx, uint8_t* q4, uint8_t* sf, int T, int k);
+/* y[t][0 .. n) = s2 * sum_k (q4, sf)[t] (w.q, w.sf)[row], fp32 sums on the tcgen05 block-scaled fp4 MMA
+ * (kind::mxf4nvf4).  The rows are rearranged into the GEMM's rows image in a scratch of (device, stream), allocated at
+ * the first call outside stream capture, as mma_nv4's is. */
+void mma_nv4_fp4(cudaStream_t s, const TNV4W& w, const uint8_t* q4, const uint8_t* sf, float* y, int ldy, int T);
 
 /* an IQ2_XXS matrix: q = 64 code bytes a row and 256 k, d = one fp16 scale a row and 256 k (bolt_common.h:49); with
  * this engine's tile_iq2 they hold the split rt32 planes (n % 32 == 0) */

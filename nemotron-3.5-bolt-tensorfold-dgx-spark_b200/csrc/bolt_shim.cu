@@ -19,6 +19,11 @@ int tc_gemv_split(int fmt, const uint8_t* qt, const uint8_t* sct, float s2, int 
 size_t tc_split_ws(int fmt, int n, int k, int T);
 constexpr int kTcNv4 = 0, kTcQ8 = 1;
 constexpr int kTcRows = 16;   // rows a decode GEMV launch takes
+// the NVFP4 prompt GEMM over libbolt's buffers (nv4_gemm.cu)
+int nv4_planes_pack(const uint8_t* q, const uint8_t* sc, uint8_t* qw, uint8_t* sfw, int n, int k, cudaStream_t s);
+int nv4_quant_plain(const float* x, int ldx, uint8_t* q4, uint8_t* sf, int T, int k, cudaStream_t s);
+int nv4_gemm_planes(const uint8_t* qw, const uint8_t* sfw, int n, int k, float s2, const uint8_t* q4, const uint8_t* sf,
+                    int T, uint8_t* rows_img, float* y, int ldy, cudaStream_t s);
 
 constexpr int kBoltLatent = 1024;   // moe_up's k, moe_down's n, k_combine's width (bolt_kernels.cu:682-695, 1714-1727)
 constexpr int kBoltTopN = 9;        // routed experts a token (bolt_common.h:25)
@@ -69,7 +74,7 @@ static GemvArgs slab_args(const IQ2Slab& slab, const MoeWork& w, int n, int k, i
 // scratch (bolt_mma.cu:1183-1187): launches on one stream are ordered, so they share it.  It grows only outside stream
 // capture.  Uses: the K-slice partials of the decode GEMVs (a capture that needs more than the buffer holds runs the
 // GEMV as one K slice, the same sums), and mma_iq2's int8 rows.
-enum { kWsPartials = 0, kWsRows = 1 };
+enum { kWsPartials = 0, kWsRows = 1, kWsFp4Rows = 2 };
 struct ShimWs { int dev; cudaStream_t s; int use; void* p; size_t bytes; };
 static ShimWs g_ws[32];
 static std::mutex g_ws_mu;
@@ -269,6 +274,33 @@ void mma_q8_multi(cudaStream_t s, const TQ8Multi& m, const float* x, int ldx, in
         if (m.w[i].n > 0)
             tc_rows("mma_q8_multi", kTcQ8, (const uint8_t*)m.w[i].q, (const uint8_t*)m.w[i].d, 1.f, m.w[i].n,
                     m.w[i].k, x, ldx, m.y[i], m.ldy[i], T, s);
+}
+
+// tile_nv4w (bolt_mma.cu:892-923, via load_nv4w bolt_host.cu:218-238): the checkpoint's q [n][k/2] and sc [n][k/16]
+// into the weight planes, in libbolt's two buffers (tile_bytes_nv4 / tile_scale_bytes_nv4 bytes)
+void tile_nv4w(cudaStream_t s, const uint8_t* q, const uint8_t* sc, void* qw, void* sfw, int n, int k) {
+    report("tile_nv4w", nv4_planes_pack(q, sc, (uint8_t*)qw, (uint8_t*)sfw, n, k, s));
+}
+// quant_nv4_rows (bolt_mma.cu:926-951): libbolt's plain rows, the same bytes
+void quant_nv4_rows(cudaStream_t s, const float* x, int ldx, uint8_t* q4, uint8_t* sf, int T, int k) {
+    report("quant_nv4_rows", nv4_quant_plain(x, ldx, q4, sf, T, k, s));
+}
+// mma_nv4_fp4 (bolt_mma.cu:961-1059): the tcgen05 block-scaled fp4 GEMM over the planes and the plain rows
+void mma_nv4_fp4(cudaStream_t s, const TNV4W& w, const uint8_t* q4, const uint8_t* sf, float* y, int ldy, int T) {
+    if (T <= 0) return;
+    const size_t need = b200q_nv4_rows_bytes(T, w.k);
+    if (need == 0) {
+        report("mma_nv4_fp4", B200Q_EINVAL);
+        return;
+    }
+    size_t have = 0;
+    uint8_t* img = (uint8_t*)shim_ws(s, need, &have, kWsFp4Rows);
+    if (!img || have < need) {
+        report("mma_nv4_fp4", B200Q_ENOSPACE);   // first grown inside a stream capture
+        return;
+    }
+    report("mma_nv4_fp4", nv4_gemm_planes((const uint8_t*)w.q, (const uint8_t*)w.sf, w.n, w.k, w.s2, q4, sf, T, img, y,
+                                          ldy, s));
 }
 
 // tile_bytes_iq2 / tile_scale_bytes_iq2 (bolt_mma.cu:1226-1227): 64 code bytes and one fp16 scale a row and 256 k,

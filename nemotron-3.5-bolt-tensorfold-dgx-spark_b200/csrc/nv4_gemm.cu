@@ -38,9 +38,12 @@ constexpr size_t kF4Smem = (size_t)kF4Stages * kF4Stage + 1024 /*align*/ + 256 /
 constexpr int kF4SfCols = 48;                             // TMEM columns of a stage's scales: 16 (A) + 32 (B)
 constexpr uint32_t kF4TmemCols = 512;                     // 256 accumulator + 4 x 48 scale columns, rounded up
 
-// instruction descriptor, kind::mxf4nvf4: e2m1 A and B (format 1), K-major, N = 256, ue4m3 scales, M = 128,
-// scale-factor ids 0 (each 32-bit TMEM column holds the four 16-k scales of a 64-k block)
-constexpr uint32_t kIdescF4 = (1u << 7) | (1u << 10) | ((uint32_t)(kF4N >> 3) << 17) | ((uint32_t)(kF4M >> 4) << 24);
+// instruction descriptor, kind::mxf4nvf4: e2m1 A and B (format 1), K-major, N = 256 (128 for a ragged last weight
+// tile), ue4m3 scales, M = 128, scale-factor ids 0 (each 32-bit TMEM column holds the four 16-k scales of a 64-k block)
+constexpr uint32_t f4_idesc(int n) {
+    return (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kF4M >> 4) << 24);
+}
+constexpr uint32_t kIdescF4 = f4_idesc(kF4N), kIdescF4Half = f4_idesc(kF4N / 2);
 
 __device__ int g_nv4_error;   // bit 0: a barrier wait timed out
 
@@ -55,11 +58,11 @@ int nv4_error_read(int clear) {
 }
 
 __device__ __forceinline__ void umma_f4(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate, uint32_t sfa,
-                                        uint32_t sfb) {
+                                        uint32_t sfb, uint32_t idesc) {
     asm volatile(
         "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p; }"
-        ::"r"(tmem_d), "l"(a), "l"(b), "r"(kIdescF4), "r"(accumulate), "r"(sfa), "r"(sfb));
+        ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb));
 }
 __device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, uint64_t src) {
     asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(src));
@@ -99,6 +102,29 @@ __device__ __forceinline__ uint32_t f4_e2m1_enc(float v) {
     return c | (v < 0.f ? 8u : 0u);
 }
 
+// 32 k of one row (two 16-k blocks) -> one 16-byte chunk of e2m1 codes (k = 2b low nibble, 2b + 1 high nibble of
+// byte b) and two e4m3 scales: quant_nv4_rows_k's steps (bolt_mma.cu:926-946), scale = e4m3(amax / 6)
+__device__ __forceinline__ void f4_quant32(const float* v, uint32_t* w, uint32_t* sc) {
+#pragma unroll
+    for (int b = 0; b < 2; b++) {
+        float amax = 0.f;
+#pragma unroll
+        for (int j = 0; j < 16; j++) amax = fmaxf(amax, fabsf(v[16 * b + j]));
+        const uint32_t code = f4_e4m3_enc(amax * (1.f / 6.f));
+        const float sq = f4_e4m3_dec(code);
+        const float inv = sq > 0.f ? 1.f / sq : 0.f;
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            lo |= f4_e2m1_enc(v[16 * b + j] * inv) << (4 * j);
+            hi |= f4_e2m1_enc(v[16 * b + 8 + j] * inv) << (4 * j);
+        }
+        w[2 * b] = lo;
+        w[2 * b + 1] = hi;
+        sc[b] = code;
+    }
+}
+
 // rows -> NVFP4 tile image.  A thread quantises 32 k of one row (two 16-k blocks: one 16-byte chunk, two scales);
 // rows T..Mp-1 of the last m-tile are written as zeros.
 __global__ void quant_nv4_rows_k(const void* __restrict__ x, int dtype, int ldx, int T, int k, int Mp,
@@ -127,24 +153,7 @@ __global__ void quant_nv4_rows_k(const void* __restrict__ x, int dtype, int ldx,
 #pragma unroll
                 for (int j = 0; j < 8; j++) { const float4 f = __ldg(p + j); v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w; }
             }
-#pragma unroll
-            for (int b = 0; b < 2; b++) {
-                float amax = 0.f;
-#pragma unroll
-                for (int j = 0; j < 16; j++) amax = fmaxf(amax, fabsf(v[16 * b + j]));
-                const uint32_t code = f4_e4m3_enc(amax * (1.f / 6.f));
-                const float sq = f4_e4m3_dec(code);
-                const float inv = sq > 0.f ? 1.f / sq : 0.f;
-                uint32_t lo = 0, hi = 0;
-#pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    lo |= f4_e2m1_enc(v[16 * b + j] * inv) << (4 * j);
-                    hi |= f4_e2m1_enc(v[16 * b + 8 + j] * inv) << (4 * j);
-                }
-                w[2 * b] = lo;
-                w[2 * b + 1] = hi;
-                sc[b] = code;
-            }
+            f4_quant32(v, w, sc);
         }
         *reinterpret_cast<uint4*>(rec + sw128_off(r, c)) = make_uint4(w[0], w[1], w[2], w[3]);
         rec[kF4AData + f4_sf_off(r, 2 * c, 1)] = (uint8_t)sc[0];
@@ -178,8 +187,82 @@ __global__ void nv4_tc_pack_k(const uint8_t* __restrict__ q, const uint8_t* __re
     pdl_trigger();
 }
 
+// ---------------------------------------------------------------------------------------------------------
+// libbolt's own buffers for its BOLT_NV4_FP4 prompt path (the shims tile_nv4w / quant_nv4_rows / mma_nv4_fp4):
+//  * rows, plain: q4 [T][k/2] (low nibble first), sf [T][k/16] e4m3 -- libbolt's quant_nv4_rows layout, the same bytes;
+//    the GEMM's rows image is made from them by f4_rows_from_plain_k;
+//  * weights, "planes": the weight image split into a code plane (in libbolt's tile buffer, n*k/2 bytes) and a scale
+//    plane (its scale buffer, n*k/16 bytes), record (n-tile, ks) at nt*KS*32 KB + ks*rows*128 in the code plane and
+//    nt*KS*4 KB + ks*rows*16 in the scale plane, rows = 256 except a last tile of 128 (n % 256 == 128, in_proj's
+//    18560), whose records are packed at half size so that both planes hold exactly libbolt's byte counts.
+// ---------------------------------------------------------------------------------------------------------
+__global__ void quant_nv4_plain_k(const float* __restrict__ x, int ldx, int T, int k, uint8_t* __restrict__ q4,
+                                  uint8_t* __restrict__ sf) {
+    pdl_wait();
+    const int per = k >> 5;
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < (size_t)T * per) {
+        const int row = (int)(i / per), c32 = (int)(i % per);
+        float v[32];
+        const float4* p = reinterpret_cast<const float4*>(x + (size_t)row * ldx + c32 * 32);
+#pragma unroll
+        for (int j = 0; j < 8; j++) { const float4 f = __ldg(p + j); v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w; }
+        uint32_t w[4], sc[2];
+        f4_quant32(v, w, sc);
+        *reinterpret_cast<uint4*>(q4 + (size_t)row * (k / 2) + (size_t)c32 * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        sf[(size_t)row * (k / 16) + 2 * c32] = (uint8_t)sc[0];
+        sf[(size_t)row * (k / 16) + 2 * c32 + 1] = (uint8_t)sc[1];
+    }
+    pdl_trigger();
+}
+
+// plain rows (q4, sf) -> the rows image; rows T..Mp-1 zero
+__global__ void f4_rows_from_plain_k(const uint8_t* __restrict__ q4, const uint8_t* __restrict__ sf, int T, int k, int Mp,
+                                     uint8_t* __restrict__ out) {
+    pdl_wait();
+    const int per = k >> 5;
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < (size_t)Mp * per) {
+        const int row = (int)(i / per), c32 = (int)(i % per);
+        const int ks = c32 >> 3, c = c32 & 7, mt = row >> 7, r = row & 127;
+        uint8_t* rec = out + ((size_t)mt * (k / kF4K) + ks) * kF4ARec;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        uint8_t s0 = 0, s1 = 0;
+        if (row < T) {
+            v = __ldg(reinterpret_cast<const uint4*>(q4 + (size_t)row * (k / 2) + (size_t)c32 * 16));
+            s0 = sf[(size_t)row * (k / 16) + 2 * c32];
+            s1 = sf[(size_t)row * (k / 16) + 2 * c32 + 1];
+        }
+        *reinterpret_cast<uint4*>(rec + sw128_off(r, c)) = v;
+        rec[kF4AData + f4_sf_off(r, 2 * c, 1)] = s0;
+        rec[kF4AData + f4_sf_off(r, 2 * c + 1, 1)] = s1;
+    }
+    pdl_trigger();
+}
+
+// checkpoint NVFP4 -> the weight planes; a thread moves one 16-byte chunk (32 k) and its two scales
+__global__ void nv4_tc_pack_planes_k(const uint8_t* __restrict__ q, const uint8_t* __restrict__ sc, int n, int k,
+                                     uint8_t* __restrict__ qw, uint8_t* __restrict__ sfw) {
+    pdl_wait();
+    const int per = k >> 5, KS = k / kF4K;
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < (size_t)n * per) {
+        const int row = (int)(i / per), c32 = (int)(i % per);
+        const int ks = c32 >> 3, c = c32 & 7, nt = row >> 8, r = row & 255;
+        const int rows = n - nt * kF4N < kF4N ? kF4N / 2 : kF4N;
+        uint8_t* code = qw + (size_t)nt * KS * kF4BData + (size_t)ks * rows * 128;
+        uint8_t* scl = sfw + (size_t)nt * KS * kF4BSf + (size_t)ks * rows * 16;
+        *reinterpret_cast<uint4*>(code + sw128_off(r, c)) =
+            __ldg(reinterpret_cast<const uint4*>(q + (size_t)row * (k / 2) + (size_t)c32 * 16));
+        scl[f4_sf_off(r, 2 * c, rows / 128)] = sc[(size_t)row * (k / 16) + 2 * c32];
+        scl[f4_sf_off(r, 2 * c + 1, rows / 128)] = sc[(size_t)row * (k / 16) + 2 * c32 + 1];
+    }
+    pdl_trigger();
+}
+
 struct F4Args {
-    const uint8_t* w;        // weight tile image
+    const uint8_t* w;        // weight tile image; with wsf, the code plane of the weight planes
+    const uint8_t* wsf;      // the scale plane of the weight planes (nullptr: w is the interleaved image)
     const uint8_t* a;        // rows tile image
     float* y;
     int n, k, T, ldy;
@@ -188,6 +271,9 @@ struct F4Args {
     float* part;             // ksplit > 1: unscaled partial sums [ksplit][T][n]
 };
 
+// PLANES: the weights are the planes form (a.wsf, a last tile of 128 rows allowed); a template parameter so that the
+// image form's MMA lane carries no per-stage branch on it
+template <bool PLANES>
 __global__ void __launch_bounds__(kF4Threads, 1) nv4_gemm_k(F4Args a) {
     extern __shared__ __align__(1024) unsigned char f4_dyn[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -201,6 +287,8 @@ __global__ void __launch_bounds__(kF4Threads, 1) nv4_gemm_k(F4Args a) {
     unsigned char* tmem_slot_ptr = f4_dyn + (tmem_slot - raw);
 
     const int MT = (a.T + kF4M - 1) / kF4M, NT = (a.n + kF4N - 1) / kF4N, KS = a.k / kF4K;
+    // weight rows of n-tile nt: 256, or 128 for the last tile of the planes form when n % 256 == 128
+    auto tile_rows = [&](int nt) { return (PLANES && a.n - nt * kF4N < kF4N) ? kF4N / 2 : kF4N; };
     const int tiles = MT * NT * a.ksplit;   // work items: (tile, K slice)
     // item -> tile (m fastest within an n-tile), K slice; stage range [ks0, ks1)
     auto item = [&](int i, int& mt, int& nt, int& ks0, int& ks1) {
@@ -237,14 +325,21 @@ __global__ void __launch_bounds__(kF4Threads, 1) nv4_gemm_k(F4Args a) {
                 int mt, nt, ks0, ks1;
                 item(tile, mt, nt, ks0, ks1);
                 const uint8_t* ap = a.a + (size_t)mt * KS * kF4ARec;
-                const uint8_t* bp = a.w + (size_t)nt * KS * kF4BRec;
+                const int rows = tile_rows(nt);
                 for (int ks = ks0; ks < ks1; ks++, it++) {
                     const int s = it % kF4Stages, use = it / kF4Stages;
                     if (use > 0 && !tc_mbar_wait(empty(s), (uint32_t)((use - 1) & 1))) { healthy = false; break; }
                     const uint32_t st = sbase + (uint32_t)(s * kF4Stage);
-                    tc_mbar_arrive_tx(full(s), (uint32_t)kF4Stage);
+                    tc_mbar_arrive_tx(full(s), (uint32_t)(kF4ARec + rows * 144));
                     tc_bulk_g2s(st, ap + (size_t)ks * kF4ARec, (uint32_t)kF4ARec, full(s));
-                    tc_bulk_g2s(st + kF4ARec, bp + (size_t)ks * kF4BRec, (uint32_t)kF4BRec, full(s));
+                    if constexpr (PLANES) {   // the planes: codes then scales, at the stage's usual places
+                        tc_bulk_g2s(st + kF4ARec, a.w + (size_t)nt * KS * kF4BData + (size_t)ks * rows * 128,
+                                    (uint32_t)(rows * 128), full(s));
+                        tc_bulk_g2s(st + kF4ARec + kF4BData, a.wsf + (size_t)nt * KS * kF4BSf + (size_t)ks * rows * 16,
+                                    (uint32_t)(rows * 16), full(s));
+                    } else {
+                        tc_bulk_g2s(st + kF4ARec, a.w + ((size_t)nt * KS + ks) * kF4BRec, (uint32_t)kF4BRec, full(s));
+                    }
                 }
             }
             // the copies of the last uses of every stage have landed before the CTA may exit
@@ -263,6 +358,8 @@ __global__ void __launch_bounds__(kF4Threads, 1) nv4_gemm_k(F4Args a) {
                 item(tile, mt, nt, ks0, ks1);
                 if (tl > 0 && !tc_mbar_wait(acc_empty, (uint32_t)((tl - 1) & 1))) { healthy = false; break; }
                 tc_fence_after();
+                const bool half_n = PLANES && tile_rows(nt) < kF4N;   // a 128-row tile: one scale atom a 64-k block, N = 128
+                const uint32_t idesc = half_n ? kIdescF4Half : kIdescF4;
                 for (int ks = ks0; ks < ks1; ks++, it++) {
                     const int s = it % kF4Stages;
                     if (!tc_mbar_wait(full(s), (uint32_t)((it / kF4Stages) & 1))) { healthy = false; break; }
@@ -273,13 +370,17 @@ __global__ void __launch_bounds__(kF4Threads, 1) nv4_gemm_k(F4Args a) {
 #pragma unroll
                     for (int kb = 0; kb < 4; kb++) {
                         tmem_cp_sf(sfa + 4u * kb, umma_desc_rows16(asf + kb * 512));
-                        tmem_cp_sf(sfb + 8u * kb, umma_desc_rows16(bsf + (2 * kb) * 512));
-                        tmem_cp_sf(sfb + 8u * kb + 4u, umma_desc_rows16(bsf + (2 * kb + 1) * 512));
+                        if (PLANES && half_n) {
+                            tmem_cp_sf(sfb + 8u * kb, umma_desc_rows16(bsf + kb * 512));
+                        } else {
+                            tmem_cp_sf(sfb + 8u * kb, umma_desc_rows16(bsf + (2 * kb) * 512));
+                            tmem_cp_sf(sfb + 8u * kb + 4u, umma_desc_rows16(bsf + (2 * kb + 1) * 512));
+                        }
                     }
 #pragma unroll
                     for (int kb = 0; kb < 4; kb++)
                         umma_f4(tmem, umma_desc_sw128(at + kb * 32), umma_desc_sw128(bt + kb * 32),
-                                (ks > ks0 || kb > 0) ? 1u : 0u, sfa + 4u * kb, sfb + 8u * kb);
+                                (ks > ks0 || kb > 0) ? 1u : 0u, sfa + 4u * kb, sfb + 8u * kb, idesc);
                     umma_commit(empty(s));
                 }
                 if (healthy) umma_commit(acc_full);
@@ -388,6 +489,55 @@ static int f4_num_sms() {
 
 static inline bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+static bool f4_opt_in() {
+    static bool opted = false;
+    if (!opted) {
+        if (cudaFuncSetAttribute(nv4_gemm_k<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kF4Smem) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(nv4_gemm_k<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kF4Smem) !=
+                cudaSuccess)
+            return false;
+        opted = true;
+    }
+    return true;
+}
+
+// ---- libbolt's BOLT_NV4_FP4 buffers (the shims in bolt_shim.cu) ----
+// the weight planes into libbolt's tile buffers: qw n*k/2 bytes, sfw n*k/16 bytes; n % 128 == 0, k % 256 == 0
+int nv4_planes_pack(const uint8_t* q, const uint8_t* sc, uint8_t* qw, uint8_t* sfw, int n, int k, cudaStream_t s) {
+    if (!q || !sc || !qw || !sfw || n <= 0 || n % 128 || k <= 0 || k % kF4K || !a16(q) || !a16(qw) || !a16(sfw))
+        return B200Q_EINVAL;
+    const size_t th = (size_t)n * (k / 32);
+    return status_from(launch(nv4_tc_pack_planes_k, dim3((unsigned)((th + 255) / 256)), dim3(256), 0, s, q, sc, n, k,
+                              qw, sfw));
+}
+// fp32 rows -> libbolt's plain NVFP4 rows (q4 [T][k/2], sf [T][k/16])
+int nv4_quant_plain(const float* x, int ldx, uint8_t* q4, uint8_t* sf, int T, int k, cudaStream_t s) {
+    if (T <= 0) return B200Q_OK;
+    if (!x || !q4 || !sf || k <= 0 || k % kF4K || ldx < k || ldx % 4 || !a16(x) || !a16(q4)) return B200Q_EINVAL;
+    const size_t th = (size_t)T * (k / 32);
+    return status_from(launch(quant_nv4_plain_k, dim3((unsigned)((th + 255) / 256)), dim3(256), 0, s, x, ldx, T, k, q4,
+                              sf));
+}
+// y = s2 * planes-weights x plain rows; rows_img: b200q_nv4_rows_bytes(T, k) bytes of scratch (the rows image)
+int nv4_gemm_planes(const uint8_t* qw, const uint8_t* sfw, int n, int k, float s2, const uint8_t* q4, const uint8_t* sf,
+                    int T, uint8_t* rows_img, float* y, int ldy, cudaStream_t s) {
+    if (T <= 0) return B200Q_OK;
+    if (!qw || !sfw || !q4 || !sf || !rows_img || !y || n <= 0 || n % 128 || k <= 0 || k % kF4K || ldy < n ||
+        !a16(qw) || !a16(sfw) || !a16(q4) || !a16(rows_img))
+        return B200Q_EINVAL;
+    if (!f4_opt_in()) return status_from(cudaGetLastError());
+    const int Mp = (T + kF4M - 1) / kF4M * kF4M;
+    const size_t th = (size_t)Mp * (k / 32);
+    cudaError_t e = launch(f4_rows_from_plain_k, dim3((unsigned)((th + 255) / 256)), dim3(256), 0, s, q4, sf, T, k, Mp,
+                           rows_img);
+    if (e != cudaSuccess) return status_from(e);
+    const int tiles = ((T + kF4M - 1) / kF4M) * ((n + kF4N - 1) / kF4N);
+    const int grid = tiles < f4_num_sms() ? tiles : f4_num_sms();
+    F4Args a{qw, sfw, rows_img, y, n, k, T, ldy, s2, 1, nullptr};
+    return status_from(launch(nv4_gemm_k<true>, dim3(grid), dim3(kF4Threads), kF4Smem, s, a));
+}
+
 }  // namespace b200q
 
 using namespace b200q;
@@ -432,19 +582,14 @@ size_t b200q_nv4_gemm_workspace_bytes(int n, int k, int T) {
 int b200q_nv4_gemm(const void* w, int n, int k, float s2, const void* rows, int T, float* y, int ldy, void* workspace,
                    size_t workspace_bytes, void* stream) {
     if (!w || !rows || !y || n <= 0 || T <= 0 || k <= 0 || k % kF4K || ldy < n || !a16(w) || !a16(rows)) return B200Q_EINVAL;
-    static bool opted = false;
-    if (!opted) {
-        const cudaError_t e = cudaFuncSetAttribute(nv4_gemm_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kF4Smem);
-        if (e != cudaSuccess) return status_from(e);
-        opted = true;
-    }
+    if (!f4_opt_in()) return status_from(cudaGetLastError());
     const int tiles = ((T + kF4M - 1) / kF4M) * ((n + kF4N - 1) / kF4N);
     int ks = f4_ksplit(tiles, k / kF4K, f4_num_sms());
     if (!workspace || workspace_bytes < (size_t)ks * T * n * sizeof(float) || !a16(workspace)) ks = 1;
     const int items = tiles * ks;
     const int grid = items < f4_num_sms() ? items : f4_num_sms();
-    F4Args a{(const uint8_t*)w, (const uint8_t*)rows, y, n, k, T, ldy, s2, ks, (float*)workspace};
-    cudaError_t e = launch(nv4_gemm_k, dim3(grid), dim3(kF4Threads), kF4Smem, (cudaStream_t)stream, a);
+    F4Args a{(const uint8_t*)w, nullptr, (const uint8_t*)rows, y, n, k, T, ldy, s2, ks, (float*)workspace};
+    cudaError_t e = launch(nv4_gemm_k<false>, dim3(grid), dim3(kF4Threads), kF4Smem, (cudaStream_t)stream, a);
     if (e != cudaSuccess || ks == 1) return status_from(e);
     const size_t th = (size_t)T * n;
     return status_from(launch(f4_splitk_sum_k, dim3((unsigned)((th + 255) / 256)), dim3(256), 0, (cudaStream_t)stream,

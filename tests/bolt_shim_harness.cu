@@ -97,6 +97,19 @@ void hs_mma_q8(void* s, const void* qt, const void* dt, int n, int k, const floa
     mma_q8((cudaStream_t)s, w, x, ldx, y, ldy, T);
 }
 
+// libbolt's BOLT_NV4_FP4 prompt path with the views load_nv4w returns (bolt_host.cu:218-238, 634, 644)
+void hs_tile_nv4w(void* s, const uint8_t* q, const uint8_t* sc, void* qw, void* sfw, int n, int k) {
+    tile_nv4w((cudaStream_t)s, q, sc, qw, sfw, n, k);
+}
+void hs_quant_nv4_rows(void* s, const float* x, int ldx, uint8_t* q4, uint8_t* sf, int T, int k) {
+    quant_nv4_rows((cudaStream_t)s, x, ldx, q4, sf, T, k);
+}
+void hs_mma_nv4_fp4(void* s, const void* qw, const void* sfw, float s2, int n, int k, const uint8_t* q4,
+                    const uint8_t* sf, float* y, int ldy, int T) {
+    const TNV4W w{(const uint4*)qw, (const uint32_t*)sfw, s2, n, k};
+    mma_nv4_fp4((cudaStream_t)s, w, q4, sf, y, ldy, T);
+}
+
 // three matrices: q* / d* / n* / y* / ldy* for each (n = 0 leaves one unused)
 void hs_mma_q8_multi(void* s, const void* const* qt, const void* const* dt, const int* n, int k, const float* x, int ldx,
                      float* const* y, const int* ldy, int T) {

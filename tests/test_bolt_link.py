@@ -23,14 +23,17 @@ def _dyn(path, flag):
 
 @pytest.fixture(scope="module")
 def linked():
-    if not os.path.exists(BOLT_DEF):
-        pytest.skip("the reference checkout is not present")
+    # built here from the reference's sources; where they are absent (a GPU box), the prebuilt library that travels
+    # with the repository
     path = build_oracle.build_bolt_link()
-    assert path and os.path.exists(path)
+    if not path or not os.path.exists(path):
+        pytest.skip("neither the reference checkout nor a prebuilt linked library is present")
     return path
 
 
 def test_exports_libbolt_c_abi(linked):
+    if not os.path.exists(BOLT_DEF):
+        pytest.skip("the reference checkout (engine/bolt.def) is not present")
     names = [l.strip() for l in open(BOLT_DEF) if l.strip().startswith("bolt_")]
     assert len(names) == 45
     exported = _dyn(linked, "--defined-only")
@@ -44,13 +47,14 @@ def test_hot_path_binds_to_libb200q(linked):
     shims = {s for s in _dyn(PKG_LIB, "--defined-only") if not s.startswith("b200q_") and not s.startswith(std)}
     undefined = _dyn(linked, "--undefined-only")
     bound = shims & undefined
-    # the routed-expert block, the shared expert and the decode projections: 25 launchers with libbolt's names
+    # the routed-expert block, the shared expert, the decode projections and the NVFP4 prompt path (BOLT_NV4_FP4):
+    # 28 launchers with libbolt's names
     demangled = subprocess.run(["c++filt"], input="\n".join(sorted(bound)), capture_output=True, text=True).stdout
     for name in ("moe_up(", "moe_down(", "k_route(", "k_moe_group(", "k_quant_rows(", "k_combine(", "repack_iq2(",
                  "moe_coop_dense(", "mma_nv4(", "mma_q8(", "mma_q8_multi(", "mma_iq2(", "tile_nv4(", "tile_q8(",
-                 "tile_iq2("):
+                 "tile_iq2(", "tile_nv4w(", "quant_nv4_rows(", "mma_nv4_fp4("):
         assert name in demangled, name
-    assert len(bound) == 25
+    assert len(bound) == 28
     # and none of them is still defined inside the linked library
     assert not (shims & _dyn(linked, "--defined-only"))
     needed = subprocess.run(["readelf", "-d", linked], capture_output=True, text=True, check=True).stdout

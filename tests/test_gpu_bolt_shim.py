@@ -39,6 +39,9 @@ def _harness():
         "hs_mma_q8_multi": [vp, vp, vp, vp, i32, vp, i32, vp, vp, i32],
         "hs_tile_iq2": [vp, vp, vp, vp, i32, i32],
         "hs_mma_iq2": [vp, vp, vp, i32, i32, vp, i32, vp, i32, i32, i32],
+        "hs_tile_nv4w": [vp, vp, vp, vp, vp, i32, i32],
+        "hs_quant_nv4_rows": [vp, vp, i32, vp, vp, i32, i32],
+        "hs_mma_nv4_fp4": [vp, vp, vp, f32, i32, i32, vp, vp, vp, i32, i32],
     }
     for n, a in sig.items():
         getattr(L, n).restype, getattr(L, n).argtypes = None, a
@@ -308,3 +311,62 @@ def test_shim_mma_iq2_shared_expert():
     assert rel_l2(act_ref, O.iq2_gemm_exact(up, F, H, x, 1)) < 1e-2
     assert rel_l2(out_ref, O.iq2_gemm_exact(down, H, F, act_ref, 0)) < 1e-2
     assert b200q.device_error() == 0
+
+
+def _guarded(nbytes, fill=0xA5, guard=4096):
+    """a device buffer of exactly nbytes followed by a guard of a known byte (to catch writes past libbolt's sizes)"""
+    t = torch.full((nbytes + guard,), fill, dtype=torch.uint8, device=DEV)
+    _KEEP.append(t)
+    return t
+
+
+def test_shim_quant_nv4_rows_matches_libbolt():
+    """quant_nv4_rows writes libbolt's plain rows (q4 [T][k/2], sf [T][k/16]): libbolt's own B200 output, byte for byte,
+    and nothing past T rows"""
+    L = _harness()
+    i, o = golden("quant_nv4_rows")
+    T, k = i["x"].shape
+    q4, sf = _guarded(T * k // 2), _guarded(T * k // 16)
+    L.hs_quant_nv4_rows(s(), p(d(i["x"])), k, p(q4), p(sf), T, k)
+    q4, sf = q4.cpu().numpy(), sf.cpu().numpy()
+    assert np.array_equal(q4[:T * k // 2].reshape(T, k // 2), o["q4"])
+    assert np.array_equal(sf[:T * k // 16].reshape(T, k // 16), o["sf"])
+    assert (q4[T * k // 2:] == 0xA5).all() and (sf[T * k // 16:] == 0xA5).all()
+    assert b200q.device_error() == 0
+
+
+@pytest.mark.parametrize("n,k,T", [(18560, 4096, 300), (4096, 8192, 256), (640, 512, 37)])
+def test_shim_nv4_fp4_prompt_path(n, k, T):
+    """libbolt's BOLT_NV4_FP4 sequence (load_nv4w's tile_nv4w into buffers of libbolt's tile_bytes_nv4 /
+    tile_scale_bytes_nv4 sizes, then quant_nv4_rows + mma_nv4_fp4 per chunk) at config 3's in_proj (18560 rows: the
+    weight planes end in a 128-row tile) and out_proj, and a small ragged case: nothing written past libbolt's buffer
+    sizes; the result is this engine's own NVFP4 prompt GEMM's (b200q_quant_nv4_rows + b200q_nv4_gemm: the same
+    products and fp32 sums, relative L2 1e-6) and the oracle's NVFP4 x NVFP4 sum on sampled rows (1e-5)."""
+    import oracle as O
+    from helpers import rel_l2
+    from test_gpu_nv4_prompt import nv4_weights
+    L = _harness()
+    q, sc = nv4_weights(n + k, n, k)
+    s2 = 0.75
+    x = np.random.default_rng(T).standard_normal((T, k)).astype(np.float32)
+    qb, sb = L.hs_tile_bytes(0, 0, n, k), L.hs_tile_bytes(0, 1, n, k)
+    assert (qb, sb) == (n * k // 2, n * k // 16)
+    qw, sfw = _guarded(qb), _guarded(sb)
+    L.hs_tile_nv4w(s(), p(d(q)), p(d(sc)), p(qw), p(sfw), n, k)
+    q4, sf = _guarded(T * k // 2), _guarded(T * k // 16)
+    xt = d(x)
+    L.hs_quant_nv4_rows(s(), p(xt), k, p(q4), p(sf), T, k)
+    y = torch.full((T, n), -1.0, device=DEV)
+    L.hs_mma_nv4_fp4(s(), p(qw), p(sfw), s2, n, k, p(q4), p(sf), p(y), n, T)
+    torch.cuda.synchronize()
+    for buf, nb in ((qw, qb), (sfw, sb), (q4, T * k // 2), (sf, T * k // 16)):
+        assert (buf[nb:] == 0xA5).all()
+    assert b200q.device_error() == 0
+    got = y.cpu().numpy()
+    w = b200q.tile_nv4w(d(q), d(sc), n, k)
+    want = b200q.mma_nv4_fp4(w, s2, n, k, b200q.quant_nv4_rows(xt), T).cpu().numpy()
+    assert rel_l2(got, want) < 1e-6
+    rows = np.unique(np.r_[0, T - 1, np.random.default_rng(1).integers(0, T, 4)])
+    q4h, sfh = q4[:T * k // 2].cpu().numpy().reshape(T, k // 2), sf[:T * k // 16].cpu().numpy().reshape(T, k // 16)
+    ref = O.nv4_gemm_q4(q, sc, s2, n, k, q4h[rows], sfh[rows])
+    assert rel_l2(got[rows], ref) < 1e-5
