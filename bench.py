@@ -178,6 +178,18 @@ def graph_ms(call, n, reps=5):
     return ms
 
 
+def _event_ms(fn, n):
+    """mean ms of n calls fn(i) on the current stream, CUDA events around them"""
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(n):
+        fn(i)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / n
+
+
 def prefill_bench(b200q, layer, device, iters=5):
     """BASELINE config 4 on the tcgen05 prompt GEMMs: the routed experts' grouped up (ReLU^2) and down GEMMs over
     8192 tokens x top-6 (Zipf 1.1), and the Q8_0 GQA projections (q/k/v fused, then o) on the same 8192 tokens."""
@@ -240,11 +252,37 @@ def prefill_bench(b200q, layer, device, iters=5):
         ms = graph_ms(lambda i: b200q.mma_q8(wd[i % copies], 6144, H, xd, y=yd), 60)
         nbytes = 6144 * H * 34 // 32 + M * H * 2 + M * 6144 * 4
         dec[f"gqa_qkv_decode_M{M}_gbs"] = round(nbytes / (ms * 1e-3) / 1e9, 1)
+    # the model's lm_head (Q8_0 131072 x 4096, 570 MB: larger than L2, no copies needed) at decode rows (M = 1 / 16, the
+    # t16 GEMV) and verify windows (M = 128, the tcgen05 prompt GEMM): GB/s over weights + x + y, and TFLOPS
+    r = np.random.default_rng(50)
+    nl = 131072
+    raw = np.concatenate([r.uniform(1e-3, 1e-2, (nl, H // 32)).astype(np.float16).view(np.uint8).reshape(nl, H // 32, 2),
+                          r.integers(-127, 128, (nl, H // 32, 32), dtype=np.int8).view(np.uint8)], -1).reshape(-1)
+    raw_d = torch.from_numpy(raw).to(device)
+    del raw
+    w16, wtc = b200q.tile_q8(raw_d, nl, H), b200q.tile_q8_tc(raw_d, nl, H)
+    del raw_d
+    for M in (1, 16, 128):
+        xd = torch.randn(M, H, generator=g).to(torch.bfloat16).to(device)
+        yd = torch.empty(M, nl, dtype=torch.float32, device=device)
+        if M <= 16:
+            fn = lambda i, xd=xd, yd=yd: b200q.mma_q8(w16, nl, H, xd, y=yd)
+        else:
+            fn = lambda i, xd=xd, yd=yd: b200q.mma_q8_prompt(wtc, nl, H, xd, y=yd)
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        ms = graph_ms(fn, 20) if M <= 16 else _event_ms(fn, 20)
+        nbytes = nl * H * 34 // 32 + M * H * 2 + M * nl * 4
+        dec[f"lm_head_M{M}_gbs"] = round(nbytes / (ms * 1e-3) / 1e9, 1)
+        if M > 16:
+            dec[f"lm_head_M{M}_tflops"] = round(2.0 * M * nl * H / (ms * 1e-3) / 1e12, 1)
+    del w16, wtc
     err = b200q.device_error()
     cnt = counts.cpu().numpy()
     return {"workload": "BASELINE config 4: 8192 tokens x top-6 = 49152 rows over 128 IQ2_XXS experts (Zipf 1.1, "
                         "seeded permutation), 4096 -> 2048 -> 4096 ReLU^2; Q8_0 GQA q/k/v (fused 6144) + o on the "
-                        "same 8192 tokens",
+                        "same 8192 tokens; the lm_head (Q8_0 131072 x 4096) at 1 / 16 decode rows and 128 verify rows",
             "arithmetic": "fp16 operands (scales folded, rounded once), fp32 accumulation: tcgen05.mma kind::f16",
             "moe_ms": round(res["moe"][0], 4), "moe_tflops": round(res["moe"][1], 1),
             "gqa_ms": round(res["gqa"][0], 4), "gqa_tflops": round(res["gqa"][1], 1), **dec,
