@@ -511,7 +511,9 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
         up, down, _, _ = full_layer(b200q, device, 0)
         ex = LocalExperts(slice_slab(up, locp, up_b), slice_slab(down, locp, down_b), len(locp), H, F)
         del up, down
-        moe = ExpertParallelMoE(plp, rank, world, H, TOPK, ex.prompt, layout="exact", device=device)
+        # the exchange as a pipeline over pieces of the 8192 tokens (transfers under the GEMMs); one piece on one GPU
+        chunks = int(os.environ.get("B200Q_EP_CHUNKS", "0")) or (1 if world == 1 else 2 if world == 2 else 4)
+        moe = ExpertParallelMoE(plp, rank, world, H, TOPK, ex.prompt, layout="exact", device=device, chunks=chunks)
         g = torch.Generator().manual_seed(300 + rank)
         x = torch.randn(Tp, H, generator=g).to(torch.bfloat16).to(device)
         ridx = torch.from_numpy(zipf_routing(12 + 1000 * rank, Tp, TOPK, perm_seed=12)).to(device)
@@ -532,7 +534,7 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
         res["prefill"] = {"tflops": round(flops / (pms * 1e-3) / 1e12, 1), "ms": round(pms, 4),
                           "tokens_per_rank": Tp, "experts_per_rank": len(locp),
                           "expected_rank_imbalance": round(plp.imbalance(), 4),
-                          "copies": int(sum(len(o) for o in plp.owners)), "layout": "exact",
+                          "copies": int(sum(len(o) for o in plp.owners)), "layout": "exact", "pieces": chunks,
                           "step": "dispatch + group + tcgen05 up/down + return + combine"}
         del moe, ex
         torch.cuda.empty_cache()

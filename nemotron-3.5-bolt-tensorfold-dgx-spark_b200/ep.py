@@ -98,8 +98,12 @@ class ExpertParallelMoE:
     default.  shared_fn(x) -> [T][H] fp32 or None: the shared expert on this rank's tokens."""
 
     def __init__(self, placement, rank, world, H, topk, expert_fn, shared_fn=None, combine_fn=None, group=None,
-                 layout="capacity", send_dtype=torch.bfloat16, device=None):
+                 layout="capacity", send_dtype=torch.bfloat16, device=None, chunks=1):
         self.p, self.rank, self.world, self.H, self.topk = placement, rank, world, H, topk
+        # the exact layout's tokens in `chunks` consecutive pieces, exchanged and computed as a pipeline: the rows of
+        # piece c + 1 travel while the experts run on piece c, and piece c's outputs return while piece c + 1 runs.
+        # The same on every rank (the collectives must match); 1: one exchange each way
+        self.chunks = max(1, int(chunks))
         self.n_local = len(placement.local[rank])
         self.expert_fn, self.shared_fn = expert_fn, shared_fn
         self.combine_fn = combine_fn or _gpu_combine(topk)
@@ -116,13 +120,14 @@ class ExpertParallelMoE:
         self.fused = True
 
     # -- the pieces ----------------------------------------------------------------------------------------
-    def _route(self, ridx):
+    def _route(self, ridx, t0=0):
         """per pair: destination rank, local expert index there, the order that sorts pairs by destination, and
-        the pair's position inside its destination's block"""
+        the pair's position inside its destination's block; the tokens are t0, t0 + 1, ... (a replicated expert's pairs
+        go to its copies by token index)"""
         e = ridx.reshape(-1).to(torch.int64)
         pairs = e.numel()
         tok = torch.arange(pairs, device=e.device) // self.topk
-        rep = tok % self.nrep_t[e]
+        rep = (tok + t0) % self.nrep_t[e]
         dest = self.dest_t[e, rep]
         lidx = self.lidx_t[e, rep]
         order = torch.sort(dest, stable=True).indices
@@ -170,42 +175,79 @@ class ExpertParallelMoE:
         weights and sums them from the return buffer.  On one rank nothing is exchanged: the local experts run on the
         tokens' pairs in place (expert_fn with topk) and b200q_combine sums their fp32 outputs."""
         import b200q
-        T, H, topk = x.shape[0], self.H, self.topk
-        pairs = T * topk
-        dest, lidx, order, counts, pos, tok = self._route(ridx)
-        shared = None
         if self.world == 1:
+            lidx = self._route(ridx)[1]
             shared = self.shared_fn(x) if self.shared_fn else None
-            mo = self.expert_fn(x, lidx, self.n_local, topk=topk)
-            return b200q.k_combine(mo, rw.reshape(-1).contiguous(), topk, shared=shared)
+            mo = self.expert_fn(x, lidx, self.n_local, topk=self.topk)
+            return b200q.k_combine(mo, rw.reshape(-1).contiguous(), self.topk, shared=shared)
+        return self._exact(x, ridx, rw, fused=True)
+
+    def _exact(self, x, ridx, rw, fused):
+        """the exact exchange, as a pipeline over self.chunks pieces of consecutive tokens: every piece's per-peer
+        counts in one exchange (one host read for all pieces), then per piece the rows (send dtype) and their local
+        indices out, the local experts on the received rows, the outputs back; the next piece's rows are sent before
+        this piece's experts run, so the transfers overlap the GEMMs.  Then one combine over all pairs (fused: the
+        outputs gathered from the return buffer by b200q_ep_combine; otherwise the tensor-operation form)."""
+        T, H, topk, C = x.shape[0], self.H, self.topk, self.chunks
+        pairs = T * topk
+        tb = [T * c // C for c in range(C + 1)]
+        routes = [self._route(ridx[tb[c]:tb[c + 1]], tb[c]) for c in range(C)]
+        counts = torch.stack([r[3] for r in routes], 1).contiguous()        # [world][C]
         rc = torch.empty_like(counts)
-        self._a2a(rc, counts)
-        send_splits = counts.tolist()
-        recv_splits = rc.tolist()
-        send = x.to(self.send_dtype).index_select(0, tok[order])
-        send_l = lidx[order]
-        recv = torch.empty(sum(recv_splits), H, dtype=self.send_dtype, device=x.device)
-        recv_l = torch.empty(sum(recv_splits), dtype=torch.int64, device=x.device)
+        self._a2a(rc.view(-1), counts.view(-1))
+        send_splits = counts.t().tolist()                                   # [C][world]
+        recv_splits = rc.t().tolist()
+        got = torch.empty(pairs, H, dtype=self.send_dtype, device=x.device)
         ev = self.timing
+
+        def dispatch(c):
+            dest, lidx, order, _, _, tok = routes[c]
+            send = x[tb[c]:tb[c + 1]].to(self.send_dtype).index_select(0, tok[order])
+            send_l = lidx[order]
+            nr = sum(recv_splits[c])
+            recv = torch.empty(nr, H, dtype=self.send_dtype, device=x.device)
+            recv_l = torch.empty(nr, dtype=torch.int64, device=x.device)
+            w1 = self._a2a(recv, send, recv_splits[c], send_splits[c], async_op=True)
+            w2 = self._a2a(recv_l, send_l, recv_splits[c], send_splits[c], async_op=True)
+            return recv, recv_l, w1, w2
+
         if ev:
             ev[0].record()
-        w1 = self._a2a(recv, send, recv_splits, send_splits, async_op=True)
-        w2 = self._a2a(recv_l, send_l, recv_splits, send_splits, async_op=True)
-        shared = self.shared_fn(x) if self.shared_fn else None   # overlaps the dispatch
-        w1.wait()
-        w2.wait()
-        if ev:
-            ev[1].record()
-        y = self.expert_fn(recv, recv_l, self.n_local, out_dtype=self.send_dtype)
-        got = torch.empty(pairs, H, dtype=self.send_dtype, device=x.device)
-        if ev:
-            ev[2].record()
-        self._a2a(got, y, send_splits, recv_splits)
+        pend = dispatch(0)
+        shared = self.shared_fn(x) if self.shared_fn else None   # overlaps the first piece's dispatch
+        back = []
+        for c in range(C):
+            nxt = dispatch(c + 1) if c + 1 < C else None
+            recv, recv_l, w1, w2 = pend
+            w1.wait()
+            w2.wait()
+            if ev and c == 0:
+                ev[1].record()
+            if fused:
+                y = self.expert_fn(recv, recv_l, self.n_local, out_dtype=self.send_dtype)
+            else:
+                y = self.expert_fn(recv, recv_l, self.n_local).to(self.send_dtype)
+            if ev and c == C - 1:
+                ev[2].record()
+            back.append(self._a2a(got[tb[c] * topk:tb[c + 1] * topk], y, send_splits[c], recv_splits[c],
+                                  async_op=True))
+            pend = nxt
+        for w in back:
+            w.wait()
         if ev:
             ev[3].record()
-        slot = torch.empty(pairs, dtype=torch.int32, device=x.device)
-        slot.scatter_(0, order, torch.arange(pairs, dtype=torch.int32, device=x.device))   # pair p's row in got
-        return b200q.ep_combine(got, slot, rw, topk, shared)
+        if fused:
+            import b200q
+            slot = torch.empty(pairs, dtype=torch.int32, device=x.device)   # pair p's row in got
+            for c in range(C):
+                p0, p1 = tb[c] * topk, tb[c + 1] * topk
+                slot[p0:p1].scatter_(0, routes[c][2], torch.arange(p0, p1, dtype=torch.int32, device=x.device))
+            return b200q.ep_combine(got, slot, rw, topk, shared)
+        mo = torch.empty(pairs, H, dtype=torch.float32, device=x.device)
+        for c in range(C):
+            p0, p1 = tb[c] * topk, tb[c + 1] * topk
+            mo[p0:p1].index_copy_(0, routes[c][2], got[p0:p1].to(torch.float32))
+        return self.combine_fn(mo, rw, shared)
 
     def __call__(self, x, ridx, rw):
         """x [T][H] (this rank's tokens), ridx [T][topk] global expert ids, rw [T][topk] -> out [T][H] fp32"""
@@ -215,6 +257,8 @@ class ExpertParallelMoE:
             if self.layout == "capacity":
                 return self._capacity_fused(x, ridx, rw)
             return self._exact_fused(x, ridx, rw)
+        if self.layout != "capacity":
+            return self._exact(x, ridx, rw, fused=False)
         dest, lidx, order, counts, pos, tok = self._route(ridx)
         xs = x.to(self.send_dtype)
         ev = self.timing
@@ -246,31 +290,6 @@ class ExpertParallelMoE:
             if ev:
                 ev[3].record()
             got = back.index_select(0, slot)                     # sorted pair order
-        else:
-            rc = torch.empty_like(counts)
-            self._a2a(rc, counts)
-            send_splits = counts.tolist()
-            recv_splits = rc.tolist()
-            send = xs.index_select(0, tok[order])
-            send_l = lidx[order]
-            recv = torch.empty(sum(recv_splits), H, dtype=self.send_dtype, device=x.device)
-            recv_l = torch.empty(sum(recv_splits), dtype=torch.int64, device=x.device)
-            if ev:
-                ev[0].record()
-            w1 = self._a2a(recv, send, recv_splits, send_splits, async_op=True)
-            w2 = self._a2a(recv_l, send_l, recv_splits, send_splits, async_op=True)
-            shared = self.shared_fn(x) if self.shared_fn else None   # overlaps the dispatch
-            w1.wait()
-            w2.wait()
-            if ev:
-                ev[1].record()
-            y = self.expert_fn(recv, recv_l, self.n_local).to(self.send_dtype)
-            got = torch.empty(pairs, H, dtype=self.send_dtype, device=x.device)
-            if ev:
-                ev[2].record()
-            self._a2a(got, y, send_splits, recv_splits)
-            if ev:
-                ev[3].record()
         mo = torch.empty(pairs, H, dtype=torch.float32, device=x.device)
         mo.index_copy_(0, order, got.to(torch.float32))
         return self.combine_fn(mo, rw, shared)

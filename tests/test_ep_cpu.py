@@ -62,7 +62,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, layout, dtype_name, replicate, q):
+def _worker(rank, world, port, layout, dtype_name, replicate, q, chunks=1):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
@@ -81,7 +81,7 @@ def _worker(rank, world, port, layout, dtype_name, replicate, q):
             return out
 
         moe = ExpertParallelMoE(pl, rank, world, H, TOPK, expert_fn, shared_fn=lambda x: x.float() @ shared.T,
-                                combine_fn=_combine, layout=layout, send_dtype=getattr(torch, dtype_name))
+                                combine_fn=_combine, layout=layout, send_dtype=getattr(torch, dtype_name), chunks=chunks)
         x, ridx, rw = _tokens(rank)
         out = moe(x, ridx, rw)
         q.put((rank, out.numpy()))
@@ -89,11 +89,12 @@ def _worker(rank, world, port, layout, dtype_name, replicate, q):
         dist.destroy_process_group()
 
 
-def _run(layout, dtype_name, replicate=0, world=2):
+def _run(layout, dtype_name, replicate=0, world=2, chunks=1):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, layout, dtype_name, replicate, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, layout, dtype_name, replicate, q, chunks))
+             for r in range(world)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=120) for _ in range(world))
@@ -114,6 +115,17 @@ def test_ep_matches_single_process_fp32(layout):
 def test_ep_matches_single_process_more_ranks(layout, world):
     """the scaling run's rank counts: 8 experts over 4 ranks (2 each) and 8 ranks (1 each), fp32 transfers"""
     got = _run(layout, "float32", world=world)
+    assert sorted(got) == list(range(world))
+    for r, out in got.items():
+        assert np.array_equal(out, _reference(r).numpy())
+
+
+@pytest.mark.parametrize("world,chunks,replicate", [(2, 3, 0), (4, 2, 0), (2, 7, 0), (2, 2, 2)])
+def test_ep_exact_pipelined_chunks(world, chunks, replicate):
+    """the exact layout as a pipeline over pieces of the tokens (5 tokens: pieces of 1 and 2 tokens, and more pieces
+    than tokens, some empty): the same values reach the same places, so the same bytes as the single-process layer;
+    with replicated experts the copies are chosen by the global token index, as without pieces"""
+    got = _run("exact", "float32", replicate=replicate, world=world, chunks=chunks)
     assert sorted(got) == list(range(world))
     for r, out in got.items():
         assert np.array_equal(out, _reference(r).numpy())

@@ -148,3 +148,69 @@ def test_two_rank_peer_decode_matches_fused_layer(dt):
     for p in procs:
         p.join(timeout=60)
     assert all(ok for _, ok, _ in res), res
+
+
+def _prompt_worker(rank, world, port, q, chunks):
+    try:
+        import datetime
+        import sys
+        here = os.path.dirname(os.path.abspath(__file__))
+        root = os.path.dirname(here)
+        for p in (here, os.path.join(root, "oracle"), os.path.join(root, "nemotron-3.5-bolt-tensorfold-dgx-spark_b200")):
+            sys.path.insert(0, p)
+        import torch.distributed as dist
+        import b200q
+        from ep import ExpertParallelMoE, LocalExperts, Placement, slice_slab
+        from helpers import iq2_blocks, normal_bf16, rel_l2
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+        T, H, F, E, topk = 600, 1024, 512, 16, 4
+        d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+        up, down = iq2_blocks(1, E * F, H), iq2_blocks(2, E * H, F)
+        pu, pd = b200q.repack_iq2(d(up.reshape(-1)), E * F, H), b200q.repack_iq2(d(down.reshape(-1)), E * H, F)
+        xb, _ = normal_bf16(30 + rank, (T, H))
+        lb, _ = normal_bf16(40 + rank, (T, E))
+        xt, lt = d(xb).view(torch.bfloat16), d(lb).view(torch.bfloat16)
+        ridx, rw = b200q.k_route(lt, topk)
+        # every expert on this GPU: the reference
+        full = Placement(E, 1, seed=0)
+        one = LocalExperts(slice_slab(pu, full.local[0], b200q.iq2_bytes(F, H)),
+                           slice_slab(pd, full.local[0], b200q.iq2_bytes(H, F)), E, H, F)
+        ref_moe = ExpertParallelMoE(full, 0, 1, H, topk, one.prompt, layout="exact", device=dev)
+        want = ref_moe(xt, ridx, rw).cpu().numpy()
+        res = []
+        for send in (torch.float32, torch.bfloat16):
+            pl = Placement(E, world, seed=3)
+            loc = pl.local[rank]
+            ex = LocalExperts(slice_slab(pu, loc, b200q.iq2_bytes(F, H)), slice_slab(pd, loc, b200q.iq2_bytes(H, F)),
+                              len(loc), H, F)
+            moe = ExpertParallelMoE(pl, rank, world, H, topk, ex.prompt, layout="exact", send_dtype=send, device=dev,
+                                    chunks=chunks)
+            got = moe(xt, ridx, rw).cpu().numpy()
+            res.append(rel_l2(got, want))
+        ok = res[0] < 1e-6 and res[1] < 1e-2 and b200q.device_error() == 0
+        dist.destroy_process_group()
+        q.put((rank, ok, res))
+    except Exception as e:   # report, never hang the parent
+        q.put((rank, False, repr(e)))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("chunks", [1, 3])
+def test_two_rank_prompt_exchange_matches_one_gpu(chunks):
+    """the prompt layer's exact exchange over NCCL on two GPUs, in one piece and as a three-piece pipeline, against the
+    same tokens with every expert on one GPU (the same tcgen05 GEMMs): fp32 transfers within 1e-6 relative L2 (the
+    GEMM's sums do not depend on which rows share a tile), bf16 transfers within BASELINE's tolerance"""
+    ctx = torch.multiprocessing.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_prompt_worker, args=(r, 2, port, q, chunks)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(ok for _, ok, _ in res), res
