@@ -511,8 +511,9 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
         up, down, _, _ = full_layer(b200q, device, 0)
         ex = LocalExperts(slice_slab(up, locp, up_b), slice_slab(down, locp, down_b), len(locp), H, F)
         del up, down
-        # the exchange as a pipeline over pieces of the 8192 tokens (transfers under the GEMMs); one piece on one GPU
-        chunks = int(os.environ.get("B200Q_EP_CHUNKS", "0")) or (1 if world == 1 else 2 if world == 2 else 4)
+        # the exchange in one piece: a pipeline over pieces (B200Q_EP_CHUNKS) measured slower at 2 GPUs (815 / 774 / 630
+        # TFLOPS for 1 / 2 / 4 pieces): the persistent GEMMs hold every SM, so NCCL's kernels wait for them
+        chunks = int(os.environ.get("B200Q_EP_CHUNKS", "1"))
         moe = ExpertParallelMoE(plp, rank, world, H, TOPK, ex.prompt, layout="exact", device=device, chunks=chunks)
         g = torch.Generator().manual_seed(300 + rank)
         x = torch.randn(Tp, H, generator=g).to(torch.bfloat16).to(device)
