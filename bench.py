@@ -514,7 +514,8 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
         # the exchange in one piece: a pipeline over pieces (B200Q_EP_CHUNKS) measured slower at 2 GPUs (815 / 774 / 630
         # TFLOPS for 1 / 2 / 4 pieces): the persistent GEMMs hold every SM, so NCCL's kernels wait for them
         chunks = int(os.environ.get("B200Q_EP_CHUNKS", "1"))
-        moe = ExpertParallelMoE(plp, rank, world, H, TOPK, ex.prompt, layout="exact", device=device, chunks=chunks)
+        moe = ExpertParallelMoE(plp, rank, world, H, TOPK, ex.prompt, layout="exact", device=device, chunks=chunks,
+                                sm_reserve=int(os.environ.get("B200Q_EP_SM_RESERVE", "16")))
         g = torch.Generator().manual_seed(300 + rank)
         x = torch.randn(Tp, H, generator=g).to(torch.bfloat16).to(device)
         ridx = torch.from_numpy(zipf_routing(12 + 1000 * rank, Tp, TOPK, perm_seed=12)).to(device)
@@ -531,11 +532,32 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
         torch.cuda.synchronize()
         barrier()
         pms = max_ms(ev0.elapsed_time(ev1)) / iters
+        # where a step's time goes (one more step, events between its pieces): routing + counts exchange + host read
+        # + dispatch of the first piece, the local experts' GEMMs, the returns, and the combine
+        parts = None
+        if dist:   # (on one rank nothing is exchanged)
+            pev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+            moe.timing = pev[1:5]
+            barrier()
+            torch.cuda.synchronize()
+            pev[0].record()
+            moe(x, ridx, rw)
+            pev[5].record()
+            torch.cuda.synchronize()
+            moe.timing = None
+            t = torch.tensor([pev[i].elapsed_time(pev[i + 1]) for i in range(5)], device=device)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            parts = t.cpu().tolist()
         flops = world * 2.0 * Tp * TOPK * H * F * 2
         res["prefill"] = {"tflops": round(flops / (pms * 1e-3) / 1e12, 1), "ms": round(pms, 4),
                           "tokens_per_rank": Tp, "experts_per_rank": len(locp),
                           "expected_rank_imbalance": round(plp.imbalance(), 4),
                           "copies": int(sum(len(o) for o in plp.owners)), "layout": "exact", "pieces": chunks,
+                          "step_parts_ms": None if parts is None else {
+                              "route_counts_hostread": round(parts[0], 4), "dispatch_first_piece": round(parts[1], 4),
+                              "experts_all_pieces": round(parts[2], 4), "returns": round(parts[3], 4),
+                              "combine": round(parts[4], 4),
+                              "note": "one step with events between its pieces, each the slowest rank's"},
                           "step": "dispatch + group + tcgen05 up/down + return + combine"}
         del moe, ex
         torch.cuda.empty_cache()

@@ -260,6 +260,11 @@ int b200q_ep_pack(const void* x, int x_dtype, int T, int H, const int* ridx, int
 int b200q_ep_combine(const void* back, int back_dtype, int ldb, const int* slot, const float* rw, const float* shared,
                      int T, int topk, int H, void* out, int out_dtype, void* stream);
 
+/* SMs the persistent prompt GEMMs (b200q_moe_prompt, b200q_q8_gemm) leave free on the current device, 0 .. 128 (0 at
+ * load): a pipelined expert-parallel exchange sets it while its transfers run beside the GEMMs, so that the
+ * collective's kernels find SMs (no counterpart in libbolt, which is single-GPU).  Host-side, per device. */
+int b200q_set_sm_reserve(int sms);
+
 /* The expert-parallel decode step with its exchange over NVLink peer memory (no counterpart in libbolt, which is
  * single-GPU; the layer is the MoE block of enqueue_block, bolt_host.cu:665-720).  Every rank holds one region of
  * b200q_ep_peer_region_bytes (allocated by b200q_peer_alloc, zeroed), exports it (b200q_peer_export), and maps every

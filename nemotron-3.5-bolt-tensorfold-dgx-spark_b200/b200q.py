@@ -66,6 +66,7 @@ def lib():
             "b200q_peer_handle_bytes": (sz, []), "b200q_peer_export": (i32, [vp, ctypes.c_char_p]),
             "b200q_peer_open": (i32, [ctypes.c_char_p, ctypes.POINTER(vp)]), "b200q_peer_close": (i32, [vp]),
             "b200q_ep_peer_error": (i32, [vp, i32]),
+            "b200q_set_sm_reserve": (i32, [i32]),
             "b200q_ep_peer_decode": (i32, [vp, i32, vp, i32, i32, i32, i32, i32, i32, i32, vp, f32, vp, vp, vp, i32,
                                            vp, vp, i32, i32, i32, i32, vp, vp, i32, vp, vp, sz, vp, i32, vp, vp, i32,
                                            vp]),

@@ -635,6 +635,10 @@ static int x_num_sms() {
     return sms[dev];
 }
 
+// SMs the persistent prompt GEMMs leave free on a device (b200q_set_sm_reserve): while a pipelined expert-parallel
+// exchange runs, NCCL's kernels need SMs beside the GEMMs
+static int g_sm_reserve[64];
+
 template <class Deq, class Epi>
 static cudaError_t launch_x(const XArgs& a, const Epi& epi, cudaStream_t s) {
     static int max_clusters = 0;   // SM pairs that can hold one cluster each
@@ -660,7 +664,11 @@ static cudaError_t launch_x(const XArgs& a, const Epi& epi, cudaStream_t s) {
         max_clusters = n;
     }
     const long long work = (long long)a.max_mtiles * ((a.N + kXN - 1) / kXN);
-    const int clusters = (int)(work < max_clusters ? work : max_clusters);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int reserve = (dev >= 0 && dev < 64) ? g_sm_reserve[dev] : 0;
+    const int avail = max_clusters - (reserve + 1) / 2 > 1 ? max_clusters - (reserve + 1) / 2 : 1;
+    const int clusters = (int)(work < avail ? work : avail);
     if (clusters <= 0) return cudaSuccess;
     return launch(tcx_gemm_k<Deq, Epi>, dim3(2 * clusters), dim3(kXThreads), x_smem<Deq>(), s, a, epi);
 }
@@ -800,6 +808,13 @@ static MoeWs moe_ws(int pairs, int E, int H, int F) {
 }  // namespace b200q
 
 using namespace b200q;
+
+extern "C" int b200q_set_sm_reserve(int sms) {
+    int dev = 0;
+    if (sms < 0 || sms > 128 || cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return B200Q_EINVAL;
+    g_sm_reserve[dev] = sms;
+    return B200Q_OK;
+}
 
 extern "C" {
 

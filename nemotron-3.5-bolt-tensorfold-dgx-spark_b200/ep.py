@@ -98,12 +98,15 @@ class ExpertParallelMoE:
     default.  shared_fn(x) -> [T][H] fp32 or None: the shared expert on this rank's tokens."""
 
     def __init__(self, placement, rank, world, H, topk, expert_fn, shared_fn=None, combine_fn=None, group=None,
-                 layout="capacity", send_dtype=torch.bfloat16, device=None, chunks=1):
+                 layout="capacity", send_dtype=torch.bfloat16, device=None, chunks=1, sm_reserve=16):
         self.p, self.rank, self.world, self.H, self.topk = placement, rank, world, H, topk
         # the exact layout's tokens in `chunks` consecutive pieces, exchanged and computed as a pipeline: the rows of
         # piece c + 1 travel while the experts run on piece c, and piece c's outputs return while piece c + 1 runs.
         # The same on every rank (the collectives must match); 1: one exchange each way
         self.chunks = max(1, int(chunks))
+        # with more than one piece on CUDA, the SMs the persistent prompt GEMMs leave free while the pipeline runs, so
+        # that the collectives' kernels can run beside them (b200q_set_sm_reserve)
+        self.sm_reserve = int(sm_reserve)
         self.n_local = len(placement.local[rank])
         self.expert_fn, self.shared_fn = expert_fn, shared_fn
         self.combine_fn = combine_fn or _gpu_combine(topk)
@@ -213,6 +216,21 @@ class ExpertParallelMoE:
 
         if ev:
             ev[0].record()
+        reserve = fused and C > 1 and x.is_cuda
+        if reserve:
+            import b200q
+            b200q.lib().b200q_set_sm_reserve(self.sm_reserve)
+        try:
+            return self._exact_pieces(x, rw, fused, tb, routes, send_splits, recv_splits, got, dispatch)
+        finally:
+            if reserve:
+                b200q.lib().b200q_set_sm_reserve(0)
+
+    def _exact_pieces(self, x, rw, fused, tb, routes, send_splits, recv_splits, got, dispatch):
+        """the pipeline of _exact over its pieces, and the combine"""
+        T, H, topk, C = x.shape[0], self.H, self.topk, self.chunks
+        pairs = T * topk
+        ev = self.timing
         pend = dispatch(0)
         shared = self.shared_fn(x) if self.shared_fn else None   # overlaps the first piece's dispatch
         back = []
