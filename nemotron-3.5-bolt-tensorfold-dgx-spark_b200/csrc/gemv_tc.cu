@@ -10,8 +10,13 @@
 //   The activations are converted to fp16 once (exact for bf16 inputs in fp16's normal range).
 // Mapping: a warp owns one 16-row tile over one K slice; the eight warps of a CTA own eight consecutive tiles and
 // share the slice's activations in shared memory.  grid.y splits K so that about four CTAs run per SM; the slices'
-// fp32 partials are summed in slice order by a second kernel, so results do not depend on timing.
+// fp32 partials are summed in slice order, so results do not depend on timing: by the last CTA of each column to
+// finish (an arrival count a column) for NVFP4 at up to 8 rows, a call then being one launch; by a second kernel
+// otherwise (measured faster there: the last CTA's sum is a serial tail the second kernel spreads over the GPU).
 #include "common.cuh"
+
+#include <atomic>
+#include <mutex>
 
 namespace b200q {
 
@@ -138,6 +143,8 @@ __global__ void q8_pack_k(const uint8_t* __restrict__ raw, uint8_t* __restrict__
 // ---------------------------------------------------------------------------------------------------------
 // the GEMV
 // ---------------------------------------------------------------------------------------------------------
+constexpr int kTcWarps = 8;
+
 struct TcArgs {
     const uint8_t* w;
     int n, k;
@@ -148,9 +155,33 @@ struct TcArgs {
     float* out;     // KS == 1: y [T][ldy]; else partials [KS][T][n]
     int ldo;
     const uint8_t* wsc;   // the split layout (libbolt's tile buffers): w holds the units' 512 code bytes, wsc their scales
+    float* y;             // KS > 1: the result y [T][ldo], summed from the partials in the launch
+    int* cols;            // KS > 1: an arrival count a column of CTAs (blockIdx.x), zero at entry, reset at exit
 };
 
-constexpr int kTcWarps = 8;
+// The K split's sum inside the launch: the last CTA of a column to finish adds its rows' partials over the slices in
+// slice order and scales by s2 (the arithmetic of a separate sum pass, s = part[0] + part[1] + ...), then resets the
+// column's count for the next launch that takes the same counters.
+// (No shared memory: a static array beside the launches' dynamic shared memory would cost a CTA an SM.)
+__device__ __forceinline__ void tc_fold(const TcArgs& a) {
+    __syncthreads();
+    int last = 0;
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(a.cols + blockIdx.x, 1) == (int)gridDim.y - 1;
+        __threadfence();
+    }
+    if (!__syncthreads_or(last)) return;
+    const int r0 = blockIdx.x * kTcWarps * 16, rows = min(kTcWarps * 16, a.n - r0);
+    for (int i = threadIdx.x; i < a.T * rows; i += blockDim.x) {
+        const int tok = i / rows, row = r0 + (i - tok * rows);
+        float s = 0.f;
+        for (int ks = 0; ks < (int)gridDim.y; ks++) s += __ldcg(a.out + ((size_t)ks * a.T + tok) * a.n + row);
+        a.y[(size_t)tok * a.ldo + row] = s * a.s2;
+    }
+    if (threadIdx.x == 0) a.cols[blockIdx.x] = 0;
+}
+
 enum { kFmtNv4 = 0, kFmtQ8 = 1 };
 // units a lane keeps in flight, and the CTAs an SM the K split aims at, per format (measured on B200 over 4 / 8 / 16
 // units and 4 / 8 CTAs at config 3's and the GQA projections' shapes, M 1 and 16: tc_gemv_k is fastest for NVFP4 at
@@ -184,7 +215,7 @@ __device__ __forceinline__ void q8_frag(uint32_t w0, uint32_t w1, uint32_t (&a)[
     a[3] = hsub2(prmt(x1, 0x64646464u, 0x7362u), bias);
 }
 
-template <int FMT, int NT, bool SPLIT>
+template <int FMT, int NT, bool SPLIT, bool FOLD = false>
 __global__ void __launch_bounds__(kTcWarps * 32) tc_gemv_k(TcArgs a) {
     pdl_wait();
     extern __shared__ __align__(16) unsigned char dyn[];
@@ -338,6 +369,7 @@ __global__ void __launch_bounds__(kTcWarps * 32) tc_gemv_k(TcArgs a) {
                 }
             }
     }
+    if constexpr (FOLD) tc_fold(a);
     pdl_trigger();
 }
 
@@ -571,6 +603,27 @@ __global__ void splitk_sum_k(const float* __restrict__ part, int KS, int T, int 
     pdl_trigger();
 }
 
+// the K-split launches' column counts: kTcSlots launch slots taken in turn (so that launches in flight on different
+// streams do not share counts), kTcMaxCols columns each; zero at load, every launch leaves its slot's counts at zero
+constexpr int kTcSlots = 32, kTcMaxCols = 2048;
+__device__ int g_tc_cols[kTcSlots][kTcMaxCols];
+
+static int* tc_cols_slot() {
+    static std::mutex mu;
+    static int* base[64] = {nullptr};
+    static std::atomic<unsigned> next{0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!base[dev] && cudaGetSymbolAddress((void**)&base[dev], g_tc_cols) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+    }
+    return base[dev] + (size_t)(next.fetch_add(1u) % kTcSlots) * kTcMaxCols;
+}
+
 // K slice: about TcTune<FMT>::kCtasPerSm CTAs an SM over the row tiles, slices a multiple of 256
 static int slice_len(int fmt, int n, int k) {
     const int ctas_x = (n / 16 + kTcWarps - 1) / kTcWarps;
@@ -595,11 +648,20 @@ constexpr size_t kMaxSmem = 232448;   // 227 KB, the opt-in limit a CTA
 
 template <int FMT, int NT, bool SPLIT>
 static cudaError_t launch_tc(const TcArgs& a, dim3 grid, cudaStream_t s) {
-    static size_t opted = 0;
+    static size_t opted = 0, opted_fold = 0;
     const size_t smem = tc_smem<FMT>(NT * 8, a.L);
     void (*kern)(TcArgs);
+    const bool fold = a.cols != nullptr;   // NVFP4 at up to 8 rows: the K split's sum in the launch
     if constexpr (FMT == kFmtQ8) kern = tc_ring_k<FMT, NT, SPLIT>;
+    else if constexpr (NT == 1) kern = fold ? tc_gemv_k<FMT, NT, SPLIT, true> : tc_gemv_k<FMT, NT, SPLIT, false>;
     else kern = tc_gemv_k<FMT, NT, SPLIT>;
+    if (fold && smem > 48 * 1024 && smem > opted_fold) {
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        opted_fold = smem;
+        return launch(kern, grid, dim3(kTcWarps * 32), smem, s, a);
+    }
+    if (fold) return launch(kern, grid, dim3(kTcWarps * 32), smem, s, a);
     if (smem > 48 * 1024 && smem > opted) {
         const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
@@ -623,13 +685,18 @@ static int run_tc(const uint8_t* w, float s2, int n, int k, const void* x, int x
         return run_tc<FMT>(w, s2, n, k, (const char*)x + 8 * (size_t)ldx * xe, x_dtype, ldx, T - 8, y + 8 * (size_t)ldy, ldy,
                            ws, ws_bytes, s, wsc);
     }
-    TcArgs a{w, n, k, x, x_dtype, ldx, T, L, s2, KS > 1 ? (float*)ws : y, ldy, wsc};
     const dim3 grid((n / 16 + kTcWarps - 1) / kTcWarps, KS);
+    // the sum in the launch: NVFP4 at up to 8 rows (measured on B200, M = 1: in_proj 2083 against 2062 GB/s, out_proj
+    // 1618 against 1511; at M = 16, and for Q8_0 at M = 1 and 16, the second kernel was faster)
+    const bool fold = FMT == kFmtNv4 && T <= 8 && KS > 1 && grid.x <= (unsigned)kTcMaxCols;
+    int* cols = fold ? tc_cols_slot() : nullptr;
+    TcArgs a{w, n, k, x, x_dtype, ldx, T, L, s2, KS > 1 ? (float*)ws : y, ldy, wsc, y, cols};
+    const dim3 grid2((n / 16 + kTcWarps - 1) / kTcWarps, KS);
     cudaError_t e;
-    if (wsc) e = T > 8 ? launch_tc<FMT, 2, true>(a, grid, s) : launch_tc<FMT, 1, true>(a, grid, s);
-    else e = T > 8 ? launch_tc<FMT, 2, false>(a, grid, s) : launch_tc<FMT, 1, false>(a, grid, s);
+    if (wsc) e = T > 8 ? launch_tc<FMT, 2, true>(a, grid2, s) : launch_tc<FMT, 1, true>(a, grid2, s);
+    else e = T > 8 ? launch_tc<FMT, 2, false>(a, grid2, s) : launch_tc<FMT, 1, false>(a, grid2, s);
     if (e != cudaSuccess) return status_from(e);
-    if (KS > 1) {
+    if (KS > 1 && !cols) {
         const int64_t tot = (int64_t)T * n;
         e = launch(splitk_sum_k, dim3((unsigned)((tot + 255) / 256)), dim3(256), 0, s, (const float*)ws, KS, T, n, s2, y, ldy);
         if (e != cudaSuccess) return status_from(e);
