@@ -11,15 +11,16 @@
 //   2. the local experts' prologue (b200q_moe_experts_decode's, the shared expert being the last local expert): wait
 //      until every sender's dispatch flag holds the epoch, then group the received rows by local expert and schedule
 //      the GEMVs.
-//   3. the fused up/down GEMVs over those rows; the outputs stay in this rank's region, and the launch's last CTA
-//      publishes the epoch in every sender's return flags (GemvArgs::done_*).
-//   4. ep_peer_combine_k: wait for every owner's return flag, then read each pair's output row from its owner's
-//      region (peer loads) and combine them with the router weights (combine_k's order, bolt_kernels.cu:1714-1727),
-//      plus the shared expert's row.
+//   3. the fused up/down GEMVs over those rows; the down GEMV stores each routed row's output straight into its
+//      sender's return rows (peer stores through a row-address table the prologue fills, GemvArgs::y_rows; the shared
+//      expert's rows stay here), and the launch's last CTA publishes the epoch in every sender's return flags
+//      (GemvArgs::done_*).
+//   4. ep_peer_combine_k: wait for every owner's return flag, then combine this rank's return rows (local loads) with
+//      the router weights (combine_k's order, bolt_kernels.cu:1714-1727), plus the shared expert's row.
 //
 // Buffer reuse needs no second copy: a sender's next dispatch comes after its combine, which waits for every owner's
-// step to be done with the rows it received; an owner's next outputs come after its next prologue, which waits for
-// every sender's next dispatch, so after every sender's combine.  Every wait is bounded (moe.cuh wait_epochs): a rank
+// step to be done with the rows it received; an owner's next outputs (into the senders' return rows) come after its
+// next prologue, which waits for every sender's next dispatch, so after every sender's combine.  Every wait is bounded (moe.cuh wait_epochs): a rank
 // that never arrives sets an error bit in the state and the step completes with wrong values instead of hanging.
 //
 // The region (one cudaMalloc a rank, exported by CUDA IPC, the same layout on every rank), R = world * cap + T rows
@@ -27,7 +28,10 @@
 // after them):
 //   xq    [R][H] int8, xs [R][H/32] fp32    the rows the GEMVs read
 //   lidx  [R] int32                         each row's local expert
-//   y     [R][H] of the return type         the GEMVs' outputs
+//   srcp  [R] int32                         each received row's pair index at its sender
+//   y     [R][H] of the return type         the shared expert's outputs (its rows, the last T)
+//   ret   [cap][H] of the return type       this rank's pairs' outputs, written by their owners
+//   yptr  [R] u64                           each row's output address (filled by the owner's prologue)
 //   flags [2][world] int32                  [0][s] the epoch of sender s's dispatch, [1][o] of owner o's outputs
 #include <cstring>
 
@@ -37,8 +41,8 @@
 namespace b200q {
 
 struct EpRegion {
-    int cap, R, elt;                          // rows from each sender, all rows, the return type's bytes
-    size_t xq, xs, lidx, y, flags, bytes;     // byte offsets in the region, its size
+    int cap, R, elt;                                        // rows from each sender, all rows, the return type's bytes
+    size_t xq, xs, lidx, srcp, y, ret, yptr, flags, bytes;  // byte offsets in the region, its size
 };
 static size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
 static EpRegion ep_region(int world, int T, int H, int topk, int elt) {
@@ -50,7 +54,10 @@ static EpRegion ep_region(int world, int T, int H, int topk, int elt) {
     r.xq = o; o += al256((size_t)r.R * H);
     r.xs = o; o += al256((size_t)r.R * (H / 32) * 4);
     r.lidx = o; o += al256((size_t)r.R * 4);
+    r.srcp = o; o += al256((size_t)r.R * 4);
     r.y = o; o += al256((size_t)r.R * H * elt);
+    r.ret = o; o += al256((size_t)r.cap * H * elt);
+    r.yptr = o; o += al256((size_t)r.R * 8);
     r.flags = o; o += al256((size_t)2 * world * 4);
     r.bytes = o;
     return r;
@@ -194,7 +201,10 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_k(const EpArgs a) {
         }
         unsigned char* dst = a.peers[d];
         quant_row_to(a, t, dst, row);
-        if (threadIdx.x == 0) reinterpret_cast<int*>(dst + a.reg.lidx)[row] = l;
+        if (threadIdx.x == 0) {
+            reinterpret_cast<int*>(dst + a.reg.lidx)[row] = l;
+            reinterpret_cast<int*>(dst + a.reg.srcp)[row] = i < pairs ? i : -1;
+        }
     }
     // the unused rows of this rank's block at every owner: the discard index (never computed there)
     for (int j = blockIdx.x * kEpThreads + threadIdx.x; j < a.world * cap; j += gridDim.x * kEpThreads) {
@@ -220,9 +230,9 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_k(const EpArgs a) {
     pdl_trigger();
 }
 
-// Launch 4 (the last): out[t][h] = sum over k in order of rw[t][k] * y_owner[row of pair (t, k)][h] (fma), + the
-// shared expert's row.  A thread owns 8 consecutive h; the pair rows come over NVLink (L1-bypassing loads), the loads
-// of up to kBatch pairs issued before their fmas so that the round trips overlap.
+// Launch 4 (the last): out[t][h] = sum over k in order of rw[t][k] * ret[pair (t, k)][h] (fma), + the shared expert's
+// row.  A thread owns 8 consecutive h; the return rows were stored here by their owners (L1-bypassing loads), the
+// loads of up to kBatch pairs issued before their fmas.
 __device__ __forceinline__ void load8(const unsigned char* p, int elt, float* v) {
     if (elt == 2) {
         const uint4 u = __ldcg(reinterpret_cast<const uint4*>(p));
@@ -262,7 +272,7 @@ __global__ void __launch_bounds__(128) ep_peer_combine_k(const EpArgs a) {
             w[b] = 0.f;
             if (ok[b]) {
                 w[b] = rw[p];
-                load8(a.peers[d] + a.reg.y + ((size_t)slot[2 * p + 1] * a.H + h0) * elt, elt, v[b]);
+                load8(a.peers[a.rank] + a.reg.ret + ((size_t)p * a.H + h0) * elt, elt, v[b]);
             }
         }
 #pragma unroll
@@ -401,6 +411,14 @@ int b200q_ep_peer_decode(const void* x, int x_dtype, const void* logits, int log
         pe.done_base = a.peers;
         pe.done_off = a.reg.flags + (size_t)(world + rank) * 4;
         pe.done_n = world;
+        pe.srcp = reinterpret_cast<const int*>(self + a.reg.srcp);
+        pe.peers = a.peers;
+        pe.ret_off = a.reg.ret;
+        pe.cap = a.reg.cap;
+        pe.world = world;
+        pe.row_bytes = H * a.reg.elt;
+        pe.yloc = self + a.reg.y;
+        pe.yptr = reinterpret_cast<unsigned long long*>(self + a.reg.yptr);
         st = experts_decode(nullptr, B200Q_BF16, H, a.reg.R, H, F, reinterpret_cast<const int*>(self + a.reg.lidx), 1,
                             n_local + 1, up, down, self + a.reg.y, ret_dtype, H, workspace, workspace_bytes, stream,
                             &pe);

@@ -583,7 +583,7 @@ struct Ids {
     int v[kUnitTok];
 };
 
-template <int NT, int EPI, bool FUSED, bool kScl>
+template <int NT, int EPI, bool FUSED, bool kScl, bool PTRS = false>
 __device__ __forceinline__ bool unit_rows(const GemvArgs& a, const GemvArgs& pa, const GemvArgs& pb, int g,
                                           const Ids& ids, int lane, Ring& r, Producer<kScl>& pr, const Sched& sc,
                                           const int* ready, int* release, int ctr, int nsb) {
@@ -689,6 +689,10 @@ __device__ __forceinline__ bool unit_rows(const GemvArgs& a, const GemvArgs& pa,
                 const float inv = am > 0.f ? 127.f / am : 0.f;
                 a.aq[(size_t)id[m] * a.n + row] = (int8_t)__float2int_rn(v * inv);
                 if (lane == 0) a.as[(size_t)id[m] * (a.n >> 5) + g] = am / 127.f;
+            } else if constexpr (PTRS) {   // every id's output row at its own address (GemvArgs::y_rows)
+                unsigned char* dst = reinterpret_cast<unsigned char*>(a.y_rows[id[m]]);
+                if (a.y_bf16) reinterpret_cast<__nv_bfloat16*>(dst)[row] = __float2bfloat16_rn(v);
+                else reinterpret_cast<float*>(dst)[row] = v;
             } else {
                 if (a.y_bf16) reinterpret_cast<__nv_bfloat16*>(a.y)[(size_t)id[m] * a.ldy + row] = __float2bfloat16_rn(v);
                 else a.y[(size_t)id[m] * a.ldy + row] = v;
@@ -834,7 +838,7 @@ __device__ void layer_epilogue(const LayerArgs& L, const GemvArgs& b, int ctr) {
 
 // One launch: the units of one phase (EPI), or a fused up (kRelu2Q8, args a) + down (kStore, args b) pair over the
 // same slots, whose schedule the fused form requires (a.sched); LAYER: the whole decode layer around the fused pair.
-template <int EPI, bool FUSED, bool LAYER>
+template <int EPI, bool FUSED, bool LAYER, bool PTRS = false>
 __device__ __forceinline__ void gemv_body(const GemvArgs& a, const GemvArgs& b, int* ready, int nslots,
                                           const LayerArgs& L) {
     static_assert(!FUSED || EPI == kRelu2Q8, "a fused launch is up (relu^2 + int8 rows) then down");
@@ -950,9 +954,9 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, const GemvArgs& b, 
         if constexpr (FUSED) down_unit = ph != 0;
         if constexpr (FUSED) {
             if (down_unit) {
-                if (nt == 1) healthy = unit_rows<1, kStore, FUSED, kScl>(b, a, b, g, id, lane, r, pr, sc, ready, nullptr, ctr, nsb2);
-                else if (nt == 2) healthy = unit_rows<2, kStore, FUSED, kScl>(b, a, b, g, id, lane, r, pr, sc, ready, nullptr, ctr, nsb2);
-                else healthy = unit_rows<3, kStore, FUSED, kScl>(b, a, b, g, id, lane, r, pr, sc, ready, nullptr, ctr, nsb2);
+                if (nt == 1) healthy = unit_rows<1, kStore, FUSED, kScl, PTRS>(b, a, b, g, id, lane, r, pr, sc, ready, nullptr, ctr, nsb2);
+                else if (nt == 2) healthy = unit_rows<2, kStore, FUSED, kScl, PTRS>(b, a, b, g, id, lane, r, pr, sc, ready, nullptr, ctr, nsb2);
+                else healthy = unit_rows<3, kStore, FUSED, kScl, PTRS>(b, a, b, g, id, lane, r, pr, sc, ready, nullptr, ctr, nsb2);
                 continue;
             }
         }
@@ -999,10 +1003,10 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, const GemvArgs& b, 
     pdl_trigger();
 }
 
-template <int EPI, bool FUSED>
+template <int EPI, bool FUSED, bool PTRS = false>
 __global__ void __launch_bounds__(kGemvWarps * 32, 1) iq2_gemv_k(GemvArgs a, GemvArgs b, int* ready, int nslots) {
     const LayerArgs none = {};
-    gemv_body<EPI, FUSED, false>(a, b, ready, nslots, none);
+    gemv_body<EPI, FUSED, false, PTRS>(a, b, ready, nslots, none);
 }
 
 __global__ void __launch_bounds__(kGemvWarps * 32, 1) decode_layer_k(GemvArgs a, GemvArgs b, int* ready, int nslots,
@@ -1023,16 +1027,17 @@ static int num_sms() {
     return sms[dev];
 }
 
-template <int EPI, bool FUSED>
+template <int EPI, bool FUSED, bool PTRS = false>
 static cudaError_t launch_gemv_e(const GemvArgs& a, const GemvArgs& b, int* ready, int nslots, cudaStream_t s) {
     static bool opted = false;
     if (!opted) {
-        cudaError_t e = cudaFuncSetAttribute(iq2_gemv_k<EPI, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(iq2_gemv_k<EPI, FUSED, PTRS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)kGemvSmem);
         if (e != cudaSuccess) return e;
         opted = true;
     }
-    return launch(iq2_gemv_k<EPI, FUSED>, dim3(num_sms()), dim3(kGemvWarps * 32), kGemvSmem, s, a, b, ready, nslots);
+    return launch(iq2_gemv_k<EPI, FUSED, PTRS>, dim3(num_sms()), dim3(kGemvWarps * 32), kGemvSmem, s, a, b, ready,
+                  nslots);
 }
 
 // launches take the counter slots in turn: kUnitCtrs launches can be in flight (on any streams) before a slot is
@@ -1079,6 +1084,7 @@ cudaError_t launch_iq2_updown(const GemvArgs& up, const GemvArgs& down, int* rea
     if (nslots <= 0 || nslots > kMaxSlots || up.sched == nullptr || ready == nullptr) return cudaErrorInvalidValue;
     GemvArgs a = up;
     a.ctr = next_ctr();
+    if (down.y_rows) return launch_gemv_e<kRelu2Q8, true, true>(a, down, ready, nslots, s);
     return launch_gemv_e<kRelu2Q8, true>(a, down, ready, nslots, s);
 }
 

@@ -47,6 +47,9 @@ struct GemvArgs {
     size_t done_off;
     int done_n;
     const int* done_epoch;
+    // Optional (the fused launch's down args): output row id at address y_rows[id] (bf16 or fp32 as y_bf16; another
+    // GPU's memory allowed) instead of y + id * ldy
+    const unsigned long long* y_rows;
 };
 
 constexpr int kIq2UnitTok = 3;   // tokens a GEMV work unit dots at most (a slot's tokens come in batches of this many)

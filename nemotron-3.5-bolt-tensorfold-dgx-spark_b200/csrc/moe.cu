@@ -153,7 +153,8 @@ __global__ void __launch_bounds__(512) moe_local_prep_k(const void* __restrict__
                                                         int* __restrict__ order, int8_t* __restrict__ xq,
                                                         float* __restrict__ xs, int* __restrict__ sched,
                                                         int* __restrict__ ready, int F, int wave, const int* wait_flags,
-                                                        int wait_n, const int* wait_epoch, int* wait_err) {
+                                                        int wait_n, const int* wait_epoch, int* wait_err,
+                                                        ExpertsPeer rt) {
     pdl_wait();
     if (wait_flags) {
         if (threadIdx.x == 0) {
@@ -170,6 +171,16 @@ __global__ void __launch_bounds__(512) moe_local_prep_k(const void* __restrict__
         for (int i = threadIdx.x; i < R; i += blockDim.x) {
             const int l = lidx[(size_t)i * lidx_stride];
             ridx_s[i] = (l < 0 || l >= n_local) ? n_local : l;   // padding: left out of the schedule
+            if (rt.yptr) {   // the row's output address (a padding row's is never used)
+                unsigned char* dst;
+                if (i < rt.world * rt.cap) {
+                    const int pp = rt.srcp[i];
+                    dst = rt.peers[i / rt.cap] + rt.ret_off + (size_t)(pp < 0 ? 0 : pp) * rt.row_bytes;
+                } else {
+                    dst = rt.yloc + (size_t)i * rt.row_bytes;
+                }
+                rt.yptr[i] = reinterpret_cast<unsigned long long>(dst);
+            }
         }
         __syncthreads();
         // counts by local expert, offsets, the ids of each expert in increasing row order (straight to `order`), the
@@ -396,7 +407,7 @@ int b200q::experts_decode(const void* rows, int rows_dtype, int ldr, int R, int 
     launch(moe_local_prep_k, dim3(given ? 1 : 1 + qblocks), dim3(512), 0, s, given ? nullptr : rows, rows_dtype, ldr,
            R, H, lidx, lidx_stride, n_local, w.counts, w.offsets, w.order, w.xq, w.xs, w.sched, w.ready, F,
            iq2_first_wave(), peer ? peer->wait_flags : nullptr, peer ? peer->wait_n : 0,
-           peer ? peer->epoch : nullptr, peer ? peer->err : nullptr);
+           peer ? peer->epoch : nullptr, peer ? peer->err : nullptr, peer ? *peer : ExpertsPeer{});
     if ((st = launched()) != B200Q_OK) return st;
     // 2. up with relu^2 and the int8 rows of the result (row id = received row), then down, in one launch
     GemvArgs a = {};
@@ -408,6 +419,7 @@ int b200q::experts_decode(const void* rows, int rows_dtype, int ldr, int R, int 
     b.counts = w.counts; b.offsets = w.offsets; b.order = w.order; b.act_div = 1; b.act_split = 1 << 30;
     b.xq = w.aq; b.xs = w.as; b.y = (float*)y; b.ldy = ldy; b.y_bf16 = y_dtype == B200Q_BF16;
     b.sched = w.sched;
+    if (peer && peer->yptr) b.y_rows = peer->yptr;   // the outputs go straight to their rows' owners
     // the launch whose end publishes the outputs: the down launch, or the fused launch (whose args are up's)
 #ifdef B200Q_X_NOFUSE
     if (peer) { b.done_base = peer->done_base; b.done_off = peer->done_off; b.done_n = peer->done_n; b.done_epoch = peer->epoch; }

@@ -65,6 +65,16 @@ struct ExpertsPeer {
     unsigned char* const* done_base;  // GemvArgs::done_* (the value published is *epoch)
     size_t done_off;
     int done_n;
+    // optional: the down outputs written straight to their senders (GemvArgs::y_rows): row r < world * cap came from
+    // sender r / cap as its pair srcp[r], whose output row is at peers[r / cap] + ret_off + srcp[r] * row_bytes; a
+    // later row (this rank's own, the shared expert's) goes to yloc + r * row_bytes.  yptr: R entries, filled by the
+    // prologue.
+    const int* srcp;
+    unsigned char* const* peers;
+    size_t ret_off;
+    int cap, world, row_bytes;
+    unsigned char* yloc;
+    unsigned long long* yptr;
 };
 // b200q_moe_experts_decode; with peer, rows may be NULL (the int8 rows are peer->xq / xs).  Defined in moe.cu.
 int experts_decode(const void* rows, int rows_dtype, int ldr, int R, int H, int F, const int* lidx, int lidx_stride,
