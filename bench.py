@@ -178,6 +178,60 @@ def graph_ms(call, n, reps=5):
     return ms
 
 
+def pipelined_e2e(run, xh, lh, steps, first, device, out_shape, bufs=None):
+    """`steps` calls run(i, x, logits, out) of the public layer over pinned host buffers, each step's inputs copied
+    host -> device and its output device -> host inside the timed region, as a serving loop does it: the copies on a
+    stream of their own, overlapped with the neighbouring steps' kernels (step i + 1's inputs go up while step i
+    runs, step i's output comes back while step i + 1 runs), device buffers doubled: step i reads bufs[i & 1] (two
+    (x, logits) pairs; fresh ones by default) and writes out[i & 1], or returns the tensor it wrote (a graph's output).
+    -> ms from before the first copy to after the last one (CUDA events on the compute stream)."""
+    comp = torch.cuda.current_stream()
+    copy = torch.cuda.Stream(device=device)
+    if bufs is None:
+        bufs = [(torch.empty(xh[0].shape, dtype=xh[0].dtype, device=device),
+                 torch.empty(lh[0].shape, dtype=lh[0].dtype, device=device)) for _ in range(2)]
+    xd, ld = [b[0] for b in bufs], [b[1] for b in bufs]
+    od = [torch.empty(out_shape, dtype=torch.float32, device=device) for _ in range(2)]
+    oh = [torch.empty(out_shape, dtype=torch.float32).pin_memory() for _ in range(2)]
+    ev = {k: [torch.cuda.Event() for _ in range(2)] for k in ("inp", "done", "outp")}
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    nb = len(xh)
+    torch.cuda.synchronize()
+    e0.record(comp)
+    copy.wait_stream(comp)
+
+    def upload(i, b):
+        with torch.cuda.stream(copy):
+            xd[b].copy_(xh[(first + i) % nb], non_blocking=True)
+            ld[b].copy_(lh[(first + i) % nb], non_blocking=True)
+            ev["inp"][b].record(copy)
+
+    upload(0, 0)
+    for i in range(steps):
+        b = i & 1
+        if i + 1 < steps:
+            if i >= 1:
+                copy.wait_event(ev["done"][1 - b])   # step i - 1 is done with the other buffers
+            upload(i + 1, 1 - b)
+        comp.wait_event(ev["inp"][b])
+        if i >= 2:
+            comp.wait_event(ev["outp"][b])           # step i - 2's output has left od[b]
+        y = run(i, xd[b], ld[b], od[b])
+        if y is None:
+            y = od[b]
+        elif y is not od[b]:
+            y.record_stream(copy)   # a tensor the layer allocated: not reused before its copy ends
+        ev["done"][b].record(comp)
+        copy.wait_event(ev["done"][b])
+        with torch.cuda.stream(copy):
+            oh[b].copy_(y, non_blocking=True)
+            ev["outp"][b].record(copy)
+    comp.wait_stream(copy)
+    e1.record(comp)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
+
+
 def _event_ms(fn, n):
     """mean ms of n calls fn(i) on the current stream, CUDA events around them"""
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -342,8 +396,10 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
     xs = [x.to(device) for x in xs_h]
     ls = [l.to(device) for l in ls_h]
 
-    xin = torch.empty(T, H, dtype=torch.bfloat16, device=device)   # the step's tokens and logits (graph inputs)
-    lin = torch.empty(T, E, dtype=torch.bfloat16, device=device)
+    # the step's tokens and logits (graph inputs), two pairs so that the end-to-end loop uploads the next step's
+    # while the current one runs
+    xin = [torch.empty(T, H, dtype=torch.bfloat16, device=device) for _ in range(2)]
+    lin = [torch.empty(T, E, dtype=torch.bfloat16, device=device) for _ in range(2)]
 
     def eager_on(L, x, lg):
         if exchange == "peer":
@@ -354,21 +410,23 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
     def eager_step(L, b):
         return eager_on(L, xs[b], ls[b])
 
-    # the step as a CUDA graph per layer copy over fixed input buffers: no host read in the capacity exchange, so the
-    # whole step (router, packing, NCCL all-to-alls, expert kernels, combine) replays as one launch
+    # the step as a CUDA graph per layer copy and input pair over fixed input buffers: no host read in the exchange,
+    # so the whole step (router, packing, the exchange, expert kernels, combine) replays as one launch
     graphs = []
     if os.environ.get("B200Q_EP_GRAPH", "1") != "0":
-        xin.copy_(xs[0])
-        lin.copy_(ls[0])
-        graphs = [GraphedStep(lambda L=L: eager_on(L, xin, lin), world) for L in range(LAYERS)]
-    graphed = bool(graphs) and all(g.ok for g in graphs)
+        for p in range(2):
+            xin[p].copy_(xs[0])
+            lin[p].copy_(ls[0])
+        graphs = [[GraphedStep(lambda L=L, p=p: eager_on(L, xin[p], lin[p]), world) for p in range(2)]
+                  for L in range(LAYERS)]
+    graphed = bool(graphs) and all(g.ok for gl in graphs for g in gl)
 
     def step(i):
         L, b = i % LAYERS, i % BATCHES
         if graphed:
-            xin.copy_(xs[b])
-            lin.copy_(ls[b])
-            return graphs[L]()
+            xin[0].copy_(xs[b])
+            lin[0].copy_(ls[b])
+            return graphs[L][0]()
         return eager_step(L, b)
 
     # bytes of a step of batch b over all ranks: every rank's touched local experts + its shared expert + activations
@@ -447,23 +505,19 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
         torch.cuda.synchronize()
         acc += [evs[0].elapsed_time(evs[1]), evs[2].elapsed_time(evs[3]), evs[4].elapsed_time(evs[5])]
     acc /= nprof
-    # end to end: every step copies its tokens and logits from pinned host memory and reads the output back
+    # end to end: every step copies its tokens and logits from pinned host memory and reads the output back, the
+    # copies overlapped with the neighbouring steps (pipelined_e2e); step i replays the graph over input pair i & 1
     xh = [x.pin_memory() for x in xs_h]
     lh = [l.pin_memory() for l in ls_h]
-    oh = torch.empty(T, H, dtype=torch.float32).pin_memory()
-    barrier()
-    torch.cuda.synchronize()
-    ev0.record()
-    for i in range(steps):
-        b = (warmup + i) % BATCHES
-        xin.copy_(xh[b], non_blocking=True)
-        lin.copy_(lh[b], non_blocking=True)
+
+    def e2e_run(i, x, lg, o):
         L = (warmup + i) % LAYERS
-        oh.copy_(graphs[L]() if graphed else eager_on(L, xin, lin), non_blocking=True)
-    ev1.record()
-    torch.cuda.synchronize()
+        return graphs[L][i & 1]() if graphed else eager_on(L, x, lg)
+
     barrier()
-    e2e_ms = max_ms(ev0.elapsed_time(ev1))
+    e2e_ms = pipelined_e2e(e2e_run, xh, lh, steps, warmup, device, (T, H), bufs=list(zip(xin, lin)))
+    barrier()
+    e2e_ms = max_ms(e2e_ms)
     if exchange == "peer" and dist:   # each piece's slowest rank
         t = torch.tensor(acc, device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -773,26 +827,14 @@ def run_ours(args, rank, world, local_rank):
     peak, peak_kind = peaks()
     achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
 
-    # ---- e2e: the public API with host buffers (pinned), H2D of x and logits, D2H of the output, every step
+    # ---- e2e: the public API with host buffers (pinned), H2D of x and logits, D2H of the output, every step; the
+    # copies overlapped with the neighbouring steps' kernels (pipelined_e2e), as a serving loop runs them
     xh = [x.pin_memory() for x in xs_h]
     lh = [l.pin_memory() for l in ls_h]
-    oh = torch.empty(T, H, dtype=torch.float32).pin_memory()
-    xd = torch.empty(T, H, dtype=torch.bfloat16, device=device)
-    ld = torch.empty(T, E, dtype=torch.bfloat16, device=device)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
-    torch.cuda.synchronize()
-    e0.record(stream)
-    for i in range(args.steps):
-        j = args.warmup + i
-        xd.copy_(xh[j % BATCHES], non_blocking=True)
-        ld.copy_(lh[j % BATCHES], non_blocking=True)
-        layers[j % LAYERS](xd, ld, out=out)
-        oh.copy_(out, non_blocking=True)
-    e1.record(stream)
-    torch.cuda.synchronize()
+    e2e_ms = pipelined_e2e(lambda i, xd, ld, od: layers[(args.warmup + i) % LAYERS](xd, ld, out=od), xh, lh,
+                           args.steps, args.warmup, device, (T, H))
     barrier()
-    e2e_ms = e0.elapsed_time(e1)
     if dist:
         t = torch.tensor([e2e_ms], device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -831,7 +873,9 @@ def run_ours(args, rank, world, local_rank):
                          "kernel_ms": round(dom_ms, 5)},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": T * H * 2 + T * E * 2,
-                    "d2h_bytes_per_step": T * H * 4},
+                    "d2h_bytes_per_step": T * H * 4,
+                    "copies": "every step's inputs host -> device and output device -> host inside the timed region, "
+                              "on a copy stream overlapped with the neighbouring steps' kernels (double-buffered)"},
             "gpu_launches": args.steps,   # one decode_layer_k launch a step
             "clocks": clk.summary(),
         }
