@@ -18,6 +18,7 @@ one rank, the basis of the scaling.
 import argparse
 import ctypes
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -410,23 +411,26 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
     def eager_step(L, b):
         return eager_on(L, xs[b], ls[b])
 
-    # the step as a CUDA graph per layer copy and input pair over fixed input buffers: no host read in the exchange,
-    # so the whole step (router, packing, the exchange, expert kernels, combine) replays as one launch
-    graphs = []
+    # the step as a CUDA graph: no host read in the exchange, so the whole step (router, packing, the exchange, expert
+    # kernels, combine) replays as one launch.  The device-resident loop replays a graph per (layer copy, batch) pair
+    # it visits, over the batch's own buffers (no input copy in the timed region); the end-to-end loop a graph per
+    # layer copy and input pair, over the buffers its host copies fill.  Every rank captures them in the same order.
+    graphs, graphs_res = [], {}
     if os.environ.get("B200Q_EP_GRAPH", "1") != "0":
+        span = LAYERS * BATCHES // math.gcd(LAYERS, BATCHES)
+        for key in sorted({(i % LAYERS, i % BATCHES) for i in range(span)}):
+            graphs_res[key] = GraphedStep(lambda L=key[0], b=key[1]: eager_on(L, xs[b], ls[b]), world)
         for p in range(2):
             xin[p].copy_(xs[0])
             lin[p].copy_(ls[0])
         graphs = [[GraphedStep(lambda L=L, p=p: eager_on(L, xin[p], lin[p]), world) for p in range(2)]
                   for L in range(LAYERS)]
-    graphed = bool(graphs) and all(g.ok for gl in graphs for g in gl)
+    graphed = bool(graphs) and all(g.ok for gl in graphs for g in gl) and all(g.ok for g in graphs_res.values())
 
     def step(i):
         L, b = i % LAYERS, i % BATCHES
         if graphed:
-            xin[0].copy_(xs[b])
-            lin[0].copy_(ls[b])
-            return graphs[L][0]()
+            return graphs_res[(L, b)]()
         return eager_step(L, b)
 
     # bytes of a step of batch b over all ranks: every rank's touched local experts + its shared expert + activations
@@ -545,7 +549,7 @@ def ep_bench(b200q, rank, world, device, steps, warmup, prefill=True, clk=None):
                      "e2e_gbs": round(nbytes / (e2e_ms * 1e-3) / 1e9, 2),
                      "h2d_bytes_per_step": T * H * 2 + T * E * 2, "d2h_bytes_per_step": T * H * 4,
                      "cuda_graph": graphed}
-    del graphs
+    del graphs, graphs_res
     if exchange == "peer":   # collective: every rank unmaps, then frees
         for m in layers:
             m.close()
