@@ -198,6 +198,9 @@ __device__ __forceinline__ int smem_rank(const int* a, int n, int c, int self) {
 // index (iq2_schedule_slots' order) with the exclusive prefix of their batches; and the down phase's batch order of
 // iq2_schedule_batches.  An id whose expert is outside 0 .. E - 1 is left out.  tmp: an int a batch (kLayerIds in
 // the one-launch layer).  s_cnt, s_bpre and tmp 16-byte aligned shared memory; s_ord and s_dord may be global.
+// The ids in slot order come from one warp's walk over the ids, 32 at a time (linear in the ids: the expert-parallel
+// prologue sees world x T x topk of them, most of them padding): match_any groups the lanes of one expert, a lane's
+// place is the expert's running count plus its rank among them, and the group's lowest lane adds the group's size.
 __device__ inline void layer_schedule(const int* ridx_s, int pairs, int E, int extra, int G, int W, int* s_cnt, int* s_offs,
                                int* s_ord, int* s_order, int* s_bpre, int* s_dord, int* tmp) {
     const int tid = threadIdx.x, nth = blockDim.x;
@@ -213,13 +216,23 @@ __device__ inline void layer_schedule(const int* ridx_s, int pairs, int E, int e
     for (int e = tid; e <= nslots; e += nth) s_offs[e] = smem_sum(s_cnt, e);
     for (int s = tid; s < nslots; s += nth) s_order[smem_rank<true>(s_cnt, nslots, s_cnt[s], s)] = s;
     __syncthreads();
-    for (int p = tid; p < pairs; p += nth) {
-        const int e = ridx_s[p];
-        if ((unsigned)e >= (unsigned)E) continue;
-        int r = 0;
-#pragma unroll 8
-        for (int q = 0; q < p; q++) r += ridx_s[q] == e;
-        s_ord[s_offs[e] + r] = p;
+    if (tid < 32) {   // s_bpre is free until its prefix below: the running counts
+        for (int e = tid; e < E; e += 32) s_bpre[e] = s_offs[e];
+        __syncwarp();
+        for (int p0 = 0; p0 < pairs; p0 += 32) {
+            const int p = p0 + tid;
+            const int e = p < pairs ? ridx_s[p] : -1;
+            const bool in = (unsigned)e < (unsigned)E;
+            const unsigned m = __match_any_sync(0xffffffffu, in ? e : -1);
+            const int before = __popc(m & ((1u << tid) - 1u));
+            const int at = in ? s_bpre[e] : 0;
+            __syncwarp();
+            if (in) {
+                s_ord[at + before] = p;
+                if (before == 0) s_bpre[e] = at + __popc(m);
+            }
+            __syncwarp();
+        }
     }
     for (int i = tid; i < extra; i += nth) s_ord[pairs + i] = pairs + i;
     for (int i = tid; i < nslots; i += nth) tmp[i] = (s_cnt[s_order[i]] + kIq2UnitTok - 1) / kIq2UnitTok;
