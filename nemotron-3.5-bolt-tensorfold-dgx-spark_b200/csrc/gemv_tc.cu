@@ -222,7 +222,10 @@ __global__ void __launch_bounds__(kTcWarps * 32) tc_gemv_k(TcArgs a) {
     const int L = a.L, stride = L + 8;   // halves a staged row (the padding spreads the B loads over the banks)
     __half* xs = reinterpret_cast<__half*>(dyn);
     const int ks = blockIdx.y, k0 = ks * L, len = min(L, a.k - k0);
-    for (int i = threadIdx.x; i < NT * 8 * (len / 2); i += blockDim.x) {
+    // only the T rows that exist are staged: the MMA's output column n reads only B column n, and the columns of
+    // the absent rows (>= T) are never stored, so those rows of B need no zeros
+    const int srows = min(a.T, NT * 8);
+    for (int i = threadIdx.x; i < srows * (len / 2); i += blockDim.x) {
         const int r = i / (len / 2), c = 2 * (i - r * (len / 2));
         float v0 = 0.f, v1 = 0.f;
         if (r < a.T) {
@@ -485,7 +488,10 @@ __global__ void __launch_bounds__(kTcWarps * 32) tc_ring_k(TcArgs a) {
     pdl_wait();
     if (lane == 0)
         for (int q = 0; q < kRingStages && q < nst; q++) issue(q);
-    for (int i = threadIdx.x; i < NT * 8 * (len / 2); i += blockDim.x) {
+    // only the T rows that exist are staged: the MMA's output column n reads only B column n, and the columns of
+    // the absent rows (>= T) are never stored, so those rows of B need no zeros
+    const int srows = min(a.T, NT * 8);
+    for (int i = threadIdx.x; i < srows * (len / 2); i += blockDim.x) {
         const int r = i / (len / 2), c = 2 * (i - r * (len / 2));
         float v0 = 0.f, v1 = 0.f;
         if (r < a.T) {
