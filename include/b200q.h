@@ -85,7 +85,8 @@ int b200q_nv4_pack(const void* q, const void* sc, void* packed, int64_t n, int k
  * (bolt_kernels.cu:228-231).  K is split across CTAs; the fp32 partials go to `workspace`
  * (>= b200q_*_gemv_workspace_bytes, 0 when no split is needed) and are summed in a fixed order.  A NULL or small
  * workspace runs without the split (slower, same result order).  w must be 16-byte aligned (the packers' output in
- * any device allocation is).
+ * any device allocation is); x on its element size (B200Q_EINVAL otherwise), any row pitch: rows on 4 elements are
+ * read four values a load, rows on 2 elements by pairs, others one value at a time.
  * --------------------------------------------------------------------------------------------------------- */
 size_t b200q_nv4_gemv_workspace_bytes(int n, int k, int T);
 int b200q_nv4_gemv(const void* w, float s2, int n, int k, const void* x, int x_dtype, int ldx, int T, float* y, int ldy,

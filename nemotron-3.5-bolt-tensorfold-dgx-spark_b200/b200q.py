@@ -142,6 +142,15 @@ def _dev(t, name, rows=False):
     return t
 
 
+def _rows_any(t, name):
+    """a CUDA tensor of rows, each row's elements contiguous, the rows at any pitch (x of the decode GEMVs)"""
+    if not (isinstance(t, torch.Tensor) and t.is_cuda):
+        raise B200QError(EINVAL, f"{name} must be a CUDA tensor")
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise B200QError(EINVAL, f"{name} must be rows with contiguous elements")
+    return t
+
+
 def _dtype_code(t):
     if t.dtype == torch.float32:
         return F32
@@ -439,8 +448,8 @@ _WS = _Workspace()
 
 
 def mma_nv4(w, s2, n, k, x, y=None):
-    """y [T][n] fp32 = s2 * W . x for T <= 16 rows of x (fp32 or bf16)."""
-    _dev(x, "x")
+    """y [T][n] fp32 = s2 * W . x for T <= 16 rows of x (fp32 or bf16; rows at any pitch)."""
+    _rows_any(x, "x")
     T = x.shape[0]
     y = torch.empty(T, n, dtype=torch.float32, device=x.device) if y is None else y
     ws, wb = _WS.get(lib().b200q_nv4_gemv_workspace_bytes(n, k, T), x.device)
@@ -450,8 +459,8 @@ def mma_nv4(w, s2, n, k, x, y=None):
 
 
 def mma_q8(w, n, k, x, y=None):
-    """y [T][n] fp32 = W . x for T <= 16 rows of x (fp32 or bf16)."""
-    _dev(x, "x")
+    """y [T][n] fp32 = W . x for T <= 16 rows of x (fp32 or bf16; rows at any pitch)."""
+    _rows_any(x, "x")
     T = x.shape[0]
     y = torch.empty(T, n, dtype=torch.float32, device=x.device) if y is None else y
     ws, wb = _WS.get(lib().b200q_q8_gemv_workspace_bytes(n, k, T), x.device)

@@ -157,7 +157,8 @@ struct TcArgs {
     const uint8_t* wsc;   // the split layout (libbolt's tile buffers): w holds the units' 512 code bytes, wsc their scales
     float* y;             // KS > 1: the result y [T][ldo], summed from the partials in the launch
     int* cols;            // KS > 1: an arrival count a column of CTAs (blockIdx.x), zero at entry, reset at exit
-    int xvec;             // x's rows start on 16 bytes (fp32) / 8 bytes (bf16): staged four values a thread
+    int xvec;             // the staging loads x's alignment allows: 2 four values (rows on 4 elements), 1 pairs (rows on
+                          // 2 elements), 0 single values
 };
 
 // The token rows of the CTA's K slice [k0, k0 + len) as fp16 into shared memory (row stride `stride` halves).  Only
@@ -170,7 +171,7 @@ __device__ __forceinline__ void stage_rows(const TcArgs& a, __half* xs, int stri
     for (int r = 0; r < rows; r++) {
         const size_t row = (size_t)r * a.ldx + k0;
         __half* dst = xs + (size_t)r * stride;
-        if (a.xvec) {
+        if (a.xvec == 2) {
             for (int q = threadIdx.x; q < len / 4; q += blockDim.x) {
                 float v[4];
                 if (bf) {
@@ -186,7 +187,7 @@ __device__ __forceinline__ void stage_rows(const TcArgs& a, __half* xs, int stri
                 *reinterpret_cast<uint2*>(dst + 4 * q) =
                     make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
             }
-        } else {
+        } else if (a.xvec == 1) {
             for (int c2 = threadIdx.x; c2 < len / 2; c2 += blockDim.x) {
                 float v0, v1;
                 if (bf) {
@@ -198,6 +199,9 @@ __device__ __forceinline__ void stage_rows(const TcArgs& a, __half* xs, int stri
                 }
                 *reinterpret_cast<__half2*>(dst + 2 * c2) = __floats2half2_rn(v0, v1);
             }
+        } else {
+            for (int c = threadIdx.x; c < len; c += blockDim.x)
+                dst[c] = __float2half_rn(bf ? __bfloat162float(xb[row + c]) : xf[row + c]);
         }
     }
 }
@@ -265,9 +269,9 @@ __global__ void __launch_bounds__(kTcWarps * 32) tc_gemv_k(TcArgs a) {
     const int L = a.L, stride = L + 8;   // halves a staged row (the padding spreads the B loads over the banks)
     __half* xs = reinterpret_cast<__half*>(dyn);
     const int ks = blockIdx.y, k0 = ks * L, len = min(L, a.k - k0);
-    if constexpr (NT == 1) {
-        // up to 8 rows: the single loop over (row, pair) measured faster here than the row-at-a-time form (NVFP4,
-        // M = 1: in_proj 2468 against 2336 GB/s, out_proj 1763 against 1527)
+    if (NT == 1 && a.xvec > 0) {
+        // up to 8 rows on pair boundaries: the single loop over (row, pair) measured faster here than the
+        // row-at-a-time form (NVFP4, M = 1: in_proj 2468 against 2336 GB/s, out_proj 1763 against 1527)
         const int srows = min(a.T, 8);
         for (int i = threadIdx.x; i < srows * (len / 2); i += blockDim.x) {
             const int r = i / (len / 2), c = 2 * (i - r * (len / 2));
@@ -711,9 +715,10 @@ static int run_tc(const uint8_t* w, float s2, int n, int k, const void* x, int x
     int KS = (k + L - 1) / L;
     if (KS > 1 && (!ws || ws_bytes < (size_t)KS * T * n * sizeof(float))) { L = k; KS = 1; }   // no workspace: one slice
     if (((uintptr_t)w | (uintptr_t)wsc) & 15) return B200Q_EINVAL;   // the ring's bulk copies start on 16-byte boundaries
+    const size_t xe = x_dtype == B200Q_BF16 ? 2 : 4;
+    if ((uintptr_t)x % xe) return B200Q_EINVAL;   // x not on its element size
     if (T > 8 && tc_smem<FMT>(16, L) > kMaxSmem) {
         // one slice's 16 staged rows do not fit (a long K without a workspace): two passes of at most 8 rows
-        const size_t xe = x_dtype == B200Q_BF16 ? 2 : 4;
         const int st = run_tc<FMT>(w, s2, n, k, x, x_dtype, ldx, 8, y, ldy, ws, ws_bytes, s, wsc);
         if (st != B200Q_OK) return st;
         return run_tc<FMT>(w, s2, n, k, (const char*)x + 8 * (size_t)ldx * xe, x_dtype, ldx, T - 8, y + 8 * (size_t)ldy, ldy,
@@ -724,8 +729,9 @@ static int run_tc(const uint8_t* w, float s2, int n, int k, const void* x, int x
     // 1618 against 1511; at M = 16, and for Q8_0 at M = 1 and 16, the second kernel was faster)
     const bool fold = FMT == kFmtNv4 && T <= 8 && KS > 1 && grid.x <= (unsigned)kTcMaxCols;
     int* cols = fold ? tc_cols_slot() : nullptr;
-    const size_t xe = x_dtype == B200Q_BF16 ? 2 : 4;   // four values: 8 bytes of bf16, 16 of fp32
-    const int xvec = ((uintptr_t)x % (4 * xe) == 0 && ((size_t)ldx * xe) % (4 * xe) == 0) ? 1 : 0;
+    // the widest staging load x's base and row pitch allow
+    const uintptr_t xa = (uintptr_t)x;
+    const int xvec = (xa % (4 * xe) == 0 && ldx % 4 == 0) ? 2 : (xa % (2 * xe) == 0 && ldx % 2 == 0) ? 1 : 0;
     TcArgs a{w, n, k, x, x_dtype, ldx, T, L, s2, KS > 1 ? (float*)ws : y, ldy, wsc, y, cols, xvec};
     const dim3 grid2((n / 16 + kTcWarps - 1) / kTcWarps, KS);
     cudaError_t e;

@@ -110,3 +110,45 @@ def test_gemv_without_workspace_matches_split():
                           ctypes.c_void_p(y2.data_ptr()), n, None, 0, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert st == 0
     assert rel_l2(y2.cpu().numpy(), y1.cpu().numpy()) < 1e-5   # the same products, summed in another order
+
+
+@pytest.mark.parametrize("fmt", ["nv4", "q8"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("T", [1, 3, 16])
+@pytest.mark.parametrize("shift", [1, 2])
+def test_gemv_unaligned_rows_match_aligned(fmt, dtype, T, shift):
+    """x's rows staged four values a load (rows on 4 elements), by pairs (a view 2 elements in, even row pitch) and one
+    value at a time (1 element in, odd pitch): the same fp16 operands, so the same outputs bit for bit; the columns
+    split over several K slices."""
+    n, k = 256, 4096
+    if fmt == "nv4":
+        q, sc = nv4_weights(91, n, k)
+        w = b200q.tile_nv4(dev(q), dev(sc), n, k)
+        run = lambda x: b200q.mma_nv4(w, 0.5, n, k, x)
+    else:
+        w = b200q.tile_q8(dev(q8_blocks(92, n, k)), n, k)
+        run = lambda x: b200q.mma_q8(w, n, k, x)
+    g = torch.Generator().manual_seed(93 + T)
+    x = torch.randn(T, k, generator=g).to(dtype).to(DEV)
+    pitch = k + (3 if shift == 1 else 2)
+    wide = torch.zeros(T, pitch, dtype=dtype, device=DEV)
+    wide[:, shift:k + shift] = x
+    xv = wide[:, shift:k + shift]
+    assert xv.stride(0) == pitch and xv.data_ptr() % (4 * x.element_size()) != 0
+    y0 = run(x).cpu()
+    y1 = run(xv).cpu()
+    assert b200q.device_error() == 0
+    assert torch.equal(y0, y1)
+    assert torch.isfinite(y0).all()
+
+
+def test_gemv_refuses_x_off_its_element_size():
+    """an x pointer that is not on its element size is refused on the host, before any launch"""
+    import ctypes
+    n, k, T = 64, 512, 1
+    w = b200q.tile_q8(dev(q8_blocks(94, n, k)), n, k)
+    x = torch.zeros(T, k + 8, dtype=torch.bfloat16, device=DEV)
+    y = torch.zeros(T, n, dtype=torch.float32, device=DEV)
+    st = b200q.lib().b200q_q8_gemv(ctypes.c_void_p(w.data_ptr()), n, k, ctypes.c_void_p(x.data_ptr() + 1),
+                                   b200q.BF16, k + 8, T, ctypes.c_void_p(y.data_ptr()), n, None, 0, None)
+    assert st == b200q.EINVAL
