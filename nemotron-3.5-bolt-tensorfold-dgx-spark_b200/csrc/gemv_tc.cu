@@ -168,26 +168,55 @@ __device__ __forceinline__ void stage_rows(const TcArgs& a, __half* xs, int stri
     const bool bf = a.x_dtype == B200Q_BF16;
     const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(a.x);
     const float* xf = reinterpret_cast<const float*>(a.x);
+    if (a.xvec == 2) {
+        // (row, four-value unit) positions in row-major order, thread p taking p, p + blockDim, ...: advanced without
+        // a division (a row holds len / 4 >= 64 units, so one step crosses at most blockDim / 64 rows), and four loads
+        // issued before their stores, so that they are in flight together
+        const int nq = len >> 2;
+        int r = 0, q = threadIdx.x;
+        while (q >= nq) { q -= nq; r++; }
+        while (r < rows) {
+            int rr[4], qq[4];
+            uint4 u[4];
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                rr[b] = r;
+                qq[b] = q;
+                if (r < rows) {
+                    const size_t off = (size_t)r * a.ldx + k0 + 4 * q;
+                    if (bf) {
+                        const uint2 t = *reinterpret_cast<const uint2*>(xb + off);
+                        u[b] = make_uint4(t.x, t.y, 0u, 0u);
+                    } else {
+                        u[b] = *reinterpret_cast<const uint4*>(xf + off);
+                    }
+                }
+                q += blockDim.x;
+                while (q >= nq) { q -= nq; r++; }
+            }
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                if (rr[b] >= rows) break;
+                float v[4];
+                if (bf) {
+                    const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[b].x));
+                    const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[b].y));
+                    v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+                } else {
+                    v[0] = __uint_as_float(u[b].x); v[1] = __uint_as_float(u[b].y);
+                    v[2] = __uint_as_float(u[b].z); v[3] = __uint_as_float(u[b].w);
+                }
+                const __half2 h0 = __floats2half2_rn(v[0], v[1]), h1 = __floats2half2_rn(v[2], v[3]);
+                *reinterpret_cast<uint2*>(xs + (size_t)rr[b] * stride + 4 * qq[b]) =
+                    make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+            }
+        }
+        return;
+    }
     for (int r = 0; r < rows; r++) {
         const size_t row = (size_t)r * a.ldx + k0;
         __half* dst = xs + (size_t)r * stride;
-        if (a.xvec == 2) {
-            for (int q = threadIdx.x; q < len / 4; q += blockDim.x) {
-                float v[4];
-                if (bf) {
-                    const uint2 u = *reinterpret_cast<const uint2*>(xb + row + 4 * q);
-                    const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-                    const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-                    v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
-                } else {
-                    const float4 f = *reinterpret_cast<const float4*>(xf + row + 4 * q);
-                    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
-                }
-                const __half2 h0 = __floats2half2_rn(v[0], v[1]), h1 = __floats2half2_rn(v[2], v[3]);
-                *reinterpret_cast<uint2*>(dst + 4 * q) =
-                    make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
-            }
-        } else if (a.xvec == 1) {
+        if (a.xvec == 1) {
             for (int c2 = threadIdx.x; c2 < len / 2; c2 += blockDim.x) {
                 float v0, v1;
                 if (bf) {
