@@ -648,6 +648,140 @@ __global__ void __launch_bounds__(kTcWarps * 32) tc_ring_k(TcArgs a) {
     pdl_trigger();
 }
 
+// The ring form over several column tiles a CTA, for 16 token rows: staging 16 rows of a long K slice is a large
+// share of a call, and a launch of one CTA a column tile re-staged them in every wave after the first (lm_head at
+// M = 16: 1024 column tiles, one K slice).  Each CTA stages its rows once; each warp runs its tiles' units through
+// its ring as one sequence.  At one row the single-tile form stays faster (its staging is cheap, and its code
+// leaner: lm_head M = 1 5820 against 5423 GB/s).
+template <int FMT, int NT, bool SPLIT>
+__global__ void __launch_bounds__(kTcWarps * 32, 4) tc_ring_tiles_k(TcArgs a) {
+    static_assert(FMT == kFmtQ8 && NT == 2, "the tiled ring form is the Q8_0 decode GEMV at 16 rows");
+    using G = RingGeom<FMT>;
+    extern __shared__ __align__(16) unsigned char dyn[];
+    const int L = a.L, stride = L + 8;
+    const int ks = blockIdx.y, k0 = ks * L, len = min(L, a.k - k0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    // the warp's tiles: tile0, tile0 + step, ... (a launch with fewer CTAs than column tiles: each CTA stages its rows
+    // of x once for all of its tiles), and their units in this K slice, nun a tile in stages of kRingUnits.  Stage
+    // Q of the warp's sequence is stage Q % nst of its tile Q / nst, in ring slot Q % kRingStages.
+    const int tile0 = blockIdx.x * kTcWarps + warp, step = gridDim.x * kTcWarps, ntile = (a.n + 15) / 16;
+    const int mine = tile0 < ntile ? (ntile - 1 - tile0) / step + 1 : 0;
+    const int nun = len / G::kKu;
+    const int nst = (nun + kRingUnits - 1) / kRingUnits;
+    const int total = mine * nst;
+    const uint32_t sb0 = (uint32_t)__cvta_generic_to_shared(dyn);
+    const uint32_t bar0 = sb0 + 8u * (uint32_t)(warp * kRingStages);
+    const uint32_t ring = sb0 + (uint32_t)ring_offset<FMT>(NT * 8, L) + (uint32_t)(warp * kRingStages * G::kStage);
+    __half* xs = reinterpret_cast<__half*>(dyn + ring_x_offset<FMT>());
+    // smem of unit i of a stage: codes at st + i * CQ, scales at st + SOFF + i * CS
+    constexpr int CQ = SPLIT ? 512 : G::kUb, SOFF = SPLIT ? kRingUnits * 512 : 512, CS = SPLIT ? G::kSsz : G::kUb;
+    auto issue = [&](int Q) {   // stage Q of the warp's sequence into its ring slot (lane 0)
+        const int j = Q / nst, q = Q - j * nst;
+        const size_t u0 = (size_t)(tile0 + j * step) * (a.k / G::kKu) + k0 / G::kKu;
+        const int u = q * kRingUnits, n = min(kRingUnits, nun - u);
+        const uint32_t st = ring + (uint32_t)((Q % kRingStages) * G::kStage), bar = bar0 + 8u * (uint32_t)(Q % kRingStages);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        ring_expect(bar, (uint32_t)(n * G::kUb));
+        if constexpr (SPLIT) {
+            ring_copy(st, a.w + (u0 + u) * 512, (uint32_t)(n * 512), bar);
+            ring_copy(st + SOFF, a.wsc + (u0 + u) * G::kSsz, (uint32_t)(n * G::kSsz), bar);
+        } else {
+            ring_copy(st, a.w + (u0 + u) * G::kUb, (uint32_t)(n * G::kUb), bar);
+        }
+    };
+    if (lane == 0 && total > 0) {
+        for (int i = 0; i < kRingStages; i++) ring_init(bar0 + 8u * (uint32_t)i);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    pdl_wait();
+    if (lane == 0)
+        for (int Q = 0; Q < kRingStages && Q < total; Q++) issue(Q);
+    stage_rows(a, xs, stride, k0, len, min(a.T, NT * 8));
+    __syncthreads();
+    if (total > 0) {
+        const __half* xb = xs + (size_t)g * stride + 2 * t;
+        auto bfrag = [&](int nt, int kk, uint32_t& b0, uint32_t& b1) {
+            const __half* p = xb + (size_t)nt * 8 * stride + kk;
+            b0 = *reinterpret_cast<const uint32_t*>(p);
+            b1 = *reinterpret_cast<const uint32_t*>(p + 8);
+        };
+        const bool partial = gridDim.y > 1;
+        const float sc = partial ? 1.f : a.s2;
+        bool healthy = true;
+        int Q = 0;
+        for (int j = 0; j < mine && healthy; j++) {
+            const int tile = tile0 + j * step;
+            float acc[NT][4];
+#pragma unroll
+            for (int i = 0; i < NT; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+            for (int q = 0; q < nst; q++, Q++) {
+                const uint32_t st = ring + (uint32_t)((Q % kRingStages) * G::kStage), bar = bar0 + 8u * (uint32_t)(Q % kRingStages);
+                const bool ok = ring_wait(bar, (uint32_t)((Q / kRingStages) & 1));
+                if (__any_sync(0xffffffffu, !ok)) {
+                    healthy = false;
+                    break;
+                }
+                const int n = min(kRingUnits, nun - q * kRingUnits);
+#pragma unroll 1
+                for (int i = 0; i < n; i++) {
+                    const uint4 qv = ring_lds128(st + (uint32_t)(i * CQ + 16 * lane));
+                    const int ku = (q * kRingUnits + i) * G::kKu;   // the unit's first k within the slice
+                    const uint32_t dd = ring_lds32(st + (uint32_t)(SOFF + i * CS + 4 * g));
+                    const float dg = __half2float(__ushort_as_half((unsigned short)(dd & 0xffff)));
+                    const float dg8 = __half2float(__ushort_as_half((unsigned short)(dd >> 16)));
+                    float part[NT][4];
+#pragma unroll
+                    for (int nt = 0; nt < NT; nt++) part[nt][0] = part[nt][1] = part[nt][2] = part[nt][3] = 0.f;
+#pragma unroll
+                    for (int u = 0; u < 2; u++) {
+                        uint32_t af[4];
+                        q8_frag(u ? qv.z : qv.x, u ? qv.w : qv.y, af);
+                        const int kk = ku + 16 * u;
+#pragma unroll
+                        for (int nt = 0; nt < NT; nt++) {
+                            uint32_t b0, b1;
+                            bfrag(nt, kk, b0, b1);
+                            mma16816(part[nt], af[0], af[1], af[2], af[3], b0, b1);
+                        }
+                    }
+#pragma unroll
+                    for (int nt = 0; nt < NT; nt++) {
+                        acc[nt][0] = fmaf(dg, part[nt][0], acc[nt][0]);
+                        acc[nt][1] = fmaf(dg, part[nt][1], acc[nt][1]);
+                        acc[nt][2] = fmaf(dg8, part[nt][2], acc[nt][2]);
+                        acc[nt][3] = fmaf(dg8, part[nt][3], acc[nt][3]);
+                    }
+                }
+                __syncwarp();   // every lane is done with the stage: lane 0 refills it
+                if (lane == 0 && Q + kRingStages < total) issue(Q + kRingStages);
+            }
+            if (!healthy) break;
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+                for (int jj = 0; jj < 4; jj++) {
+                    const int tok = nt * 8 + 2 * t + (jj & 1);
+                    const int row = tile * 16 + g + ((jj >> 1) ? 8 : 0);
+                    if (tok < a.T && row < a.n) {
+                        float* o = partial ? a.out + ((size_t)ks * a.T + tok) * a.n + row : a.out + (size_t)tok * a.ldo + row;
+                        *o = acc[nt][jj] * sc;
+                    }
+                }
+        }
+        if (!healthy) {
+            // a stage never filled: flag it, and let this warp's copies in flight land before the CTA's memory goes
+            if (lane == 0) {
+                atomicOr(&g_gemv_error, 1);
+                for (int i = Q; i < total && i < Q + kRingStages; i++)
+                    ring_wait(bar0 + 8u * (uint32_t)(i % kRingStages), (uint32_t)((i / kRingStages) & 1));
+            }
+            __syncwarp();
+        }
+    }
+    pdl_trigger();
+}
+
 int gemv_error_read(int clear) {
     int v = 0;
     if (cudaMemcpyFromSymbol(&v, g_gemv_error, sizeof(int)) != cudaSuccess) return -1;
@@ -717,6 +851,44 @@ template <int FMT, int NT, bool SPLIT>
 static cudaError_t launch_tc(const TcArgs& a, dim3 grid, cudaStream_t s) {
     static size_t opted = 0, opted_fold = 0;
     const size_t smem = tc_smem<FMT>(NT * 8, a.L);
+    if constexpr (FMT == kFmtQ8 && NT == 2) {
+        // 16 rows: the tiled form where the column tiles outnumber the CTAs resident at once (each CTA stages its rows
+        // of x once for all of its tiles), one CTA a column tile where they fit (measured faster there: q/k/v
+        // M = 16 2146 against 2117 GB/s)
+        void (*tiles)(TcArgs) = tc_ring_tiles_k<FMT, NT, SPLIT>;
+        void (*one)(TcArgs) = tc_ring_k<FMT, NT, SPLIT>;
+        static size_t opt_tiles = 0, opt_one = 0, cap_smem = 0;
+        static int per_sm = 0;
+        if (smem > 48 * 1024 && smem > opt_tiles) {
+            const cudaError_t e = cudaFuncSetAttribute(tiles, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            opt_tiles = smem;
+        }
+        if (smem > 48 * 1024 && smem > opt_one) {
+            const cudaError_t e = cudaFuncSetAttribute(one, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            opt_one = smem;
+        }
+        if (cap_smem != smem) {
+            int nb = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, tiles, kTcWarps * 32, smem) != cudaSuccess) {
+                cudaGetLastError();
+                nb = 1;
+            }
+            per_sm = nb > 0 ? nb : 1;
+            cap_smem = smem;
+        }
+        int dev = 0, sms = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            sms <= 0)
+            sms = 148;
+        const unsigned cap = (unsigned)(per_sm * sms) / grid.y;
+        if (cap >= 1 && grid.x > cap) {
+            grid.x = cap;
+            return launch(tiles, grid, dim3(kTcWarps * 32), smem, s, a);
+        }
+        return launch(one, grid, dim3(kTcWarps * 32), smem, s, a);
+    }
     void (*kern)(TcArgs);
     const bool fold = a.cols != nullptr;   // NVFP4 at up to 8 rows: the K split's sum in the launch
     if constexpr (FMT == kFmtQ8) kern = tc_ring_k<FMT, NT, SPLIT>;
