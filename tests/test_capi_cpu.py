@@ -42,6 +42,11 @@ def test_bad_arguments_fail_before_any_launch():
     assert L.b200q_route(p, 1, 128, null, 4, 128, 20, 0, 1.0, p, p, null) == b200q.EINVAL  # topk > 16
     assert L.b200q_moe_group(p, 5000, 128, p, p, p, null) == b200q.EINVAL
     assert L.b200q_quant_rows(p, 0, 64, p, 64, p, 2, 4, 48, null) == b200q.EINVAL         # k % 32
+    # decode GEMVs: x off its element size is refused before anything touches it (the addresses are never read)
+    w, y = ctypes.c_void_p(0x100000), ctypes.c_void_p(0x300000)
+    for x, dt in ((0x200001, b200q.BF16), (0x200002, b200q.F32)):
+        assert L.b200q_q8_gemv(w, 64, 512, ctypes.c_void_p(x), dt, 512, 1, y, 64, null, 0, null) == b200q.EINVAL
+        assert L.b200q_nv4_gemv(w, 1.0, 64, 512, ctypes.c_void_p(x), dt, 512, 1, y, 64, null, 0, null) == b200q.EINVAL
     # workspace too small / misaligned
     ws = L.b200q_moe_decode_workspace_bytes(16, 4096, 2048, 128, 6)
     assert ws > 16 * 6 * 4096 * 4
