@@ -163,7 +163,8 @@ struct TcArgs {
 
 // The token rows of the CTA's K slice [k0, k0 + len) as fp16 into shared memory (row stride `stride` halves).  Only
 // the `rows` rows that exist are staged: the MMA's output column n reads only B column n, and the columns of the
-// absent rows are never stored, so those rows of B need no zeros.  A row at a time, so no index needs a division.
+// absent rows are never stored, so those rows of B need no zeros.  No index needs a division: the four-value form
+// walks (row, unit) positions across the CTA's threads, the pair and single-value forms go a row at a time.
 __device__ __forceinline__ void stage_rows(const TcArgs& a, __half* xs, int stride, int k0, int len, int rows) {
     const bool bf = a.x_dtype == B200Q_BF16;
     const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(a.x);
