@@ -833,10 +833,11 @@ static int slice_len(int fmt, int n, int k) {
     const int want = (per_sm * 148 + ctas_x - 1) / ctas_x;
     int L = (k + want - 1) / want;
     L = ((L + 255) / 256) * 256;
-    // Q8_0 with enough column tiles for one slice (lm_head): two slices from K = 2048 on, so that a CTA stages half
-    // the rows' length and two fit an SM (measured on B200, lm_head 131072 x 4096: M = 1 5817 -> 6213 GB/s, M = 16
-    // 2886 -> 4004; the projections with fewer columns already take several slices)
-    if (fmt == kFmtQ8 && L >= k && k >= 2048) L = ((k / 2 + 255) / 256) * 256;
+    // Q8_0 with enough column tiles for one slice (lm_head): four slices from K = 2048 on, so that a CTA stages a
+    // quarter of the rows' length and more CTAs fit an SM (measured on B200, lm_head 131072 x 4096, one / two / four
+    // slices: M = 1 5817 / 6213 / 6360 GB/s, M = 16 2886 / 4004 / 4005; the projections with fewer columns already
+    // take several slices)
+    if (fmt == kFmtQ8 && L >= k && k >= 2048) L = ((k / 4 + 255) / 256) * 256;
     return L > k ? k : L;
 }
 
