@@ -628,7 +628,7 @@ def nvfp4_bench(b200q, device, iters=20):
     U{0..15}, e4m3 scales U[0.5, 2] per 16, an fp32 tensor scale), activations bf16 N(0, 1).  M <= 16: the t16 decode
     GEMV, GB/s over weights + x + y, rotating weight copies of twice the L2 (6 of in_proj, 14 of out_proj), timed as a
     CUDA graph of 60 calls.  M >= 512: quant_nv4_rows + the block-scaled fp4 tcgen05 GEMM, TFLOPS of the GEMM alone
-    and of quantiser + GEMM."""
+    and of quantiser + GEMM, each timed as a CUDA graph of `iters` calls."""
     shapes = {"in_proj": (18560, 4096), "out_proj": (4096, 8192)}
     ncopies = {"in_proj": 6, "out_proj": 14}
     g = torch.Generator(device="cpu").manual_seed(31)
@@ -641,7 +641,6 @@ def nvfp4_bench(b200q, device, iters=20):
             W[name].append((b200q.tile_nv4(q, sc, n, k), b200q.tile_nv4w(q, sc, n, k) if c == 0 else None))
     s2 = 0.01
     out = {}
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     for name, (n, k) in shapes.items():
         copies = ncopies[name]
         for M in (1, 16):
@@ -659,21 +658,17 @@ def nvfp4_bench(b200q, device, iters=20):
             y = torch.empty(M, n, device=device)
             wt = W[name][0][1]
             for _ in range(3):
-                b200q.mma_nv4_fp4(wt, s2, n, k, rows, M, y=y)
-            torch.cuda.synchronize()
-            e0.record()
-            for _ in range(iters):
-                b200q.mma_nv4_fp4(wt, s2, n, k, rows, M, y=y)
-            e1.record()
-            torch.cuda.synchronize()
-            gemm_ms = e0.elapsed_time(e1) / iters
-            e0.record()
-            for _ in range(iters):
                 b200q.quant_nv4_rows(x, out=rows)
                 b200q.mma_nv4_fp4(wt, s2, n, k, rows, M, y=y)
-            e1.record()
             torch.cuda.synchronize()
-            both_ms = e0.elapsed_time(e1) / iters
+            # as CUDA graphs of `iters` calls: at M = 512 a call is some 10-40 us of GPU time, about what the Python
+            # side of a launch takes, so launch-by-launch timing would measure the host
+            gemm_ms = graph_ms(lambda i: b200q.mma_nv4_fp4(wt, s2, n, k, rows, M, y=y), iters)
+
+            def both(i):
+                b200q.quant_nv4_rows(x, out=rows)
+                b200q.mma_nv4_fp4(wt, s2, n, k, rows, M, y=y)
+            both_ms = graph_ms(both, iters)
             fl = 2.0 * M * n * k
             out[f"{name}_M{M}_tflops"] = round(fl / (gemm_ms * 1e-3) / 1e12, 1)
             out[f"{name}_M{M}_with_quant_tflops"] = round(fl / (both_ms * 1e-3) / 1e12, 1)
