@@ -641,6 +641,8 @@ def nvfp4_bench(b200q, device, iters=20):
             W[name].append((b200q.tile_nv4(q, sc, n, k), b200q.tile_nv4w(q, sc, n, k) if c == 0 else None))
     s2 = 0.01
     out = {}
+    # the decode GEMVs of both matrices first, then the prompt GEMMs: a GEMV timed right after seconds of
+    # back-to-back fp4 GEMMs runs on a GPU held at its power cap (out_proj M = 1 measured 7 % lower there)
     for name, (n, k) in shapes.items():
         copies = ncopies[name]
         for M in (1, 16):
@@ -652,6 +654,7 @@ def nvfp4_bench(b200q, device, iters=20):
             ms = graph_ms(lambda i: b200q.mma_nv4(W[name][i % copies][0], s2, n, k, x, y=y), 60)
             nbytes = n * k // 2 + n * k // 16 + M * k * 2 + M * n * 4
             out[f"{name}_M{M}_gbs"] = round(nbytes / (ms * 1e-3) / 1e9, 1)
+    for name, (n, k) in shapes.items():
         for M in (512, 4096):
             x = torch.randn(M, k, generator=g).to(torch.bfloat16).to(device)
             rows = b200q.quant_nv4_rows(x)
